@@ -1,0 +1,121 @@
+"""The oracle's homomorphic ops decrypt to the plaintext results: decrypt(eval(enc(x))) ~ f(x).
+
+Small rings (N = 2^10) so the pure-CPU suite stays fast; the same code paths run at the BASELINE sizes in the GPU
+parity tests. The parameter shape mirrors BASELINE config 1 (50-bit Q primes, one 60-bit special prime, one limb per
+digit) and config 2 (several limbs per digit, several special primes).
+"""
+import numpy as np
+import pytest
+
+from tests import _oracle as O
+
+LOGN = 10
+N = 1 << LOGN
+SLOTS = N // 2
+SCALE = 2.0**40
+
+
+def make_ctx(nq=4, kp=1, dnum=4, pbits=60, steps=(1, 2, 4, -1)):
+    q = O.ntt_primes(50, LOGN, nq)
+    p = O.ntt_primes(pbits, LOGN, kp, skip=nq if pbits == 50 else 0)
+    c = O.Ctx(LOGN, q, p, dnum)
+    gal = [1] + [O.lib().orc_rotation_galois(s, LOGN) for s in steps]
+    c.keygen(seed=0, h=192, sigma=3.2, galois=gal)
+    return c
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    return make_ctx()
+
+
+@pytest.fixture(scope="module")
+def ctx3():
+    # three limbs per digit (dnum 2 over 6 limbs), two 50-bit special primes: config 2's structure
+    return make_ctx(nq=6, kp=3, dnum=2, pbits=50)
+
+
+def vals(seed, n=SLOTS, scale=1.0):
+    r = np.random.default_rng(seed)
+    return r.normal(0, 1, n) * scale
+
+
+def test_encrypt_decrypt(ctx):
+    x = vals(1)
+    top = ctx.nq - 1
+    ct = ctx.encrypt(x, SLOTS, SCALE, top)
+    y = ctx.decrypt(ct, top, SLOTS, SCALE)
+    assert np.abs(y.real - x).max() < 1e-7
+
+
+def test_secret_weight(ctx):
+    s = ctx.secret()
+    assert int((s != 0).sum()) == 192
+
+
+@pytest.mark.parametrize("which", ["ctx", "ctx3"])
+def test_mult_relin_rescale(which, request):
+    c = request.getfixturevalue(which)
+    top = c.nq - 1
+    x, y = vals(2), vals(3)
+    a = c.encrypt(x, SLOTS, SCALE, top)
+    b = c.encrypt(y, SLOTS, SCALE, top)
+    m = c.mult(a, b, top)
+    # decode reads the bottom prime only (crates/pc-core/src/encode.rs:236-268): rescale before decrypting
+    r = c.rescale(m, top)
+    got = c.decrypt(r, top - 1, SLOTS, SCALE * SCALE / c.q[top])
+    assert np.abs(got.real - x * y).max() < 1e-4
+
+
+@pytest.mark.parametrize("which", ["ctx", "ctx3"])
+@pytest.mark.parametrize("step", [1, 4, -1])
+def test_rotate(which, step, request):
+    c = request.getfixturevalue(which)
+    top = c.nq - 1
+    x = vals(4)
+    ct = c.encrypt(x, SLOTS, SCALE, top)
+    r = c.rotate(ct, step, top)
+    got = c.decrypt(r, top, SLOTS, SCALE)
+    assert np.abs(got.real - np.roll(x, -step)).max() < 1e-6
+
+
+def test_rotate_lower_level(ctx3):
+    # key switching below the top: live digits and limbs cut at the level (crates/pc-gpu/src/ks.rs:579-582)
+    c = ctx3
+    top = 3
+    x = vals(5)
+    ct = c.encrypt(x, SLOTS, SCALE, top)
+    r = c.rotate(ct, 2, top)
+    got = c.decrypt(r, top, SLOTS, SCALE)
+    assert np.abs(got.real - np.roll(x, -2)).max() < 1e-6
+
+
+def test_rotate_and_sum(ctx):
+    top = ctx.nq - 1
+    x = vals(6)
+    ct = ctx.encrypt(x, SLOTS, SCALE, top)
+    r = ctx.rotate_and_sum(ct, 1, 8, top)
+    got = ctx.decrypt(r, top, SLOTS, SCALE)
+    want = sum(np.roll(x, -k) for k in range(8))
+    assert np.abs(got.real - want).max() < 1e-5
+
+
+def test_mult_pt_and_add_pt(ctx):
+    top = ctx.nq - 1
+    x, w = vals(7), vals(8)
+    ct = ctx.encrypt(x, SLOTS, SCALE, top)
+    pt = ctx.encode(w, SLOTS, SCALE, top)
+    prod = ctx.rescale(ctx.mult_pt(ct, pt, top), top)
+    got = ctx.decrypt(prod, top - 1, SLOTS, SCALE * SCALE / ctx.q[top])
+    assert np.abs(got.real - x * w).max() < 1e-4
+    got = ctx.decrypt(ctx.add_pt(ct, pt, top), top, SLOTS, SCALE)
+    assert np.abs(got.real - (x + w)).max() < 1e-6
+
+
+def test_determinism(ctx):
+    # the same seed reproduces keys and encryptions word for word (the parity tests rely on it)
+    c2 = make_ctx()
+    for i in range(3):
+        b1, a1, s1 = ctx.key(i)
+        b2, a2, s2 = c2.key(i)
+        assert (b1 == b2).all() and (a1 == a2).all() and (s1 == s2).all()

@@ -1,0 +1,421 @@
+/*
+ * perseus-b200 — the C ABI of the B200-native CKKS hot path.
+ *
+ * Two layers, both plain C (pointers and sizes; no torch types):
+ *
+ *  1. The launcher table that the reference's device runtime binds (crates/pc-kernels/kernels/args.cuh:1034-1097,
+ *     Rust mirror crates/pc-kernels/src/args.rs, loader crates/pc-kernels/src/table.rs:325-336):
+ *        const PcbKernelTable* pc_table_u64_barrett64(void);   ring N = 2^16
+ *        const PcbRingTable*   pc_ring_u64_14(void);           ring N = 2^14 (args.cuh:1099-1119)
+ *     Every argument struct below keeps the reference's field order, types and size (checked by static asserts and
+ *     by tests/test_abi.py) so a reference caller's #[repr(C)] values can be handed over unchanged. Launchers copy
+ *     their arguments, are stream-ordered and return 0 (ok), -1 / -2 (argument out of range) or a positive
+ *     cudaError_t (args.cuh:1036). Entries this library does not provide are non-null and return -1.
+ *
+ *  2. The evaluator (the reference's pc-gpu Evaluator / KeySwitcher / Rescaler, crates/pc-gpu/src/{relin,rotate,
+ *     ks,rescale,encrypt,keygen}.rs): a context over one chain with device-resident keys, and ciphertext ops on
+ *     caller-owned device buffers (pcb_*). The same return-code convention; pcb_last_error() gives the message.
+ *
+ * Words are uint64_t residues in [0, p). A row holds N words. A ciphertext of the evaluator is [2][nq + kp][N]
+ * words (part 0 = c0, part 1 = c1; row r = prime id r; Q ids 0..nq-1 then the special ids), evaluation form
+ * (bit-reversed negacyclic NTT order), matching the reference's layout (crates/pc-gpu/src/poly.rs).
+ */
+#ifndef PCB200_H
+#define PCB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__CUDACC__) || defined(PCB_WITH_CUDA_RUNTIME)
+#include <cuda_runtime_api.h>
+#else
+typedef struct CUstream_st* cudaStream_t;
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ================================================================ 1. launcher table (args.cuh layouts) */
+
+/* args.cuh:38-49: per prime id, 64 bytes. u64 words: mu = floor((2^128 - 1) / p) split into mu_lo / mu_hi. */
+typedef struct PcbPrimeConst {
+    uint64_t p, mu_lo, mu_hi, neal_mu;
+    uint32_t bits, word_bits;
+    uint64_t mont_pinv, mont_r2, split;
+} PcbPrimeConst;
+
+/* args.cuh:51-58: grid row y -> prime id y < nq ? y : qmax + (y - nq) */
+typedef struct PcbRowSet {
+    int32_t nq, np, qmax, pad;
+} PcbRowSet;
+
+/* args.cuh:60-65: part `part` of ciphertext c, row r at base + c*ct_stride + part*part_stride + r*N words */
+typedef struct PcbPolyRef {
+    void* base;
+    uint64_t ct_stride, part_stride;
+} PcbPolyRef;
+
+/* args.cuh:67-107: in-place negacyclic NTT of nrows rows (row i at base + roff[i]*N, prime id rprime[i]);
+ * twiddles [prime id][N] bit-reversed (fw[m+i] = psi^brev(m+i)) with Shoup companions; soff: out-of-place sources
+ * (sum of snum rows sstride words apart); forward epilogues epi 1: eout = (x - v) es, 2: eout = d + (x - v) es,
+ * 3: eout = x es + v; inverse: es non-null scales row i by es[i] in place of N^-1. */
+typedef struct PcbNttArgs {
+    void* base;
+    const uint32_t* roff;
+    const int32_t* rprime;
+    const void* fw;
+    const void* fws;
+    const void* iw;
+    const void* iws;
+    const void* ninv;
+    const void* ninvs;
+    const PcbPrimeConst* pr;
+    int32_t nrows, chunk;
+    const void* src;
+    const uint32_t* soff;
+    void* eout;
+    const void* ex;
+    const void* es;
+    const void* ess;
+    int32_t epi, snum;
+    uint64_t sstride;
+    int32_t xnum, lazy;
+    uint64_t xstride;
+    const void* ed;
+} PcbNttArgs;
+
+/* args.cuh:109-141: batched fast base conversion, pool layout src_row[ns] src_prime[ns] pre[ns] tgt_row[nt]
+ * tgt_prime[nt] M[ns][nt] (words). out_t = sum_i y_i M[i][t] mod t, y_i = x_i pre_i (or x_i when prescaled). */
+typedef struct PcbBconvJob {
+    uint32_t src_off, dst_off, nsrc, ntgt, pool_off, exact, prescaled, split;
+} PcbBconvJob;
+typedef struct PcbBconvArgs {
+    const void* src;
+    void* dst;
+    const PcbBconvJob* jobs;
+    const void* pool;
+    const PcbPrimeConst* pr;
+    int32_t njobs, max_tgt;
+    int32_t kind, pad;
+} PcbBconvArgs;
+
+/* args.cuh:143-157: ew_add (sub: a - b), ew_scale (a * sc[row]), ew_sub_mul ((a - b) * sc[row]), ew_copy */
+typedef struct PcbEwArgs {
+    PcbPolyRef out, a, b;
+    PcbRowSet rs;
+    const void* sc;
+    const void* scs;
+    const PcbPrimeConst* pr;
+    int32_t K, nparts, sub, zero_p;
+} PcbEwArgs;
+
+/* args.cuh:202-228: key inner product of K ciphertexts x R keys; outputs at automorph_slot(autok[r], i) */
+#define PCB_KS_ACC 4
+typedef struct PcbKsArgs {
+    const void* c1;
+    const void* modup;
+    const void* c0;
+    void* out0;
+    void* out1;
+    const void* const* kb;
+    const void* const* ka;
+    const uint32_t* autok;
+    const uint32_t* rows;
+    const int32_t* digit_of;
+    const void* pmod;
+    const void* pmods;
+    const PcbPrimeConst* pr;
+    uint64_t ct_stride, mu_ct_stride, mu_digit_stride, out_ct_stride, out_rot_stride, key_digit_stride;
+    int32_t K, R, ndig, c0_mode, nq, nrows;
+} PcbKsArgs;
+
+/* args.cuh:258-271 (relin epilogue), :273-283 (KeyTab), :285-304 (KsRegenArgs); ks_dot_regen is not provided */
+typedef struct PcbEpiArgs {
+    void* dst;
+    const void* conv;
+    const void* binv;
+    const void* binvs;
+    const void* k;
+    uint64_t part_stride;
+    int32_t dbl, pad;
+    const void* alpha;
+    const void* alphas;
+} PcbEpiArgs;
+typedef struct PcbKeyTab {
+    const void* const* kb;
+    const uint32_t* const* seed;
+    uint64_t row_words;
+    int32_t bits, q_top, srows, nregen;
+} PcbKeyTab;
+typedef struct PcbKsRegenArgs {
+    PcbKsArgs ks;
+    const uint32_t* seed;
+    PcbEpiArgs epi;
+    int32_t use_epi, pad;
+    PcbKeyTab key;
+    const void* add;
+} PcbKsRegenArgs;
+
+/* args.cuh:306-323: out[d][m][N] = expander(seed, digit d, prime prime_ids[m]) (u64: the frozen KSKB lane) */
+typedef struct PcbKskExpandArgs {
+    void* out;
+    const uint32_t* seed;
+    const int32_t* prime_ids;
+    const PcbPrimeConst* pr;
+    int32_t nmod, dnum;
+    int32_t d0, pad;
+} PcbKskExpandArgs;
+
+/* args.cuh:355-367: (c0, c1, d2) (= | +=) sum_j (a0 b0, a0 b1 + a1 b0, a1 b1) over Q rows [0, n) of K cts */
+typedef struct PcbTensorArgs {
+    PcbPolyRef out, d2, a0, b0, a1, b1;
+    void* coef;
+    uint64_t coef_ct_stride;
+    const PcbPrimeConst* pr;
+    int32_t npairs, acc, n, K;
+    int32_t dbl, acc_d2;
+} PcbTensorArgs;
+
+/* args.cuh:438-447: for parts 0, 1: dst = f (dst + (x - t) binv) [+ k on part 0], f = 2 when dbl */
+typedef struct PcbMdEpiArgs {
+    PcbPolyRef dst, x, t;
+    const void* binv;
+    const void* binvs;
+    const void* k;
+    const PcbPrimeConst* pr;
+    int32_t dbl, n, K, pad;
+} PcbMdEpiArgs;
+
+/* args.cuh:525-572: composite rescale; ndrop 1: tmp_i = A_i lift(y_top); combine x_i = alpha_i x_i + tmp_i */
+typedef struct PcbRescaleArgs {
+    PcbPolyRef x, tmp;
+    const void* A;
+    const void* B;
+    const void* As;
+    const void* Bs;
+    const void* qam;
+    const void* qbm;
+    const PcbPrimeConst* pr;
+    uint64_t qinv_ab, C_ab, ca, cb;
+    int32_t top, nrows, K, ndrop;
+} PcbRescaleArgs;
+typedef struct PcbRescaleCombineArgs {
+    PcbPolyRef x, tmp;
+    const void* alpha;
+    const void* alphas;
+    const PcbPrimeConst* pr;
+    int32_t n, K;
+} PcbRescaleCombineArgs;
+
+/* args.cuh:580-592: out[o] = in[automorph_slot(k, o)] (+ add[o]) over row set rs, K cts x nparts parts */
+typedef struct PcbAutomorphArgs {
+    PcbPolyRef out, in, add;
+    PcbRowSet rs;
+    const PcbPrimeConst* pr;
+    uint32_t k;
+    int32_t K, nparts, has_add;
+} PcbAutomorphArgs;
+
+/* args.cuh:613-628: c0 = -a s + e + m, c1 = a, a from the ENCA lane (u64: ENCB) keyed by the nonce */
+typedef struct PcbEncryptArgs {
+    void* c0;
+    void* c1;
+    const void* s;
+    const void* e;
+    const void* m;
+    const uint32_t* seed;
+    const PcbPrimeConst* pr;
+    uint32_t nonce;
+    int32_t nl;
+} PcbEncryptArgs;
+
+/* args.cuh:630-654: b = e - a s_new + [digit] P s_old' (dense rows only at u64: bits must be 0) */
+typedef struct PcbKskGenArgs {
+    void* b;
+    void* a;
+    const void* e;
+    const void* s_new;
+    const void* s_old;
+    const uint32_t* seed;
+    const int32_t* ids;
+    const int32_t* digit_of;
+    const void* pmod;
+    const void* pmods;
+    const PcbPrimeConst* pr;
+    uint64_t row_words;
+    int32_t nrows, ndig, nq, bits, sq, pad;
+} PcbKskGenArgs;
+
+typedef int (*PcbLaunch)(const void* args, cudaStream_t stream);
+
+/* args.cuh:1034-1097: 16-byte header then 52 launchers, in the reference's order */
+typedef struct PcbKernelTable {
+    uint32_t abi, word_bytes, mm, log_n;
+    int (*ntt_fwd)(const PcbNttArgs*, cudaStream_t);
+    int (*ntt_inv)(const PcbNttArgs*, cudaStream_t);
+    int (*bconv)(const PcbBconvArgs*, cudaStream_t);
+    int (*ew_add)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_scale)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_sub_mul)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_copy)(const PcbEwArgs*, cudaStream_t);
+    PcbLaunch pt_dot;
+    int (*ks_dot)(const PcbKsArgs*, cudaStream_t);
+    int (*ks_dot_regen)(const PcbKsRegenArgs*, cudaStream_t);
+    int (*ksk_expand)(const PcbKskExpandArgs*, cudaStream_t);
+    PcbLaunch cts_fused;
+    int (*tensor)(const PcbTensorArgs*, cudaStream_t);
+    int (*md_epilogue)(const PcbMdEpiArgs*, cudaStream_t);
+    PcbLaunch wsum;
+    PcbLaunch add_const;
+    PcbLaunch mul_table;
+    int (*rescale_coef)(const PcbRescaleArgs*, cudaStream_t);
+    int (*rescale_combine)(const PcbRescaleCombineArgs*, cudaStream_t);
+    int (*automorph)(const PcbAutomorphArgs*, cudaStream_t);
+    PcbLaunch encode;
+    int (*encrypt)(const PcbEncryptArgs*, cudaStream_t);
+    int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
+    PcbLaunch ksk_unpack, mod_raise, small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen,
+        ks_dot_key, pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum, mul_add,
+        rescale_fwd, mul_add_n, tensor_y, wsum_multi, bconv_wide, tfhe, tensor_sum, tensor_multi, tensor_seeded,
+        ew_many, submul_many, pack_split, pack_dot;
+} PcbKernelTable;
+
+/* args.cuh:1099-1119: ring-size tables (rows of 2^log_n words) */
+typedef struct PcbRingTable {
+    uint32_t abi, word_bytes, mm, log_n;
+    int (*ntt_fwd)(const PcbNttArgs*, cudaStream_t);
+    int (*ntt_inv)(const PcbNttArgs*, cudaStream_t);
+    int (*ntt_fwd_g)(const PcbNttArgs*, cudaStream_t);
+    int (*ntt_inv_g)(const PcbNttArgs*, cudaStream_t);
+    int (*bconv)(const PcbBconvArgs*, cudaStream_t);
+    int (*ew_add)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_scale)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_sub_mul)(const PcbEwArgs*, cudaStream_t);
+    int (*ew_copy)(const PcbEwArgs*, cudaStream_t);
+} PcbRingTable;
+
+#define PCB_KERNELS_ABI 30u
+#define PCB_RING_ABI 7u
+
+/* replaces `pc_table_u64_barrett64` of crates/pc-kernels/kernels/inst/instantiate.inc:368-428 (u64, Barrett64) */
+const PcbKernelTable* pc_table_u64_barrett64(void);
+/* replaces `pc_ring_u64_<log_n>` of crates/pc-kernels/kernels/args.cuh:1099-1104 at log_n 14 and 16 */
+const PcbRingTable* pc_ring_u64_14(void);
+const PcbRingTable* pc_ring_u64_16(void);
+
+/* ================================================================ 2. evaluator */
+
+typedef struct PcbCtx PcbCtx;
+
+/* Chain parameters (the reference's Chain, crates/pc-core/src/params.rs:225-258, given as explicit prime lists). */
+typedef struct PcbParams {
+    uint32_t log_n;      /* 14 or 16 */
+    int32_t nq, kp;      /* Q primes (bottom first), special primes */
+    int32_t dnum;        /* hybrid digits: ceil(nq / dnum) limbs each (params.rs:486-495) */
+    const uint64_t* q;   /* nq primes, p = 1 mod 2N, < 2^61 */
+    const uint64_t* p;   /* kp primes */
+    int32_t k_max;       /* ciphertexts per batched key switch */
+    int32_t pad;
+} PcbParams;
+
+/* Message of the last failed call on this thread (empty when none). */
+const char* pcb_last_error(void);
+
+/* Device bytes a context of `prm` needs in its arena (tables, plans, key-switch workspaces for k_max cts) plus
+ * `nkeys` switching keys with stored `a`. */
+int64_t pcb_ctx_bytes(const PcbParams* prm, int32_t nkeys);
+/* Build a context on the current device. `arena` is caller-owned device memory of `arena_bytes` >= pcb_ctx_bytes
+ * (the frozen arena of crates/pc-cuda/src/lib.rs:9-10); the context allocates nothing else on the device. */
+int pcb_ctx_create(const PcbParams* prm, int32_t nkeys, void* arena, size_t arena_bytes, cudaStream_t stream,
+                   PcbCtx** out);
+void pcb_ctx_destroy(PcbCtx* ctx);
+int pcb_ctx_rows(const PcbCtx* ctx);
+/* Device tables: PrimeConst by prime id, and the four NTT twiddle tables [prime id][N] + N^-1 (value, Shoup). */
+int pcb_ctx_tables(const PcbCtx* ctx, const PcbPrimeConst** pr, const uint64_t** fw, const uint64_t** fws,
+                   const uint64_t** iw, const uint64_t** iws, const uint64_t** ninv, const uint64_t** ninvs);
+
+/* Session keys (crates/pc-gpu/src/keygen.rs:184-284, crates/pc-py/src/session.rs:1438-1450): the DRBG
+ * Prng([0x5e551013, lo32(seed), hi32(seed), 4..8], 0) draws the secret (sparse ternary of Hamming weight h; 0 =
+ * uniform ternary), then per key (galois[i]; 1 = relinearization) its KSKB seed and error-stream seed, then the
+ * encryptor seed. Keys are generated on the device (ksk_gen) into the arena. */
+int pcb_keygen(PcbCtx* ctx, uint64_t seed, uint32_t h, double sigma, int32_t ngal, const uint64_t* galois,
+               cudaStream_t stream);
+/* key `idx` in keygen order: device pointers of b and a ([dnum][nq + kp][N]) and its galois element */
+int pcb_key_ptrs(const PcbCtx* ctx, int32_t idx, const uint64_t** b, const uint64_t** a, uint64_t* galois);
+
+/* Copy key `idx` (b then a, [dnum][nq + kp][N] words each) into caller device buffers on `stream`. */
+int pcb_key_copy(const PcbCtx* ctx, int32_t idx, uint64_t* b_out, uint64_t* a_out, cudaStream_t stream);
+
+/* Secret-key encryption of nvals (re, im) values into nslots slots at `scale`, rows 0..=top of ct (device). */
+int pcb_encrypt(PcbCtx* ctx, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
+                uint64_t* ct, cudaStream_t stream);
+/* Decrypt rows 0..=top of ct (device) to nslots (re, im) values on the host (synchronizes `stream`). */
+int pcb_decrypt(PcbCtx* ctx, const uint64_t* ct, int32_t top, int32_t nslots, double scale, double* vals,
+                cudaStream_t stream);
+/* Encode values into coefficient-form rows 0..=top on the host (plaintext operands of pcb_mult_pt / pcb_add_pt). */
+int pcb_encode(PcbCtx* ctx, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
+               uint64_t* rows);
+/* Upload host coefficient rows 0..=top and take them to evaluation form into pt (device, [nq][N]). */
+int pcb_pt_load(PcbCtx* ctx, const uint64_t* rows_host, int32_t top, uint64_t* pt, cudaStream_t stream);
+
+/* Ciphertext ops over K ciphertexts `ct_stride` words apart (0 = one ciphertext layout apart), rows 0..=top. */
+int pcb_add(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
+            cudaStream_t stream);
+int pcb_sub(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
+            cudaStream_t stream);
+/* out = a * b relinearized, rescale pending (crates/pc-gpu/src/relin.rs:213-232); out may alias a or b */
+int pcb_mult(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
+             cudaStream_t stream);
+/* in place: rows 0..top-1 = q_top^-1 (x - lift(x_top)) (crates/pc-gpu/src/rescale.rs:230) */
+int pcb_rescale(PcbCtx* ctx, uint64_t* ct, int32_t top, int32_t K, cudaStream_t stream);
+/* out = rot(x, step), left by step slots (crates/pc-gpu/src/rotate.rs:147-204); out must not alias x */
+int pcb_rotate(PcbCtx* ctx, const uint64_t* x, int64_t step, uint64_t* out, int32_t top, int32_t K,
+               cudaStream_t stream);
+/* out = x + rot(x, g) ladder over gaps start, 2 start, .. < stop (crates/pc-gpu/src/rotate.rs:924-992) */
+int pcb_rotate_and_sum(PcbCtx* ctx, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int32_t top,
+                       int32_t K, cudaStream_t stream);
+/* out = x * pt (pt: device evaluation rows [nq][N] from pcb_pt_load); out = x + pt on part 0 */
+int pcb_mult_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
+                cudaStream_t stream);
+int pcb_add_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
+               cudaStream_t stream);
+
+/* The hybrid key switch of one polynomial per ciphertext (the north star's fused KeySwitcher): ext = dot(ModUp(d))
+ * against key `kidx` with c0 mode (0 none, 1 P c0 on Q rows) and output permutation autok, then ModDown into out.
+ * d, c0: rows 0..=top of K polynomials `in_stride` words apart; out: K ciphertexts. */
+int pcb_keyswitch(PcbCtx* ctx, const uint64_t* d, const uint64_t* c0, int32_t c0_mode, int32_t kidx, uint32_t autok,
+                  uint64_t* out, int32_t top, int32_t K, uint64_t in_stride, cudaStream_t stream);
+
+/* Batched NTT over nrows rows of `x` ([nrows][N]) cycling over the Q primes (row i: prime i mod nq). */
+int pcb_ntt_batch(PcbCtx* ctx, uint64_t* x, int32_t nrows, int32_t inverse, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#ifdef __cplusplus
+static_assert(sizeof(PcbPrimeConst) == 64, "PrimeConst layout");
+static_assert(sizeof(PcbRowSet) == 16, "RowSet layout");
+static_assert(sizeof(PcbPolyRef) == 24, "PolyRef layout");
+static_assert(sizeof(PcbNttArgs) == 176, "NttArgs layout");
+static_assert(sizeof(PcbBconvJob) == 32, "BconvJob layout");
+static_assert(sizeof(PcbBconvArgs) == 56, "BconvArgs layout");
+static_assert(sizeof(PcbEwArgs) == 128, "EwArgs layout");
+static_assert(sizeof(PcbKsArgs) == 176, "KsArgs layout");
+static_assert(sizeof(PcbEpiArgs) == 72, "EpiArgs layout");
+static_assert(sizeof(PcbKeyTab) == 40, "KeyTab layout");
+static_assert(sizeof(PcbKsRegenArgs) == 312, "KsRegenArgs layout");
+static_assert(sizeof(PcbKskExpandArgs) == 48, "KskExpandArgs layout");
+static_assert(sizeof(PcbTensorArgs) == 192, "TensorArgs layout");
+static_assert(sizeof(PcbMdEpiArgs) == 120, "MdEpiArgs layout");
+static_assert(sizeof(PcbRescaleArgs) == 152, "RescaleArgs layout");
+static_assert(sizeof(PcbRescaleCombineArgs) == 80, "RescaleCombineArgs layout");
+static_assert(sizeof(PcbAutomorphArgs) == 112, "AutomorphArgs layout");
+static_assert(sizeof(PcbEncryptArgs) == 64, "EncryptArgs layout");
+static_assert(sizeof(PcbKskGenArgs) == 120, "KskGenArgs layout");
+static_assert(sizeof(PcbKernelTable) == 16 + 52 * 8, "KernelTable layout");
+static_assert(sizeof(PcbRingTable) == 16 + 9 * 8, "RingTable layout");
+#endif
+
+#endif /* PCB200_H */

@@ -1,0 +1,217 @@
+"""ctypes binding of perseus_b200/libpcb200.so (the C ABI declared in include/pcb200.h).
+
+The library is built in-tree (perseus_b200/build.py). Loading fails loudly when it is missing: there is no CPU
+fallback for any op of this package.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libpcb200.so")
+
+vp = C.c_void_p
+u64p = C.POINTER(C.c_uint64)
+
+
+class PrimeConst(C.Structure):
+    _fields_ = [("p", C.c_uint64), ("mu_lo", C.c_uint64), ("mu_hi", C.c_uint64), ("neal_mu", C.c_uint64),
+                ("bits", C.c_uint32), ("word_bits", C.c_uint32), ("mont_pinv", C.c_uint64),
+                ("mont_r2", C.c_uint64), ("split", C.c_uint64)]
+
+
+class RowSet(C.Structure):
+    _fields_ = [("nq", C.c_int32), ("np", C.c_int32), ("qmax", C.c_int32), ("pad", C.c_int32)]
+
+
+class PolyRef(C.Structure):
+    _fields_ = [("base", vp), ("ct_stride", C.c_uint64), ("part_stride", C.c_uint64)]
+
+
+class NttArgs(C.Structure):
+    _fields_ = [("base", vp), ("roff", vp), ("rprime", vp), ("fw", vp), ("fws", vp), ("iw", vp), ("iws", vp),
+                ("ninv", vp), ("ninvs", vp), ("pr", vp), ("nrows", C.c_int32), ("chunk", C.c_int32), ("src", vp),
+                ("soff", vp), ("eout", vp), ("ex", vp), ("es", vp), ("ess", vp), ("epi", C.c_int32),
+                ("snum", C.c_int32), ("sstride", C.c_uint64), ("xnum", C.c_int32), ("lazy", C.c_int32),
+                ("xstride", C.c_uint64), ("ed", vp)]
+
+
+class BconvJob(C.Structure):
+    _fields_ = [(f, C.c_uint32) for f in ("src_off", "dst_off", "nsrc", "ntgt", "pool_off", "exact", "prescaled", "split")]
+
+
+class BconvArgs(C.Structure):
+    _fields_ = [("src", vp), ("dst", vp), ("jobs", vp), ("pool", vp), ("pr", vp), ("njobs", C.c_int32),
+                ("max_tgt", C.c_int32), ("kind", C.c_int32), ("pad", C.c_int32)]
+
+
+class EwArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("a", PolyRef), ("b", PolyRef), ("rs", RowSet), ("sc", vp), ("scs", vp),
+                ("pr", vp), ("K", C.c_int32), ("nparts", C.c_int32), ("sub", C.c_int32), ("zero_p", C.c_int32)]
+
+
+class KsArgs(C.Structure):
+    _fields_ = [("c1", vp), ("modup", vp), ("c0", vp), ("out0", vp), ("out1", vp), ("kb", vp), ("ka", vp),
+                ("autok", vp), ("rows", vp), ("digit_of", vp), ("pmod", vp), ("pmods", vp), ("pr", vp),
+                ("ct_stride", C.c_uint64), ("mu_ct_stride", C.c_uint64), ("mu_digit_stride", C.c_uint64),
+                ("out_ct_stride", C.c_uint64), ("out_rot_stride", C.c_uint64), ("key_digit_stride", C.c_uint64),
+                ("K", C.c_int32), ("R", C.c_int32), ("ndig", C.c_int32), ("c0_mode", C.c_int32), ("nq", C.c_int32),
+                ("nrows", C.c_int32)]
+
+
+class EpiArgs(C.Structure):
+    _fields_ = [("dst", vp), ("conv", vp), ("binv", vp), ("binvs", vp), ("k", vp), ("part_stride", C.c_uint64),
+                ("dbl", C.c_int32), ("pad", C.c_int32), ("alpha", vp), ("alphas", vp)]
+
+
+class KeyTab(C.Structure):
+    _fields_ = [("kb", vp), ("seed", vp), ("row_words", C.c_uint64), ("bits", C.c_int32), ("q_top", C.c_int32),
+                ("srows", C.c_int32), ("nregen", C.c_int32)]
+
+
+class KsRegenArgs(C.Structure):
+    _fields_ = [("ks", KsArgs), ("seed", vp), ("epi", EpiArgs), ("use_epi", C.c_int32), ("pad", C.c_int32),
+                ("key", KeyTab), ("add", vp)]
+
+
+class KskExpandArgs(C.Structure):
+    _fields_ = [("out", vp), ("seed", vp), ("prime_ids", vp), ("pr", vp), ("nmod", C.c_int32), ("dnum", C.c_int32),
+                ("d0", C.c_int32), ("pad", C.c_int32)]
+
+
+class TensorArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("d2", PolyRef), ("a0", PolyRef), ("b0", PolyRef), ("a1", PolyRef),
+                ("b1", PolyRef), ("coef", vp), ("coef_ct_stride", C.c_uint64), ("pr", vp), ("npairs", C.c_int32),
+                ("acc", C.c_int32), ("n", C.c_int32), ("K", C.c_int32), ("dbl", C.c_int32), ("acc_d2", C.c_int32)]
+
+
+class MdEpiArgs(C.Structure):
+    _fields_ = [("dst", PolyRef), ("x", PolyRef), ("t", PolyRef), ("binv", vp), ("binvs", vp), ("k", vp),
+                ("pr", vp), ("dbl", C.c_int32), ("n", C.c_int32), ("K", C.c_int32), ("pad", C.c_int32)]
+
+
+class RescaleArgs(C.Structure):
+    _fields_ = [("x", PolyRef), ("tmp", PolyRef), ("A", vp), ("B", vp), ("As", vp), ("Bs", vp), ("qam", vp),
+                ("qbm", vp), ("pr", vp), ("qinv_ab", C.c_uint64), ("C_ab", C.c_uint64), ("ca", C.c_uint64),
+                ("cb", C.c_uint64), ("top", C.c_int32), ("nrows", C.c_int32), ("K", C.c_int32), ("ndrop", C.c_int32)]
+
+
+class RescaleCombineArgs(C.Structure):
+    _fields_ = [("x", PolyRef), ("tmp", PolyRef), ("alpha", vp), ("alphas", vp), ("pr", vp), ("n", C.c_int32),
+                ("K", C.c_int32)]
+
+
+class AutomorphArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("in_", PolyRef), ("add", PolyRef), ("rs", RowSet), ("pr", vp), ("k", C.c_uint32),
+                ("K", C.c_int32), ("nparts", C.c_int32), ("has_add", C.c_int32)]
+
+
+class EncryptArgs(C.Structure):
+    _fields_ = [("c0", vp), ("c1", vp), ("s", vp), ("e", vp), ("m", vp), ("seed", vp), ("pr", vp),
+                ("nonce", C.c_uint32), ("nl", C.c_int32)]
+
+
+class KskGenArgs(C.Structure):
+    _fields_ = [("b", vp), ("a", vp), ("e", vp), ("s_new", vp), ("s_old", vp), ("seed", vp), ("ids", vp),
+                ("digit_of", vp), ("pmod", vp), ("pmods", vp), ("pr", vp), ("row_words", C.c_uint64),
+                ("nrows", C.c_int32), ("ndig", C.c_int32), ("nq", C.c_int32), ("bits", C.c_int32), ("sq", C.c_int32),
+                ("pad", C.c_int32)]
+
+
+LAUNCHERS = ["ntt_fwd", "ntt_inv", "bconv", "ew_add", "ew_scale", "ew_sub_mul", "ew_copy", "pt_dot", "ks_dot",
+             "ks_dot_regen", "ksk_expand", "cts_fused", "tensor", "md_epilogue", "wsum", "add_const", "mul_table",
+             "rescale_coef", "rescale_combine", "automorph", "encode", "encrypt", "ksk_gen", "ksk_unpack",
+             "mod_raise", "small_int", "spru_extract", "spru_fft_pass", "spru_scatter", "cts_fused_regen",
+             "ks_dot_key", "pcmm", "ccmm", "wsum_k", "rescale_combine_to", "md_epilogue_to", "small_int1",
+             "coeff_sum", "mul_add", "rescale_fwd", "mul_add_n", "tensor_y", "wsum_multi", "bconv_wide", "tfhe",
+             "tensor_sum", "tensor_multi", "tensor_seeded", "ew_many", "submul_many", "pack_split", "pack_dot"]
+LAUNCH = C.CFUNCTYPE(C.c_int, vp, vp)
+
+
+class KernelTable(C.Structure):
+    _fields_ = [("abi", C.c_uint32), ("word_bytes", C.c_uint32), ("mm", C.c_uint32), ("log_n", C.c_uint32)] + [
+        (n, LAUNCH) for n in LAUNCHERS]
+
+
+RING_LAUNCHERS = ["ntt_fwd", "ntt_inv", "ntt_fwd_g", "ntt_inv_g", "bconv", "ew_add", "ew_scale", "ew_sub_mul", "ew_copy"]
+
+
+class RingTable(C.Structure):
+    _fields_ = [("abi", C.c_uint32), ("word_bytes", C.c_uint32), ("mm", C.c_uint32), ("log_n", C.c_uint32)] + [
+        (n, LAUNCH) for n in RING_LAUNCHERS]
+
+
+class Params(C.Structure):
+    _fields_ = [("log_n", C.c_uint32), ("nq", C.c_int32), ("kp", C.c_int32), ("dnum", C.c_int32), ("q", u64p),
+                ("p", u64p), ("k_max", C.c_int32), ("pad", C.c_int32)]
+
+
+SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJob": 32, "BconvArgs": 56,
+         "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
+         "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
+         "EncryptArgs": 64, "KskGenArgs": 120, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
+
+_lib = None
+
+
+class PcbError(RuntimeError):
+    pass
+
+
+def lib():
+    """The loaded CUDA library (raises when it has not been built: no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise PcbError(f"{LIB_PATH} is missing: build it with `python perseus_b200/build.py` (no CPU fallback)")
+    L = C.CDLL(LIB_PATH)
+    i32, i64, u32, u64, dbl = C.c_int32, C.c_int64, C.c_uint32, C.c_uint64, C.c_double
+    sig = {
+        "pc_table_u64_barrett64": (C.POINTER(KernelTable), []),
+        "pc_ring_u64_14": (C.POINTER(RingTable), []),
+        "pc_ring_u64_16": (C.POINTER(RingTable), []),
+        "pcb_last_error": (C.c_char_p, []),
+        "pcb_ctx_bytes": (i64, [C.POINTER(Params), i32]),
+        "pcb_ctx_create": (C.c_int, [C.POINTER(Params), i32, vp, C.c_size_t, vp, C.POINTER(vp)]),
+        "pcb_ctx_destroy": (None, [vp]),
+        "pcb_ctx_rows": (C.c_int, [vp]),
+        "pcb_ctx_tables": (C.c_int, [vp] + [C.POINTER(vp)] * 7),
+        "pcb_keygen": (C.c_int, [vp, u64, u32, dbl, i32, u64p, vp]),
+        "pcb_key_ptrs": (C.c_int, [vp, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(u64)]),
+        "pcb_key_copy": (C.c_int, [vp, i32, vp, vp, vp]),
+        "pcb_encrypt": (C.c_int, [vp, C.POINTER(dbl), i32, i32, dbl, i32, vp, vp]),
+        "pcb_decrypt": (C.c_int, [vp, vp, i32, i32, dbl, C.POINTER(dbl), vp]),
+        "pcb_encode": (C.c_int, [vp, C.POINTER(dbl), i32, i32, dbl, i32, u64p]),
+        "pcb_pt_load": (C.c_int, [vp, u64p, i32, vp, vp]),
+        "pcb_add": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_sub": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_mult": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_rescale": (C.c_int, [vp, vp, i32, i32, vp]),
+        "pcb_rotate": (C.c_int, [vp, vp, i64, vp, i32, i32, vp]),
+        "pcb_rotate_and_sum": (C.c_int, [vp, vp, i64, i64, vp, i32, i32, vp]),
+        "pcb_mult_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_add_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
+        "pcb_ntt_batch": (C.c_int, [vp, vp, i32, i32, vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc, what=""):
+    if rc != 0:
+        msg = lib().pcb_last_error().decode(errors="replace")
+        raise PcbError(f"{what} failed ({rc}): {msg}")
+    return rc
+
+
+def kernel_table():
+    return lib().pc_table_u64_barrett64().contents
+
+
+def ring_table(log_n):
+    return (lib().pc_ring_u64_14() if log_n == 14 else lib().pc_ring_u64_16()).contents

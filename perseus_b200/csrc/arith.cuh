@@ -1,0 +1,101 @@
+// 64-bit modular arithmetic on the B200's integer pipes.
+//
+// Residues are uint64_t in [0, p) with p < 2^61 (the chains here use 50- and 60-bit primes). Constant operands
+// (twiddles, per-row scalars) use Shoup products with a precomputed companion w' = floor(w 2^64 / p); products of two
+// runtime residues and lazy sums of products go through a 128-bit accumulator reduced once by a double-word Barrett
+// step with mu = floor((2^128 - 1) / p) (the PrimeConst's mu_lo / mu_hi, crates/pc-kernels/kernels/args.cuh:26-37).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pcb200.h"
+
+namespace pcb {
+
+__device__ __forceinline__ uint64_t add_mod(uint64_t a, uint64_t b, uint64_t p) {
+    const uint64_t s = a + b;
+    return s >= p ? s - p : s;
+}
+__device__ __forceinline__ uint64_t sub_mod(uint64_t a, uint64_t b, uint64_t p) {
+    return a >= b ? a - b : a + p - b;
+}
+// a w mod p in [0, 2p) for any a < 2^64 (Shoup): the quotient estimate is low by at most one
+__device__ __forceinline__ uint64_t shoup_lazy(uint64_t a, uint64_t w, uint64_t ws, uint64_t p) {
+    const uint64_t q = __umul64hi(a, ws);
+    return a * w - q * p;
+}
+__device__ __forceinline__ uint64_t shoup(uint64_t a, uint64_t w, uint64_t ws, uint64_t p) {
+    const uint64_t r = shoup_lazy(a, w, ws, p);
+    return r >= p ? r - p : r;
+}
+
+// 128-bit accumulator: acc += a b with the carry chain in PTX (mad.lo.cc / madc.hi)
+struct Acc {
+    uint64_t lo, hi;
+};
+__device__ __forceinline__ void mac(Acc& acc, uint64_t a, uint64_t b) {
+    asm("mad.lo.cc.u64 %0, %2, %3, %0;\n\tmadc.hi.u64 %1, %2, %3, %1;"
+        : "+l"(acc.lo), "+l"(acc.hi)
+        : "l"(a), "l"(b));
+}
+__device__ __forceinline__ Acc mul_wide(uint64_t a, uint64_t b) { return Acc{a * b, __umul64hi(a, b)}; }
+
+// Exact x mod p for any 128-bit x, p < 2^62. q = floor(x mu / 2^128) estimated from the three upper partial
+// products (the dropped low product and carries make it low by at most 2); only q mod 2^64 matters because the true
+// remainder x - q p is below 4p < 2^64.
+__device__ __forceinline__ uint64_t reduce(Acc x, uint64_t p, uint64_t m0, uint64_t m1) {
+    const uint64_t t = __umul64hi(x.lo, m0);
+    uint64_t s_hi;
+    // s = x.hi m0 + x.lo m1 + t, we need its high word (mod 2^64)
+    asm("{\n\t"
+        ".reg .u64 l1, h1, l2, h2, sl;\n\t"
+        "mul.lo.u64 l1, %1, %2;\n\t"
+        "mul.hi.u64 h1, %1, %2;\n\t"
+        "mul.lo.u64 l2, %3, %4;\n\t"
+        "mul.hi.u64 h2, %3, %4;\n\t"
+        "add.cc.u64 sl, l1, l2;\n\t"
+        "addc.u64 %0, h1, h2;\n\t"
+        "add.cc.u64 sl, sl, %5;\n\t"
+        "addc.u64 %0, %0, 0;\n\t"
+        "}"
+        : "=l"(s_hi)
+        : "l"(x.hi), "l"(m0), "l"(x.lo), "l"(m1), "l"(t));
+    const uint64_t q = x.hi * m1 + s_hi;
+    uint64_t r = x.lo - q * p;
+    if (r >= p) r -= p;
+    if (r >= p) r -= p;
+    if (r >= p) r -= p;
+    return r;
+}
+__device__ __forceinline__ uint64_t reduce(Acc x, const PcbPrimeConst& c) { return reduce(x, c.p, c.mu_lo, c.mu_hi); }
+__device__ __forceinline__ uint64_t mul_mod(uint64_t a, uint64_t b, const PcbPrimeConst& c) {
+    return reduce(mul_wide(a, b), c);
+}
+
+// Source slot of sigma_k in the bit-reversed evaluation order (crates/pc-host/src/arith.rs:181-187):
+// brev(((2 brev(o) + 1) k mod 2N) >> 1)
+template <int LOGN>
+__device__ __forceinline__ uint32_t automorph_slot(uint32_t k, uint32_t o) {
+    const uint32_t j = __brev(o) >> (32 - LOGN);
+    const uint32_t r = (((j << 1) + 1) * k & ((2u << LOGN) - 1)) >> 1;
+    return __brev(r) >> (32 - LOGN);
+}
+__device__ __forceinline__ uint32_t automorph_slot_n(uint32_t k, uint32_t o, int logn) {
+    const uint32_t j = __brev(o) >> (32 - logn);
+    const uint32_t r = (((j << 1) + 1) * k & ((2u << logn) - 1)) >> 1;
+    return __brev(r) >> (32 - logn);
+}
+
+__device__ __forceinline__ const uint64_t* at_row(const PcbPolyRef& r, int c, int part, int row, int logn) {
+    return (const uint64_t*)r.base + (size_t)c * r.ct_stride + (size_t)part * r.part_stride + ((size_t)row << logn);
+}
+__device__ __forceinline__ uint64_t* at_row_w(const PcbPolyRef& r, int c, int part, int row, int logn) {
+    return (uint64_t*)r.base + (size_t)c * r.ct_stride + (size_t)part * r.part_stride + ((size_t)row << logn);
+}
+__device__ __forceinline__ int rs_row(const PcbRowSet& rs, int y) { return y < rs.nq ? y : rs.qmax + (y - rs.nq); }
+
+}  // namespace pcb
+
+// launcher return codes (crates/pc-kernels/kernels/args.cuh:1036)
+#define PCB_BAD_ARGS (-1)
+#define PCB_LAUNCH_RESULT() ((int)cudaGetLastError())

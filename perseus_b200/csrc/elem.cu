@@ -1,0 +1,294 @@
+// Element-wise kernels of the hot path: ew_* (row sets), tensor, md_epilogue, rescale_coef / rescale_combine,
+// automorph. Semantics of crates/pc-kernels/kernels/args.cuh (EwArgs :143-157, TensorArgs :355-367, MdEpiArgs
+// :438-447, RescaleArgs :525-572, AutomorphArgs :580-592); host twin crates/pc-host/src/{elem,rescale}.rs.
+//
+// All of these are HBM-bound streams: every thread moves 4 consecutive words (two 16-byte vector accesses per
+// operand), grids are (N / 1024, rows, ciphertexts x parts) so one launch covers a whole batch.
+#include "arith.cuh"
+
+namespace pcb {
+namespace elem {
+
+constexpr int BX = 256;
+constexpr int WPT = 4;  // words per thread
+
+struct V4 {
+    uint64_t v[4];
+};
+__device__ __forceinline__ V4 ld4(const uint64_t* p) {
+    const ulonglong2 a = ((const ulonglong2*)p)[0], b = ((const ulonglong2*)p)[1];
+    return V4{{a.x, a.y, b.x, b.y}};
+}
+__device__ __forceinline__ void st4(uint64_t* p, const uint64_t (&r)[4]) {
+    ((ulonglong2*)p)[0] = make_ulonglong2(r[0], r[1]);
+    ((ulonglong2*)p)[1] = make_ulonglong2(r[2], r[3]);
+}
+
+enum EwOp { EW_ADD = 0, EW_SCALE = 1, EW_SUB_MUL = 2, EW_COPY = 3 };
+
+template <int LOGN, int OP>
+__global__ void __launch_bounds__(BX) ew(PcbEwArgs a) {
+    const int row = rs_row(a.rs, blockIdx.y);
+    const int c = blockIdx.z / a.nparts, part = blockIdx.z % a.nparts;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    uint64_t* o = at_row_w(a.out, c, part, row, LOGN) + i;
+    uint64_t r[4];
+    if (OP == EW_COPY) {
+        const V4 x = ld4(at_row(a.a, c, part, row, LOGN) + i);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r[w] = x.v[w];
+        st4(o, r);
+        return;
+    }
+    const uint64_t p = a.pr[row].p;
+    if (OP == EW_SCALE && a.zero_p && (int)blockIdx.y >= a.rs.nq) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r[w] = 0;
+        st4(o, r);
+        return;
+    }
+    const V4 x = ld4(at_row(a.a, c, part, row, LOGN) + i);
+    if (OP == EW_SCALE) {
+        const uint64_t s = ((const uint64_t*)a.sc)[row], ss = ((const uint64_t*)a.scs)[row];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r[w] = shoup(x.v[w], s, ss, p);
+    } else {
+        const V4 y = ld4(at_row(a.b, c, part, row, LOGN) + i);
+        if (OP == EW_ADD) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) r[w] = a.sub ? sub_mod(x.v[w], y.v[w], p) : add_mod(x.v[w], y.v[w], p);
+        } else {
+            const uint64_t s = ((const uint64_t*)a.sc)[row], ss = ((const uint64_t*)a.scs)[row];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) r[w] = shoup(sub_mod(x.v[w], y.v[w], p), s, ss, p);
+        }
+    }
+    st4(o, r);
+}
+
+template <int LOGN, int OP>
+int ew_launch(const PcbEwArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbEwArgs& a = *ap;
+    const int rows = a.rs.nq + a.rs.np;
+    if (a.K < 0 || a.nparts < 1 || a.rs.nq < 0 || a.rs.np < 0 || !a.out.base || !a.a.base) return PCB_BAD_ARGS;
+    if (OP != EW_COPY && !a.pr) return PCB_BAD_ARGS;
+    if ((OP == EW_ADD || OP == EW_SUB_MUL) && !a.b.base) return PCB_BAD_ARGS;
+    if ((OP == EW_SCALE || OP == EW_SUB_MUL) && (!a.sc || !a.scs)) return PCB_BAD_ARGS;
+    if (rows == 0 || a.K == 0) return 0;
+    ew<LOGN, OP><<<dim3((1 << LOGN) / (BX * WPT), rows, a.K * a.nparts), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+// ------------------------------------------------------------------------------------------------ tensor
+// (c0, c1, d2) = sum over up to two pairs (a, b) of (a0 b0, a0 b1 + a1 b0, a1 b1): lazy 128-bit sums, one reduction
+template <int LOGN>
+__global__ void __launch_bounds__(BX) tensor(PcbTensorArgs a) {
+    const int row = blockIdx.y, c = blockIdx.z;
+    const PcbPrimeConst& pc = a.pr[row];
+    const uint64_t p = pc.p;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    Acc s0[4], s1[4], s2[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) s0[w] = s1[w] = s2[w] = Acc{0, 0};
+    for (int j = 0; j < a.npairs && j < 2; ++j) {
+        const PcbPolyRef& x = j ? a.a1 : a.a0;
+        const PcbPolyRef& y = j ? a.b1 : a.b0;
+        const V4 x0 = ld4(at_row(x, c, 0, row, LOGN) + i), x1 = ld4(at_row(x, c, 1, row, LOGN) + i);
+        const V4 y0 = ld4(at_row(y, c, 0, row, LOGN) + i), y1 = ld4(at_row(y, c, 1, row, LOGN) + i);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            mac(s0[w], x0.v[w], y0.v[w]);
+            mac(s1[w], x0.v[w], y1.v[w]);
+            mac(s1[w], x1.v[w], y0.v[w]);
+            mac(s2[w], x1.v[w], y1.v[w]);
+        }
+    }
+    uint64_t r0[4], r1[4], r2[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        r0[w] = reduce(s0[w], pc);
+        r1[w] = reduce(s1[w], pc);
+        r2[w] = reduce(s2[w], pc);
+    }
+    uint64_t* o0 = at_row_w(a.out, c, 0, row, LOGN) + i;
+    uint64_t* o1 = at_row_w(a.out, c, 1, row, LOGN) + i;
+    uint64_t* o2 = at_row_w(a.d2, c, 1, row, LOGN) + i;
+    if (a.acc) {
+        const V4 d0 = ld4(o0), d1 = ld4(o1);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            r0[w] = add_mod(r0[w], d0.v[w], p);
+            r1[w] = add_mod(r1[w], d1.v[w], p);
+        }
+    }
+    if (a.acc_d2) {
+        const V4 d2 = ld4(o2);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r2[w] = add_mod(r2[w], d2.v[w], p);
+    }
+    if (a.dbl) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            r0[w] = add_mod(r0[w], r0[w], p);
+            r1[w] = add_mod(r1[w], r1[w], p);
+            r2[w] = add_mod(r2[w], r2[w], p);
+        }
+    }
+    st4(o0, r0);
+    st4(o1, r1);
+    st4(o2, r2);
+    if (a.coef) st4((uint64_t*)a.coef + (size_t)c * a.coef_ct_stride + ((size_t)row << LOGN) + i, r2);
+}
+
+template <int LOGN>
+int tensor_launch(const PcbTensorArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbTensorArgs& a = *ap;
+    if (a.npairs < 1 || a.npairs > 2 || a.n < 0 || a.K < 0 || !a.pr || !a.out.base || !a.d2.base || !a.a0.base ||
+        !a.b0.base || (a.npairs == 2 && (!a.a1.base || !a.b1.base)))
+        return PCB_BAD_ARGS;
+    if (a.n == 0 || a.K == 0) return 0;
+    tensor<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+// ------------------------------------------------------------------------------------------------ md_epilogue
+// parts 0, 1 of K cts over Q rows [0, n): dst = f (dst + (x - t) binv) [+ k on part 0]
+template <int LOGN>
+__global__ void __launch_bounds__(BX) md_epilogue(PcbMdEpiArgs a) {
+    const int row = blockIdx.y, c = blockIdx.z >> 1, part = blockIdx.z & 1;
+    const uint64_t p = a.pr[row].p;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    uint64_t* d = at_row_w(a.dst, c, part, row, LOGN) + i;
+    const uint64_t bi = ((const uint64_t*)a.binv)[row], bis = ((const uint64_t*)a.binvs)[row];
+    uint64_t kk = 0;
+    const bool addk = a.k && part == 0;
+    if (addk) {
+        kk = ((const uint64_t*)a.k)[row];
+        kk = kk >= p ? kk - p : kk;
+    }
+    const V4 x = ld4(at_row(a.x, c, part, row, LOGN) + i), t = ld4(at_row(a.t, c, part, row, LOGN) + i), dv = ld4(d);
+    uint64_t r[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        r[w] = add_mod(dv.v[w], shoup(sub_mod(x.v[w], t.v[w], p), bi, bis, p), p);
+        if (a.dbl) r[w] = add_mod(r[w], r[w], p);
+        if (addk) r[w] = add_mod(r[w], kk, p);
+    }
+    st4(d, r);
+}
+
+template <int LOGN>
+int md_epilogue_launch(const PcbMdEpiArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbMdEpiArgs& a = *ap;
+    if (a.n < 0 || a.K < 0 || !a.pr || !a.dst.base || !a.x.base || !a.t.base || !a.binv || !a.binvs) return PCB_BAD_ARGS;
+    if (a.n == 0 || a.K == 0) return 0;
+    md_epilogue<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, 2 * a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+// ------------------------------------------------------------------------------------------------ rescale
+// ndrop 1 (the u64 chains here have one prime per level): tmp_i = A_i lift(y_top) with lift(y) = y - q_top when
+// y > q_top / 2, reduced mod q_i (crates/pc-host/src/rescale.rs:54-70)
+template <int LOGN>
+__global__ void __launch_bounds__(BX) rescale_coef(PcbRescaleArgs a) {
+    const int c = blockIdx.z >> 1, part = blockIdx.z & 1;
+    const size_t i = (size_t)blockIdx.x * BX + threadIdx.x;
+    const PcbPrimeConst& pa = a.pr[a.top];
+    const uint64_t qa = pa.p;
+    uint64_t ya = at_row(a.x, c, part, a.top, LOGN)[i];
+    if (a.ca != 1) ya = mul_mod(ya, a.ca, pa);
+    const bool neg = ya > (qa >> 1);
+    const uint64_t* Av = (const uint64_t*)a.A;
+    const uint64_t* As = (const uint64_t*)a.As;
+    const uint64_t* qam = (const uint64_t*)a.qam;
+    for (int row = blockIdx.y; row < a.nrows; row += gridDim.y) {
+        const PcbPrimeConst& pq = a.pr[row];
+        const uint64_t q = pq.p;
+        uint64_t l = ya < q ? ya : (ya < 2 * q ? ya - q : reduce(Acc{ya, 0}, pq));
+        if (neg) l = sub_mod(l, qam[row], q);
+        at_row_w(a.tmp, c, part, row, LOGN)[i] = shoup(l, Av[row], As[row], q);
+    }
+}
+
+template <int LOGN>
+int rescale_coef_launch(const PcbRescaleArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbRescaleArgs& a = *ap;
+    if (a.ndrop != 1) return PCB_BAD_ARGS;  // two-prime (composite) levels are not part of the u64 chains here
+    if (a.top < 1 || a.nrows < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.A || !a.As || !a.qam)
+        return PCB_BAD_ARGS;
+    if (a.nrows == 0 || a.K == 0) return 0;
+    const int gy = a.nrows < 8 ? a.nrows : 8;
+    rescale_coef<LOGN><<<dim3((1 << LOGN) / BX, gy, 2 * a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+__global__ void __launch_bounds__(BX) rescale_combine(PcbRescaleCombineArgs a) {
+    const int row = blockIdx.y, c = blockIdx.z >> 1, part = blockIdx.z & 1;
+    const uint64_t p = a.pr[row].p;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    uint64_t* d = at_row_w(a.x, c, part, row, LOGN) + i;
+    const uint64_t al = ((const uint64_t*)a.alpha)[row], als = ((const uint64_t*)a.alphas)[row];
+    const V4 x = ld4(d), t = ld4(at_row(a.tmp, c, part, row, LOGN) + i);
+    uint64_t r[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) r[w] = add_mod(shoup(x.v[w], al, als, p), t.v[w], p);
+    st4(d, r);
+}
+
+template <int LOGN>
+int rescale_combine_launch(const PcbRescaleCombineArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbRescaleCombineArgs& a = *ap;
+    if (a.n < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.alpha || !a.alphas) return PCB_BAD_ARGS;
+    if (a.n == 0 || a.K == 0) return 0;
+    rescale_combine<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, 2 * a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+// ------------------------------------------------------------------------------------------------ automorph
+// out[o] = in[automorph_slot(k, o)] (+ add[o]): aligned 32-slot runs of o map to aligned 32-slot runs of the source,
+// so the gather stays sector-coalesced
+template <int LOGN, bool ADD>
+__global__ void __launch_bounds__(BX) automorph(PcbAutomorphArgs a) {
+    const int row = rs_row(a.rs, blockIdx.y);
+    const int c = blockIdx.z / a.nparts, part = blockIdx.z % a.nparts;
+    const uint32_t o = blockIdx.x * BX + threadIdx.x;
+    uint64_t v = at_row(a.in, c, part, row, LOGN)[automorph_slot<LOGN>(a.k, o)];
+    if (ADD) v = add_mod(v, at_row(a.add, c, part, row, LOGN)[o], a.pr[row].p);
+    at_row_w(a.out, c, part, row, LOGN)[o] = v;
+}
+
+template <int LOGN>
+int automorph_launch(const PcbAutomorphArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbAutomorphArgs& a = *ap;
+    if ((a.k & 1u) == 0 || a.K < 0 || a.nparts < 1 || !a.out.base || !a.in.base || (a.has_add && (!a.add.base || !a.pr)))
+        return PCB_BAD_ARGS;
+    const int rows = a.rs.nq + a.rs.np;
+    if (rows == 0 || a.K == 0) return 0;
+    const dim3 g((1 << LOGN) / BX, rows, a.K * a.nparts);
+    if (a.has_add) automorph<LOGN, true><<<g, BX, 0, s>>>(a);
+    else automorph<LOGN, false><<<g, BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+#define PCB_INST(L)                                                                                  \
+    template int ew_launch<L, EW_ADD>(const PcbEwArgs*, cudaStream_t);                               \
+    template int ew_launch<L, EW_SCALE>(const PcbEwArgs*, cudaStream_t);                             \
+    template int ew_launch<L, EW_SUB_MUL>(const PcbEwArgs*, cudaStream_t);                           \
+    template int ew_launch<L, EW_COPY>(const PcbEwArgs*, cudaStream_t);                              \
+    template int tensor_launch<L>(const PcbTensorArgs*, cudaStream_t);                               \
+    template int md_epilogue_launch<L>(const PcbMdEpiArgs*, cudaStream_t);                           \
+    template int rescale_coef_launch<L>(const PcbRescaleArgs*, cudaStream_t);                        \
+    template int rescale_combine_launch<L>(const PcbRescaleCombineArgs*, cudaStream_t);              \
+    template int automorph_launch<L>(const PcbAutomorphArgs*, cudaStream_t);
+PCB_INST(14)
+PCB_INST(16)
+
+}  // namespace elem
+}  // namespace pcb

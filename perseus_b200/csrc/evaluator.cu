@@ -1,0 +1,1136 @@
+// The evaluator: context, device-resident keys and the ciphertext ops of the hot path, behind the pcb_* C ABI.
+//
+// Restates the orchestration of the reference's device runtime (crates/pc-gpu): the per-level key-switching plans
+// of ks.rs:602-677 (level_specs_with), ModUp = INTT with the digit pre factor folded in (ks.rs:954-980) -> one
+// conversion launch over every live digit -> NTT of the targets (ks.rs:1037-1043), the inner product (ks.rs:1109),
+// ModDown = INTT of the special rows -> conversion P -> Q -> NTT whose epilogue writes (x - conv) P^-1 (ks.rs:
+// 1604-1656); relinearized products (relin.rs:84-134), rotations (rotate.rs:147-204, 924-992), the rescale
+// (rescale.rs:230), encryption (encrypt.rs:93-134) and key generation (keygen.rs:184-284).
+//
+// All device memory comes from one caller-owned arena carved at creation (the frozen arena of
+// crates/pc-cuda/src/lib.rs:9-10); the context never allocates device memory itself. Every op is stream-ordered on
+// the caller's stream and batches K ciphertexts per launch.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <string>
+#include <vector>
+
+#include "arith.cuh"
+#include "host_math.h"
+#include "kernels.h"
+
+namespace pcb {
+const PcbKernelTable* table_for(int logn);
+}
+
+using namespace pcb;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+#define CK(call)                                                                                  \
+    do {                                                                                          \
+        int _rc = (int)(call);                                                                    \
+        if (_rc != 0) return fail(_rc, "%s failed with %d (%s:%d)", #call, _rc, __FILE__, __LINE__); \
+    } while (0)
+
+// Bump allocator over the caller's arena; in measuring mode it only counts bytes.
+struct Arena {
+    char* base = nullptr;
+    size_t cap = 0, used = 0;
+    bool measure = true;
+    template <class T>
+    T* take(size_t count) {
+        used = (used + 255) & ~(size_t)255;
+        T* p = measure ? nullptr : (T*)(base + used);
+        used += count * sizeof(T);
+        return p;
+    }
+};
+
+struct LevelPlan {
+    int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0;
+    // ModUp: INTT rows (out of place, last pass x N^-1 pre_t), conversion jobs, NTT of the targets
+    uint32_t *mu_intt_roff = nullptr, *mu_intt_soff = nullptr;
+    int32_t* mu_intt_rprime = nullptr;
+    uint64_t *mu_intt_es = nullptr, *mu_intt_ess = nullptr;
+    PcbBconvJob* mu_jobs = nullptr;
+    uint64_t* mu_pool = nullptr;
+    uint32_t* mu_ntt_roff = nullptr;
+    int32_t* mu_ntt_rprime = nullptr;
+    uint32_t* ks_rows = nullptr;
+    // ModDown: INTT of the special rows (N^-1 pre_j), conversion P -> Q rows 0..top, NTT + epilogue
+    uint32_t* md_intt_roff = nullptr;
+    int32_t* md_intt_rprime = nullptr;
+    uint64_t *md_es = nullptr, *md_ess = nullptr;
+    PcbBconvJob* md_jobs = nullptr;
+    uint64_t* md_pool = nullptr;
+    uint32_t* md_ntt_roff = nullptr;
+    int32_t* md_ntt_rprime = nullptr;
+    // rescale by q_top: INTT of the top rows, correction rows, NTT + combine epilogue
+    uint32_t* rs_intt_roff = nullptr;
+    int32_t* rs_intt_rprime = nullptr;
+    uint32_t* rs_ntt_roff = nullptr;
+    int32_t* rs_ntt_rprime = nullptr;
+    uint64_t *rs_A = nullptr, *rs_As = nullptr, *rs_qam = nullptr, *rs_alpha = nullptr, *rs_alphas = nullptr;
+};
+
+struct KeySlot {
+    uint64_t galois = 0, autok = 1;
+    uint64_t *b = nullptr, *a = nullptr;
+    uint32_t* seed = nullptr;
+    const void** kb = nullptr;  // device arrays of one pointer (KsArgs kb / ka)
+    const void** ka = nullptr;
+    uint32_t* autok_dev = nullptr;
+};
+
+}  // namespace
+
+struct PcbCtx {
+    int logn = 0;
+    size_t n = 0;
+    int nq = 0, kp = 0, rows = 0, dnum = 0, alpha = 0, k_max = 0, nkeys = 0;
+    std::vector<uint64_t> primes;
+    const PcbKernelTable* tab = nullptr;
+    Arena arena;
+    // device tables
+    PcbPrimeConst* pr = nullptr;
+    uint64_t *fw = nullptr, *fws = nullptr, *iw = nullptr, *iws = nullptr, *ninv = nullptr, *ninvs = nullptr;
+    int32_t* digit_of = nullptr;
+    uint64_t *pmod = nullptr, *pmods = nullptr, *pinv = nullptr, *pinvs = nullptr;
+    uint32_t* id_roff = nullptr;   // i
+    int32_t* id_rprime = nullptr;  // i mod rows (keys, secret) — see id_rprime_q for batches
+    int32_t* id_rprime_q = nullptr;
+    uint32_t* key_roff = nullptr;
+    int32_t* key_rprime = nullptr;
+    std::vector<LevelPlan> lv;
+    // workspaces
+    uint64_t *coef = nullptr, *digits = nullptr, *ext = nullptr, *conv = nullptr, *dbuf = nullptr, *row = nullptr;
+    // keys and session
+    std::vector<KeySlot> keys;
+    int nkeys_made = 0;
+    uint64_t* s_eval = nullptr;
+    uint32_t* enc_seed = nullptr;
+    std::vector<int8_t> secret;
+    hm::Drbg* drbg = nullptr;
+    hm::Gauss* gauss = nullptr;
+    uint32_t nonce = 0;
+    hm::Encoder* enc = nullptr;
+    ~PcbCtx() {
+        delete drbg;
+        delete gauss;
+        delete enc;
+    }
+    size_t ct_words() const { return 2 * (size_t)rows * n; }
+    int live_digits(int top) const { return top / alpha + 1; }
+    void digit_range(int d, int top, int& lo, int& hi) const {
+        lo = d * alpha;
+        hi = std::min(std::min((d + 1) * alpha, nq), top + 1);
+    }
+};
+
+namespace {
+
+template <class T>
+int upload(T* dst, const std::vector<T>& v, cudaStream_t s) {
+    if (!dst || v.empty()) return 0;
+    return (int)cudaMemcpyAsync(dst, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, s);
+}
+
+uint64_t prod_mod(const std::vector<uint64_t>& ps, int skip, uint64_t t) {
+    uint64_t v = 1 % t;
+    for (size_t k = 0; k < ps.size(); ++k)
+        if ((int)k != skip) v = hm::mulmod(v, ps[k] % t, t);
+    return v;
+}
+
+// One conversion job's pool words (crates/pc-kernels/kernels/args.cuh:114-118): src rows, src primes, pre, target
+// rows, target primes, M[i][t] = (B / b_i) mod t
+void job_pool(const std::vector<uint64_t>& primes, const std::vector<int>& src, const std::vector<int>& tgt,
+              std::vector<uint64_t>& pool) {
+    std::vector<uint64_t> bp;
+    for (int s : src) bp.push_back(primes[s]);
+    for (int s : src) pool.push_back((uint64_t)s);
+    for (int s : src) pool.push_back((uint64_t)s);
+    for (size_t i = 0; i < src.size(); ++i)
+        pool.push_back(hm::invmod(prod_mod(bp, (int)i, bp[i]), bp[i]));
+    for (int t : tgt) pool.push_back((uint64_t)t);
+    for (int t : tgt) pool.push_back((uint64_t)t);
+    for (size_t i = 0; i < src.size(); ++i)
+        for (int t : tgt) pool.push_back(prod_mod(bp, (int)i, primes[t]));
+}
+
+// Carve (or measure) every device buffer and fill the tables. Host tables are built only when not measuring.
+int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
+    Arena& A = c.arena;
+    const bool fill = !A.measure;
+    const size_t n = c.n;
+    const int rows = c.rows, nq = c.nq, kp = c.kp, km = c.k_max, L = c.logn;
+    const uint32_t m = 2u << L;
+    // primes and NTT tables
+    c.pr = A.take<PcbPrimeConst>(rows);
+    c.fw = A.take<uint64_t>((size_t)rows * n);
+    c.fws = A.take<uint64_t>((size_t)rows * n);
+    c.iw = A.take<uint64_t>((size_t)rows * n);
+    c.iws = A.take<uint64_t>((size_t)rows * n);
+    c.ninv = A.take<uint64_t>(rows);
+    c.ninvs = A.take<uint64_t>(rows);
+    if (fill) {
+        std::vector<PcbPrimeConst> pr(rows);
+        std::vector<uint64_t> ni(rows), nis(rows);
+        for (int r = 0; r < rows; ++r) {
+            pr[r] = hm::prime_const(c.primes[r]);
+            ni[r] = hm::invmod(n % c.primes[r], c.primes[r]);
+            nis[r] = hm::shoup_of(ni[r], c.primes[r]);
+        }
+        CK(upload(c.pr, pr, s));
+        CK(upload(c.ninv, ni, s));
+        CK(upload(c.ninvs, nis, s));
+        std::vector<uint64_t> w(n), ws(n), iw(n), iws(n), pw(n), ipw(n);
+        for (int r = 0; r < rows; ++r) {
+            const uint64_t p = c.primes[r], psi = hm::min_root(m, p), ipsi = hm::invmod(psi, p);
+            if (!psi) return fail(PCB_BAD_ARGS, "prime %llu has no primitive %u-th root of unity", (unsigned long long)p, m);
+            pw[0] = ipw[0] = 1;
+            for (size_t i = 1; i < n; ++i) {
+                pw[i] = hm::mulmod(pw[i - 1], psi, p);
+                ipw[i] = hm::mulmod(ipw[i - 1], ipsi, p);
+            }
+            for (size_t i = 0; i < n; ++i) {
+                const uint32_t b = hm::bitrev((uint32_t)i, L);
+                w[i] = pw[b];
+                iw[i] = ipw[b];
+                ws[i] = hm::shoup_of(w[i], p);
+                iws[i] = hm::shoup_of(iw[i], p);
+            }
+            CK(cudaMemcpyAsync(c.fw + (size_t)r * n, w.data(), n * 8, cudaMemcpyHostToDevice, s));
+            CK(cudaMemcpyAsync(c.fws + (size_t)r * n, ws.data(), n * 8, cudaMemcpyHostToDevice, s));
+            CK(cudaMemcpyAsync(c.iw + (size_t)r * n, iw.data(), n * 8, cudaMemcpyHostToDevice, s));
+            CK(cudaMemcpyAsync(c.iws + (size_t)r * n, iws.data(), n * 8, cudaMemcpyHostToDevice, s));
+            CK(cudaStreamSynchronize(s));  // the host staging vectors are reused per prime
+        }
+    }
+    // digit map, P mod q, P^-1 mod q
+    c.digit_of = A.take<int32_t>(rows);
+    c.pmod = A.take<uint64_t>(rows);
+    c.pmods = A.take<uint64_t>(rows);
+    c.pinv = A.take<uint64_t>(rows);
+    c.pinvs = A.take<uint64_t>(rows);
+    std::vector<uint64_t> P(c.primes.begin() + nq, c.primes.end());
+    if (fill) {
+        std::vector<int32_t> dof(rows, -1);
+        std::vector<uint64_t> pm(rows, 0), pms(rows, 0), pi(rows, 0), pis(rows, 0);
+        for (int t = 0; t < nq; ++t) {
+            const uint64_t q = c.primes[t];
+            dof[t] = t / c.alpha;
+            pm[t] = prod_mod(P, -1, q);
+            pms[t] = hm::shoup_of(pm[t], q);
+            pi[t] = hm::invmod(pm[t], q);
+            pis[t] = hm::shoup_of(pi[t], q);
+        }
+        CK(upload(c.digit_of, dof, s));
+        CK(upload(c.pmod, pm, s));
+        CK(upload(c.pmods, pms, s));
+        CK(upload(c.pinv, pi, s));
+        CK(upload(c.pinvs, pis, s));
+    }
+    // identity row tables: batches up to k_max cts x 2 parts x rows
+    const size_t nid = (size_t)km * 2 * rows;
+    c.id_roff = A.take<uint32_t>(nid);
+    c.id_rprime = A.take<int32_t>(nid);
+    c.id_rprime_q = A.take<int32_t>(nid);
+    c.key_roff = A.take<uint32_t>((size_t)c.dnum * rows);
+    c.key_rprime = A.take<int32_t>((size_t)c.dnum * rows);
+    if (fill) {
+        std::vector<uint32_t> ro(nid);
+        std::vector<int32_t> rp(nid), rq(nid);
+        for (size_t i = 0; i < nid; ++i) {
+            ro[i] = (uint32_t)i;
+            rp[i] = (int32_t)(i % rows);
+            rq[i] = (int32_t)(i % nq);
+        }
+        CK(upload(c.id_roff, ro, s));
+        CK(upload(c.id_rprime, rp, s));
+        CK(upload(c.id_rprime_q, rq, s));
+        std::vector<uint32_t> kro((size_t)c.dnum * rows);
+        std::vector<int32_t> krp((size_t)c.dnum * rows);
+        for (int d = 0; d < c.dnum; ++d)
+            for (int r = 0; r < rows; ++r) {
+                kro[(size_t)d * rows + r] = (uint32_t)(d * rows + r);
+                krp[(size_t)d * rows + r] = r;
+            }
+        CK(upload(c.key_roff, kro, s));
+        CK(upload(c.key_rprime, krp, s));
+    }
+    // per-level plans (crates/pc-gpu/src/ks.rs:602-677)
+    c.lv.assign(nq, LevelPlan());
+    std::vector<uint64_t> preP(kp);
+    for (int j = 0; j < kp; ++j) preP[j] = hm::invmod(prod_mod(P, j, P[j]), P[j]);
+    for (int top = 0; top < nq; ++top) {
+        LevelPlan& l = c.lv[top];
+        l.top = top;
+        l.ndig = c.live_digits(top);
+        const int T = top + 1;
+        // ModUp INTT
+        l.mu_intt_roff = A.take<uint32_t>((size_t)km * T);
+        l.mu_intt_soff = A.take<uint32_t>((size_t)km * T);
+        l.mu_intt_rprime = A.take<int32_t>((size_t)km * T);
+        l.mu_intt_es = A.take<uint64_t>((size_t)km * T);
+        l.mu_intt_ess = A.take<uint64_t>((size_t)km * T);
+        // targets of every live digit
+        std::vector<std::vector<int>> src(l.ndig), tgt(l.ndig);
+        for (int d = 0; d < l.ndig; ++d) {
+            int lo, hi;
+            c.digit_range(d, top, lo, hi);
+            for (int t = lo; t < hi; ++t) src[d].push_back(t);
+            for (int t = 0; t <= top; ++t)
+                if (t < lo || t >= hi) tgt[d].push_back(t);
+            for (int j = 0; j < kp; ++j) tgt[d].push_back(nq + j);
+            l.mu_max_tgt = std::max(l.mu_max_tgt, (int)tgt[d].size());
+        }
+        l.mu_rows = 0;
+        for (int d = 0; d < l.ndig; ++d) l.mu_rows += (int)tgt[d].size();
+        std::vector<uint64_t> pool;
+        std::vector<uint32_t> pool_off(l.ndig);
+        for (int d = 0; d < l.ndig; ++d) {
+            pool_off[d] = (uint32_t)pool.size();
+            job_pool(c.primes, src[d], tgt[d], pool);
+        }
+        l.mu_jobs = A.take<PcbBconvJob>((size_t)km * l.ndig);
+        l.mu_pool = A.take<uint64_t>(pool.size());
+        l.mu_ntt_roff = A.take<uint32_t>((size_t)km * l.mu_rows);
+        l.mu_ntt_rprime = A.take<int32_t>((size_t)km * l.mu_rows);
+        l.ks_rows = A.take<uint32_t>(T + kp);
+        // ModDown
+        l.md_intt_roff = A.take<uint32_t>((size_t)km * 2 * kp);
+        l.md_intt_rprime = A.take<int32_t>((size_t)km * 2 * kp);
+        l.md_es = A.take<uint64_t>((size_t)km * 2 * kp);
+        l.md_ess = A.take<uint64_t>((size_t)km * 2 * kp);
+        std::vector<int> psrc, qtgt;
+        for (int j = 0; j < kp; ++j) psrc.push_back(nq + j);
+        for (int t = 0; t <= top; ++t) qtgt.push_back(t);
+        std::vector<uint64_t> mdpool;
+        job_pool(c.primes, psrc, qtgt, mdpool);
+        l.md_jobs = A.take<PcbBconvJob>((size_t)km * 2);
+        l.md_pool = A.take<uint64_t>(mdpool.size());
+        l.md_ntt_roff = A.take<uint32_t>((size_t)km * 2 * T);
+        l.md_ntt_rprime = A.take<int32_t>((size_t)km * 2 * T);
+        // rescale
+        l.rs_intt_roff = A.take<uint32_t>((size_t)km * 2);
+        l.rs_intt_rprime = A.take<int32_t>((size_t)km * 2);
+        l.rs_ntt_roff = A.take<uint32_t>((size_t)km * 2 * (top ? top : 1));
+        l.rs_ntt_rprime = A.take<int32_t>((size_t)km * 2 * (top ? top : 1));
+        l.rs_A = A.take<uint64_t>(rows);
+        l.rs_As = A.take<uint64_t>(rows);
+        l.rs_qam = A.take<uint64_t>(rows);
+        l.rs_alpha = A.take<uint64_t>(rows);
+        l.rs_alphas = A.take<uint64_t>(rows);
+        if (!fill) continue;
+        // ModUp tables: row (c, t) of the coefficient workspace [c][rows] reads part 1 of ct c ([c][2][rows])
+        std::vector<uint32_t> ro, so;
+        std::vector<int32_t> rp;
+        std::vector<uint64_t> es, ess;
+        std::vector<uint64_t> pre(T);
+        for (int d = 0; d < l.ndig; ++d) {
+            std::vector<uint64_t> bp;
+            for (int t : src[d]) bp.push_back(c.primes[t]);
+            for (size_t i = 0; i < src[d].size(); ++i) pre[src[d][i]] = hm::invmod(prod_mod(bp, (int)i, bp[i]), bp[i]);
+        }
+        for (int cc = 0; cc < km; ++cc)
+            for (int t = 0; t <= top; ++t) {
+                const uint64_t q = c.primes[t];
+                ro.push_back((uint32_t)(cc * rows + t));
+                so.push_back((uint32_t)(cc * 2 * rows + t));
+                rp.push_back(t);
+                const uint64_t v = hm::mulmod(hm::invmod(n % q, q), pre[t], q);
+                es.push_back(v);
+                ess.push_back(hm::shoup_of(v, q));
+            }
+        CK(upload(l.mu_intt_roff, ro, s));
+        CK(upload(l.mu_intt_soff, so, s));
+        CK(upload(l.mu_intt_rprime, rp, s));
+        CK(upload(l.mu_intt_es, es, s));
+        CK(upload(l.mu_intt_ess, ess, s));
+        std::vector<PcbBconvJob> jobs;
+        std::vector<uint32_t> nro;
+        std::vector<int32_t> nrp;
+        for (int cc = 0; cc < km; ++cc)
+            for (int d = 0; d < l.ndig; ++d) {
+                PcbBconvJob j;
+                j.src_off = (uint32_t)(cc * rows);
+                j.dst_off = (uint32_t)((cc * c.dnum + d) * rows);
+                j.nsrc = (uint32_t)src[d].size();
+                j.ntgt = (uint32_t)tgt[d].size();
+                j.pool_off = pool_off[d];
+                j.exact = 0;
+                j.prescaled = 1;
+                j.split = 0;
+                jobs.push_back(j);
+                for (int t : tgt[d]) {
+                    nro.push_back(j.dst_off + (uint32_t)t);
+                    nrp.push_back(t);
+                }
+            }
+        CK(upload(l.mu_jobs, jobs, s));
+        CK(upload(l.mu_pool, pool, s));
+        CK(upload(l.mu_ntt_roff, nro, s));
+        CK(upload(l.mu_ntt_rprime, nrp, s));
+        std::vector<uint32_t> ksr;
+        for (int t = 0; t <= top; ++t) ksr.push_back((uint32_t)t);
+        for (int j = 0; j < kp; ++j) ksr.push_back((uint32_t)(nq + j));
+        CK(upload(l.ks_rows, ksr, s));
+        // ModDown tables over the extended ciphertext layout [c][2][rows]
+        std::vector<uint32_t> mro;
+        std::vector<int32_t> mrp;
+        std::vector<uint64_t> mes, mess;
+        for (int cc = 0; cc < km; ++cc)
+            for (int part = 0; part < 2; ++part)
+                for (int j = 0; j < kp; ++j) {
+                    mro.push_back((uint32_t)((2 * cc + part) * rows + nq + j));
+                    mrp.push_back(nq + j);
+                    const uint64_t p = P[j], v = hm::mulmod(hm::invmod(n % p, p), preP[j], p);
+                    mes.push_back(v);
+                    mess.push_back(hm::shoup_of(v, p));
+                }
+        CK(upload(l.md_intt_roff, mro, s));
+        CK(upload(l.md_intt_rprime, mrp, s));
+        CK(upload(l.md_es, mes, s));
+        CK(upload(l.md_ess, mess, s));
+        std::vector<PcbBconvJob> mj;
+        std::vector<uint32_t> qro;
+        std::vector<int32_t> qrp;
+        for (int cc = 0; cc < km; ++cc)
+            for (int part = 0; part < 2; ++part) {
+                PcbBconvJob j;
+                j.src_off = j.dst_off = (uint32_t)((2 * cc + part) * rows);
+                j.nsrc = (uint32_t)kp;
+                j.ntgt = (uint32_t)T;
+                j.pool_off = 0;
+                j.exact = 0;
+                j.prescaled = 1;
+                j.split = 0;
+                mj.push_back(j);
+                for (int t = 0; t <= top; ++t) {
+                    qro.push_back(j.dst_off + (uint32_t)t);
+                    qrp.push_back(t);
+                }
+            }
+        CK(upload(l.md_jobs, mj, s));
+        CK(upload(l.md_pool, mdpool, s));
+        CK(upload(l.md_ntt_roff, qro, s));
+        CK(upload(l.md_ntt_rprime, qrp, s));
+        // rescale tables (ndrop 1; crates/pc-kernels/kernels/args.cuh:530-552)
+        std::vector<uint32_t> rro, nro2;
+        std::vector<int32_t> rrp, nrp2;
+        for (int cc = 0; cc < km; ++cc)
+            for (int part = 0; part < 2; ++part) {
+                rro.push_back((uint32_t)((2 * cc + part) * rows + top));
+                rrp.push_back(top);
+                for (int i = 0; i < top; ++i) {
+                    nro2.push_back((uint32_t)((2 * cc + part) * rows + i));
+                    nrp2.push_back(i);
+                }
+            }
+        if (top == 0) {
+            nro2.assign((size_t)km * 2, 0);
+            nrp2.assign((size_t)km * 2, 0);
+        }
+        CK(upload(l.rs_intt_roff, rro, s));
+        CK(upload(l.rs_intt_rprime, rrp, s));
+        CK(upload(l.rs_ntt_roff, nro2, s));
+        CK(upload(l.rs_ntt_rprime, nrp2, s));
+        std::vector<uint64_t> Av(rows, 0), Asv(rows, 0), qam(rows, 0), al(rows, 0), als(rows, 0);
+        const uint64_t qa = c.primes[top];
+        for (int i = 0; i < top; ++i) {
+            const uint64_t q = c.primes[i];
+            al[i] = hm::invmod(qa % q, q);
+            als[i] = hm::shoup_of(al[i], q);
+            Av[i] = (q - al[i]) % q;
+            Asv[i] = hm::shoup_of(Av[i], q);
+            qam[i] = qa % q;
+        }
+        CK(upload(l.rs_A, Av, s));
+        CK(upload(l.rs_As, Asv, s));
+        CK(upload(l.rs_qam, qam, s));
+        CK(upload(l.rs_alpha, al, s));
+        CK(upload(l.rs_alphas, als, s));
+        CK(cudaStreamSynchronize(s));
+    }
+    // workspaces: coefficients [k][rows], ModUp digits [k][dnum][rows], extended / conversion / d2 in ct layout
+    c.coef = A.take<uint64_t>((size_t)km * rows * n);
+    c.digits = A.take<uint64_t>((size_t)km * c.dnum * rows * n);
+    c.ext = A.take<uint64_t>((size_t)km * c.ct_words());
+    c.conv = A.take<uint64_t>((size_t)km * c.ct_words());
+    c.dbuf = A.take<uint64_t>((size_t)km * c.ct_words());
+    c.row = A.take<uint64_t>(n);
+    // keys and the session secret
+    c.keys.assign(nkeys, KeySlot());
+    for (int k = 0; k < nkeys; ++k) {
+        KeySlot& ks = c.keys[k];
+        ks.b = A.take<uint64_t>((size_t)c.dnum * rows * n);
+        ks.a = A.take<uint64_t>((size_t)c.dnum * rows * n);
+        ks.seed = A.take<uint32_t>(8);
+        ks.kb = A.take<const void*>(1);
+        ks.ka = A.take<const void*>(1);
+        ks.autok_dev = A.take<uint32_t>(1);
+        if (fill) {
+            std::vector<const void*> pb{ks.b}, pa{ks.a};
+            CK(upload(ks.kb, pb, s));
+            CK(upload(ks.ka, pa, s));
+        }
+    }
+    c.s_eval = A.take<uint64_t>((size_t)rows * n);
+    c.enc_seed = A.take<uint32_t>(8);
+    if (fill) CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+// ------------------------------------------------------------------------------------------------ launch helpers
+PcbNttArgs ntt_args(const PcbCtx& c, void* base, const uint32_t* roff, const int32_t* rprime, int nrows) {
+    PcbNttArgs a;
+    memset(&a, 0, sizeof a);
+    a.base = base;
+    a.roff = roff;
+    a.rprime = rprime;
+    a.fw = c.fw;
+    a.fws = c.fws;
+    a.iw = c.iw;
+    a.iws = c.iws;
+    a.ninv = c.ninv;
+    a.ninvs = c.ninvs;
+    a.pr = c.pr;
+    a.nrows = nrows;
+    a.snum = 1;
+    a.xnum = 1;
+    return a;
+}
+
+PcbPolyRef ct_ref(const PcbCtx& c, const void* base) {
+    PcbPolyRef r;
+    r.base = (void*)base;
+    r.ct_stride = c.ct_words();
+    r.part_stride = (uint64_t)c.rows * c.n;
+    return r;
+}
+
+int check_top(const PcbCtx& c, int top, int K) {
+    if (top < 0 || top >= c.nq) return fail(PCB_BAD_ARGS, "top limb %d outside [0, %d)", top, c.nq);
+    if (K < 1 || K > c.k_max) return fail(PCB_BAD_ARGS, "batch of %d ciphertexts outside [1, k_max = %d]", K, c.k_max);
+    return 0;
+}
+
+// ModUp of the c1 parts of K cts (ct layout at `x`, part 1 read) into the digits workspace
+int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
+    const LevelPlan& l = c.lv[top];
+    const int T = top + 1;
+    PcbNttArgs a = ntt_args(c, c.coef, l.mu_intt_roff, l.mu_intt_rprime, K * T);
+    a.src = c1;
+    a.soff = l.mu_intt_soff;
+    a.es = l.mu_intt_es;
+    a.ess = l.mu_intt_ess;
+    CK(c.tab->ntt_inv(&a, s));
+    PcbBconvArgs b;
+    memset(&b, 0, sizeof b);
+    b.src = c.coef;
+    b.dst = c.digits;
+    b.jobs = l.mu_jobs;
+    b.pool = l.mu_pool;
+    b.pr = c.pr;
+    b.njobs = K * l.ndig;
+    b.max_tgt = l.mu_max_tgt;
+    CK(c.tab->bconv(&b, s));
+    PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
+    CK(c.tab->ntt_fwd(&f, s));
+    return 0;
+}
+
+// key inner product of K cts against key `ks` into c.ext: c1 / c0 in ct layout (c0 mode 1 adds P c0 on Q rows)
+int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, int c0_mode, int top, int K,
+        cudaStream_t s) {
+    const LevelPlan& l = c.lv[top];
+    const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
+    for (int c0i = 0; c0i < K; c0i += 8) {
+        const int kk = std::min(8, K - c0i);
+        PcbKsArgs a;
+        memset(&a, 0, sizeof a);
+        a.c1 = c1 + c0i * cw;
+        a.modup = c.digits + (size_t)c0i * c.dnum * rn;
+        a.c0 = c0 ? c0 + c0i * cw : nullptr;
+        a.out0 = c.ext + c0i * cw;
+        a.out1 = c.ext + c0i * cw + rn;
+        a.kb = ks.kb;
+        a.ka = ks.ka;
+        a.autok = ks.autok_dev;
+        a.rows = l.ks_rows;
+        a.digit_of = c.digit_of;
+        a.pmod = c.pmod;
+        a.pmods = c.pmods;
+        a.pr = c.pr;
+        a.ct_stride = cw;
+        a.mu_ct_stride = (uint64_t)c.dnum * rn;
+        a.mu_digit_stride = rn;
+        a.out_ct_stride = cw;
+        a.out_rot_stride = 0;
+        a.key_digit_stride = rn;
+        a.K = kk;
+        a.R = 1;
+        a.ndig = l.ndig;
+        a.c0_mode = c0_mode;
+        a.nq = c.nq;
+        a.nrows = top + 1 + c.kp;
+        CK(c.tab->ks_dot(&a, s));
+    }
+    return 0;
+}
+
+// ModDown of c.ext (K cts) into out: epi 1 (out = (x - conv) P^-1) or 2 (out += ...)
+int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStream_t s) {
+    const LevelPlan& l = c.lv[top];
+    PcbNttArgs a = ntt_args(c, c.ext, l.md_intt_roff, l.md_intt_rprime, K * 2 * c.kp);
+    a.es = l.md_es;
+    a.ess = l.md_ess;
+    CK(c.tab->ntt_inv(&a, s));
+    PcbBconvArgs b;
+    memset(&b, 0, sizeof b);
+    b.src = c.ext;
+    b.dst = c.conv;
+    b.jobs = l.md_jobs;
+    b.pool = l.md_pool;
+    b.pr = c.pr;
+    b.njobs = 2 * K;
+    b.max_tgt = top + 1;
+    CK(c.tab->bconv(&b, s));
+    PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
+    f.epi = accumulate ? 2 : 1;
+    f.eout = out;
+    f.ex = c.ext;
+    f.es = c.pinv;
+    f.ess = c.pinvs;
+    CK(c.tab->ntt_fwd(&f, s));
+    return 0;
+}
+
+const KeySlot* key_of(const PcbCtx& c, uint64_t g) {
+    for (int k = 0; k < c.nkeys_made; ++k)
+        if (c.keys[k].galois == g) return &c.keys[k];
+    return nullptr;
+}
+
+uint64_t rot_galois(const PcbCtx& c, int64_t step) {
+    const int64_t h = (int64_t)c.n / 2;
+    return hm::powmod(5, (uint64_t)(((step % h) + h) % h), 2 * c.n);
+}
+
+__global__ void dec_row0(const uint64_t* c0, const uint64_t* c1, const uint64_t* s, uint64_t* out, PcbPrimeConst pc) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    out[i] = add_mod(c0[i], mul_mod(c1[i], s[i], pc), pc.p);
+}
+
+template <int LOGN, bool ADD>
+__global__ void pt_op(PcbPolyRef out, PcbPolyRef x, const uint64_t* pt, const PcbPrimeConst* pr) {
+    const int row = blockIdx.y, cc = blockIdx.z >> 1, part = blockIdx.z & 1;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const PcbPrimeConst& pc = pr[row];
+    const uint64_t v = at_row(x, cc, part, row, LOGN)[i];
+    const uint64_t w = pt[((size_t)row << LOGN) + i];
+    uint64_t r;
+    if (ADD) r = part == 0 ? add_mod(v, w, pc.p) : v;
+    else r = mul_mod(v, w, pc);
+    at_row_w(out, cc, part, row, LOGN)[i] = r;
+}
+
+template <bool ADD>
+int launch_pt_op(PcbCtx& c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int top, int K, cudaStream_t s) {
+    const dim3 g((unsigned)(c.n / 256), top + 1, 2 * K);
+    if (c.logn == 14) pt_op<14, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
+    else pt_op<16, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+// ================================================================================================ C API
+extern "C" {
+
+const char* pcb_last_error(void) { return g_err.c_str(); }
+
+static int init_ctx(PcbCtx& c, const PcbParams* prm, int nkeys) {
+    if (!prm) return fail(PCB_BAD_ARGS, "null params");
+    if (prm->log_n != 14 && prm->log_n != 16) return fail(PCB_BAD_ARGS, "log_n %u (14 or 16)", prm->log_n);
+    if (prm->nq < 1 || prm->kp < 1 || prm->dnum < 1 || prm->dnum > 16 || prm->dnum > prm->nq || !prm->q || !prm->p)
+        return fail(PCB_BAD_ARGS, "nq %d, kp %d, dnum %d", prm->nq, prm->kp, prm->dnum);
+    if (prm->k_max < 1 || prm->k_max > 256 || nkeys < 0) return fail(PCB_BAD_ARGS, "k_max %d, nkeys %d", prm->k_max, nkeys);
+    c.logn = (int)prm->log_n;
+    c.n = (size_t)1 << c.logn;
+    c.nq = prm->nq;
+    c.kp = prm->kp;
+    c.rows = c.nq + c.kp;
+    c.dnum = prm->dnum;
+    c.alpha = (c.nq + c.dnum - 1) / c.dnum;
+    if (c.nq <= c.alpha * (c.dnum - 1)) return fail(PCB_BAD_ARGS, "%d limbs do not split into %d digits", c.nq, c.dnum);
+    if (c.alpha > 16 || c.kp > 16) return fail(PCB_BAD_ARGS, "digits of %d limbs / %d special primes (max 16)", c.alpha, c.kp);
+    c.k_max = prm->k_max;
+    c.nkeys = nkeys;
+    c.primes.assign(prm->q, prm->q + c.nq);
+    c.primes.insert(c.primes.end(), prm->p, prm->p + c.kp);
+    for (uint64_t p : c.primes)
+        if (p < 3 || !(p & 1) || p >= (1ull << 61) || (p - 1) % (2 * c.n))
+            return fail(PCB_BAD_ARGS, "prime %llu is not an odd NTT prime below 2^61 (p = 1 mod 2N)", (unsigned long long)p);
+    c.tab = table_for(c.logn);
+    return 0;
+}
+
+int64_t pcb_ctx_bytes(const PcbParams* prm, int32_t nkeys) {
+    PcbCtx c;
+    int rc = init_ctx(c, prm, nkeys);
+    if (rc) return rc;
+    c.arena.measure = true;
+    rc = layout(c, nkeys, nullptr);
+    if (rc) return rc;
+    return (int64_t)c.arena.used + 256;
+}
+
+int pcb_ctx_create(const PcbParams* prm, int32_t nkeys, void* arena, size_t arena_bytes, cudaStream_t stream,
+                   PcbCtx** out) {
+    if (!out) return fail(PCB_BAD_ARGS, "null output");
+    *out = nullptr;
+    PcbCtx* c = new PcbCtx();
+    int rc = init_ctx(*c, prm, nkeys);
+    if (rc) {
+        delete c;
+        return rc;
+    }
+    const int64_t need = pcb_ctx_bytes(prm, nkeys);
+    if (!arena || (int64_t)arena_bytes < need) {
+        delete c;
+        return fail(PCB_BAD_ARGS, "arena of %zu bytes, %lld needed", arena_bytes, (long long)need);
+    }
+    c->arena.base = (char*)(((uintptr_t)arena + 255) & ~(uintptr_t)255);
+    c->arena.cap = arena_bytes - (size_t)(c->arena.base - (char*)arena);
+    c->arena.measure = false;
+    c->enc = new hm::Encoder(c->n);
+    rc = layout(*c, nkeys, stream);
+    if (rc) {
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return 0;
+}
+
+void pcb_ctx_destroy(PcbCtx* ctx) { delete ctx; }
+int pcb_ctx_rows(const PcbCtx* ctx) { return ctx ? ctx->rows : PCB_BAD_ARGS; }
+
+int pcb_ctx_tables(const PcbCtx* c, const PcbPrimeConst** pr, const uint64_t** fw, const uint64_t** fws,
+                   const uint64_t** iw, const uint64_t** iws, const uint64_t** ninv, const uint64_t** ninvs) {
+    if (!c) return fail(PCB_BAD_ARGS, "null context");
+    if (pr) *pr = c->pr;
+    if (fw) *fw = c->fw;
+    if (fws) *fws = c->fws;
+    if (iw) *iw = c->iw;
+    if (iws) *iws = c->iws;
+    if (ninv) *ninv = c->ninv;
+    if (ninvs) *ninvs = c->ninvs;
+    return 0;
+}
+
+int pcb_keygen(PcbCtx* c, uint64_t seed, uint32_t h, double sigma, int32_t ngal, const uint64_t* galois,
+               cudaStream_t s) {
+    if (!c) return fail(PCB_BAD_ARGS, "null context");
+    if (ngal < 0 || ngal > c->nkeys || (ngal && !galois))
+        return fail(PCB_BAD_ARGS, "%d keys requested, the context holds %d", ngal, c->nkeys);
+    if (!(sigma > 0.0 && sigma < 1e6)) return fail(PCB_BAD_ARGS, "sigma %g", sigma);
+    const size_t n = c->n;
+    const int rows = c->rows;
+    const uint32_t key0[8] = {0x5e551013u, (uint32_t)seed, (uint32_t)(seed >> 32), 4, 5, 6, 7, 8};
+    delete c->drbg;
+    delete c->gauss;
+    c->drbg = new hm::Drbg(key0, 0);
+    c->gauss = new hm::Gauss(sigma);
+    c->secret.assign(n, 0);
+    if (h == 0) hm::ternary(*c->drbg, n, c->secret.data());
+    else if (!hm::sparse_ternary(*c->drbg, n, h, c->secret.data()))
+        return fail(PCB_BAD_ARGS, "Hamming weight %u > N", h);
+    // the secret in evaluation form over every prime id
+    std::vector<uint64_t> host((size_t)rows * n);
+    for (int r = 0; r < rows; ++r)
+        for (size_t i = 0; i < n; ++i)
+            host[(size_t)r * n + i] = c->secret[i] < 0 ? c->primes[r] - 1 : (uint64_t)c->secret[i];
+    CK(cudaMemcpyAsync(c->s_eval, host.data(), host.size() * 8, cudaMemcpyHostToDevice, s));
+    PcbNttArgs a = ntt_args(*c, c->s_eval, c->id_roff, c->id_rprime, rows);
+    CK(c->tab->ntt_fwd(&a, s));
+    CK(cudaStreamSynchronize(s));
+    c->nkeys_made = 0;
+    std::vector<uint64_t> err((size_t)c->dnum * rows * n);
+    for (int gi = 0; gi < ngal; ++gi) {
+        KeySlot& k = c->keys[gi];
+        k.galois = galois[gi] % (2 * n);
+        if (!(k.galois & 1)) return fail(PCB_BAD_ARGS, "galois element %llu is even", (unsigned long long)galois[gi]);
+        k.autok = hm::powmod(k.galois, (2 * n >> 2) - 1, 2 * n);
+        uint32_t kseed[8], sub[8];
+        c->drbg->seed8(kseed);
+        c->drbg->seed8(sub);
+        for (int d = 0; d < c->dnum; ++d) {
+            hm::Drbg g(sub, (uint32_t)d);
+            std::vector<int64_t> e(n);
+            for (size_t i = 0; i < n; ++i) e[i] = c->gauss->draw(g);
+            for (int r = 0; r < rows; ++r) {
+                const int64_t p = (int64_t)c->primes[r];
+                uint64_t* o = &err[((size_t)d * rows + r) * n];
+                for (size_t i = 0; i < n; ++i) {
+                    const int64_t v = e[i] % p;
+                    o[i] = (uint64_t)(v < 0 ? v + p : v);
+                }
+            }
+        }
+        std::vector<uint32_t> sd(kseed, kseed + 8), ak{(uint32_t)k.autok};
+        CK(upload(k.seed, sd, s));
+        CK(upload(k.autok_dev, ak, s));
+        CK(cudaMemcpyAsync(c->digits, err.data(), err.size() * 8, cudaMemcpyHostToDevice, s));
+        PcbNttArgs e = ntt_args(*c, c->digits, c->key_roff, c->key_rprime, c->dnum * rows);
+        CK(c->tab->ntt_fwd(&e, s));
+        const uint64_t* s_new = c->s_eval;
+        if (k.galois != 1) {
+            // sigma_{g^-1}(s): the rotation key switches s to it (crates/pc-gpu/src/keygen.rs:235-256)
+            PcbAutomorphArgs am;
+            memset(&am, 0, sizeof am);
+            am.out = ct_ref(*c, c->coef);
+            am.in = ct_ref(*c, c->s_eval);
+            am.rs.nq = rows;
+            am.pr = c->pr;
+            am.k = (uint32_t)k.autok;
+            am.K = 1;
+            am.nparts = 1;
+            CK(c->tab->automorph(&am, s));
+            s_new = c->coef;
+        }
+        PcbKskGenArgs g;
+        memset(&g, 0, sizeof g);
+        g.b = k.b;
+        g.a = k.a;
+        g.e = c->digits;
+        g.s_new = s_new;
+        g.s_old = c->s_eval;
+        g.seed = k.seed;
+        g.ids = c->id_rprime;
+        g.digit_of = c->digit_of;
+        g.pmod = c->pmod;
+        g.pmods = c->pmods;
+        g.pr = c->pr;
+        g.nrows = rows;
+        g.ndig = c->dnum;
+        g.nq = c->nq;
+        g.sq = k.galois == 1;
+        CK(c->tab->ksk_gen(&g, s));
+        CK(cudaStreamSynchronize(s));
+        c->nkeys_made = gi + 1;
+    }
+    uint32_t es[8];
+    c->drbg->seed8(es);
+    std::vector<uint32_t> esv(es, es + 8);
+    CK(upload(c->enc_seed, esv, s));
+    c->nonce = 0;
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int pcb_key_ptrs(const PcbCtx* c, int32_t idx, const uint64_t** b, const uint64_t** a, uint64_t* galois) {
+    if (!c || idx < 0 || idx >= c->nkeys_made) return fail(PCB_BAD_ARGS, "no key %d", idx);
+    if (b) *b = c->keys[idx].b;
+    if (a) *a = c->keys[idx].a;
+    if (galois) *galois = c->keys[idx].galois;
+    return 0;
+}
+
+int pcb_key_copy(const PcbCtx* c, int32_t idx, uint64_t* b_out, uint64_t* a_out, cudaStream_t s) {
+    if (!c || idx < 0 || idx >= c->nkeys_made) return fail(PCB_BAD_ARGS, "no key %d", idx);
+    const size_t bytes = (size_t)c->dnum * c->rows * c->n * 8;
+    if (b_out) CK(cudaMemcpyAsync(b_out, c->keys[idx].b, bytes, cudaMemcpyDeviceToDevice, s));
+    if (a_out) CK(cudaMemcpyAsync(a_out, c->keys[idx].a, bytes, cudaMemcpyDeviceToDevice, s));
+    return 0;
+}
+
+int pcb_encode(PcbCtx* c, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
+               uint64_t* rows) {
+    if (!c || !rows || (nvals && !vals)) return fail(PCB_BAD_ARGS, "null argument");
+    if (nslots < 1 || (nslots & (nslots - 1)) || (size_t)nslots > c->n / 2 || nvals < 0 || nvals > nslots)
+        return fail(PCB_BAD_ARGS, "%d values into %d slots", nvals, nslots);
+    if (top < 0 || top >= c->nq) return fail(PCB_BAD_ARGS, "top %d", top);
+    std::vector<hm::i128> co;
+    if (!c->enc->encode(vals, nvals, nslots, scale, co)) return fail(-2, "scaled value exceeds 2^126");
+    for (int r = 0; r <= top; ++r)
+        for (size_t k = 0; k < c->n; ++k) rows[(size_t)r * c->n + k] = hm::mod_i128(co[k], c->primes[r]);
+    return 0;
+}
+
+int pcb_encrypt(PcbCtx* c, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top, uint64_t* ct,
+                cudaStream_t s) {
+    if (!c || !ct) return fail(PCB_BAD_ARGS, "null argument");
+    if (!c->drbg) return fail(-3, "no session keys (pcb_keygen first)");
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    const size_t n = c->n;
+    std::vector<uint64_t> m((size_t)(top + 1) * n);
+    rc = pcb_encode(c, vals, nvals, nslots, scale, top, m.data());
+    if (rc) return rc;
+    std::vector<int64_t> e(n);
+    for (size_t i = 0; i < n; ++i) e[i] = c->gauss->draw(*c->drbg);
+    for (int r = 0; r <= top; ++r) {
+        const int64_t p = (int64_t)c->primes[r];
+        for (size_t i = 0; i < n; ++i) {
+            const int64_t v = e[i] % p;
+            const uint64_t ev = (uint64_t)(v < 0 ? v + p : v);
+            uint64_t& x = m[(size_t)r * n + i];
+            x = (x + ev) % (uint64_t)p;
+        }
+    }
+    CK(cudaMemcpyAsync(ct, m.data(), m.size() * 8, cudaMemcpyHostToDevice, s));
+    PcbNttArgs a = ntt_args(*c, ct, c->id_roff, c->id_rprime, top + 1);
+    CK(c->tab->ntt_fwd(&a, s));
+    PcbEncryptArgs ea;
+    memset(&ea, 0, sizeof ea);
+    ea.c0 = ct;
+    ea.c1 = ct + (size_t)c->rows * n;
+    ea.s = c->s_eval;
+    ea.e = ct;
+    ea.seed = c->enc_seed;
+    ea.pr = c->pr;
+    ea.nonce = c->nonce++;
+    ea.nl = top + 1;
+    CK(c->tab->encrypt(&ea, s));
+    CK(cudaStreamSynchronize(s));  // the host staging rows go out of scope
+    return 0;
+}
+
+int pcb_decrypt(PcbCtx* c, const uint64_t* ct, int32_t top, int32_t nslots, double scale, double* vals,
+                cudaStream_t s) {
+    if (!c || !ct || !vals) return fail(PCB_BAD_ARGS, "null argument");
+    if (c->secret.empty()) return fail(-3, "no secret (pcb_keygen first)");
+    if (nslots < 1 || (nslots & (nslots - 1)) || (size_t)nslots > c->n / 2) return fail(PCB_BAD_ARGS, "slots %d", nslots);
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    const size_t n = c->n;
+    const PcbPrimeConst pc = hm::prime_const(c->primes[0]);
+    dec_row0<<<(unsigned)(n / 256), 256, 0, s>>>(ct, ct + (size_t)c->rows * n, c->s_eval, c->row, pc);
+    CK(cudaGetLastError());
+    PcbNttArgs a = ntt_args(*c, c->row, c->id_roff, c->id_rprime, 1);
+    CK(c->tab->ntt_inv(&a, s));
+    std::vector<uint64_t> m(n);
+    CK(cudaMemcpyAsync(m.data(), c->row, n * 8, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    const uint64_t q0 = c->primes[0];
+    std::vector<hm::i128> co(n);
+    for (size_t k = 0; k < n; ++k) co[k] = m[k] > q0 / 2 ? -(hm::i128)(q0 - m[k]) : (hm::i128)m[k];
+    c->enc->decode(co, nslots, scale, vals);
+    return 0;
+}
+
+int pcb_pt_load(PcbCtx* c, const uint64_t* rows_host, int32_t top, uint64_t* pt, cudaStream_t s) {
+    if (!c || !rows_host || !pt) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(pt, rows_host, (size_t)(top + 1) * c->n * 8, cudaMemcpyHostToDevice, s));
+    PcbNttArgs a = ntt_args(*c, pt, c->id_roff, c->id_rprime, top + 1);
+    CK(c->tab->ntt_fwd(&a, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+static int ew_ct(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int top, int K, int sub,
+                 cudaStream_t s) {
+    if (!c || !a || !b || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    PcbEwArgs e;
+    memset(&e, 0, sizeof e);
+    e.out = ct_ref(*c, out);
+    e.a = ct_ref(*c, a);
+    e.b = ct_ref(*c, b);
+    e.rs.nq = top + 1;
+    e.pr = c->pr;
+    e.K = K;
+    e.nparts = 2;
+    e.sub = sub;
+    CK(c->tab->ew_add(&e, s));
+    return 0;
+}
+int pcb_add(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    return ew_ct(c, a, b, out, top, K, 0, s);
+}
+int pcb_sub(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    return ew_ct(c, a, b, out, top, K, 1, s);
+}
+
+int pcb_mult(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !a || !b || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    const KeySlot* k = key_of(*c, 1);
+    if (!k) return fail(-3, "no relinearization key");
+    // tensor: (c0, c1) into out, d2 into part 1 of the d2 workspace (ct layout), then out += KS(d2)
+    PcbTensorArgs t;
+    memset(&t, 0, sizeof t);
+    t.out = ct_ref(*c, out);
+    t.d2 = ct_ref(*c, c->dbuf);
+    t.a0 = ct_ref(*c, a);
+    t.b0 = ct_ref(*c, b);
+    t.pr = c->pr;
+    t.npairs = 1;
+    t.n = top + 1;
+    t.K = K;
+    CK(c->tab->tensor(&t, s));
+    const uint64_t* d2 = c->dbuf + (size_t)c->rows * c->n;
+    rc = modup(*c, d2, top, K, s);
+    if (rc) return rc;
+    rc = dot(*c, *k, d2, nullptr, 0, top, K, s);
+    if (rc) return rc;
+    return moddown(*c, out, true, top, K, s);
+}
+
+int pcb_rescale(PcbCtx* c, uint64_t* ct, int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !ct) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    if (top < 1) return fail(PCB_BAD_ARGS, "rescale at the bottom limb");
+    const LevelPlan& l = c->lv[top];
+    // INTT of the top rows (out of place into the conversion workspace)
+    PcbNttArgs a = ntt_args(*c, c->conv, l.rs_intt_roff, l.rs_intt_rprime, 2 * K);
+    a.src = ct;
+    a.soff = l.rs_intt_roff;
+    CK(c->tab->ntt_inv(&a, s));
+    PcbRescaleArgs r;
+    memset(&r, 0, sizeof r);
+    r.x = ct_ref(*c, c->conv);
+    r.tmp = ct_ref(*c, c->conv);
+    r.A = l.rs_A;
+    r.As = l.rs_As;
+    r.qam = l.rs_qam;
+    r.pr = c->pr;
+    r.ca = r.cb = 1;
+    r.top = top;
+    r.nrows = top;
+    r.K = K;
+    r.ndrop = 1;
+    CK(c->tab->rescale_coef(&r, s));
+    // NTT of the correction rows; the epilogue combines x_i = alpha_i x_i + tmp_i (epi 3)
+    PcbNttArgs f = ntt_args(*c, c->conv, l.rs_ntt_roff, l.rs_ntt_rprime, 2 * K * top);
+    f.epi = 3;
+    f.eout = ct;
+    f.ex = ct;
+    f.es = l.rs_alpha;
+    f.ess = l.rs_alphas;
+    CK(c->tab->ntt_fwd(&f, s));
+    return 0;
+}
+
+int pcb_keyswitch(PcbCtx* c, const uint64_t* d, const uint64_t* c0, int32_t c0_mode, int32_t kidx, uint32_t autok,
+                  uint64_t* out, int32_t top, int32_t K, uint64_t in_stride, cudaStream_t s) {
+    if (!c || !d || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    if (in_stride != 0 && in_stride != c->ct_words())
+        return fail(PCB_BAD_ARGS, "input polynomials must sit one ciphertext layout apart");
+    if (kidx < 0 || kidx >= c->nkeys_made) return fail(-3, "no key %d", kidx);
+    if ((c0_mode != 0 && c0_mode != 1) || (c0_mode && !c0)) return fail(PCB_BAD_ARGS, "c0 mode %d", c0_mode);
+    KeySlot k = c->keys[kidx];
+    if (autok != k.autok) return fail(PCB_BAD_ARGS, "autok %u differs from the key's %llu", autok, (unsigned long long)k.autok);
+    rc = modup(*c, d, top, K, s);
+    if (rc) return rc;
+    rc = dot(*c, k, d, c0, c0_mode, top, K, s);
+    if (rc) return rc;
+    return moddown(*c, out, false, top, K, s);
+}
+
+int pcb_rotate(PcbCtx* c, const uint64_t* x, int64_t step, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !x || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (x == out) return fail(PCB_BAD_ARGS, "rotate: out must not alias x");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    const uint64_t g = rot_galois(*c, step);
+    if (g == 1) {
+        // rotation by a multiple of N/2 is the identity (crates/pc-gpu/src/rotate.rs:190-192): a copy
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, out);
+        e.a = ct_ref(*c, x);
+        e.rs.nq = top + 1;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+        return 0;
+    }
+    const KeySlot* k = key_of(*c, g);
+    if (!k) return fail(-3, "no rotation key for step %lld (galois %llu)", (long long)step, (unsigned long long)g);
+    const uint64_t* c1 = x + (size_t)c->rows * c->n;
+    rc = modup(*c, c1, top, K, s);
+    if (rc) return rc;
+    rc = dot(*c, *k, c1, x, 1, top, K, s);
+    if (rc) return rc;
+    return moddown(*c, out, false, top, K, s);
+}
+
+int pcb_rotate_and_sum(PcbCtx* c, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int32_t top, int32_t K,
+                       cudaStream_t s) {
+    if (!c || !x || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (start == 0 || stop <= 0) return fail(PCB_BAD_ARGS, "start %lld must be non-zero, stop %lld positive", (long long)start, (long long)stop);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    // out = x, then out += rot(out, sign g) for g = |start|, 2|start|, .. < stop; the rotation lands in dbuf
+    if (out != x) {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, out);
+        e.a = ct_ref(*c, x);
+        e.rs.nq = top + 1;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+    }
+    const int64_t sign = start < 0 ? -1 : 1;
+    for (int64_t g = start < 0 ? -start : start; g < stop; g *= 2) {
+        rc = pcb_rotate(c, out, sign * g, c->dbuf, top, K, s);
+        if (rc) return rc;
+        rc = pcb_add(c, out, c->dbuf, out, top, K, s);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int pcb_mult_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
+                cudaStream_t s) {
+    if (!c || !x || !pt || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    CK(launch_pt_op<false>(*c, x, pt, out, top, K, s));
+    return 0;
+}
+
+int pcb_add_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
+               cudaStream_t s) {
+    if (!c || !x || !pt || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    CK(launch_pt_op<true>(*c, x, pt, out, top, K, s));
+    return 0;
+}
+
+int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaStream_t s) {
+    if (!c || !x) return fail(PCB_BAD_ARGS, "null argument");
+    if (nrows < 0 || nrows > c->k_max * 2 * c->rows)
+        return fail(PCB_BAD_ARGS, "%d rows (row tables hold %d)", nrows, c->k_max * 2 * c->rows);
+    PcbNttArgs a = ntt_args(*c, x, c->id_roff, c->id_rprime_q, nrows);
+    CK(inverse ? c->tab->ntt_inv(&a, s) : c->tab->ntt_fwd(&a, s));
+    return 0;
+}
+
+}  // extern "C"

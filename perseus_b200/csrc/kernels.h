@@ -1,0 +1,28 @@
+// Internal declarations of the launchers (one instantiation per ring size LOGN in {14, 16}).
+#pragma once
+#include "../../include/pcb200.h"
+
+namespace pcb {
+namespace ntt {
+template <int LOGN> int fwd(const PcbNttArgs*, cudaStream_t);
+template <int LOGN> int inv(const PcbNttArgs*, cudaStream_t);
+}  // namespace ntt
+namespace elem {
+enum EwOpDecl { ADD = 0, SCALE = 1, SUB_MUL = 2, COPY = 3 };
+template <int LOGN, int OP> int ew_launch(const PcbEwArgs*, cudaStream_t);
+template <int LOGN> int tensor_launch(const PcbTensorArgs*, cudaStream_t);
+template <int LOGN> int md_epilogue_launch(const PcbMdEpiArgs*, cudaStream_t);
+template <int LOGN> int rescale_coef_launch(const PcbRescaleArgs*, cudaStream_t);
+template <int LOGN> int rescale_combine_launch(const PcbRescaleCombineArgs*, cudaStream_t);
+template <int LOGN> int automorph_launch(const PcbAutomorphArgs*, cudaStream_t);
+}  // namespace elem
+namespace ks {
+template <int LOGN> int bconv_launch(const PcbBconvArgs*, cudaStream_t);
+template <int LOGN> int ks_dot_launch(const PcbKsArgs*, cudaStream_t);
+}  // namespace ks
+namespace keys {
+template <int LOGN> int ksk_expand_launch(const PcbKskExpandArgs*, cudaStream_t);
+template <int LOGN> int encrypt_launch(const PcbEncryptArgs*, cudaStream_t);
+template <int LOGN> int ksk_gen_launch(const PcbKskGenArgs*, cudaStream_t);
+}  // namespace keys
+}  // namespace pcb

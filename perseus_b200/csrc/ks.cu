@@ -1,0 +1,182 @@
+// Key-switching kernels behind the launcher table: the batched fast base conversion (bconv) and the key inner
+// product (ks_dot). Semantics: crates/pc-kernels/kernels/args.cuh:109-141 (BconvArgs) and :202-228 (KsArgs); host
+// twins crates/pc-host/src/bconv.rs:13-108 and crates/pc-host/src/ks.rs:60-140.
+//
+// Both are multiply-accumulate streams over 64-bit residues: every product goes into a 128-bit accumulator
+// (mad.lo.cc / madc.hi) and each output is reduced once. The conversion matrix of a job and its target primes'
+// Barrett constants sit in shared memory; source words stay in registers across all targets.
+#include "arith.cuh"
+
+namespace pcb {
+namespace ks {
+
+constexpr int BX = 128;
+constexpr int MAX_SRC = 16;
+constexpr int MAX_TGT = 64;
+
+// ------------------------------------------------------------------------------------------------ bconv
+template <int LOGN>
+__global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
+    __shared__ uint64_t sM[MAX_SRC * MAX_TGT];
+    __shared__ uint64_t sP[MAX_TGT], sM0[MAX_TGT], sM1[MAX_TGT];
+    __shared__ uint32_t sRow[MAX_TGT];
+    const PcbBconvJob j = a.jobs[blockIdx.y];
+    const uint64_t* pool = (const uint64_t*)a.pool + j.pool_off;
+    const int ns = (int)j.nsrc, nt = (int)j.ntgt;
+    if (ns < 1 || ns > MAX_SRC || nt > MAX_TGT) return;  // outside the kernel's job shape: nothing is written
+    const uint64_t* srow = pool;
+    const uint64_t* sprime = pool + ns;
+    const uint64_t* pre = pool + 2 * ns;
+    const uint64_t* trow = pool + 3 * ns;
+    const uint64_t* tprime = pool + 3 * ns + nt;
+    const uint64_t* M = pool + 3 * ns + 2 * nt;
+    for (int e = threadIdx.x; e < ns * nt; e += BX) sM[e] = M[e];
+    for (int t = threadIdx.x; t < nt; t += BX) {
+        const PcbPrimeConst& pc = a.pr[tprime[t]];
+        sP[t] = pc.p;
+        sM0[t] = pc.mu_lo;
+        sM1[t] = pc.mu_hi;
+        sRow[t] = (uint32_t)trow[t];
+    }
+    __syncthreads();
+    const size_t k = (size_t)blockIdx.x * BX + threadIdx.x;
+    const uint64_t* src = (const uint64_t*)a.src + ((size_t)j.src_off << LOGN) + k;
+    uint64_t* dst = (uint64_t*)a.dst + ((size_t)j.dst_off << LOGN) + k;
+    uint64_t y[MAX_SRC];
+#pragma unroll
+    for (int i = 0; i < MAX_SRC; ++i) {
+        if (i < ns) {
+            const uint64_t x = src[(size_t)srow[i] << LOGN];
+            if (j.prescaled) {
+                y[i] = x;
+            } else {
+                const PcbPrimeConst& q = a.pr[sprime[i]];
+                y[i] = mul_mod(x, pre[i], q);
+            }
+        }
+    }
+    // exact jobs (HPS): u from the double estimate in source order (one fma per source), or the centred mean
+    uint64_t u = 0;
+    const uint64_t* bmod = nullptr;
+    if (j.exact) {
+        const uint64_t* rbw = M + ns * nt;  // u64 words are 8-byte aligned: the doubles start right after M
+        if (j.exact == 2) {
+            u = (uint64_t)(ns >> 1) + (uint64_t)((ns & 1) & (((uint32_t)k * 0x9E3779B1u) >> 31));
+        } else {
+            double v = 0.0;
+            for (int i = 0; i < ns; ++i) v = __fma_rn((double)y[i], __longlong_as_double((long long)rbw[i]), v);
+            u = (uint64_t)floor(v + 0.5);
+        }
+        bmod = rbw + ns;
+    }
+    for (int t = 0; t < nt; ++t) {
+        Acc acc{0, 0};
+#pragma unroll
+        for (int i = 0; i < MAX_SRC; ++i)
+            if (i < ns) mac(acc, y[i], sM[i * nt + t]);
+        const uint64_t p = sP[t];
+        uint64_t r = reduce(acc, p, sM0[t], sM1[t]);
+        if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
+        dst[(size_t)sRow[t] << LOGN] = r;
+    }
+}
+
+template <int LOGN>
+int bconv_launch(const PcbBconvArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbBconvArgs& a = *ap;
+    if (a.njobs < 0 || a.max_tgt < 0 || a.max_tgt > MAX_TGT || !a.src || !a.dst || !a.jobs || !a.pool || !a.pr)
+        return PCB_BAD_ARGS;
+    if (a.njobs == 0) return 0;
+    bconv<LOGN><<<dim3((1 << LOGN) / BX, a.njobs), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+// ------------------------------------------------------------------------------------------------ ks_dot
+// s1 = sum_d D_d a_d, s0 = C0 + sum_d D_d b_d for K <= KMAX ciphertexts x R keys; D_d[t] is c1 itself on digit d's
+// own rows, else the ModUp output; each key word is read once per launch and reused by all K ciphertexts.
+template <int LOGN, int KMAX>
+__global__ void __launch_bounds__(BX) ks_dot(PcbKsArgs a) {
+    const uint32_t t = a.rows[blockIdx.y];
+    const PcbPrimeConst& pc = a.pr[t];
+    const uint64_t p = pc.p;
+    const uint32_t idx = blockIdx.x * BX + threadIdx.x;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t roff = ((size_t)t << LOGN) + idx;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    const uint64_t* c0 = (const uint64_t*)a.c0;
+    uint64_t pm = 0, pms = 0;
+    if ((a.c0_mode & 3) == 1 && (int)t < a.nq) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    for (int r = 0; r < a.R; ++r) {
+        Acc s0[KMAX], s1[KMAX];
+#pragma unroll
+        for (int c = 0; c < KMAX; ++c) s0[c] = s1[c] = Acc{0, 0};
+        const uint64_t* kb = (const uint64_t*)a.kb[r] + roff;
+        const uint64_t* ka = (const uint64_t*)a.ka[r] + roff;
+        for (int d = 0; d < a.ndig; ++d) {
+            const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
+            const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
+#pragma unroll
+            for (int c = 0; c < KMAX; ++c) {
+                if (c < a.K) {
+                    const uint64_t x = d == dt ? c1[(size_t)c * a.ct_stride + roff]
+                                               : mu[(size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff];
+                    mac(s0[c], x, b);
+                    mac(s1[c], x, av);
+                }
+            }
+        }
+        const uint32_t k = a.autok[r];
+        const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
+#pragma unroll
+        for (int c = 0; c < KMAX; ++c) {
+            if (c < a.K) {
+                uint64_t r0 = reduce(s0[c], pc), r1 = reduce(s1[c], pc);
+                if ((a.c0_mode & 3) == 1) {
+                    if ((int)t < a.nq) r0 = add_mod(r0, shoup(c0[(size_t)c * a.ct_stride + roff], pm, pms, p), p);
+                } else if ((a.c0_mode & 3) == 2) {
+                    r0 = add_mod(r0, c0[(size_t)c * a.ct_stride + roff], p);
+                }
+                const size_t ob = (size_t)c * a.out_ct_stride + (size_t)r * a.out_rot_stride + ((size_t)t << LOGN) + o;
+                if (a.c0_mode & PCB_KS_ACC) {
+                    r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
+                    r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
+                }
+                ((uint64_t*)a.out0)[ob] = r0;
+                ((uint64_t*)a.out1)[ob] = r1;
+            }
+        }
+    }
+}
+
+template <int LOGN>
+int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbKsArgs& a = *ap;
+    if (a.K < 0 || a.K > 8 || a.R < 0 || a.ndig < 1 || a.ndig > 16 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
+        (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.kb || !a.ka || !a.autok || !a.rows ||
+        !a.digit_of || !a.pr)
+        return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
+    if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
+    if (a.K == 0 || a.R == 0 || a.nrows == 0) return 0;
+    const dim3 g((1 << LOGN) / BX, a.nrows);
+    if (a.K <= 1) ks_dot<LOGN, 1><<<g, BX, 0, s>>>(a);
+    else if (a.K <= 2) ks_dot<LOGN, 2><<<g, BX, 0, s>>>(a);
+    else if (a.K <= 4) ks_dot<LOGN, 4><<<g, BX, 0, s>>>(a);
+    else ks_dot<LOGN, 8><<<g, BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
+template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
+template int ks_dot_launch<14>(const PcbKsArgs*, cudaStream_t);
+template int ks_dot_launch<16>(const PcbKsArgs*, cudaStream_t);
+
+}  // namespace ks
+}  // namespace pcb

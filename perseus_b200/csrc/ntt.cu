@@ -1,0 +1,345 @@
+// Negacyclic NTT / INTT of 64-bit RNS rows on sm_100a.
+//
+// Transform (crates/pc-kernels/kernels/args.cuh:67-107; host twin crates/pc-host/src/ntt.rs:85-130): OpenFHE order,
+// Cooley-Tukey forward to bit-reversed output with twiddles w[m + i] = psi^brev(m + i), Gentleman-Sande inverse with
+// psi^-brev and N^-1 (or a per-row factor) folded into its last pass. Canonical words in and out.
+//
+// B200 design. A row of N = 2^LOGN words is viewed as R = N / 256 "columns" x 256: stages 0 .. A-1 (A = LOGN - 8,
+// butterfly spans >= 256 words) run in the column pass, the last 8 stages (spans 128 .. 1) in the row pass over
+// 256-word blocks. Each pass keeps 16 (or 8) words per thread in registers and does two register rounds of 4 (or 3)
+// stages around one shared-memory exchange, so a pass reads and writes HBM once. Butterflies are Harvey-lazy (words
+// in [0, 4p) forward, [0, 2p) inverse) with Shoup twiddles, which needs p < 2^62. Launches go in chunks of rows,
+// both passes of a chunk back to back, so the intermediate state stays in the 126 MB L2.
+#include "arith.cuh"
+
+namespace pcb {
+namespace ntt {
+
+constexpr int THREADS = 256;
+
+// ------------------------------------------------------------------------------------------------ butterflies
+__device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, uint64_t p, uint64_t p2) {
+    uint64_t u = x >= p2 ? x - p2 : x;
+    const uint64_t v = shoup_lazy(y, w, ws, p);
+    x = u + v;
+    y = u + p2 - v;
+}
+__device__ __forceinline__ void gs_bfly(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, uint64_t p, uint64_t p2) {
+    const uint64_t u = x, v = y;
+    uint64_t s = u + v;
+    x = s >= p2 ? s - p2 : s;
+    y = shoup_lazy(u + p2 - v, w, ws, p);
+}
+__device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t p) {
+    const uint64_t p2 = 2 * p;
+    x = x >= p2 ? x - p2 : x;
+    return x >= p ? x - p : x;
+}
+
+struct RowInfo {
+    uint64_t* row;
+    int pid;
+};
+
+// Rows of a launch: row i at base + roff[i] * N, prime id rprime[i]
+template <int LOGN>
+__device__ __forceinline__ RowInfo row_of(const PcbNttArgs& a, int i) {
+    return RowInfo{(uint64_t*)a.base + ((size_t)a.roff[i] << LOGN), a.rprime[i]};
+}
+
+// The first pass's input word: the row itself, or the sum mod p of snum source rows (ABI 11 out-of-place)
+template <int LOGN>
+__device__ __forceinline__ uint64_t load_in(const PcbNttArgs& a, int i, const uint64_t* row, size_t off, uint64_t p) {
+    if (a.soff == nullptr) return row[off];
+    const uint64_t* s = (const uint64_t*)a.src + ((size_t)a.soff[i] << LOGN) + off;
+    uint64_t v = s[0];
+    for (int m = 1; m < a.snum; ++m) v = add_mod(v, s[(size_t)m * a.sstride], p);
+    return v;
+}
+
+// ------------------------------------------------------------------------------------------------ forward
+// Column pass: stages 0 .. A-1 on COLS columns; thread (cc, g) holds rows g + E k (round 1), then E g + k (round 2)
+template <int LOGN>
+__global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
+    constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
+    __shared__ uint64_t sm[R * COLS];
+    const int i = row0 + blockIdx.y;
+    const RowInfo ri = row_of<LOGN>(a, i);
+    const PcbPrimeConst& pc = a.pr[ri.pid];
+    const uint64_t p = pc.p, p2 = 2 * p;
+    const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
+    const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+    const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
+    const int col = blockIdx.x * COLS + cc;
+    uint64_t x[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) x[k] = load_in<LOGN>(a, i, ri.row, (size_t)(g + E * k) * 256 + col, p);
+    // round 1: stages 0 .. H-1, rows g + E k: butterfly partners differ in k by E/2, E/4, ..
+#pragma unroll
+    for (int s = 0; s < H; ++s) {
+        const int half = E >> (s + 1);
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            if (k & half) continue;
+            const int m = 1 << s, idx = m + (k >> (H - s));
+            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) sm[(g + E * k) * COLS + cc] = x[k];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < E; ++k) x[k] = sm[(E * g + k) * COLS + cc];
+    // round 2: stages H .. A-1, rows E g + k
+#pragma unroll
+    for (int s = H; s < A; ++s) {
+        const int half = E >> (s - H + 1);
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            if (k & half) continue;
+            const int m = 1 << s, idx = m + (g << (s - H)) + (k >> (A - s));
+            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) ri.row[(size_t)(E * g + k) * 256 + col] = x[k];
+}
+
+// Row pass: the last 8 stages over 256-word blocks, 16 blocks per CTA, 16 threads per block; thread u holds words
+// u + 16 k (round 1) then 16 u + k (round 2, 16 consecutive words: vector stores and the epilogue)
+template <int LOGN>
+__global__ void __launch_bounds__(THREADS) fwd_rows(PcbNttArgs a, int row0) {
+    constexpr int A = LOGN - 8;
+    __shared__ uint64_t sm[16 * 256];
+    const int i = row0 + blockIdx.y;
+    const RowInfo ri = row_of<LOGN>(a, i);
+    const PcbPrimeConst& pc = a.pr[ri.pid];
+    const uint64_t p = pc.p, p2 = 2 * p;
+    const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
+    const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+    const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
+    const int b = blockIdx.x * 16 + lb;  // 256-word block of the row
+    uint64_t* blk = ri.row + (size_t)b * 256;
+    uint64_t x[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = blk[u + 16 * k];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const int half = 16 >> (l + 1);
+        const int m = 1 << (A + l);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & half) continue;
+            const int idx = m + (b << l) + (k >> (4 - l));
+            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+        }
+    }
+    uint64_t* s = sm + lb * 256;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) s[u + 16 * k] = x[k];
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = s[16 * u + k];
+#pragma unroll
+    for (int l = 4; l < 8; ++l) {
+        const int half = 16 >> (l - 3);
+        const int m = 1 << (A + l);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & half) continue;
+            const int idx = m + (b << l) + (u << (l - 4)) + (k >> (8 - l));
+            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = canon4(x[k], p);
+    const size_t w0 = (size_t)b * 256 + 16 * u;  // word offset in the row
+    if (a.epi == 0) {
+        ulonglong2* o = (ulonglong2*)(blk + 16 * u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = make_ulonglong2(x[2 * k], x[2 * k + 1]);
+        return;
+    }
+    // forward epilogues (args.cuh:82-87): x = sum of xnum rows of ex, s = es[prime id]
+    const size_t r = ((size_t)a.roff[i] << LOGN) + w0;
+    const uint64_t sc = ((const uint64_t*)a.es)[ri.pid], scs = ((const uint64_t*)a.ess)[ri.pid];
+    const uint64_t* ex = (const uint64_t*)a.ex + r;
+    uint64_t* eo = (uint64_t*)a.eout + r;
+    const uint64_t* ed = a.ed ? (const uint64_t*)a.ed + r : eo;
+#pragma unroll 4
+    for (int k = 0; k < 16; ++k) {
+        uint64_t xs = ex[k];
+        for (int j = 1; j < a.xnum; ++j) xs = add_mod(xs, ex[k + (size_t)j * a.xstride], p);
+        uint64_t y;
+        if (a.epi == 1) y = shoup(sub_mod(xs, x[k], p), sc, scs, p);
+        else if (a.epi == 2) y = add_mod(ed[k], shoup(sub_mod(xs, x[k], p), sc, scs, p), p);
+        else y = add_mod(shoup(xs, sc, scs, p), x[k], p);
+        eo[k] = y;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ inverse
+// Row pass first (GS spans 1 .. 128 inside 256-word blocks); thread u holds 16 u + k (round 1), then u + 16 k
+template <int LOGN>
+__global__ void __launch_bounds__(THREADS) inv_rows(PcbNttArgs a, int row0) {
+    constexpr int A = LOGN - 8;
+    constexpr int N = 1 << LOGN;
+    __shared__ uint64_t sm[16 * 256];
+    const int i = row0 + blockIdx.y;
+    const RowInfo ri = row_of<LOGN>(a, i);
+    const PcbPrimeConst& pc = a.pr[ri.pid];
+    const uint64_t p = pc.p, p2 = 2 * p;
+    const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
+    const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+    const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
+    const int b = blockIdx.x * 16 + lb;
+    uint64_t* blk = ri.row + (size_t)b * 256;
+    uint64_t x[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p);
+    // spans h = 1, 2, 4, 8: group index j / (2h), m = N / (2h)
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const int h = 1 << l;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & h) continue;
+            const int m = N / (2 * h);
+            const int idx = m + ((b * 256 + 16 * u + k) >> (l + 1));
+            gs_bfly(x[k], x[k + h], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+        }
+    }
+    uint64_t* s = sm + lb * 256;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) s[16 * u + k] = x[k];
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = s[u + 16 * k];
+    // spans h = 16 .. 128: partners differ in k by h / 16
+#pragma unroll
+    for (int l = 4; l < 8; ++l) {
+        const int hk = 1 << (l - 4);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & hk) continue;
+            const int m = N >> (l + 1);
+            const int idx = m + ((b * 256 + u + 16 * k) >> (l + 1));
+            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+        }
+    }
+    (void)A;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) blk[u + 16 * k] = x[k];
+}
+
+// Column pass: spans 256 .. N/2, then the row's last-pass factor (N^-1, or es[i] with ess[i])
+template <int LOGN>
+__global__ void __launch_bounds__(THREADS) inv_cols(PcbNttArgs a, int row0) {
+    constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
+    __shared__ uint64_t sm[R * COLS];
+    const int i = row0 + blockIdx.y;
+    const RowInfo ri = row_of<LOGN>(a, i);
+    const PcbPrimeConst& pc = a.pr[ri.pid];
+    const uint64_t p = pc.p, p2 = 2 * p;
+    const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
+    const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+    const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
+    const int col = blockIdx.x * COLS + cc;
+    uint64_t x[E];
+    // round 1: row spans 1 .. E/2 (word spans 256 ..) on rows E g + k
+#pragma unroll
+    for (int k = 0; k < E; ++k) x[k] = ri.row[(size_t)(E * g + k) * 256 + col];
+#pragma unroll
+    for (int l = 0; l < H; ++l) {
+        const int hk = 1 << l;
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            if (k & hk) continue;
+            const int m = R >> (l + 1);
+            const int idx = m + ((E * g + k) >> (l + 1));
+            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) sm[(E * g + k) * COLS + cc] = x[k];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < E; ++k) x[k] = sm[(g + E * k) * COLS + cc];
+    // round 2: row spans E .. R/2 on rows g + E k: partners differ in k by span / E
+#pragma unroll
+    for (int l = H; l < A; ++l) {
+        const int hk = 1 << (l - H);
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+            if (k & hk) continue;
+            const int m = R >> (l + 1);
+            const int idx = m + ((g + E * k) >> (l + 1));
+            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+        }
+    }
+    uint64_t ni, nis;
+    if (a.es) {
+        ni = ((const uint64_t*)a.es)[i];
+        nis = ((const uint64_t*)a.ess)[i];
+    } else {
+        ni = ((const uint64_t*)a.ninv)[ri.pid];
+        nis = ((const uint64_t*)a.ninvs)[ri.pid];
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) ri.row[(size_t)(g + E * k) * 256 + col] = shoup(x[k], ni, nis, p);
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+// Rows per chunk: both passes of a chunk run back to back so the intermediate state is read back from L2.
+template <int LOGN>
+__host__ int chunk_rows(const PcbNttArgs& a) {
+    if (a.chunk > 0) return a.chunk;
+    const int per = (int)((48u << 20) >> (LOGN + 3));  // ~48 MiB of rows in flight
+    return per < 1 ? 1 : per;
+}
+
+template <int LOGN>
+int fwd(const PcbNttArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbNttArgs a = *ap;
+    if (a.nrows < 0 || a.epi < 0 || a.epi > 3 || !a.base || !a.roff || !a.rprime || !a.fw || !a.fws || !a.pr)
+        return PCB_BAD_ARGS;
+    if (a.epi != 0 && (!a.eout || !a.ex || !a.es || !a.ess)) return PCB_BAD_ARGS;
+    if (a.soff && (!a.src || a.snum < 1)) return PCB_BAD_ARGS;
+    if (a.nrows == 0) return 0;
+    constexpr int A = LOGN - 8, COLS = 256 / (1 << (A / 2));
+    const int ch = chunk_rows<LOGN>(a);
+    for (int r0 = 0; r0 < a.nrows; r0 += ch) {
+        const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
+        fwd_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+        fwd_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+    }
+    return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int inv(const PcbNttArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbNttArgs a = *ap;
+    if (a.nrows < 0 || a.epi != 0 || !a.base || !a.roff || !a.rprime || !a.iw || !a.iws || !a.pr) return PCB_BAD_ARGS;
+    if (!a.es && (!a.ninv || !a.ninvs)) return PCB_BAD_ARGS;
+    if (a.es && !a.ess) return PCB_BAD_ARGS;
+    if (a.soff && (!a.src || a.snum < 1)) return PCB_BAD_ARGS;
+    if (a.nrows == 0) return 0;
+    constexpr int A = LOGN - 8, COLS = 256 / (1 << (A / 2));
+    const int ch = chunk_rows<LOGN>(a);
+    for (int r0 = 0; r0 < a.nrows; r0 += ch) {
+        const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
+        inv_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+        inv_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+    }
+    return PCB_LAUNCH_RESULT();
+}
+
+template int fwd<14>(const PcbNttArgs*, cudaStream_t);
+template int fwd<16>(const PcbNttArgs*, cudaStream_t);
+template int inv<14>(const PcbNttArgs*, cudaStream_t);
+template int inv<16>(const PcbNttArgs*, cudaStream_t);
+
+}  // namespace ntt
+}  // namespace pcb

@@ -1,0 +1,75 @@
+// The exported launcher tables (crates/pc-kernels/kernels/args.cuh:1034-1119): the reference's L3 seam.
+// Entries outside this library's hot path are non-null and return -1 ("argument out of the kernel's range"), as the
+// reference's own tables do for kernels an instantiation lacks.
+#include "kernels.h"
+
+namespace {
+int absent(const void*, cudaStream_t) { return -1; }
+int no_regen(const PcbKsRegenArgs*, cudaStream_t) { return -1; }
+
+template <int LOGN>
+PcbKernelTable make_table() {
+    using namespace pcb;
+    PcbKernelTable t;
+    PcbLaunch* all = (PcbLaunch*)&t.ntt_fwd;
+    for (int i = 0; i < 52; ++i) all[i] = absent;
+    t.abi = PCB_KERNELS_ABI;
+    t.word_bytes = 8;
+    t.mm = 0;
+    t.log_n = LOGN;
+    t.ntt_fwd = ntt::fwd<LOGN>;
+    t.ntt_inv = ntt::inv<LOGN>;
+    t.bconv = ks::bconv_launch<LOGN>;
+    t.ew_add = elem::ew_launch<LOGN, elem::ADD>;
+    t.ew_scale = elem::ew_launch<LOGN, elem::SCALE>;
+    t.ew_sub_mul = elem::ew_launch<LOGN, elem::SUB_MUL>;
+    t.ew_copy = elem::ew_launch<LOGN, elem::COPY>;
+    t.ks_dot = ks::ks_dot_launch<LOGN>;
+    t.ks_dot_regen = no_regen;
+    t.ksk_expand = keys::ksk_expand_launch<LOGN>;
+    t.tensor = elem::tensor_launch<LOGN>;
+    t.md_epilogue = elem::md_epilogue_launch<LOGN>;
+    t.rescale_coef = elem::rescale_coef_launch<LOGN>;
+    t.rescale_combine = elem::rescale_combine_launch<LOGN>;
+    t.automorph = elem::automorph_launch<LOGN>;
+    t.encrypt = keys::encrypt_launch<LOGN>;
+    t.ksk_gen = keys::ksk_gen_launch<LOGN>;
+    return t;
+}
+
+template <int LOGN>
+PcbRingTable make_ring() {
+    using namespace pcb;
+    PcbRingTable r;
+    r.abi = PCB_RING_ABI;
+    r.word_bytes = 8;
+    r.mm = 0;
+    r.log_n = LOGN;
+    r.ntt_fwd = ntt::fwd<LOGN>;
+    r.ntt_inv = ntt::inv<LOGN>;
+    r.ntt_fwd_g = ntt::fwd<LOGN>;
+    r.ntt_inv_g = ntt::inv<LOGN>;
+    r.bconv = ks::bconv_launch<LOGN>;
+    r.ew_add = elem::ew_launch<LOGN, elem::ADD>;
+    r.ew_scale = elem::ew_launch<LOGN, elem::SCALE>;
+    r.ew_sub_mul = elem::ew_launch<LOGN, elem::SUB_MUL>;
+    r.ew_copy = elem::ew_launch<LOGN, elem::COPY>;
+    return r;
+}
+
+const PcbKernelTable g_table16 = make_table<16>();
+const PcbKernelTable g_table14 = make_table<14>();
+const PcbRingTable g_ring14 = make_ring<14>();
+const PcbRingTable g_ring16 = make_ring<16>();
+}  // namespace
+
+namespace pcb {
+// the full launcher set at either ring size, for the evaluator
+const PcbKernelTable* table_for(int logn) { return logn == 14 ? &g_table14 : logn == 16 ? &g_table16 : nullptr; }
+}  // namespace pcb
+
+extern "C" {
+const PcbKernelTable* pc_table_u64_barrett64(void) { return &g_table16; }
+const PcbRingTable* pc_ring_u64_14(void) { return &g_ring14; }
+const PcbRingTable* pc_ring_u64_16(void) { return &g_ring16; }
+}

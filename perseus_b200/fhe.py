@@ -1,0 +1,313 @@
+"""The evaluator API over the CUDA library, mirroring the reference's `Fhe` session (crates/pc-py/src/fhe.rs:770-1640):
+encrypt, decrypt_slots, add, sub, mult, square, rescale_one, rotate, rotate_and_sum, mult_pt, add_pt, plus the
+batched forms the benchmarks use. Device memory and streams come from torch; every op runs on the CUDA library
+through its C ABI (there is no CPU path).
+
+A `Ct` holds K ciphertexts [K][2][nq + kp][N] (uint64 residues viewed as torch.int64), its top limb, its scale and
+its slot count. Products leave the rescale pending (scale = product of the scales), as the reference's relin::mult
+does (crates/pc-gpu/src/relin.rs:1-4); `rescale_one` pays it.
+"""
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+# ------------------------------------------------------------------------------------------------ chain helpers
+
+
+def _is_prime(n):
+    if n < 2:
+        return False
+    small = (2, 3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37)
+    for p in small:
+        if n % p == 0:
+            return n == p
+    d, s = n - 1, 0
+    while d % 2 == 0:
+        d //= 2
+        s += 1
+    for a in small:
+        x = pow(a, d, n)
+        if x in (1, n - 1):
+            continue
+        for _ in range(s - 1):
+            x = x * x % n
+            if x == n - 1:
+                break
+        else:
+            return False
+    return True
+
+
+def ntt_primes(bits, log_n, count, skip=0):
+    """`count` primes p = 1 mod 2N just below 2^bits, largest first, after skipping `skip` of them
+    (crates/pc-kernels/src/bin/selftest/host.rs:76-88)."""
+    step = 2 << log_n
+    c = (1 << bits) + 1
+    out, seen = [], 0
+    while len(out) < count:
+        c -= step
+        if _is_prime(c):
+            if seen >= skip:
+                out.append(c)
+            seen += 1
+    return out
+
+
+@dataclass(frozen=True)
+class Chain:
+    """Explicit prime lists (the reference's Chain, crates/pc-core/src/params.rs:225-258)."""
+
+    log_n: int
+    q: tuple
+    p: tuple
+    dnum: int
+
+    @property
+    def n(self):
+        return 1 << self.log_n
+
+    @property
+    def rows(self):
+        return len(self.q) + len(self.p)
+
+
+def config1_chain():
+    """BASELINE config 1 made sound: N = 2^14, 8 x 50-bit Q primes, one 60-bit special prime, dnum 8 (one limb per
+    digit, so the single special prime covers every digit)."""
+    return Chain(14, tuple(ntt_primes(50, 14, 8)), tuple(ntt_primes(60, 14, 1)), 8)
+
+
+def config2_chain():
+    """N = 2^16, 24 x 50-bit Q primes + 8 x 50-bit special primes, dnum 3 (8 limbs per digit)."""
+    return Chain(16, tuple(ntt_primes(50, 16, 24)), tuple(ntt_primes(50, 16, 8, skip=24)), 3)
+
+
+def rotation_galois(step, log_n):
+    """5^(step mod N/2) mod 2N (crates/pc-core/src/galois.rs:38-44)."""
+    h = 1 << (log_n - 1)
+    return pow(5, step % h, 2 << log_n)
+
+
+# ------------------------------------------------------------------------------------------------ ciphertexts
+
+
+@dataclass
+class Ct:
+    data: torch.Tensor  # [K][2][rows][N] int64 on the device
+    top: int
+    scale: float
+    slots: int
+
+    @property
+    def k(self):
+        return self.data.shape[0]
+
+    def ptr(self):
+        return C.c_void_p(self.data.data_ptr())
+
+    def clone(self):
+        return Ct(self.data.clone(), self.top, self.scale, self.slots)
+
+
+class Session:
+    """A context over one chain with device-resident keys (relinearization + the given rotation steps)."""
+
+    def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None):
+        self.chain = chain
+        self.device = torch.device(device or "cuda")
+        self.n, self.log_n = chain.n, chain.log_n
+        self.nq, self.kp, self.rows = len(chain.q), len(chain.p), chain.rows
+        self.k_max = k_max
+        gal = [1]
+        for s in rot_steps:
+            g = rotation_galois(s, chain.log_n)
+            if g != 1 and g not in gal:
+                gal.append(g)
+        self.galois = gal
+        self._q = (C.c_uint64 * self.nq)(*chain.q)
+        self._p = (C.c_uint64 * self.kp)(*chain.p)
+        self.params = L.Params(chain.log_n, self.nq, self.kp, chain.dnum,
+                               C.cast(self._q, L.u64p), C.cast(self._p, L.u64p), k_max, 0)
+        lib = L.lib()
+        nbytes = lib.pcb_ctx_bytes(C.byref(self.params), len(gal))
+        if nbytes < 0:
+            L.check(int(nbytes), "pcb_ctx_bytes")
+        with torch.cuda.device(self.device):
+            self.arena = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+            h_ctx = C.c_void_p()
+            L.check(lib.pcb_ctx_create(C.byref(self.params), len(gal), C.c_void_p(self.arena.data_ptr()),
+                                       int(nbytes), self._stream(), C.byref(h_ctx)), "pcb_ctx_create")
+            self.ctx = h_ctx
+            g = (C.c_uint64 * len(gal))(*gal)
+            L.check(lib.pcb_keygen(self.ctx, seed, h, sigma, len(gal), C.cast(g, L.u64p), self._stream()), "pcb_keygen")
+
+    def __del__(self):
+        ctx = getattr(self, "ctx", None)
+        if not ctx:
+            return
+        self.ctx = None
+        try:
+            torch.cuda.synchronize(self.device)
+            L.lib().pcb_ctx_destroy(ctx)
+        except Exception:
+            pass  # interpreter teardown: the process exit releases the host state
+
+    def _stream(self):
+        return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    # -------------------------------------------------------------------------------------------- buffers
+    def empty(self, k=1):
+        return torch.empty((k, 2, self.rows, self.n), dtype=torch.int64, device=self.device)
+
+    def ct_like(self, x):
+        return Ct(self.empty(x.k), x.top, x.scale, x.slots)
+
+    def top(self):
+        return self.nq - 1
+
+    def key(self, idx):
+        b, a, g = C.c_void_p(), C.c_void_p(), C.c_uint64()
+        L.check(L.lib().pcb_key_ptrs(self.ctx, idx, C.byref(b), C.byref(a), C.byref(g)), "pcb_key_ptrs")
+        words = self.chain.dnum * self.rows * self.n
+        return b.value, a.value, g.value, words
+
+    def key_tensors(self, idx):
+        """Copies of key `idx` (b, a) as [dnum][rows][N] device tensors."""
+        shape = (self.chain.dnum, self.rows, self.n)
+        b = torch.empty(shape, dtype=torch.int64, device=self.device)
+        a = torch.empty(shape, dtype=torch.int64, device=self.device)
+        L.check(L.lib().pcb_key_copy(self.ctx, idx, C.c_void_p(b.data_ptr()), C.c_void_p(a.data_ptr()),
+                                     self._stream()), "pcb_key_copy")
+        return b, a
+
+    def tables(self):
+        ptrs = [C.c_void_p() for _ in range(7)]
+        L.check(L.lib().pcb_ctx_tables(self.ctx, *[C.byref(p) for p in ptrs]), "pcb_ctx_tables")
+        return [p.value for p in ptrs]
+
+    # -------------------------------------------------------------------------------------------- encode / encrypt
+    @staticmethod
+    def _vals(values):
+        v = np.asarray(values, dtype=np.complex128).ravel()
+        flat = np.ascontiguousarray(np.stack([v.real, v.imag], 1).ravel())
+        return flat, len(v)
+
+    def encode(self, values, slots=None, scale=2.0**40, top=None):
+        """Coefficient-form rows 0..=top (host numpy uint64) of the encoding of `values`."""
+        top = self.top() if top is None else top
+        flat, nv = self._vals(values)
+        slots = slots or max(1, 1 << (nv - 1).bit_length())
+        rows = np.zeros((top + 1, self.n), np.uint64)
+        L.check(L.lib().pcb_encode(self.ctx, flat.ctypes.data_as(C.POINTER(C.c_double)), nv, slots, scale, top,
+                                   rows.ctypes.data_as(L.u64p)), "pcb_encode")
+        return rows
+
+    def encrypt(self, values, top=None, scale=2.0**40, slots=None):
+        top = self.top() if top is None else top
+        flat, nv = self._vals(values)
+        slots = slots or max(1, 1 << (nv - 1).bit_length())
+        out = self.empty(1)
+        L.check(L.lib().pcb_encrypt(self.ctx, flat.ctypes.data_as(C.POINTER(C.c_double)), nv, slots, scale, top,
+                                    C.c_void_p(out.data_ptr()), self._stream()), "pcb_encrypt")
+        return Ct(out, top, scale, slots)
+
+    def decrypt_slots(self, ct, index=0):
+        vals = np.zeros(2 * ct.slots, np.float64)
+        ptr = ct.data[index].data_ptr()
+        L.check(L.lib().pcb_decrypt(self.ctx, C.c_void_p(ptr), ct.top, ct.slots, ct.scale,
+                                    vals.ctypes.data_as(C.POINTER(C.c_double)), self._stream()), "pcb_decrypt")
+        return vals[0::2] + 1j * vals[1::2]
+
+    def pt(self, values, top, scale, slots):
+        """A plaintext in evaluation form on the device ([nq][N]) for mult_pt / add_pt."""
+        rows = self.encode(values, slots=slots, scale=scale, top=top)
+        dev = torch.zeros((self.nq, self.n), dtype=torch.int64, device=self.device)
+        L.check(L.lib().pcb_pt_load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(dev.data_ptr()),
+                                    self._stream()), "pcb_pt_load")
+        return dev
+
+    # -------------------------------------------------------------------------------------------- ops
+    def _same(self, a, b):
+        if a.top != b.top or a.k != b.k:
+            raise ValueError(f"operands at tops {a.top} / {b.top}, batches {a.k} / {b.k}")
+
+    def add(self, a, b):
+        self._same(a, b)
+        out = self.ct_like(a)
+        L.check(L.lib().pcb_add(self.ctx, a.ptr(), b.ptr(), out.ptr(), a.top, a.k, self._stream()), "pcb_add")
+        return out
+
+    def sub(self, a, b):
+        self._same(a, b)
+        out = self.ct_like(a)
+        L.check(L.lib().pcb_sub(self.ctx, a.ptr(), b.ptr(), out.ptr(), a.top, a.k, self._stream()), "pcb_sub")
+        return out
+
+    def inplace_add(self, a, b):
+        self._same(a, b)
+        L.check(L.lib().pcb_add(self.ctx, a.ptr(), b.ptr(), a.ptr(), a.top, a.k, self._stream()), "pcb_add")
+        return a
+
+    def mult(self, a, b):
+        """Relinearized product, rescale pending."""
+        self._same(a, b)
+        out = Ct(self.empty(a.k), a.top, a.scale * b.scale, a.slots)
+        L.check(L.lib().pcb_mult(self.ctx, a.ptr(), b.ptr(), out.ptr(), a.top, a.k, self._stream()), "pcb_mult")
+        return out
+
+    def square(self, a):
+        return self.mult(a, a)
+
+    def rescale_one(self, a):
+        """In place: drop the top prime, scale / q_top."""
+        L.check(L.lib().pcb_rescale(self.ctx, a.ptr(), a.top, a.k, self._stream()), "pcb_rescale")
+        a.scale /= self.chain.q[a.top]
+        a.top -= 1
+        return a
+
+    def drop_to(self, a, top):
+        """The same ciphertext over fewer limbs (residues mod the lower primes are unchanged)."""
+        if top > a.top:
+            raise ValueError("drop_to raises no level")
+        return Ct(a.data, top, a.scale, a.slots)
+
+    def rotate(self, a, step):
+        out = self.ct_like(a)
+        L.check(L.lib().pcb_rotate(self.ctx, a.ptr(), int(step), out.ptr(), a.top, a.k, self._stream()), "pcb_rotate")
+        return out
+
+    def rotate_and_sum(self, a, start, stop):
+        out = self.ct_like(a)
+        L.check(L.lib().pcb_rotate_and_sum(self.ctx, a.ptr(), int(start), int(stop), out.ptr(), a.top, a.k,
+                                           self._stream()), "pcb_rotate_and_sum")
+        return out
+
+    def mult_pt(self, a, pt, pt_scale):
+        out = Ct(self.empty(a.k), a.top, a.scale * pt_scale, a.slots)
+        L.check(L.lib().pcb_mult_pt(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), out.ptr(), a.top, a.k,
+                                    self._stream()), "pcb_mult_pt")
+        return out
+
+    def add_pt(self, a, pt):
+        out = self.ct_like(a)
+        L.check(L.lib().pcb_add_pt(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), out.ptr(), a.top, a.k,
+                                   self._stream()), "pcb_add_pt")
+        return out
+
+    def keyswitch(self, d, c0, c0_mode, kidx, autok, out, top, k):
+        L.check(L.lib().pcb_keyswitch(self.ctx, C.c_void_p(d), C.c_void_p(c0 or 0), c0_mode, kidx, autok,
+                                      C.c_void_p(out), top, k, 0, self._stream()), "pcb_keyswitch")
+
+    def ntt_batch(self, x, nrows, inverse=False):
+        L.check(L.lib().pcb_ntt_batch(self.ctx, C.c_void_p(x.data_ptr()), nrows, int(inverse), self._stream()),
+                "pcb_ntt_batch")
+
+    def device_sync(self):
+        torch.cuda.synchronize(self.device)
+
+
+Fhe = Session

@@ -1,0 +1,80 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/pcb200.h declares, and its argument
+structs and tables have the reference's sizes (crates/pc-kernels/kernels/args.cuh static asserts)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from perseus_b200 import _lib as L
+from perseus_b200 import fhe
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "pcb200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b((?:pc|pcb)_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_declared_symbols():
+    lib = L.lib()
+    names = declared_symbols()
+    assert "pc_table_u64_barrett64" in names and "pcb_mult" in names and len(names) > 20
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+@pytest.mark.parametrize("name,size", sorted(L.SIZES.items()))
+def test_struct_sizes(name, size):
+    assert C.sizeof(getattr(L, name)) == size
+
+
+def test_table_headers():
+    t = L.kernel_table()
+    assert (t.abi, t.word_bytes, t.mm, t.log_n) == (30, 8, 0, 16)
+    for n in L.LAUNCHERS:
+        assert getattr(t, n), n  # every entry is non-null (absent ones return -1)
+    for ln in (14, 16):
+        r = L.ring_table(ln)
+        assert (r.abi, r.word_bytes, r.mm, r.log_n) == (7, 8, 0, ln)
+
+
+def test_absent_entries_refuse():
+    t = L.kernel_table()
+    assert t.pt_dot(None, None) == -1 and t.ks_dot_regen(None, None) == -1 and t.tfhe(None, None) == -1
+
+
+def test_null_arguments_refused_without_launch():
+    t = L.kernel_table()
+    a = L.NttArgs()
+    assert t.ntt_fwd(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    assert t.ntt_fwd(None, None) == -1
+
+
+def test_ctx_bytes_config2():
+    ch = fhe.config2_chain()
+    q = (C.c_uint64 * 24)(*ch.q)
+    p = (C.c_uint64 * 8)(*ch.p)
+    prm = L.Params(16, 24, 8, 3, C.cast(q, L.u64p), C.cast(p, L.u64p), 64, 0)
+    nb = L.lib().pcb_ctx_bytes(C.byref(prm), 16)
+    assert nb > 0
+    gib = nb / 2**30
+    assert 5 < gib < 40, gib  # workspaces for 64 ciphertexts + 16 keys fit one B200 many times over
+
+
+def test_ctx_bytes_rejects_bad_chains():
+    q = (C.c_uint64 * 2)(97, 193)
+    p = (C.c_uint64 * 1)(257)
+    prm = L.Params(16, 2, 1, 1, C.cast(q, L.u64p), C.cast(p, L.u64p), 1, 0)
+    assert L.lib().pcb_ctx_bytes(C.byref(prm), 1) < 0
+    assert "NTT prime" in L.lib().pcb_last_error().decode()
+
+
+def test_chain_primes():
+    c1, c2 = fhe.config1_chain(), fhe.config2_chain()
+    assert len(c1.q) == 8 and len(c1.p) == 1 and all(q.bit_length() == 50 for q in c1.q) and c1.p[0].bit_length() == 60
+    assert len(c2.q) == 24 and len(c2.p) == 8 and all(x.bit_length() == 50 for x in c2.q + c2.p)
+    assert len(set(c2.q + c2.p)) == 32
+    assert all((x - 1) % (2 << 16) == 0 for x in c2.q + c2.p)

@@ -1,0 +1,283 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle: bit-exact residues on the same seeded keys,
+encryption randomness and inputs, decrypted values against the plaintext math.
+
+Launcher-level tests drive the reference-compatible table entries (ntt_fwd / ntt_inv with their epilogues and
+out-of-place sources, bconv, ks_dot, tensor, automorph) on rows of both rings; evaluator-level tests compare keys,
+encryptions, products, rescales and rotations of a Session with the oracle context built from the same seed.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from perseus_b200 import _lib as L
+from perseus_b200 import fhe
+from tests import _oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SEED, H, SIGMA = 0, 192, 3.2
+STEPS1 = (1, 2, 4, 8, 16, 32, 64, -1)
+
+
+def host(t):
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int64)).cuda()
+
+
+def vp(t):
+    return C.c_void_p(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def s1():
+    ch = fhe.config1_chain()
+    s = fhe.Session(ch, rot_steps=STEPS1, k_max=4, seed=SEED, h=H, sigma=SIGMA)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(SEED, H, SIGMA, s.galois)
+    return s, o
+
+
+@pytest.fixture(scope="module")
+def s2():
+    ch = fhe.config2_chain()
+    s = fhe.Session(ch, rot_steps=(1, 5), k_max=2, seed=SEED, h=H, sigma=SIGMA)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(SEED, H, SIGMA, s.galois)
+    return s, o
+
+
+# ------------------------------------------------------------------------------------------------ launchers
+
+
+def _ntt_args(s, x, rows_pid, **kw):
+    pr, fw, fws, iw, iws, ni, nis = s.tables()
+    nrows = len(rows_pid)
+    roff = torch.arange(nrows, dtype=torch.int32, device="cuda")
+    rprime = torch.tensor(rows_pid, dtype=torch.int32, device="cuda")
+    a = L.NttArgs()
+    a.base, a.roff, a.rprime = x.data_ptr(), roff.data_ptr(), rprime.data_ptr()
+    a.fw, a.fws, a.iw, a.iws, a.ninv, a.ninvs, a.pr = fw, fws, iw, iws, ni, nis, pr
+    a.nrows, a.snum, a.xnum = nrows, 1, 1
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a, (roff, rprime)
+
+
+def _table(s):
+    return L.kernel_table() if s.log_n == 16 else L.ring_table(14)
+
+
+@pytest.mark.parametrize("which", ["s1", "s2"])
+def test_ntt_launchers_match_oracle(which, request):
+    s, o = request.getfixturevalue(which)
+    rng = np.random.default_rng(11)
+    pids = [0, 1, s.nq - 1, s.nq, s.rows - 1, 2]
+    primes = [o.q[i] if i < o.nq else o.p[i - o.nq] for i in pids]
+    x = np.stack([rng.integers(0, p, s.n, dtype=np.uint64) for p in primes])
+    xd = dev(x)
+    a, keep = _ntt_args(s, xd, pids)
+    t = _table(s)
+    assert t.ntt_fwd(C.cast(C.pointer(a), C.c_void_p), None) == 0
+    want = x.copy()
+    O.lib().orc_ntt_fwd(want, len(pids), np.array(primes, np.uint64), s.log_n)
+    assert (host(xd) == want).all()
+    assert t.ntt_inv(C.cast(C.pointer(a), C.c_void_p), None) == 0
+    assert (host(xd) == x).all()
+
+
+def test_ntt_epilogues_and_sources(s2):
+    s, o = s2
+    rng = np.random.default_rng(12)
+    pids = [3, 7, 30]
+    primes = np.array([o.q[3], o.q[7], o.p[6]], np.uint64)
+    n = s.n
+    src = np.stack([rng.integers(0, int(p), n, dtype=np.uint64) for p in primes for _ in range(2)])  # 2 sources/row
+    ex = np.stack([rng.integers(0, int(p), n, dtype=np.uint64) for p in primes])
+    sc = rng.integers(1, int(min(primes)), s.rows, dtype=np.uint64)
+    scs = np.array([(int(v) << 64) // int(primes[pids.index(i)]) if i in pids else 0 for i, v in enumerate(sc)], np.uint64)
+    summed = np.stack([(src[2 * i].astype(object) + src[2 * i + 1]) % int(primes[i]) for i in range(3)]).astype(np.uint64)
+    ref = summed.copy()
+    O.lib().orc_ntt_fwd(ref, 3, primes, s.log_n)
+    srcd, exd, scd, scsd = dev(src), dev(ex), dev(sc), dev(scs)
+    soff = torch.tensor([0, 2, 4], dtype=torch.int32, device="cuda")
+    t = _table(s)
+    for epi in (1, 2, 3):
+        base = torch.zeros((3, n), dtype=torch.int64, device="cuda")
+        eout = dev(np.stack([rng.integers(0, int(p), n, dtype=np.uint64) for p in primes]))
+        before = host(eout).astype(object)
+        a, keep = _ntt_args(s, base, pids, src=srcd.data_ptr(), soff=soff.data_ptr(), snum=2, sstride=n, epi=epi,
+                            eout=eout.data_ptr(), ex=exd.data_ptr(), es=scd.data_ptr(), ess=scsd.data_ptr())
+        assert t.ntt_fwd(C.cast(C.pointer(a), C.c_void_p), None) == 0
+        got = host(eout).astype(object)
+        for i, pid in enumerate(pids):
+            p, v, xs, w = int(primes[i]), ref[i].astype(object), ex[i].astype(object), int(sc[pid])
+            if epi == 1:
+                want = (xs - v) % p * w % p
+            elif epi == 2:
+                want = (before[i] + (xs - v) % p * w) % p
+            else:
+                want = (xs * w + v) % p
+            assert (got[i] == want).all(), f"epilogue {epi} row {i}"
+
+
+def test_bconv_launcher(s2):
+    s, o = s2
+    rng = np.random.default_rng(13)
+    srcp = [0, 1, 2, 3]
+    tgtp = [5, 9, 24, 31]
+    primes = list(o.q) + list(o.p)
+    bp = [primes[i] for i in srcp]
+    pool = []
+    pool += srcp + srcp
+    B = 1
+    for b in bp:
+        B *= b
+    pool += [pow(B // b % b, -1, b) for b in bp]
+    pool += tgtp + tgtp
+    for b in bp:
+        pool += [(B // b) % primes[t] for t in tgtp]
+    x = np.zeros((s.rows, s.n), np.uint64)
+    for i in srcp:
+        x[i] = rng.integers(0, primes[i], s.n, dtype=np.uint64)
+    out = torch.zeros((s.rows, s.n), dtype=torch.int64, device="cuda")
+    xd, poold = dev(x), dev(np.array(pool, np.uint64))
+    jobs = (L.BconvJob * 1)(L.BconvJob(0, 0, 4, 4, 0, 0, 0, 0))
+    jd = torch.from_numpy(np.frombuffer(bytes(jobs), np.uint8).copy()).cuda()
+    a = L.BconvArgs()
+    a.src, a.dst, a.jobs, a.pool, a.pr = xd.data_ptr(), out.data_ptr(), jd.data_ptr(), poold.data_ptr(), s.tables()[0]
+    a.njobs, a.max_tgt = 1, 4
+    assert _table(s).bconv(C.cast(C.pointer(a), C.c_void_p), None) == 0
+    got = host(out)
+    xs = x.astype(object)
+    for j, t in enumerate(tgtp):
+        y = [(xs[i] * pool[8 + k]) % bp[k] for k, i in enumerate(srcp)]
+        want = sum(y[k] * ((B // bp[k]) % primes[t]) for k in range(4)) % primes[t]
+        assert (got[t].astype(object) == want).all()
+
+
+# ------------------------------------------------------------------------------------------------ evaluator
+
+
+@pytest.mark.parametrize("which", ["s1", "s2"])
+def test_keys_bit_exact(which, request):
+    s, o = request.getfixturevalue(which)
+    for idx in range(len(s.galois)):
+        b, a = s.key_tensors(idx)
+        ob, oa, _ = o.key(idx)
+        assert (host(a) == oa).all(), f"key {idx} a"
+        assert (host(b) == ob).all(), f"key {idx} b"
+
+
+def _pair(s, o, x, top, slots=None):
+    ct = s.encrypt(x, top=top, slots=slots)
+    oc = o.encrypt(x, ct.slots, ct.scale, top)
+    return ct, oc
+
+
+def _eq(ct, oc, top, rows):
+    g = host(ct.data[0])
+    return (g[:, : top + 1] == oc[:, : top + 1]).all()
+
+
+@pytest.mark.parametrize("which", ["s1", "s2"])
+def test_encrypt_bit_exact_and_decrypts(which, request):
+    s, o = request.getfixturevalue(which)
+    rng = np.random.default_rng(1)
+    x = rng.normal(0, 1, 256) / 8
+    top = s.top()
+    ct, oc = _pair(s, o, x, top)
+    assert _eq(ct, oc, top, s.rows)
+    got = s.decrypt_slots(ct)
+    assert np.abs(got.real - x).max() < 1e-6
+
+
+def test_mult_rescale_bit_exact(s1):
+    s, o = s1
+    rng = np.random.default_rng(2)
+    x, y = rng.normal(0, 1, 512) / 8, rng.normal(0, 1, 512) / 8
+    top = s.top()
+    a, oa = _pair(s, o, x, top)
+    b, ob = _pair(s, o, y, top)
+    m = s.mult(a, b)
+    om = o.mult(oa, ob, top)
+    assert _eq(m, om, top, s.rows)
+    s.rescale_one(m)
+    om = o.rescale(om, top)
+    assert _eq(m, om, top - 1, s.rows)
+    got = s.decrypt_slots(m)
+    assert np.abs(got.real - x * y).max() < 1e-6
+
+
+@pytest.mark.parametrize("step", [1, 4, 64, -1])
+def test_rotate_bit_exact(s1, step):
+    s, o = s1
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, 8192) / 8
+    top = s.top()
+    a, oa = _pair(s, o, x, top)
+    r = s.rotate(a, step)
+    assert _eq(r, o.rotate(oa, step, top), top, s.rows)
+    assert np.abs(s.decrypt_slots(r).real - np.roll(x, -step)).max() < 1e-6
+
+
+def test_rotate_lower_level_and_sum(s1):
+    s, o = s1
+    rng = np.random.default_rng(4)
+    x = rng.normal(0, 1, 8192) / 8
+    top = 4
+    a, oa = _pair(s, o, x, top)
+    r = s.rotate_and_sum(a, 1, 16)
+    assert _eq(r, o.rotate_and_sum(oa, 1, 16, top), top, s.rows)
+    want = sum(np.roll(x, -k) for k in range(16))
+    assert np.abs(s.decrypt_slots(r).real - want).max() < 1e-5
+
+
+def test_pt_ops_bit_exact(s1):
+    s, o = s1
+    rng = np.random.default_rng(5)
+    x, w = rng.normal(0, 1, 512) / 8, rng.normal(0, 1, 512)
+    top = s.top()
+    a, oa = _pair(s, o, x, top)
+    pt = s.pt(w, top, 2.0**40, a.slots)
+    rows = s.encode(w, slots=a.slots, scale=2.0**40, top=top)
+    assert (rows == o.encode(w, a.slots, 2.0**40, top)).all()
+    assert _eq(s.mult_pt(a, pt, 2.0**40), o.mult_pt(oa, rows, top), top, s.rows)
+    assert _eq(s.add_pt(a, pt), o.add_pt(oa, rows, top), top, s.rows)
+
+
+def test_config2_relin_and_rotation_bit_exact(s2):
+    s, o = s2
+    rng = np.random.default_rng(6)
+    x, y = rng.normal(0, 1, 1024) / 8, rng.normal(0, 1, 1024) / 8
+    top = s.top()
+    a, oa = _pair(s, o, x, top)
+    b, ob = _pair(s, o, y, top)
+    m = s.mult(a, b)
+    assert _eq(m, o.mult(oa, ob, top), top, s.rows)
+    r = s.rotate(a, 5)
+    assert _eq(r, o.rotate(oa, 5, top), top, s.rows)
+    # a level with a partial top digit (limbs 0..12: digits of 8 + 5 limbs)
+    lo = 12
+    a2, oa2 = _pair(s, o, x, lo)
+    r2 = s.rotate(a2, 1)
+    assert _eq(r2, o.rotate(oa2, 1, lo), lo, s.rows)
+    # config 2's digits are as large as P (8 x 50 bits each), so a key switch adds ~N sigma digit / P ~ 2^18 to the
+    # coefficients: ~1e-6 on slots at scale 2^40
+    assert np.abs(s.decrypt_slots(r2).real[:1024] - np.roll(np.pad(x, (0, r2.slots - 1024)), -1)[:1024]).max() < 2e-5
+
+
+def test_batched_ops_equal_single(s1):
+    s, o = s1
+    rng = np.random.default_rng(7)
+    top = s.top()
+    cts = [s.encrypt(rng.normal(0, 1, 512) / 8, top=top) for _ in range(3)]
+    batch = fhe.Ct(torch.cat([c.data for c in cts]), top, cts[0].scale, cts[0].slots)
+    rb = s.rotate(batch, 2)
+    for i, c in enumerate(cts):
+        r = s.rotate(c, 2)
+        assert torch.equal(rb.data[i, :, : top + 1], r.data[0, :, : top + 1])

@@ -1,0 +1,308 @@
+"""Throughput of the CKKS key-switching hot path on B200: BASELINE config 2 (the headline microbenchmark).
+
+A step is one pass of the hot path over one batch of 64 ciphertexts at N = 2^16 (24 x 50-bit Q limbs + 8 x 50-bit
+special primes, dnum 3) whose residues are uniform random mod each prime (seeded): a forward + inverse NTT pass over
+the batch (3072 rows each way) and the batch's key switches, 1 relinearization and the 16 rotations by 2^k,
+k = 0..15. Rotation by 2^15 is the identity at N = 2^16 (g = 5^0 = 1) and runs as a copy, so 16 key switches per
+ciphertext are counted (1024 per step per GPU). `value` = key switches per second over the whole job with the inputs
+resident in HBM; `e2e` = the same step through the public API with the inputs copied in from pinned host memory and
+the step's result (the summed outputs) copied back, inside the timed region.
+
+Multi-GPU: one process per GPU, every rank its own batch (independent ciphertexts, keys replicated; no collective on
+the data path): weak scaling, time = max over ranks.
+
+--impl reference: the reference's CPU path for the same workload (the oracle port of crates/pc-host, all host
+threads), rank 0 only; the same metric.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "key-switches/s at N=2^16 (config 2: 24+8 x 50-bit limbs, dnum 3, batch 64)"
+UNIT = "key-switches/s"
+BATCH = 64
+ROT_STEPS = [1 << k for k in range(16)]  # 2^15 is the identity at N = 2^16
+KS_PER_CT = 1 + sum(1 for s in ROT_STEPS if s % (1 << 15))
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi samples during the timed region: median SM MHz under load and the throttle reasons seen."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU path
+_CPU = {}
+
+
+def cpu_rate(samples):
+    """Key switches per second of the oracle port (crates/pc-host restated) on this host's cores: `samples` rotation
+    key switches of one config-2 ciphertext. Returns (rate, cores, seconds)."""
+    import numpy as np
+
+    from perseus_b200 import fhe
+    from tests import _oracle as O
+
+    if not _CPU:
+        ch = fhe.config2_chain()
+        o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+        o.keygen(0, 192, 3.2, [1, fhe.rotation_galois(1, ch.log_n)])
+        rng = np.random.default_rng(0)
+        x = o.ct()
+        for r in range(o.nq):
+            x[:, r] = rng.integers(0, ch.q[r], (2, o.n), dtype=np.uint64)
+        o.rotate(x, 1, o.nq - 1)  # warm
+        _CPU.update(o=o, x=x)
+    o, x = _CPU["o"], _CPU["x"]
+    cores = O.lib().orc_get_threads()
+    t0 = time.perf_counter()
+    for _ in range(samples):
+        o.rotate(x, 1, o.nq - 1)
+    dt = time.perf_counter() - t0
+    return samples / dt, cores, dt
+
+
+def run_reference(a):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    for _ in range(max(a.warmup, 1)):
+        cpu_rate(1)
+    times, cores = [], 0
+    for _ in range(a.steps):
+        _, cores, dt = cpu_rate(1)
+        times.append(dt)
+    rate = len(times) / sum(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic (uniform residues, seeded)",
+        "config": {"workload": "config 2: hybrid key switch (rotation) of one N=2^16 ciphertext per step",
+                   "limbs": "24+8 x 50-bit", "dnum": 3},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "one rotation key switch of one config-2 ciphertext per step (oracle port of "
+                                   "crates/pc-host, OpenMP over rows)"},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU path
+def run_ours(a):
+    import torch
+
+    from perseus_b200 import _lib as L
+    from perseus_b200 import fhe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    ch = fhe.config2_chain()
+    s = fhe.Session(ch, rot_steps=ROT_STEPS, k_max=BATCH, seed=0)
+    n, nq, rows = ch.n, len(ch.q), ch.rows
+    # the batch: residues uniform mod each prime, seeded per rank
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.zeros((BATCH, 2, rows, n), dtype=torch.int64, device="cuda")
+    for r in range(nq):
+        x[:, :, r].random_(0, ch.q[r], generator=g)
+    ct = fhe.Ct(x, nq - 1, 2.0**40, n // 2)
+    ntt_rows = BATCH * 2 * nq
+    nbuf = torch.empty((ntt_rows, n), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def step(inp, ntt_t=None):
+        # NTT / INTT pass over the batch's Q rows (3072 rows each way)
+        nbuf.view(BATCH, 2, nq, n).copy_(inp.data[:, :, :nq])
+        if ntt_t is not None:
+            ntt_t[0].record(stream)
+        s.ntt_batch(nbuf, ntt_rows, inverse=False)
+        if ntt_t is not None:
+            ntt_t[1].record(stream)
+        s.ntt_batch(nbuf, ntt_rows, inverse=True)
+        # 1 relinearization + 16 rotations (2^15: the identity copy), summed into one result
+        acc = s.mult(inp, inp)
+        for st in ROT_STEPS:
+            s.inplace_add(acc, s.rotate(inp, st))
+        return acc
+
+    for _ in range(a.warmup):
+        step(ct)
+    torch.cuda.synchronize()
+    # device-resident timing: 1.5 GiB of residues per batch, larger than the 126 MB L2 (no flush needed)
+    clocks = Clocks(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = L.lib().pcb_launch_count()
+    t0, t1 = ev(), ev()
+    ntt_ev = [(ev(), ev()) for _ in range(a.steps)]
+    t0.record(stream)
+    for i in range(a.steps):
+        step(ct, ntt_ev[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    launches = L.lib().pcb_launch_count() - l0
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / a.steps
+    ntt_ms = sum(b.elapsed_time(e) for b, e in ntt_ev) / a.steps
+    # e2e through the public API: pinned host inputs in, the summed result out, every step
+    host_in = torch.empty((BATCH, 2, nq, n), dtype=torch.int64, pin_memory=True)
+    host_in.copy_(x[:, :, :nq])
+    host_out = torch.empty((BATCH, 2, nq, n), dtype=torch.int64, pin_memory=True)
+    dev_in = fhe.Ct(torch.zeros_like(x), nq - 1, 2.0**40, n // 2)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record(stream)
+    for _ in range(a.steps):
+        dev_in.data[:, :, :nq].copy_(host_in, non_blocking=True)
+        res = step(dev_in)
+        host_out.copy_(res.data[:, :, :nq], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    barrier()
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, ntt_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, ntt_ms = t.tolist()
+    ks = world * BATCH * KS_PER_CT
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    ntt_bytes = 2 * ntt_rows * n * 8
+    ntt_gbs = ntt_bytes / (ntt_ms * 1e-3) / 1e9
+    traffic = None
+    try:
+        traffic = json.load(open(os.path.join(ROOT, "profiles", "ntt_fwd_traffic.json")))["bytes_per_3072_row_pass"]
+    except Exception:
+        pass
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u64", "data": "synthetic (uniform residues mod each prime, seeded)",
+            "config": {"workload": "config 2: per GPU 64 ciphertexts, NTT+INTT pass (3072 rows) + 1 relin + 16 "
+                                   "rotations 2^0..2^15 (2^15 = identity copy, 16 key switches / ct counted)",
+                       "N": n, "limbs": "24+8 x 50-bit", "dnum": 3, "batch_per_gpu": BATCH,
+                       "parallelism": f"replicas x{world} (independent ciphertexts, no collective)",
+                       "l2": "inputs larger than L2 (1.5 GiB of residues per batch)"},
+            "e2e": {"value": ks / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 8,
+                    "d2h_bytes_per_step": host_out.numel() * 8},
+            "gpu_launches": int(launches),
+            "roofline": {"kernel": "ntt fwd (fwd_cols + fwd_rows) over the batch's 3072 rows", "bound": "hbm",
+                         "achieved": ntt_gbs, "peak": hbm, "unit": "GB/s", "frac": ntt_gbs / hbm,
+                         "traffic": traffic, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                         "ms": ntt_ms, "algorithmic_bytes": ntt_bytes},
+            "clocks": clk,
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            try:
+                rate, cores, dt = cpu_rate(2)
+                line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                                        "sample": f"2 rotation key switches of one config-2 ciphertext ({dt:.1f} s)"}
+            except Exception as e:  # the baseline is reported, never required
+                line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": None, "kind": "port",
+                                        "sample": f"failed: {e}"}
+        print(json.dumps(line), flush=True)
+    del s
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

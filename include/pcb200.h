@@ -304,6 +304,9 @@ const PcbKernelTable* pc_table_u64_barrett64(void);
 const PcbRingTable* pc_ring_u64_14(void);
 const PcbRingTable* pc_ring_u64_16(void);
 
+/* Kernels this library has launched since it was loaded (all threads, all devices). */
+uint64_t pcb_launch_count(void);
+
 /* ================================================================ 2. evaluator */
 
 typedef struct PcbCtx PcbCtx;

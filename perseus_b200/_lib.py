@@ -171,6 +171,7 @@ def lib():
         "pc_ring_u64_14": (C.POINTER(RingTable), []),
         "pc_ring_u64_16": (C.POINTER(RingTable), []),
         "pcb_last_error": (C.c_char_p, []),
+        "pcb_launch_count": (C.c_uint64, []),
         "pcb_ctx_bytes": (i64, [C.POINTER(Params), i32]),
         "pcb_ctx_create": (C.c_int, [C.POINTER(Params), i32, vp, C.c_size_t, vp, C.POINTER(vp)]),
         "pcb_ctx_destroy": (None, [vp]),

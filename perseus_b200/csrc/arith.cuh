@@ -94,8 +94,12 @@ __device__ __forceinline__ uint64_t* at_row_w(const PcbPolyRef& r, int c, int pa
 }
 __device__ __forceinline__ int rs_row(const PcbRowSet& rs, int y) { return y < rs.nq ? y : rs.qmax + (y - rs.nq); }
 
+// process-wide count of kernels this library launched (pcb_launch_count)
+void note_launches(unsigned n);
+
 }  // namespace pcb
 
-// launcher return codes (crates/pc-kernels/kernels/args.cuh:1036)
+// launcher return codes (crates/pc-kernels/kernels/args.cuh:1036); PCB_LAUNCH_RESULT counts one launch
 #define PCB_BAD_ARGS (-1)
-#define PCB_LAUNCH_RESULT() ((int)cudaGetLastError())
+#define PCB_LAUNCHED(n) (pcb::note_launches(n), (int)cudaGetLastError())
+#define PCB_LAUNCH_RESULT() PCB_LAUNCHED(1)

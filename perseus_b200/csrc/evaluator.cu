@@ -654,7 +654,7 @@ int launch_pt_op(PcbCtx& c, const uint64_t* x, const uint64_t* pt, uint64_t* out
     const dim3 g((unsigned)(c.n / 256), top + 1, 2 * K);
     if (c.logn == 14) pt_op<14, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
     else pt_op<16, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
-    return (int)cudaGetLastError();
+    return PCB_LAUNCH_RESULT();
 }
 
 }  // namespace
@@ -922,7 +922,7 @@ int pcb_decrypt(PcbCtx* c, const uint64_t* ct, int32_t top, int32_t nslots, doub
     const size_t n = c->n;
     const PcbPrimeConst pc = hm::prime_const(c->primes[0]);
     dec_row0<<<(unsigned)(n / 256), 256, 0, s>>>(ct, ct + (size_t)c->rows * n, c->s_eval, c->row, pc);
-    CK(cudaGetLastError());
+    CK(PCB_LAUNCH_RESULT());
     PcbNttArgs a = ntt_args(*c, c->row, c->id_roff, c->id_rprime, 1);
     CK(c->tab->ntt_inv(&a, s));
     std::vector<uint64_t> m(n);

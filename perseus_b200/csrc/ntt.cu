@@ -314,7 +314,7 @@ int fwd(const PcbNttArgs* ap, cudaStream_t s) {
         fwd_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
         fwd_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
     }
-    return PCB_LAUNCH_RESULT();
+    return PCB_LAUNCHED(2u * (unsigned)((a.nrows + ch - 1) / ch));
 }
 
 template <int LOGN>
@@ -333,7 +333,7 @@ int inv(const PcbNttArgs* ap, cudaStream_t s) {
         inv_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
         inv_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
     }
-    return PCB_LAUNCH_RESULT();
+    return PCB_LAUNCHED(2u * (unsigned)((a.nrows + ch - 1) / ch));
 }
 
 template int fwd<14>(const PcbNttArgs*, cudaStream_t);

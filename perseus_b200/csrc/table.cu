@@ -63,12 +63,21 @@ const PcbRingTable g_ring14 = make_ring<14>();
 const PcbRingTable g_ring16 = make_ring<16>();
 }  // namespace
 
+#include <atomic>
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}
+
 namespace pcb {
+void note_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
 // the full launcher set at either ring size, for the evaluator
 const PcbKernelTable* table_for(int logn) { return logn == 14 ? &g_table14 : logn == 16 ? &g_table16 : nullptr; }
 }  // namespace pcb
 
 extern "C" {
+uint64_t pcb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 const PcbKernelTable* pc_table_u64_barrett64(void) { return &g_table16; }
 const PcbRingTable* pc_ring_u64_14(void) { return &g_ring14; }
 const PcbRingTable* pc_ring_u64_16(void) { return &g_ring16; }

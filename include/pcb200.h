@@ -372,6 +372,13 @@ int pcb_mult(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, i
              cudaStream_t stream);
 /* in place: rows 0..top-1 = q_top^-1 (x - lift(x_top)) (crates/pc-gpu/src/rescale.rs:230) */
 int pcb_rescale(PcbCtx* ctx, uint64_t* ct, int32_t top, int32_t K, cudaStream_t stream);
+/* The rescale of ONE ciphertext (as pcb_rescale with K = 1, the same words out) without any workspace from the
+ * arena: its working rows live in a fixed 16 MiB device array the library owns (every GPU that loads the library
+ * holds it until exit). For callers that must not allocate device memory where they call it. No counterpart in the
+ * reference. Limit: 2 (nq + kp) N <= 2^21 words, else -1 with a message. The first call on each device looks the
+ * array's address up (make it before any stream capture); calls share the array, so calls that overlap on the GPU
+ * (other streams, other threads) race — issue them in one stream order. */
+int pcb_rescale_static(PcbCtx* ctx, uint64_t* ct, int32_t top, cudaStream_t stream);
 /* out = rot(x, step), left by step slots (crates/pc-gpu/src/rotate.rs:147-204); out must not alias x */
 int pcb_rotate(PcbCtx* ctx, const uint64_t* x, int64_t step, uint64_t* out, int32_t top, int32_t K,
                cudaStream_t stream);

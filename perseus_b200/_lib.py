@@ -188,6 +188,7 @@ def lib():
         "pcb_sub": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_mult": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_rescale": (C.c_int, [vp, vp, i32, i32, vp]),
+        "pcb_rescale_static": (C.c_int, [vp, vp, i32, vp]),
         "pcb_rotate": (C.c_int, [vp, vp, i64, vp, i32, i32, vp]),
         "pcb_rotate_and_sum": (C.c_int, [vp, vp, i64, i64, vp, i32, i32, vp]),
         "pcb_mult_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),

@@ -1134,3 +1134,91 @@ int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaSt
 }
 
 }  // extern "C"
+
+// ================================================================================================ allocation-free rescale
+// pcb_rescale_static: the rescale of one ciphertext with its working rows in a fixed device array that this library
+// owns, for callers that cannot allocate device memory while they run: code that may only use memory set aside
+// ahead of time (a host that has handed all of its device memory to an arena, or a caller whose allocator must
+// not be entered from where it calls this). The context's arena still holds the tables; the op itself takes no
+// workspace from it and allocates nothing.
+#include <mutex>
+
+namespace {
+
+// Working rows of pcb_rescale_static: the inverse-transformed top row and the correction rows of both parts, in the
+// ciphertext layout [2][nq + kp][N]. 2^21 words = 16 MiB, held on every GPU that loads the library until exit.
+constexpr size_t STATIC_SCRATCH_WORDS = (size_t)1 << 21;
+static __device__ __align__(256) uint64_t g_static_scratch[STATIC_SCRATCH_WORDS];
+
+// The array's device address per device, looked up once per device with that device current (host code cannot
+// use the symbol itself: on the host it names a stand-in, not device memory).
+constexpr int MAX_DEVICES = 64;
+std::mutex g_scratch_mu;
+uint64_t* g_scratch_ptr[MAX_DEVICES] = {};
+
+int static_scratch(uint64_t** out) {
+    int dev = -1;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= MAX_DEVICES) return fail(PCB_BAD_ARGS, "device %d beyond %d", dev, MAX_DEVICES);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess)
+            return fail((int)e, "cudaGetSymbolAddress of the static scratch failed on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        g_scratch_ptr[dev] = (uint64_t*)p;
+    }
+    *out = g_scratch_ptr[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pcb_rescale_static(PcbCtx* c, uint64_t* ct, int32_t top, cudaStream_t s) {
+    if (!c || !ct) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    if (top < 1) return fail(PCB_BAD_ARGS, "rescale at the bottom limb");
+    const size_t need = c->ct_words();
+    if (need > STATIC_SCRATCH_WORDS)
+        return fail(PCB_BAD_ARGS,
+                    "pcb_rescale_static: a ciphertext of %d rows of N = %zu needs %zu scratch words, beyond the "
+                    "maximum of %zu (2 (nq + kp) N <= 2^21); use pcb_rescale",
+                    c->rows, c->n, need, STATIC_SCRATCH_WORDS);
+    uint64_t* scratch = nullptr;
+    rc = static_scratch(&scratch);
+    if (rc) return rc;
+    // the same three launches as pcb_rescale with K = 1; every scratch word read is written first in this call
+    const LevelPlan& l = c->lv[top];
+    PcbNttArgs a = ntt_args(*c, scratch, l.rs_intt_roff, l.rs_intt_rprime, 2);
+    a.src = ct;
+    a.soff = l.rs_intt_roff;
+    CK(c->tab->ntt_inv(&a, s));
+    PcbRescaleArgs r;
+    memset(&r, 0, sizeof r);
+    r.x = ct_ref(*c, scratch);
+    r.tmp = ct_ref(*c, scratch);
+    r.A = l.rs_A;
+    r.As = l.rs_As;
+    r.qam = l.rs_qam;
+    r.pr = c->pr;
+    r.ca = r.cb = 1;
+    r.top = top;
+    r.nrows = top;
+    r.K = 1;
+    r.ndrop = 1;
+    CK(c->tab->rescale_coef(&r, s));
+    PcbNttArgs f = ntt_args(*c, scratch, l.rs_ntt_roff, l.rs_ntt_rprime, 2 * top);
+    f.epi = 3;
+    f.eout = ct;
+    f.ex = ct;
+    f.es = l.rs_alpha;
+    f.ess = l.rs_alphas;
+    CK(c->tab->ntt_fwd(&f, s));
+    return 0;
+}
+
+}  // extern "C"

@@ -103,6 +103,7 @@ struct PcbCtx {
     int nq = 0, kp = 0, rows = 0, dnum = 0, alpha = 0, k_max = 0, nkeys = 0;
     std::vector<uint64_t> primes;
     const PcbKernelTable* tab = nullptr;
+    bool narrow = false;  // every prime below 2^52: the 26-bit-split conversion and inner-product kernels
     Arena arena;
     // device tables
     PcbPrimeConst* pr = nullptr;
@@ -548,7 +549,7 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     b.pr = c.pr;
     b.njobs = K * l.ndig;
     b.max_tgt = l.mu_max_tgt;
-    CK(c.tab->bconv(&b, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, s) : ks::bconv_run<16>(&b, c.narrow, s));
     PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
     CK(c.tab->ntt_fwd(&f, s));
     return 0;
@@ -559,8 +560,9 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         cudaStream_t s) {
     const LevelPlan& l = c.lv[top];
     const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
-    for (int c0i = 0; c0i < K; c0i += 8) {
-        const int kk = std::min(8, K - c0i);
+    const int kmax = c.narrow ? 4 : 8;
+    for (int c0i = 0; c0i < K; c0i += kmax) {
+        const int kk = std::min(kmax, K - c0i);
         PcbKsArgs a;
         memset(&a, 0, sizeof a);
         a.c1 = c1 + c0i * cw;
@@ -588,7 +590,7 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.c0_mode = c0_mode;
         a.nq = c.nq;
         a.nrows = top + 1 + c.kp;
-        CK(c.tab->ks_dot(&a, s));
+        CK(c.logn == 14 ? ks::ks_dot_run<14>(&a, c.narrow, s) : ks::ks_dot_run<16>(&a, c.narrow, s));
     }
     return 0;
 }
@@ -609,7 +611,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     b.pr = c.pr;
     b.njobs = 2 * K;
     b.max_tgt = top + 1;
-    CK(c.tab->bconv(&b, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, s) : ks::bconv_run<16>(&b, c.narrow, s));
     PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
     f.epi = accumulate ? 2 : 1;
     f.eout = out;
@@ -687,6 +689,8 @@ static int init_ctx(PcbCtx& c, const PcbParams* prm, int nkeys) {
         if (p < 3 || !(p & 1) || p >= (1ull << 61) || (p - 1) % (2 * c.n))
             return fail(PCB_BAD_ARGS, "prime %llu is not an odd NTT prime below 2^61 (p = 1 mod 2N)", (unsigned long long)p);
     c.tab = table_for(c.logn);
+    c.narrow = true;
+    for (uint64_t p : c.primes) c.narrow = c.narrow && p < (1ull << 52);
     return 0;
 }
 

@@ -2,9 +2,14 @@
 // product (ks_dot). Semantics: crates/pc-kernels/kernels/args.cuh:109-141 (BconvArgs) and :202-228 (KsArgs); host
 // twins crates/pc-host/src/bconv.rs:13-108 and crates/pc-host/src/ks.rs:60-140.
 //
-// Both are multiply-accumulate streams over 64-bit residues: every product goes into a 128-bit accumulator
-// (mad.lo.cc / madc.hi) and each output is reduced once. The conversion matrix of a job and its target primes'
-// Barrett constants sit in shared memory; source words stay in registers across all targets.
+// Both are multiply-accumulate streams over 64-bit residues, each output reduced once. Two accumulator forms:
+//  - general (any prime < 2^62): a 128-bit accumulator fed by mad.lo.cc / madc.hi;
+//  - narrow (every residue and constant < 2^52, the 50-bit chains): operands split at bit 26 into 26-bit halves, and
+//    three 64-bit partial sums (hi x hi, the two cross products, lo x lo) fed by one 32 x 32 + 64 IMAD.WIDE each —
+//    four integer multiply-adds per product and no carry chain; up to 2^12 products fit before any partial sum could
+//    overflow. The table's launchers use the general form; the evaluator picks the narrow one when its chain allows.
+// The conversion matrix of a job and its target primes' Barrett constants sit in shared memory; source words stay in
+// registers across all targets.
 #include "arith.cuh"
 
 namespace pcb {
@@ -13,9 +18,30 @@ namespace ks {
 constexpr int BX = 128;
 constexpr int MAX_SRC = 16;
 constexpr int MAX_TGT = 64;
+constexpr uint64_t LO26 = (1ull << 26) - 1;
+
+// Three-part accumulator of 26-bit-split products: value = H 2^52 + M 2^26 + L
+struct Acc3 {
+    uint64_t h, m, l;
+};
+__device__ __forceinline__ void mac3(Acc3& a, uint32_t x1, uint32_t x0, uint32_t y1, uint32_t y0) {
+    a.h += (uint64_t)x1 * y1;
+    a.m += (uint64_t)x1 * y0;
+    a.m += (uint64_t)x0 * y1;
+    a.l += (uint64_t)x0 * y0;
+}
+__device__ __forceinline__ Acc to_acc(const Acc3& a) {
+    const uint64_t t = a.m << 26;
+    uint64_t lo = a.l + t;
+    uint64_t hi = (a.m >> 38) + (lo < t);
+    const uint64_t u = a.h << 52;
+    lo += u;
+    hi += (a.h >> 12) + (lo < u);
+    return Acc{lo, hi};
+}
 
 // ------------------------------------------------------------------------------------------------ bconv
-template <int LOGN>
+template <int LOGN, bool NARROW>
 __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     __shared__ uint64_t sM[MAX_SRC * MAX_TGT];
     __shared__ uint64_t sP[MAX_TGT], sM0[MAX_TGT], sM1[MAX_TGT];
@@ -30,7 +56,11 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     const uint64_t* trow = pool + 3 * ns;
     const uint64_t* tprime = pool + 3 * ns + nt;
     const uint64_t* M = pool + 3 * ns + 2 * nt;
-    for (int e = threadIdx.x; e < ns * nt; e += BX) sM[e] = M[e];
+    for (int e = threadIdx.x; e < ns * nt; e += BX) {
+        const uint64_t v = M[e];
+        // narrow: the two 26-bit halves packed as (hi << 32) | lo for one 8-byte shared load
+        sM[e] = NARROW ? ((v >> 26) << 32) | (v & LO26) : v;
+    }
     for (int t = threadIdx.x; t < nt; t += BX) {
         const PcbPrimeConst& pc = a.pr[tprime[t]];
         sP[t] = pc.p;
@@ -69,6 +99,29 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
         }
         bmod = rbw + ns;
     }
+    if (NARROW) {
+        uint32_t y1[MAX_SRC], y0[MAX_SRC];
+#pragma unroll
+        for (int i = 0; i < MAX_SRC; ++i) {
+            y1[i] = (uint32_t)(y[i] >> 26);
+            y0[i] = (uint32_t)(y[i] & LO26);
+        }
+        for (int t = 0; t < nt; ++t) {
+            Acc3 acc{0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < MAX_SRC; ++i) {
+                if (i < ns) {
+                    const uint64_t m = sM[i * nt + t];
+                    mac3(acc, y1[i], y0[i], (uint32_t)(m >> 32), (uint32_t)m);
+                }
+            }
+            const uint64_t p = sP[t];
+            uint64_t r = reduce(to_acc(acc), p, sM0[t], sM1[t]);
+            if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
+            dst[(size_t)sRow[t] << LOGN] = r;
+        }
+        return;
+    }
     for (int t = 0; t < nt; ++t) {
         Acc acc{0, 0};
 #pragma unroll
@@ -82,20 +135,45 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
 }
 
 template <int LOGN>
-int bconv_launch(const PcbBconvArgs* ap, cudaStream_t s) {
+int bconv_run(const PcbBconvArgs* ap, bool narrow, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbBconvArgs& a = *ap;
     if (a.njobs < 0 || a.max_tgt < 0 || a.max_tgt > MAX_TGT || !a.src || !a.dst || !a.jobs || !a.pool || !a.pr)
         return PCB_BAD_ARGS;
     if (a.njobs == 0) return 0;
-    bconv<LOGN><<<dim3((1 << LOGN) / BX, a.njobs), BX, 0, s>>>(a);
+    const dim3 g((1 << LOGN) / BX, a.njobs);
+    if (narrow) bconv<LOGN, true><<<g, BX, 0, s>>>(a);
+    else bconv<LOGN, false><<<g, BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int bconv_launch(const PcbBconvArgs* ap, cudaStream_t s) {
+    return bconv_run<LOGN>(ap, false, s);
 }
 
 // ------------------------------------------------------------------------------------------------ ks_dot
 // s1 = sum_d D_d a_d, s0 = C0 + sum_d D_d b_d for K <= KMAX ciphertexts x R keys; D_d[t] is c1 itself on digit d's
 // own rows, else the ModUp output; each key word is read once per launch and reused by all K ciphertexts.
-template <int LOGN, int KMAX>
+template <int LOGN>
+__device__ __forceinline__ void ks_store(const PcbKsArgs& a, int c, int r, uint32_t t, size_t roff, uint32_t o,
+                                         uint64_t r0, uint64_t r1, uint64_t p, uint64_t pm, uint64_t pms) {
+    const uint64_t* c0 = (const uint64_t*)a.c0;
+    if ((a.c0_mode & 3) == 1) {
+        if ((int)t < a.nq) r0 = add_mod(r0, shoup(c0[(size_t)c * a.ct_stride + roff], pm, pms, p), p);
+    } else if ((a.c0_mode & 3) == 2) {
+        r0 = add_mod(r0, c0[(size_t)c * a.ct_stride + roff], p);
+    }
+    const size_t ob = (size_t)c * a.out_ct_stride + (size_t)r * a.out_rot_stride + ((size_t)t << LOGN) + o;
+    if (a.c0_mode & PCB_KS_ACC) {
+        r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
+        r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
+    }
+    ((uint64_t*)a.out0)[ob] = r0;
+    ((uint64_t*)a.out1)[ob] = r1;
+}
+
+template <int LOGN, int KMAX, bool NARROW>
 __global__ void __launch_bounds__(BX) ks_dot(PcbKsArgs a) {
     const uint32_t t = a.rows[blockIdx.y];
     const PcbPrimeConst& pc = a.pr[t];
@@ -105,56 +183,70 @@ __global__ void __launch_bounds__(BX) ks_dot(PcbKsArgs a) {
     const size_t roff = ((size_t)t << LOGN) + idx;
     const uint64_t* c1 = (const uint64_t*)a.c1;
     const uint64_t* mu = (const uint64_t*)a.modup;
-    const uint64_t* c0 = (const uint64_t*)a.c0;
     uint64_t pm = 0, pms = 0;
     if ((a.c0_mode & 3) == 1 && (int)t < a.nq) {
         pm = ((const uint64_t*)a.pmod)[t];
         pms = ((const uint64_t*)a.pmods)[t];
     }
     for (int r = 0; r < a.R; ++r) {
-        Acc s0[KMAX], s1[KMAX];
-#pragma unroll
-        for (int c = 0; c < KMAX; ++c) s0[c] = s1[c] = Acc{0, 0};
         const uint64_t* kb = (const uint64_t*)a.kb[r] + roff;
         const uint64_t* ka = (const uint64_t*)a.ka[r] + roff;
-        for (int d = 0; d < a.ndig; ++d) {
-            const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
-            const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
-#pragma unroll
-            for (int c = 0; c < KMAX; ++c) {
-                if (c < a.K) {
-                    const uint64_t x = d == dt ? c1[(size_t)c * a.ct_stride + roff]
-                                               : mu[(size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff];
-                    mac(s0[c], x, b);
-                    mac(s1[c], x, av);
-                }
-            }
-        }
         const uint32_t k = a.autok[r];
         const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
+        if (NARROW) {
+            Acc3 s0[KMAX], s1[KMAX];
 #pragma unroll
-        for (int c = 0; c < KMAX; ++c) {
-            if (c < a.K) {
-                uint64_t r0 = reduce(s0[c], pc), r1 = reduce(s1[c], pc);
-                if ((a.c0_mode & 3) == 1) {
-                    if ((int)t < a.nq) r0 = add_mod(r0, shoup(c0[(size_t)c * a.ct_stride + roff], pm, pms, p), p);
-                } else if ((a.c0_mode & 3) == 2) {
-                    r0 = add_mod(r0, c0[(size_t)c * a.ct_stride + roff], p);
+            for (int c = 0; c < KMAX; ++c) s0[c] = s1[c] = Acc3{0, 0, 0};
+            for (int d = 0; d < a.ndig; ++d) {
+                const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
+                const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
+                uint64_t x[KMAX];
+#pragma unroll
+                for (int c = 0; c < KMAX; ++c)
+                    if (c < a.K)
+                        x[c] = d == dt ? c1[(size_t)c * a.ct_stride + roff]
+                                       : mu[(size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff];
+                const uint32_t b1 = (uint32_t)(b >> 26), b0 = (uint32_t)(b & LO26);
+                const uint32_t a1 = (uint32_t)(av >> 26), a0 = (uint32_t)(av & LO26);
+#pragma unroll
+                for (int c = 0; c < KMAX; ++c) {
+                    if (c < a.K) {
+                        const uint32_t x1 = (uint32_t)(x[c] >> 26), x0 = (uint32_t)(x[c] & LO26);
+                        mac3(s0[c], x1, x0, b1, b0);
+                        mac3(s1[c], x1, x0, a1, a0);
+                    }
                 }
-                const size_t ob = (size_t)c * a.out_ct_stride + (size_t)r * a.out_rot_stride + ((size_t)t << LOGN) + o;
-                if (a.c0_mode & PCB_KS_ACC) {
-                    r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
-                    r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
-                }
-                ((uint64_t*)a.out0)[ob] = r0;
-                ((uint64_t*)a.out1)[ob] = r1;
             }
+#pragma unroll
+            for (int c = 0; c < KMAX; ++c)
+                if (c < a.K)
+                    ks_store<LOGN>(a, c, r, t, roff, o, reduce(to_acc(s0[c]), pc), reduce(to_acc(s1[c]), pc), p, pm, pms);
+        } else {
+            Acc s0[KMAX], s1[KMAX];
+#pragma unroll
+            for (int c = 0; c < KMAX; ++c) s0[c] = s1[c] = Acc{0, 0};
+            for (int d = 0; d < a.ndig; ++d) {
+                const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
+                const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
+#pragma unroll
+                for (int c = 0; c < KMAX; ++c) {
+                    if (c < a.K) {
+                        const uint64_t x = d == dt ? c1[(size_t)c * a.ct_stride + roff]
+                                                   : mu[(size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff];
+                        mac(s0[c], x, b);
+                        mac(s1[c], x, av);
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < KMAX; ++c)
+                if (c < a.K) ks_store<LOGN>(a, c, r, t, roff, o, reduce(s0[c], pc), reduce(s1[c], pc), p, pm, pms);
         }
     }
 }
 
 template <int LOGN>
-int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
+int ks_dot_run(const PcbKsArgs* ap, bool narrow, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbKsArgs& a = *ap;
     if (a.K < 0 || a.K > 8 || a.R < 0 || a.ndig < 1 || a.ndig > 16 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
@@ -164,19 +256,35 @@ int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
     if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
+    if (narrow && a.K > 4) return PCB_BAD_ARGS;  // the narrow accumulators hold four ciphertexts per thread
     if (a.K == 0 || a.R == 0 || a.nrows == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.nrows);
-    if (a.K <= 1) ks_dot<LOGN, 1><<<g, BX, 0, s>>>(a);
-    else if (a.K <= 2) ks_dot<LOGN, 2><<<g, BX, 0, s>>>(a);
-    else if (a.K <= 4) ks_dot<LOGN, 4><<<g, BX, 0, s>>>(a);
-    else ks_dot<LOGN, 8><<<g, BX, 0, s>>>(a);
+    if (narrow) {
+        if (a.K <= 1) ks_dot<LOGN, 1, true><<<g, BX, 0, s>>>(a);
+        else if (a.K <= 2) ks_dot<LOGN, 2, true><<<g, BX, 0, s>>>(a);
+        else ks_dot<LOGN, 4, true><<<g, BX, 0, s>>>(a);
+    } else {
+        if (a.K <= 1) ks_dot<LOGN, 1, false><<<g, BX, 0, s>>>(a);
+        else if (a.K <= 2) ks_dot<LOGN, 2, false><<<g, BX, 0, s>>>(a);
+        else if (a.K <= 4) ks_dot<LOGN, 4, false><<<g, BX, 0, s>>>(a);
+        else ks_dot<LOGN, 8, false><<<g, BX, 0, s>>>(a);
+    }
     return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
+    return ks_dot_run<LOGN>(ap, false, s);
 }
 
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
+template int bconv_run<14>(const PcbBconvArgs*, bool, cudaStream_t);
+template int bconv_run<16>(const PcbBconvArgs*, bool, cudaStream_t);
 template int ks_dot_launch<14>(const PcbKsArgs*, cudaStream_t);
 template int ks_dot_launch<16>(const PcbKsArgs*, cudaStream_t);
+template int ks_dot_run<14>(const PcbKsArgs*, bool, cudaStream_t);
+template int ks_dot_run<16>(const PcbKsArgs*, bool, cudaStream_t);
 
 }  // namespace ks
 }  // namespace pcb

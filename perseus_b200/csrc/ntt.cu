@@ -16,6 +16,9 @@ namespace pcb {
 namespace ntt {
 
 constexpr int THREADS = 256;
+#ifndef NTT_MIN_BLOCKS
+#define NTT_MIN_BLOCKS 3  // at most 80 registers per thread: 24 warps per SM (measured faster than 4 CTAs with spills)
+#endif
 
 // ------------------------------------------------------------------------------------------------ butterflies
 __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, uint64_t p, uint64_t p2) {
@@ -35,6 +38,11 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t p) {
     x = x >= p2 ? x - p2 : x;
     return x >= p ? x - p : x;
 }
+
+// Shared-memory exchange of a 256-word block: one pad word after every 16, so both the strided (u + 16 k) and the
+// contiguous (16 u + k) views of a half-warp hit 16 distinct 8-byte bank pairs.
+constexpr int BLKPAD = 256 + 16;
+__device__ __forceinline__ int pad(int e) { return e + (e >> 4); }
 
 struct RowInfo {
     uint64_t* row;
@@ -60,9 +68,10 @@ __device__ __forceinline__ uint64_t load_in(const PcbNttArgs& a, int i, const ui
 // ------------------------------------------------------------------------------------------------ forward
 // Column pass: stages 0 .. A-1 on COLS columns; thread (cc, g) holds rows g + E k (round 1), then E g + k (round 2)
 template <int LOGN>
-__global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a, int row0) {
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ uint64_t sm[R * COLS];
+    __shared__ uint64_t stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const PcbPrimeConst& pc = a.pr[ri.pid];
@@ -74,6 +83,11 @@ __global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
     uint64_t x[E];
 #pragma unroll
     for (int k = 0; k < E; ++k) x[k] = load_in<LOGN>(a, i, ri.row, (size_t)(g + E * k) * 256 + col, p);
+    for (int t = threadIdx.x; t < R; t += THREADS) {
+        stw[t] = fw[t];
+        stws[t] = fws[t];
+    }
+    __syncthreads();
     // round 1: stages 0 .. H-1, rows g + E k: butterfly partners differ in k by E/2, E/4, ..
 #pragma unroll
     for (int s = 0; s < H; ++s) {
@@ -82,7 +96,7 @@ __global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
             const int m = 1 << s, idx = m + (k >> (H - s));
-            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+            ct_bfly(x[k], x[k + half], stw[idx], stws[idx], p, p2);
         }
     }
 #pragma unroll
@@ -98,7 +112,7 @@ __global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
             const int m = 1 << s, idx = m + (g << (s - H)) + (k >> (A - s));
-            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+            ct_bfly(x[k], x[k + half], stw[idx], stws[idx], p, p2);
         }
     }
 #pragma unroll
@@ -108,9 +122,9 @@ __global__ void __launch_bounds__(THREADS) fwd_cols(PcbNttArgs a, int row0) {
 // Row pass: the last 8 stages over 256-word blocks, 16 blocks per CTA, 16 threads per block; thread u holds words
 // u + 16 k (round 1) then 16 u + k (round 2, 16 consecutive words: vector stores and the epilogue)
 template <int LOGN>
-__global__ void __launch_bounds__(THREADS) fwd_rows(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a, int row0) {
     constexpr int A = LOGN - 8;
-    __shared__ uint64_t sm[16 * 256];
+    __shared__ uint64_t sm[16 * BLKPAD];
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const PcbPrimeConst& pc = a.pr[ri.pid];
@@ -134,12 +148,12 @@ __global__ void __launch_bounds__(THREADS) fwd_rows(PcbNttArgs a, int row0) {
             ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
         }
     }
-    uint64_t* s = sm + lb * 256;
+    uint64_t* s = sm + lb * BLKPAD;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) s[u + 16 * k] = x[k];
+    for (int k = 0; k < 16; ++k) s[pad(u + 16 * k)] = x[k];
     __syncwarp();
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = s[16 * u + k];
+    for (int k = 0; k < 16; ++k) x[k] = s[pad(16 * u + k)];
 #pragma unroll
     for (int l = 4; l < 8; ++l) {
         const int half = 16 >> (l - 3);
@@ -166,7 +180,7 @@ __global__ void __launch_bounds__(THREADS) fwd_rows(PcbNttArgs a, int row0) {
     const uint64_t* ex = (const uint64_t*)a.ex + r;
     uint64_t* eo = (uint64_t*)a.eout + r;
     const uint64_t* ed = a.ed ? (const uint64_t*)a.ed + r : eo;
-#pragma unroll 4
+#pragma unroll
     for (int k = 0; k < 16; ++k) {
         uint64_t xs = ex[k];
         for (int j = 1; j < a.xnum; ++j) xs = add_mod(xs, ex[k + (size_t)j * a.xstride], p);
@@ -181,10 +195,10 @@ __global__ void __launch_bounds__(THREADS) fwd_rows(PcbNttArgs a, int row0) {
 // ------------------------------------------------------------------------------------------------ inverse
 // Row pass first (GS spans 1 .. 128 inside 256-word blocks); thread u holds 16 u + k (round 1), then u + 16 k
 template <int LOGN>
-__global__ void __launch_bounds__(THREADS) inv_rows(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a, int row0) {
     constexpr int A = LOGN - 8;
     constexpr int N = 1 << LOGN;
-    __shared__ uint64_t sm[16 * 256];
+    __shared__ uint64_t sm[16 * BLKPAD];
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const PcbPrimeConst& pc = a.pr[ri.pid];
@@ -209,12 +223,12 @@ __global__ void __launch_bounds__(THREADS) inv_rows(PcbNttArgs a, int row0) {
             gs_bfly(x[k], x[k + h], __ldg(iw + idx), __ldg(iws + idx), p, p2);
         }
     }
-    uint64_t* s = sm + lb * 256;
+    uint64_t* s = sm + lb * BLKPAD;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) s[16 * u + k] = x[k];
+    for (int k = 0; k < 16; ++k) s[pad(16 * u + k)] = x[k];
     __syncwarp();
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = s[u + 16 * k];
+    for (int k = 0; k < 16; ++k) x[k] = s[pad(u + 16 * k)];
     // spans h = 16 .. 128: partners differ in k by h / 16
 #pragma unroll
     for (int l = 4; l < 8; ++l) {
@@ -234,9 +248,10 @@ __global__ void __launch_bounds__(THREADS) inv_rows(PcbNttArgs a, int row0) {
 
 // Column pass: spans 256 .. N/2, then the row's last-pass factor (N^-1, or es[i] with ess[i])
 template <int LOGN>
-__global__ void __launch_bounds__(THREADS) inv_cols(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a, int row0) {
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ uint64_t sm[R * COLS];
+    __shared__ uint64_t stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const PcbPrimeConst& pc = a.pr[ri.pid];
@@ -249,6 +264,11 @@ __global__ void __launch_bounds__(THREADS) inv_cols(PcbNttArgs a, int row0) {
     // round 1: row spans 1 .. E/2 (word spans 256 ..) on rows E g + k
 #pragma unroll
     for (int k = 0; k < E; ++k) x[k] = ri.row[(size_t)(E * g + k) * 256 + col];
+    for (int t = threadIdx.x; t < R; t += THREADS) {
+        stw[t] = iw[t];
+        stws[t] = iws[t];
+    }
+    __syncthreads();
 #pragma unroll
     for (int l = 0; l < H; ++l) {
         const int hk = 1 << l;
@@ -257,7 +277,7 @@ __global__ void __launch_bounds__(THREADS) inv_cols(PcbNttArgs a, int row0) {
             if (k & hk) continue;
             const int m = R >> (l + 1);
             const int idx = m + ((E * g + k) >> (l + 1));
-            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+            gs_bfly(x[k], x[k + hk], stw[idx], stws[idx], p, p2);
         }
     }
 #pragma unroll
@@ -274,7 +294,7 @@ __global__ void __launch_bounds__(THREADS) inv_cols(PcbNttArgs a, int row0) {
             if (k & hk) continue;
             const int m = R >> (l + 1);
             const int idx = m + ((g + E * k) >> (l + 1));
-            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+            gs_bfly(x[k], x[k + hk], stw[idx], stws[idx], p, p2);
         }
     }
     uint64_t ni, nis;

@@ -60,7 +60,7 @@ struct Arena {
 };
 
 struct LevelPlan {
-    int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0;
+    int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0, mu_ns = 0;  // mu_ns: limbs of every live digit (0: mixed)
     // ModUp: INTT rows (out of place, last pass x N^-1 pre_t), conversion jobs, NTT of the targets
     uint32_t *mu_intt_roff = nullptr, *mu_intt_soff = nullptr;
     int32_t* mu_intt_rprime = nullptr;
@@ -299,6 +299,9 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             for (int j = 0; j < kp; ++j) tgt[d].push_back(nq + j);
             l.mu_max_tgt = std::max(l.mu_max_tgt, (int)tgt[d].size());
         }
+        l.mu_ns = (int)src[0].size();
+        for (int d = 1; d < l.ndig; ++d)
+            if ((int)src[d].size() != l.mu_ns) l.mu_ns = 0;
         l.mu_rows = 0;
         for (int d = 0; d < l.ndig; ++d) l.mu_rows += (int)tgt[d].size();
         std::vector<uint64_t> pool;
@@ -549,7 +552,7 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     b.pr = c.pr;
     b.njobs = K * l.ndig;
     b.max_tgt = l.mu_max_tgt;
-    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, s) : ks::bconv_run<16>(&b, c.narrow, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, l.mu_ns, s));
     PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
     CK(c.tab->ntt_fwd(&f, s));
     return 0;
@@ -560,9 +563,9 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         cudaStream_t s) {
     const LevelPlan& l = c.lv[top];
     const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
-    const int kmax = c.narrow ? 4 : 8;
-    for (int c0i = 0; c0i < K; c0i += kmax) {
-        const int kk = std::min(kmax, K - c0i);
+    // one launch for the batch: every key word is read once (the inputs never alias c.ext)
+    {
+        const int c0i = 0, kk = K;
         PcbKsArgs a;
         memset(&a, 0, sizeof a);
         a.c1 = c1 + c0i * cw;
@@ -590,7 +593,7 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.c0_mode = c0_mode;
         a.nq = c.nq;
         a.nrows = top + 1 + c.kp;
-        CK(c.logn == 14 ? ks::ks_dot_run<14>(&a, c.narrow, s) : ks::ks_dot_run<16>(&a, c.narrow, s));
+        CK(c.logn == 14 ? ks::dot_all_run<14>(&a, c.narrow, s) : ks::dot_all_run<16>(&a, c.narrow, s));
     }
     return 0;
 }
@@ -611,7 +614,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     b.pr = c.pr;
     b.njobs = 2 * K;
     b.max_tgt = top + 1;
-    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, s) : ks::bconv_run<16>(&b, c.narrow, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.kp, s) : ks::bconv_run<16>(&b, c.narrow, c.kp, s));
     PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
     f.epi = accumulate ? 2 : 1;
     f.eout = out;

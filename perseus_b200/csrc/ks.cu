@@ -41,15 +41,18 @@ __device__ __forceinline__ Acc to_acc(const Acc3& a) {
 }
 
 // ------------------------------------------------------------------------------------------------ bconv
-template <int LOGN, bool NARROW>
+// NS > 0: every job of the launch has exactly NS sources (the source loops unroll without guards); 0: any count.
+template <int LOGN, bool NARROW, int NS>
 __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
+    constexpr int S = NS > 0 ? NS : MAX_SRC;
     __shared__ uint64_t sM[MAX_SRC * MAX_TGT];
     __shared__ uint64_t sP[MAX_TGT], sM0[MAX_TGT], sM1[MAX_TGT];
     __shared__ uint32_t sRow[MAX_TGT];
     const PcbBconvJob j = a.jobs[blockIdx.y];
     const uint64_t* pool = (const uint64_t*)a.pool + j.pool_off;
-    const int ns = (int)j.nsrc, nt = (int)j.ntgt;
-    if (ns < 1 || ns > MAX_SRC || nt > MAX_TGT) return;  // outside the kernel's job shape: nothing is written
+    const int ns = NS > 0 ? NS : (int)j.nsrc, nt = (int)j.ntgt;
+    // outside the kernel's job shape: nothing is written
+    if (ns < 1 || ns > MAX_SRC || nt > MAX_TGT || (int)j.nsrc != ns) return;
     const uint64_t* srow = pool;
     const uint64_t* sprime = pool + ns;
     const uint64_t* pre = pool + 2 * ns;
@@ -72,10 +75,10 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     const size_t k = (size_t)blockIdx.x * BX + threadIdx.x;
     const uint64_t* src = (const uint64_t*)a.src + ((size_t)j.src_off << LOGN) + k;
     uint64_t* dst = (uint64_t*)a.dst + ((size_t)j.dst_off << LOGN) + k;
-    uint64_t y[MAX_SRC];
+    uint64_t y[S];
 #pragma unroll
-    for (int i = 0; i < MAX_SRC; ++i) {
-        if (i < ns) {
+    for (int i = 0; i < S; ++i) {
+        if (NS > 0 || i < ns) {
             const uint64_t x = src[(size_t)srow[i] << LOGN];
             if (j.prescaled) {
                 y[i] = x;
@@ -94,23 +97,25 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
             u = (uint64_t)(ns >> 1) + (uint64_t)((ns & 1) & (((uint32_t)k * 0x9E3779B1u) >> 31));
         } else {
             double v = 0.0;
-            for (int i = 0; i < ns; ++i) v = __fma_rn((double)y[i], __longlong_as_double((long long)rbw[i]), v);
+#pragma unroll
+            for (int i = 0; i < S; ++i)
+                if (NS > 0 || i < ns) v = __fma_rn((double)y[i], __longlong_as_double((long long)rbw[i]), v);
             u = (uint64_t)floor(v + 0.5);
         }
         bmod = rbw + ns;
     }
     if (NARROW) {
-        uint32_t y1[MAX_SRC], y0[MAX_SRC];
+        uint32_t y1[S], y0[S];
 #pragma unroll
-        for (int i = 0; i < MAX_SRC; ++i) {
+        for (int i = 0; i < S; ++i) {
             y1[i] = (uint32_t)(y[i] >> 26);
             y0[i] = (uint32_t)(y[i] & LO26);
         }
         for (int t = 0; t < nt; ++t) {
             Acc3 acc{0, 0, 0};
 #pragma unroll
-            for (int i = 0; i < MAX_SRC; ++i) {
-                if (i < ns) {
+            for (int i = 0; i < S; ++i) {
+                if (NS > 0 || i < ns) {
                     const uint64_t m = sM[i * nt + t];
                     mac3(acc, y1[i], y0[i], (uint32_t)(m >> 32), (uint32_t)m);
                 }
@@ -125,8 +130,8 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     for (int t = 0; t < nt; ++t) {
         Acc acc{0, 0};
 #pragma unroll
-        for (int i = 0; i < MAX_SRC; ++i)
-            if (i < ns) mac(acc, y[i], sM[i * nt + t]);
+        for (int i = 0; i < S; ++i)
+            if (NS > 0 || i < ns) mac(acc, y[i], sM[i * nt + t]);
         const uint64_t p = sP[t];
         uint64_t r = reduce(acc, p, sM0[t], sM1[t]);
         if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
@@ -134,22 +139,34 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     }
 }
 
+template <int LOGN, bool NARROW>
+void bconv_dispatch(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
+    switch (ns_all) {
+        case 1: bconv<LOGN, NARROW, 1><<<g, BX, 0, s>>>(a); break;
+        case 2: bconv<LOGN, NARROW, 2><<<g, BX, 0, s>>>(a); break;
+        case 4: bconv<LOGN, NARROW, 4><<<g, BX, 0, s>>>(a); break;
+        case 8: bconv<LOGN, NARROW, 8><<<g, BX, 0, s>>>(a); break;
+        default: bconv<LOGN, NARROW, 0><<<g, BX, 0, s>>>(a);
+    }
+}
+
+// ns_all: the source count every job of the launch shares (1, 2, 4 or 8 get unrolled kernels), 0 when they differ
 template <int LOGN>
-int bconv_run(const PcbBconvArgs* ap, bool narrow, cudaStream_t s) {
+int bconv_run(const PcbBconvArgs* ap, bool narrow, int ns_all, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbBconvArgs& a = *ap;
     if (a.njobs < 0 || a.max_tgt < 0 || a.max_tgt > MAX_TGT || !a.src || !a.dst || !a.jobs || !a.pool || !a.pr)
         return PCB_BAD_ARGS;
     if (a.njobs == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.njobs);
-    if (narrow) bconv<LOGN, true><<<g, BX, 0, s>>>(a);
-    else bconv<LOGN, false><<<g, BX, 0, s>>>(a);
+    if (narrow) bconv_dispatch<LOGN, true>(a, ns_all, g, s);
+    else bconv_dispatch<LOGN, false>(a, ns_all, g, s);
     return PCB_LAUNCH_RESULT();
 }
 
 template <int LOGN>
 int bconv_launch(const PcbBconvArgs* ap, cudaStream_t s) {
-    return bconv_run<LOGN>(ap, false, s);
+    return bconv_run<LOGN>(ap, false, 0, s);
 }
 
 // ------------------------------------------------------------------------------------------------ ks_dot
@@ -277,10 +294,118 @@ int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
     return ks_dot_run<LOGN>(ap, false, s);
 }
 
+// ------------------------------------------------------------------------------------------------ dot over a batch
+// The evaluator's inner product: one key (R = 1), any number K of ciphertexts. Each thread reads its slot's key
+// words of every digit once and then walks the K ciphertexts, so a batch streams the key once (ks_dot re-reads it
+// for every group of <= 8). The inputs (c1, the ModUp digits, c0) must not alias the outputs. ND > 0: exactly ND
+// live digits (unrolled); 0: a.ndig <= 16.
+template <int LOGN, int ND, bool NARROW>
+__global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
+    constexpr int D = ND > 0 ? ND : 16;
+    const int nd = ND > 0 ? ND : a.ndig;
+    const uint32_t t = a.rows[blockIdx.y];
+    const PcbPrimeConst& pc = a.pr[t];
+    const uint64_t p = pc.p;
+    const uint32_t idx = blockIdx.x * BX + threadIdx.x;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t roff = ((size_t)t << LOGN) + idx;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    uint64_t pm = 0, pms = 0;
+    if ((a.c0_mode & 3) == 1 && (int)t < a.nq) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    const uint64_t* kb = (const uint64_t*)a.kb[0] + roff;
+    const uint64_t* ka = (const uint64_t*)a.ka[0] + roff;
+    uint64_t bv[D], av[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+        if (ND > 0 || d < nd) {
+            bv[d] = __ldcs(kb + (size_t)d * a.key_digit_stride);
+            av[d] = __ldcs(ka + (size_t)d * a.key_digit_stride);
+        }
+    }
+    const uint32_t k = a.autok[0];
+    const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
+    if (NARROW) {
+        uint32_t b1[D], b0[D], a1[D], a0[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            b1[d] = (uint32_t)(bv[d] >> 26);
+            b0[d] = (uint32_t)(bv[d] & LO26);
+            a1[d] = (uint32_t)(av[d] >> 26);
+            a0[d] = (uint32_t)(av[d] & LO26);
+        }
+#pragma unroll 2
+        for (int c = 0; c < a.K; ++c) {
+            Acc3 s0{0, 0, 0}, s1{0, 0, 0};
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                if (ND > 0 || d < nd) {
+                    const uint64_t x = d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + roff)
+                                               : __ldg(mu + (size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff);
+                    const uint32_t x1 = (uint32_t)(x >> 26), x0 = (uint32_t)(x & LO26);
+                    mac3(s0, x1, x0, b1[d], b0[d]);
+                    mac3(s1, x1, x0, a1[d], a0[d]);
+                }
+            }
+            ks_store<LOGN>(a, c, 0, t, roff, o, reduce(to_acc(s0), pc), reduce(to_acc(s1), pc), p, pm, pms);
+        }
+    } else {
+#pragma unroll 2
+        for (int c = 0; c < a.K; ++c) {
+            Acc s0{0, 0}, s1{0, 0};
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                if (ND > 0 || d < nd) {
+                    const uint64_t x = d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + roff)
+                                               : __ldg(mu + (size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff);
+                    mac(s0, x, bv[d]);
+                    mac(s1, x, av[d]);
+                }
+            }
+            ks_store<LOGN>(a, c, 0, t, roff, o, reduce(s0, pc), reduce(s1, pc), p, pm, pms);
+        }
+    }
+}
+
+template <int LOGN, bool NARROW>
+void dot_dispatch(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
+    switch (a.ndig) {
+        case 1: dot_all<LOGN, 1, NARROW><<<g, BX, 0, s>>>(a); break;
+        case 2: dot_all<LOGN, 2, NARROW><<<g, BX, 0, s>>>(a); break;
+        case 3: dot_all<LOGN, 3, NARROW><<<g, BX, 0, s>>>(a); break;
+        case 4: dot_all<LOGN, 4, NARROW><<<g, BX, 0, s>>>(a); break;
+        case 8: dot_all<LOGN, 8, NARROW><<<g, BX, 0, s>>>(a); break;
+        default: dot_all<LOGN, 0, NARROW><<<g, BX, 0, s>>>(a);
+    }
+}
+
+template <int LOGN>
+int dot_all_run(const PcbKsArgs* ap, bool narrow, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbKsArgs& a = *ap;
+    if (a.K < 0 || a.R != 1 || a.ndig < 1 || a.ndig > 16 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
+        (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.kb || !a.ka || !a.autok || !a.rows ||
+        !a.digit_of || !a.pr)
+        return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
+    if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
+    if (a.K == 0 || a.nrows == 0) return 0;
+    const dim3 g((1 << LOGN) / BX, a.nrows);
+    if (narrow) dot_dispatch<LOGN, true>(a, g, s);
+    else dot_dispatch<LOGN, false>(a, g, s);
+    return PCB_LAUNCH_RESULT();
+}
+
+template int dot_all_run<14>(const PcbKsArgs*, bool, cudaStream_t);
+template int dot_all_run<16>(const PcbKsArgs*, bool, cudaStream_t);
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
-template int bconv_run<14>(const PcbBconvArgs*, bool, cudaStream_t);
-template int bconv_run<16>(const PcbBconvArgs*, bool, cudaStream_t);
+template int bconv_run<14>(const PcbBconvArgs*, bool, int, cudaStream_t);
+template int bconv_run<16>(const PcbBconvArgs*, bool, int, cudaStream_t);
 template int ks_dot_launch<14>(const PcbKsArgs*, cudaStream_t);
 template int ks_dot_launch<16>(const PcbKsArgs*, cudaStream_t);
 template int ks_dot_run<14>(const PcbKsArgs*, bool, cudaStream_t);

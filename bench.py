@@ -262,6 +262,10 @@ def run_ours(a):
         traffic = json.load(open(os.path.join(ROOT, "profiles", "ntt_fwd_traffic.json")))["bytes_per_3072_row_pass"]
     except Exception:
         pass
+    h2d, d2h = host_in.numel() * 8, host_out.numel() * 8
+    del s, x, nbuf, dev_in, host_in, host_out, ct, res
+    torch.cuda.empty_cache()
+    attn = attention_decode(a, world, rank, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -272,14 +276,15 @@ def run_ours(a):
                        "N": n, "limbs": "24+8 x 50-bit", "dnum": 3, "batch_per_gpu": BATCH,
                        "parallelism": f"replicas x{world} (independent ciphertexts, no collective)",
                        "l2": "inputs larger than L2 (1.5 GiB of residues per batch)"},
-            "e2e": {"value": ks / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * 8,
-                    "d2h_bytes_per_step": host_out.numel() * 8},
+            "e2e": {"value": ks / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "roofline": {"kernel": "ntt fwd (fwd_cols + fwd_rows) over the batch's 3072 rows", "bound": "hbm",
                          "achieved": ntt_gbs, "peak": hbm, "unit": "GB/s", "frac": ntt_gbs / hbm,
                          "traffic": traffic, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                          "ms": ntt_ms, "algorithmic_bytes": ntt_bytes},
             "clocks": clk,
+            "attn_decode_ms_per_token": attn,
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
@@ -290,10 +295,56 @@ def run_ours(a):
                 line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": None, "kind": "port",
                                         "sample": f"failed: {e}"}
         print(json.dumps(line), flush=True)
-    del s
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def attention_decode(a, world, rank, barrier, dist):
+    """Encrypted attention decode ms/token (the step with the KV cache resident in HBM, CUDA events, max over ranks):
+    config 1 (one head, N = 2^14, 32 tokens) on rank 0's GPU, and config 3's attention core (12 heads x 64, 128
+    tokens, N = 2^16 with the 24-limb chain), heads sharded over the ranks (ceil(12 / ranks) heads each, no
+    communication: the per-head outputs stay on their GPU)."""
+    import numpy as np
+    import torch
+
+    from perseus_b200 import attention as A
+    from perseus_b200 import fhe
+
+    rng = np.random.default_rng(100 + rank)
+    out = {}
+    for name, ch, tokens, heads in (("config1_1head_N2^14_32tok", fhe.config1_chain(), 32, 1),
+                                    ("config3_12heads_N2^16_128tok", fhe.config2_chain(), 128, 12)):
+        mine = heads if heads == 1 else -(-heads // world)
+        lay = A.Layout(64, tokens, ch.n // 2)
+        s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=mine, seed=0)
+        top = len(ch.q) - 1
+        caches, qs = [], []
+        for _ in range(mine):
+            c = A.KVCache(s, lay, top)
+            c.load(rng.normal(0, 1, (tokens, 64)) / 8, rng.normal(0, 1, (tokens, 64)) / 8)
+            caches.append(c)
+            qs.append(A.encrypt_query(s, rng.normal(0, 1, 64) / 8, lay, top, ch.q[top]))
+        cache = caches[0] if mine == 1 else A.HeadBatch(s, caches)
+        q = qs[0] if mine == 1 else s.stack(qs)
+        coeffs = A.softmax_poly(tokens)
+        for _ in range(max(a.warmup, 3)):
+            A.attend(s, q, cache, coeffs, ch.q)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            A.attend(s, q, cache, coeffs, ch.q)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / a.steps], dtype=torch.float64, device="cuda")
+        if dist and heads > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = t.item()
+        del s, caches, qs, cache, q
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():

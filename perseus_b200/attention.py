@@ -1,0 +1,176 @@
+"""Encrypted attention decode over the evaluator: the encrypted KV cache and one decode step (Q K^T, polynomial
+softmax, P V), the role of the reference's attention driver (python/perseus/impl/attention.py:491-551 KVCache,
+:698-800 complex_qkt, :897-962 complex_softmax_v, :1394 attend) re-laid-out for one head per ciphertext (the reference
+interleaves heads in one ciphertext; here heads are separate ciphertexts so a batch of heads runs as one K-batched
+launch set and heads shard across GPUs without communication).
+
+Layout (d = head_dim, T = token capacity, both powers of two, d T <= slots):
+- K cache: slot t d + j = K[t][j]; V cache: slot t d + j = V[t][j] (tokens pushed by adding an encryption of the
+  token's row at its offset, the reference's cache_k_push / cache_v_push).
+- query: slot t d + j = Q[j] / sqrt(d) for every t (the client folds the 1/sqrt(d) in and replicates).
+
+Step (all rotations left; rotate_and_sum(x, s, e) = x + rot(x, s) + ... ladder, python/perseus/impl/poly.py:24-39):
+1. prod = Q * K, rescale; scores = rotate_and_sum(prod, 1, d): slot t d holds s_t = <Q, K_t> / sqrt(d);
+2. P = mask * p(scores), p the degree-7 polynomial standing in for softmax, mask = 1 on slots t d of live tokens:
+   baby-step giant-step p = (c0 + c1 x + c2 x^2 + c3 x^3) + x^4 (c4 + c5 x + c6 x^2 + c7 x^3), the coefficients as
+   masked plaintexts (the mask costs no level), each term's plaintext scale chosen so all terms meet at one scale;
+3. replicate: R = rotate_and_sum(P, -1, d) puts P_t on slots t d .. t d + d - 1;
+4. out = rotate_and_sum(rescale(R * V), d, d T): slot j holds sum_t P_t V[t][j].
+Depth 6: from top L the output lands at top L - 6 (config 1: 8 limbs, decrypted at top 1).
+
+Scales are tracked exactly (doubles). The inputs K, V are encrypted at 2^40 (BASELINE); the query is encoded at
+q_top 2^10 so the score lands near 2^50, the size of the primes, which keeps every power of the polynomial near 2^50
+after each rescale. The same function runs on the CUDA session and, in the tests, on an oracle-backed adapter.
+"""
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+INPUT_SCALE = 2.0**40
+
+
+def softmax_poly(n_tokens, lo=-1.0, hi=1.0, degree=7):
+    """Power-basis coefficients c_0..c_7 of the degree-7 Chebyshev interpolant of exp(x) / n_tokens on [lo, hi]:
+    the polynomial that replaces softmax (weights ~ exp(s_t) / sum_u exp(s_u) for scores near 0)."""
+    k = np.arange(degree + 1)
+    xs = np.cos((2 * k + 1) * np.pi / (2 * (degree + 1)))  # Chebyshev nodes on [-1, 1]
+    xt = 0.5 * (hi - lo) * xs + 0.5 * (hi + lo)
+    coef = np.polynomial.polynomial.polyfit(xt, np.exp(xt) / n_tokens, degree)
+    return [float(c) for c in coef]
+
+
+def poly_eval(coeffs, x):
+    return sum(c * x**i for i, c in enumerate(coeffs))
+
+
+def plain_attention(q, k, v, coeffs):
+    """fp64 reference of the decode step with the same polynomial softmax."""
+    d = q.shape[-1]
+    s = k @ q / math.sqrt(d)
+    w = poly_eval(coeffs, s)
+    return w @ v
+
+
+@dataclass
+class Layout:
+    head_dim: int
+    tokens: int
+    slots: int
+
+    def rot_steps(self):
+        d, t = self.head_dim, self.tokens
+        up = [1 << i for i in range(int(math.log2(d)))]
+        return up + [-s for s in up] + [d << i for i in range(int(math.log2(t)))]
+
+
+class KVCache:
+    """One head's encrypted K and V caches (one ciphertext each), tokens appended in place."""
+
+    def __init__(self, ops, layout, top):
+        self.ops, self.lay, self.top = ops, layout, top
+        self.k = None
+        self.v = None
+        self.count = 0
+
+    def _row_ct(self, row, t):
+        vec = np.zeros(self.lay.slots)
+        vec[t * self.lay.head_dim:(t + 1) * self.lay.head_dim] = row
+        return self.ops.encrypt(vec, top=self.top, scale=INPUT_SCALE, slots=self.lay.slots)
+
+    def push(self, k_row, v_row):
+        """cache_k_push / cache_v_push: the token's rows encrypted at its offset and added into the caches."""
+        t = self.count
+        if t >= self.lay.tokens:
+            raise ValueError(f"KV cache full ({self.lay.tokens} tokens)")
+        kc, vc = self._row_ct(k_row, t), self._row_ct(v_row, t)
+        self.k = kc if self.k is None else self.ops.add(self.k, kc)
+        self.v = vc if self.v is None else self.ops.add(self.v, vc)
+        self.count += 1
+
+    def load(self, K, V):
+        """The whole cache at once (T x d each): one encryption per cache."""
+        n = K.shape[0]
+        d = self.lay.head_dim
+        kv, vv = np.zeros(self.lay.slots), np.zeros(self.lay.slots)
+        kv[: n * d] = K.ravel()
+        vv[: n * d] = V.ravel()
+        self.k = self.ops.encrypt(kv, top=self.top, scale=INPUT_SCALE, slots=self.lay.slots)
+        self.v = self.ops.encrypt(vv, top=self.top, scale=INPUT_SCALE, slots=self.lay.slots)
+        self.count = n
+
+
+class HeadBatch:
+    """Several heads' caches as one K-batched cache (the session's ops run every head in the same launches)."""
+
+    def __init__(self, ops, caches):
+        self.lay = caches[0].lay
+        self.count = caches[0].count
+        if any(c.count != self.count for c in caches):
+            raise ValueError("heads of one batch hold the same number of tokens")
+        self.k = ops.stack([c.k for c in caches])
+        self.v = ops.stack([c.v for c in caches])
+
+
+def encrypt_query(ops, q, layout, top, q_top_prime):
+    """The client's query ciphertext: Q / sqrt(d) replicated per token block, at scale q_top 2^10 (see above)."""
+    d, t = layout.head_dim, layout.tokens
+    vec = np.zeros(layout.slots)
+    vec[: d * t] = np.tile(q / math.sqrt(d), t)
+    return ops.encrypt(vec, top=top, scale=q_top_prime * 2.0**10, slots=layout.slots)
+
+
+def _mask(layout, n_live):
+    m = np.zeros(layout.slots)
+    m[0 : n_live * layout.head_dim : layout.head_dim] = 1.0
+    return m
+
+
+def attend(ops, q_ct, cache, coeffs, primes):
+    """One decode step for one head: the encrypted attention output (slots 0..d-1). `primes` = the chain's Q primes
+    (bottom first); `ops` provides mult, rescale_one, rotate_and_sum, drop_to, add, pt, mult_pt, add_pt."""
+    lay = cache.lay
+    d, T = lay.head_dim, lay.tokens
+    top = q_ct.top
+    # 1. scores
+    k_ct = ops.drop_to(cache.k, top)
+    prod = ops.rescale_one(ops.mult(q_ct, k_ct))
+    x = ops.rotate_and_sum(prod, 1, d)  # top L-1
+    L1 = x.top
+    # 2. masked polynomial (baby steps x, x^2, x^3; giant step x^4)
+    x2 = ops.rescale_one(ops.mult(x, x))  # L-2
+    x3 = ops.rescale_one(ops.mult(x2, ops.drop_to(x, L1 - 1)))  # L-3
+    x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
+    lvl = L1 - 2  # the level of x^3 / x^4
+    mask = _mask(lay, cache.count)
+
+    def term(pw, c, target_scale):
+        # c * mask * x^pw, landing at level lvl - 1 with scale target_scale (the plaintext scale solves for it)
+        src = ops.drop_to(pw, lvl)
+        pscale = target_scale * primes[lvl] / src.scale
+        pt = ops.pt(mask * c, lvl, pscale, lay.slots)
+        return ops.rescale_one(ops.mult_pt(src, pt, pscale))
+
+    def inner(cs, target_scale):
+        acc = None
+        for i, (pw, c) in enumerate(zip((x, x2, x3), cs[1:])):
+            t_ = term(pw, c, target_scale)
+            acc = t_ if acc is None else ops.add(acc, t_)
+        pt0 = ops.pt(mask * cs[0], acc.top, acc.scale, lay.slots)
+        return ops.add_pt(acc, pt0)
+
+    # p = A + x^4 B: A at level lvl - 2 with scale S; B at lvl - 1 with scale S q_{lvl-1} / scale(x^4)
+    S = primes[lvl - 1]  # A's scale (~2^50)
+    x4d = ops.drop_to(x4, lvl - 1)
+    B = inner(coeffs[4:8] if len(coeffs) > 4 else [0.0], S * primes[lvl - 1] / x4d.scale)
+    xb = ops.rescale_one(ops.mult(x4d, B))  # lvl - 2, scale ~ S
+    A = inner(coeffs[:4], xb.scale)  # lvl - 1, the same scale as x^4 B ...
+    A = ops.drop_to(A, xb.top)  # ... at the same level
+    A.scale = xb.scale
+    P = ops.add(A, xb)
+    # 3. replicate each weight over its block
+    R = ops.rotate_and_sum(P, -1, d)
+    # 4. weighted values, summed over tokens
+    v_ct = ops.drop_to(cache.v, R.top)
+    y = ops.rescale_one(ops.mult(R, v_ct))
+    return ops.rotate_and_sum(y, d, d * T)

@@ -169,6 +169,13 @@ class Session:
     def top(self):
         return self.nq - 1
 
+    def stack(self, cts):
+        """One K-batched ciphertext from single ones at the same level (heads, independent ciphertexts)."""
+        c0 = cts[0]
+        if any(c.top != c0.top for c in cts):
+            raise ValueError("stack: ciphertexts at different tops")
+        return Ct(torch.cat([c.data for c in cts]), c0.top, c0.scale, c0.slots)
+
     def key(self, idx):
         b, a, g = C.c_void_p(), C.c_void_p(), C.c_uint64()
         L.check(L.lib().pcb_key_ptrs(self.ctx, idx, C.byref(b), C.byref(a), C.byref(g)), "pcb_key_ptrs")

@@ -1,0 +1,53 @@
+"""Test infrastructure: the session op signatures over the oracle context, so the attention driver can run the same
+op sequence on the CPU restatement as on the CUDA path."""
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class OCt:
+    data: np.ndarray  # [2][rows][N] uint64
+    top: int
+    scale: float
+    slots: int
+
+
+class OracleOps:
+    def __init__(self, ctx):
+        self.c = ctx
+
+    def encrypt(self, values, top, scale, slots):
+        return OCt(self.c.encrypt(values, slots, scale, top), top, scale, slots)
+
+    def add(self, a, b):
+        assert a.top == b.top
+        return OCt(self.c.add(a.data, b.data, a.top), a.top, a.scale, a.slots)
+
+    def mult(self, a, b):
+        assert a.top == b.top
+        return OCt(self.c.mult(a.data, b.data, a.top), a.top, a.scale * b.scale, a.slots)
+
+    def rescale_one(self, a):
+        a.data = self.c.rescale(a.data, a.top)
+        a.scale /= self.c.q[a.top]
+        a.top -= 1
+        return a
+
+    def rotate_and_sum(self, a, start, stop):
+        return OCt(self.c.rotate_and_sum(a.data, start, stop, a.top), a.top, a.scale, a.slots)
+
+    def drop_to(self, a, top):
+        return OCt(a.data, top, a.scale, a.slots)
+
+    def pt(self, values, top, scale, slots):
+        return self.c.encode(values, slots, scale, top)
+
+    def mult_pt(self, a, pt, pt_scale):
+        return OCt(self.c.mult_pt(a.data, pt, a.top), a.top, a.scale * pt_scale, a.slots)
+
+    def add_pt(self, a, pt):
+        return OCt(self.c.add_pt(a.data, pt, a.top), a.top, a.scale, a.slots)
+
+    def decrypt_slots(self, a):
+        return self.c.decrypt(a.data, a.top, a.slots, a.scale)

@@ -382,6 +382,11 @@ int pcb_rescale_static(PcbCtx* ctx, uint64_t* ct, int32_t top, cudaStream_t stre
 /* out = rot(x, step), left by step slots (crates/pc-gpu/src/rotate.rs:147-204); out must not alias x */
 int pcb_rotate(PcbCtx* ctx, const uint64_t* x, int64_t step, uint64_t* out, int32_t top, int32_t K,
                cudaStream_t stream);
+/* outs[i] = rot(x, steps[i]) for nsteps steps sharing one ModUp of x (crates/pc-gpu/src/rotate.rs:456,
+ * crates/pc-py/src/fhe.rs:1156 rotate_hoisted): word for word the plain rotations. outs: host array of device
+ * pointers, none aliasing x. */
+int pcb_rotate_hoisted(PcbCtx* ctx, const uint64_t* x, const int64_t* steps, int32_t nsteps, uint64_t* const* outs,
+                       int32_t top, int32_t K, cudaStream_t stream);
 /* out = x + rot(x, g) ladder over gaps start, 2 start, .. < stop (crates/pc-gpu/src/rotate.rs:924-992) */
 int pcb_rotate_and_sum(PcbCtx* ctx, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int32_t top,
                        int32_t K, cudaStream_t stream);

@@ -191,6 +191,7 @@ def lib():
         "pcb_rescale_static": (C.c_int, [vp, vp, i32, vp]),
         "pcb_rotate": (C.c_int, [vp, vp, i64, vp, i32, i32, vp]),
         "pcb_rotate_and_sum": (C.c_int, [vp, vp, i64, i64, vp, i32, i32, vp]),
+        "pcb_rotate_hoisted": (C.c_int, [vp, vp, C.POINTER(i64), i32, C.POINTER(vp), i32, i32, vp]),
         "pcb_mult_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_add_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),

@@ -1086,6 +1086,50 @@ int pcb_rotate(PcbCtx* c, const uint64_t* x, int64_t step, uint64_t* out, int32_
     return moddown(*c, out, false, top, K, s);
 }
 
+// Hoisted rotations (crates/pc-gpu/src/rotate.rs:456): the ModUp of x's c1 is shared by every step, each step then
+// runs its own inner product (output scattered by g^-1) and ModDown, so outs[i] is word for word pcb_rotate(x, steps[i]).
+int pcb_rotate_hoisted(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32_t nsteps, uint64_t* const* outs,
+                       int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !x || (nsteps > 0 && (!steps || !outs))) return fail(PCB_BAD_ARGS, "null argument");
+    if (nsteps < 0) return fail(PCB_BAD_ARGS, "%d steps", nsteps);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    std::vector<const KeySlot*> keys(nsteps, nullptr);
+    bool any = false;
+    for (int i = 0; i < nsteps; ++i) {
+        if (!outs[i] || outs[i] == x) return fail(PCB_BAD_ARGS, "output %d is null or aliases the input", i);
+        const uint64_t g = rot_galois(*c, steps[i]);
+        if (g == 1) continue;
+        keys[i] = key_of(*c, g);
+        if (!keys[i])
+            return fail(-3, "no rotation key for step %lld (galois %llu)", (long long)steps[i], (unsigned long long)g);
+        any = true;
+    }
+    const uint64_t* c1 = x + (size_t)c->rows * c->n;
+    if (any) {
+        rc = modup(*c, c1, top, K, s);
+        if (rc) return rc;
+    }
+    for (int i = 0; i < nsteps; ++i) {
+        if (!keys[i]) {
+            PcbEwArgs e;
+            memset(&e, 0, sizeof e);
+            e.out = ct_ref(*c, outs[i]);
+            e.a = ct_ref(*c, x);
+            e.rs.nq = top + 1;
+            e.K = K;
+            e.nparts = 2;
+            CK(c->tab->ew_copy(&e, s));
+            continue;
+        }
+        rc = dot(*c, *keys[i], c1, x, 1, top, K, s);
+        if (rc) return rc;
+        rc = moddown(*c, outs[i], false, top, K, s);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 int pcb_rotate_and_sum(PcbCtx* c, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int32_t top, int32_t K,
                        cudaStream_t s) {
     if (!c || !x || !out) return fail(PCB_BAD_ARGS, "null argument");

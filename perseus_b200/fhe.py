@@ -287,6 +287,15 @@ class Session:
         L.check(L.lib().pcb_rotate(self.ctx, a.ptr(), int(step), out.ptr(), a.top, a.k, self._stream()), "pcb_rotate")
         return out
 
+    def rotate_hoisted(self, a, steps):
+        """[rot(a, s) for s in steps] sharing one ModUp (the reference's Fhe.rotate_hoisted)."""
+        outs = [self.ct_like(a) for _ in steps]
+        st = (C.c_int64 * len(steps))(*[int(x) for x in steps])
+        ptrs = (C.c_void_p * len(steps))(*[o.data.data_ptr() for o in outs])
+        L.check(L.lib().pcb_rotate_hoisted(self.ctx, a.ptr(), st, len(steps), ptrs, a.top, a.k, self._stream()),
+                "pcb_rotate_hoisted")
+        return outs
+
     def rotate_and_sum(self, a, start, stop):
         out = self.ct_like(a)
         L.check(L.lib().pcb_rotate_and_sum(self.ctx, a.ptr(), int(start), int(stop), out.ptr(), a.top, a.k,

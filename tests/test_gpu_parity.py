@@ -281,3 +281,17 @@ def test_batched_ops_equal_single(s1):
     for i, c in enumerate(cts):
         r = s.rotate(c, 2)
         assert torch.equal(rb.data[i, :, : top + 1], r.data[0, :, : top + 1])
+
+
+@pytest.mark.parametrize("which", ["s1", "s2"])
+def test_hoisted_rotations_equal_plain(which, request):
+    # one shared ModUp (crates/pc-gpu/src/rotate.rs:456): every output word for word the plain rotation's
+    s, o = request.getfixturevalue(which)
+    steps = [1, 4, 0, -1] if which == "s1" else [5, 1, 1 << 15]
+    rng = np.random.default_rng(8)
+    top = s.top() - 1
+    a = s.encrypt(rng.normal(0, 1, 256) / 8, top=top)
+    outs = s.rotate_hoisted(a, steps)
+    for st, h in zip(steps, outs):
+        p = s.rotate(a, st) if st % (s.n // 2) else a
+        assert torch.equal(h.data[:, :, : top + 1], p.data[:, :, : top + 1]), st

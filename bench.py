@@ -41,6 +41,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
+    ap.add_argument("--profile", action="store_true",
+                    help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
     return ap.parse_args()
 
 
@@ -176,6 +179,7 @@ def run_ours(a):
         if dist:
             dist.barrier()
 
+    BATCH = a.batch
     ch = fhe.config2_chain()
     s = fhe.Session(ch, rot_steps=ROT_STEPS, k_max=BATCH, seed=0)
     n, nq, rows = ch.n, len(ch.q), ch.rows
@@ -228,6 +232,11 @@ def run_ours(a):
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / a.steps
     ntt_ms = sum(b.elapsed_time(e) for b, e in ntt_ev) / a.steps
+    if a.profile:
+        if rank == 0:
+            print(json.dumps({"profile": True, "batch": BATCH, "ms_per_step": ms, "ntt_fwd_ms": ntt_ms,
+                              "gpu_launches": int(launches)}), flush=True)
+        return
     # e2e through the public API: pinned host inputs in, the summed result out, every step
     host_in = torch.empty((BATCH, 2, nq, n), dtype=torch.int64, pin_memory=True)
     host_in.copy_(x[:, :, :nq])

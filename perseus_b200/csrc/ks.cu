@@ -24,11 +24,17 @@ constexpr uint64_t LO26 = (1ull << 26) - 1;
 struct Acc3 {
     uint64_t h, m, l;
 };
+// 32 x 32 -> 64 multiply with a 64-bit addend in one instruction (mad.wide.u32)
+__device__ __forceinline__ uint64_t madw(uint32_t x, uint32_t y, uint64_t acc) {
+    uint64_t r;
+    asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(r) : "r"(x), "r"(y), "l"(acc));
+    return r;
+}
 __device__ __forceinline__ void mac3(Acc3& a, uint32_t x1, uint32_t x0, uint32_t y1, uint32_t y0) {
-    a.h += (uint64_t)x1 * y1;
-    a.m += (uint64_t)x1 * y0;
-    a.m += (uint64_t)x0 * y1;
-    a.l += (uint64_t)x0 * y0;
+    a.h = madw(x1, y1, a.h);
+    a.m = madw(x1, y0, a.m);
+    a.m = madw(x0, y1, a.m);
+    a.l = madw(x0, y0, a.l);
 }
 __device__ __forceinline__ Acc to_acc(const Acc3& a) {
     const uint64_t t = a.m << 26;

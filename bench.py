@@ -324,19 +324,20 @@ def run_ours(a):
 def attention_decode(a, world, rank, barrier, dist):
     """Encrypted attention decode ms/token (the step with the KV cache resident in HBM, CUDA events, max over ranks):
     config 1 (one head, N = 2^14, 32 tokens) on rank 0's GPU, and config 3's attention core (12 heads x 64, 128
-    tokens, N = 2^16 with the 24-limb chain), heads sharded over the ranks (ceil(12 / ranks) heads each, no
+    tokens, N = 2^16 with the 24-limb chain), heads sharded over the ranks (perseus_b200.shard.head_range, no
     communication: the per-head outputs stay on their GPU)."""
     import numpy as np
     import torch
 
     from perseus_b200 import attention as A
-    from perseus_b200 import fhe
+    from perseus_b200 import fhe, shard
 
     rng = np.random.default_rng(100 + rank)
     out = {}
     for name, ch, tokens, heads in (("config1_1head_N2^14_32tok", fhe.config1_chain(), 32, 1),
                                     ("config3_12heads_N2^16_128tok", fhe.config2_chain(), 128, 12)):
-        mine = heads if heads == 1 else -(-heads // world)
+        # config 1 runs on every rank (rank 0 reports it); config 3's heads are split, at most one apart
+        mine = heads if heads == 1 else len(shard.head_range(heads, world, rank))
         lay = A.Layout(64, tokens, ch.n // 2)
         s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=mine, seed=0)
         top = len(ch.q) - 1

@@ -104,10 +104,12 @@ struct PcbCtx {
     std::vector<uint64_t> primes;
     const PcbKernelTable* tab = nullptr;
     bool narrow = false;  // every prime below 2^52: the 26-bit-split conversion and inner-product kernels
+    bool f64 = false;     // every prime below 2^50: FP64 NTT butterflies
     Arena arena;
     // device tables
     PcbPrimeConst* pr = nullptr;
     uint64_t *fw = nullptr, *fws = nullptr, *iw = nullptr, *iws = nullptr, *ninv = nullptr, *ninvs = nullptr;
+    double *fwf = nullptr, *fwp = nullptr, *iwf = nullptr, *iwp = nullptr;  // centred twiddles w, fl(w / p) (f64)
     int32_t* digit_of = nullptr;
     uint64_t *pmod = nullptr, *pmods = nullptr, *pinv = nullptr, *pinvs = nullptr;
     uint32_t* id_roff = nullptr;   // i
@@ -187,6 +189,12 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
     c.iws = A.take<uint64_t>((size_t)rows * n);
     c.ninv = A.take<uint64_t>(rows);
     c.ninvs = A.take<uint64_t>(rows);
+    if (c.f64) {
+        c.fwf = A.take<double>((size_t)rows * n);
+        c.fwp = A.take<double>((size_t)rows * n);
+        c.iwf = A.take<double>((size_t)rows * n);
+        c.iwp = A.take<double>((size_t)rows * n);
+    }
     if (fill) {
         std::vector<PcbPrimeConst> pr(rows);
         std::vector<uint64_t> ni(rows), nis(rows);
@@ -199,6 +207,13 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
         CK(upload(c.ninv, ni, s));
         CK(upload(c.ninvs, nis, s));
         std::vector<uint64_t> w(n), ws(n), iw(n), iws(n), pw(n), ipw(n);
+        std::vector<double> wf(n), wp(n), iwf(n), iwp(n);
+        // centred twiddle and its quotient by p, both exact or correctly rounded (|w| < 2^49)
+        auto centred = [](uint64_t v, uint64_t p, double& f, double& q) {
+            const int64_t cv = v > p / 2 ? -(int64_t)(p - v) : (int64_t)v;
+            f = (double)cv;
+            q = f / (double)p;
+        };
         for (int r = 0; r < rows; ++r) {
             const uint64_t p = c.primes[r], psi = hm::min_root(m, p), ipsi = hm::invmod(psi, p);
             if (!psi) return fail(PCB_BAD_ARGS, "prime %llu has no primitive %u-th root of unity", (unsigned long long)p, m);
@@ -218,6 +233,16 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             CK(cudaMemcpyAsync(c.fws + (size_t)r * n, ws.data(), n * 8, cudaMemcpyHostToDevice, s));
             CK(cudaMemcpyAsync(c.iw + (size_t)r * n, iw.data(), n * 8, cudaMemcpyHostToDevice, s));
             CK(cudaMemcpyAsync(c.iws + (size_t)r * n, iws.data(), n * 8, cudaMemcpyHostToDevice, s));
+            if (c.f64) {
+                for (size_t i = 0; i < n; ++i) {
+                    centred(w[i], p, wf[i], wp[i]);
+                    centred(iw[i], p, iwf[i], iwp[i]);
+                }
+                CK(cudaMemcpyAsync(c.fwf + (size_t)r * n, wf.data(), n * 8, cudaMemcpyHostToDevice, s));
+                CK(cudaMemcpyAsync(c.fwp + (size_t)r * n, wp.data(), n * 8, cudaMemcpyHostToDevice, s));
+                CK(cudaMemcpyAsync(c.iwf + (size_t)r * n, iwf.data(), n * 8, cudaMemcpyHostToDevice, s));
+                CK(cudaMemcpyAsync(c.iwp + (size_t)r * n, iwp.data(), n * 8, cudaMemcpyHostToDevice, s));
+            }
             CK(cudaStreamSynchronize(s));  // the host staging vectors are reused per prime
         }
     }
@@ -506,10 +531,17 @@ PcbNttArgs ntt_args(const PcbCtx& c, void* base, const uint32_t* roff, const int
     a.base = base;
     a.roff = roff;
     a.rprime = rprime;
-    a.fw = c.fw;
-    a.fws = c.fws;
-    a.iw = c.iw;
-    a.iws = c.iws;
+    if (c.f64) {
+        a.fw = c.fwf;
+        a.fws = c.fwp;
+        a.iw = c.iwf;
+        a.iws = c.iwp;
+    } else {
+        a.fw = c.fw;
+        a.fws = c.fws;
+        a.iw = c.iw;
+        a.iws = c.iws;
+    }
     a.ninv = c.ninv;
     a.ninvs = c.ninvs;
     a.pr = c.pr;
@@ -517,6 +549,14 @@ PcbNttArgs ntt_args(const PcbCtx& c, void* base, const uint32_t* roff, const int
     a.snum = 1;
     a.xnum = 1;
     return a;
+}
+
+// NTT launches of the context (the tables of ntt_args: FP64 ones when every prime is below 2^50)
+int ntt_fwd(const PcbCtx& c, const PcbNttArgs* a, cudaStream_t s) {
+    return c.logn == 14 ? ntt::fwd_run<14>(a, c.f64, s) : ntt::fwd_run<16>(a, c.f64, s);
+}
+int ntt_inv(const PcbCtx& c, const PcbNttArgs* a, cudaStream_t s) {
+    return c.logn == 14 ? ntt::inv_run<14>(a, c.f64, s) : ntt::inv_run<16>(a, c.f64, s);
 }
 
 PcbPolyRef ct_ref(const PcbCtx& c, const void* base) {
@@ -542,7 +582,7 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     a.soff = l.mu_intt_soff;
     a.es = l.mu_intt_es;
     a.ess = l.mu_intt_ess;
-    CK(c.tab->ntt_inv(&a, s));
+    CK(ntt_inv(c, &a, s));
     PcbBconvArgs b;
     memset(&b, 0, sizeof b);
     b.src = c.coef;
@@ -554,7 +594,7 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     b.max_tgt = l.mu_max_tgt;
     CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, l.mu_ns, s));
     PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
-    CK(c.tab->ntt_fwd(&f, s));
+    CK(ntt_fwd(c, &f, s));
     return 0;
 }
 
@@ -604,7 +644,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     PcbNttArgs a = ntt_args(c, c.ext, l.md_intt_roff, l.md_intt_rprime, K * 2 * c.kp);
     a.es = l.md_es;
     a.ess = l.md_ess;
-    CK(c.tab->ntt_inv(&a, s));
+    CK(ntt_inv(c, &a, s));
     PcbBconvArgs b;
     memset(&b, 0, sizeof b);
     b.src = c.ext;
@@ -621,7 +661,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     f.ex = c.ext;
     f.es = c.pinv;
     f.ess = c.pinvs;
-    CK(c.tab->ntt_fwd(&f, s));
+    CK(ntt_fwd(c, &f, s));
     return 0;
 }
 
@@ -692,8 +732,11 @@ static int init_ctx(PcbCtx& c, const PcbParams* prm, int nkeys) {
         if (p < 3 || !(p & 1) || p >= (1ull << 61) || (p - 1) % (2 * c.n))
             return fail(PCB_BAD_ARGS, "prime %llu is not an odd NTT prime below 2^61 (p = 1 mod 2N)", (unsigned long long)p);
     c.tab = table_for(c.logn);
-    c.narrow = true;
-    for (uint64_t p : c.primes) c.narrow = c.narrow && p < (1ull << 52);
+    c.narrow = c.f64 = true;
+    for (uint64_t p : c.primes) {
+        c.narrow = c.narrow && p < (1ull << 52);
+        c.f64 = c.f64 && p < (1ull << 50);
+    }
     return 0;
 }
 
@@ -775,7 +818,7 @@ int pcb_keygen(PcbCtx* c, uint64_t seed, uint32_t h, double sigma, int32_t ngal,
             host[(size_t)r * n + i] = c->secret[i] < 0 ? c->primes[r] - 1 : (uint64_t)c->secret[i];
     CK(cudaMemcpyAsync(c->s_eval, host.data(), host.size() * 8, cudaMemcpyHostToDevice, s));
     PcbNttArgs a = ntt_args(*c, c->s_eval, c->id_roff, c->id_rprime, rows);
-    CK(c->tab->ntt_fwd(&a, s));
+    CK(ntt_fwd(*c, &a, s));
     CK(cudaStreamSynchronize(s));
     c->nkeys_made = 0;
     std::vector<uint64_t> err((size_t)c->dnum * rows * n);
@@ -805,7 +848,7 @@ int pcb_keygen(PcbCtx* c, uint64_t seed, uint32_t h, double sigma, int32_t ngal,
         CK(upload(k.autok_dev, ak, s));
         CK(cudaMemcpyAsync(c->digits, err.data(), err.size() * 8, cudaMemcpyHostToDevice, s));
         PcbNttArgs e = ntt_args(*c, c->digits, c->key_roff, c->key_rprime, c->dnum * rows);
-        CK(c->tab->ntt_fwd(&e, s));
+        CK(ntt_fwd(*c, &e, s));
         const uint64_t* s_new = c->s_eval;
         if (k.galois != 1) {
             // sigma_{g^-1}(s): the rotation key switches s to it (crates/pc-gpu/src/keygen.rs:235-256)
@@ -903,7 +946,7 @@ int pcb_encrypt(PcbCtx* c, const double* vals, int32_t nvals, int32_t nslots, do
     }
     CK(cudaMemcpyAsync(ct, m.data(), m.size() * 8, cudaMemcpyHostToDevice, s));
     PcbNttArgs a = ntt_args(*c, ct, c->id_roff, c->id_rprime, top + 1);
-    CK(c->tab->ntt_fwd(&a, s));
+    CK(ntt_fwd(*c, &a, s));
     PcbEncryptArgs ea;
     memset(&ea, 0, sizeof ea);
     ea.c0 = ct;
@@ -931,7 +974,7 @@ int pcb_decrypt(PcbCtx* c, const uint64_t* ct, int32_t top, int32_t nslots, doub
     dec_row0<<<(unsigned)(n / 256), 256, 0, s>>>(ct, ct + (size_t)c->rows * n, c->s_eval, c->row, pc);
     CK(PCB_LAUNCH_RESULT());
     PcbNttArgs a = ntt_args(*c, c->row, c->id_roff, c->id_rprime, 1);
-    CK(c->tab->ntt_inv(&a, s));
+    CK(ntt_inv(*c, &a, s));
     std::vector<uint64_t> m(n);
     CK(cudaMemcpyAsync(m.data(), c->row, n * 8, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
@@ -948,7 +991,7 @@ int pcb_pt_load(PcbCtx* c, const uint64_t* rows_host, int32_t top, uint64_t* pt,
     if (rc) return rc;
     CK(cudaMemcpyAsync(pt, rows_host, (size_t)(top + 1) * c->n * 8, cudaMemcpyHostToDevice, s));
     PcbNttArgs a = ntt_args(*c, pt, c->id_roff, c->id_rprime, top + 1);
-    CK(c->tab->ntt_fwd(&a, s));
+    CK(ntt_fwd(*c, &a, s));
     CK(cudaStreamSynchronize(s));
     return 0;
 }
@@ -1014,7 +1057,7 @@ int pcb_rescale(PcbCtx* c, uint64_t* ct, int32_t top, int32_t K, cudaStream_t s)
     PcbNttArgs a = ntt_args(*c, c->conv, l.rs_intt_roff, l.rs_intt_rprime, 2 * K);
     a.src = ct;
     a.soff = l.rs_intt_roff;
-    CK(c->tab->ntt_inv(&a, s));
+    CK(ntt_inv(*c, &a, s));
     PcbRescaleArgs r;
     memset(&r, 0, sizeof r);
     r.x = ct_ref(*c, c->conv);
@@ -1036,7 +1079,7 @@ int pcb_rescale(PcbCtx* c, uint64_t* ct, int32_t top, int32_t K, cudaStream_t s)
     f.ex = ct;
     f.es = l.rs_alpha;
     f.ess = l.rs_alphas;
-    CK(c->tab->ntt_fwd(&f, s));
+    CK(ntt_fwd(*c, &f, s));
     return 0;
 }
 
@@ -1180,7 +1223,7 @@ int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaSt
     if (nrows < 0 || nrows > c->k_max * 2 * c->rows)
         return fail(PCB_BAD_ARGS, "%d rows (row tables hold %d)", nrows, c->k_max * 2 * c->rows);
     PcbNttArgs a = ntt_args(*c, x, c->id_roff, c->id_rprime_q, nrows);
-    CK(inverse ? c->tab->ntt_inv(&a, s) : c->tab->ntt_fwd(&a, s));
+    CK(inverse ? ntt_inv(*c, &a, s) : ntt_fwd(*c, &a, s));
     return 0;
 }
 
@@ -1247,7 +1290,7 @@ int pcb_rescale_static(PcbCtx* c, uint64_t* ct, int32_t top, cudaStream_t s) {
     PcbNttArgs a = ntt_args(*c, scratch, l.rs_intt_roff, l.rs_intt_rprime, 2);
     a.src = ct;
     a.soff = l.rs_intt_roff;
-    CK(c->tab->ntt_inv(&a, s));
+    CK(ntt_inv(*c, &a, s));
     PcbRescaleArgs r;
     memset(&r, 0, sizeof r);
     r.x = ct_ref(*c, scratch);
@@ -1268,7 +1311,7 @@ int pcb_rescale_static(PcbCtx* c, uint64_t* ct, int32_t top, cudaStream_t s) {
     f.ex = ct;
     f.es = l.rs_alpha;
     f.ess = l.rs_alphas;
-    CK(c->tab->ntt_fwd(&f, s));
+    CK(ntt_fwd(*c, &f, s));
     return 0;
 }
 

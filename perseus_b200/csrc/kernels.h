@@ -6,6 +6,9 @@ namespace pcb {
 namespace ntt {
 template <int LOGN> int fwd(const PcbNttArgs*, cudaStream_t);
 template <int LOGN> int inv(const PcbNttArgs*, cudaStream_t);
+// f64: every prime of the launch is below 2^50 and fw/fws (iw/iws) hold centred double twiddles w and fl(w / p)
+template <int LOGN> int fwd_run(const PcbNttArgs*, bool f64, cudaStream_t);
+template <int LOGN> int inv_run(const PcbNttArgs*, bool f64, cudaStream_t);
 }  // namespace ntt
 namespace elem {
 enum EwOpDecl { ADD = 0, SCALE = 1, SUB_MUL = 2, COPY = 3 };

@@ -7,9 +7,18 @@
 // B200 design. A row of N = 2^LOGN words is viewed as R = N / 256 "columns" x 256: stages 0 .. A-1 (A = LOGN - 8,
 // butterfly spans >= 256 words) run in the column pass, the last 8 stages (spans 128 .. 1) in the row pass over
 // 256-word blocks. Each pass keeps 16 (or 8) words per thread in registers and does two register rounds of 4 (or 3)
-// stages around one shared-memory exchange, so a pass reads and writes HBM once. Butterflies are Harvey-lazy (words
-// in [0, 4p) forward, [0, 2p) inverse) with Shoup twiddles, which needs p < 2^62. Launches go in chunks of rows,
+// stages around one shared-memory exchange, so a pass reads and writes HBM once. Launches go in chunks of rows,
 // both passes of a chunk back to back, so the intermediate state stays in the 126 MB L2.
+//
+// Two arithmetics, one kernel body (template flag F):
+//  - integer (any p < 2^62): Harvey-lazy butterflies (words in [0, 4p) forward, [0, 2p) inverse) with Shoup
+//    twiddles w' = floor(w 2^64 / p); 64-bit products are emulated on the 32-bit integer multiplier.
+//  - FP64 (every prime of the launch below 2^50): words are integer-valued doubles, signed and lazy (|x| < 4p), and
+//    a product y w mod p is six FP64 operations, exact (mul_f). The B200 retires 64 FP64 FMAs per clock per SM;
+//    this butterfly measured 2.4x the integer one. Twiddles come as centred doubles w (|w| <= p/2) with
+//    wp = fl(w / p); the intermediate between the passes is stored as raw doubles.
+#include <type_traits>
+
 #include "arith.cuh"
 
 namespace pcb {
@@ -20,7 +29,7 @@ constexpr int THREADS = 256;
 #define NTT_MIN_BLOCKS 3  // at most 80 registers per thread: 24 warps per SM (measured faster than 4 CTAs with spills)
 #endif
 
-// ------------------------------------------------------------------------------------------------ butterflies
+// ------------------------------------------------------------------------------------------------ integer butterflies
 __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, uint64_t p, uint64_t p2) {
     uint64_t u = x >= p2 ? x - p2 : x;
     const uint64_t v = shoup_lazy(y, w, ws, p);
@@ -38,6 +47,106 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t p) {
     x = x >= p2 ? x - p2 : x;
     return x >= p ? x - p : x;
 }
+
+// ------------------------------------------------------------------------------------------------ FP64 arithmetic
+constexpr double MAGIC = 6755399441055744.0;  // 1.5 * 2^52: fl(t + MAGIC) - MAGIC = rint(t) while |t| < 2^51
+constexpr double TWO52 = 4503599627370496.0;
+
+// y w mod p as an integer-valued double in [-0.75p, 0.75p], exact, for |y| < 2^52 and |w| <= p/2 (|y wp| < 2^51).
+// h + l = y w exactly (FMA error-free product); q = rint(y wp) is within 0.75 of y w / p (wp carries a relative
+// error of 2^-53), so h - q p is an integer below 2^53 and the FMA computes it exactly; |l| <= ulp(h) / 2 <= 2^47.
+__device__ __forceinline__ double mul_f(double y, double w, double wp, double p) {
+    const double h = __dmul_rn(y, w);
+    const double l = __fma_rn(y, w, -h);
+    const double q = __dsub_rn(__fma_rn(y, wp, MAGIC), MAGIC);
+    return __dadd_rn(__fma_rn(-q, p, h), l);
+}
+// x - rint(x / p) p, in [-p/2 - 1, p/2 + 1] for integer-valued |x| < 2^52
+__device__ __forceinline__ double red_f(double x, double p, double pinv) {
+    const double q = __dsub_rn(__fma_rn(x, pinv, MAGIC), MAGIC);
+    return __fma_rn(-q, p, x);
+}
+// the canonical word of an integer-valued |x| < 2^52: floor(x / p) is off by at most one, fixed by two selects; the
+// result r < 2^52 is the mantissa of r + 2^52
+__device__ __forceinline__ uint64_t canon_f(double x, double p, double pinv) {
+    const double q = __dsub_rn(__fma_rd(x, pinv, MAGIC), MAGIC);
+    double r = __fma_rn(-q, p, x);
+    r = r < 0.0 ? __dadd_rn(r, p) : r;
+    r = r >= p ? __dsub_rn(r, p) : r;
+    return (uint64_t)__double_as_longlong(__dadd_rn(r, TWO52)) & ((1ull << 52) - 1);
+}
+// a word below 2^52 as a double (exact)
+__device__ __forceinline__ double to_f(uint64_t x) {
+    return __dsub_rn(__longlong_as_double((long long)(x | 0x4330000000000000ull)), TWO52);
+}
+// a canonical word as a centred double and its quotient by p (per-row constants of the FP64 path)
+__device__ __forceinline__ void centred_f(uint64_t w, uint64_t p, double pf, double& wc, double& wp) {
+    wc = w > p / 2 ? -to_f(p - w) : to_f(w);
+    wp = wc / pf;
+}
+
+// ------------------------------------------------------------------------------------------------ arithmetic policy
+// Mod<F>: the per-row constants; Word<F>: the register word. Forward words grow by 0.75p per FP64 stage, so each
+// round of <= 4 stages starts reduced (|x| <= p); inverse sums double per stage, so even stages reduce them.
+struct IntMod {
+    uint64_t p, p2;
+};
+struct FpMod {
+    double p, pinv;
+};
+template <bool F> using Mod = std::conditional_t<F, FpMod, IntMod>;
+template <bool F> using Word = std::conditional_t<F, double, uint64_t>;
+
+template <bool F>
+__device__ __forceinline__ Mod<F> make_mod(uint64_t p) {
+    if constexpr (F) {
+        const double pf = to_f(p);
+        return FpMod{pf, 1.0 / pf};
+    } else {
+        return IntMod{p, 2 * p};
+    }
+}
+template <bool F>
+__device__ __forceinline__ Word<F> from_u64(uint64_t x) {
+    if constexpr (F) return to_f(x);
+    else return x;
+}
+// the intermediate between the passes, kept in the row's own words
+template <bool F>
+__device__ __forceinline__ Word<F> load_mid(const uint64_t* a) {
+    if constexpr (F) return __longlong_as_double((long long)*a);
+    else return *a;
+}
+template <bool F>
+__device__ __forceinline__ void store_mid(uint64_t* a, Word<F> x) {
+    if constexpr (F) *a = (uint64_t)__double_as_longlong(x);
+    else *a = x;
+}
+__device__ __forceinline__ void ct(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, const IntMod& m) {
+    ct_bfly(x, y, w, ws, m.p, m.p2);
+}
+__device__ __forceinline__ void ct(double& x, double& y, double w, double wp, const FpMod& m) {
+    const double v = mul_f(y, w, wp, m.p), u = x;
+    x = __dadd_rn(u, v);
+    y = __dsub_rn(u, v);
+}
+__device__ __forceinline__ void gs(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, const IntMod& m, bool) {
+    gs_bfly(x, y, w, ws, m.p, m.p2);
+}
+__device__ __forceinline__ void gs(double& x, double& y, double w, double wp, const FpMod& m, bool reduce) {
+    const double s = __dadd_rn(x, y), d = __dsub_rn(x, y);
+    x = reduce ? red_f(s, m.p, m.pinv) : s;
+    y = mul_f(d, w, wp, m.p);
+}
+__device__ __forceinline__ void round_end(uint64_t&, const IntMod&) {}
+__device__ __forceinline__ void round_end(double& x, const FpMod& m) { x = red_f(x, m.p, m.pinv); }
+// the canonical word, kept in the register word's bits (so the epilogue reuses the registers)
+__device__ __forceinline__ void canon(uint64_t& x, const IntMod& m) { x = canon4(x, m.p); }
+__device__ __forceinline__ void canon(double& x, const FpMod& m) {
+    x = __longlong_as_double((long long)canon_f(x, m.p, m.pinv));
+}
+__device__ __forceinline__ uint64_t bits(uint64_t x) { return x; }
+__device__ __forceinline__ uint64_t bits(double x) { return (uint64_t)__double_as_longlong(x); }
 
 // Shared-memory exchange of a 256-word block: one pad word after every 16, so both the strided (u + 16 k) and the
 // contiguous (16 u + k) views of a half-warp hit 16 distinct 8-byte bank pairs.
@@ -67,22 +176,23 @@ __device__ __forceinline__ uint64_t load_in(const PcbNttArgs& a, int i, const ui
 
 // ------------------------------------------------------------------------------------------------ forward
 // Column pass: stages 0 .. A-1 on COLS columns; thread (cc, g) holds rows g + E k (round 1), then E g + k (round 2)
-template <int LOGN>
+template <int LOGN, bool F>
 __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a, int row0) {
+    using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
-    __shared__ uint64_t sm[R * COLS];
-    __shared__ uint64_t stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
+    __shared__ T sm[R * COLS];
+    __shared__ T stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
-    const PcbPrimeConst& pc = a.pr[ri.pid];
-    const uint64_t p = pc.p, p2 = 2 * p;
-    const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
-    const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+    const uint64_t p = a.pr[ri.pid].p;
+    const Mod<F> md = make_mod<F>(p);
+    const T* fw = (const T*)a.fw + ((size_t)ri.pid << LOGN);
+    const T* fws = (const T*)a.fws + ((size_t)ri.pid << LOGN);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
-    uint64_t x[E];
+    T x[E];
 #pragma unroll
-    for (int k = 0; k < E; ++k) x[k] = load_in<LOGN>(a, i, ri.row, (size_t)(g + E * k) * 256 + col, p);
+    for (int k = 0; k < E; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)(g + E * k) * 256 + col, p));
     for (int t = threadIdx.x; t < R; t += THREADS) {
         stw[t] = fw[t];
         stws[t] = fws[t];
@@ -96,11 +206,14 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
             const int m = 1 << s, idx = m + (k >> (H - s));
-            ct_bfly(x[k], x[k + half], stw[idx], stws[idx], p, p2);
+            ct(x[k], x[k + half], stw[idx], stws[idx], md);
         }
     }
 #pragma unroll
-    for (int k = 0; k < E; ++k) sm[(g + E * k) * COLS + cc] = x[k];
+    for (int k = 0; k < E; ++k) {
+        round_end(x[k], md);
+        sm[(g + E * k) * COLS + cc] = x[k];
+    }
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < E; ++k) x[k] = sm[(E * g + k) * COLS + cc];
@@ -112,31 +225,35 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
             const int m = 1 << s, idx = m + (g << (s - H)) + (k >> (A - s));
-            ct_bfly(x[k], x[k + half], stw[idx], stws[idx], p, p2);
+            ct(x[k], x[k + half], stw[idx], stws[idx], md);
         }
     }
 #pragma unroll
-    for (int k = 0; k < E; ++k) ri.row[(size_t)(E * g + k) * 256 + col] = x[k];
+    for (int k = 0; k < E; ++k) {
+        round_end(x[k], md);
+        store_mid<F>(ri.row + (size_t)(E * g + k) * 256 + col, x[k]);
+    }
 }
 
 // Row pass: the last 8 stages over 256-word blocks, 16 blocks per CTA, 16 threads per block; thread u holds words
 // u + 16 k (round 1) then 16 u + k (round 2, 16 consecutive words: vector stores and the epilogue)
-template <int LOGN>
+template <int LOGN, bool F>
 __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a, int row0) {
+    using T = Word<F>;
     constexpr int A = LOGN - 8;
-    __shared__ uint64_t sm[16 * BLKPAD];
+    __shared__ T sm[16 * BLKPAD];
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
-    const PcbPrimeConst& pc = a.pr[ri.pid];
-    const uint64_t p = pc.p, p2 = 2 * p;
-    const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
-    const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+    const uint64_t p = a.pr[ri.pid].p;
+    const Mod<F> md = make_mod<F>(p);
+    const T* fw = (const T*)a.fw + ((size_t)ri.pid << LOGN);
+    const T* fws = (const T*)a.fws + ((size_t)ri.pid << LOGN);
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;  // 256-word block of the row
     uint64_t* blk = ri.row + (size_t)b * 256;
-    uint64_t x[16];
+    T x[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = blk[u + 16 * k];
+    for (int k = 0; k < 16; ++k) x[k] = load_mid<F>(blk + u + 16 * k);
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
         const int half = 16 >> (l + 1);
@@ -145,12 +262,15 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
         for (int k = 0; k < 16; ++k) {
             if (k & half) continue;
             const int idx = m + (b << l) + (k >> (4 - l));
-            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+            ct(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), md);
         }
     }
-    uint64_t* s = sm + lb * BLKPAD;
+    T* s = sm + lb * BLKPAD;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) s[pad(u + 16 * k)] = x[k];
+    for (int k = 0; k < 16; ++k) {
+        round_end(x[k], md);
+        s[pad(u + 16 * k)] = x[k];
+    }
     __syncwarp();
 #pragma unroll
     for (int k = 0; k < 16; ++k) x[k] = s[pad(16 * u + k)];
@@ -162,16 +282,16 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
         for (int k = 0; k < 16; ++k) {
             if (k & half) continue;
             const int idx = m + (b << l) + (u << (l - 4)) + (k >> (8 - l));
-            ct_bfly(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), p, p2);
+            ct(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), md);
         }
     }
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = canon4(x[k], p);
+    for (int k = 0; k < 16; ++k) canon(x[k], md);
     const size_t w0 = (size_t)b * 256 + 16 * u;  // word offset in the row
     if (a.epi == 0) {
-        ulonglong2* o = (ulonglong2*)(blk + 16 * u);
+        ulonglong2* op = (ulonglong2*)(blk + 16 * u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = make_ulonglong2(x[2 * k], x[2 * k + 1]);
+        for (int k = 0; k < 8; ++k) op[k] = make_ulonglong2(bits(x[2 * k]), bits(x[2 * k + 1]));
         return;
     }
     // forward epilogues (args.cuh:82-87): x = sum of xnum rows of ex, s = es[prime id]
@@ -184,33 +304,34 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
     for (int k = 0; k < 16; ++k) {
         uint64_t xs = ex[k];
         for (int j = 1; j < a.xnum; ++j) xs = add_mod(xs, ex[k + (size_t)j * a.xstride], p);
+        const uint64_t o = bits(x[k]);
         uint64_t y;
-        if (a.epi == 1) y = shoup(sub_mod(xs, x[k], p), sc, scs, p);
-        else if (a.epi == 2) y = add_mod(ed[k], shoup(sub_mod(xs, x[k], p), sc, scs, p), p);
-        else y = add_mod(shoup(xs, sc, scs, p), x[k], p);
+        if (a.epi == 1) y = shoup(sub_mod(xs, o, p), sc, scs, p);
+        else if (a.epi == 2) y = add_mod(ed[k], shoup(sub_mod(xs, o, p), sc, scs, p), p);
+        else y = add_mod(shoup(xs, sc, scs, p), o, p);
         eo[k] = y;
     }
 }
 
 // ------------------------------------------------------------------------------------------------ inverse
 // Row pass first (GS spans 1 .. 128 inside 256-word blocks); thread u holds 16 u + k (round 1), then u + 16 k
-template <int LOGN>
+template <int LOGN, bool F>
 __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a, int row0) {
-    constexpr int A = LOGN - 8;
+    using T = Word<F>;
     constexpr int N = 1 << LOGN;
-    __shared__ uint64_t sm[16 * BLKPAD];
+    __shared__ T sm[16 * BLKPAD];
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
-    const PcbPrimeConst& pc = a.pr[ri.pid];
-    const uint64_t p = pc.p, p2 = 2 * p;
-    const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
-    const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+    const uint64_t p = a.pr[ri.pid].p;
+    const Mod<F> md = make_mod<F>(p);
+    const T* iw = (const T*)a.iw + ((size_t)ri.pid << LOGN);
+    const T* iws = (const T*)a.iws + ((size_t)ri.pid << LOGN);
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;
     uint64_t* blk = ri.row + (size_t)b * 256;
-    uint64_t x[16];
+    T x[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p);
+    for (int k = 0; k < 16; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p));
     // spans h = 1, 2, 4, 8: group index j / (2h), m = N / (2h)
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
@@ -220,10 +341,10 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
             if (k & h) continue;
             const int m = N / (2 * h);
             const int idx = m + ((b * 256 + 16 * u + k) >> (l + 1));
-            gs_bfly(x[k], x[k + h], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+            gs(x[k], x[k + h], __ldg(iw + idx), __ldg(iws + idx), md, (l & 1) == 0);
         }
     }
-    uint64_t* s = sm + lb * BLKPAD;
+    T* s = sm + lb * BLKPAD;
 #pragma unroll
     for (int k = 0; k < 16; ++k) s[pad(16 * u + k)] = x[k];
     __syncwarp();
@@ -238,32 +359,32 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
             if (k & hk) continue;
             const int m = N >> (l + 1);
             const int idx = m + ((b * 256 + u + 16 * k) >> (l + 1));
-            gs_bfly(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), p, p2);
+            gs(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), md, (l & 1) == 0);
         }
     }
-    (void)A;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) blk[u + 16 * k] = x[k];
+    for (int k = 0; k < 16; ++k) store_mid<F>(blk + u + 16 * k, x[k]);
 }
 
 // Column pass: spans 256 .. N/2, then the row's last-pass factor (N^-1, or es[i] with ess[i])
-template <int LOGN>
+template <int LOGN, bool F>
 __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a, int row0) {
+    using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
-    __shared__ uint64_t sm[R * COLS];
-    __shared__ uint64_t stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
+    __shared__ T sm[R * COLS];
+    __shared__ T stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
-    const PcbPrimeConst& pc = a.pr[ri.pid];
-    const uint64_t p = pc.p, p2 = 2 * p;
-    const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
-    const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+    const uint64_t p = a.pr[ri.pid].p;
+    const Mod<F> md = make_mod<F>(p);
+    const T* iw = (const T*)a.iw + ((size_t)ri.pid << LOGN);
+    const T* iws = (const T*)a.iws + ((size_t)ri.pid << LOGN);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
-    uint64_t x[E];
+    T x[E];
     // round 1: row spans 1 .. E/2 (word spans 256 ..) on rows E g + k
 #pragma unroll
-    for (int k = 0; k < E; ++k) x[k] = ri.row[(size_t)(E * g + k) * 256 + col];
+    for (int k = 0; k < E; ++k) x[k] = load_mid<F>(ri.row + (size_t)(E * g + k) * 256 + col);
     for (int t = threadIdx.x; t < R; t += THREADS) {
         stw[t] = iw[t];
         stws[t] = iws[t];
@@ -277,7 +398,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
             if (k & hk) continue;
             const int m = R >> (l + 1);
             const int idx = m + ((E * g + k) >> (l + 1));
-            gs_bfly(x[k], x[k + hk], stw[idx], stws[idx], p, p2);
+            gs(x[k], x[k + hk], stw[idx], stws[idx], md, (l & 1) == 0);
         }
     }
 #pragma unroll
@@ -294,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
             if (k & hk) continue;
             const int m = R >> (l + 1);
             const int idx = m + ((g + E * k) >> (l + 1));
-            gs_bfly(x[k], x[k + hk], stw[idx], stws[idx], p, p2);
+            gs(x[k], x[k + hk], stw[idx], stws[idx], md, (l & 1) == 0);
         }
     }
     uint64_t ni, nis;
@@ -305,8 +426,16 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
         ni = ((const uint64_t*)a.ninv)[ri.pid];
         nis = ((const uint64_t*)a.ninvs)[ri.pid];
     }
+    if constexpr (F) {
+        double nc, np;
+        centred_f(ni, p, md.p, nc, np);
 #pragma unroll
-    for (int k = 0; k < E; ++k) ri.row[(size_t)(g + E * k) * 256 + col] = shoup(x[k], ni, nis, p);
+        for (int k = 0; k < E; ++k)
+            ri.row[(size_t)(g + E * k) * 256 + col] = canon_f(mul_f(x[k], nc, np, md.p), md.p, md.pinv);
+    } else {
+#pragma unroll
+        for (int k = 0; k < E; ++k) ri.row[(size_t)(g + E * k) * 256 + col] = shoup(x[k], ni, nis, p);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -319,7 +448,7 @@ __host__ int chunk_rows(const PcbNttArgs& a) {
 }
 
 template <int LOGN>
-int fwd(const PcbNttArgs* ap, cudaStream_t s) {
+int fwd_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbNttArgs a = *ap;
     if (a.nrows < 0 || a.epi < 0 || a.epi > 3 || !a.base || !a.roff || !a.rprime || !a.fw || !a.fws || !a.pr)
@@ -331,14 +460,19 @@ int fwd(const PcbNttArgs* ap, cudaStream_t s) {
     const int ch = chunk_rows<LOGN>(a);
     for (int r0 = 0; r0 < a.nrows; r0 += ch) {
         const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
-        fwd_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
-        fwd_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+        if (f64) {
+            fwd_cols<LOGN, true><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+            fwd_rows<LOGN, true><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+        } else {
+            fwd_cols<LOGN, false><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+            fwd_rows<LOGN, false><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+        }
     }
     return PCB_LAUNCHED(2u * (unsigned)((a.nrows + ch - 1) / ch));
 }
 
 template <int LOGN>
-int inv(const PcbNttArgs* ap, cudaStream_t s) {
+int inv_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbNttArgs a = *ap;
     if (a.nrows < 0 || a.epi != 0 || !a.base || !a.roff || !a.rprime || !a.iw || !a.iws || !a.pr) return PCB_BAD_ARGS;
@@ -350,16 +484,35 @@ int inv(const PcbNttArgs* ap, cudaStream_t s) {
     const int ch = chunk_rows<LOGN>(a);
     for (int r0 = 0; r0 < a.nrows; r0 += ch) {
         const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
-        inv_rows<LOGN><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
-        inv_cols<LOGN><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+        if (f64) {
+            inv_rows<LOGN, true><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+            inv_cols<LOGN, true><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+        } else {
+            inv_rows<LOGN, false><<<dim3((1 << A) / 16, n), THREADS, 0, s>>>(a, r0);
+            inv_cols<LOGN, false><<<dim3(256 / COLS, n), THREADS, 0, s>>>(a, r0);
+        }
     }
     return PCB_LAUNCHED(2u * (unsigned)((a.nrows + ch - 1) / ch));
+}
+
+// The table entries take the reference's integer twiddle tables (w, Shoup w')
+template <int LOGN>
+int fwd(const PcbNttArgs* ap, cudaStream_t s) {
+    return fwd_run<LOGN>(ap, false, s);
+}
+template <int LOGN>
+int inv(const PcbNttArgs* ap, cudaStream_t s) {
+    return inv_run<LOGN>(ap, false, s);
 }
 
 template int fwd<14>(const PcbNttArgs*, cudaStream_t);
 template int fwd<16>(const PcbNttArgs*, cudaStream_t);
 template int inv<14>(const PcbNttArgs*, cudaStream_t);
 template int inv<16>(const PcbNttArgs*, cudaStream_t);
+template int fwd_run<14>(const PcbNttArgs*, bool, cudaStream_t);
+template int fwd_run<16>(const PcbNttArgs*, bool, cudaStream_t);
+template int inv_run<14>(const PcbNttArgs*, bool, cudaStream_t);
+template int inv_run<16>(const PcbNttArgs*, bool, cudaStream_t);
 
 }  // namespace ntt
 }  // namespace pcb

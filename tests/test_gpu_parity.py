@@ -90,6 +90,38 @@ def test_ntt_launchers_match_oracle(which, request):
     assert (host(xd) == x).all()
 
 
+def test_ntt_batch_fp64_path_matches_oracle(s2):
+    """Config 2's primes are all below 2^50, so the evaluator's transforms take the FP64 butterflies; rows with the
+    extreme words (0, p - 1, (p +- 1) / 2) and uniform rows, forward and inverse, against the oracle."""
+    s, o = s2
+    rng = np.random.default_rng(14)
+    nrows = 2 * s.nq + 5
+    x = np.empty((nrows, s.n), np.uint64)
+    for i in range(nrows):
+        p = o.q[i % s.nq]
+        kind = i % 5
+        if kind == 0:
+            x[i] = p - 1
+        elif kind == 1:
+            x[i] = np.where(np.arange(s.n) % 2 == 0, p - 1, 0)
+        elif kind == 2:
+            x[i] = rng.choice(np.array([0, 1, (p - 1) // 2, (p + 1) // 2, p - 1], np.uint64), s.n)
+        else:
+            x[i] = rng.integers(0, p, s.n, dtype=np.uint64)
+    xd = dev(x)
+    s.ntt_batch(xd, nrows)
+    want = x.copy()
+    O.lib().orc_ntt_batch(o.h, want, nrows, 0)
+    assert (host(xd) == want).all()
+    s.ntt_batch(xd, nrows, inverse=True)
+    assert (host(xd) == x).all()
+    inv_want = x.copy()
+    O.lib().orc_ntt_batch(o.h, inv_want, nrows, 1)
+    xd = dev(x)
+    s.ntt_batch(xd, nrows, inverse=True)
+    assert (host(xd) == inv_want).all()
+
+
 def test_ntt_epilogues_and_sources(s2):
     s, o = s2
     rng = np.random.default_rng(12)

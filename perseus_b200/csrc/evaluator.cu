@@ -109,7 +109,8 @@ struct PcbCtx {
     // device tables
     PcbPrimeConst* pr = nullptr;
     uint64_t *fw = nullptr, *fws = nullptr, *iw = nullptr, *iws = nullptr, *ninv = nullptr, *ninvs = nullptr;
-    double *fwf = nullptr, *fwp = nullptr, *iwf = nullptr, *iwp = nullptr;  // centred twiddles w, fl(w / p) (f64)
+    double *fpk = nullptr, *ipk = nullptr;  // f64: forward / inverse twiddle packs, pack_words() doubles per prime
+    size_t pack_words() const { return 2 * ((n >> 8) + 256 + n); }
     int32_t* digit_of = nullptr;
     uint64_t *pmod = nullptr, *pmods = nullptr, *pinv = nullptr, *pinvs = nullptr;
     uint32_t* id_roff = nullptr;   // i
@@ -190,10 +191,8 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
     c.ninv = A.take<uint64_t>(rows);
     c.ninvs = A.take<uint64_t>(rows);
     if (c.f64) {
-        c.fwf = A.take<double>((size_t)rows * n);
-        c.fwp = A.take<double>((size_t)rows * n);
-        c.iwf = A.take<double>((size_t)rows * n);
-        c.iwp = A.take<double>((size_t)rows * n);
+        c.fpk = A.take<double>((size_t)rows * c.pack_words());
+        c.ipk = A.take<double>((size_t)rows * c.pack_words());
     }
     if (fill) {
         std::vector<PcbPrimeConst> pr(rows);
@@ -207,12 +206,12 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
         CK(upload(c.ninv, ni, s));
         CK(upload(c.ninvs, nis, s));
         std::vector<uint64_t> w(n), ws(n), iw(n), iws(n), pw(n), ipw(n);
-        std::vector<double> wf(n), wp(n), iwf(n), iwp(n);
-        // centred twiddle and its quotient by p, both exact or correctly rounded (|w| < 2^49)
-        auto centred = [](uint64_t v, uint64_t p, double& f, double& q) {
+        std::vector<double> fpk(c.f64 ? c.pack_words() : 0), ipk(c.f64 ? c.pack_words() : 0);
+        // a pack entry: the centred twiddle and its quotient by p, exact and correctly rounded (|w| < 2^49)
+        auto centred = [](std::vector<double>& pk, size_t at, uint64_t v, uint64_t p) {
             const int64_t cv = v > p / 2 ? -(int64_t)(p - v) : (int64_t)v;
-            f = (double)cv;
-            q = f / (double)p;
+            pk[2 * at] = (double)cv;
+            pk[2 * at + 1] = (double)cv / (double)p;
         };
         for (int r = 0; r < rows; ++r) {
             const uint64_t p = c.primes[r], psi = hm::min_root(m, p), ipsi = hm::invmod(psi, p);
@@ -234,14 +233,30 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             CK(cudaMemcpyAsync(c.iw + (size_t)r * n, iw.data(), n * 8, cudaMemcpyHostToDevice, s));
             CK(cudaMemcpyAsync(c.iws + (size_t)r * n, iws.data(), n * 8, cudaMemcpyHostToDevice, s));
             if (c.f64) {
-                for (size_t i = 0; i < n; ++i) {
-                    centred(w[i], p, wf[i], wp[i]);
-                    centred(iw[i], p, iwf[i], iwp[i]);
+                // pack: column twiddles w[0 .. R), the 256-point twiddles of psi^(N/256) in OpenFHE order, the twist
+                // gamma_b^k = psi^(k c_b) at b 256 + k with c_b = 1 - 2^(L-8) + 2 brev(b) (inverse: psi^-(k c_b))
+                const size_t R = n >> 8, m2 = 2 * n;
+                auto psi_pow = [&](size_t e) { e %= m2; return e < n ? pw[e] : (pw[e - n] ? p - pw[e - n] : 0); };
+                for (size_t t = 0; t < R; ++t) {
+                    centred(fpk, t, w[t], p);
+                    centred(ipk, t, iw[t], p);
                 }
-                CK(cudaMemcpyAsync(c.fwf + (size_t)r * n, wf.data(), n * 8, cudaMemcpyHostToDevice, s));
-                CK(cudaMemcpyAsync(c.fwp + (size_t)r * n, wp.data(), n * 8, cudaMemcpyHostToDevice, s));
-                CK(cudaMemcpyAsync(c.iwf + (size_t)r * n, iwf.data(), n * 8, cudaMemcpyHostToDevice, s));
-                CK(cudaMemcpyAsync(c.iwp + (size_t)r * n, iwp.data(), n * 8, cudaMemcpyHostToDevice, s));
+                for (uint32_t t = 0; t < 256; ++t) {
+                    const size_t e = (size_t)hm::bitrev(t, 8) * (n >> 8);
+                    centred(fpk, R + t, psi_pow(e), p);
+                    centred(ipk, R + t, psi_pow(m2 - e), p);
+                }
+                for (size_t b = 0; b < R; ++b) {
+                    const size_t cb = (1 + m2 - (n >> 8) + 2 * (size_t)hm::bitrev((uint32_t)b, L - 8)) % m2;
+                    for (size_t k = 0; k < 256; ++k) {
+                        const size_t e = k * cb % m2;
+                        centred(fpk, R + 256 + b * 256 + k, psi_pow(e), p);
+                        centred(ipk, R + 256 + b * 256 + k, psi_pow(m2 - e), p);
+                    }
+                }
+                const size_t pwd = c.pack_words();
+                CK(cudaMemcpyAsync(c.fpk + r * pwd, fpk.data(), pwd * 8, cudaMemcpyHostToDevice, s));
+                CK(cudaMemcpyAsync(c.ipk + r * pwd, ipk.data(), pwd * 8, cudaMemcpyHostToDevice, s));
             }
             CK(cudaStreamSynchronize(s));  // the host staging vectors are reused per prime
         }
@@ -532,10 +547,8 @@ PcbNttArgs ntt_args(const PcbCtx& c, void* base, const uint32_t* roff, const int
     a.roff = roff;
     a.rprime = rprime;
     if (c.f64) {
-        a.fw = c.fwf;
-        a.fws = c.fwp;
-        a.iw = c.iwf;
-        a.iws = c.iwp;
+        a.fw = a.fws = c.fpk;
+        a.iw = a.iws = c.ipk;
     } else {
         a.fw = c.fw;
         a.fws = c.fws;

@@ -15,8 +15,14 @@
 //    twiddles w' = floor(w 2^64 / p); 64-bit products are emulated on the 32-bit integer multiplier.
 //  - FP64 (every prime of the launch below 2^50): words are integer-valued doubles, signed and lazy (|x| < 4p), and
 //    a product y w mod p is six FP64 operations, exact (mul_f). The B200 retires 64 FP64 FMAs per clock per SM;
-//    this butterfly measured 2.4x the integer one. Twiddles come as centred doubles w (|w| <= p/2) with
-//    wp = fl(w / p); the intermediate between the passes is stored as raw doubles.
+//    this butterfly measured 2.4x the integer one. Twiddles are pairs {w, fl(w / p)} with w centred (|w| <= p/2);
+//    the intermediate between the passes is stored as raw doubles.
+//    The row pass of this path runs one fixed 256-point transform on every block: block b's stage-l twiddles are
+//    w8[2^l + j] gamma_b^(2^(7-l)) (w8: the OpenFHE twiddles of psi^(N/256); gamma_b = psi^c_b with
+//    c_b = 1 - 2^(LOGN-8) + 2 brev(b)), which equals the fixed transform of the block pre-multiplied word-wise by
+//    gamma_b^k. The column pass applies that twist as it stores (one product per word, coalesced table reads) and
+//    the row pass reads its 255 twiddles from shared memory instead of N scattered global ones; the inverse runs the
+//    fixed inverse transform, then the inverse twist. Tables per prime: Pack<LOGN>.
 #include <type_traits>
 
 #include "arith.cuh"
@@ -122,21 +128,40 @@ __device__ __forceinline__ void store_mid(uint64_t* a, Word<F> x) {
     if constexpr (F) *a = (uint64_t)__double_as_longlong(x);
     else *a = x;
 }
-__device__ __forceinline__ void ct(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, const IntMod& m) {
-    ct_bfly(x, y, w, ws, m.p, m.p2);
+// a twiddle: {w, w'} (integer, Shoup companion) or {w, fl(w / p)} (FP64)
+template <bool F> using Tw = std::conditional_t<F, double2, ulonglong2>;
+__device__ __forceinline__ void ct(uint64_t& x, uint64_t& y, ulonglong2 t, const IntMod& m) {
+    ct_bfly(x, y, t.x, t.y, m.p, m.p2);
 }
-__device__ __forceinline__ void ct(double& x, double& y, double w, double wp, const FpMod& m) {
-    const double v = mul_f(y, w, wp, m.p), u = x;
+__device__ __forceinline__ void ct(double& x, double& y, double2 t, const FpMod& m) {
+    const double v = mul_f(y, t.x, t.y, m.p), u = x;
     x = __dadd_rn(u, v);
     y = __dsub_rn(u, v);
 }
-__device__ __forceinline__ void gs(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, const IntMod& m, bool) {
-    gs_bfly(x, y, w, ws, m.p, m.p2);
+__device__ __forceinline__ void gs(uint64_t& x, uint64_t& y, ulonglong2 t, const IntMod& m, bool) {
+    gs_bfly(x, y, t.x, t.y, m.p, m.p2);
 }
-__device__ __forceinline__ void gs(double& x, double& y, double w, double wp, const FpMod& m, bool reduce) {
+__device__ __forceinline__ void gs(double& x, double& y, double2 t, const FpMod& m, bool reduce) {
     const double s = __dadd_rn(x, y), d = __dsub_rn(x, y);
     x = reduce ? red_f(s, m.p, m.pinv) : s;
-    y = mul_f(d, w, wp, m.p);
+    y = mul_f(d, t.x, t.y, m.p);
+}
+__device__ __forceinline__ ulonglong2 tw_int(const uint64_t* w, const uint64_t* ws, int idx) {
+    return make_ulonglong2(__ldg(w + idx), __ldg(ws + idx));
+}
+
+// FP64 twiddle pack of one prime (forward and inverse each): the column stages' twiddles (indices 0 .. R-1), the
+// fixed 256-point transform's twiddles, the N twist factors gamma_b^k (forward) or gamma_b^-k (inverse) at b 256 + k
+template <int LOGN>
+struct Pack {
+    static constexpr int R = 1 << (LOGN - 8), ROW = R, TWIST = R + 256, SIZE = R + 256 + (1 << LOGN);
+};
+// Shared-memory slot of fixed twiddle t. Stages whose twiddle varies with the thread (4 .. 7 forward, 0 .. 3
+// inverse) read region [2^e, 2^(e+1)) at offset u 2^(e-4) + j; stored as [j][u], 16 threads read consecutive slots.
+__device__ __forceinline__ int tw_slot(int t) {
+    if (t < 16) return t;
+    const int e = 31 - __clz(t), off = t - (1 << e), sh = e - 4;
+    return (1 << e) + ((off & ((1 << sh) - 1)) << 4) + (off >> sh);
 }
 __device__ __forceinline__ void round_end(uint64_t&, const IntMod&) {}
 __device__ __forceinline__ void round_end(double& x, const FpMod& m) { x = red_f(x, m.p, m.pinv); }
@@ -181,21 +206,24 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
     using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ T sm[R * COLS];
-    __shared__ T stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
+    __shared__ Tw<F> stw[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
     const Mod<F> md = make_mod<F>(p);
-    const T* fw = (const T*)a.fw + ((size_t)ri.pid << LOGN);
-    const T* fws = (const T*)a.fws + ((size_t)ri.pid << LOGN);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
     T x[E];
 #pragma unroll
     for (int k = 0; k < E; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)(g + E * k) * 256 + col, p));
-    for (int t = threadIdx.x; t < R; t += THREADS) {
-        stw[t] = fw[t];
-        stws[t] = fws[t];
+    const double2* pk = nullptr;
+    if constexpr (F) {
+        pk = (const double2*)a.fw + (size_t)ri.pid * Pack<LOGN>::SIZE;
+        for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = pk[t];
+    } else {
+        const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
+        const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+        for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = make_ulonglong2(fw[t], fws[t]);
     }
     __syncthreads();
     // round 1: stages 0 .. H-1, rows g + E k: butterfly partners differ in k by E/2, E/4, ..
@@ -205,8 +233,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
-            const int m = 1 << s, idx = m + (k >> (H - s));
-            ct(x[k], x[k + half], stw[idx], stws[idx], md);
+            ct(x[k], x[k + half], stw[(1 << s) + (k >> (H - s))], md);
         }
     }
 #pragma unroll
@@ -224,14 +251,17 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < E; ++k) {
             if (k & half) continue;
-            const int m = 1 << s, idx = m + (g << (s - H)) + (k >> (A - s));
-            ct(x[k], x[k + half], stw[idx], stws[idx], md);
+            ct(x[k], x[k + half], stw[(1 << s) + (g << (s - H)) + (k >> (A - s))], md);
         }
     }
 #pragma unroll
     for (int k = 0; k < E; ++k) {
-        round_end(x[k], md);
-        store_mid<F>(ri.row + (size_t)(E * g + k) * 256 + col, x[k]);
+        const size_t w = (size_t)(E * g + k) * 256 + col;  // block E g + k, word col: twist gamma_b^col
+        if constexpr (F) {
+            const double2 t = __ldg(pk + Pack<LOGN>::TWIST + w);
+            x[k] = mul_f(x[k], t.x, t.y, md.p);
+        }
+        store_mid<F>(ri.row + w, x[k]);
     }
 }
 
@@ -242,27 +272,32 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
     using T = Word<F>;
     constexpr int A = LOGN - 8;
     __shared__ T sm[16 * BLKPAD];
+    __shared__ double2 sw[F ? 256 : 1];  // FP64: the fixed transform's twiddles, slots tw_slot(t)
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
     const Mod<F> md = make_mod<F>(p);
-    const T* fw = (const T*)a.fw + ((size_t)ri.pid << LOGN);
-    const T* fws = (const T*)a.fws + ((size_t)ri.pid << LOGN);
+    const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
+    const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
+    if constexpr (F) {
+        const double2* pk = (const double2*)a.fw + (size_t)ri.pid * Pack<LOGN>::SIZE + Pack<LOGN>::ROW;
+        sw[tw_slot(threadIdx.x)] = pk[threadIdx.x];
+    }
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;  // 256-word block of the row
     uint64_t* blk = ri.row + (size_t)b * 256;
     T x[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) x[k] = load_mid<F>(blk + u + 16 * k);
+    if constexpr (F) __syncthreads();
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
         const int half = 16 >> (l + 1);
-        const int m = 1 << (A + l);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             if (k & half) continue;
-            const int idx = m + (b << l) + (k >> (4 - l));
-            ct(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), md);
+            if constexpr (F) ct(x[k], x[k + half], sw[(1 << l) + (k >> (4 - l))], md);
+            else ct(x[k], x[k + half], tw_int(fw, fws, (1 << (A + l)) + (b << l) + (k >> (4 - l))), md);
         }
     }
     T* s = sm + lb * BLKPAD;
@@ -277,12 +312,13 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
 #pragma unroll
     for (int l = 4; l < 8; ++l) {
         const int half = 16 >> (l - 3);
-        const int m = 1 << (A + l);
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             if (k & half) continue;
-            const int idx = m + (b << l) + (u << (l - 4)) + (k >> (8 - l));
-            ct(x[k], x[k + half], __ldg(fw + idx), __ldg(fws + idx), md);
+            if constexpr (F) ct(x[k], x[k + half], sw[(1 << l) + ((k >> (8 - l)) << 4) + u], md);
+            else
+                ct(x[k], x[k + half],
+                   tw_int(fw, fws, (1 << (A + l)) + (b << l) + (u << (l - 4)) + (k >> (8 - l))), md);
         }
     }
 #pragma unroll
@@ -320,18 +356,25 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
     using T = Word<F>;
     constexpr int N = 1 << LOGN;
     __shared__ T sm[16 * BLKPAD];
+    __shared__ double2 sw[F ? 256 : 1];  // FP64: the fixed inverse transform's twiddles, slots tw_slot(t)
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
     const Mod<F> md = make_mod<F>(p);
-    const T* iw = (const T*)a.iw + ((size_t)ri.pid << LOGN);
-    const T* iws = (const T*)a.iws + ((size_t)ri.pid << LOGN);
+    const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
+    const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+    const double2* pk = nullptr;
+    if constexpr (F) {
+        pk = (const double2*)a.iw + (size_t)ri.pid * Pack<LOGN>::SIZE;
+        sw[tw_slot(threadIdx.x)] = pk[Pack<LOGN>::ROW + threadIdx.x];
+    }
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;
     uint64_t* blk = ri.row + (size_t)b * 256;
     T x[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p));
+    if constexpr (F) __syncthreads();
     // spans h = 1, 2, 4, 8: group index j / (2h), m = N / (2h)
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
@@ -339,9 +382,8 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             if (k & h) continue;
-            const int m = N / (2 * h);
-            const int idx = m + ((b * 256 + 16 * u + k) >> (l + 1));
-            gs(x[k], x[k + h], __ldg(iw + idx), __ldg(iws + idx), md, (l & 1) == 0);
+            if constexpr (F) gs(x[k], x[k + h], sw[(1 << (7 - l)) + ((k >> (l + 1)) << 4) + u], md, (l & 1) == 0);
+            else gs(x[k], x[k + h], tw_int(iw, iws, N / (2 * h) + ((b * 256 + 16 * u + k) >> (l + 1))), md, false);
         }
     }
     T* s = sm + lb * BLKPAD;
@@ -357,13 +399,18 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
             if (k & hk) continue;
-            const int m = N >> (l + 1);
-            const int idx = m + ((b * 256 + u + 16 * k) >> (l + 1));
-            gs(x[k], x[k + hk], __ldg(iw + idx), __ldg(iws + idx), md, (l & 1) == 0);
+            if constexpr (F) gs(x[k], x[k + hk], sw[(1 << (7 - l)) + (k >> (l - 3))], md, (l & 1) == 0);
+            else gs(x[k], x[k + hk], tw_int(iw, iws, (N >> (l + 1)) + ((b * 256 + u + 16 * k) >> (l + 1))), md, false);
         }
     }
 #pragma unroll
-    for (int k = 0; k < 16; ++k) store_mid<F>(blk + u + 16 * k, x[k]);
+    for (int k = 0; k < 16; ++k) {
+        if constexpr (F) {  // the inverse twist gamma_b^-k of word u + 16 k
+            const double2 t = __ldg(pk + Pack<LOGN>::TWIST + (size_t)b * 256 + u + 16 * k);
+            x[k] = mul_f(x[k], t.x, t.y, md.p);
+        }
+        store_mid<F>(blk + u + 16 * k, x[k]);
+    }
 }
 
 // Column pass: spans 256 .. N/2, then the row's last-pass factor (N^-1, or es[i] with ess[i])
@@ -372,22 +419,24 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
     using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ T sm[R * COLS];
-    __shared__ T stw[R], stws[R];  // the column stages use twiddles 1 .. R-1 only
+    __shared__ Tw<F> stw[R];  // the column stages use twiddles 1 .. R-1 only
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
     const Mod<F> md = make_mod<F>(p);
-    const T* iw = (const T*)a.iw + ((size_t)ri.pid << LOGN);
-    const T* iws = (const T*)a.iws + ((size_t)ri.pid << LOGN);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
     T x[E];
     // round 1: row spans 1 .. E/2 (word spans 256 ..) on rows E g + k
 #pragma unroll
     for (int k = 0; k < E; ++k) x[k] = load_mid<F>(ri.row + (size_t)(E * g + k) * 256 + col);
-    for (int t = threadIdx.x; t < R; t += THREADS) {
-        stw[t] = iw[t];
-        stws[t] = iws[t];
+    if constexpr (F) {
+        const double2* pk = (const double2*)a.iw + (size_t)ri.pid * Pack<LOGN>::SIZE;
+        for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = pk[t];
+    } else {
+        const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
+        const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
+        for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = make_ulonglong2(iw[t], iws[t]);
     }
     __syncthreads();
 #pragma unroll
@@ -396,9 +445,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < E; ++k) {
             if (k & hk) continue;
-            const int m = R >> (l + 1);
-            const int idx = m + ((E * g + k) >> (l + 1));
-            gs(x[k], x[k + hk], stw[idx], stws[idx], md, (l & 1) == 0);
+            gs(x[k], x[k + hk], stw[(R >> (l + 1)) + ((E * g + k) >> (l + 1))], md, (l & 1) == 0);
         }
     }
 #pragma unroll
@@ -413,9 +460,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a
 #pragma unroll
         for (int k = 0; k < E; ++k) {
             if (k & hk) continue;
-            const int m = R >> (l + 1);
-            const int idx = m + ((g + E * k) >> (l + 1));
-            gs(x[k], x[k + hk], stw[idx], stws[idx], md, (l & 1) == 0);
+            gs(x[k], x[k + hk], stw[(R >> (l + 1)) + ((g + E * k) >> (l + 1))], md, (l & 1) == 0);
         }
     }
     uint64_t ni, nis;

@@ -29,6 +29,45 @@ __device__ __forceinline__ uint64_t shoup(uint64_t a, uint64_t w, uint64_t ws, u
     return r >= p ? r - p : r;
 }
 
+// ------------------------------------------------------------------------------------------------ FP64 arithmetic
+// For primes below 2^50 residues can live in the FP64 pipe as integer-valued doubles (B200: 64 FP64 FMAs per clock
+// per SM, as many as 32-bit integer multiplies, and a 50-bit product takes one FMA pair instead of four IMADs).
+constexpr double MAGIC = 6755399441055744.0;  // 1.5 * 2^52: fl(t + MAGIC) - MAGIC = rint(t) while |t| < 2^51
+constexpr double TWO52 = 4503599627370496.0;
+
+// y w mod p as an integer-valued double in [-0.75p, 0.75p], exact, for |y| < 2^52 and |w| <= p/2 (|y wp| < 2^51).
+// h + l = y w exactly (FMA error-free product); q = rint(y wp) is within 0.75 of y w / p (wp carries a relative
+// error of 2^-53), so h - q p is an integer below 2^53 and the FMA computes it exactly; |l| <= ulp(h) / 2 <= 2^47.
+__device__ __forceinline__ double mul_f(double y, double w, double wp, double p) {
+    const double h = __dmul_rn(y, w);
+    const double l = __fma_rn(y, w, -h);
+    const double q = __dsub_rn(__fma_rn(y, wp, MAGIC), MAGIC);
+    return __dadd_rn(__fma_rn(-q, p, h), l);
+}
+// x - rint(x / p) p, in [-p/2 - 1, p/2 + 1] for integer-valued |x| < 2^52
+__device__ __forceinline__ double red_f(double x, double p, double pinv) {
+    const double q = __dsub_rn(__fma_rn(x, pinv, MAGIC), MAGIC);
+    return __fma_rn(-q, p, x);
+}
+// the canonical word of an integer-valued |x| < 2^52: floor(x / p) is off by at most one, fixed by two selects; the
+// result r < 2^52 is the mantissa of r + 2^52
+__device__ __forceinline__ uint64_t canon_f(double x, double p, double pinv) {
+    const double q = __dsub_rn(__fma_rd(x, pinv, MAGIC), MAGIC);
+    double r = __fma_rn(-q, p, x);
+    r = r < 0.0 ? __dadd_rn(r, p) : r;
+    r = r >= p ? __dsub_rn(r, p) : r;
+    return (uint64_t)__double_as_longlong(__dadd_rn(r, TWO52)) & ((1ull << 52) - 1);
+}
+// a word below 2^52 as a double (exact)
+__device__ __forceinline__ double to_f(uint64_t x) {
+    return __dsub_rn(__longlong_as_double((long long)(x | 0x4330000000000000ull)), TWO52);
+}
+// a canonical word as a centred double and its quotient by p (per-row constants of the FP64 path)
+__device__ __forceinline__ void centred_f(uint64_t w, uint64_t p, double pf, double& wc, double& wp) {
+    wc = w > p / 2 ? -to_f(p - w) : to_f(w);
+    wp = wc / pf;
+}
+
 // 128-bit accumulator: acc += a b with the carry chain in PTX (mad.lo.cc / madc.hi)
 struct Acc {
     uint64_t lo, hi;

@@ -646,7 +646,7 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.c0_mode = c0_mode;
         a.nq = c.nq;
         a.nrows = top + 1 + c.kp;
-        CK(c.logn == 14 ? ks::dot_all_run<14>(&a, c.narrow, s) : ks::dot_all_run<16>(&a, c.narrow, s));
+        CK(c.logn == 14 ? ks::dot_all_run<14>(&a, c.narrow, c.f64, s) : ks::dot_all_run<16>(&a, c.narrow, c.f64, s));
     }
     return 0;
 }

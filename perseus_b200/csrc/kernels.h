@@ -27,7 +27,8 @@ template <int LOGN> int ks_dot_launch(const PcbKsArgs*, cudaStream_t);
 template <int LOGN> int bconv_run(const PcbBconvArgs*, bool narrow, int ns_all, cudaStream_t);
 template <int LOGN> int ks_dot_run(const PcbKsArgs*, bool narrow, cudaStream_t);
 // one key, any batch K: key words read once per launch; inputs must not alias outputs
-template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, cudaStream_t);
+// f64: every prime below 2^50 (FP64 products)
+template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, cudaStream_t);
 }  // namespace ks
 namespace keys {
 template <int LOGN> int ksk_expand_launch(const PcbKskExpandArgs*, cudaStream_t);

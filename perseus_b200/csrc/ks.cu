@@ -376,6 +376,62 @@ __global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
     }
 }
 
+// FP64 form of dot_all for primes below 2^50: a digit product x b mod p is mul_f with b centred and its quotient
+// b / p taken as fl(b fl(1 / p)) (relative error <= 2^-52: |x b / p| < 2^49, so q is within 0.63 of it and each
+// product lies in [-0.63p, 0.63p]); sums are reduced every 4 digits and made canonical once per output word.
+template <int LOGN, int ND>
+__global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
+    constexpr int D = ND > 0 ? ND : 16;
+    const int nd = ND > 0 ? ND : a.ndig;
+    const uint32_t t = a.rows[blockIdx.y];
+    const uint64_t p = a.pr[t].p;
+    const double pf = to_f(p), pinv = 1.0 / pf;
+    const uint32_t idx = blockIdx.x * BX + threadIdx.x;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t roff = ((size_t)t << LOGN) + idx;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    uint64_t pm = 0, pms = 0;
+    if ((a.c0_mode & 3) == 1 && (int)t < a.nq) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    const uint64_t* kb = (const uint64_t*)a.kb[0] + roff;
+    const uint64_t* ka = (const uint64_t*)a.ka[0] + roff;
+    double bw[D], bq[D], aw[D], aq[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+        if (ND > 0 || d < nd) {
+            const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
+            const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
+            bw[d] = b > p / 2 ? -to_f(p - b) : to_f(b);
+            aw[d] = av > p / 2 ? -to_f(p - av) : to_f(av);
+            bq[d] = __dmul_rn(bw[d], pinv);
+            aq[d] = __dmul_rn(aw[d], pinv);
+        }
+    }
+    const uint32_t k = a.autok[0];
+    const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
+#pragma unroll 2
+    for (int c = 0; c < a.K; ++c) {
+        double s0 = 0.0, s1 = 0.0;
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            if (ND > 0 || d < nd) {
+                const double x = to_f(d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + roff)
+                                              : __ldg(mu + (size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff));
+                s0 = __dadd_rn(s0, mul_f(x, bw[d], bq[d], pf));
+                s1 = __dadd_rn(s1, mul_f(x, aw[d], aq[d], pf));
+                if ((d & 3) == 3) {
+                    s0 = red_f(s0, pf, pinv);
+                    s1 = red_f(s1, pf, pinv);
+                }
+            }
+        }
+        ks_store<LOGN>(a, c, 0, t, roff, o, canon_f(s0, pf, pinv), canon_f(s1, pf, pinv), p, pm, pms);
+    }
+}
+
 template <int LOGN, bool NARROW>
 void dot_dispatch(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
     switch (a.ndig) {
@@ -389,7 +445,18 @@ void dot_dispatch(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
 }
 
 template <int LOGN>
-int dot_all_run(const PcbKsArgs* ap, bool narrow, cudaStream_t s) {
+void dot_dispatch_f(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
+    switch (a.ndig) {
+        case 1: dot_all_f<LOGN, 1><<<g, BX, 0, s>>>(a); break;
+        case 2: dot_all_f<LOGN, 2><<<g, BX, 0, s>>>(a); break;
+        case 3: dot_all_f<LOGN, 3><<<g, BX, 0, s>>>(a); break;
+        case 4: dot_all_f<LOGN, 4><<<g, BX, 0, s>>>(a); break;
+        default: dot_all_f<LOGN, 0><<<g, BX, 0, s>>>(a);
+    }
+}
+
+template <int LOGN>
+int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbKsArgs& a = *ap;
     if (a.K < 0 || a.R != 1 || a.ndig < 1 || a.ndig > 16 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
@@ -401,13 +468,14 @@ int dot_all_run(const PcbKsArgs* ap, bool narrow, cudaStream_t s) {
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
     if (a.K == 0 || a.nrows == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.nrows);
-    if (narrow) dot_dispatch<LOGN, true>(a, g, s);
+    if (f64) dot_dispatch_f<LOGN>(a, g, s);
+    else if (narrow) dot_dispatch<LOGN, true>(a, g, s);
     else dot_dispatch<LOGN, false>(a, g, s);
     return PCB_LAUNCH_RESULT();
 }
 
-template int dot_all_run<14>(const PcbKsArgs*, bool, cudaStream_t);
-template int dot_all_run<16>(const PcbKsArgs*, bool, cudaStream_t);
+template int dot_all_run<14>(const PcbKsArgs*, bool, bool, cudaStream_t);
+template int dot_all_run<16>(const PcbKsArgs*, bool, bool, cudaStream_t);
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_run<14>(const PcbBconvArgs*, bool, int, cudaStream_t);

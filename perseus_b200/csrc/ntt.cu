@@ -34,6 +34,14 @@ constexpr int THREADS = 256;
 #ifndef NTT_MIN_BLOCKS
 #define NTT_MIN_BLOCKS 3  // at most 80 registers per thread: 24 warps per SM (measured faster than 4 CTAs with spills)
 #endif
+// CTAs per SM of the FP64 passes (column passes, row passes); 4 fit in 64 registers without spills but measured
+// slower on the config-2 step (160.4 and 164.6 ms against 159.8 ms at 3 and 3)
+#ifndef NTT_COLS_BLOCKS_F
+#define NTT_COLS_BLOCKS_F 3
+#endif
+#ifndef NTT_ROWS_BLOCKS_F
+#define NTT_ROWS_BLOCKS_F 3
+#endif
 
 // ------------------------------------------------------------------------------------------------ integer butterflies
 __device__ __forceinline__ void ct_bfly(uint64_t& x, uint64_t& y, uint64_t w, uint64_t ws, uint64_t p, uint64_t p2) {
@@ -52,43 +60,6 @@ __device__ __forceinline__ uint64_t canon4(uint64_t x, uint64_t p) {
     const uint64_t p2 = 2 * p;
     x = x >= p2 ? x - p2 : x;
     return x >= p ? x - p : x;
-}
-
-// ------------------------------------------------------------------------------------------------ FP64 arithmetic
-constexpr double MAGIC = 6755399441055744.0;  // 1.5 * 2^52: fl(t + MAGIC) - MAGIC = rint(t) while |t| < 2^51
-constexpr double TWO52 = 4503599627370496.0;
-
-// y w mod p as an integer-valued double in [-0.75p, 0.75p], exact, for |y| < 2^52 and |w| <= p/2 (|y wp| < 2^51).
-// h + l = y w exactly (FMA error-free product); q = rint(y wp) is within 0.75 of y w / p (wp carries a relative
-// error of 2^-53), so h - q p is an integer below 2^53 and the FMA computes it exactly; |l| <= ulp(h) / 2 <= 2^47.
-__device__ __forceinline__ double mul_f(double y, double w, double wp, double p) {
-    const double h = __dmul_rn(y, w);
-    const double l = __fma_rn(y, w, -h);
-    const double q = __dsub_rn(__fma_rn(y, wp, MAGIC), MAGIC);
-    return __dadd_rn(__fma_rn(-q, p, h), l);
-}
-// x - rint(x / p) p, in [-p/2 - 1, p/2 + 1] for integer-valued |x| < 2^52
-__device__ __forceinline__ double red_f(double x, double p, double pinv) {
-    const double q = __dsub_rn(__fma_rn(x, pinv, MAGIC), MAGIC);
-    return __fma_rn(-q, p, x);
-}
-// the canonical word of an integer-valued |x| < 2^52: floor(x / p) is off by at most one, fixed by two selects; the
-// result r < 2^52 is the mantissa of r + 2^52
-__device__ __forceinline__ uint64_t canon_f(double x, double p, double pinv) {
-    const double q = __dsub_rn(__fma_rd(x, pinv, MAGIC), MAGIC);
-    double r = __fma_rn(-q, p, x);
-    r = r < 0.0 ? __dadd_rn(r, p) : r;
-    r = r >= p ? __dsub_rn(r, p) : r;
-    return (uint64_t)__double_as_longlong(__dadd_rn(r, TWO52)) & ((1ull << 52) - 1);
-}
-// a word below 2^52 as a double (exact)
-__device__ __forceinline__ double to_f(uint64_t x) {
-    return __dsub_rn(__longlong_as_double((long long)(x | 0x4330000000000000ull)), TWO52);
-}
-// a canonical word as a centred double and its quotient by p (per-row constants of the FP64 path)
-__device__ __forceinline__ void centred_f(uint64_t w, uint64_t p, double pf, double& wc, double& wp) {
-    wc = w > p / 2 ? -to_f(p - w) : to_f(w);
-    wp = wc / pf;
 }
 
 // ------------------------------------------------------------------------------------------------ arithmetic policy
@@ -202,7 +173,7 @@ __device__ __forceinline__ uint64_t load_in(const PcbNttArgs& a, int i, const ui
 // ------------------------------------------------------------------------------------------------ forward
 // Column pass: stages 0 .. A-1 on COLS columns; thread (cc, g) holds rows g + E k (round 1), then E g + k (round 2)
 template <int LOGN, bool F>
-__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a, int row0) {
     using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ T sm[R * COLS];
@@ -268,7 +239,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_cols(PcbNttArgs a
 // Row pass: the last 8 stages over 256-word blocks, 16 blocks per CTA, 16 threads per block; thread u holds words
 // u + 16 k (round 1) then 16 u + k (round 2, 16 consecutive words: vector stores and the epilogue)
 template <int LOGN, bool F>
-__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a, int row0) {
     using T = Word<F>;
     constexpr int A = LOGN - 8;
     __shared__ T sm[16 * BLKPAD];
@@ -352,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) fwd_rows(PcbNttArgs a
 // ------------------------------------------------------------------------------------------------ inverse
 // Row pass first (GS spans 1 .. 128 inside 256-word blocks); thread u holds 16 u + k (round 1), then u + 16 k
 template <int LOGN, bool F>
-__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a, int row0) {
     using T = Word<F>;
     constexpr int N = 1 << LOGN;
     __shared__ T sm[16 * BLKPAD];
@@ -372,8 +343,18 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
     const int b = blockIdx.x * 16 + lb;
     uint64_t* blk = ri.row + (size_t)b * 256;
     T x[16];
+    if (a.soff == nullptr) {  // 16 consecutive words: 16-byte loads
+        const ulonglong2* v = (const ulonglong2*)(blk + 16 * u);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p));
+        for (int k = 0; k < 8; ++k) {
+            const ulonglong2 t = v[k];
+            x[2 * k] = from_u64<F>(t.x);
+            x[2 * k + 1] = from_u64<F>(t.y);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) x[k] = from_u64<F>(load_in<LOGN>(a, i, ri.row, (size_t)b * 256 + 16 * u + k, p));
+    }
     if constexpr (F) __syncthreads();
     // spans h = 1, 2, 4, 8: group index j / (2h), m = N / (2h)
 #pragma unroll
@@ -415,7 +396,7 @@ __global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_rows(PcbNttArgs a
 
 // Column pass: spans 256 .. N/2, then the row's last-pass factor (N^-1, or es[i] with ess[i])
 template <int LOGN, bool F>
-__global__ void __launch_bounds__(THREADS, NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a, int row0) {
+__global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCKS) inv_cols(PcbNttArgs a, int row0) {
     using T = Word<F>;
     constexpr int A = LOGN - 8, R = 1 << A, H = A / 2, E = 1 << H, COLS = 256 / E;
     __shared__ T sm[R * COLS];

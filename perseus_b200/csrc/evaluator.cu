@@ -605,7 +605,7 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     b.pr = c.pr;
     b.njobs = K * l.ndig;
     b.max_tgt = l.mu_max_tgt;
-    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, l.mu_ns, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, l.mu_ns, s));
     PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
     CK(ntt_fwd(c, &f, s));
     return 0;
@@ -667,7 +667,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     b.pr = c.pr;
     b.njobs = 2 * K;
     b.max_tgt = top + 1;
-    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.kp, s) : ks::bconv_run<16>(&b, c.narrow, c.kp, s));
+    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, c.kp, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, c.kp, s));
     PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
     f.epi = accumulate ? 2 : 1;
     f.eout = out;

@@ -24,7 +24,8 @@ template <int LOGN> int bconv_launch(const PcbBconvArgs*, cudaStream_t);
 template <int LOGN> int ks_dot_launch(const PcbKsArgs*, cudaStream_t);
 // narrow = every residue and constant of the launch is below 2^52 (26-bit-split accumulators; ks_dot: K <= 4)
 // ns_all: the source count shared by every job of the launch (0: mixed)
-template <int LOGN> int bconv_run(const PcbBconvArgs*, bool narrow, int ns_all, cudaStream_t);
+// f64: every prime of the launch below 2^50 (FP64 products)
+template <int LOGN> int bconv_run(const PcbBconvArgs*, bool narrow, bool f64, int ns_all, cudaStream_t);
 template <int LOGN> int ks_dot_run(const PcbKsArgs*, bool narrow, cudaStream_t);
 // one key, any batch K: key words read once per launch; inputs must not alias outputs
 // f64: every prime below 2^50 (FP64 products)

@@ -145,6 +145,101 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
     }
 }
 
+// FP64 form for chains whose primes are all below 2^50: each product y_i M[i][t] mod t is mul_f with M centred and
+// M / t taken as fl(M fl(1 / t)); sources enter as canonical doubles (|y M / t| < 2^49, so every product lies in
+// [-0.625t, 0.625t]); the sum is reduced every 4 sources and made canonical once. The conversion matrix sits in shared
+// memory as {M, M / t} pairs. Exact (HPS) jobs take their correction through the integer Barrett step.
+template <int LOGN, int NS>
+__global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
+    constexpr int S = NS > 0 ? NS : MAX_SRC;
+    __shared__ double2 sM[MAX_SRC * MAX_TGT];
+    __shared__ double2 sP[MAX_TGT];  // {t, fl(1 / t)}
+    __shared__ uint32_t sRow[MAX_TGT];
+    const PcbBconvJob j = a.jobs[blockIdx.y];
+    const uint64_t* pool = (const uint64_t*)a.pool + j.pool_off;
+    const int ns = NS > 0 ? NS : (int)j.nsrc, nt = (int)j.ntgt;
+    // outside the kernel's job shape: nothing is written
+    if (ns < 1 || ns > MAX_SRC || nt > MAX_TGT || (int)j.nsrc != ns) return;
+    const uint64_t* srow = pool;
+    const uint64_t* sprime = pool + ns;
+    const uint64_t* pre = pool + 2 * ns;
+    const uint64_t* trow = pool + 3 * ns;
+    const uint64_t* tprime = pool + 3 * ns + nt;
+    const uint64_t* M = pool + 3 * ns + 2 * nt;
+    for (int t = threadIdx.x; t < nt; t += BX) {
+        const double tf = to_f(a.pr[tprime[t]].p);
+        sP[t] = make_double2(tf, 1.0 / tf);
+        sRow[t] = (uint32_t)trow[t];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < ns * nt; e += BX) {
+        const uint64_t v = M[e], tp = a.pr[tprime[e % nt]].p;
+        const double2 pt = sP[e % nt];
+        const double w = v > tp / 2 ? -to_f(tp - v) : to_f(v);
+        sM[e] = make_double2(w, __dmul_rn(w, pt.y));
+    }
+    __syncthreads();
+    const size_t k = (size_t)blockIdx.x * BX + threadIdx.x;
+    const uint64_t* src = (const uint64_t*)a.src + ((size_t)j.src_off << LOGN) + k;
+    uint64_t* dst = (uint64_t*)a.dst + ((size_t)j.dst_off << LOGN) + k;
+    uint64_t y[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+        if (NS > 0 || i < ns) {
+            const uint64_t x = src[(size_t)srow[i] << LOGN];
+            y[i] = j.prescaled ? x : mul_mod(x, pre[i], a.pr[sprime[i]]);
+        }
+    }
+    uint64_t u = 0;
+    const uint64_t* bmod = nullptr;
+    if (j.exact) {
+        const uint64_t* rbw = M + ns * nt;
+        if (j.exact == 2) {
+            u = (uint64_t)(ns >> 1) + (uint64_t)((ns & 1) & (((uint32_t)k * 0x9E3779B1u) >> 31));
+        } else {
+            double v = 0.0;
+#pragma unroll
+            for (int i = 0; i < S; ++i)
+                if (NS > 0 || i < ns) v = __fma_rn((double)y[i], __longlong_as_double((long long)rbw[i]), v);
+            u = (uint64_t)floor(v + 0.5);
+        }
+        bmod = rbw + ns;
+    }
+    double yf[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i)
+        if (NS > 0 || i < ns) yf[i] = to_f(y[i]);
+    for (int t = 0; t < nt; ++t) {
+        const double2 pt = sP[t];
+        double acc = 0.0;
+#pragma unroll
+        for (int i = 0; i < S; ++i) {
+            if (NS > 0 || i < ns) {
+                const double2 m = sM[i * nt + t];
+                acc = __dadd_rn(acc, mul_f(yf[i], m.x, m.y, pt.x));
+                if ((i & 3) == 3 && i + 1 < ns) acc = red_f(acc, pt.x, pt.y);
+            }
+        }
+        uint64_t r = canon_f(acc, pt.x, pt.y);
+        if (bmod) {
+            const PcbPrimeConst& pc = a.pr[tprime[t]];
+            r = sub_mod(r, reduce(mul_wide(u, bmod[t]), pc), pc.p);
+        }
+        dst[(size_t)sRow[t] << LOGN] = r;
+    }
+}
+
+template <int LOGN>
+void bconv_dispatch_f(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
+    switch (ns_all) {
+        case 1: bconv_f<LOGN, 1><<<g, BX, 0, s>>>(a); break;
+        case 2: bconv_f<LOGN, 2><<<g, BX, 0, s>>>(a); break;
+        case 4: bconv_f<LOGN, 4><<<g, BX, 0, s>>>(a); break;
+        case 8: bconv_f<LOGN, 8><<<g, BX, 0, s>>>(a); break;
+        default: bconv_f<LOGN, 0><<<g, BX, 0, s>>>(a);
+    }
+}
+
 template <int LOGN, bool NARROW>
 void bconv_dispatch(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
     switch (ns_all) {
@@ -158,21 +253,22 @@ void bconv_dispatch(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
 
 // ns_all: the source count every job of the launch shares (1, 2, 4 or 8 get unrolled kernels), 0 when they differ
 template <int LOGN>
-int bconv_run(const PcbBconvArgs* ap, bool narrow, int ns_all, cudaStream_t s) {
+int bconv_run(const PcbBconvArgs* ap, bool narrow, bool f64, int ns_all, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbBconvArgs& a = *ap;
     if (a.njobs < 0 || a.max_tgt < 0 || a.max_tgt > MAX_TGT || !a.src || !a.dst || !a.jobs || !a.pool || !a.pr)
         return PCB_BAD_ARGS;
     if (a.njobs == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.njobs);
-    if (narrow) bconv_dispatch<LOGN, true>(a, ns_all, g, s);
+    if (f64) bconv_dispatch_f<LOGN>(a, ns_all, g, s);
+    else if (narrow) bconv_dispatch<LOGN, true>(a, ns_all, g, s);
     else bconv_dispatch<LOGN, false>(a, ns_all, g, s);
     return PCB_LAUNCH_RESULT();
 }
 
 template <int LOGN>
 int bconv_launch(const PcbBconvArgs* ap, cudaStream_t s) {
-    return bconv_run<LOGN>(ap, false, 0, s);
+    return bconv_run<LOGN>(ap, false, false, 0, s);
 }
 
 // ------------------------------------------------------------------------------------------------ ks_dot
@@ -478,8 +574,8 @@ template int dot_all_run<14>(const PcbKsArgs*, bool, bool, cudaStream_t);
 template int dot_all_run<16>(const PcbKsArgs*, bool, bool, cudaStream_t);
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
-template int bconv_run<14>(const PcbBconvArgs*, bool, int, cudaStream_t);
-template int bconv_run<16>(const PcbBconvArgs*, bool, int, cudaStream_t);
+template int bconv_run<14>(const PcbBconvArgs*, bool, bool, int, cudaStream_t);
+template int bconv_run<16>(const PcbBconvArgs*, bool, bool, int, cudaStream_t);
 template int ks_dot_launch<14>(const PcbKsArgs*, cudaStream_t);
 template int ks_dot_launch<16>(const PcbKsArgs*, cudaStream_t);
 template int ks_dot_run<14>(const PcbKsArgs*, bool, cudaStream_t);

@@ -11,6 +11,8 @@
  *     by tests/test_abi.py) so a reference caller's #[repr(C)] values can be handed over unchanged. Launchers copy
  *     their arguments, are stream-ordered and return 0 (ok), -1 / -2 (argument out of range) or a positive
  *     cudaError_t (args.cuh:1036). Entries this library does not provide are non-null and return -1.
+ *     Rows are moved 16 bytes at a time: row bases must be 16-byte aligned and row strides even (in words); the
+ *     NTT and element-wise launchers refuse other pointers with -1 (device allocations are 256-byte aligned).
  *
  *  2. The evaluator (the reference's pc-gpu Evaluator / KeySwitcher / Rescaler, crates/pc-gpu/src/{relin,rotate,
  *     ks,rescale,encrypt,keygen}.rs): a context over one chain with device-resident keys, and ciphertext ops on
@@ -368,6 +370,10 @@ int pcb_add(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, in
 int pcb_sub(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
             cudaStream_t stream);
 /* out = a * b relinearized, rescale pending (crates/pc-gpu/src/relin.rs:213-232); out may alias a or b */
+/* out = a_0 + a_1 + ... + a_(n-1) for n (1 .. 32) batches of K ciphertexts at level top, every input read once; out
+ * may be one of the inputs. No counterpart in the reference (its Fhe.add is pairwise): one pass instead of n - 1. */
+int pcb_sum(PcbCtx* ctx, const uint64_t* const* ins, int32_t n, uint64_t* out, int32_t top, int32_t K,
+            cudaStream_t stream);
 int pcb_mult(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
              cudaStream_t stream);
 /* in place: rows 0..top-1 = q_top^-1 (x - lift(x_top)) (crates/pc-gpu/src/rescale.rs:230) */

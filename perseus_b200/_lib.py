@@ -185,6 +185,7 @@ def lib():
         "pcb_encode": (C.c_int, [vp, C.POINTER(dbl), i32, i32, dbl, i32, u64p]),
         "pcb_pt_load": (C.c_int, [vp, u64p, i32, vp, vp]),
         "pcb_add": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_sum": (C.c_int, [vp, vp, i32, vp, i32, i32, vp]),
         "pcb_sub": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_mult": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_rescale": (C.c_int, [vp, vp, i32, i32, vp]),

@@ -5,6 +5,7 @@
 // All of these are HBM-bound streams: every thread moves 4 consecutive words (two 16-byte vector accesses per
 // operand), grids are (N / 1024, rows, ciphertexts x parts) so one launch covers a whole batch.
 #include "arith.cuh"
+#include "kernels.h"
 
 namespace pcb {
 namespace elem {
@@ -66,6 +67,12 @@ __global__ void __launch_bounds__(BX) ew(PcbEwArgs a) {
     st4(o, r);
 }
 
+// Kernels that move 4 words per thread as two 16-byte accesses need every row to start on a 16-byte boundary: the
+// base 16-byte aligned and both strides even (a null base is checked by the caller)
+__host__ inline bool ok16(const PcbPolyRef& r) {
+    return ((uintptr_t)r.base & 15) == 0 && (r.ct_stride & 1) == 0 && (r.part_stride & 1) == 0;
+}
+
 template <int LOGN, int OP>
 int ew_launch(const PcbEwArgs* ap, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
@@ -75,6 +82,7 @@ int ew_launch(const PcbEwArgs* ap, cudaStream_t s) {
     if (OP != EW_COPY && !a.pr) return PCB_BAD_ARGS;
     if ((OP == EW_ADD || OP == EW_SUB_MUL) && !a.b.base) return PCB_BAD_ARGS;
     if ((OP == EW_SCALE || OP == EW_SUB_MUL) && (!a.sc || !a.scs)) return PCB_BAD_ARGS;
+    if (!ok16(a.out) || !ok16(a.a) || ((OP == EW_ADD || OP == EW_SUB_MUL) && !ok16(a.b))) return PCB_BAD_ARGS;
     if (rows == 0 || a.K == 0) return 0;
     ew<LOGN, OP><<<dim3((1 << LOGN) / (BX * WPT), rows, a.K * a.nparts), BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
@@ -148,6 +156,8 @@ int tensor_launch(const PcbTensorArgs* ap, cudaStream_t s) {
     if (a.npairs < 1 || a.npairs > 2 || a.n < 0 || a.K < 0 || !a.pr || !a.out.base || !a.d2.base || !a.a0.base ||
         !a.b0.base || (a.npairs == 2 && (!a.a1.base || !a.b1.base)))
         return PCB_BAD_ARGS;
+    if (!ok16(a.out) || !ok16(a.d2) || !ok16(a.a0) || !ok16(a.b0) || (a.npairs == 2 && (!ok16(a.a1) || !ok16(a.b1))))
+        return PCB_BAD_ARGS;
     if (a.n == 0 || a.K == 0) return 0;
     tensor<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, a.K), BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
@@ -184,6 +194,7 @@ int md_epilogue_launch(const PcbMdEpiArgs* ap, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbMdEpiArgs& a = *ap;
     if (a.n < 0 || a.K < 0 || !a.pr || !a.dst.base || !a.x.base || !a.t.base || !a.binv || !a.binvs) return PCB_BAD_ARGS;
+    if (!ok16(a.dst) || !ok16(a.x) || !ok16(a.t)) return PCB_BAD_ARGS;
     if (a.n == 0 || a.K == 0) return 0;
     md_epilogue<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, 2 * a.K), BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
@@ -245,6 +256,7 @@ int rescale_combine_launch(const PcbRescaleCombineArgs* ap, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbRescaleCombineArgs& a = *ap;
     if (a.n < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.alpha || !a.alphas) return PCB_BAD_ARGS;
+    if (!ok16(a.x) || !ok16(a.tmp)) return PCB_BAD_ARGS;
     if (a.n == 0 || a.K == 0) return 0;
     rescale_combine<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, 2 * a.K), BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
@@ -277,7 +289,41 @@ int automorph_launch(const PcbAutomorphArgs* ap, cudaStream_t s) {
     return PCB_LAUNCH_RESULT();
 }
 
+// ------------------------------------------------------------------------------------------------ sum
+// one pass over n inputs (each read once) instead of n - 1 pairwise adds; out may be one of the inputs
+template <int LOGN>
+__global__ void __launch_bounds__(BX) sum_cts(SumArgs a) {
+    const int row = blockIdx.y, c = blockIdx.z >> 1, part = blockIdx.z & 1;
+    const size_t off = (size_t)c * a.ct_stride + (size_t)part * a.part_stride + ((size_t)row << LOGN) +
+                       ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    const uint64_t p = a.pr[row].p;
+    V4 acc = ld4(a.in[0] + off);
+    for (int m = 1; m < a.n; ++m) {
+        const V4 x = ld4(a.in[m] + off);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) acc.v[w] = add_mod(acc.v[w], x.v[w], p);
+    }
+    uint64_t r[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) r[w] = acc.v[w];
+    st4(a.out + off, r);
+}
+
+template <int LOGN>
+int sum_launch(const SumArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const SumArgs& a = *ap;
+    if (a.n < 1 || a.n > SUM_MAX || a.nrows < 0 || a.K < 0 || !a.out || !a.pr) return PCB_BAD_ARGS;
+    if (((uintptr_t)a.out & 15) || (a.ct_stride & 1) || (a.part_stride & 1)) return PCB_BAD_ARGS;
+    for (int m = 0; m < a.n; ++m)
+        if (!a.in[m] || ((uintptr_t)a.in[m] & 15)) return PCB_BAD_ARGS;
+    if (a.nrows == 0 || a.K == 0) return 0;
+    sum_cts<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.nrows, 2 * a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
 #define PCB_INST(L)                                                                                  \
+    template int sum_launch<L>(const SumArgs*, cudaStream_t);                                        \
     template int ew_launch<L, EW_ADD>(const PcbEwArgs*, cudaStream_t);                               \
     template int ew_launch<L, EW_SCALE>(const PcbEwArgs*, cudaStream_t);                             \
     template int ew_launch<L, EW_SUB_MUL>(const PcbEwArgs*, cudaStream_t);                           \

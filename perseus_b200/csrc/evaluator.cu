@@ -1034,6 +1034,28 @@ int pcb_sub(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int3
     return ew_ct(c, a, b, out, top, K, 1, s);
 }
 
+int pcb_sum(PcbCtx* c, const uint64_t* const* ins, int32_t n, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !ins || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (n < 1 || n > elem::SUM_MAX) return fail(PCB_BAD_ARGS, "%d inputs (1 .. %d)", n, elem::SUM_MAX);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    elem::SumArgs a;
+    memset(&a, 0, sizeof a);
+    for (int m = 0; m < n; ++m) {
+        if (!ins[m]) return fail(PCB_BAD_ARGS, "input %d is null", m);
+        a.in[m] = ins[m];
+    }
+    a.out = out;
+    a.pr = c->pr;
+    a.ct_stride = c->ct_words();
+    a.part_stride = (uint64_t)c->rows * c->n;
+    a.n = n;
+    a.nrows = top + 1;
+    a.K = K;
+    CK(c->logn == 14 ? elem::sum_launch<14>(&a, s) : elem::sum_launch<16>(&a, s));
+    return 0;
+}
+
 int pcb_mult(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
     if (!c || !a || !b || !out) return fail(PCB_BAD_ARGS, "null argument");
     int rc = check_top(*c, top, K);

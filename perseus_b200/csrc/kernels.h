@@ -12,6 +12,16 @@ template <int LOGN> int inv_run(const PcbNttArgs*, bool f64, cudaStream_t);
 }  // namespace ntt
 namespace elem {
 enum EwOpDecl { ADD = 0, SCALE = 1, SUB_MUL = 2, COPY = 3 };
+// out = sum of n batches of ciphertexts mod p, rows 0 .. nrows-1 of both parts (an internal launch, not a table entry)
+constexpr int SUM_MAX = 32;
+struct SumArgs {
+    const uint64_t* in[SUM_MAX];
+    uint64_t* out;
+    const PcbPrimeConst* pr;
+    uint64_t ct_stride, part_stride;  // words
+    int32_t n, nrows, K;
+};
+template <int LOGN> int sum_launch(const SumArgs*, cudaStream_t);
 template <int LOGN, int OP> int ew_launch(const PcbEwArgs*, cudaStream_t);
 template <int LOGN> int tensor_launch(const PcbTensorArgs*, cudaStream_t);
 template <int LOGN> int md_epilogue_launch(const PcbMdEpiArgs*, cudaStream_t);

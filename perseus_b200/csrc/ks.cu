@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
 // M / t taken as fl(M fl(1 / t)); sources enter as canonical doubles (|y M / t| < 2^49, so every product lies in
 // [-0.625t, 0.625t]); the sum is reduced every 4 sources and made canonical once. The conversion matrix sits in shared
 // memory as {M, M / t} pairs. Exact (HPS) jobs take their correction through the integer Barrett step.
+constexpr int BCONV_F_SPAN = 4;  // 128-coefficient spans per CTA: the shared tables are built once for all of them
 template <int LOGN, int NS>
 __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
     constexpr int S = NS > 0 ? NS : MAX_SRC;
@@ -179,7 +180,8 @@ __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
         sM[e] = make_double2(w, __dmul_rn(w, pt.y));
     }
     __syncthreads();
-    const size_t k = (size_t)blockIdx.x * BX + threadIdx.x;
+    for (int rep = 0; rep < BCONV_F_SPAN; ++rep) {
+    const size_t k = ((size_t)blockIdx.x * BCONV_F_SPAN + rep) * BX + threadIdx.x;
     const uint64_t* src = (const uint64_t*)a.src + ((size_t)j.src_off << LOGN) + k;
     uint64_t* dst = (uint64_t*)a.dst + ((size_t)j.dst_off << LOGN) + k;
     uint64_t y[S];
@@ -227,6 +229,7 @@ __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
         }
         dst[(size_t)sRow[t] << LOGN] = r;
     }
+    }
 }
 
 template <int LOGN>
@@ -260,7 +263,7 @@ int bconv_run(const PcbBconvArgs* ap, bool narrow, bool f64, int ns_all, cudaStr
         return PCB_BAD_ARGS;
     if (a.njobs == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.njobs);
-    if (f64) bconv_dispatch_f<LOGN>(a, ns_all, g, s);
+    if (f64) bconv_dispatch_f<LOGN>(a, ns_all, dim3((1 << LOGN) / (BX * BCONV_F_SPAN), a.njobs), s);
     else if (narrow) bconv_dispatch<LOGN, true>(a, ns_all, g, s);
     else bconv_dispatch<LOGN, false>(a, ns_all, g, s);
     return PCB_LAUNCH_RESULT();
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
     }
     const uint32_t k = a.autok[0];
     const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
-#pragma unroll 2
+#pragma unroll 4
     for (int c = 0; c < a.K; ++c) {
         double s0 = 0.0, s1 = 0.0;
 #pragma unroll

@@ -236,6 +236,15 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     }
 }
 
+// A forward epilogue word (args.cuh:82-87) of the transformed word o, the summed source xs and the previous output d:
+// 1: (xs - o) s, 2: d + (xs - o) s, 3: xs s + o
+__device__ __forceinline__ uint64_t epi_word(int epi, uint64_t xs, uint64_t o, uint64_t d, uint64_t sc, uint64_t scs,
+                                             uint64_t p) {
+    if (epi == 1) return shoup(sub_mod(xs, o, p), sc, scs, p);
+    if (epi == 2) return add_mod(d, shoup(sub_mod(xs, o, p), sc, scs, p), p);
+    return add_mod(shoup(xs, sc, scs, p), o, p);
+}
+
 // Row pass: the last 8 stages over 256-word blocks, 16 blocks per CTA, 16 threads per block; thread u holds words
 // u + 16 k (round 1) then 16 u + k (round 2, 16 consecutive words: vector stores and the epilogue)
 template <int LOGN, bool F>
@@ -302,21 +311,23 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
         return;
     }
     // forward epilogues (args.cuh:82-87): x = sum of xnum rows of ex, s = es[prime id]
+    // 16-byte accesses: the launcher checks that ex, eout, ed and the row strides keep 16-byte alignment
     const size_t r = ((size_t)a.roff[i] << LOGN) + w0;
     const uint64_t sc = ((const uint64_t*)a.es)[ri.pid], scs = ((const uint64_t*)a.ess)[ri.pid];
-    const uint64_t* ex = (const uint64_t*)a.ex + r;
-    uint64_t* eo = (uint64_t*)a.eout + r;
-    const uint64_t* ed = a.ed ? (const uint64_t*)a.ed + r : eo;
+    const ulonglong2* ex = (const ulonglong2*)((const uint64_t*)a.ex + r);
+    ulonglong2* eo = (ulonglong2*)((uint64_t*)a.eout + r);
+    const ulonglong2* ed = a.ed ? (const ulonglong2*)((const uint64_t*)a.ed + r) : eo;
+    const size_t xs2 = a.xstride / 2;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        uint64_t xs = ex[k];
-        for (int j = 1; j < a.xnum; ++j) xs = add_mod(xs, ex[k + (size_t)j * a.xstride], p);
-        const uint64_t o = bits(x[k]);
-        uint64_t y;
-        if (a.epi == 1) y = shoup(sub_mod(xs, o, p), sc, scs, p);
-        else if (a.epi == 2) y = add_mod(ed[k], shoup(sub_mod(xs, o, p), sc, scs, p), p);
-        else y = add_mod(shoup(xs, sc, scs, p), o, p);
-        eo[k] = y;
+    for (int k = 0; k < 8; ++k) {
+        ulonglong2 xs = ex[k];
+        for (int j = 1; j < a.xnum; ++j) {
+            const ulonglong2 t = ex[k + (size_t)j * xs2];
+            xs = make_ulonglong2(add_mod(xs.x, t.x, p), add_mod(xs.y, t.y, p));
+        }
+        const ulonglong2 d = a.epi == 2 ? ed[k] : make_ulonglong2(0, 0);
+        eo[k] = make_ulonglong2(epi_word(a.epi, xs.x, bits(x[2 * k]), d.x, sc, scs, p),
+                                epi_word(a.epi, xs.y, bits(x[2 * k + 1]), d.y, sc, scs, p));
     }
 }
 
@@ -473,6 +484,9 @@ __host__ int chunk_rows(const PcbNttArgs& a) {
     return per < 1 ? 1 : per;
 }
 
+// The row passes move 16 bytes at a time: rows (and the epilogue's rows) must start on 16-byte boundaries
+__host__ inline bool misaligned(const void* p) { return ((uintptr_t)p & 15) != 0; }
+
 template <int LOGN>
 int fwd_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
@@ -480,6 +494,9 @@ int fwd_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (a.nrows < 0 || a.epi < 0 || a.epi > 3 || !a.base || !a.roff || !a.rprime || !a.fw || !a.fws || !a.pr)
         return PCB_BAD_ARGS;
     if (a.epi != 0 && (!a.eout || !a.ex || !a.es || !a.ess)) return PCB_BAD_ARGS;
+    if (misaligned(a.base) || (a.epi != 0 && (misaligned(a.eout) || misaligned(a.ex) || misaligned(a.ed) ||
+                                              (a.xnum > 1 && (a.xstride & 1)))))
+        return PCB_BAD_ARGS;
     if (a.soff && (!a.src || a.snum < 1)) return PCB_BAD_ARGS;
     if (a.nrows == 0) return 0;
     constexpr int A = LOGN - 8, COLS = 256 / (1 << (A / 2));
@@ -502,6 +519,7 @@ int inv_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbNttArgs a = *ap;
     if (a.nrows < 0 || a.epi != 0 || !a.base || !a.roff || !a.rprime || !a.iw || !a.iws || !a.pr) return PCB_BAD_ARGS;
+    if (misaligned(a.base)) return PCB_BAD_ARGS;
     if (!a.es && (!a.ninv || !a.ninvs)) return PCB_BAD_ARGS;
     if (a.es && !a.ess) return PCB_BAD_ARGS;
     if (a.soff && (!a.src || a.snum < 1)) return PCB_BAD_ARGS;

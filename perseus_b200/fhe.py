@@ -254,6 +254,16 @@ class Session:
         L.check(L.lib().pcb_sub(self.ctx, a.ptr(), b.ptr(), out.ptr(), a.top, a.k, self._stream()), "pcb_sub")
         return out
 
+    def sum(self, cts, out=None):
+        """Sum of up to 32 ciphertext batches of one level in one pass (each input read once)."""
+        cts = list(cts)
+        for x in cts[1:]:
+            self._same(cts[0], x)
+        out = out if out is not None else self.ct_like(cts[0])
+        ptrs = (C.c_void_p * len(cts))(*[x.data.data_ptr() for x in cts])
+        L.check(L.lib().pcb_sum(self.ctx, ptrs, len(cts), out.ptr(), cts[0].top, cts[0].k, self._stream()), "pcb_sum")
+        return out
+
     def inplace_add(self, a, b):
         self._same(a, b)
         L.check(L.lib().pcb_add(self.ctx, a.ptr(), b.ptr(), a.ptr(), a.top, a.k, self._stream()), "pcb_add")

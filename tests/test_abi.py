@@ -53,6 +53,21 @@ def test_null_arguments_refused_without_launch():
     assert t.ntt_fwd(None, None) == -1
 
 
+def test_misaligned_rows_refused_without_launch():
+    """Rows move 16 bytes at a time: a row base off a 16-byte boundary is refused on the host (-1) before any
+    launch. The pointers are fakes that no kernel ever sees: the refusal comes first."""
+    t = L.kernel_table()
+    a = L.NttArgs()
+    a.base, a.roff, a.rprime, a.fw, a.fws, a.iw, a.iws, a.ninv, a.ninvs, a.pr = (0x1008,) + (0x2000,) * 9
+    a.nrows, a.snum, a.xnum = 1, 1, 1
+    assert t.ntt_fwd(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    assert t.ntt_inv(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    e = L.EwArgs()
+    e.out.base, e.a.base, e.b.base, e.pr = 0x1000, 0x1008, 0x1000, 0x2000
+    e.rs.nq, e.K, e.nparts = 1, 1, 1
+    assert t.ew_add(C.cast(C.pointer(e), C.c_void_p), None) == -1
+
+
 def test_ctx_bytes_config2():
     ch = fhe.config2_chain()
     q = (C.c_uint64 * 24)(*ch.q)

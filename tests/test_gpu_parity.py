@@ -316,6 +316,23 @@ def test_batched_ops_equal_single(s1):
 
 
 @pytest.mark.parametrize("which", ["s1", "s2"])
+def test_sum_equals_pairwise_adds(which, request):
+    s, o = request.getfixturevalue(which)
+    rng = np.random.default_rng(8)
+    top = s.top() - 1
+    cts = [s.encrypt(rng.normal(0, 1, 64) / 8, top=top) for _ in range(5)]
+    want = cts[0]
+    for c in cts[1:]:
+        want = s.add(want, c)
+    got = s.sum(cts)
+    assert torch.equal(got.data[:, :, : top + 1], want.data[:, :, : top + 1])
+    inplace = s.sum(cts, out=cts[0])  # the output may be one of the inputs
+    assert torch.equal(inplace.data[:, :, : top + 1], want.data[:, :, : top + 1])
+    with pytest.raises(L.PcbError, match="33 inputs"):
+        s.sum([cts[1]] * 33)
+
+
+@pytest.mark.parametrize("which", ["s1", "s2"])
 def test_hoisted_rotations_equal_plain(which, request):
     # one shared ModUp (crates/pc-gpu/src/rotate.rs:456): every output word for word the plain rotation's
     s, o = request.getfixturevalue(which)

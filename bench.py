@@ -375,21 +375,27 @@ def attention_decode(a, world, rank, barrier, dist):
         cache = caches[0] if mine == 1 else A.HeadBatch(s, caches)
         q = qs[0] if mine == 1 else s.stack(qs)
         coeffs = A.softmax_poly(tokens)
-        for _ in range(max(a.warmup, 3)):
-            A.attend(s, q, cache, coeffs, ch.q)
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(a.steps):
-            A.attend(s, q, cache, coeffs, ch.q)
-        e1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / a.steps], dtype=torch.float64, device="cuda")
+        # eager steps (host dispatch of every op), then the same step replayed as one CUDA graph
+        graph = A.DecodeGraph(s, cache, coeffs, ch.q, q)
+        times = []
+        for run in (lambda: A.attend(s, q, cache, coeffs, ch.q), lambda: graph(q)):
+            for _ in range(max(a.warmup, 3)):
+                run()
+            torch.cuda.synchronize()
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / a.steps)
+        t = torch.tensor(times, dtype=torch.float64, device="cuda")
         if dist and heads > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        out[name] = t.item()
-        del s, caches, qs, cache, q
+        out[name] = t[1].item()
+        out[name + "_eager"] = t[0].item()
+        del s, caches, qs, cache, q, graph
         torch.cuda.empty_cache()
     return out
 

@@ -11,9 +11,11 @@ Layout (d = head_dim, T = token capacity, both powers of two, d T <= slots):
 
 Step (all rotations left; rotate_and_sum(x, s, e) = x + rot(x, s) + ... ladder, python/perseus/impl/poly.py:24-39):
 1. prod = Q * K, rescale; scores = rotate_and_sum(prod, 1, d): slot t d holds s_t = <Q, K_t> / sqrt(d);
-2. P = mask * p(scores), p the degree-7 polynomial standing in for softmax, mask = 1 on slots t d of live tokens:
-   baby-step giant-step p = (c0 + c1 x + c2 x^2 + c3 x^3) + x^4 (c4 + c5 x + c6 x^2 + c7 x^3), the coefficients as
-   masked plaintexts (the mask costs no level), each term's plaintext scale chosen so all terms meet at one scale;
+2. P = mask * p(scores), p the degree-7 polynomial standing in for softmax, mask = 1 on slots t d of the T token
+   blocks (tokens not yet pushed hold zero K and V, so their weights multiply zeros): baby-step giant-step
+   p = (c0 + c1 x + c2 x^2 + c3 x^3) + x^4 (c4 + c5 x + c6 x^2 + c7 x^3), the coefficients as masked plaintexts (the
+   mask costs no level), each term's plaintext scale chosen so all terms meet at one scale; these plaintexts are
+   constants of the layout, encoded on the first step and kept in the cache's plan;
 3. replicate: R = rotate_and_sum(P, -1, d) puts P_t on slots t d .. t d + d - 1;
 4. out = rotate_and_sum(rescale(R * V), d, d T): slot j holds sum_t P_t V[t][j].
 Depth 6: from top L the output lands at top L - 6 (config 1: 8 limbs, decrypted at top 1).
@@ -72,6 +74,7 @@ class KVCache:
         self.k = None
         self.v = None
         self.count = 0
+        self.plan = {}  # the decode step's plaintexts, encoded once (attend)
 
     def _row_ct(self, row, t):
         vec = np.zeros(self.lay.slots)
@@ -110,6 +113,7 @@ class HeadBatch:
             raise ValueError("heads of one batch hold the same number of tokens")
         self.k = ops.stack([c.k for c in caches])
         self.v = ops.stack([c.v for c in caches])
+        self.plan = {}
 
 
 def encrypt_query(ops, q, layout, top, q_top_prime):
@@ -120,10 +124,23 @@ def encrypt_query(ops, q, layout, top, q_top_prime):
     return ops.encrypt(vec, top=top, scale=q_top_prime * 2.0**10, slots=layout.slots)
 
 
-def _mask(layout, n_live):
+def _mask(layout):
+    """Slot 0 of every token block of the cache's capacity. Tokens not yet in the cache hold zero K and V words: their
+    scores are zero and the weights they get multiply zero values, so the mask does not follow the token count and
+    the masked coefficient plaintexts are constants of the layout."""
     m = np.zeros(layout.slots)
-    m[0 : n_live * layout.head_dim : layout.head_dim] = 1.0
+    m[0 : layout.tokens * layout.head_dim : layout.head_dim] = 1.0
     return m
+
+
+def _pt(ops, plan, values, top, scale, slots):
+    """A plaintext of the decode step (mask x polynomial coefficient at a fixed level and scale): encoded on first use
+    and kept in the cache's plan, so later tokens reuse it."""
+    key = (top, float(scale), slots, np.asarray(values, np.float64).tobytes())
+    pt = plan.get(key)
+    if pt is None:
+        pt = plan[key] = ops.pt(values, top, scale, slots)
+    return pt
 
 
 def attend(ops, q_ct, cache, coeffs, primes):
@@ -142,13 +159,13 @@ def attend(ops, q_ct, cache, coeffs, primes):
     x3 = ops.rescale_one(ops.mult(x2, ops.drop_to(x, L1 - 1)))  # L-3
     x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
     lvl = L1 - 2  # the level of x^3 / x^4
-    mask = _mask(lay, cache.count)
+    mask = _mask(lay)
 
     def term(pw, c, target_scale):
         # c * mask * x^pw, landing at level lvl - 1 with scale target_scale (the plaintext scale solves for it)
         src = ops.drop_to(pw, lvl)
         pscale = target_scale * primes[lvl] / src.scale
-        pt = ops.pt(mask * c, lvl, pscale, lay.slots)
+        pt = _pt(ops, cache.plan, mask * c, lvl, pscale, lay.slots)
         return ops.rescale_one(ops.mult_pt(src, pt, pscale))
 
     def inner(cs, target_scale):
@@ -156,7 +173,7 @@ def attend(ops, q_ct, cache, coeffs, primes):
         for i, (pw, c) in enumerate(zip((x, x2, x3), cs[1:])):
             t_ = term(pw, c, target_scale)
             acc = t_ if acc is None else ops.add(acc, t_)
-        pt0 = ops.pt(mask * cs[0], acc.top, acc.scale, lay.slots)
+        pt0 = _pt(ops, cache.plan, mask * cs[0], acc.top, acc.scale, lay.slots)
         return ops.add_pt(acc, pt0)
 
     # p = A + x^4 B: A at level lvl - 2 with scale S; B at lvl - 1 with scale S q_{lvl-1} / scale(x^4)
@@ -174,3 +191,30 @@ def attend(ops, q_ct, cache, coeffs, primes):
     v_ct = ops.drop_to(cache.v, R.top)
     y = ops.rescale_one(ops.mult(R, v_ct))
     return ops.rotate_and_sum(y, d, d * T)
+
+
+class DecodeGraph:
+    """The decode step of one cache as a CUDA graph: the query is copied into a fixed device buffer and the graph
+    replays every kernel of attend, with no host work per token (at N = 2^14 the step is otherwise bound by the
+    hundreds of launches and the host's op dispatch). Session ops only (device buffers from torch); the first,
+    eager step runs at construction and fills the cache's plan, so capture sees no host copies. The returned
+    ciphertext is the graph's output buffer, overwritten by the next call."""
+
+    def __init__(self, ops, cache, coeffs, primes, q_ct):
+        import torch
+
+        self.q = ops.ct_like(q_ct)
+        self.q.data.copy_(q_ct.data)
+        attend(ops, self.q, cache, coeffs, primes)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = attend(ops, self.q, cache, coeffs, primes)
+        torch.cuda.synchronize()
+
+    def __call__(self, q_ct):
+        if q_ct.top != self.q.top or q_ct.scale != self.q.scale or q_ct.data.shape != self.q.data.shape:
+            raise ValueError("the query must have the captured level, scale and batch")
+        self.q.data.copy_(q_ct.data)
+        self.graph.replay()
+        return self.out

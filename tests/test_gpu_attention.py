@@ -50,3 +50,19 @@ def test_attention_decode_bit_exact(pair, push):
     got = s.decrypt_slots(g).real[:64]
     want = A.plain_attention(q, K, V, A.softmax_poly(lay.tokens))
     assert np.abs(got - want).max() < 1e-3
+
+
+def test_decode_graph_replays_eager_step(pair):
+    """The captured decode step gives, token after token, the eager step's ciphertext word for word."""
+    ch, lay, s, oo = pair
+    rng = np.random.default_rng(21)
+    top = len(ch.q) - 1
+    cache = A.KVCache(s, lay, top)
+    cache.load(rng.normal(0, 1, (lay.tokens, 64)) / 8, rng.normal(0, 1, (lay.tokens, 64)) / 8)
+    coeffs = A.softmax_poly(lay.tokens)
+    qs = [A.encrypt_query(s, rng.normal(0, 1, 64) / 8, lay, top, ch.q[top]) for _ in range(3)]
+    g = A.DecodeGraph(s, cache, coeffs, ch.q, qs[0])
+    for q in qs:
+        got = g(q).data.clone()
+        want = A.attend(s, q, cache, coeffs, ch.q)
+        assert torch.equal(got[:, :, : want.top + 1], want.data[:, :, : want.top + 1])

@@ -113,6 +113,8 @@ def cpu_rate(samples):
     from tests import _oracle as O
 
     if not _CPU:
+        # every host thread, whatever OMP_NUM_THREADS a launcher set (torchrun sets 1 per process)
+        O.lib().orc_set_threads(len(os.sched_getaffinity(0)))
         ch = fhe.config2_chain()
         o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
         o.keygen(0, 192, 3.2, [1, fhe.rotation_galois(1, ch.log_n)])

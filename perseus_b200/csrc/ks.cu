@@ -477,7 +477,8 @@ __global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
 
 // FP64 form of dot_all for primes below 2^50: a digit product x b mod p is mul_f with b centred and its quotient
 // b / p taken as fl(b fl(1 / p)) (relative error <= 2^-52: |x b / p| < 2^49, so q is within 0.63 of it and each
-// product lies in [-0.63p, 0.63p]); sums are reduced every 4 digits and made canonical once per output word.
+// product lies in [-0.63p, 0.63p]); sums are reduced every 4 digits and made canonical once per output word. Each
+// thread takes two adjacent words (16-byte loads; the launcher checks the alignment) of every ciphertext.
 template <int LOGN, int ND>
 __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
     constexpr int D = ND > 0 ? ND : 16;
@@ -485,7 +486,7 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
     const uint32_t t = a.rows[blockIdx.y];
     const uint64_t p = a.pr[t].p;
     const double pf = to_f(p), pinv = 1.0 / pf;
-    const uint32_t idx = blockIdx.x * BX + threadIdx.x;
+    const uint32_t idx = 2 * (blockIdx.x * BX + threadIdx.x);  // words idx, idx + 1
     const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
     const size_t roff = ((size_t)t << LOGN) + idx;
     const uint64_t* c1 = (const uint64_t*)a.c1;
@@ -497,37 +498,48 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
     }
     const uint64_t* kb = (const uint64_t*)a.kb[0] + roff;
     const uint64_t* ka = (const uint64_t*)a.ka[0] + roff;
-    double bw[D], bq[D], aw[D], aq[D];
+    double bw[D][2], bq[D][2], aw[D][2], aq[D][2];
 #pragma unroll
     for (int d = 0; d < D; ++d) {
         if (ND > 0 || d < nd) {
-            const uint64_t b = __ldcs(kb + (size_t)d * a.key_digit_stride);
-            const uint64_t av = __ldcs(ka + (size_t)d * a.key_digit_stride);
-            bw[d] = b > p / 2 ? -to_f(p - b) : to_f(b);
-            aw[d] = av > p / 2 ? -to_f(p - av) : to_f(av);
-            bq[d] = __dmul_rn(bw[d], pinv);
-            aq[d] = __dmul_rn(aw[d], pinv);
+            const ulonglong2 b = __ldcs((const ulonglong2*)(kb + (size_t)d * a.key_digit_stride));
+            const ulonglong2 av = __ldcs((const ulonglong2*)(ka + (size_t)d * a.key_digit_stride));
+            const uint64_t bb[2] = {b.x, b.y}, aa[2] = {av.x, av.y};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                bw[d][h] = bb[h] > p / 2 ? -to_f(p - bb[h]) : to_f(bb[h]);
+                aw[d][h] = aa[h] > p / 2 ? -to_f(p - aa[h]) : to_f(aa[h]);
+                bq[d][h] = __dmul_rn(bw[d][h], pinv);
+                aq[d][h] = __dmul_rn(aw[d][h], pinv);
+            }
         }
     }
     const uint32_t k = a.autok[0];
-    const uint32_t o = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
-#pragma unroll 4
+    const uint32_t o0 = k == 1 ? idx : automorph_slot<LOGN>(k, idx);
+    const uint32_t o1 = k == 1 ? idx + 1 : automorph_slot<LOGN>(k, idx + 1);
+#pragma unroll 2
     for (int c = 0; c < a.K; ++c) {
-        double s0 = 0.0, s1 = 0.0;
+        double s0[2] = {0.0, 0.0}, s1[2] = {0.0, 0.0};
 #pragma unroll
         for (int d = 0; d < D; ++d) {
             if (ND > 0 || d < nd) {
-                const double x = to_f(d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + roff)
-                                              : __ldg(mu + (size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff));
-                s0 = __dadd_rn(s0, mul_f(x, bw[d], bq[d], pf));
-                s1 = __dadd_rn(s1, mul_f(x, aw[d], aq[d], pf));
-                if ((d & 3) == 3) {
-                    s0 = red_f(s0, pf, pinv);
-                    s1 = red_f(s1, pf, pinv);
+                const ulonglong2 w = __ldg((const ulonglong2*)(d == dt ? c1 + (size_t)c * a.ct_stride + roff
+                                                                        : mu + (size_t)c * a.mu_ct_stride +
+                                                                              (size_t)d * a.mu_digit_stride + roff));
+                const double x[2] = {to_f(w.x), to_f(w.y)};
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    s0[h] = __dadd_rn(s0[h], mul_f(x[h], bw[d][h], bq[d][h], pf));
+                    s1[h] = __dadd_rn(s1[h], mul_f(x[h], aw[d][h], aq[d][h], pf));
+                    if ((d & 3) == 3) {
+                        s0[h] = red_f(s0[h], pf, pinv);
+                        s1[h] = red_f(s1[h], pf, pinv);
+                    }
                 }
             }
         }
-        ks_store<LOGN>(a, c, 0, t, roff, o, canon_f(s0, pf, pinv), canon_f(s1, pf, pinv), p, pm, pms);
+        ks_store<LOGN>(a, c, 0, t, roff, o0, canon_f(s0[0], pf, pinv), canon_f(s1[0], pf, pinv), p, pm, pms);
+        ks_store<LOGN>(a, c, 0, t, roff + 1, o1, canon_f(s0[1], pf, pinv), canon_f(s1[1], pf, pinv), p, pm, pms);
     }
 }
 
@@ -567,9 +579,18 @@ int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
     if (a.K == 0 || a.nrows == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.nrows);
-    if (f64) dot_dispatch_f<LOGN>(a, g, s);
-    else if (narrow) dot_dispatch<LOGN, true>(a, g, s);
-    else dot_dispatch<LOGN, false>(a, g, s);
+    if (f64) {  // two words per thread, 16-byte loads: row bases 16-byte aligned, strides even
+        // (kb / ka are device arrays of key pointers, not readable here: the evaluator's keys are arena rows,
+        // 256-byte aligned)
+        const bool odd = (a.ct_stride | a.mu_ct_stride | a.mu_digit_stride | a.key_digit_stride) & 1;
+        const uintptr_t bases = (uintptr_t)a.c1 | (uintptr_t)a.modup;
+        if (odd || (bases & 15)) return PCB_BAD_ARGS;
+        dot_dispatch_f<LOGN>(a, dim3((1 << LOGN) / (2 * BX), a.nrows), s);
+    } else if (narrow) {
+        dot_dispatch<LOGN, true>(a, g, s);
+    } else {
+        dot_dispatch<LOGN, false>(a, g, s);
+    }
     return PCB_LAUNCH_RESULT();
 }
 

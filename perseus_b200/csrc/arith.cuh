@@ -133,6 +133,29 @@ __device__ __forceinline__ uint64_t* at_row_w(const PcbPolyRef& r, int c, int pa
 }
 __device__ __forceinline__ int rs_row(const PcbRowSet& rs, int y) { return y < rs.nq ? y : rs.qmax + (y - rs.nq); }
 
+// Programmatic dependent launch: a kernel may start while the previous kernel of its stream is finishing; it stages
+// constant tables (twiddles, conversion matrices, keys: written when the context was built), then waits for the
+// previous kernel's writes before it reads anything that kernel may have produced. Every CTA allows the next kernel to
+// launch as soon as it has passed its wait; that takes effect once the whole grid has (its last wave), so the next
+// kernel's CTAs fill SMs as this one's finish.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialization: the kernel must call pdl_wait before its dependent reads
+template <typename... KArgs, typename... Args>
+__host__ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // process-wide count of kernels this library launched (pcb_launch_count)
 void note_launches(unsigned n);
 

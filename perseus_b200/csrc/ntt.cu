@@ -144,13 +144,6 @@ __device__ __forceinline__ void canon(double& x, const FpMod& m) {
 __device__ __forceinline__ uint64_t bits(uint64_t x) { return x; }
 __device__ __forceinline__ uint64_t bits(double x) { return (uint64_t)__double_as_longlong(x); }
 
-// Programmatic dependent launch: a pass may start while the previous kernel of the stream is finishing; it stages
-// its constant tables (twiddles, written when the context was built), then waits for the previous kernel's writes
-// before it reads any row. Every CTA allows the next pass to launch as soon as it starts, which takes effect once the
-// whole grid has started (its last wave), so the next pass's CTAs fill SMs as this one's finish.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // Shared-memory exchange of a 256-word block: one pad word after every 16, so both the strided (u + 16 k) and the
 // contiguous (16 u + k) views of a half-warp hit 16 distinct 8-byte bank pairs.
 constexpr int BLKPAD = 256 + 16;
@@ -529,27 +522,13 @@ __host__ inline bool misaligned(const void* p) { return ((uintptr_t)p & 15) != 0
 template <int LOGN, bool F>
 __host__ void launch_rows(const PcbNttArgs& a, dim3 grid, cudaStream_t s, int r0);
 
-// Launch with programmatic stream serialization (the kernel waits on its predecessor itself: pdl_wait)
-__host__ void launch_pdl(void (*kern)(PcbNttArgs, int), dim3 grid, cudaStream_t s, const PcbNttArgs& a, int r0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(THREADS);
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kern, a, r0);
-}
-
 template <int LOGN, bool F>
 __host__ void launch_rows(const PcbNttArgs& a, dim3 grid, cudaStream_t s, int r0) {
     switch (a.epi) {
-        case 0: launch_pdl(fwd_rows<LOGN, F, 0>, grid, s, a, r0); break;
-        case 1: launch_pdl(fwd_rows<LOGN, F, 1>, grid, s, a, r0); break;
-        case 2: launch_pdl(fwd_rows<LOGN, F, 2>, grid, s, a, r0); break;
-        default: launch_pdl(fwd_rows<LOGN, F, 3>, grid, s, a, r0);
+        case 0: launch_pdl(fwd_rows<LOGN, F, 0>, grid, dim3(THREADS), s, a, r0); break;
+        case 1: launch_pdl(fwd_rows<LOGN, F, 1>, grid, dim3(THREADS), s, a, r0); break;
+        case 2: launch_pdl(fwd_rows<LOGN, F, 2>, grid, dim3(THREADS), s, a, r0); break;
+        default: launch_pdl(fwd_rows<LOGN, F, 3>, grid, dim3(THREADS), s, a, r0);
     }
 }
 
@@ -570,10 +549,10 @@ int fwd_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     for (int r0 = 0; r0 < a.nrows; r0 += ch) {
         const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
         if (f64) {
-            launch_pdl(fwd_cols<LOGN, true>, dim3(256 / COLS, n), s, a, r0);
+            launch_pdl(fwd_cols<LOGN, true>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
             launch_rows<LOGN, true>(a, dim3((1 << A) / 16, n), s, r0);
         } else {
-            launch_pdl(fwd_cols<LOGN, false>, dim3(256 / COLS, n), s, a, r0);
+            launch_pdl(fwd_cols<LOGN, false>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
             launch_rows<LOGN, false>(a, dim3((1 << A) / 16, n), s, r0);
         }
     }
@@ -595,11 +574,11 @@ int inv_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     for (int r0 = 0; r0 < a.nrows; r0 += ch) {
         const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
         if (f64) {
-            launch_pdl(inv_rows<LOGN, true>, dim3((1 << A) / 16, n), s, a, r0);
-            launch_pdl(inv_cols<LOGN, true>, dim3(256 / COLS, n), s, a, r0);
+            launch_pdl(inv_rows<LOGN, true>, dim3((1 << A) / 16, n), dim3(THREADS), s, a, r0);
+            launch_pdl(inv_cols<LOGN, true>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
         } else {
-            launch_pdl(inv_rows<LOGN, false>, dim3((1 << A) / 16, n), s, a, r0);
-            launch_pdl(inv_cols<LOGN, false>, dim3(256 / COLS, n), s, a, r0);
+            launch_pdl(inv_rows<LOGN, false>, dim3((1 << A) / 16, n), dim3(THREADS), s, a, r0);
+            launch_pdl(inv_cols<LOGN, false>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
         }
     }
     return PCB_LAUNCHED(2u * (unsigned)((a.nrows + ch - 1) / ch));

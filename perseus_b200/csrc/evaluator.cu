@@ -121,6 +121,7 @@ struct PcbCtx {
     std::vector<LevelPlan> lv;
     // workspaces
     uint64_t *coef = nullptr, *digits = nullptr, *ext = nullptr, *conv = nullptr, *dbuf = nullptr, *row = nullptr;
+    int ext_groups = 1;  // extended-output batches in c.ext (keys of one grouped inner product)
     // keys and session
     std::vector<KeySlot> keys;
     int nkeys_made = 0;
@@ -513,7 +514,9 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
     // workspaces: coefficients [k][rows], ModUp digits [k][dnum][rows], extended / conversion / d2 in ct layout
     c.coef = A.take<uint64_t>((size_t)km * rows * n);
     c.digits = A.take<uint64_t>((size_t)km * c.dnum * rows * n);
-    c.ext = A.take<uint64_t>((size_t)km * c.ct_words());
+    // extended outputs: one batch per key of a hoisted group (FP64 chains group up to KEYS_MAX keys), else one
+    c.ext_groups = c.f64 ? ks::KEYS_MAX : 1;
+    c.ext = A.take<uint64_t>((size_t)c.ext_groups * km * c.ct_words());
     c.conv = A.take<uint64_t>((size_t)km * c.ct_words());
     c.dbuf = A.take<uint64_t>((size_t)km * c.ct_words());
     c.row = A.take<uint64_t>(n);
@@ -651,16 +654,60 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
     return 0;
 }
 
-// ModDown of c.ext (K cts) into out: epi 1 (out = (x - conv) P^-1) or 2 (out += ...)
-int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStream_t s) {
+// Key inner products of K cts against up to KEYS_MAX keys at once (FP64 chains): key r's extended outputs go to
+// the r-th batch of c.ext; the ModUp digits are read once for the whole group
+int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, const uint64_t* c0, int c0_mode,
+              int top, int K, cudaStream_t s) {
     const LevelPlan& l = c.lv[top];
-    PcbNttArgs a = ntt_args(c, c.ext, l.md_intt_roff, l.md_intt_rprime, K * 2 * c.kp);
+    const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
+    PcbKsArgs a;
+    memset(&a, 0, sizeof a);
+    a.c1 = c1;
+    a.modup = c.digits;
+    a.c0 = c0;
+    a.out0 = c.ext;
+    a.out1 = c.ext + rn;
+    a.rows = l.ks_rows;
+    a.digit_of = c.digit_of;
+    a.pmod = c.pmod;
+    a.pmods = c.pmods;
+    a.pr = c.pr;
+    a.ct_stride = cw;
+    a.mu_ct_stride = (uint64_t)c.dnum * rn;
+    a.mu_digit_stride = rn;
+    a.out_ct_stride = cw;
+    a.out_rot_stride = (uint64_t)c.k_max * cw;
+    a.key_digit_stride = rn;
+    a.K = K;
+    a.R = n;
+    a.ndig = l.ndig;
+    a.c0_mode = c0_mode;
+    a.nq = c.nq;
+    a.nrows = top + 1 + c.kp;
+    ks::KeyGroup kg;
+    memset(&kg, 0, sizeof kg);
+    kg.n = n;
+    for (int r = 0; r < n; ++r) {
+        kg.kb[r] = keys[r]->b;
+        kg.ka[r] = keys[r]->a;
+        kg.autok[r] = (uint32_t)keys[r]->autok;
+    }
+    CK(c.logn == 14 ? ks::dot_keys_run<14>(&a, kg, s) : ks::dot_keys_run<16>(&a, kg, s));
+    return 0;
+}
+
+// ModDown of the K cts of one extended-output batch (c.ext by default) into out: epi 1 (out = (x - conv) P^-1) or
+// 2 (out += ...)
+int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStream_t s, uint64_t* ext = nullptr) {
+    if (!ext) ext = c.ext;
+    const LevelPlan& l = c.lv[top];
+    PcbNttArgs a = ntt_args(c, ext, l.md_intt_roff, l.md_intt_rprime, K * 2 * c.kp);
     a.es = l.md_es;
     a.ess = l.md_ess;
     CK(ntt_inv(c, &a, s));
     PcbBconvArgs b;
     memset(&b, 0, sizeof b);
-    b.src = c.ext;
+    b.src = ext;
     b.dst = c.conv;
     b.jobs = l.md_jobs;
     b.pool = l.md_pool;
@@ -671,7 +718,7 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
     f.epi = accumulate ? 2 : 1;
     f.eout = out;
-    f.ex = c.ext;
+    f.ex = ext;
     f.es = c.pinv;
     f.ess = c.pinvs;
     CK(ntt_fwd(c, &f, s));
@@ -1188,7 +1235,24 @@ int pcb_rotate_hoisted(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32
         rc = modup(*c, c1, top, K, s);
         if (rc) return rc;
     }
+    if (c->ext_groups > 1) {  // FP64 chains: the steps' inner products in groups sharing one read of the digits
+        std::vector<int> todo;
+        for (int i = 0; i < nsteps; ++i)
+            if (keys[i]) todo.push_back(i);
+        for (size_t g0 = 0; g0 < todo.size(); g0 += c->ext_groups) {
+            const int n = (int)std::min(todo.size() - g0, (size_t)c->ext_groups);
+            const KeySlot* grp[ks::KEYS_MAX];
+            for (int r = 0; r < n; ++r) grp[r] = keys[todo[g0 + r]];
+            rc = dot_group(*c, grp, n, c1, x, 1, top, K, s);
+            if (rc) return rc;
+            for (int r = 0; r < n; ++r) {
+                rc = moddown(*c, outs[todo[g0 + r]], false, top, K, s, c->ext + (size_t)r * c->k_max * c->ct_words());
+                if (rc) return rc;
+            }
+        }
+    }
     for (int i = 0; i < nsteps; ++i) {
+        if (keys[i] && c->ext_groups > 1) continue;
         if (!keys[i]) {
             PcbEwArgs e;
             memset(&e, 0, sizeof e);

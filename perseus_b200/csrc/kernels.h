@@ -37,6 +37,16 @@ template <int LOGN> int ks_dot_launch(const PcbKsArgs*, cudaStream_t);
 // f64: every prime of the launch below 2^50 (FP64 products)
 template <int LOGN> int bconv_run(const PcbBconvArgs*, bool narrow, bool f64, int ns_all, cudaStream_t);
 template <int LOGN> int ks_dot_run(const PcbKsArgs*, bool narrow, cudaStream_t);
+// Up to KEYS_MAX keys against the same inputs in one launch (hoisted rotations): key pointers and automorphism
+// indices by value; key r's outputs go to out0 / out1 + r out_rot_stride. FP64 form (every prime below 2^50).
+constexpr int KEYS_MAX = 4;
+struct KeyGroup {
+    const uint64_t* kb[KEYS_MAX];
+    const uint64_t* ka[KEYS_MAX];
+    uint32_t autok[KEYS_MAX];
+    int32_t n;
+};
+template <int LOGN> int dot_keys_run(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
 // one key, any batch K: key words read once per launch; inputs must not alias outputs
 // f64: every prime below 2^50 (FP64 products)
 template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, cudaStream_t);

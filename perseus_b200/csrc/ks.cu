@@ -11,6 +11,7 @@
 // The conversion matrix of a job and its target primes' Barrett constants sit in shared memory; source words stay in
 // registers across all targets.
 #include "arith.cuh"
+#include "kernels.h"
 
 namespace pcb {
 namespace ks {
@@ -543,6 +544,93 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
     }
 }
 
+// Several keys against the same ModUp digits (the steps of a hoisted rotation): each digit word is read once and
+// multiplied by every key of the group, so the digits stream once per group instead of once per key. One word per
+// thread; the keys stay in registers as centred doubles (their quotients by p are formed per use, as in dot_all_f).
+template <int LOGN, int ND, int RK>
+__global__ void __launch_bounds__(BX) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
+    const uint32_t t = a.rows[blockIdx.y];
+    const uint64_t p = a.pr[t].p;
+    const double pf = to_f(p), pinv = 1.0 / pf;
+    const uint32_t idx = blockIdx.x * BX + threadIdx.x;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t roff = ((size_t)t << LOGN) + idx;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    uint64_t pm = 0, pms = 0;
+    if ((a.c0_mode & 3) == 1 && (int)t < a.nq) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    double bw[RK][ND], aw[RK][ND];
+    uint32_t o[RK];
+#pragma unroll
+    for (int r = 0; r < RK; ++r) {
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            const uint64_t b = __ldcs(kg.kb[r] + roff + (size_t)d * a.key_digit_stride);
+            const uint64_t av = __ldcs(kg.ka[r] + roff + (size_t)d * a.key_digit_stride);
+            bw[r][d] = b > p / 2 ? -to_f(p - b) : to_f(b);
+            aw[r][d] = av > p / 2 ? -to_f(p - av) : to_f(av);
+        }
+        o[r] = kg.autok[r] == 1 ? idx : automorph_slot<LOGN>(kg.autok[r], idx);
+    }
+    for (int c = 0; c < a.K; ++c) {
+        double x[ND];
+#pragma unroll
+        for (int d = 0; d < ND; ++d)
+            x[d] = to_f(d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + roff)
+                                : __ldg(mu + (size_t)c * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + roff));
+#pragma unroll
+        for (int r = 0; r < RK; ++r) {
+            double s0 = 0.0, s1 = 0.0;
+#pragma unroll
+            for (int d = 0; d < ND; ++d) {
+                s0 = __dadd_rn(s0, mul_f(x[d], bw[r][d], __dmul_rn(bw[r][d], pinv), pf));
+                s1 = __dadd_rn(s1, mul_f(x[d], aw[r][d], __dmul_rn(aw[r][d], pinv), pf));
+                if ((d & 3) == 3 && d + 1 < ND) {
+                    s0 = red_f(s0, pf, pinv);
+                    s1 = red_f(s1, pf, pinv);
+                }
+            }
+            ks_store<LOGN>(a, c, r, t, roff, o[r], canon_f(s0, pf, pinv), canon_f(s1, pf, pinv), p, pm, pms);
+        }
+    }
+}
+
+template <int LOGN, int ND>
+void dot_keys_dispatch(const PcbKsArgs& a, const KeyGroup& kg, dim3 g, cudaStream_t s) {
+    switch (kg.n) {
+        case 1: dot_keys_f<LOGN, ND, 1><<<g, BX, 0, s>>>(a, kg); break;
+        case 2: dot_keys_f<LOGN, ND, 2><<<g, BX, 0, s>>>(a, kg); break;
+        case 3: dot_keys_f<LOGN, ND, 3><<<g, BX, 0, s>>>(a, kg); break;
+        default: dot_keys_f<LOGN, ND, 4><<<g, BX, 0, s>>>(a, kg);
+    }
+}
+
+template <int LOGN>
+int dot_keys_run(const PcbKsArgs* ap, const KeyGroup& kg, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbKsArgs& a = *ap;
+    if (kg.n < 1 || kg.n > KEYS_MAX || a.K < 0 || a.ndig < 1 || a.ndig > 4 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
+        (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.rows || !a.digit_of || !a.pr)
+        return PCB_BAD_ARGS;
+    for (int r = 0; r < kg.n; ++r)
+        if (!kg.kb[r] || !kg.ka[r] || !(kg.autok[r] & 1)) return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
+    if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
+    if (a.K == 0 || a.nrows == 0) return 0;
+    const dim3 g((1 << LOGN) / BX, a.nrows);
+    switch (a.ndig) {
+        case 1: dot_keys_dispatch<LOGN, 1>(a, kg, g, s); break;
+        case 2: dot_keys_dispatch<LOGN, 2>(a, kg, g, s); break;
+        case 3: dot_keys_dispatch<LOGN, 3>(a, kg, g, s); break;
+        default: dot_keys_dispatch<LOGN, 4>(a, kg, g, s);
+    }
+    return PCB_LAUNCH_RESULT();
+}
+
 template <int LOGN, bool NARROW>
 void dot_dispatch(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
     switch (a.ndig) {
@@ -596,6 +684,8 @@ int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
     return PCB_LAUNCH_RESULT();
 }
 
+template int dot_keys_run<14>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
+template int dot_keys_run<16>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
 template int dot_all_run<14>(const PcbKsArgs*, bool, bool, cudaStream_t);
 template int dot_all_run<16>(const PcbKsArgs*, bool, bool, cudaStream_t);
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);

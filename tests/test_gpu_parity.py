@@ -336,10 +336,13 @@ def test_sum_equals_pairwise_adds(which, request):
 def test_hoisted_rotations_equal_plain(which, request):
     # one shared ModUp (crates/pc-gpu/src/rotate.rs:456): every output word for word the plain rotation's
     s, o = request.getfixturevalue(which)
-    steps = [1, 4, 0, -1] if which == "s1" else [5, 1, 1 << 15]
+    # config 2 (FP64 chain) takes its inner products in groups of up to 4 keys: 6 keyed steps make groups of 4 and 2
+    steps = [1, 4, 0, -1] if which == "s1" else [5, 1, 1 << 15, 1, 5, 5, 1]
     rng = np.random.default_rng(8)
     top = s.top() - 1
     a = s.encrypt(rng.normal(0, 1, 256) / 8, top=top)
+    if which == "s2":
+        a = s.stack([a, s.encrypt(rng.normal(0, 1, 256) / 8, top=top)])  # a batch of two
     outs = s.rotate_hoisted(a, steps)
     for st, h in zip(steps, outs):
         p = s.rotate(a, st) if st % (s.n // 2) else a

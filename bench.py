@@ -365,7 +365,7 @@ def attention_decode(a, world, rank, barrier, dist):
                                     ("config3_12heads_N2^16_128tok", fhe.config2_chain(), 128, 12)):
         # config 1 runs on every rank (rank 0 reports it); config 3's heads are split, at most one apart
         mine = heads if heads == 1 else len(shard.head_range(heads, world, rank))
-        lay = A.Layout(64, tokens, ch.n // 2)
+        lay = A.Layout(64, tokens, ch.n // 2, radix_bits=3)  # radix-3 ladders (rotate_sum groups)
         s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=mine, seed=0)
         top = len(ch.q) - 1
         caches, qs = [], []

@@ -396,6 +396,14 @@ int pcb_rotate_hoisted(PcbCtx* ctx, const uint64_t* x, const int64_t* steps, int
 /* out = x + rot(x, g) ladder over gaps start, 2 start, .. < stop (crates/pc-gpu/src/rotate.rs:924-992) */
 int pcb_rotate_and_sum(PcbCtx* ctx, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int32_t top,
                        int32_t K, cudaStream_t stream);
+/* out = x + sum_k rot(x, steps[k]), the rotations summed in the extended basis with one ModDown (crates/pc-gpu/src/
+ * rotate.rs:690-775 rotate_sum); out may be x; steps of Galois element 1 are refused. */
+int pcb_rotate_sum(PcbCtx* ctx, const uint64_t* x, const int64_t* steps, int32_t nsteps, uint64_t* out, int32_t top,
+                   int32_t K, cudaStream_t stream);
+/* rotate_and_sum with radix groups (crates/pc-gpu/src/rotate.rs:924-992, radix_bits >= 2): groups of gaps whose
+ * steps all have keys run as one pcb_rotate_sum, the rest rung by rung; radix_bits < 2 is pcb_rotate_and_sum. */
+int pcb_rotate_and_sum_radix(PcbCtx* ctx, const uint64_t* x, int64_t start, int64_t stop, int32_t radix_bits,
+                             uint64_t* out, int32_t top, int32_t K, cudaStream_t stream);
 /* out = x * pt (pt: device evaluation rows [nq][N] from pcb_pt_load); out = x + pt on part 0 */
 int pcb_mult_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
                 cudaStream_t stream);

@@ -1095,6 +1095,81 @@ int orc_rotate_and_sum(void* cv, const uint64_t* x, int64_t start, int64_t stop,
     memcpy(out, cur.data(), cw * 8);
     return 0;
 }
+// crates/pc-gpu/src/rotate.rs:690-775 (rotate_sum_core, the sum formed in the ModDown): out = x + sum_k rot(x, s_k)
+// with every rotation's extended ciphertext (ModUp of c1, the key dot with P sigma(c0) added, output at the
+// automorphism slot) summed in the extended basis and one ModDown, whose result is added to x. A step of Galois
+// element 1 is refused, as the reference refuses step 0 in a group.
+int orc_rotate_sum(void* cv, const uint64_t* x, const int64_t* steps, int nsteps, uint64_t* out, int top) {
+    Ctx& c = *(Ctx*)cv;
+    if (nsteps < 1) return -1;
+    const size_t n = c.n, cw = c.ct_words();
+    const int rows = c.rows();
+    std::vector<uint64_t> sum(cw, 0), ext(cw), md(cw);
+    for (int k = 0; k < nsteps; ++k) {
+        const int64_t h = (int64_t)n / 2;
+        const uint64_t g = powmod(5, (uint64_t)(((steps[k] % h) + h) % h), 2 * n);
+        if (g == 1) return -1;
+        const Key* key = c.key_of(g);
+        if (!key) return -3;
+        const uint64_t ginv = powmod(g, (2 * n >> 2) - 1, 2 * n);
+        keyswitch_ext(c, x + (size_t)rows * n, x, 1, *key, (uint32_t)ginv, ext.data(), top);
+        for (int part = 0; part < 2; ++part)
+            for (int t = 0; t < rows; ++t) {
+                if (t > top && t < c.nq) continue;
+                const uint64_t p = c.primes[t];
+                const size_t o = ((size_t)part * rows + t) * n;
+                for (size_t j = 0; j < n; ++j) sum[o + j] = addmod(sum[o + j], ext[o + j], p);
+            }
+    }
+    moddown(c, sum.data(), md.data(), top);
+    for (int part = 0; part < 2; ++part)
+        for (int t = 0; t <= top; ++t) {
+            const uint64_t p = c.primes[t];
+            const size_t o = ((size_t)part * rows + t) * n;
+            for (size_t j = 0; j < n; ++j) out[o + j] = addmod(x[o + j], md[o + j], p);
+        }
+    return 0;
+}
+
+// crates/pc-gpu/src/rotate.rs:924-992 with radix_bits >= 2: the gaps |start|, 2|start|, .. below stop taken n =
+// min(radix_bits, left) at a time; a group of n > 1 gaps whose steps j g (j = 1 .. 2^n - 1) all have keys is one
+// rotate_sum in place (out = out + sum rot(out, j g)), anything else rung by rung (out += rot(out, g))
+int orc_rotate_and_sum_radix(void* cv, const uint64_t* x, int64_t start, int64_t stop, int radix_bits, uint64_t* out,
+                             int top) {
+    Ctx& c = *(Ctx*)cv;
+    if (start == 0 || stop <= 0) return -1;
+    const size_t n = c.n, cw = c.ct_words();
+    std::vector<uint64_t> cur(x, x + cw), tmp(cw);
+    const int64_t sign = start < 0 ? -1 : 1;
+    std::vector<int64_t> gaps;
+    for (int64_t g = start < 0 ? -start : start; g < stop; g *= 2) gaps.push_back(g);
+    const size_t rb = radix_bits >= 2 ? (size_t)radix_bits : 1;
+    for (size_t i0 = 0; i0 < gaps.size();) {
+        const size_t m = std::min(rb, gaps.size() - i0);
+        std::vector<int64_t> steps;
+        bool keyed = radix_bits >= 2 && m > 1;
+        for (int64_t j = 1; keyed && j < ((int64_t)1 << m); ++j) {
+            const int64_t st = sign * j * gaps[i0], h = (int64_t)n / 2;
+            const uint64_t g = powmod(5, (uint64_t)(((st % h) + h) % h), 2 * n);
+            keyed = g != 1 && c.key_of(g) != nullptr;
+            steps.push_back(st);
+        }
+        if (keyed) {
+            int rc = orc_rotate_sum(cv, cur.data(), steps.data(), (int)steps.size(), cur.data(), top);
+            if (rc) return rc;
+            i0 += m;
+            continue;
+        }
+        for (size_t r = 0; r < m; ++r) {
+            int rc = rotate(c, cur.data(), sign * gaps[i0 + r], tmp.data(), top);
+            if (rc) return rc;
+            orc_add(cv, cur.data(), tmp.data(), cur.data(), top);
+        }
+        i0 += m;
+    }
+    memcpy(out, cur.data(), cw * 8);
+    return 0;
+}
 int orc_mult_pt_rows(void* cv, const uint64_t* x, const uint64_t* pt, uint64_t* out, int top) {
     Ctx& c = *(Ctx*)cv;
     const size_t n = c.n;

@@ -97,6 +97,9 @@ int orc_rescale(void* c, uint64_t* ct, int top);
 int orc_rotate(void* c, const uint64_t* x, int64_t step, uint64_t* out, int top);
 /* x + rot(x, s) ladder: gaps start, 2 start, ... < stop (rotate_and_sum, radix 1) */
 int orc_rotate_and_sum(void* c, const uint64_t* x, int64_t start, int64_t stop, uint64_t* out, int top);
+int orc_rotate_sum(void* c, const uint64_t* x, const int64_t* steps, int nsteps, uint64_t* out, int top);
+int orc_rotate_and_sum_radix(void* c, const uint64_t* x, int64_t start, int64_t stop, int radix_bits, uint64_t* out,
+                             int top);
 /* out = x * pt (pt: encoded rows in coefficient form, NTT'd inside), rows 0..=top */
 int orc_mult_pt_rows(void* c, const uint64_t* x, const uint64_t* pt_coef, uint64_t* out, int top);
 /* out = x + pt (part 0 only) */

@@ -186,6 +186,8 @@ def lib():
         "pcb_pt_load": (C.c_int, [vp, u64p, i32, vp, vp]),
         "pcb_add": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_sum": (C.c_int, [vp, vp, i32, vp, i32, i32, vp]),
+        "pcb_rotate_sum": (C.c_int, [vp, vp, vp, i32, vp, i32, i32, vp]),
+        "pcb_rotate_and_sum_radix": (C.c_int, [vp, vp, C.c_int64, C.c_int64, i32, vp, i32, i32, vp]),
         "pcb_sub": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_mult": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_rescale": (C.c_int, [vp, vp, i32, i32, vp]),

@@ -59,11 +59,31 @@ class Layout:
     head_dim: int
     tokens: int
     slots: int
+    radix_bits: int = 1  # rotate_and_sum ladders: 1 = rung by rung; >= 2 = groups of that many gaps (rotate_sum)
+
+    def ladders(self):
+        d, t = self.head_dim, self.tokens
+        return [(1, d), (-1, d), (d, d * t)]
 
     def rot_steps(self):
-        d, t = self.head_dim, self.tokens
-        up = [1 << i for i in range(int(math.log2(d)))]
-        return up + [-s for s in up] + [d << i for i in range(int(math.log2(t)))]
+        """The rotation keys the decode step needs: every rung (gap) of the three ladders, and with radix groups
+        every step j g (j < 2^n) of each group."""
+        steps = []
+        for start, stop in self.ladders():
+            sign, gaps = (1 if start > 0 else -1), []
+            g = abs(start)
+            while g < stop:
+                gaps.append(g)
+                g *= 2
+            rb = self.radix_bits if self.radix_bits >= 2 else 1
+            for i0 in range(0, len(gaps), rb):
+                n = min(rb, len(gaps) - i0)
+                if n > 1:
+                    steps += [sign * j * gaps[i0] for j in range(1, 1 << n)]
+                else:
+                    steps.append(sign * gaps[i0])
+        seen = set()
+        return [s for s in steps if not (s in seen or seen.add(s))]
 
 
 class KVCache:
@@ -152,7 +172,7 @@ def attend(ops, q_ct, cache, coeffs, primes):
     # 1. scores
     k_ct = ops.drop_to(cache.k, top)
     prod = ops.rescale_one(ops.mult(q_ct, k_ct))
-    x = ops.rotate_and_sum(prod, 1, d)  # top L-1
+    x = ops.rotate_and_sum(prod, 1, d, lay.radix_bits)  # top L-1
     L1 = x.top
     # 2. masked polynomial (baby steps x, x^2, x^3; giant step x^4)
     x2 = ops.rescale_one(ops.mult(x, x))  # L-2
@@ -186,11 +206,11 @@ def attend(ops, q_ct, cache, coeffs, primes):
     A.scale = xb.scale
     P = ops.add(A, xb)
     # 3. replicate each weight over its block
-    R = ops.rotate_and_sum(P, -1, d)
+    R = ops.rotate_and_sum(P, -1, d, lay.radix_bits)
     # 4. weighted values, summed over tokens
     v_ct = ops.drop_to(cache.v, R.top)
     y = ops.rescale_one(ops.mult(R, v_ct))
-    return ops.rotate_and_sum(y, d, d * T)
+    return ops.rotate_and_sum(y, d, d * T, lay.radix_bits)
 
 
 class DecodeGraph:

@@ -698,7 +698,9 @@ int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, 
 
 // ModDown of the K cts of one extended-output batch (c.ext by default) into out: epi 1 (out = (x - conv) P^-1) or
 // 2 (out += ...)
-int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStream_t s, uint64_t* ext = nullptr) {
+// acc_src: out = acc_src + (x - conv) P^-1 (epi 2 reading acc_src, which may be out itself)
+int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStream_t s, uint64_t* ext = nullptr,
+            const uint64_t* acc_src = nullptr) {
     if (!ext) ext = c.ext;
     const LevelPlan& l = c.lv[top];
     PcbNttArgs a = ntt_args(c, ext, l.md_intt_roff, l.md_intt_rprime, K * 2 * c.kp);
@@ -716,8 +718,9 @@ int moddown(PcbCtx& c, uint64_t* out, bool accumulate, int top, int K, cudaStrea
     b.max_tgt = top + 1;
     CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, c.kp, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, c.kp, s));
     PcbNttArgs f = ntt_args(c, c.conv, l.md_ntt_roff, l.md_ntt_rprime, K * 2 * (top + 1));
-    f.epi = accumulate ? 2 : 1;
+    f.epi = accumulate || acc_src ? 2 : 1;
     f.eout = out;
+    f.ed = acc_src;
     f.ex = ext;
     f.es = c.pinv;
     f.ess = c.pinvs;
@@ -1295,6 +1298,82 @@ int pcb_rotate_and_sum(PcbCtx* c, const uint64_t* x, int64_t start, int64_t stop
         if (rc) return rc;
         rc = pcb_add(c, out, c->dbuf, out, top, K, s);
         if (rc) return rc;
+    }
+    return 0;
+}
+
+// out = x + sum_k rot(x, steps[k]) (the reference's rotate_sum, crates/pc-gpu/src/rotate.rs:690-775, the sum formed
+// in the ModDown): one ModUp of x's c1, every key's inner product accumulated into one extended batch (c0 mode 1: each
+// adds its own P sigma_k(c0)), one ModDown whose epilogue adds x. Steps of Galois element 1 are refused. out may be x.
+int pcb_rotate_sum(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32_t nsteps, uint64_t* out, int32_t top,
+                   int32_t K, cudaStream_t s) {
+    if (!c || !x || !out || !steps) return fail(PCB_BAD_ARGS, "null argument");
+    if (nsteps < 1) return fail(PCB_BAD_ARGS, "%d steps", nsteps);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    std::vector<const KeySlot*> keys(nsteps);
+    for (int i = 0; i < nsteps; ++i) {
+        const uint64_t g = rot_galois(*c, steps[i]);
+        if (g == 1) return fail(PCB_BAD_ARGS, "rotate_sum: step %lld is the identity", (long long)steps[i]);
+        keys[i] = key_of(*c, g);
+        if (!keys[i])
+            return fail(-3, "no rotation key for step %lld (galois %llu)", (long long)steps[i], (unsigned long long)g);
+    }
+    const uint64_t* c1 = x + (size_t)c->rows * c->n;
+    rc = modup(*c, c1, top, K, s);
+    if (rc) return rc;
+    for (int i = 0; i < nsteps; ++i) {
+        rc = dot(*c, *keys[i], c1, x, i == 0 ? 1 : 1 | PCB_KS_ACC, top, K, s);
+        if (rc) return rc;
+    }
+    return moddown(*c, out, false, top, K, s, nullptr, x);
+}
+
+// The rotate-and-sum ladder with radix groups (crates/pc-gpu/src/rotate.rs:924-992, radix_bits >= 2): the gaps
+// |start|, 2|start|, .. below stop taken n = min(radix_bits, left) at a time; a group of n > 1 whose steps
+// j g (j = 1 .. 2^n - 1) all have keys is one rotate_sum in place, the rest rung by rung. radix_bits < 2: the rungs.
+int pcb_rotate_and_sum_radix(PcbCtx* c, const uint64_t* x, int64_t start, int64_t stop, int32_t radix_bits,
+                             uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    if (radix_bits < 2) return pcb_rotate_and_sum(c, x, start, stop, out, top, K, s);
+    if (!c || !x || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (start == 0 || stop <= 0) return fail(PCB_BAD_ARGS, "start %lld must be non-zero, stop %lld positive", (long long)start, (long long)stop);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    if (out != x) {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, out);
+        e.a = ct_ref(*c, x);
+        e.rs.nq = top + 1;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+    }
+    const int64_t sign = start < 0 ? -1 : 1;
+    std::vector<int64_t> gaps;
+    for (int64_t g = start < 0 ? -start : start; g < stop; g *= 2) gaps.push_back(g);
+    for (size_t i0 = 0; i0 < gaps.size();) {
+        const size_t m = std::min((size_t)radix_bits, gaps.size() - i0);
+        std::vector<int64_t> steps;
+        bool keyed = m > 1;
+        for (int64_t j = 1; keyed && j < ((int64_t)1 << m); ++j) {
+            const uint64_t g = rot_galois(*c, sign * j * gaps[i0]);
+            keyed = g != 1 && key_of(*c, g) != nullptr;
+            steps.push_back(sign * j * gaps[i0]);
+        }
+        if (keyed) {
+            rc = pcb_rotate_sum(c, out, steps.data(), (int32_t)steps.size(), out, top, K, s);
+            if (rc) return rc;
+            i0 += m;
+            continue;
+        }
+        for (size_t r = 0; r < m; ++r) {
+            rc = pcb_rotate(c, out, sign * gaps[i0 + r], c->dbuf, top, K, s);
+            if (rc) return rc;
+            rc = pcb_add(c, out, c->dbuf, out, top, K, s);
+            if (rc) return rc;
+        }
+        i0 += m;
     }
     return 0;
 }

@@ -306,10 +306,20 @@ class Session:
                 "pcb_rotate_hoisted")
         return outs
 
-    def rotate_and_sum(self, a, start, stop):
+    def rotate_and_sum(self, a, start, stop, radix_bits=1):
+        """a + rot(a, s) + rot(a, 2s) + ... below stop: rung by rung, or (radix_bits >= 2) with groups of gaps that
+        have keys for all their steps summed by rotate_sum (the reference's radix ladder)."""
         out = self.ct_like(a)
-        L.check(L.lib().pcb_rotate_and_sum(self.ctx, a.ptr(), int(start), int(stop), out.ptr(), a.top, a.k,
-                                           self._stream()), "pcb_rotate_and_sum")
+        L.check(L.lib().pcb_rotate_and_sum_radix(self.ctx, a.ptr(), int(start), int(stop), int(radix_bits), out.ptr(),
+                                                 a.top, a.k, self._stream()), "pcb_rotate_and_sum_radix")
+        return out
+
+    def rotate_sum(self, a, steps):
+        """a + sum rot(a, s) over steps, the rotations summed in the extended basis with one ModDown."""
+        out = self.ct_like(a)
+        st = (C.c_int64 * len(steps))(*[int(x) for x in steps])
+        L.check(L.lib().pcb_rotate_sum(self.ctx, a.ptr(), st, len(steps), out.ptr(), a.top, a.k, self._stream()),
+                "pcb_rotate_sum")
         return out
 
     def mult_pt(self, a, pt, pt_scale):

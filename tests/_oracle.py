@@ -80,6 +80,8 @@ def lib():
         "orc_rescale": (C.c_int, [C.c_void_p, u64p, C.c_int]),
         "orc_rotate": (C.c_int, [C.c_void_p, u64p, C.c_int64, u64p, C.c_int]),
         "orc_rotate_and_sum": (C.c_int, [C.c_void_p, u64p, C.c_int64, C.c_int64, u64p, C.c_int]),
+        "orc_rotate_sum": (C.c_int, [C.c_void_p, u64p, C.c_void_p, C.c_int, u64p, C.c_int]),
+        "orc_rotate_and_sum_radix": (C.c_int, [C.c_void_p, u64p, C.c_int64, C.c_int64, C.c_int, u64p, C.c_int]),
         "orc_mult_pt_rows": (C.c_int, [C.c_void_p, u64p, u64p, u64p, C.c_int]),
         "orc_add_pt_rows": (C.c_int, [C.c_void_p, u64p, u64p, u64p, C.c_int]),
         "orc_keyswitch_ext": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_uint32, u64p, C.c_int]),
@@ -197,8 +199,18 @@ class Ctx:
         assert rc == 0, rc
         return out
 
-    def rotate_and_sum(self, ct, start, stop, top):
+    def rotate_and_sum(self, ct, start, stop, top, radix_bits=1):
         out = self.ct()
-        rc = lib().orc_rotate_and_sum(self.h, np.ascontiguousarray(ct), start, stop, out, top)
+        if radix_bits >= 2:
+            rc = lib().orc_rotate_and_sum_radix(self.h, np.ascontiguousarray(ct), start, stop, radix_bits, out, top)
+        else:
+            rc = lib().orc_rotate_and_sum(self.h, np.ascontiguousarray(ct), start, stop, out, top)
+        assert rc == 0, rc
+        return out
+
+    def rotate_sum(self, ct, steps, top):
+        out = self.ct()
+        st = np.asarray(steps, np.int64)
+        rc = lib().orc_rotate_sum(self.h, np.ascontiguousarray(ct), st.ctypes.data, len(st), out, top)
         assert rc == 0, rc
         return out

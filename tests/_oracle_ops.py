@@ -34,8 +34,11 @@ class OracleOps:
         a.top -= 1
         return a
 
-    def rotate_and_sum(self, a, start, stop):
-        return OCt(self.c.rotate_and_sum(a.data, start, stop, a.top), a.top, a.scale, a.slots)
+    def rotate_and_sum(self, a, start, stop, radix_bits=1):
+        return OCt(self.c.rotate_and_sum(a.data, start, stop, a.top, radix_bits), a.top, a.scale, a.slots)
+
+    def rotate_sum(self, a, steps):
+        return OCt(self.c.rotate_sum(a.data, steps, a.top), a.top, a.scale, a.slots)
 
     def drop_to(self, a, top):
         return OCt(a.data, top, a.scale, a.slots)

@@ -66,3 +66,35 @@ def test_decode_graph_replays_eager_step(pair):
         got = g(q).data.clone()
         want = A.attend(s, q, cache, coeffs, ch.q)
         assert torch.equal(got[:, :, : want.top + 1], want.data[:, :, : want.top + 1])
+
+
+@pytest.fixture(scope="module")
+def pair3():
+    """Config 1 with the radix ladder (groups of 3 gaps summed by rotate_sum; 38 rotation keys)."""
+    ch = fhe.config1_chain()
+    lay = A.Layout(head_dim=64, tokens=32, slots=ch.n // 2, radix_bits=3)
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=1, seed=0, h=192, sigma=3.2)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(0, 192, 3.2, s.galois)
+    return ch, lay, s, OracleOps(o)
+
+
+def test_attention_decode_radix_bit_exact(pair3):
+    """The decode step with radix-3 ladders, the CUDA path against the oracle word for word, and replayed as a graph."""
+    ch, lay, s, oo = pair3
+    rng = np.random.default_rng(31)
+    q, K, V = rng.normal(0, 1, 64) / 8, rng.normal(0, 1, (32, 64)) / 8, rng.normal(0, 1, (32, 64)) / 8
+    g = run(s, ch, lay, q, K, V, False)
+    want_ct = run(oo, ch, lay, q, K, V, False)
+    torch.cuda.synchronize()
+    gh = g.data[0].cpu().numpy().view(np.uint64)
+    assert (gh[:, : g.top + 1] == want_ct.data[:, : g.top + 1]).all()
+    got = s.decrypt_slots(g).real[:64]
+    assert np.abs(got - A.plain_attention(q, K, V, A.softmax_poly(lay.tokens))).max() < 1e-3
+    top = len(ch.q) - 1
+    cache = A.KVCache(s, lay, top)
+    cache.load(K, V)
+    qc = A.encrypt_query(s, q, lay, top, ch.q[top])
+    graph = A.DecodeGraph(s, cache, A.softmax_poly(lay.tokens), ch.q, qc)
+    eager = A.attend(s, qc, cache, A.softmax_poly(lay.tokens), ch.q)
+    assert torch.equal(graph(qc).data[:, :, : eager.top + 1], eager.data[:, :, : eager.top + 1])

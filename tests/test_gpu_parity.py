@@ -303,6 +303,22 @@ def test_config2_relin_and_rotation_bit_exact(s2):
     assert np.abs(s.decrypt_slots(r2).real[:1024] - np.roll(np.pad(x, (0, r2.slots - 1024)), -1)[:1024]).max() < 2e-5
 
 
+def test_config2_rotate_sum_bit_exact(s2):
+    # the rotations summed in the extended basis with one ModDown (the reference's rotate_sum): FP64 inner products
+    # accumulated across keys, the ModDown epilogue adding x
+    s, o = s2
+    rng = np.random.default_rng(9)
+    x = rng.normal(0, 1, 1024) / 8
+    top = s.top() - 2
+    a, oa = _pair(s, o, x, top)
+    r = s.rotate_sum(a, [1, 5])
+    assert _eq(r, o.rotate_sum(oa, [1, 5], top), top, s.rows)
+    want = x + np.roll(np.pad(x, (0, r.slots - 1024)), -1)[:1024] + np.roll(np.pad(x, (0, r.slots - 1024)), -5)[:1024]
+    assert np.abs(s.decrypt_slots(r).real[:1024] - want).max() < 5e-5
+    with pytest.raises(L.PcbError, match="identity"):
+        s.rotate_sum(a, [1, s.n // 2])
+
+
 def test_batched_ops_equal_single(s1):
     s, o = s1
     rng = np.random.default_rng(7)

@@ -100,6 +100,36 @@ def test_rotate_and_sum(ctx):
     assert np.abs(got.real - want).max() < 1e-5
 
 
+@pytest.fixture(scope="module")
+def ctx_r():
+    # keys for radix-2 groups of gaps 1, 2 (steps 1, 2, 3) and 4, 8 (steps 4, 8, 12), plus rung steps
+    return make_ctx(nq=6, kp=3, dnum=2, pbits=50, steps=(1, 2, 3, 4, 8, 12, 16, -1, -2, -3))
+
+
+def test_rotate_sum(ctx_r):
+    """out = x + sum rot(x, s): the rotations summed in the extended basis, one ModDown (the reference's rotate_sum)."""
+    top = ctx_r.nq - 1
+    x = vals(16)
+    ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    got = ctx_r.decrypt(ctx_r.rotate_sum(ct, [1, 2, 3], top), top, SLOTS, SCALE).real
+    want = x + np.roll(x, -1) + np.roll(x, -2) + np.roll(x, -3)
+    assert np.abs(got - want).max() < 1e-5
+    # a step of Galois element 1 is refused, as in a reference group
+    with pytest.raises(AssertionError):
+        ctx_r.rotate_sum(ct, [SLOTS], top)
+
+
+@pytest.mark.parametrize("start,stop,radix", [(1, 16, 2), (1, 32, 2), (-1, 4, 2), (1, 8, 3)])
+def test_rotate_and_sum_radix(ctx_r, start, stop, radix):
+    """The radix ladder: groups with keys go through rotate_sum, the rest rung by rung; the same sum as the rungs."""
+    top = ctx_r.nq - 1
+    x = vals(17)
+    ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    got = ctx_r.decrypt(ctx_r.rotate_and_sum(ct, start, stop, top, radix), top, SLOTS, SCALE).real
+    want = sum(np.roll(x, -start * k) for k in range(stop // abs(start)))
+    assert np.abs(got - want).max() < 1e-4
+
+
 def test_mult_pt_and_add_pt(ctx):
     top = ctx.nq - 1
     x, w = vals(7), vals(8)

@@ -313,6 +313,9 @@ def test_config2_rotate_sum_bit_exact(s2):
     a, oa = _pair(s, o, x, top)
     r = s.rotate_sum(a, [1, 5])
     assert _eq(r, o.rotate_sum(oa, [1, 5], top), top, s.rows)
+    # five keys: two groups of inner products (4 + 1) summed by the ModDown as it reads them
+    r5 = s.rotate_sum(a, [1, 5, 1, 5, 1])
+    assert _eq(r5, o.rotate_sum(oa, [1, 5, 1, 5, 1], top), top, s.rows)
     want = x + np.roll(np.pad(x, (0, r.slots - 1024)), -1)[:1024] + np.roll(np.pad(x, (0, r.slots - 1024)), -5)[:1024]
     assert np.abs(s.decrypt_slots(r).real[:1024] - want).max() < 5e-5
     with pytest.raises(L.PcbError, match="identity"):

@@ -295,6 +295,12 @@ def run_ours(a):
     hbm = peaks.get("hbm_gbs") or 6650.0
     ntt_bytes = 2 * ntt_rows * n * 8
     ntt_gbs = ntt_bytes / (ntt_ms * 1e-3) / 1e9
+    # the same pass against the FP64 pipe, which is what bounds it: per N = 2^16 row, 16 stages x 2^15 butterflies of 8
+    # FP64 operations (six for the exact product, the sum and the difference), the round reductions (3 per word, two
+    # rounds), the column pass's twist product (6 per word), the conversion in (1) and the canonical form out (9)
+    fp64_ops_row = 16 * (n // 2) * 8 + 2 * 3 * n + 6 * n + n + 9 * n
+    fp64_tops = fp64_ops_row * ntt_rows / (ntt_ms * 1e-3) / 1e12
+    fp64_peak = 64 * 148 * 1.965e9 / 1e12  # FP64 FMA per clock per SM x SMs x max clock
     traffic = None
     try:
         traffic = json.load(open(os.path.join(ROOT, "profiles", "ntt_fwd_traffic.json")))["bytes_per_3072_row_pass"]
@@ -329,7 +335,10 @@ def run_ours(a):
             "roofline": {"kernel": "ntt fwd (fwd_cols + fwd_rows) over the batch's 3072 rows", "bound": "hbm",
                          "achieved": ntt_gbs, "peak": hbm, "unit": "GB/s", "frac": ntt_gbs / hbm,
                          "traffic": traffic, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                         "ms": ntt_ms, "algorithmic_bytes": ntt_bytes},
+                         "ms": ntt_ms, "algorithmic_bytes": ntt_bytes,
+                         "fp64_pipe": {"ops_per_row": fp64_ops_row, "achieved_tops": fp64_tops, "peak_tops": fp64_peak,
+                                       "frac": fp64_tops / fp64_peak,
+                                       "peak_source": "nominal: 64 FP64 FMA / clock / SM x 148 SMs x 1.965 GHz"}},
             "clocks": clk,
             "attn_decode_ms_per_token": attn,
             "plain_rotation_ks_per_s": plain_ks,

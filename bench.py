@@ -318,7 +318,7 @@ def run_ours(a):
     h2d, d2h = host_in.numel() * 8, host_out[0].numel() * 8
     del s, x, nbuf, bufs, host_in, host_out, ct, res
     torch.cuda.empty_cache()
-    attn = attention_decode(a, world, rank, barrier, dist)
+    attn, attn_err = attention_decode(a, world, rank, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -341,6 +341,7 @@ def run_ours(a):
                                        "peak_source": "nominal: 64 FP64 FMA / clock / SM x 148 SMs x 1.965 GHz"}},
             "clocks": clk,
             "attn_decode_ms_per_token": attn,
+            "attn_decode_max_abs_err_vs_fp64": attn_err,
             "plain_rotation_ks_per_s": plain_ks,
         }
         if world == 1 and not a.no_cpu_baseline:
@@ -368,21 +369,25 @@ def attention_decode(a, world, rank, barrier, dist):
     from perseus_b200 import attention as A
     from perseus_b200 import fhe, shard
 
-    rng = np.random.default_rng(100 + rank)
-    out = {}
+    out, err = {}, {}
     for name, ch, tokens, heads in (("config1_1head_N2^14_32tok", fhe.config1_chain(), 32, 1),
                                     ("config3_12heads_N2^16_128tok", fhe.config2_chain(), 128, 12)):
-        # config 1 runs on every rank (rank 0 reports it); config 3's heads are split, at most one apart
+        # config 1 runs on every rank (rank 0 reports it) on BASELINE's data (default_rng(0): K, V then Q); config
+        # 3's heads are split, at most one apart, each rank drawing its own
+        rng = np.random.default_rng(0 if heads == 1 else 100 + rank)
         mine = heads if heads == 1 else len(shard.head_range(heads, world, rank))
         lay = A.Layout(64, tokens, ch.n // 2, radix_bits=3)  # radix-3 ladders (rotate_sum groups)
         s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=mine, seed=0)
         top = len(ch.q) - 1
-        caches, qs = [], []
+        caches, qs, plain = [], [], []
         for _ in range(mine):
             c = A.KVCache(s, lay, top)
-            c.load(rng.normal(0, 1, (tokens, 64)) / 8, rng.normal(0, 1, (tokens, 64)) / 8)
+            K, V = rng.normal(0, 1, (tokens, 64)) / 8, rng.normal(0, 1, (tokens, 64)) / 8
+            qv = rng.normal(0, 1, 64) / 8
+            c.load(K, V)
             caches.append(c)
-            qs.append(A.encrypt_query(s, rng.normal(0, 1, 64) / 8, lay, top, ch.q[top]))
+            qs.append(A.encrypt_query(s, qv, lay, top, ch.q[top]))
+            plain.append((qv, K, V))
         cache = caches[0] if mine == 1 else A.HeadBatch(s, caches)
         q = qs[0] if mine == 1 else s.stack(qs)
         coeffs = A.softmax_poly(tokens)
@@ -406,9 +411,14 @@ def attention_decode(a, world, rank, barrier, dist):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out[name] = t[1].item()
         out[name + "_eager"] = t[0].item()
-        del s, caches, qs, cache, q, graph
+        # decrypted output of this rank's first head against fp64 attention with the same polynomial softmax
+        res = graph(q)
+        qv, K, V = plain[0]
+        got = s.decrypt_slots(res, 0).real[:64]
+        err[name] = float(np.abs(got - A.plain_attention(qv, K, V, coeffs)).max())
+        del s, caches, qs, cache, q, graph, res
         torch.cuda.empty_cache()
-    return out
+    return out, err
 
 
 def main():

@@ -51,6 +51,16 @@ def s2():
     return s, o
 
 
+@pytest.fixture(scope="module")
+def s3():
+    # N = 2^14 with every prime below 2^50 (8 Q + 2 special, dnum 4): the FP64 kernels at the smaller ring
+    ch = fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 8)), tuple(fhe.ntt_primes(50, 14, 2, skip=8)), 4)
+    s = fhe.Session(ch, rot_steps=(1, 3, 2), k_max=2, seed=SEED, h=H, sigma=SIGMA)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(SEED, H, SIGMA, s.galois)
+    return s, o
+
+
 # ------------------------------------------------------------------------------------------------ launchers
 
 
@@ -366,3 +376,33 @@ def test_hoisted_rotations_equal_plain(which, request):
     for st, h in zip(steps, outs):
         p = s.rotate(a, st) if st % (s.n // 2) else a
         assert torch.equal(h.data[:, :, : top + 1], p.data[:, :, : top + 1]), st
+
+
+def test_fp64_small_ring_bit_exact(s3):
+    """The FP64 path at N = 2^14 (column pass in rounds of 3 stages): NTT batch, relinearized product, rotation,
+    hoisted rotations in one group, rotate_sum and the radix ladder, all against the oracle word for word."""
+    s, o = s3
+    rng = np.random.default_rng(15)
+    x = np.empty((2 * s.nq, s.n), np.uint64)
+    for i in range(2 * s.nq):
+        x[i] = rng.integers(0, o.q[i % s.nq], s.n, dtype=np.uint64)
+    xd = dev(x)
+    s.ntt_batch(xd, 2 * s.nq)
+    want = x.copy()
+    O.lib().orc_ntt_batch(o.h, want, 2 * s.nq, 0)
+    assert (host(xd) == want).all()
+    s.ntt_batch(xd, 2 * s.nq, inverse=True)
+    assert (host(xd) == x).all()
+    top = s.top()
+    v, w = rng.normal(0, 1, 256) / 8, rng.normal(0, 1, 256) / 8
+    a, oa = _pair(s, o, v, top)
+    b, ob = _pair(s, o, w, top)
+    assert _eq(s.mult(a, b), o.mult(oa, ob, top), top, s.rows)
+    assert _eq(s.rotate(a, 3), o.rotate(oa, 3, top), top, s.rows)
+    outs = s.rotate_hoisted(a, [1, 3, 2])
+    for st, h in zip([1, 3, 2], outs):
+        assert torch.equal(h.data[:, :, : top + 1], s.rotate(a, st).data[:, :, : top + 1]), st
+    assert _eq(s.rotate_sum(a, [1, 2, 3]), o.rotate_sum(oa, [1, 2, 3], top), top, s.rows)
+    r = s.rotate_and_sum(a, 1, 4, radix_bits=2)
+    assert _eq(r, o.rotate_and_sum(oa, 1, 4, top, 2), top, s.rows)
+    assert np.abs(s.decrypt_slots(r).real - sum(np.roll(v, -k) for k in range(4))).max() < 1e-4

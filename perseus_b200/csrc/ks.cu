@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
 // M / t taken as fl(M fl(1 / t)); sources enter as canonical doubles (|y M / t| < 2^49, so every product lies in
 // [-0.625t, 0.625t]); the sum is reduced every 4 sources and made canonical once. The conversion matrix sits in shared
 // memory as {M, M / t} pairs. Exact (HPS) jobs take their correction through the integer Barrett step.
-constexpr int BCONV_F_SPAN = 4;  // 128-coefficient spans per CTA: the shared tables are built once for all of them
+// 128-coefficient spans per CTA: the shared tables are built once for all of them (2 and 8 measured the same)
+constexpr int BCONV_F_SPAN = 4;
 template <int LOGN, int NS>
 __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
     constexpr int S = NS > 0 ? NS : MAX_SRC;
@@ -547,8 +548,10 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
 // Several keys against the same ModUp digits (the steps of a hoisted rotation): each digit word is read once and
 // multiplied by every key of the group, so the digits stream once per group instead of once per key. One word per
 // thread; the keys stay in registers as centred doubles (their quotients by p are formed per use, as in dot_all_f).
+// 6 CTAs per SM (at most 85 registers, 24 warps): the config-2 step took 100.0 ms, against 101.0 at 5 CTAs
+// (102 registers) and 101.5-102.5 with the compiler's choice of 116
 template <int LOGN, int ND, int RK>
-__global__ void __launch_bounds__(BX) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
+__global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
     const uint32_t t = a.rows[blockIdx.y];
     const uint64_t p = a.pr[t].p;
     const double pf = to_f(p), pinv = 1.0 / pf;

@@ -235,7 +235,8 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             CK(cudaMemcpyAsync(c.iws + (size_t)r * n, iws.data(), n * 8, cudaMemcpyHostToDevice, s));
             if (c.f64) {
                 // pack: column twiddles w[0 .. R), the 256-point twiddles of psi^(N/256) in OpenFHE order, the twist
-                // gamma_b^k = psi^(k c_b) at b 256 + k with c_b = 1 - 2^(L-8) + 2 brev(b) (inverse: psi^-(k c_b))
+                // gamma_b^k = psi^(k c_b) at b 256 + k with c_b = 1 - 2^(L-8) + 2 brev(b) (inverse: psi^-(k c_b)).
+                // Entry 0 is psi^0 = 1: {1, fl(1 / p)}, which the kernels read as 1 / p
                 const size_t R = n >> 8, m2 = 2 * n;
                 auto psi_pow = [&](size_t e) { e %= m2; return e < n ? pw[e] : (pw[e - n] ? p - pw[e - n] : 0); };
                 for (size_t t = 0; t < R; ++t) {

@@ -75,15 +75,6 @@ template <bool F> using Mod = std::conditional_t<F, FpMod, IntMod>;
 template <bool F> using Word = std::conditional_t<F, double, uint64_t>;
 
 template <bool F>
-__device__ __forceinline__ Mod<F> make_mod(uint64_t p) {
-    if constexpr (F) {
-        const double pf = to_f(p);
-        return FpMod{pf, 1.0 / pf};
-    } else {
-        return IntMod{p, 2 * p};
-    }
-}
-template <bool F>
 __device__ __forceinline__ Word<F> from_u64(uint64_t x) {
     if constexpr (F) return to_f(x);
     else return x;
@@ -129,6 +120,17 @@ struct Pack {
 };
 // Shared-memory slot of fixed twiddle t. Stages whose twiddle varies with the thread (4 .. 7 forward, 0 .. 3
 // inverse) read region [2^e, 2^(e+1)) at offset u 2^(e-4) + j; stored as [j][u], 16 threads read consecutive slots.
+// The per-row constants: FP64 takes fl(1 / p) from entry 0 of the row's pack ({1, fl(1 / p)}: twiddle index 0 is
+// psi^0 and no stage uses it), which spares every thread a division before its first butterfly
+template <int LOGN, bool F>
+__device__ __forceinline__ Mod<F> mod_of(uint64_t p, const void* tw, int pid) {
+    if constexpr (F) {
+        const double2* pk = (const double2*)tw + (size_t)pid * Pack<LOGN>::SIZE;
+        return FpMod{to_f(p), __ldg(&pk->y)};
+    } else {
+        return IntMod{p, 2 * p};
+    }
+}
 __device__ __forceinline__ int tw_slot(int t) {
     if (t < 16) return t;
     const int e = 31 - __clz(t), off = t - (1 << e), sh = e - 4;
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
-    const Mod<F> md = make_mod<F>(p);
+    const Mod<F> md = mod_of<LOGN, F>(p, a.fw, ri.pid);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
     const double2* pk = nullptr;
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
-    const Mod<F> md = make_mod<F>(p);
+    const Mod<F> md = mod_of<LOGN, F>(p, a.fw, ri.pid);
     const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
     const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
     if constexpr (F) {
@@ -351,7 +353,7 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
-    const Mod<F> md = make_mod<F>(p);
+    const Mod<F> md = mod_of<LOGN, F>(p, a.iw, ri.pid);
     const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
     const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
     const double2* pk = nullptr;
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     const int i = row0 + blockIdx.y;
     const RowInfo ri = row_of<LOGN>(a, i);
     const uint64_t p = a.pr[ri.pid].p;
-    const Mod<F> md = make_mod<F>(p);
+    const Mod<F> md = mod_of<LOGN, F>(p, a.iw, ri.pid);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
     if constexpr (F) {
@@ -477,8 +479,9 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
         nis = ((const uint64_t*)a.ninvs)[ri.pid];
     }
     if constexpr (F) {
-        double nc, np;
-        centred_f(ni, p, md.p, nc, np);
+        // the row's factor as a centred double, its quotient by p as fl(nc fl(1 / p)) (relative error 2^-52: the
+        // product lies in [-p, p], made canonical right after)
+        const double nc = ni > p / 2 ? -to_f(p - ni) : to_f(ni), np = __dmul_rn(nc, md.pinv);
 #pragma unroll
         for (int k = 0; k < E; ++k)
             ri.row[(size_t)(g + E * k) * 256 + col] = canon_f(mul_f(x[k], nc, np, md.p), md.p, md.pinv);

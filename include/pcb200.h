@@ -179,6 +179,57 @@ typedef struct PcbTensorArgs {
     int32_t dbl, acc_d2;
 } PcbTensorArgs;
 
+/* args.cuh:184-200: BSGS plaintext dot of K ciphertexts' baby rotations (rows of rs, both parts):
+ *   res[c][j] = sum_{b < bstep, d = bstep j + b < npts} rot[c][b] * pts[d]   for j < gstep
+ * rot (c, b) at rot.base + c rot.ct_stride + b rot_stride, res (c, j) at res.base + c res.ct_stride + j res_stride.
+ * pts[d] (a device array of device pointers): rows of ptw words, Q rows at their grid index y, special rows at
+ * pt_prow + (y - nq); word i read at the compact index (enc = 0xFFFFFFFF: i; (enc >> 24) == 0x7F: i >> (enc & 0xFF);
+ * else i & enc). K <= 8; bstep (max p)^2 below 2^128 (128-bit sums, one reduction). */
+typedef struct PcbPtDotArgs {
+    PcbPolyRef rot, res;
+    uint64_t rot_stride, res_stride;
+    const void* const* pts;
+    const PcbPrimeConst* pr;
+    PcbRowSet rs;
+    int32_t npts, bstep, gstep, K;
+    int32_t ptw, pt_prow;
+    uint32_t enc;
+    int32_t pad;
+} PcbPtDotArgs;
+
+/* args.cuh:491-498: part 0 of K ciphertexts += k[row] over rows [0, n) (k raw words, k == p allowed) */
+typedef struct PcbAddConstArgs {
+    PcbPolyRef x;
+    const void* k;
+    const PcbPrimeConst* pr;
+    int32_t n, K;
+} PcbAddConstArgs;
+
+/* args.cuh:500-506: out = in * t[row] over rows [0, n) of K ciphertexts, both parts (t: [row][N] words) */
+typedef struct PcbMulTableArgs {
+    PcbPolyRef out, in;
+    const void* t;
+    const PcbPrimeConst* pr;
+    int32_t n, K;
+} PcbMulTableArgs;
+
+/* args.cuh:508-515: out = y + m (sub 0), y - m (1), m - y (2), m = in * t as mul_table; out may alias y or in */
+typedef struct PcbMulAddArgs {
+    PcbMulTableArgs m;
+    PcbPolyRef y;
+    int32_t sub, pad;
+} PcbMulAddArgs;
+
+/* args.cuh:517-528: out = y + sum_{j < nterm} x[j] * t[j] (y.base null: no y), rows [0, n) of K ciphertexts, both
+ * parts, nterm <= 8; lazy selects one reduction of the 128-bit sum or one per product (the same canonical words) */
+typedef struct PcbMulAddNArgs {
+    PcbPolyRef out, y;
+    PcbPolyRef x[8];
+    const void* t[8];
+    const PcbPrimeConst* pr;
+    int32_t n, K, nterm, lazy;
+} PcbMulAddNArgs;
+
 /* args.cuh:438-447: for parts 0, 1: dst = f (dst + (x - t) binv) [+ k on part 0], f = 2 when dbl */
 typedef struct PcbMdEpiArgs {
     PcbPolyRef dst, x, t;
@@ -261,7 +312,7 @@ typedef struct PcbKernelTable {
     int (*ew_scale)(const PcbEwArgs*, cudaStream_t);
     int (*ew_sub_mul)(const PcbEwArgs*, cudaStream_t);
     int (*ew_copy)(const PcbEwArgs*, cudaStream_t);
-    PcbLaunch pt_dot;
+    int (*pt_dot)(const PcbPtDotArgs*, cudaStream_t);
     int (*ks_dot)(const PcbKsArgs*, cudaStream_t);
     int (*ks_dot_regen)(const PcbKsRegenArgs*, cudaStream_t);
     int (*ksk_expand)(const PcbKskExpandArgs*, cudaStream_t);
@@ -269,8 +320,8 @@ typedef struct PcbKernelTable {
     int (*tensor)(const PcbTensorArgs*, cudaStream_t);
     int (*md_epilogue)(const PcbMdEpiArgs*, cudaStream_t);
     PcbLaunch wsum;
-    PcbLaunch add_const;
-    PcbLaunch mul_table;
+    int (*add_const)(const PcbAddConstArgs*, cudaStream_t);
+    int (*mul_table)(const PcbMulTableArgs*, cudaStream_t);
     int (*rescale_coef)(const PcbRescaleArgs*, cudaStream_t);
     int (*rescale_combine)(const PcbRescaleCombineArgs*, cudaStream_t);
     int (*automorph)(const PcbAutomorphArgs*, cudaStream_t);
@@ -278,9 +329,12 @@ typedef struct PcbKernelTable {
     int (*encrypt)(const PcbEncryptArgs*, cudaStream_t);
     int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
     PcbLaunch ksk_unpack, mod_raise, small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen,
-        ks_dot_key, pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum, mul_add,
-        rescale_fwd, mul_add_n, tensor_y, wsum_multi, bconv_wide, tfhe, tensor_sum, tensor_multi, tensor_seeded,
-        ew_many, submul_many, pack_split, pack_dot;
+        ks_dot_key, pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum;
+    int (*mul_add)(const PcbMulAddArgs*, cudaStream_t);
+    PcbLaunch rescale_fwd;
+    int (*mul_add_n)(const PcbMulAddNArgs*, cudaStream_t);
+    PcbLaunch tensor_y, wsum_multi, bconv_wide, tfhe, tensor_sum, tensor_multi, tensor_seeded, ew_many, submul_many,
+        pack_split, pack_dot;
 } PcbKernelTable;
 
 /* args.cuh:1099-1119: ring-size tables (rows of 2^log_n words) */
@@ -409,6 +463,19 @@ int pcb_mult_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* ou
                 cudaStream_t stream);
 int pcb_add_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
                cudaStream_t stream);
+/* out = y + x * pt (sub 0), y - x * pt (1), x * pt - y (2) in one pass: the reference's mult_pt_add
+ * (crates/pc-gpu/src/ops.rs:968-1005, one mul_add launch). out may alias x or y. */
+int pcb_mult_pt_add(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, const uint64_t* y, uint64_t* out, int32_t sub,
+                    int32_t top, int32_t K, cudaStream_t stream);
+/* The BSGS plaintext-matrix product of K ciphertexts (the LT stage of crates/pc-gpu/src/bts/cts.rs; apply_linear of
+ * python/perseus/impl/linear.py):
+ *   out = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) * pts[bstep j + b], bstep j stride),
+ * gstep = ceil(npts / bstep). pts: a DEVICE array of npts device plaintexts ([nq][N] evaluation rows, pcb_pt_load),
+ * diagonal d pre-rotated by -bstep j stride. Needs rotation keys for b stride (b < bstep) and bstep j stride (j >= 1,
+ * none the identity). work: (bstep + gstep) K ciphertexts of device scratch ([2][nq + kp][N] each) that neither x nor
+ * out may overlap. The result's scale is x's times the plaintexts'; out may be x. */
+int pcb_linear_transform(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t npts, int32_t bstep,
+                         int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K, cudaStream_t stream);
 
 /* The hybrid key switch of one polynomial per ciphertext (the north star's fused KeySwitcher): ext = dot(ModUp(d))
  * against key `kidx` with c0 mode (0 none, 1 P c0 on Q rows) and output permutation autok, then ModDown into out.
@@ -443,6 +510,11 @@ static_assert(sizeof(PcbRescaleCombineArgs) == 80, "RescaleCombineArgs layout");
 static_assert(sizeof(PcbAutomorphArgs) == 112, "AutomorphArgs layout");
 static_assert(sizeof(PcbEncryptArgs) == 64, "EncryptArgs layout");
 static_assert(sizeof(PcbKskGenArgs) == 120, "KskGenArgs layout");
+static_assert(sizeof(PcbPtDotArgs) == 128, "PtDotArgs layout");
+static_assert(sizeof(PcbAddConstArgs) == 48, "AddConstArgs layout");
+static_assert(sizeof(PcbMulTableArgs) == 72, "MulTableArgs layout");
+static_assert(sizeof(PcbMulAddArgs) == 104, "MulAddArgs layout");
+static_assert(sizeof(PcbMulAddNArgs) == 328, "MulAddNArgs layout");
 static_assert(sizeof(PcbKernelTable) == 16 + 52 * 8, "KernelTable layout");
 static_assert(sizeof(PcbRingTable) == 16 + 9 * 8, "RingTable layout");
 #endif

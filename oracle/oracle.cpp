@@ -1234,4 +1234,115 @@ int orc_rotate_batch(void* cv, const uint64_t* x, int k, int64_t step, uint64_t*
     return 0;
 }
 
+/* ---------------------------------------------------------------- plaintext-operand kernels (linear layers) */
+
+// out[m][y] = x[m][y] t[y] mod primes[y] for nx polynomials of nrows rows: the product of mul_table / mul_add /
+// mul_add_n (crates/pc-kernels/kernels/args.cuh:500-528, host twin crates/pc-host/src/elem.rs)
+int orc_mul_rows(const uint64_t* x, const uint64_t* t, uint64_t* out, const uint64_t* primes, int nrows, int logn,
+                 int nx) {
+    const size_t n = (size_t)1 << logn;
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < nx; ++m)
+        for (int y = 0; y < nrows; ++y) {
+            const size_t o = ((size_t)m * nrows + y) * n;
+            for (size_t i = 0; i < n; ++i) out[o + i] = mulmod(x[o + i], t[(size_t)y * n + i], primes[y]);
+        }
+    return 0;
+}
+
+// The BSGS plaintext dot (crates/pc-host/src/elem.rs:145-180; kernel crates/pc-kernels/kernels/elem.cuh:84-130):
+// res[c][j][part][y] = sum_{b < bstep, d = bstep j + b < npts} rot[c][b][part][y] pts[d][prow[y]][idx(i)] mod p_y,
+// the sum taken exactly in 128 bits. Dense layouts: rot [K][bstep][2][nrows][N], res [K][gstep][2][nrows][N],
+// pts [npts][nprow][ptw]; idx as the kernel's compact index (enc).
+int orc_pt_dot(const uint64_t* rot, uint64_t* res, const uint64_t* pts, const uint64_t* primes, const int32_t* prow,
+               int nrows, int logn, int K, int bstep, int gstep, int npts, int ptw, int nprow, uint32_t enc) {
+    const size_t n = (size_t)1 << logn;
+    if (K < 1 || bstep < 0 || gstep < 0 || npts < 0) return -1;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int c = 0; c < K; ++c)
+        for (int j = 0; j < gstep; ++j)
+            for (int part = 0; part < 2; ++part)
+                for (int y = 0; y < nrows; ++y) {
+                    const uint64_t p = primes[y];
+                    uint64_t* o = res + ((((size_t)c * gstep + j) * 2 + part) * nrows + y) * n;
+                    for (size_t i = 0; i < n; ++i) {
+                        const size_t pi = enc == 0xFFFFFFFFu ? i : (enc >> 24) == 0x7Fu ? i >> (enc & 0xFFu) : (i & enc);
+                        u128 acc = 0;
+                        for (int b = 0; b < bstep; ++b) {
+                            const int d = bstep * j + b;
+                            if (d >= npts) break;
+                            const uint64_t w = pts[((size_t)d * nprow + prow[y]) * ptw + pi];
+                            acc += (u128)rot[((((size_t)c * bstep + b) * 2 + part) * nrows + y) * n + i] * w;
+                        }
+                        o[i] = (uint64_t)(acc % p);
+                    }
+                }
+    return 0;
+}
+
+// The BSGS plaintext-matrix product (the LT stage of crates/pc-gpu/src/bts/cts.rs; python/perseus/impl/linear.py
+// apply_linear): out = sum_j rot(sum_b rot(x, b stride) pts[bstep j + b], bstep j stride). Babies by plain rotation,
+// baby sums exact mod p, the giant rotations' extended-basis outputs summed mod p with one ModDown plus giant step 0
+// (the reference's rotate_sum form, as orc_rotate_sum). pts: npts evaluation-form plaintexts [nq][N] (rows 0..=top
+// read).
+int orc_linear_transform(void* cv, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
+                         uint64_t* out, int top) {
+    Ctx& c = *(Ctx*)cv;
+    if (npts < 1 || bstep < 1 || stride == 0) return -1;
+    const size_t n = c.n, cw = c.ct_words();
+    const int rows = c.rows();
+    const int gstep = (npts + bstep - 1) / bstep;
+    std::vector<uint64_t> baby((size_t)bstep * cw), res((size_t)gstep * cw, 0);
+    std::copy(x, x + cw, baby.begin());
+    for (int b = 1; b < bstep; ++b) {
+        const int rc = orc_rotate(cv, x, (int64_t)b * stride, baby.data() + (size_t)b * cw, top);
+        if (rc) return rc;
+    }
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int j = 0; j < gstep; ++j)
+        for (int t = 0; t <= top; ++t) {
+            const uint64_t p = c.primes[t];
+            for (int part = 0; part < 2; ++part) {
+                uint64_t* o = res.data() + (size_t)j * cw + ((size_t)part * rows + t) * n;
+                for (size_t i = 0; i < n; ++i) {
+                    u128 acc = 0;
+                    for (int b = 0; b < bstep && bstep * j + b < npts; ++b)
+                        acc += (u128)baby[(size_t)b * cw + ((size_t)part * rows + t) * n + i] *
+                               pts[((size_t)(bstep * j + b) * c.nq + t) * n + i];
+                    o[i] = (uint64_t)(acc % p);
+                }
+            }
+        }
+    if (gstep == 1) {
+        std::copy(res.begin(), res.begin() + cw, out);
+        return 0;
+    }
+    std::vector<uint64_t> sum(cw, 0), ext(cw), md(cw);
+    for (int j = 1; j < gstep; ++j) {
+        const int64_t h = (int64_t)n / 2, st = (int64_t)j * bstep * stride;
+        const uint64_t g = powmod(5, (uint64_t)(((st % h) + h) % h), 2 * n);
+        if (g == 1) return -1;
+        const Key* key = c.key_of(g);
+        if (!key) return -3;
+        const uint64_t ginv = powmod(g, (2 * n >> 2) - 1, 2 * n);
+        const uint64_t* rj = res.data() + (size_t)j * cw;
+        keyswitch_ext(c, rj + (size_t)rows * n, rj, 1, *key, (uint32_t)ginv, ext.data(), top);
+        for (int part = 0; part < 2; ++part)
+            for (int t = 0; t < rows; ++t) {
+                if (t > top && t < c.nq) continue;
+                const uint64_t p = c.primes[t];
+                const size_t o = ((size_t)part * rows + t) * n;
+                for (size_t i = 0; i < n; ++i) sum[o + i] = addmod(sum[o + i], ext[o + i], p);
+            }
+    }
+    moddown(c, sum.data(), md.data(), top);
+    for (int part = 0; part < 2; ++part)
+        for (int t = 0; t <= top; ++t) {
+            const uint64_t p = c.primes[t];
+            const size_t o = ((size_t)part * rows + t) * n;
+            for (size_t i = 0; i < n; ++i) out[o + i] = addmod(res[o + i], md[o + i], p);
+        }
+    return 0;
+}
+
 }  // extern "C"

@@ -116,6 +116,19 @@ int orc_moddown(void* c, const uint64_t* ext, uint64_t* out, int top);
 int orc_ntt_batch(void* c, uint64_t* x, int nrows, int inverse);
 int orc_rotate_batch(void* c, const uint64_t* x, int k, int64_t step, uint64_t* out, int top);
 
+/* ---------------------------------------------------------------- plaintext-operand kernels (linear layers)
+ * out[m][y] = x[m][y] t[y] for nx polynomials of nrows rows ([nx][nrows][N]; t [nrows][N]; row y mod primes[y]) */
+int orc_mul_rows(const uint64_t* x, const uint64_t* t, uint64_t* out, const uint64_t* primes, int nrows, int logn,
+                 int nx);
+/* BSGS plaintext dot: rot [K][bstep][2][nrows][N] -> res [K][gstep][2][nrows][N]; pts [npts][nprow][ptw], grid row y
+ * reads plaintext row prow[y] at the compact index of enc (0xFFFFFFFF: i; 0x7F0000ss: i >> ss; else i & enc) */
+int orc_pt_dot(const uint64_t* rot, uint64_t* res, const uint64_t* pts, const uint64_t* primes, const int32_t* prow,
+               int nrows, int logn, int K, int bstep, int gstep, int npts, int ptw, int nprow, uint32_t enc);
+/* out = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) pts[bstep j + b], bstep j stride), gstep =
+ * ceil(npts / bstep); pts [npts][nq][N] evaluation form; the giant rotations summed in the extended basis */
+int orc_linear_transform(void* c, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
+                         uint64_t* out, int top);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,6 +100,30 @@ class RescaleCombineArgs(C.Structure):
                 ("K", C.c_int32)]
 
 
+class PtDotArgs(C.Structure):
+    _fields_ = [("rot", PolyRef), ("res", PolyRef), ("rot_stride", C.c_uint64), ("res_stride", C.c_uint64),
+                ("pts", vp), ("pr", vp), ("rs", RowSet), ("npts", C.c_int32), ("bstep", C.c_int32),
+                ("gstep", C.c_int32), ("K", C.c_int32), ("ptw", C.c_int32), ("pt_prow", C.c_int32),
+                ("enc", C.c_uint32), ("pad", C.c_int32)]
+
+
+class AddConstArgs(C.Structure):
+    _fields_ = [("x", PolyRef), ("k", vp), ("pr", vp), ("n", C.c_int32), ("K", C.c_int32)]
+
+
+class MulTableArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("in_", PolyRef), ("t", vp), ("pr", vp), ("n", C.c_int32), ("K", C.c_int32)]
+
+
+class MulAddArgs(C.Structure):
+    _fields_ = [("m", MulTableArgs), ("y", PolyRef), ("sub", C.c_int32), ("pad", C.c_int32)]
+
+
+class MulAddNArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("y", PolyRef), ("x", PolyRef * 8), ("t", vp * 8), ("pr", vp), ("n", C.c_int32),
+                ("K", C.c_int32), ("nterm", C.c_int32), ("lazy", C.c_int32)]
+
+
 class AutomorphArgs(C.Structure):
     _fields_ = [("out", PolyRef), ("in_", PolyRef), ("add", PolyRef), ("rs", RowSet), ("pr", vp), ("k", C.c_uint32),
                 ("K", C.c_int32), ("nparts", C.c_int32), ("has_add", C.c_int32)]
@@ -148,7 +172,8 @@ class Params(C.Structure):
 SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJob": 32, "BconvArgs": 56,
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
-         "EncryptArgs": 64, "KskGenArgs": 120, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
+         "EncryptArgs": 64, "KskGenArgs": 120, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
+         "MulAddArgs": 104, "MulAddNArgs": 328, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
 
 _lib = None
 
@@ -197,6 +222,8 @@ def lib():
         "pcb_rotate_hoisted": (C.c_int, [vp, vp, C.POINTER(i64), i32, C.POINTER(vp), i32, i32, vp]),
         "pcb_mult_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_add_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
+        "pcb_mult_pt_add": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+        "pcb_linear_transform": (C.c_int, [vp, vp, vp, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
         "pcb_ntt_batch": (C.c_int, [vp, vp, i32, i32, vp]),
     }

@@ -745,25 +745,37 @@ __global__ void dec_row0(const uint64_t* c0, const uint64_t* c1, const uint64_t*
     out[i] = add_mod(c0[i], mul_mod(c1[i], s[i], pc), pc.p);
 }
 
-template <int LOGN, bool ADD>
-__global__ void pt_op(PcbPolyRef out, PcbPolyRef x, const uint64_t* pt, const PcbPrimeConst* pr) {
+// add_pt: part 0 += pt, part 1 copied (out may be x)
+template <int LOGN>
+__global__ void add_pt_k(PcbPolyRef out, PcbPolyRef x, const uint64_t* pt, const PcbPrimeConst* pr) {
     const int row = blockIdx.y, cc = blockIdx.z >> 1, part = blockIdx.z & 1;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const PcbPrimeConst& pc = pr[row];
     const uint64_t v = at_row(x, cc, part, row, LOGN)[i];
-    const uint64_t w = pt[((size_t)row << LOGN) + i];
-    uint64_t r;
-    if (ADD) r = part == 0 ? add_mod(v, w, pc.p) : v;
-    else r = mul_mod(v, w, pc);
-    at_row_w(out, cc, part, row, LOGN)[i] = r;
+    at_row_w(out, cc, part, row, LOGN)[i] = part == 0 ? add_mod(v, pt[((size_t)row << LOGN) + i], pr[row].p) : v;
 }
 
-template <bool ADD>
-int launch_pt_op(PcbCtx& c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int top, int K, cudaStream_t s) {
+int launch_add_pt(PcbCtx& c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int top, int K, cudaStream_t s) {
     const dim3 g((unsigned)(c.n / 256), top + 1, 2 * K);
-    if (c.logn == 14) pt_op<14, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
-    else pt_op<16, ADD><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
+    if (c.logn == 14) add_pt_k<14><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
+    else add_pt_k<16><<<g, 256, 0, s>>>(ct_ref(c, out), ct_ref(c, x), pt, c.pr);
     return PCB_LAUNCH_RESULT();
+}
+
+// x * pt (or y +- x * pt) over Q rows 0..=top through the mul_table / mul_add launchers
+int launch_mul_pt(PcbCtx& c, const uint64_t* x, const uint64_t* pt, const uint64_t* y, int sub, uint64_t* out, int top,
+                  int K, cudaStream_t s) {
+    PcbMulAddArgs a;
+    memset(&a, 0, sizeof a);
+    a.m.out = ct_ref(c, out);
+    a.m.in = ct_ref(c, x);
+    a.m.t = pt;
+    a.m.pr = c.pr;
+    a.m.n = top + 1;
+    a.m.K = K;
+    if (!y) return c.logn == 14 ? pt::mul_table_launch<14>(&a.m, s) : pt::mul_table_launch<16>(&a.m, s);
+    a.y = ct_ref(c, y);
+    a.sub = sub;
+    return c.logn == 14 ? pt::mul_add_launch<14>(&a, s) : pt::mul_add_launch<16>(&a, s);
 }
 
 }  // namespace
@@ -1384,7 +1396,17 @@ int pcb_mult_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out,
     if (!c || !x || !pt || !out) return fail(PCB_BAD_ARGS, "null argument");
     int rc = check_top(*c, top, K);
     if (rc) return rc;
-    CK(launch_pt_op<false>(*c, x, pt, out, top, K, s));
+    CK(launch_mul_pt(*c, x, pt, nullptr, 0, out, top, K, s));
+    return 0;
+}
+
+int pcb_mult_pt_add(PcbCtx* c, const uint64_t* x, const uint64_t* pt, const uint64_t* y, uint64_t* out, int32_t sub,
+                    int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !x || !pt || !y || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (sub < 0 || sub > 2) return fail(PCB_BAD_ARGS, "sub %d outside [0, 2]", sub);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    CK(launch_mul_pt(*c, x, pt, y, sub, out, top, K, s));
     return 0;
 }
 
@@ -1393,8 +1415,98 @@ int pcb_add_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out, 
     if (!c || !x || !pt || !out) return fail(PCB_BAD_ARGS, "null argument");
     int rc = check_top(*c, top, K);
     if (rc) return rc;
-    CK(launch_pt_op<true>(*c, x, pt, out, top, K, s));
+    CK(launch_add_pt(*c, x, pt, out, top, K, s));
     return 0;
+}
+
+// The BSGS plaintext-matrix product (the LT stage of crates/pc-gpu/src/bts/cts.rs and apply_linear of
+// python/perseus/impl/linear.py, in the baby / giant split of FIDESlib's LTstep):
+//   out = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) pts[bstep j + b], bstep j stride)
+// 1. the bstep - 1 baby rotations hoisted (one ModUp of x), x itself as baby 0;
+// 2. every giant step's baby sum in one pt_dot launch per 8 ciphertexts (the plaintext read once for all of them);
+// 3. the giant rotations' key inner products accumulated in the extended basis (one ModUp each, no ModDown between)
+//    and one ModDown whose epilogue adds giant step 0 (which needs no rotation).
+int pcb_linear_transform(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t npts, int32_t bstep,
+                         int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !x || !pts || !work || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (npts < 1 || bstep < 1 || bstep > 256 || stride == 0)
+        return fail(PCB_BAD_ARGS, "npts %d, bstep %d (1..256), stride %lld", npts, bstep, (long long)stride);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    const int gstep = (npts + bstep - 1) / bstep;
+    const size_t cw = c->ct_words(), kw = (size_t)K * cw;
+    uint64_t* baby = work;
+    uint64_t* res = work + (size_t)bstep * kw;
+    if ((out >= work && out < res + (size_t)gstep * kw) || (x >= work && x < res + (size_t)gstep * kw))
+        return fail(PCB_BAD_ARGS, "x or out inside the workspace");
+    std::vector<const KeySlot*> giant(gstep, nullptr);
+    for (int j = 1; j < gstep; ++j) {
+        const int64_t st = (int64_t)j * bstep * stride;
+        const uint64_t g = rot_galois(*c, st);
+        if (g == 1) return fail(PCB_BAD_ARGS, "giant step %lld is the identity", (long long)st);
+        giant[j] = key_of(*c, g);
+        if (!giant[j]) return fail(-3, "no rotation key for giant step %lld (galois %llu)", (long long)st, (unsigned long long)g);
+    }
+    // 1. babies
+    {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, baby);
+        e.a = ct_ref(*c, x);
+        e.rs.nq = top + 1;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+    }
+    if (bstep > 1) {
+        std::vector<int64_t> steps(bstep - 1);
+        std::vector<uint64_t*> outs(bstep - 1);
+        for (int b = 1; b < bstep; ++b) {
+            steps[b - 1] = (int64_t)b * stride;
+            outs[b - 1] = baby + (size_t)b * kw;
+        }
+        rc = pcb_rotate_hoisted(c, x, steps.data(), bstep - 1, outs.data(), top, K, s);
+        if (rc) return rc;
+    }
+    // 2. baby sums
+    for (int c0 = 0; c0 < K; c0 += 8) {
+        PcbPtDotArgs a;
+        memset(&a, 0, sizeof a);
+        a.rot = ct_ref(*c, baby + (size_t)c0 * cw);
+        a.res = ct_ref(*c, res + (size_t)c0 * cw);
+        a.rot_stride = a.res_stride = kw;
+        a.pts = (const void* const*)pts;
+        a.pr = c->pr;
+        a.rs.nq = top + 1;
+        a.rs.qmax = top + 1;
+        a.npts = npts;
+        a.bstep = bstep;
+        a.gstep = gstep;
+        a.K = std::min(8, K - c0);
+        a.ptw = (int32_t)c->n;
+        a.enc = 0xFFFFFFFFu;
+        CK(c->logn == 14 ? pt::pt_dot_launch<14>(&a, s) : pt::pt_dot_launch<16>(&a, s));
+    }
+    // 3. giant steps
+    if (gstep == 1) {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, out);
+        e.a = ct_ref(*c, res);
+        e.rs.nq = top + 1;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+        return 0;
+    }
+    for (int j = 1; j < gstep; ++j) {
+        const uint64_t* rj = res + (size_t)j * kw;
+        rc = modup(*c, rj + (size_t)c->rows * c->n, top, K, s);
+        if (rc) return rc;
+        rc = dot(*c, *giant[j], rj + (size_t)c->rows * c->n, rj, j == 1 ? 1 : 1 | PCB_KS_ACC, top, K, s);
+        if (rc) return rc;
+    }
+    return moddown(*c, out, false, top, K, s, nullptr, res);
 }
 
 int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaStream_t s) {

@@ -29,6 +29,13 @@ template <int LOGN> int rescale_coef_launch(const PcbRescaleArgs*, cudaStream_t)
 template <int LOGN> int rescale_combine_launch(const PcbRescaleCombineArgs*, cudaStream_t);
 template <int LOGN> int automorph_launch(const PcbAutomorphArgs*, cudaStream_t);
 }  // namespace elem
+namespace pt {
+template <int LOGN> int add_const_launch(const PcbAddConstArgs*, cudaStream_t);
+template <int LOGN> int mul_table_launch(const PcbMulTableArgs*, cudaStream_t);
+template <int LOGN> int mul_add_launch(const PcbMulAddArgs*, cudaStream_t);
+template <int LOGN> int mul_add_n_launch(const PcbMulAddNArgs*, cudaStream_t);
+template <int LOGN> int pt_dot_launch(const PcbPtDotArgs*, cudaStream_t);
+}  // namespace pt
 namespace ks {
 template <int LOGN> int bconv_launch(const PcbBconvArgs*, cudaStream_t);
 template <int LOGN> int ks_dot_launch(const PcbKsArgs*, cudaStream_t);

@@ -27,6 +27,11 @@ PcbKernelTable make_table() {
     t.ks_dot = ks::ks_dot_launch<LOGN>;
     t.ks_dot_regen = no_regen;
     t.ksk_expand = keys::ksk_expand_launch<LOGN>;
+    t.pt_dot = pt::pt_dot_launch<LOGN>;
+    t.add_const = pt::add_const_launch<LOGN>;
+    t.mul_table = pt::mul_table_launch<LOGN>;
+    t.mul_add = pt::mul_add_launch<LOGN>;
+    t.mul_add_n = pt::mul_add_n_launch<LOGN>;
     t.tensor = elem::tensor_launch<LOGN>;
     t.md_epilogue = elem::md_epilogue_launch<LOGN>;
     t.rescale_coef = elem::rescale_coef_launch<LOGN>;

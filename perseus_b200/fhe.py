@@ -113,6 +113,33 @@ class Ct:
         return Ct(self.data.clone(), self.top, self.scale, self.slots)
 
 
+@dataclass
+class Diagonals:
+    """The plaintexts of a BSGS plaintext-matrix product on the device: pts [npts][nq][N] evaluation rows (diagonal
+    d = bstep j + b pre-rotated by -bstep j stride) and the device table of their addresses that pt_dot reads."""
+
+    pts: torch.Tensor
+    table: torch.Tensor
+    bstep: int
+    stride: int
+    top: int
+    scale: float
+    slots: int
+
+    @property
+    def npts(self):
+        return self.pts.shape[0]
+
+    @property
+    def gstep(self):
+        return -(-self.npts // self.bstep)
+
+    def steps(self):
+        """The rotation steps the product needs keys for: the babies b stride and the giants bstep j stride."""
+        return [b * self.stride for b in range(1, self.bstep)] + \
+            [j * self.bstep * self.stride for j in range(1, self.gstep)]
+
+
 class Session:
     """A context over one chain with device-resident keys (relinearization + the given rotation steps)."""
 
@@ -326,6 +353,50 @@ class Session:
         out = Ct(self.empty(a.k), a.top, a.scale * pt_scale, a.slots)
         L.check(L.lib().pcb_mult_pt(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), out.ptr(), a.top, a.k,
                                     self._stream()), "pcb_mult_pt")
+        return out
+
+    def mult_pt_add(self, a, pt, pt_scale, y, sub=0, out=None):
+        """y + a * pt (sub 1: y - a * pt, 2: a * pt - y) in one pass (the reference's mult_pt_add); the product's
+        scale must be y's."""
+        if a.top != y.top or a.k != y.k:
+            raise ValueError(f"operands at tops {a.top} / {y.top}, batches {a.k} / {y.k}")
+        out = out if out is not None else self.ct_like(y)
+        L.check(L.lib().pcb_mult_pt_add(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), y.ptr(), out.ptr(), int(sub),
+                                        a.top, a.k, self._stream()), "pcb_mult_pt_add")
+        return out
+
+    def diagonals(self, diags, bstep, top=None, scale=None, slots=None, stride=1):
+        """Encode the generalized diagonals diag_d (d < npts; slot vectors) of a slots x slots matrix M (diag_d[i] =
+        M[i, i + d stride]) for linear_transform: y = sum_d diag_d * rot(x, d stride). scale defaults to q_top, so
+        one rescale returns the product to x's scale."""
+        top = self.top() if top is None else top
+        diags = [np.asarray(v) for v in diags]
+        slots = slots or len(diags[0])
+        scale = float(self.chain.q[top]) if scale is None else scale
+        pts = torch.zeros((len(diags), self.nq, self.n), dtype=torch.int64, device=self.device)
+        for d, v in enumerate(diags):
+            g = (d // bstep) * bstep * stride
+            rows = self.encode(np.roll(v, g), slots=slots, scale=scale, top=top)
+            L.check(L.lib().pcb_pt_load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(pts[d].data_ptr()),
+                                        self._stream()), "pcb_pt_load")
+        table = torch.tensor([pts[d].data_ptr() for d in range(len(diags))], dtype=torch.int64, device=self.device)
+        return Diagonals(pts, table, int(bstep), int(stride), top, scale, slots)
+
+    def linear_work(self, lt, k=1):
+        """Scratch for linear_transform: (bstep + gstep) k ciphertexts."""
+        return torch.empty(((lt.bstep + lt.gstep) * k, 2, self.rows, self.n), dtype=torch.int64, device=self.device)
+
+    def linear_transform(self, a, lt, out=None, work=None):
+        """The BSGS plaintext-matrix product sum_d diag_d * rot(a, d stride) of a K-batch (hoisted babies, one
+        pt_dot launch, the giant rotations summed in the extended basis with one ModDown). Scale a.scale lt.scale."""
+        if a.top != lt.top:
+            raise ValueError(f"ciphertext at top {a.top}, diagonals encoded at top {lt.top}")
+        out = out if out is not None else Ct(self.empty(a.k), a.top, a.scale * lt.scale, a.slots)
+        work = work if work is not None else self.linear_work(lt, a.k)
+        L.check(L.lib().pcb_linear_transform(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), lt.npts, lt.bstep,
+                                             lt.stride, C.c_void_p(work.data_ptr()), out.ptr(), a.top, a.k,
+                                             self._stream()), "pcb_linear_transform")
+        out.scale = a.scale * lt.scale
         return out
 
     def add_pt(self, a, pt):

@@ -88,6 +88,10 @@ def lib():
         "orc_moddown": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int]),
         "orc_ntt_batch": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int]),
         "orc_rotate_batch": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int64, u64p, C.c_int]),
+        "orc_linear_transform": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_int64, u64p, C.c_int]),
+        "orc_mul_rows": (C.c_int, [u64p, u64p, u64p, u64p, C.c_int, C.c_int, C.c_int]),
+        "orc_pt_dot": (C.c_int, [u64p, u64p, u64p, u64p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                 C.c_int, C.c_int, C.c_int, C.c_uint32]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -107,6 +111,43 @@ def expand_row(seed, w13, p, tag, logn):
     out = np.zeros(1 << logn, np.uint64)
     lib().orc_expand_row_u64(np.asarray(seed, np.uint32), w13, p, tag, logn, out)
     return out
+
+
+def mul_rows(x, t, primes):
+    """x [..., nrows, N] times t [nrows, N] row-wise mod primes[row] (the mul_table product)."""
+    x = np.ascontiguousarray(x, np.uint64)
+    t = np.ascontiguousarray(t, np.uint64)
+    nrows, n = t.shape
+    out = np.empty_like(x)
+    rc = lib().orc_mul_rows(x, t, out, np.asarray(primes, np.uint64), nrows, n.bit_length() - 1, x.size // (nrows * n))
+    assert rc == 0
+    return out
+
+
+def pt_dot(rot, pts, primes, prow, gstep, enc=0xFFFFFFFF):
+    """rot [K][bstep][2][nrows][N], pts [npts][nprow][ptw] -> res [K][gstep][2][nrows][N] (the BSGS plaintext dot)."""
+    rot = np.ascontiguousarray(rot, np.uint64)
+    pts = np.ascontiguousarray(pts, np.uint64)
+    K, bstep, _, nrows, n = rot.shape
+    npts, nprow, ptw = pts.shape
+    res = np.zeros((K, gstep, 2, nrows, n), np.uint64)
+    pr = np.asarray(prow, np.int32)
+    rc = lib().orc_pt_dot(rot, res, pts, np.asarray(primes, np.uint64), pr.ctypes.data, nrows, n.bit_length() - 1, K,
+                          bstep, gstep, npts, ptw, nprow, enc)
+    assert rc == 0
+    return res
+
+
+def add_rows(a, b, primes):
+    """(a + b) mod p row-wise; a, b [..., nrows, N] canonical."""
+    p = np.asarray(primes, np.uint64)[:, None]
+    s = a + b
+    return np.where(s >= p, s - p, s)
+
+
+def sub_rows(a, b, primes):
+    p = np.asarray(primes, np.uint64)[:, None]
+    return np.where(a >= b, a - b, a + (p - b))
 
 
 class Ctx:
@@ -205,6 +246,14 @@ class Ctx:
             rc = lib().orc_rotate_and_sum_radix(self.h, np.ascontiguousarray(ct), start, stop, radix_bits, out, top)
         else:
             rc = lib().orc_rotate_and_sum(self.h, np.ascontiguousarray(ct), start, stop, out, top)
+        assert rc == 0, rc
+        return out
+
+    def linear_transform(self, ct, pts, bstep, stride, top):
+        """BSGS plaintext-matrix product; pts [npts][nq][N] evaluation-form plaintexts (diagonals pre-rotated)."""
+        out = self.ct()
+        pts = np.ascontiguousarray(pts, np.uint64)
+        rc = lib().orc_linear_transform(self.h, np.ascontiguousarray(ct), pts, pts.shape[0], bstep, stride, out, top)
         assert rc == 0, rc
         return out
 

@@ -43,7 +43,36 @@ def test_table_headers():
 
 def test_absent_entries_refuse():
     t = L.kernel_table()
-    assert t.pt_dot(None, None) == -1 and t.ks_dot_regen(None, None) == -1 and t.tfhe(None, None) == -1
+    assert t.ks_dot_regen(None, None) == -1 and t.tfhe(None, None) == -1 and t.pcmm(None, None) == -1
+    assert t.pt_dot(None, None) == -1  # a null argument pointer is refused by every entry
+
+
+def test_plaintext_entries_refuse_out_of_range():
+    """pt_dot K in [1, 8], mul_add_n nterm in [1, 8], mul_add sub in [0, 2] (args.cuh:184-200, :508-528): refused on
+    the host (-1) before any launch; the pointers are fakes that no kernel sees."""
+    t = L.kernel_table()
+    n = 1 << 16
+    a = L.PtDotArgs()
+    a.rot = a.res = L.PolyRef(0x1000, 0, 0)
+    a.pr, a.pts, a.rs = 0x2000, 0x3000, L.RowSet(1, 0, 1, 0)
+    a.npts, a.bstep, a.gstep, a.ptw, a.enc = 1, 1, 1, n, 0xFFFFFFFF
+    for k in (0, 9):
+        a.K = k
+        assert t.pt_dot(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    a.K, a.bstep = 1, 257  # 128-bit sums of at most 256 products
+    assert t.pt_dot(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    m = L.MulAddNArgs()
+    m.out, m.pr, m.n, m.K = L.PolyRef(0x1000, 0, 0), 0x2000, 1, 1
+    for nt in (0, 9):
+        m.nterm = nt
+        assert t.mul_add_n(C.cast(C.pointer(m), C.c_void_p), None) == -1
+    z = L.PolyRef(0x1000, 0, 0)
+    ma = L.MulAddArgs(L.MulTableArgs(z, z, 0x3000, 0x2000, 1, 1), z, 3, 0)
+    assert t.mul_add(C.cast(C.pointer(ma), C.c_void_p), None) == -1
+    mt = L.MulTableArgs(L.PolyRef(0x1008, 0, 0), z, 0x3000, 0x2000, 1, 1)  # misaligned row base
+    assert t.mul_table(C.cast(C.pointer(mt), C.c_void_p), None) == -1
+    ac = L.AddConstArgs(z, None, 0x2000, 1, 1)
+    assert t.add_const(C.cast(C.pointer(ac), C.c_void_p), None) == -1
 
 
 def test_null_arguments_refused_without_launch():

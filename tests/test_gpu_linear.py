@@ -1,0 +1,100 @@
+"""The plaintext-weight linear layer on the GPU against the oracle, word for word: the BSGS plaintext-matrix product
+(hoisted babies, one pt_dot launch, giant rotations summed in the extended basis) and mult_pt_add, on the integer
+chain of config 1, the FP64 path at N = 2^14 and config 2's chain; decrypted results against the generalized
+diagonal method in numpy."""
+import numpy as np
+import pytest
+
+from perseus_b200 import fhe
+from tests import _oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SEED, H, SIGMA = 0, 192, 3.2
+
+
+def host(t):
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+def _session(ch, steps, k_max):
+    s = fhe.Session(ch, rot_steps=steps, k_max=k_max, seed=SEED, h=H, sigma=SIGMA)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(SEED, H, SIGMA, s.galois)
+    return s, o
+
+
+def _lt_steps(bstep, npts, stride=1):
+    return [b * stride for b in range(1, bstep)] + [j * bstep * stride for j in range(1, -(-npts // bstep))]
+
+
+CASES = {
+    # name: (chain, bstep, npts, stride, K)
+    "int14": (fhe.config1_chain, 4, 14, 1, 1),
+    "fp64_14": (lambda: fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 8)), tuple(fhe.ntt_primes(50, 14, 2, skip=8)), 4),
+                4, 16, 2, 2),
+    "config2": (fhe.config2_chain, 8, 30, 1, 1),
+}
+
+
+@pytest.fixture(scope="module", params=sorted(CASES))
+def case(request):
+    mk, bstep, npts, stride, k = CASES[request.param]
+    s, o = _session(mk(), _lt_steps(bstep, npts, stride), k)
+    return request.param, s, o, bstep, npts, stride, k
+
+
+def _oracle_pts(s, o, lt, diags):
+    """The diagonals encoded and transformed by the oracle: they must equal the product's device plaintexts."""
+    top = lt.top
+    pts = np.zeros((len(diags), s.nq, s.n), np.uint64)
+    for d, v in enumerate(diags):
+        g = (d // lt.bstep) * lt.bstep * lt.stride
+        rows = o.encode(np.roll(v, g), lt.slots, lt.scale, top)
+        O.lib().orc_ntt_fwd(rows, top + 1, np.asarray(o.q[: top + 1], np.uint64), s.log_n)
+        pts[d, : top + 1] = rows
+    return pts
+
+
+def test_linear_transform_bit_exact(case):
+    name, s, o, bstep, npts, stride, k = case
+    rng = np.random.default_rng(40)
+    slots = s.n // 2
+    top = s.top()
+    xs = [rng.normal(0, 1, slots) / 4 for _ in range(k)]
+    cts = [s.encrypt(x, top=top, slots=slots) for x in xs]
+    a = s.stack(cts) if k > 1 else cts[0]
+    diags = [rng.normal(0, 1, slots) / 4 for _ in range(npts)]
+    lt = s.diagonals(diags, bstep, top=top, stride=stride)
+    opts = _oracle_pts(s, o, lt, diags)
+    assert (host(lt.pts) == opts).all()
+    out = s.linear_transform(a, lt)
+    for c in range(k):
+        oc = o.encrypt(xs[c], slots, cts[c].scale, top)
+        assert (host(cts[c].data[0])[:, : top + 1] == oc[:, : top + 1]).all()
+        want = o.linear_transform(oc, opts, bstep, stride, top)
+        assert (host(out.data[c])[:, : top + 1] == want[:, : top + 1]).all(), (name, c)
+    s.rescale_one(out)
+    for c in range(k):
+        got = s.decrypt_slots(out, c).real
+        ref = sum(dg * np.roll(xs[c], -d * stride) for d, dg in enumerate(diags))
+        assert np.abs(got - ref).max() < 1e-4, name
+
+
+def test_mult_pt_add_bit_exact(case):
+    name, s, o, *_ = case
+    rng = np.random.default_rng(41)
+    top = s.top()
+    x, y, w = (rng.normal(0, 1, 256) / 4 for _ in range(3))
+    # residue-level parity: the operands' scales need not match for the words to be compared
+    a = s.encrypt(x, top=top)
+    yv = s.encrypt(y, top=top)
+    sc = 2.0**30
+    pt = s.pt(w, top, sc, a.slots)
+    rows = s.encode(w, slots=a.slots, scale=sc, top=top)
+    oa = o.encrypt(x, a.slots, a.scale, top)
+    oy = o.encrypt(y, a.slots, yv.scale, top)
+    prod = o.mult_pt(oa, rows, top)
+    for sub, want in ((0, o.add(oy, prod, top)), (1, o.sub(oy, prod, top)), (2, o.sub(prod, oy, top))):
+        out = s.mult_pt_add(a, pt, sc, yv, sub)
+        assert (host(out.data[0])[:, : top + 1] == want[:, : top + 1]).all(), (name, sub)

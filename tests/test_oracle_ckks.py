@@ -149,3 +149,34 @@ def test_determinism(ctx):
         b1, a1, s1 = ctx.key(i)
         b2, a2, s2 = c2.key(i)
         assert (b1 == b2).all() and (a1 == a2).all() and (s1 == s2).all()
+
+
+def bsgs_diagonals(diags, bstep, stride):
+    """The plaintext vectors of a BSGS product: diagonal d = bstep j + b pre-rotated by -bstep j stride."""
+    return [np.roll(v, (d // bstep) * bstep * stride) for d, v in enumerate(diags)]
+
+
+def eval_pts(ctx, vecs, scale, top):
+    pts = np.zeros((len(vecs), ctx.nq, N), np.uint64)
+    for d, v in enumerate(vecs):
+        rows = ctx.encode(v, SLOTS, scale, top)
+        O.lib().orc_ntt_fwd(rows, top + 1, np.asarray(ctx.q[: top + 1], np.uint64), LOGN)
+        pts[d, : top + 1] = rows
+    return pts
+
+
+@pytest.mark.parametrize("npts,bstep", [(8, 4), (7, 4), (3, 4), (6, 2)])
+def test_linear_transform(ctx_r, npts, bstep):
+    """The BSGS product decrypts to sum_d diag_d * rot(x, d) (the generalized diagonal method), ragged last giant
+    steps and a single giant step included."""
+    top = ctx_r.nq - 1
+    x = vals(18)
+    rng = np.random.default_rng(19)
+    diags = [rng.normal(0, 1, SLOTS) for _ in range(npts)]
+    ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    pscale = float(ctx_r.q[top])
+    pts = eval_pts(ctx_r, bsgs_diagonals(diags, bstep, 1), pscale, top)
+    out = ctx_r.rescale(ctx_r.linear_transform(ct, pts, bstep, 1, top), top)
+    got = ctx_r.decrypt(out, top - 1, SLOTS, SCALE).real
+    want = sum(dg * np.roll(x, -d) for d, dg in enumerate(diags))
+    assert np.abs(got - want).max() < 1e-4

@@ -319,6 +319,7 @@ def run_ours(a):
     del s, x, nbuf, bufs, host_in, host_out, ct, res
     torch.cuda.empty_cache()
     attn, attn_err = attention_decode(a, world, rank, barrier, dist)
+    proj = projection(a, world, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -343,6 +344,7 @@ def run_ours(a):
             "attn_decode_ms_per_token": attn,
             "attn_decode_max_abs_err_vs_fp64": attn_err,
             "plain_rotation_ks_per_s": plain_ks,
+            "projection": proj,
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
@@ -419,6 +421,55 @@ def attention_decode(a, world, rank, barrier, dist):
         del s, caches, qs, cache, q, graph, res
         torch.cuda.empty_cache()
     return out, err
+
+
+def projection(a, world, barrier, dist):
+    """GPT-2's attention projections at config 3's ring (N = 2^16, 24+8 limbs): the Q, K and V linears of one
+    activation (768 of the padded 1024, weights N(0, 0.02), shared prepared input and babies) and the output linear,
+    ms per token with CUDA events (every rank runs the same replica; max over ranks), and the decrypted error against
+    fp64 x W + b."""
+    import numpy as np
+    import torch
+
+    from perseus_b200 import fhe
+    from perseus_b200 import linear as LIN
+
+    ch = fhe.config2_chain()
+    geo = LIN.geometry(ch.n // 2, 1024)
+    radix = 3
+    s = fhe.Session(ch, rot_steps=geo.rot_steps(radix), k_max=1, seed=0)
+    rng = np.random.default_rng(7)
+    n, top = 768, len(ch.q) - 1
+    x = rng.normal(0, 1, n)
+    Ws = [rng.normal(0, 0.02, (n, n)) for _ in range(4)]
+    bs = [rng.normal(0, 0.02, n) for _ in range(4)]
+    xc = s.encrypt(LIN.input_vector(x, geo), top=top, scale=2.0**40, slots=geo.slots)
+    qkv = [LIN.encode(s, W, geo, top, xc.scale, bias=b) for W, b in zip(Ws[:3], bs[:3])]
+    out = LIN.encode(s, Ws[3], geo, top, xc.scale, bias=bs[3])
+    times = []
+    for run in (lambda: LIN.linear_multi(s, xc, qkv, radix), lambda: LIN.linear(s, xc, out, radix)):
+        for _ in range(max(a.warmup, 3)):
+            run()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) / a.steps)
+    t = torch.tensor(times, dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ys = LIN.linear_multi(s, xc, qkv, radix)
+    err = max(float(np.abs(LIN.output_values(s.decrypt_slots(y).real, geo, n) - (x @ W + b)).max())
+              for y, W, b in zip(ys, Ws, bs))
+    del s, qkv, out, xc, ys
+    torch.cuda.empty_cache()
+    return {"workload": "GPT-2 attention projections, one token: Q/K/V linears (768 of 1024, shared input) and the "
+                        "output linear, N=2^16 24+8 limbs, 32 weight plaintexts each (8 baby x 4 giant), radix-3 "
+                        "ladders", "qkv_ms": t[0].item(), "out_ms": t[1].item(), "max_abs_err_vs_fp64": err}
 
 
 def main():

@@ -224,6 +224,7 @@ def lib():
         "pcb_add_pt": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_mult_pt_add": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
         "pcb_linear_transform": (C.c_int, [vp, vp, vp, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
+        "pcb_linear_transform_multi": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
         "pcb_ntt_batch": (C.c_int, [vp, vp, i32, i32, vp]),
     }

@@ -70,20 +70,28 @@ class Layout:
         every step j g (j < 2^n) of each group."""
         steps = []
         for start, stop in self.ladders():
-            sign, gaps = (1 if start > 0 else -1), []
-            g = abs(start)
-            while g < stop:
-                gaps.append(g)
-                g *= 2
-            rb = self.radix_bits if self.radix_bits >= 2 else 1
-            for i0 in range(0, len(gaps), rb):
-                n = min(rb, len(gaps) - i0)
-                if n > 1:
-                    steps += [sign * j * gaps[i0] for j in range(1, 1 << n)]
-                else:
-                    steps.append(sign * gaps[i0])
+            steps += ladder_steps(start, stop, self.radix_bits)
         seen = set()
         return [s for s in steps if not (s in seen or seen.add(s))]
+
+
+def ladder_steps(start, stop, radix_bits=1):
+    """The rotation steps of rotate_and_sum(x, start, stop) (gaps |start| 2^k below stop, signed like start): each
+    gap alone, or with radix_bits >= 2 every step j g (j < 2^n) of each group of n gaps."""
+    sign, gaps = (1 if start > 0 else -1), []
+    g = abs(start)
+    while g < stop:
+        gaps.append(g)
+        g *= 2
+    rb = radix_bits if radix_bits >= 2 else 1
+    steps = []
+    for i0 in range(0, len(gaps), rb):
+        n = min(rb, len(gaps) - i0)
+        if n > 1:
+            steps += [sign * j * gaps[i0] for j in range(1, 1 << n)]
+        else:
+            steps.append(sign * gaps[i0])
+    return steps
 
 
 class KVCache:

@@ -399,6 +399,23 @@ class Session:
         out.scale = a.scale * lt.scale
         return out
 
+    def linear_transform_multi(self, a, lts, work=None):
+        """linear_transform of one input against several diagonal sets of one shape (the babies computed once)."""
+        lt0 = lts[0]
+        for lt in lts:
+            if (lt.npts, lt.bstep, lt.stride, lt.top) != (lt0.npts, lt0.bstep, lt0.stride, lt0.top):
+                raise ValueError("linear_transform_multi: diagonal sets of different shapes")
+        if a.top != lt0.top:
+            raise ValueError(f"ciphertext at top {a.top}, diagonals encoded at top {lt0.top}")
+        outs = [Ct(self.empty(a.k), a.top, a.scale * lt.scale, a.slots) for lt in lts]
+        work = work if work is not None else self.linear_work(lt0, a.k)
+        table = torch.cat([lt.table for lt in lts])
+        ptrs = (C.c_void_p * len(outs))(*[o.data.data_ptr() for o in outs])
+        L.check(L.lib().pcb_linear_transform_multi(self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts),
+                                                   lt0.npts, lt0.bstep, lt0.stride, C.c_void_p(work.data_ptr()), ptrs,
+                                                   a.top, a.k, self._stream()), "pcb_linear_transform_multi")
+        return outs
+
     def add_pt(self, a, pt):
         out = self.ct_like(a)
         L.check(L.lib().pcb_add_pt(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), out.ptr(), a.top, a.k,

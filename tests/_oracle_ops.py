@@ -54,3 +54,32 @@ class OracleOps:
 
     def decrypt_slots(self, a):
         return self.c.decrypt(a.data, a.top, a.slots, a.scale)
+
+    def diagonals(self, diags, bstep, top, scale=None, slots=None, stride=1):
+        """Evaluation-form plaintexts of a BSGS product (diagonal d pre-rotated by -bstep (d // bstep) stride)."""
+        from tests import _oracle as O
+        slots = slots or len(diags[0])
+        scale = float(self.c.q[top]) if scale is None else scale
+        pts = np.zeros((len(diags), self.c.nq, self.c.n), np.uint64)
+        for d, v in enumerate(diags):
+            rows = self.c.encode(np.roll(np.asarray(v), (d // bstep) * bstep * stride), slots, scale, top)
+            O.lib().orc_ntt_fwd(rows, top + 1, np.asarray(self.c.q[: top + 1], np.uint64), self.c.logn)
+            pts[d, : top + 1] = rows
+        return OracleDiagonals(pts, bstep, stride, top, scale)
+
+    def linear_transform(self, a, lt):
+        assert a.top == lt.top
+        out = self.c.linear_transform(a.data, lt.pts, lt.bstep, lt.stride, a.top)
+        return OCt(out, a.top, a.scale * lt.scale, a.slots)
+
+    def linear_transform_multi(self, a, lts):
+        return [self.linear_transform(a, lt) for lt in lts]
+
+
+@dataclass
+class OracleDiagonals:
+    pts: np.ndarray
+    bstep: int
+    stride: int
+    top: int
+    scale: float

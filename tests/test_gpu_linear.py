@@ -98,3 +98,41 @@ def test_mult_pt_add_bit_exact(case):
     for sub, want in ((0, o.add(oy, prod, top)), (1, o.sub(oy, prod, top)), (2, o.sub(prod, oy, top))):
         out = s.mult_pt_add(a, pt, sc, yv, sub)
         assert (host(out.data[0])[:, : top + 1] == want[:, : top + 1]).all(), (name, sub)
+
+
+# ------------------------------------------------------------------------------------------------ projections
+
+from perseus_b200 import linear as LIN  # noqa: E402
+from tests._oracle_ops import OracleOps  # noqa: E402
+
+
+def _fp64_14():
+    return fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 8)), tuple(fhe.ntt_primes(50, 14, 2, skip=8)), 4)
+
+
+@pytest.mark.parametrize("mk,d,n,nw,radix", [(_fp64_14, 256, 200, 1, 1), (_fp64_14, 256, 256, 2, 2),
+                                            (fhe.config2_chain, 1024, 768, 3, 1)])
+def test_projection_bit_exact(mk, d, n, nw, radix):
+    """y = x W + b in the reference's layout, GPU against the same op sequence on the oracle, word for word; the
+    config-2 case is GPT-2's geometry (768 of 1024, 2^15 slots) with three weights sharing the input (Q, K, V)."""
+    ch = mk()
+    geo = LIN.geometry(ch.n // 2, d)
+    s, o = _session(ch, geo.rot_steps(radix), 1)
+    oops = OracleOps(o)
+    rng = np.random.default_rng(d + nw)
+    x = rng.normal(0, 1, n)
+    Ws = [rng.normal(0, 0.02, (n, n)) for _ in range(nw)]
+    bs = [rng.normal(0, 0.02, n) for _ in range(nw)]
+    top = s.top()
+    vec = LIN.input_vector(x, geo)
+    a = s.encrypt(vec, top=top, scale=2.0**40, slots=geo.slots)
+    oa = oops.encrypt(vec, top, 2.0**40, geo.slots)
+    lins = [LIN.encode(s, W, geo, top, a.scale, bias=b) for W, b in zip(Ws, bs)]
+    olins = [LIN.encode(oops, W, geo, top, oa.scale, bias=b) for W, b in zip(Ws, bs)]
+    ys = LIN.linear_multi(s, a, lins, radix) if nw > 1 else [LIN.linear(s, a, lins[0], radix)]
+    oys = LIN.linear_multi(oops, oa, olins, radix) if nw > 1 else [LIN.linear(oops, oa, olins[0], radix)]
+    for w, (y, oy) in enumerate(zip(ys, oys)):
+        assert y.top == oy.top == top - 1
+        assert (host(y.data[0])[:, : y.top + 1] == oy.data[:, : y.top + 1]).all(), w
+        got = LIN.output_values(s.decrypt_slots(y).real, geo, n)
+        assert np.abs(got - (x @ Ws[w] + bs[w])).max() < 1e-3, w

@@ -44,6 +44,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
     ap.add_argument("--profile", action="store_true",
                     help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
+    ap.add_argument("--part", choices=["all", "projection"], default="all",
+                    help="projection: only the GPT-2 projection timing (one GPU; its timed steps in the NVTX range "
+                         "'projection_step', the ncu case)")
     return ap.parse_args()
 
 
@@ -437,7 +440,7 @@ def projection(a, world, barrier, dist):
     ch = fhe.config2_chain()
     geo = LIN.geometry(ch.n // 2, 1024)
     radix = 3
-    s = fhe.Session(ch, rot_steps=geo.rot_steps(radix), k_max=1, seed=0)
+    s = fhe.Session(ch, rot_steps=geo.rot_steps(radix), k_max=3, seed=0)  # Q, K, V run as one batch of 3
     rng = np.random.default_rng(7)
     n, top = 768, len(ch.q) - 1
     x = rng.normal(0, 1, n)
@@ -453,10 +456,12 @@ def projection(a, world, barrier, dist):
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("projection_step")
         e0.record()
         for _ in range(a.steps):
             run()
         e1.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) / a.steps)
     t = torch.tensor(times, dtype=torch.float64, device="cuda")
@@ -474,6 +479,9 @@ def projection(a, world, barrier, dist):
 
 def main():
     a = parse()
+    if a.part == "projection":
+        print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
+        return
     if a.impl == "reference":
         run_reference(a)
     else:

@@ -477,11 +477,12 @@ int pcb_mult_pt_add(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, const ui
 int pcb_linear_transform(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t npts, int32_t bstep,
                          int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K, cudaStream_t stream);
 /* nw weights over the same input (linear_multi of python/perseus/impl/linear.py: Q, K, V of one activation): the
- * babies computed once; weight w's plaintexts at pts[w npts .. w npts + npts - 1], its result in outs[w] (a host
- * array of device pointers; x is not read after the babies, so an output may be x). */
+ * babies computed once; weight w's plaintexts at pts[w npts .. w npts + npts - 1]; out holds nw K ciphertexts,
+ * weight w's results at out + w K (ciphertexts), and the giant rotations run over that one batch (nw K <= k_max).
+ * work: (bstep K + gstep nw K) ciphertexts. x is not read after the babies, so out may hold x. */
 int pcb_linear_transform_multi(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
-                               int32_t bstep, int64_t stride, uint64_t* work, uint64_t* const* outs, int32_t top,
-                               int32_t K, cudaStream_t stream);
+                               int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
+                               cudaStream_t stream);
 
 /* The hybrid key switch of one polynomial per ciphertext (the north star's fused KeySwitcher): ext = dot(ModUp(d))
  * against key `kidx` with c0 mode (0 none, 1 P c0 on Q rows) and output permutation autok, then ModDown into out.

@@ -1422,29 +1422,30 @@ int pcb_add_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out, 
 // The BSGS plaintext-matrix product (the LT stage of crates/pc-gpu/src/bts/cts.rs and apply_linear of
 // python/perseus/impl/linear.py, in the baby / giant split of FIDESlib's LTstep), for nw weights sharing the input
 // (linear_multi of linear.py: the Q, K and V projections of one activation):
-//   outs[w] = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) pts[w npts + bstep j + b], bstep j stride)
+//   out[w] = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) pts[w npts + bstep j + b], bstep j stride)
 // 1. the bstep - 1 baby rotations hoisted (one ModUp of x), x itself as baby 0, shared by every weight;
 // 2. per weight, every giant step's baby sum in one pt_dot launch per 8 ciphertexts (each plaintext read once for
-//    all of them);
-// 3. per weight, the giant rotations' key inner products accumulated in the extended basis (one ModUp each, no
-//    ModDown between) and one ModDown whose epilogue adds giant step 0 (which needs no rotation).
+//    all of them), written as giant step j of batch member w: the nw weights' results of one giant step form one
+//    batch of nw K ciphertexts;
+// 3. the giant rotations over that batch: one ModUp and one key inner product per giant step, accumulated in the
+//    extended basis, then one ModDown whose epilogue adds giant step 0 (which needs no rotation).
 int pcb_linear_transform_multi(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
-                               int32_t bstep, int64_t stride, uint64_t* work, uint64_t* const* outs, int32_t top,
-                               int32_t K, cudaStream_t s) {
-    if (!c || !x || !pts || !work || !outs) return fail(PCB_BAD_ARGS, "null argument");
+                               int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
+                               cudaStream_t s) {
+    if (!c || !x || !pts || !work || !out) return fail(PCB_BAD_ARGS, "null argument");
     if (nw < 1 || npts < 1 || bstep < 1 || bstep > 256 || stride == 0)
         return fail(PCB_BAD_ARGS, "nw %d, npts %d, bstep %d (1..256), stride %lld", nw, npts, bstep, (long long)stride);
     int rc = check_top(*c, top, K);
     if (rc) return rc;
+    const int KW = nw * K;  // the giant stage's batch
+    if (KW > c->k_max) return fail(PCB_BAD_ARGS, "%d weights x %d ciphertexts exceed k_max %d", nw, K, c->k_max);
     const int gstep = (npts + bstep - 1) / bstep;
-    const size_t cw = c->ct_words(), kw = (size_t)K * cw;
+    const size_t cw = c->ct_words(), kw = (size_t)K * cw, gw = (size_t)KW * cw;
     uint64_t* baby = work;
-    uint64_t* res = work + (size_t)bstep * kw;
-    const uint64_t* wend = res + (size_t)gstep * kw;
+    uint64_t* res = work + (size_t)bstep * kw;  // [gstep][nw][K]
+    const uint64_t* wend = res + (size_t)gstep * gw;
     if (x >= work && x < wend) return fail(PCB_BAD_ARGS, "x inside the workspace");
-    for (int w = 0; w < nw; ++w) {
-        if (!outs[w] || (outs[w] >= work && outs[w] < wend)) return fail(PCB_BAD_ARGS, "output %d null or inside the workspace", w);
-    }
+    if (out + gw > work && out < wend) return fail(PCB_BAD_ARGS, "out overlaps the workspace");
     std::vector<const KeySlot*> giant(gstep, nullptr);
     for (int j = 1; j < gstep; ++j) {
         const int64_t st = (int64_t)j * bstep * stride;
@@ -1474,14 +1475,15 @@ int pcb_linear_transform_multi(PcbCtx* c, const uint64_t* x, const uint64_t* con
         rc = pcb_rotate_hoisted(c, x, steps.data(), bstep - 1, bo.data(), top, K, s);
         if (rc) return rc;
     }
-    for (int w = 0; w < nw; ++w) {
-        // 2. baby sums
+    // 2. baby sums
+    for (int w = 0; w < nw; ++w)
         for (int c0 = 0; c0 < K; c0 += 8) {
             PcbPtDotArgs a;
             memset(&a, 0, sizeof a);
             a.rot = ct_ref(*c, baby + (size_t)c0 * cw);
-            a.res = ct_ref(*c, res + (size_t)c0 * cw);
-            a.rot_stride = a.res_stride = kw;
+            a.res = ct_ref(*c, res + (size_t)w * kw + (size_t)c0 * cw);
+            a.rot_stride = kw;
+            a.res_stride = gw;
             a.pts = (const void* const*)(pts + (size_t)w * npts);
             a.pr = c->pr;
             a.rs.nq = top + 1;
@@ -1494,34 +1496,31 @@ int pcb_linear_transform_multi(PcbCtx* c, const uint64_t* x, const uint64_t* con
             a.enc = 0xFFFFFFFFu;
             CK(c->logn == 14 ? pt::pt_dot_launch<14>(&a, s) : pt::pt_dot_launch<16>(&a, s));
         }
-        // 3. giant steps
-        if (gstep == 1) {
-            PcbEwArgs e;
-            memset(&e, 0, sizeof e);
-            e.out = ct_ref(*c, outs[w]);
-            e.a = ct_ref(*c, res);
-            e.rs.nq = top + 1;
-            e.K = K;
-            e.nparts = 2;
-            CK(c->tab->ew_copy(&e, s));
-            continue;
-        }
-        for (int j = 1; j < gstep; ++j) {
-            const uint64_t* rj = res + (size_t)j * kw;
-            rc = modup(*c, rj + (size_t)c->rows * c->n, top, K, s);
-            if (rc) return rc;
-            rc = dot(*c, *giant[j], rj + (size_t)c->rows * c->n, rj, j == 1 ? 1 : 1 | PCB_KS_ACC, top, K, s);
-            if (rc) return rc;
-        }
-        rc = moddown(*c, outs[w], false, top, K, s, nullptr, res);
+    // 3. giant steps over the nw K batch
+    if (gstep == 1) {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, out);
+        e.a = ct_ref(*c, res);
+        e.rs.nq = top + 1;
+        e.K = KW;
+        e.nparts = 2;
+        CK(c->tab->ew_copy(&e, s));
+        return 0;
+    }
+    for (int j = 1; j < gstep; ++j) {
+        const uint64_t* rj = res + (size_t)j * gw;
+        rc = modup(*c, rj + (size_t)c->rows * c->n, top, KW, s);
+        if (rc) return rc;
+        rc = dot(*c, *giant[j], rj + (size_t)c->rows * c->n, rj, j == 1 ? 1 : 1 | PCB_KS_ACC, top, KW, s);
         if (rc) return rc;
     }
-    return 0;
+    return moddown(*c, out, false, top, KW, s, nullptr, res);
 }
 
 int pcb_linear_transform(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t npts, int32_t bstep,
                          int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
-    return pcb_linear_transform_multi(c, x, pts, 1, npts, bstep, stride, work, &out, top, K, s);
+    return pcb_linear_transform_multi(c, x, pts, 1, npts, bstep, stride, work, out, top, K, s);
 }
 
 int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaStream_t s) {

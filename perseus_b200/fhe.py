@@ -382,9 +382,10 @@ class Session:
         table = torch.tensor([pts[d].data_ptr() for d in range(len(diags))], dtype=torch.int64, device=self.device)
         return Diagonals(pts, table, int(bstep), int(stride), top, scale, slots)
 
-    def linear_work(self, lt, k=1):
-        """Scratch for linear_transform: (bstep + gstep) k ciphertexts."""
-        return torch.empty(((lt.bstep + lt.gstep) * k, 2, self.rows, self.n), dtype=torch.int64, device=self.device)
+    def linear_work(self, lt, k=1, nw=1):
+        """Scratch for linear_transform(_multi): (bstep + gstep nw) k ciphertexts."""
+        return torch.empty(((lt.bstep + lt.gstep * nw) * k, 2, self.rows, self.n), dtype=torch.int64,
+                           device=self.device)
 
     def linear_transform(self, a, lt, out=None, work=None):
         """The BSGS plaintext-matrix product sum_d diag_d * rot(a, d stride) of a K-batch (hoisted babies, one
@@ -400,21 +401,27 @@ class Session:
         return out
 
     def linear_transform_multi(self, a, lts, work=None):
-        """linear_transform of one input against several diagonal sets of one shape (the babies computed once)."""
+        """linear_transform of one input against several diagonal sets of one shape: the babies computed once, the
+        giant rotations of all weights run as one batch. Returns one batch: weight w's results are members
+        w k .. w k + k - 1 (split() gives them apart)."""
         lt0 = lts[0]
         for lt in lts:
-            if (lt.npts, lt.bstep, lt.stride, lt.top) != (lt0.npts, lt0.bstep, lt0.stride, lt0.top):
-                raise ValueError("linear_transform_multi: diagonal sets of different shapes")
+            if (lt.npts, lt.bstep, lt.stride, lt.top, lt.scale) != (lt0.npts, lt0.bstep, lt0.stride, lt0.top, lt0.scale):
+                raise ValueError("linear_transform_multi: diagonal sets of different shapes or scales")
         if a.top != lt0.top:
             raise ValueError(f"ciphertext at top {a.top}, diagonals encoded at top {lt0.top}")
-        outs = [Ct(self.empty(a.k), a.top, a.scale * lt.scale, a.slots) for lt in lts]
-        work = work if work is not None else self.linear_work(lt0, a.k)
+        out = Ct(self.empty(len(lts) * a.k), a.top, a.scale * lt0.scale, a.slots)
+        work = work if work is not None else self.linear_work(lt0, a.k, len(lts))
         table = torch.cat([lt.table for lt in lts])
-        ptrs = (C.c_void_p * len(outs))(*[o.data.data_ptr() for o in outs])
         L.check(L.lib().pcb_linear_transform_multi(self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts),
-                                                   lt0.npts, lt0.bstep, lt0.stride, C.c_void_p(work.data_ptr()), ptrs,
-                                                   a.top, a.k, self._stream()), "pcb_linear_transform_multi")
-        return outs
+                                                   lt0.npts, lt0.bstep, lt0.stride, C.c_void_p(work.data_ptr()),
+                                                   out.ptr(), a.top, a.k, self._stream()), "pcb_linear_transform_multi")
+        return out
+
+    def split(self, a, n):
+        """n equal batches of a batch (views, no copies)."""
+        k = a.k // n
+        return [Ct(a.data[i * k:(i + 1) * k], a.top, a.scale, a.slots) for i in range(n)]
 
     def add_pt(self, a, pt):
         out = self.ct_like(a)

@@ -141,8 +141,12 @@ def linear(ops, x, lin, radix_bits=1):
 
 
 def linear_multi(ops, x, lins, radix_bits=1):
-    """One prepared input, one output per weight (linear.py:151-156: K, V and Q of one activation); the babies of
-    the product shared as well."""
+    """One prepared input, one output per weight (linear.py:151-156: K, V and Q of one activation). The babies of the
+    product are shared too, and the weights' results form one batch through the giant rotations, the rescale and the
+    fold; the biases go on per weight."""
     xp = prepare(ops, x, lins[0].geo, radix_bits)
-    ys = ops.linear_transform_multi(xp, [l.lt for l in lins])
-    return [finish(ops, y, l, radix_bits) for y, l in zip(ys, lins)]
+    y = ops.linear_transform_multi(xp, [l.lt for l in lins])
+    y = ops.rescale_one(y)
+    y = ops.rotate_and_sum(y, *lins[0].geo.fold_ladder(), radix_bits)
+    ys = ops.split(y, len(lins))
+    return [ops.add_pt(y, l.bias) if l.bias is not None else y for y, l in zip(ys, lins)]

@@ -29,12 +29,16 @@ class OracleOps:
         return OCt(self.c.mult(a.data, b.data, a.top), a.top, a.scale * b.scale, a.slots)
 
     def rescale_one(self, a):
+        if isinstance(a, OBatch):
+            return OBatch([self.rescale_one(c) for c in a.cts])
         a.data = self.c.rescale(a.data, a.top)
         a.scale /= self.c.q[a.top]
         a.top -= 1
         return a
 
     def rotate_and_sum(self, a, start, stop, radix_bits=1):
+        if isinstance(a, OBatch):
+            return OBatch([self.rotate_and_sum(c, start, stop, radix_bits) for c in a.cts])
         return OCt(self.c.rotate_and_sum(a.data, start, stop, a.top, radix_bits), a.top, a.scale, a.slots)
 
     def rotate_sum(self, a, steps):
@@ -73,7 +77,17 @@ class OracleOps:
         return OCt(out, a.top, a.scale * lt.scale, a.slots)
 
     def linear_transform_multi(self, a, lts):
-        return [self.linear_transform(a, lt) for lt in lts]
+        return OBatch([self.linear_transform(a, lt) for lt in lts])
+
+    def split(self, a, n):
+        assert len(a.cts) == n
+        return list(a.cts)
+
+
+@dataclass
+class OBatch:
+    """A batch of oracle ciphertexts: the batch-taking ops map over its members."""
+    cts: list
 
 
 @dataclass

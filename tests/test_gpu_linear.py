@@ -117,7 +117,7 @@ def test_projection_bit_exact(mk, d, n, nw, radix):
     config-2 case is GPT-2's geometry (768 of 1024, 2^15 slots) with three weights sharing the input (Q, K, V)."""
     ch = mk()
     geo = LIN.geometry(ch.n // 2, d)
-    s, o = _session(ch, geo.rot_steps(radix), 1)
+    s, o = _session(ch, geo.rot_steps(radix), nw)  # the weights' giant steps run as one batch of nw
     oops = OracleOps(o)
     rng = np.random.default_rng(d + nw)
     x = rng.normal(0, 1, n)

@@ -44,9 +44,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
     ap.add_argument("--profile", action="store_true",
                     help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
-    ap.add_argument("--part", choices=["all", "projection"], default="all",
-                    help="projection: only the GPT-2 projection timing (one GPU; its timed steps in the NVTX range "
-                         "'projection_step', the ncu case)")
+    ap.add_argument("--part", choices=["all", "projection", "attention"], default="all",
+                    help="projection / attention: only that timing (one GPU; the timed steps in the NVTX range "
+                         "'projection_step' / 'attention_step', the ncu case)")
     return ap.parse_args()
 
 
@@ -405,10 +405,12 @@ def attention_decode(a, world, rank, barrier, dist):
             torch.cuda.synchronize()
             barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push("attention_step")
             e0.record()
             for _ in range(a.steps):
                 run()
             e1.record()
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             times.append(e0.elapsed_time(e1) / a.steps)
         t = torch.tensor(times, dtype=torch.float64, device="cuda")
@@ -481,6 +483,10 @@ def main():
     a = parse()
     if a.part == "projection":
         print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
+        return
+    if a.part == "attention":
+        ms, err = attention_decode(a, 1, 0, lambda: None, None)
+        print(json.dumps({"part": "attention", "ms_per_token": ms, "max_abs_err_vs_fp64": err}), flush=True)
         return
     if a.impl == "reference":
         run_reference(a)

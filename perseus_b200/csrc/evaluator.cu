@@ -697,6 +697,47 @@ int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, 
     return 0;
 }
 
+// The inner products of up to SUM_KEYS_MAX keys against the same ModUp digits summed into c.ext (FP64 chains, the
+// gather-form kernel): c0_mode 1 adds each key's P sigma(c0), | PCB_KS_ACC adds the batch already in c.ext
+int dot_sum(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, const uint64_t* c0, int c0_mode, int top,
+            int K, cudaStream_t s) {
+    const LevelPlan& l = c.lv[top];
+    const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
+    PcbKsArgs a;
+    memset(&a, 0, sizeof a);
+    a.c1 = c1;
+    a.modup = c.digits;
+    a.c0 = c0;
+    a.out0 = c.ext;
+    a.out1 = c.ext + rn;
+    a.rows = l.ks_rows;
+    a.digit_of = c.digit_of;
+    a.pmod = c.pmod;
+    a.pmods = c.pmods;
+    a.pr = c.pr;
+    a.ct_stride = cw;
+    a.mu_ct_stride = (uint64_t)c.dnum * rn;
+    a.mu_digit_stride = rn;
+    a.out_ct_stride = cw;
+    a.key_digit_stride = rn;
+    a.K = K;
+    a.R = n;
+    a.ndig = l.ndig;
+    a.c0_mode = c0_mode;
+    a.nq = c.nq;
+    a.nrows = top + 1 + c.kp;
+    ks::KeySum kg;
+    memset(&kg, 0, sizeof kg);
+    kg.n = n;
+    for (int r = 0; r < n; ++r) {
+        kg.kb[r] = keys[r]->b;
+        kg.ka[r] = keys[r]->a;
+        kg.g[r] = (uint32_t)keys[r]->galois;
+    }
+    CK(c.logn == 14 ? ks::dot_sum_run<14>(&a, kg, s) : ks::dot_sum_run<16>(&a, kg, s));
+    return 0;
+}
+
 // ModDown of the K cts of one extended-output batch (c.ext by default) into out: epi 1 (out = (x - conv) P^-1) or
 // 2 (out += ...)
 // acc_src: out = acc_src + (x - conv) P^-1 (epi 2 reading acc_src, which may be out itself)
@@ -1335,9 +1376,17 @@ int pcb_rotate_sum(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32_t n
     const uint64_t* c1 = x + (size_t)c->rows * c->n;
     rc = modup(*c, c1, top, K, s);
     if (rc) return rc;
-    for (int i = 0; i < nsteps; ++i) {
-        rc = dot(*c, *keys[i], c1, x, i == 0 ? 1 : 1 | PCB_KS_ACC, top, K, s);
-        if (rc) return rc;
+    if (c->f64) {  // every key's products summed in registers, SUM_KEYS_MAX keys per launch
+        for (int i0 = 0; i0 < nsteps; i0 += ks::SUM_KEYS_MAX) {
+            const int n = std::min(nsteps - i0, ks::SUM_KEYS_MAX);
+            rc = dot_sum(*c, keys.data() + i0, n, c1, x, i0 == 0 ? 1 : 1 | PCB_KS_ACC, top, K, s);
+            if (rc) return rc;
+        }
+    } else {
+        for (int i = 0; i < nsteps; ++i) {
+            rc = dot(*c, *keys[i], c1, x, i == 0 ? 1 : 1 | PCB_KS_ACC, top, K, s);
+            if (rc) return rc;
+        }
     }
     return moddown(*c, out, false, top, K, s, nullptr, x);
 }

@@ -54,6 +54,17 @@ struct KeyGroup {
     int32_t n;
 };
 template <int LOGN> int dot_keys_run(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
+// The keys of a rotate_sum group summed into ONE extended batch (out0 / out1, out_ct_stride), gather form: g[r] is
+// key r's Galois element (its output slot o reads slot automorph_slot(g[r], o)). FP64 form (every prime below 2^50);
+// c0_mode 0 or 1, optionally | PCB_KS_ACC.
+constexpr int SUM_KEYS_MAX = 8;
+struct KeySum {
+    const uint64_t* kb[SUM_KEYS_MAX];
+    const uint64_t* ka[SUM_KEYS_MAX];
+    uint32_t g[SUM_KEYS_MAX];
+    int32_t n;
+};
+template <int LOGN> int dot_sum_run(const PcbKsArgs*, const KeySum&, cudaStream_t);
 // one key, any batch K: key words read once per launch; inputs must not alias outputs
 // f64: every prime below 2^50 (FP64 products)
 template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, cudaStream_t);

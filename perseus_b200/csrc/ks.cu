@@ -601,6 +601,88 @@ __global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
     }
 }
 
+// The inner products of a rotate_sum group (crates/pc-gpu/src/rotate.rs:690-775) in gather form, summed in
+// registers: for every output slot o of row t and ciphertext c,
+//   out0[o] = sum_r ( P c0[i_r] (Q rows) + sum_d x_d[i_r] b_{r,d}[i_r] ),  out1[o] = sum_r sum_d x_d[i_r] a_{r,d}[i_r]
+// with i_r = automorph_slot(g_r, o), the slot the rotation by key r moves to o (the scatter form writes the same
+// sums at automorph_slot(g_r^-1, i)). One launch writes the group's extended batch once, where a chain of
+// accumulate-mode launches reads and rewrites it once per key; the digit words the keys gather from the same row
+// are re-read from L2 (a row of K ciphertexts' digits is a few tens of MB). Ciphertexts in chunks of CB with their
+// sums in registers, one key's words at a time; with PCB_KS_ACC the previous batch is added.
+template <int LOGN, int ND, int CB>
+__global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
+    const uint32_t t = a.rows[blockIdx.y];
+    const uint64_t p = a.pr[t].p;
+    const double pf = to_f(p), pinv = 1.0 / pf;
+    const uint32_t o = blockIdx.x * BX + threadIdx.x;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t row = (size_t)t << LOGN;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    const uint64_t* c0 = (const uint64_t*)a.c0;
+    const bool addc0 = (a.c0_mode & 3) == 1 && (int)t < a.nq;
+    uint64_t pm = 0, pms = 0;
+    if (addc0) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    uint32_t src[SUM_KEYS_MAX];
+#pragma unroll
+    for (int r = 0; r < SUM_KEYS_MAX; ++r) src[r] = r < ks.n ? automorph_slot<LOGN>(ks.g[r], o) : 0;
+    for (int cb = 0; cb < a.K; cb += CB) {
+        double s0[CB], s1[CB];
+#pragma unroll
+        for (int u = 0; u < CB; ++u) s0[u] = s1[u] = 0.0;
+        for (int r = 0; r < ks.n; ++r) {
+            const size_t off = row + src[r];
+            double bw[ND], aw[ND], bq[ND], aq[ND];
+#pragma unroll
+            for (int d = 0; d < ND; ++d) {
+                const uint64_t b = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
+                const uint64_t av = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
+                bw[d] = b > p / 2 ? -to_f(p - b) : to_f(b);
+                aw[d] = av > p / 2 ? -to_f(p - av) : to_f(av);
+                bq[d] = __dmul_rn(bw[d], pinv);
+                aq[d] = __dmul_rn(aw[d], pinv);
+            }
+#pragma unroll
+            for (int u = 0; u < CB; ++u) {
+                const int c = cb + u;
+                if (c < a.K) {
+#pragma unroll
+                    for (int d = 0; d < ND; ++d) {
+                        const double x = to_f(d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + off)
+                                                      : __ldg(mu + (size_t)c * a.mu_ct_stride +
+                                                              (size_t)d * a.mu_digit_stride + off));
+                        s0[u] = __dadd_rn(s0[u], mul_f(x, bw[d], bq[d], pf));
+                        s1[u] = __dadd_rn(s1[u], mul_f(x, aw[d], aq[d], pf));
+                    }
+                    // at most ND <= 4 products since the last reduction: |s| < 9 p < 2^53
+                    s0[u] = red_f(s0[u], pf, pinv);
+                    s1[u] = red_f(s1[u], pf, pinv);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+            const int c = cb + u;
+            if (c < a.K) {
+                uint64_t r0 = canon_f(s0[u], pf, pinv), r1 = canon_f(s1[u], pf, pinv);
+                if (addc0)
+                    for (int r = 0; r < ks.n; ++r)
+                        r0 = add_mod(r0, shoup(__ldg(c0 + (size_t)c * a.ct_stride + row + src[r]), pm, pms, p), p);
+                const size_t ob = (size_t)c * a.out_ct_stride + row + o;
+                if (a.c0_mode & PCB_KS_ACC) {
+                    r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
+                    r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
+                }
+                ((uint64_t*)a.out0)[ob] = r0;
+                ((uint64_t*)a.out1)[ob] = r1;
+            }
+        }
+    }
+}
+
 template <int LOGN, int ND>
 void dot_keys_dispatch(const PcbKsArgs& a, const KeyGroup& kg, dim3 g, cudaStream_t s) {
     switch (kg.n) {
@@ -630,6 +712,29 @@ int dot_keys_run(const PcbKsArgs* ap, const KeyGroup& kg, cudaStream_t s) {
         case 2: dot_keys_dispatch<LOGN, 2>(a, kg, g, s); break;
         case 3: dot_keys_dispatch<LOGN, 3>(a, kg, g, s); break;
         default: dot_keys_dispatch<LOGN, 4>(a, kg, g, s);
+    }
+    return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int dot_sum_run(const PcbKsArgs* ap, const KeySum& ks, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbKsArgs& a = *ap;
+    if (ks.n < 1 || ks.n > SUM_KEYS_MAX || a.K < 0 || a.ndig < 1 || a.ndig > 4 || a.nrows < 0 ||
+        (a.c0_mode & 3) == 2 || (a.c0_mode & 3) == 3 || (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 ||
+        !a.out1 || !a.rows || !a.digit_of || !a.pr)
+        return PCB_BAD_ARGS;
+    for (int r = 0; r < ks.n; ++r)
+        if (!ks.kb[r] || !ks.ka[r] || !(ks.g[r] & 1)) return PCB_BAD_ARGS;
+    if ((a.c0_mode & 3) == 1 && (!a.c0 || !a.pmod || !a.pmods)) return PCB_BAD_ARGS;
+    if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
+    if (a.K == 0 || a.nrows == 0) return 0;
+    const dim3 g((1 << LOGN) / BX, a.nrows);
+    switch (a.ndig) {
+        case 1: dot_sum_f<LOGN, 1, 8><<<g, BX, 0, s>>>(a, ks); break;
+        case 2: dot_sum_f<LOGN, 2, 8><<<g, BX, 0, s>>>(a, ks); break;
+        case 3: dot_sum_f<LOGN, 3, 8><<<g, BX, 0, s>>>(a, ks); break;
+        default: dot_sum_f<LOGN, 4, 8><<<g, BX, 0, s>>>(a, ks);
     }
     return PCB_LAUNCH_RESULT();
 }
@@ -687,6 +792,8 @@ int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
     return PCB_LAUNCH_RESULT();
 }
 
+template int dot_sum_run<14>(const PcbKsArgs*, const KeySum&, cudaStream_t);
+template int dot_sum_run<16>(const PcbKsArgs*, const KeySum&, cudaStream_t);
 template int dot_keys_run<14>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
 template int dot_keys_run<16>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
 template int dot_all_run<14>(const PcbKsArgs*, bool, bool, cudaStream_t);

@@ -607,80 +607,100 @@ __global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
 // with i_r = automorph_slot(g_r, o), the slot the rotation by key r moves to o (the scatter form writes the same
 // sums at automorph_slot(g_r^-1, i)). One launch writes the group's extended batch once, where a chain of
 // accumulate-mode launches reads and rewrites it once per key; the digit words the keys gather from the same row
-// are re-read from L2 (a row of K ciphertexts' digits is a few tens of MB). Ciphertexts in chunks of CB with their
-// sums in registers, one key's words at a time; with PCB_KS_ACC the previous batch is added.
+// are re-read from L2 (a row of K ciphertexts' digits is a few tens of MB).
+struct SumRow {
+    uint32_t t;
+    size_t row;
+    int dt;
+    uint64_t p, pm, pms;
+    double pf, pinv;
+    bool addc0;
+};
+
+// CB ciphertexts from cb: per key, its 2 ND words and the CB x ND digit words are all loaded before any product (no
+// predicate between them), so each key costs one memory latency instead of one per ciphertext
 template <int LOGN, int ND, int CB>
-__global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
-    const uint32_t t = a.rows[blockIdx.y];
-    const uint64_t p = a.pr[t].p;
-    const double pf = to_f(p), pinv = 1.0 / pf;
-    const uint32_t o = blockIdx.x * BX + threadIdx.x;
-    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
-    const size_t row = (size_t)t << LOGN;
+__device__ __forceinline__ void dot_sum_chunk(const PcbKsArgs& a, const KeySum& ks, const SumRow& w,
+                                              const uint32_t* src, uint32_t o, int cb) {
     const uint64_t* c1 = (const uint64_t*)a.c1;
     const uint64_t* mu = (const uint64_t*)a.modup;
-    const uint64_t* c0 = (const uint64_t*)a.c0;
-    const bool addc0 = (a.c0_mode & 3) == 1 && (int)t < a.nq;
-    uint64_t pm = 0, pms = 0;
-    if (addc0) {
-        pm = ((const uint64_t*)a.pmod)[t];
-        pms = ((const uint64_t*)a.pmods)[t];
+    double s0[CB], s1[CB];
+#pragma unroll
+    for (int u = 0; u < CB; ++u) s0[u] = s1[u] = 0.0;
+    for (int r = 0; r < ks.n; ++r) {
+        const size_t off = w.row + src[r];
+        uint64_t kbv[ND], kav[ND], xw[CB][ND];
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            kbv[d] = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
+            kav[d] = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
+        }
+#pragma unroll
+        for (int u = 0; u < CB; ++u)
+#pragma unroll
+            for (int d = 0; d < ND; ++d)
+                xw[u][d] = __ldg(d == w.dt ? c1 + (size_t)(cb + u) * a.ct_stride + off
+                                           : mu + (size_t)(cb + u) * a.mu_ct_stride + (size_t)d * a.mu_digit_stride + off);
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            const double bw = kbv[d] > w.p / 2 ? -to_f(w.p - kbv[d]) : to_f(kbv[d]);
+            const double aw = kav[d] > w.p / 2 ? -to_f(w.p - kav[d]) : to_f(kav[d]);
+            const double bq = __dmul_rn(bw, w.pinv), aq = __dmul_rn(aw, w.pinv);
+#pragma unroll
+            for (int u = 0; u < CB; ++u) {
+                const double x = to_f(xw[u][d]);
+                s0[u] = __dadd_rn(s0[u], mul_f(x, bw, bq, w.pf));
+                s1[u] = __dadd_rn(s1[u], mul_f(x, aw, aq, w.pf));
+            }
+        }
+        // at most ND <= 4 products since the last reduction: |s| < 9 p < 2^53
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+            s0[u] = red_f(s0[u], w.pf, w.pinv);
+            s1[u] = red_f(s1[u], w.pf, w.pinv);
+        }
     }
+    const uint64_t* c0 = (const uint64_t*)a.c0;
+#pragma unroll
+    for (int u = 0; u < CB; ++u) {
+        const int c = cb + u;
+        uint64_t r0 = canon_f(s0[u], w.pf, w.pinv), r1 = canon_f(s1[u], w.pf, w.pinv);
+        if (w.addc0)
+            for (int r = 0; r < ks.n; ++r)
+                r0 = add_mod(r0, shoup(__ldg(c0 + (size_t)c * a.ct_stride + w.row + src[r]), w.pm, w.pms, w.p), w.p);
+        const size_t ob = (size_t)c * a.out_ct_stride + w.row + o;
+        if (a.c0_mode & PCB_KS_ACC) {
+            r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], w.p);
+            r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], w.p);
+        }
+        ((uint64_t*)a.out0)[ob] = r0;
+        ((uint64_t*)a.out1)[ob] = r1;
+    }
+}
+
+// Ciphertexts in chunks of CB (then one at a time for the rest); with PCB_KS_ACC the previous batch is added
+template <int LOGN, int ND, int CB>
+__global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
+    SumRow w;
+    w.t = a.rows[blockIdx.y];
+    w.p = a.pr[w.t].p;
+    w.pf = to_f(w.p);
+    w.pinv = 1.0 / w.pf;
+    w.dt = (int)w.t < a.nq ? a.digit_of[w.t] : -1;
+    w.row = (size_t)w.t << LOGN;
+    w.addc0 = (a.c0_mode & 3) == 1 && (int)w.t < a.nq;
+    w.pm = w.pms = 0;
+    if (w.addc0) {
+        w.pm = ((const uint64_t*)a.pmod)[w.t];
+        w.pms = ((const uint64_t*)a.pmods)[w.t];
+    }
+    const uint32_t o = blockIdx.x * BX + threadIdx.x;
     uint32_t src[SUM_KEYS_MAX];
 #pragma unroll
     for (int r = 0; r < SUM_KEYS_MAX; ++r) src[r] = r < ks.n ? automorph_slot<LOGN>(ks.g[r], o) : 0;
-    for (int cb = 0; cb < a.K; cb += CB) {
-        double s0[CB], s1[CB];
-#pragma unroll
-        for (int u = 0; u < CB; ++u) s0[u] = s1[u] = 0.0;
-        for (int r = 0; r < ks.n; ++r) {
-            const size_t off = row + src[r];
-            double bw[ND], aw[ND], bq[ND], aq[ND];
-#pragma unroll
-            for (int d = 0; d < ND; ++d) {
-                const uint64_t b = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
-                const uint64_t av = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
-                bw[d] = b > p / 2 ? -to_f(p - b) : to_f(b);
-                aw[d] = av > p / 2 ? -to_f(p - av) : to_f(av);
-                bq[d] = __dmul_rn(bw[d], pinv);
-                aq[d] = __dmul_rn(aw[d], pinv);
-            }
-#pragma unroll
-            for (int u = 0; u < CB; ++u) {
-                const int c = cb + u;
-                if (c < a.K) {
-#pragma unroll
-                    for (int d = 0; d < ND; ++d) {
-                        const double x = to_f(d == dt ? __ldg(c1 + (size_t)c * a.ct_stride + off)
-                                                      : __ldg(mu + (size_t)c * a.mu_ct_stride +
-                                                              (size_t)d * a.mu_digit_stride + off));
-                        s0[u] = __dadd_rn(s0[u], mul_f(x, bw[d], bq[d], pf));
-                        s1[u] = __dadd_rn(s1[u], mul_f(x, aw[d], aq[d], pf));
-                    }
-                    // at most ND <= 4 products since the last reduction: |s| < 9 p < 2^53
-                    s0[u] = red_f(s0[u], pf, pinv);
-                    s1[u] = red_f(s1[u], pf, pinv);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < CB; ++u) {
-            const int c = cb + u;
-            if (c < a.K) {
-                uint64_t r0 = canon_f(s0[u], pf, pinv), r1 = canon_f(s1[u], pf, pinv);
-                if (addc0)
-                    for (int r = 0; r < ks.n; ++r)
-                        r0 = add_mod(r0, shoup(__ldg(c0 + (size_t)c * a.ct_stride + row + src[r]), pm, pms, p), p);
-                const size_t ob = (size_t)c * a.out_ct_stride + row + o;
-                if (a.c0_mode & PCB_KS_ACC) {
-                    r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
-                    r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
-                }
-                ((uint64_t*)a.out0)[ob] = r0;
-                ((uint64_t*)a.out1)[ob] = r1;
-            }
-        }
-    }
+    int cb = 0;
+    for (; cb + CB <= a.K; cb += CB) dot_sum_chunk<LOGN, ND, CB>(a, ks, w, src, o, cb);
+    for (; cb < a.K; ++cb) dot_sum_chunk<LOGN, ND, 1>(a, ks, w, src, o, cb);
 }
 
 template <int LOGN, int ND>
@@ -731,10 +751,10 @@ int dot_sum_run(const PcbKsArgs* ap, const KeySum& ks, cudaStream_t s) {
     if (a.K == 0 || a.nrows == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.nrows);
     switch (a.ndig) {
-        case 1: dot_sum_f<LOGN, 1, 8><<<g, BX, 0, s>>>(a, ks); break;
-        case 2: dot_sum_f<LOGN, 2, 8><<<g, BX, 0, s>>>(a, ks); break;
-        case 3: dot_sum_f<LOGN, 3, 8><<<g, BX, 0, s>>>(a, ks); break;
-        default: dot_sum_f<LOGN, 4, 8><<<g, BX, 0, s>>>(a, ks);
+        case 1: dot_sum_f<LOGN, 1, 4><<<g, BX, 0, s>>>(a, ks); break;
+        case 2: dot_sum_f<LOGN, 2, 4><<<g, BX, 0, s>>>(a, ks); break;
+        case 3: dot_sum_f<LOGN, 3, 4><<<g, BX, 0, s>>>(a, ks); break;
+        default: dot_sum_f<LOGN, 4, 4><<<g, BX, 0, s>>>(a, ks);
     }
     return PCB_LAUNCH_RESULT();
 }

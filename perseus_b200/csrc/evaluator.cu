@@ -60,7 +60,7 @@ struct Arena {
 };
 
 struct LevelPlan {
-    int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0, mu_ns = 0;  // mu_ns: limbs of every live digit (0: mixed)
+    int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0, mu_ns = 0;  // mu_ns: limbs of every live digit (< 0: mixed, -max)
     // ModUp: INTT rows (out of place, last pass x N^-1 pre_t), conversion jobs, NTT of the targets
     uint32_t *mu_intt_roff = nullptr, *mu_intt_soff = nullptr;
     int32_t* mu_intt_rprime = nullptr;
@@ -341,9 +341,14 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             for (int j = 0; j < kp; ++j) tgt[d].push_back(nq + j);
             l.mu_max_tgt = std::max(l.mu_max_tgt, (int)tgt[d].size());
         }
-        l.mu_ns = (int)src[0].size();
-        for (int d = 1; d < l.ndig; ++d)
-            if ((int)src[d].size() != l.mu_ns) l.mu_ns = 0;
+        // the digits' common limb count, or minus the largest when they differ (a partial top digit)
+        int ns_max = 0;
+        bool same = true;
+        for (int d = 0; d < l.ndig; ++d) {
+            ns_max = std::max(ns_max, (int)src[d].size());
+            same = same && src[d].size() == src[0].size();
+        }
+        l.mu_ns = same ? ns_max : -ns_max;
         l.mu_rows = 0;
         for (int d = 0; d < l.ndig; ++d) l.mu_rows += (int)tgt[d].size();
         std::vector<uint64_t> pool;

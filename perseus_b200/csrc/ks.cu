@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
         }
         bmod = rbw + ns;
     }
-    if (NARROW) {
+    if constexpr (NARROW) {
         uint32_t y1[S], y0[S];
 #pragma unroll
         for (int i = 0; i < S; ++i) {
@@ -132,17 +132,17 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
             if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
             dst[(size_t)sRow[t] << LOGN] = r;
         }
-        return;
-    }
-    for (int t = 0; t < nt; ++t) {
-        Acc acc{0, 0};
+    } else {
+        for (int t = 0; t < nt; ++t) {
+            Acc acc{0, 0};
 #pragma unroll
-        for (int i = 0; i < S; ++i)
-            if (NS > 0 || i < ns) mac(acc, y[i], sM[i * nt + t]);
-        const uint64_t p = sP[t];
-        uint64_t r = reduce(acc, p, sM0[t], sM1[t]);
-        if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
-        dst[(size_t)sRow[t] << LOGN] = r;
+            for (int i = 0; i < S; ++i)
+                if (NS > 0 || i < ns) mac(acc, y[i], sM[i * nt + t]);
+            const uint64_t p = sP[t];
+            uint64_t r = reduce(acc, p, sM0[t], sM1[t]);
+            if (bmod) r = sub_mod(r, reduce(mul_wide(u, bmod[t]), p, sM0[t], sM1[t]), p);
+            dst[(size_t)sRow[t] << LOGN] = r;
+        }
     }
 }
 
@@ -152,9 +152,10 @@ __global__ void __launch_bounds__(BX) bconv(PcbBconvArgs a) {
 // memory as {M, M / t} pairs. Exact (HPS) jobs take their correction through the integer Barrett step.
 // 128-coefficient spans per CTA: the shared tables are built once for all of them (2 and 8 measured the same)
 constexpr int BCONV_F_SPAN = 4;
+// NS > 0: every job has NS sources; NS < 0: at most -NS (a mixed launch of short digits); 0: any count up to MAX_SRC
 template <int LOGN, int NS>
 __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
-    constexpr int S = NS > 0 ? NS : MAX_SRC;
+    constexpr int S = NS > 0 ? NS : NS < 0 ? -NS : MAX_SRC;
     __shared__ double2 sM[MAX_SRC * MAX_TGT];
     __shared__ double2 sP[MAX_TGT];  // {t, fl(1 / t)}
     __shared__ uint32_t sRow[MAX_TGT];
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(BX) bconv_f(PcbBconvArgs a) {
     const uint64_t* pool = (const uint64_t*)a.pool + j.pool_off;
     const int ns = NS > 0 ? NS : (int)j.nsrc, nt = (int)j.ntgt;
     // outside the kernel's job shape: nothing is written
-    if (ns < 1 || ns > MAX_SRC || nt > MAX_TGT || (int)j.nsrc != ns) return;
+    if (ns < 1 || ns > S || nt > MAX_TGT || (int)j.nsrc != ns) return;
     const uint64_t* srow = pool;
     const uint64_t* sprime = pool + ns;
     const uint64_t* pre = pool + 2 * ns;
@@ -241,7 +242,9 @@ void bconv_dispatch_f(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s)
         case 2: bconv_f<LOGN, 2><<<g, BX, 0, s>>>(a); break;
         case 4: bconv_f<LOGN, 4><<<g, BX, 0, s>>>(a); break;
         case 8: bconv_f<LOGN, 8><<<g, BX, 0, s>>>(a); break;
-        default: bconv_f<LOGN, 0><<<g, BX, 0, s>>>(a);
+        default:
+            if (ns_all < 0 && ns_all >= -8) bconv_f<LOGN, -8><<<g, BX, 0, s>>>(a);
+            else bconv_f<LOGN, 0><<<g, BX, 0, s>>>(a);
     }
 }
 
@@ -256,7 +259,8 @@ void bconv_dispatch(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
     }
 }
 
-// ns_all: the source count every job of the launch shares (1, 2, 4 or 8 get unrolled kernels), 0 when they differ
+// ns_all: the source count every job of the launch shares (1, 2, 4 or 8 get unrolled kernels); when they differ, minus
+// the largest (FP64: up to 8 sources get an 8-wide kernel) or 0
 template <int LOGN>
 int bconv_run(const PcbBconvArgs* ap, bool narrow, bool f64, int ns_all, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;

@@ -203,25 +203,29 @@ int md_epilogue_launch(const PcbMdEpiArgs* ap, cudaStream_t s) {
 // ------------------------------------------------------------------------------------------------ rescale
 // ndrop 1 (the u64 chains here have one prime per level): tmp_i = A_i lift(y_top) with lift(y) = y - q_top when
 // y > q_top / 2, reduced mod q_i (crates/pc-host/src/rescale.rs:54-70)
+// two consecutive words per thread, one row per grid row (the top word is re-read per row from L2)
 template <int LOGN>
 __global__ void __launch_bounds__(BX) rescale_coef(PcbRescaleArgs a) {
-    const int c = blockIdx.z >> 1, part = blockIdx.z & 1;
-    const size_t i = (size_t)blockIdx.x * BX + threadIdx.x;
+    const int c = blockIdx.z >> 1, part = blockIdx.z & 1, row = blockIdx.y;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * 2;
     const PcbPrimeConst& pa = a.pr[a.top];
     const uint64_t qa = pa.p;
-    uint64_t ya = at_row(a.x, c, part, a.top, LOGN)[i];
-    if (a.ca != 1) ya = mul_mod(ya, a.ca, pa);
-    const bool neg = ya > (qa >> 1);
-    const uint64_t* Av = (const uint64_t*)a.A;
-    const uint64_t* As = (const uint64_t*)a.As;
-    const uint64_t* qam = (const uint64_t*)a.qam;
-    for (int row = blockIdx.y; row < a.nrows; row += gridDim.y) {
-        const PcbPrimeConst& pq = a.pr[row];
-        const uint64_t q = pq.p;
-        uint64_t l = ya < q ? ya : (ya < 2 * q ? ya - q : reduce(Acc{ya, 0}, pq));
-        if (neg) l = sub_mod(l, qam[row], q);
-        at_row_w(a.tmp, c, part, row, LOGN)[i] = shoup(l, Av[row], As[row], q);
+    const ulonglong2 yv = *(const ulonglong2*)(at_row(a.x, c, part, a.top, LOGN) + i);
+    uint64_t ya[2] = {yv.x, yv.y};
+    const PcbPrimeConst& pq = a.pr[row];
+    const uint64_t q = pq.p;
+    const uint64_t A = ((const uint64_t*)a.A)[row], As = ((const uint64_t*)a.As)[row];
+    const uint64_t qm = ((const uint64_t*)a.qam)[row];
+    uint64_t r[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (a.ca != 1) ya[h] = mul_mod(ya[h], a.ca, pa);
+        const bool neg = ya[h] > (qa >> 1);
+        uint64_t l = ya[h] < q ? ya[h] : (ya[h] < 2 * q ? ya[h] - q : reduce(Acc{ya[h], 0}, pq));
+        if (neg) l = sub_mod(l, qm, q);
+        r[h] = shoup(l, A, As, q);
     }
+    *(ulonglong2*)(at_row_w(a.tmp, c, part, row, LOGN) + i) = make_ulonglong2(r[0], r[1]);
 }
 
 template <int LOGN>
@@ -231,9 +235,9 @@ int rescale_coef_launch(const PcbRescaleArgs* ap, cudaStream_t s) {
     if (a.ndrop != 1) return PCB_BAD_ARGS;  // two-prime (composite) levels are not part of the u64 chains here
     if (a.top < 1 || a.nrows < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.A || !a.As || !a.qam)
         return PCB_BAD_ARGS;
+    if (!ok16(a.x) || !ok16(a.tmp)) return PCB_BAD_ARGS;
     if (a.nrows == 0 || a.K == 0) return 0;
-    const int gy = a.nrows < 8 ? a.nrows : 8;
-    rescale_coef<LOGN><<<dim3((1 << LOGN) / BX, gy, 2 * a.K), BX, 0, s>>>(a);
+    rescale_coef<LOGN><<<dim3((1 << LOGN) / (BX * 2), a.nrows, 2 * a.K), BX, 0, s>>>(a);
     return PCB_LAUNCH_RESULT();
 }
 

@@ -61,6 +61,9 @@ struct Arena {
 
 struct LevelPlan {
     int top = 0, ndig = 0, mu_rows = 0, mu_max_tgt = 0, mu_ns = 0;  // mu_ns: limbs of every live digit (< 0: mixed, -max)
+    // FP64 chains with a partial top digit: the jobs are stored full digits first (mu_ns limbs each), the partial
+    // digit's (mu_part_ns limbs) after all of them, and ModUp converts them in two launches of exact source counts
+    int mu_part_ns = 0;
     // ModUp: INTT rows (out of place, last pass x N^-1 pre_t), conversion jobs, NTT of the targets
     uint32_t *mu_intt_roff = nullptr, *mu_intt_soff = nullptr;
     int32_t* mu_intt_rprime = nullptr;
@@ -349,6 +352,15 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             same = same && src[d].size() == src[0].size();
         }
         l.mu_ns = same ? ns_max : -ns_max;
+        l.mu_part_ns = 0;
+        if (!same && c.f64 && l.ndig >= 2) {
+            bool full_same = true;
+            for (int d = 0; d + 1 < l.ndig; ++d) full_same = full_same && src[d].size() == src[0].size();
+            if (full_same && src[l.ndig - 1].size() < src[0].size()) {
+                l.mu_ns = (int)src[0].size();
+                l.mu_part_ns = (int)src[l.ndig - 1].size();
+            }
+        }
         l.mu_rows = 0;
         for (int d = 0; d < l.ndig; ++d) l.mu_rows += (int)tgt[d].size();
         std::vector<uint64_t> pool;
@@ -412,7 +424,7 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
         CK(upload(l.mu_intt_rprime, rp, s));
         CK(upload(l.mu_intt_es, es, s));
         CK(upload(l.mu_intt_ess, ess, s));
-        std::vector<PcbBconvJob> jobs;
+        std::vector<PcbBconvJob> jobs, part;
         std::vector<uint32_t> nro;
         std::vector<int32_t> nrp;
         for (int cc = 0; cc < km; ++cc)
@@ -426,12 +438,13 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
                 j.exact = 0;
                 j.prescaled = 1;
                 j.split = 0;
-                jobs.push_back(j);
+                (l.mu_part_ns && d == l.ndig - 1 ? part : jobs).push_back(j);
                 for (int t : tgt[d]) {
                     nro.push_back(j.dst_off + (uint32_t)t);
                     nrp.push_back(t);
                 }
             }
+        jobs.insert(jobs.end(), part.begin(), part.end());
         CK(upload(l.mu_jobs, jobs, s));
         CK(upload(l.mu_pool, pool, s));
         CK(upload(l.mu_ntt_roff, nro, s));
@@ -614,7 +627,16 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
     b.pr = c.pr;
     b.njobs = K * l.ndig;
     b.max_tgt = l.mu_max_tgt;
-    CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, l.mu_ns, s));
+    if (l.mu_part_ns) {  // the full digits, then the partial top digit, each at its exact source count
+        b.njobs = K * (l.ndig - 1);
+        CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, l.mu_ns, s));
+        b.jobs = l.mu_jobs + (size_t)c.k_max * (l.ndig - 1);
+        b.njobs = K;
+        CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, l.mu_part_ns, s)
+                        : ks::bconv_run<16>(&b, c.narrow, c.f64, l.mu_part_ns, s));
+    } else {
+        CK(c.logn == 14 ? ks::bconv_run<14>(&b, c.narrow, c.f64, l.mu_ns, s) : ks::bconv_run<16>(&b, c.narrow, c.f64, l.mu_ns, s));
+    }
     PcbNttArgs f = ntt_args(c, c.digits, l.mu_ntt_roff, l.mu_ntt_rprime, K * l.mu_rows);
     CK(ntt_fwd(c, &f, s));
     return 0;

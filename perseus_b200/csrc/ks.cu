@@ -240,7 +240,11 @@ void bconv_dispatch_f(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s)
     switch (ns_all) {
         case 1: bconv_f<LOGN, 1><<<g, BX, 0, s>>>(a); break;
         case 2: bconv_f<LOGN, 2><<<g, BX, 0, s>>>(a); break;
+        case 3: bconv_f<LOGN, 3><<<g, BX, 0, s>>>(a); break;
         case 4: bconv_f<LOGN, 4><<<g, BX, 0, s>>>(a); break;
+        case 5: bconv_f<LOGN, 5><<<g, BX, 0, s>>>(a); break;
+        case 6: bconv_f<LOGN, 6><<<g, BX, 0, s>>>(a); break;
+        case 7: bconv_f<LOGN, 7><<<g, BX, 0, s>>>(a); break;
         case 8: bconv_f<LOGN, 8><<<g, BX, 0, s>>>(a); break;
         default:
             if (ns_all < 0 && ns_all >= -8) bconv_f<LOGN, -8><<<g, BX, 0, s>>>(a);
@@ -259,8 +263,8 @@ void bconv_dispatch(const PcbBconvArgs& a, int ns_all, dim3 g, cudaStream_t s) {
     }
 }
 
-// ns_all: the source count every job of the launch shares (1, 2, 4 or 8 get unrolled kernels); when they differ, minus
-// the largest (FP64: up to 8 sources get an 8-wide kernel) or 0
+// ns_all: the source count every job of the launch shares (unrolled kernels: FP64 1 .. 8, integer 1, 2, 4, 8); when
+// they differ, minus the largest (FP64: up to 8 sources get an 8-wide kernel) or 0
 template <int LOGN>
 int bconv_run(const PcbBconvArgs* ap, bool narrow, bool f64, int ns_all, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;

@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
     ap.add_argument("--profile", action="store_true",
                     help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
-    ap.add_argument("--part", choices=["all", "projection", "attention"], default="all",
+    ap.add_argument("--part", choices=["all", "projection", "attention", "block"], default="all",
                     help="projection / attention: only that timing (one GPU; the timed steps in the NVTX range "
                          "'projection_step' / 'attention_step', the ncu case)")
     return ap.parse_args()
@@ -323,6 +323,7 @@ def run_ours(a):
     torch.cuda.empty_cache()
     attn, attn_err = attention_decode(a, world, rank, barrier, dist)
     proj = projection(a, world, barrier, dist)
+    blk = block_decode(a, world, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -348,6 +349,7 @@ def run_ours(a):
             "attn_decode_max_abs_err_vs_fp64": attn_err,
             "plain_rotation_ks_per_s": plain_ks,
             "projection": proj,
+            "attention_block": blk,
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
@@ -479,10 +481,72 @@ def projection(a, world, barrier, dist):
                         "ladders", "qkv_ms": t[0].item(), "out_ms": t[1].item(), "max_abs_err_vs_fp64": err}
 
 
+def block_decode(a, world, barrier, dist):
+    """Config 3's attention block, one token per step: Q/K/V projections of the activation, the token's K and V pushed
+    into the lane cache (128 tokens in 4 blocks of 32, all 12 heads per block), attention over the cache, output
+    projection (perseus_b200.block; N = 2^16 with the 24-limb chain, weights N(0, 0.02), biases, activation N(0, 1)).
+    The cache starts with client-encrypted tokens and grows by one per step up to its 128; ms per token with CUDA events (every
+    rank runs the same replica; max over ranks), and the last step's decrypted error against the fp64 step."""
+    import numpy as np
+    import torch
+
+    from perseus_b200 import attention as A
+    from perseus_b200 import block as B
+    from perseus_b200 import fhe
+
+    ch = fhe.config2_chain()
+    lay = B.layout(ch.n // 2, 1024, heads=12, head_dim=64, tokens=128, radix_bits=3)
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=4, seed=0)
+    rng = np.random.default_rng(11)
+    warm, steps = max(a.warmup, 3), min(a.steps, 64)  # the cache holds 128 tokens: the steps fill its last lanes
+    n, pre, top = 768, lay.tokens - warm - steps, len(ch.q) - 1
+    w = B.Weights(*[rng.normal(0, 0.02, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+    cache = B.LaneCache(s, lay, top - 2)
+    cache.load(K, V)
+    coeffs = A.softmax_poly(lay.tokens)
+    xs = [rng.normal(0, 1, n) for _ in range(warm + steps)]
+    cts = [s.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots) for x in xs]
+    Kp, Vp = [K], [V]
+    y = None
+    for i in range(warm):
+        y = B.decode(s, cts[i], w, cache, coeffs, ch.q)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("block_step")
+    e0.record()
+    for i in range(warm, len(cts)):
+        y = B.decode(s, cts[i], w, cache, coeffs, ch.q)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # the fp64 step of the last token, with every earlier token's K and V rows appended as the cache saw them
+    for x in xs[:-1]:
+        Kp.append((x @ w.wk + w.bk)[None])
+        Vp.append((x @ w.wv + w.bv)[None])
+    want = B.plain_decode(xs[-1], w, np.vstack(Kp), np.vstack(Vp), coeffs, 12, 64)
+    got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
+    err = float(np.abs(got - want).max())
+    del s, cache, cts, y
+    torch.cuda.empty_cache()
+    return {"workload": "config 3 attention block, one token: Q/K/V projections (768 of 1024), push into a 128-token "
+                        "lane cache (4 blocks x 32 tokens, 12 heads x 64 per block), attention with the degree-7 "
+                        "polynomial softmax, output projection; N=2^16 24+8 limbs, radix-3 ladders, eager",
+            "ms_per_token": t.item(), "timed_tokens": steps, "max_abs_err_vs_fp64": err,
+            "tokens_in_cache_at_end": pre + len(xs)}
+
+
 def main():
     a = parse()
     if a.part == "projection":
         print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
+        return
+    if a.part == "block":
+        print(json.dumps({"part": "block", **block_decode(a, 1, lambda: None, None)}), flush=True)
         return
     if a.part == "attention":
         ms, err = attention_decode(a, 1, 0, lambda: None, None)

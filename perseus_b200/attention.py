@@ -62,8 +62,25 @@ class Layout:
     radix_bits: int = 1  # rotate_and_sum ladders: 1 = rung by rung; >= 2 = groups of that many gaps (rotate_sum)
 
     def ladders(self):
-        d, t = self.head_dim, self.tokens
-        return [(1, d), (-1, d), (d, d * t)]
+        return [self.score_ladder(), self.replicate_ladder(), self.sum_ladder()]
+
+    # the decode step's three rotate_and_sum ladders (start, stop) and its score mask
+    def score_ladder(self):
+        return 1, self.head_dim
+
+    def replicate_ladder(self):
+        return -1, self.head_dim
+
+    def sum_ladder(self):
+        return self.head_dim, self.head_dim * self.tokens
+
+    def mask(self):
+        """Slot 0 of every token block of the cache's capacity. Tokens not yet in the cache hold zero K and V
+        words: their scores are zero and the weights they get multiply zero values, so the mask does not follow the
+        token count and the masked coefficient plaintexts are constants of the layout."""
+        m = np.zeros(self.slots)
+        m[0 : self.tokens * self.head_dim : self.head_dim] = 1.0
+        return m
 
     def rot_steps(self):
         """The rotation keys the decode step needs: every rung (gap) of the three ladders, and with radix groups
@@ -152,15 +169,6 @@ def encrypt_query(ops, q, layout, top, q_top_prime):
     return ops.encrypt(vec, top=top, scale=q_top_prime * 2.0**10, slots=layout.slots)
 
 
-def _mask(layout):
-    """Slot 0 of every token block of the cache's capacity. Tokens not yet in the cache hold zero K and V words: their
-    scores are zero and the weights they get multiply zero values, so the mask does not follow the token count and
-    the masked coefficient plaintexts are constants of the layout."""
-    m = np.zeros(layout.slots)
-    m[0 : layout.tokens * layout.head_dim : layout.head_dim] = 1.0
-    return m
-
-
 def _pt(ops, plan, values, top, scale, slots):
     """A plaintext of the decode step (mask x polynomial coefficient at a fixed level and scale): encoded on first use
     and kept in the cache's plan, so later tokens reuse it."""
@@ -172,22 +180,22 @@ def _pt(ops, plan, values, top, scale, slots):
 
 
 def attend(ops, q_ct, cache, coeffs, primes):
-    """One decode step for one head: the encrypted attention output (slots 0..d-1). `primes` = the chain's Q primes
-    (bottom first); `ops` provides mult, rescale_one, rotate_and_sum, drop_to, add, pt, mult_pt, add_pt."""
+    """One decode step: the encrypted attention output (one head: slots 0..d-1; the lane layout of the block: slot m t
+    per block). `primes` = the chain's Q primes (bottom first); `ops` provides mult, rescale_one, rotate_and_sum,
+    drop_to, add, pt, mult_pt, add_pt. The layout gives the three ladders and the score mask."""
     lay = cache.lay
-    d, T = lay.head_dim, lay.tokens
     top = q_ct.top
     # 1. scores
     k_ct = ops.drop_to(cache.k, top)
     prod = ops.rescale_one(ops.mult(q_ct, k_ct))
-    x = ops.rotate_and_sum(prod, 1, d, lay.radix_bits)  # top L-1
+    x = ops.rotate_and_sum(prod, *lay.score_ladder(), lay.radix_bits)  # top L-1
     L1 = x.top
     # 2. masked polynomial (baby steps x, x^2, x^3; giant step x^4)
     x2 = ops.rescale_one(ops.mult(x, x))  # L-2
     x3 = ops.rescale_one(ops.mult(x2, ops.drop_to(x, L1 - 1)))  # L-3
     x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
     lvl = L1 - 2  # the level of x^3 / x^4
-    mask = _mask(lay)
+    mask = lay.mask()
 
     def term(pw, c, target_scale):
         # c * mask * x^pw, landing at level lvl - 1 with scale target_scale (the plaintext scale solves for it)
@@ -214,11 +222,11 @@ def attend(ops, q_ct, cache, coeffs, primes):
     A.scale = xb.scale
     P = ops.add(A, xb)
     # 3. replicate each weight over its block
-    R = ops.rotate_and_sum(P, -1, d, lay.radix_bits)
+    R = ops.rotate_and_sum(P, *lay.replicate_ladder(), lay.radix_bits)
     # 4. weighted values, summed over tokens
     v_ct = ops.drop_to(cache.v, R.top)
     y = ops.rescale_one(ops.mult(R, v_ct))
-    return ops.rotate_and_sum(y, d, d * T, lay.radix_bits)
+    return ops.rotate_and_sum(y, *lay.sum_ladder(), lay.radix_bits)
 
 
 class DecodeGraph:

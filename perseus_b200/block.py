@@ -1,0 +1,218 @@
+"""The attention block's decode step in the projection layout: Q, K, V projections of the token's activation, the
+token's K and V rows pushed into the encrypted cache, attention over the cache, the output projection. The role of the
+reference's GPT-2 attention block (python/perseus/impl/attention.py:491-551 KVCache and cache_kv_push, :698-800
+complex_qkt, :897-962 complex_softmax_v; python/perseus/impl/linear.py:151-156 linear_multi), laid out on the slots of
+the projections (perseus_b200/linear.py: element m of the padded width d at slot m t, t = slots / d lanes per element).
+
+Tokens in lanes: a cache block of t tokens is ONE ciphertext holding every head, slot m t + tau = K[b t + tau][m]
+(likewise V); the cache is a batch of T / t blocks. With q replicated over the lanes (q_rep[m t + tau] = q[m]):
+1. scores: prod = q_rep K_b, then rotate_and_sum(prod, t, d_h t) sums each head's d_h element blocks at a fixed lane:
+   slot (d_h h) t + tau holds s_{h, tau} = <q_h, K_tau,h> (q carries 1 / sqrt(d_h));
+2. weights P = mask p7(s) (mask: lane tau of each head's first element block), the polynomial of attention.attend;
+3. rotate_and_sum(P, -t, d_h t) replicates P_{h, tau} over the head's element blocks at lane tau;
+4. y = P V_b, then rotate_and_sum(y, 1, t) sums the lanes: slot m t holds sum_tau P_{h, tau} V_tau[m], element m of
+   the block's attention output, in the layout the output projection reads; the blocks' outputs are added.
+The decode math (steps 1-4, its polynomial, levels and scales) is attention.attend's with these three ladders; a block
+runs every head and every token of the block in the same launches, and the batch of blocks runs together.
+
+Pushing a token: the projections leave K[m] (V[m]) at lane 0 of element block m and partial sums in the other lanes;
+a lane-0 mask (one plaintext product) keeps K[m], a rotation by -(position mod t) moves it to the token's lane, and
+the row is added into its block. The query is masked the same way with 1 / sqrt(d_h) folded in, then replicated over
+the lanes by rotate_and_sum(q, -1, t).
+
+The attention output is masked to lane 0 as well before the output projection, whose replication ladder reads every
+lane. Levels from the activation's top L: projections L - 1, masks L - 2 (the cache's level), attention L - 8, mask
+L - 9, output projection L - 10.
+"""
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import attention as A
+from . import linear as LIN
+from .attention import ladder_steps
+
+
+@dataclass
+class LaneLayout:
+    geo: LIN.Geometry  # the projections' geometry (slots, padded width d, lanes t)
+    heads: int  # heads with weights (the rest of the padded width is zero)
+    head_dim: int
+    blocks: int  # cache blocks of t tokens
+    radix_bits: int = 1
+
+    @property
+    def slots(self):
+        return self.geo.slots
+
+    @property
+    def t(self):
+        return self.geo.t
+
+    @property
+    def tokens(self):
+        return self.blocks * self.t
+
+    @property
+    def width(self):
+        return self.heads * self.head_dim
+
+    def score_ladder(self):
+        return self.t, self.head_dim * self.t
+
+    def replicate_ladder(self):
+        return -self.t, self.head_dim * self.t
+
+    def sum_ladder(self):
+        return 1, self.t
+
+    def query_ladder(self):
+        return -1, self.t
+
+    def mask(self):
+        """Every lane (token) of each head's first element block: where the scores land."""
+        m = np.zeros(self.slots)
+        for h in range(self.heads):
+            m[h * self.head_dim * self.t:h * self.head_dim * self.t + self.t] = 1.0
+        return m
+
+    def lane0(self, value=1.0):
+        m = np.zeros(self.slots)
+        m[np.arange(self.width) * self.t] = value
+        return m
+
+    def push_steps(self, lane):
+        """Rotations (each with a key of the query ladder) that move lane 0 to `lane`: the largest available right
+        rotation first."""
+        avail = sorted({-s for s in ladder_steps(*self.query_ladder(), self.radix_bits)}, reverse=True)
+        steps, left = [], lane
+        while left:
+            s = next(a for a in avail if a <= left)
+            steps.append(-s)
+            left -= s
+        return steps
+
+    def rot_steps(self):
+        steps = self.geo.rot_steps(self.radix_bits)
+        for lad in (self.score_ladder(), self.replicate_ladder(), self.sum_ladder(), self.query_ladder()):
+            steps += ladder_steps(*lad, self.radix_bits)
+        seen = set()
+        return [s % self.slots for s in steps if s % self.slots and not (s % self.slots in seen or seen.add(s % self.slots))]
+
+
+def layout(slots, d, heads, head_dim, tokens, radix_bits=1):
+    geo = LIN.geometry(slots, d)
+    if heads * head_dim > d or tokens % geo.t:
+        raise ValueError(f"{heads} x {head_dim} wider than {d}, or {tokens} tokens not in blocks of {geo.t}")
+    return LaneLayout(geo, heads, head_dim, tokens // geo.t, radix_bits)
+
+
+@dataclass
+class Weights:
+    """The block's weights (d_real x d_real each, d_real = heads x head_dim) and biases, as numpy arrays."""
+
+    wq: np.ndarray
+    bq: np.ndarray
+    wk: np.ndarray
+    bk: np.ndarray
+    wv: np.ndarray
+    bv: np.ndarray
+    wo: np.ndarray
+    bo: np.ndarray
+
+
+class LaneCache:
+    """The encrypted K and V caches as batches of token blocks, at the level the pushed rows arrive at; the decode
+    step's plaintexts (masks, encoded weights) are kept in `plan`."""
+
+    def __init__(self, ops, lay, top, scale=2.0**40):
+        self.ops, self.lay, self.top, self.scale = ops, lay, top, scale
+        self.k = self.v = None
+        self.count = 0
+        self.plan = {}
+
+    def _blocks(self, rows):
+        lay = self.lay
+        vecs = [np.zeros(lay.slots) for _ in range(lay.blocks)]
+        for tok, row in enumerate(rows):
+            b, lane = divmod(tok, lay.t)
+            vecs[b][np.arange(lay.width) * lay.t + lane] = row
+        cts = [self.ops.encrypt(v, top=self.top, scale=self.scale, slots=lay.slots) for v in vecs]
+        return self.ops.stack(cts)
+
+    def load(self, K, V):
+        """The client's cache of n tokens (n x d_real each), one encryption per block."""
+        if K.shape[0] > self.lay.tokens:
+            raise ValueError("more tokens than the cache holds")
+        self.k, self.v = self._blocks(K), self._blocks(V)
+        self.count = K.shape[0]
+
+    def push(self, k_row, v_row):
+        """The token's K and V rows (one batch of two at this cache's level and scale, each value at lane 0 of its
+        element block, nothing in the other lanes) rotated to the token's lane and added into its block."""
+        ops, lay = self.ops, self.lay
+        if self.count >= lay.tokens:
+            raise ValueError(f"KV cache full ({lay.tokens} tokens)")
+        b, lane = divmod(self.count, lay.t)
+        kv = ops.stack([k_row, v_row])
+        for st in lay.push_steps(lane):
+            kv = ops.rotate(kv, st)
+        kr, vr = ops.split(kv, 2)
+        ops.inplace_add(ops.split(self.k, lay.blocks)[b], kr)
+        ops.inplace_add(ops.split(self.v, lay.blocks)[b], vr)
+        self.count += 1
+
+
+def _masked(ops, cache, x, values, target_scale, primes):
+    """x * values (a plaintext of the plan), rescaled, landing at target_scale one level below x."""
+    pscale = target_scale * primes[x.top] / x.scale
+    pt = A._pt(ops, cache.plan, values, x.top, pscale, cache.lay.slots)
+    return ops.rescale_one(ops.mult_pt(x, pt, pscale))
+
+
+def _linear(ops, cache, name, W, b, top, scale):
+    key = ("linear", name, top, float(scale))
+    lin = cache.plan.get(key)
+    if lin is None:
+        lin = cache.plan[key] = LIN.encode(ops, W, cache.lay.geo, top, scale, bias=b)
+    return lin
+
+
+def decode(ops, x_ct, w, cache, coeffs, primes):
+    """One token: x_ct the activation (projection layout, at the cache's level + 2), w the block's Weights. Pushes the
+    token's K and V into the cache and returns the block's output (projection layout)."""
+    lay = cache.lay
+    rb = lay.radix_bits
+    if x_ct.top != cache.top + 2:
+        raise ValueError(f"activation at top {x_ct.top}; the cache lives at {cache.top} (= the activation's - 2)")
+    lins = [_linear(ops, cache, n, W, b, x_ct.top, x_ct.scale)
+            for n, W, b in (("q", w.wq, w.bq), ("k", w.wk, w.bk), ("v", w.wv, w.bv))]
+    q, k, v = LIN.linear_multi(ops, x_ct, lins, rb)
+    # the token's K and V rows: lane 0 kept, at the cache's scale
+    kv = _masked(ops, cache, ops.stack([k, v]), lay.lane0(), cache.scale, primes)
+    kr, vr = ops.split(kv, 2)
+    cache.push(kr, vr)
+    # the query: lane 0 with 1 / sqrt(d_h), at q_top 2^10 so the products land near the primes' size
+    qm = _masked(ops, cache, q, lay.lane0(1.0 / math.sqrt(lay.head_dim)), primes[q.top - 1] * 2.0**10, primes)
+    qr = ops.rotate_and_sum(qm, *lay.query_ladder(), rb)
+    qb = ops.stack([qr] * lay.blocks) if lay.blocks > 1 else qr
+    yb = A.attend(ops, qb, cache, coeffs, primes)
+    y = ops.sum(ops.split(yb, lay.blocks)) if lay.blocks > 1 else yb
+    # the lane sums leave partial sums in lanes 1 .. t-1; the projection's replication ladder needs them zero
+    y = _masked(ops, cache, y, lay.lane0(), y.scale, primes)
+    lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)
+    return LIN.linear(ops, y, lin_o, rb)
+
+
+def plain_decode(x, w, K, V, coeffs, heads, head_dim):
+    """fp64 reference of the step: projections, the token appended to the cache, per-head attention with the same
+    polynomial softmax, output projection."""
+    q, k, v = x @ w.wq + w.bq, x @ w.wk + w.bk, x @ w.wv + w.bv
+    Ka, Va = np.vstack([K, k]), np.vstack([V, v])
+    out = np.zeros(heads * head_dim)
+    for h in range(heads):
+        sl = slice(h * head_dim, (h + 1) * head_dim)
+        s = Ka[:, sl] @ q[sl] / math.sqrt(head_dim)
+        out[sl] = A.poly_eval(coeffs, s) @ Va[:, sl]
+    return out @ w.wo + w.bo

@@ -1,5 +1,6 @@
-"""Test infrastructure: the session op signatures over the oracle context, so the attention driver can run the same
-op sequence on the CPU restatement as on the CUDA path."""
+"""Test infrastructure: the session op signatures over the oracle context, so the attention, projection and block
+drivers can run the same op sequence on the CPU restatement as on the CUDA path. A batch (the session's K-batched
+ciphertext) is an OBatch of single ciphertexts; every op maps over its members."""
 from dataclasses import dataclass
 
 import numpy as np
@@ -13,6 +14,55 @@ class OCt:
     slots: int
 
 
+class OBatch:
+    """A batch of oracle ciphertexts at one level and scale."""
+
+    def __init__(self, cts):
+        self.cts = list(cts)
+
+    @property
+    def k(self):
+        return len(self.cts)
+
+    @property
+    def top(self):
+        return self.cts[0].top
+
+    @property
+    def scale(self):
+        return self.cts[0].scale
+
+    @scale.setter
+    def scale(self, v):
+        for c in self.cts:
+            c.scale = v
+
+    @property
+    def slots(self):
+        return self.cts[0].slots
+
+
+@dataclass
+class OracleDiagonals:
+    pts: np.ndarray
+    bstep: int
+    stride: int
+    top: int
+    scale: float
+
+
+def _batched(f):
+    """Apply f member by member when an argument is a batch (other arguments shared)."""
+
+    def g(self, *args):
+        n = next((a.k for a in args if isinstance(a, OBatch)), None)
+        if n is None:
+            return f(self, *args)
+        return OBatch([f(self, *[a.cts[i] if isinstance(a, OBatch) else a for a in args]) for i in range(n)])
+
+    return g
+
+
 class OracleOps:
     def __init__(self, ctx):
         self.c = ctx
@@ -20,44 +70,77 @@ class OracleOps:
     def encrypt(self, values, top, scale, slots):
         return OCt(self.c.encrypt(values, slots, scale, top), top, scale, slots)
 
+    @_batched
     def add(self, a, b):
         assert a.top == b.top
         return OCt(self.c.add(a.data, b.data, a.top), a.top, a.scale, a.slots)
 
+    @_batched
     def mult(self, a, b):
         assert a.top == b.top
         return OCt(self.c.mult(a.data, b.data, a.top), a.top, a.scale * b.scale, a.slots)
 
+    @_batched
     def rescale_one(self, a):
-        if isinstance(a, OBatch):
-            return OBatch([self.rescale_one(c) for c in a.cts])
         a.data = self.c.rescale(a.data, a.top)
         a.scale /= self.c.q[a.top]
         a.top -= 1
         return a
 
+    @_batched
     def rotate_and_sum(self, a, start, stop, radix_bits=1):
-        if isinstance(a, OBatch):
-            return OBatch([self.rotate_and_sum(c, start, stop, radix_bits) for c in a.cts])
         return OCt(self.c.rotate_and_sum(a.data, start, stop, a.top, radix_bits), a.top, a.scale, a.slots)
 
+    @_batched
+    def rotate(self, a, step):
+        return OCt(self.c.rotate(a.data, step, a.top), a.top, a.scale, a.slots)
+
+    @_batched
     def rotate_sum(self, a, steps):
         return OCt(self.c.rotate_sum(a.data, steps, a.top), a.top, a.scale, a.slots)
 
+    @_batched
     def drop_to(self, a, top):
         return OCt(a.data, top, a.scale, a.slots)
 
     def pt(self, values, top, scale, slots):
         return self.c.encode(values, slots, scale, top)
 
+    @_batched
     def mult_pt(self, a, pt, pt_scale):
         return OCt(self.c.mult_pt(a.data, pt, a.top), a.top, a.scale * pt_scale, a.slots)
 
+    @_batched
     def add_pt(self, a, pt):
         return OCt(self.c.add_pt(a.data, pt, a.top), a.top, a.scale, a.slots)
 
-    def decrypt_slots(self, a):
+    def decrypt_slots(self, a, index=0):
+        if isinstance(a, OBatch):
+            a = a.cts[index]
         return self.c.decrypt(a.data, a.top, a.slots, a.scale)
+
+    def inplace_add(self, a, b):
+        assert a.top == b.top
+        a.data = self.c.add(a.data, b.data, a.top)
+        return a
+
+    def stack(self, cts):
+        out = []
+        for c in cts:
+            out += c.cts if isinstance(c, OBatch) else [c]
+        return OBatch(out)
+
+    def split(self, a, n):
+        assert a.k % n == 0
+        k = a.k // n
+        parts = [a.cts[i * k:(i + 1) * k] for i in range(n)]
+        return [p[0] if k == 1 else OBatch(p) for p in parts]
+
+    def sum(self, cts):
+        acc = cts[0]
+        for c in cts[1:]:
+            acc = self.add(acc, c)
+        return acc
 
     def diagonals(self, diags, bstep, top, scale=None, slots=None, stride=1):
         """Evaluation-form plaintexts of a BSGS product (diagonal d pre-rotated by -bstep (d // bstep) stride)."""
@@ -71,29 +154,11 @@ class OracleOps:
             pts[d, : top + 1] = rows
         return OracleDiagonals(pts, bstep, stride, top, scale)
 
+    @_batched
     def linear_transform(self, a, lt):
         assert a.top == lt.top
         out = self.c.linear_transform(a.data, lt.pts, lt.bstep, lt.stride, a.top)
         return OCt(out, a.top, a.scale * lt.scale, a.slots)
 
     def linear_transform_multi(self, a, lts):
-        return OBatch([self.linear_transform(a, lt) for lt in lts])
-
-    def split(self, a, n):
-        assert len(a.cts) == n
-        return list(a.cts)
-
-
-@dataclass
-class OBatch:
-    """A batch of oracle ciphertexts: the batch-taking ops map over its members."""
-    cts: list
-
-
-@dataclass
-class OracleDiagonals:
-    pts: np.ndarray
-    bstep: int
-    stride: int
-    top: int
-    scale: float
+        return self.stack([self.linear_transform(a, lt) for lt in lts])

@@ -1,0 +1,42 @@
+"""The attention block's decode step (projections, cache push, attention in lanes, output projection) on the oracle:
+decrypted against the fp64 step with the same polynomial softmax (small ring; the GPU parity test runs the same
+sequence on both sides word for word)."""
+import numpy as np
+import pytest
+
+from perseus_b200 import attention as A
+from perseus_b200 import block as B
+from tests import _oracle as O
+from tests._oracle_ops import OracleOps
+
+LOGN = 10
+
+
+def _weights(rng, n, s=0.1):
+    return B.Weights(*[rng.normal(0, s, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+
+
+@pytest.mark.parametrize("radix", [1, 3])
+def test_block_decode_on_the_oracle(radix):
+    lay = B.layout(1 << (LOGN - 1), 32, heads=4, head_dim=8, tokens=32, radix_bits=radix)
+    assert (lay.t, lay.blocks) == (16, 2)
+    q = O.ntt_primes(50, LOGN, 12)
+    p = O.ntt_primes(50, LOGN, 3, skip=12)  # the special primes cover a digit (3 limbs)
+    c = O.Ctx(LOGN, q, p, 4)
+    c.keygen(seed=0, h=64, sigma=3.2, galois=[1] + [O.lib().orc_rotation_galois(s, LOGN) for s in lay.rot_steps()])
+    ops = OracleOps(c)
+    rng = np.random.default_rng(9)
+    n, pre = 32, 21  # the new token lands in block 1, lane 5
+    w = _weights(rng, n)
+    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+    x = rng.normal(0, 1, n) / 2
+    top = c.nq - 1
+    cache = B.LaneCache(ops, lay, top - 2)
+    cache.load(K, V)
+    coeffs = A.softmax_poly(lay.tokens)
+    xc = ops.encrypt(B.LIN.input_vector(x, lay.geo), top, 2.0**40, lay.slots)
+    y = B.decode(ops, xc, w, cache, coeffs, c.q)
+    assert cache.count == pre + 1 and y.top == top - 10
+    got = B.LIN.output_values(ops.decrypt_slots(y).real, lay.geo, n)
+    want = B.plain_decode(x, w, K, V, coeffs, 4, 8)
+    assert np.abs(got - want).max() < 1e-3, np.abs(got - want).max()

@@ -1,0 +1,49 @@
+"""The attention block's decode step on the GPU against the same op sequence on the oracle, word for word: Q/K/V
+projections, the token pushed into the lane cache, attention over two token blocks, the output projection (FP64
+chain at N = 2^14 with 12 limbs); decrypted against the fp64 step."""
+import numpy as np
+import pytest
+
+from perseus_b200 import attention as A
+from perseus_b200 import block as B
+from perseus_b200 import fhe
+from tests import _oracle as O
+from tests._oracle_ops import OracleOps
+
+pytestmark = pytest.mark.gpu
+
+
+def host(t):
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+@pytest.mark.parametrize("radix", [3])
+def test_block_decode_bit_exact(radix):
+    ch = fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 12)), tuple(fhe.ntt_primes(50, 14, 3, skip=12)), 4)
+    lay = B.layout(ch.n // 2, 256, heads=4, head_dim=64, tokens=64, radix_bits=radix)
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=3, seed=0)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(0, 192, 3.2, s.galois)
+    oops = OracleOps(o)
+    rng = np.random.default_rng(12)
+    n, pre = 256, 37  # the new token: block 1, lane 5
+    w = B.Weights(*[rng.normal(0, 0.05, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+    x = rng.normal(0, 1, n) / 2
+    top = s.top()
+    coeffs = A.softmax_poly(lay.tokens)
+    outs = []
+    for ops in (s, oops):
+        cache = B.LaneCache(ops, lay, top - 2)
+        cache.load(K, V)
+        xc = ops.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots)
+        outs.append((B.decode(ops, xc, w, cache, coeffs, ch.q), cache))
+    (y, cache), (oy, ocache) = outs
+    assert y.top == oy.top == top - 10
+    assert (host(y.data[0])[:, : y.top + 1] == oy.data[:, : y.top + 1]).all()
+    for blk in range(lay.blocks):
+        for dev, orc in ((cache.k, ocache.k), (cache.v, ocache.v)):
+            assert (host(dev.data[blk])[:, : cache.top + 1] == orc.cts[blk].data[:, : cache.top + 1]).all(), blk
+    got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
+    want = B.plain_decode(x, w, K, V, coeffs, 4, 64)
+    assert np.abs(got - want).max() < 1e-3

@@ -482,9 +482,10 @@ def projection(a, world, barrier, dist):
 
 
 def block_decode(a, world, barrier, dist):
-    """Config 3's attention block, one token per step: Q/K/V projections of the activation, the token's K and V pushed
-    into the lane cache (128 tokens in 4 blocks of 32, all 12 heads per block), attention over the cache, output
-    projection (perseus_b200.block; N = 2^16 with the 24-limb chain, weights N(0, 0.02), biases, activation N(0, 1)).
+    """Config 3's attention block, one token per step: the polynomial LayerNorm (gamma, beta folded into Q/K/V), Q/K/V
+    projections, the token's K and V pushed into the lane cache (128 tokens in 4 blocks of 32, all 12 heads per
+    block), attention over the cache, output projection, residual (perseus_b200.block; N = 2^16 with the 24-limb
+    chain, weights N(0, 0.02), biases, gamma 1 + N(0, 0.02), activation N(0, 1)).
     The cache starts with client-encrypted tokens and grows by one per step up to its 128; ms per token with CUDA events (every
     rank runs the same replica; max over ranks), and the last step's decrypted error against the fp64 step."""
     import numpy as np
@@ -501,8 +502,10 @@ def block_decode(a, world, barrier, dist):
     warm, steps = max(a.warmup, 3), min(a.steps, 64)  # the cache holds 128 tokens: the steps fill its last lanes
     n, pre, top = 768, lay.tokens - warm - steps, len(ch.q) - 1
     w = B.Weights(*[rng.normal(0, 0.02, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+    gamma, beta = 1 + rng.normal(0, 0.02, n), rng.normal(0, 0.02, n)
+    wf, norm = B.fold_norm(w, gamma, beta), B.NormCfg()
     K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
-    cache = B.LaneCache(s, lay, top - 2)
+    cache = B.LaneCache(s, lay, top - 10)
     cache.load(K, V)
     coeffs = A.softmax_poly(lay.tokens)
     xs = [rng.normal(0, 1, n) for _ in range(warm + steps)]
@@ -510,14 +513,14 @@ def block_decode(a, world, barrier, dist):
     Kp, Vp = [K], [V]
     y = None
     for i in range(warm):
-        y = B.decode(s, cts[i], w, cache, coeffs, ch.q)
+        y = B.decode(s, cts[i], wf, cache, coeffs, ch.q, norm=norm, residual=True)
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("block_step")
     e0.record()
     for i in range(warm, len(cts)):
-        y = B.decode(s, cts[i], w, cache, coeffs, ch.q)
+        y = B.decode(s, cts[i], wf, cache, coeffs, ch.q, norm=norm, residual=True)
     e1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
@@ -526,16 +529,18 @@ def block_decode(a, world, barrier, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     # the fp64 step of the last token, with every earlier token's K and V rows appended as the cache saw them
     for x in xs[:-1]:
-        Kp.append((x @ w.wk + w.bk)[None])
-        Vp.append((x @ w.wv + w.bv)[None])
-    want = B.plain_decode(xs[-1], w, np.vstack(Kp), np.vstack(Vp), coeffs, 12, 64)
+        xn = norm.plain(x) * gamma + beta
+        Kp.append((xn @ w.wk + w.bk)[None])
+        Vp.append((xn @ w.wv + w.bv)[None])
+    want = B.plain_decode(norm.plain(xs[-1]) * gamma + beta, w, np.vstack(Kp), np.vstack(Vp), coeffs, 12, 64) + xs[-1]
     got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
     err = float(np.abs(got - want).max())
     del s, cache, cts, y
     torch.cuda.empty_cache()
-    return {"workload": "config 3 attention block, one token: Q/K/V projections (768 of 1024), push into a 128-token "
-                        "lane cache (4 blocks x 32 tokens, 12 heads x 64 per block), attention with the degree-7 "
-                        "polynomial softmax, output projection; N=2^16 24+8 limbs, radix-3 ladders, eager",
+    return {"workload": "config 3 attention block, one token: LayerNorm (degree-7 inverse square root), Q/K/V "
+                        "projections (768 of 1024), push into a 128-token lane cache (4 blocks x 32 tokens, 12 heads "
+                        "x 64 per block), attention with the degree-7 polynomial softmax, output projection, "
+                        "residual; N=2^16 24+8 limbs, radix-3 ladders, eager",
             "ms_per_token": t.item(), "timed_tokens": steps, "max_abs_err_vs_fp64": err,
             "tokens_in_cache_at_end": pre + len(xs)}
 

@@ -179,29 +179,22 @@ def _pt(ops, plan, values, top, scale, slots):
     return pt
 
 
-def attend(ops, q_ct, cache, coeffs, primes):
-    """One decode step: the encrypted attention output (one head: slots 0..d-1; the lane layout of the block: slot m t
-    per block). `primes` = the chain's Q primes (bottom first); `ops` provides mult, rescale_one, rotate_and_sum,
-    drop_to, add, pt, mult_pt, add_pt. The layout gives the three ladders and the score mask."""
-    lay = cache.lay
-    top = q_ct.top
-    # 1. scores
-    k_ct = ops.drop_to(cache.k, top)
-    prod = ops.rescale_one(ops.mult(q_ct, k_ct))
-    x = ops.rotate_and_sum(prod, *lay.score_ladder(), lay.radix_bits)  # top L-1
+def poly7(ops, plan, x, coeffs, mask, primes, slots):
+    """mask * p(x) for a polynomial of degree <= 7 (power-basis coefficients), x at a scale near its level's prime:
+    baby steps x, x^2, x^3, giant step x^4, p = (c0 + c1 x + c2 x^2 + c3 x^3) + x^4 (c4 + c5 x + c6 x^2 + c7 x^3), the
+    coefficients as masked plaintexts (the mask costs no level) whose scales make every term meet at one scale; the
+    plaintexts are kept in `plan`. Four levels: the result sits at x.top - 4."""
     L1 = x.top
-    # 2. masked polynomial (baby steps x, x^2, x^3; giant step x^4)
     x2 = ops.rescale_one(ops.mult(x, x))  # L-2
     x3 = ops.rescale_one(ops.mult(x2, ops.drop_to(x, L1 - 1)))  # L-3
     x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
     lvl = L1 - 2  # the level of x^3 / x^4
-    mask = lay.mask()
 
     def term(pw, c, target_scale):
         # c * mask * x^pw, landing at level lvl - 1 with scale target_scale (the plaintext scale solves for it)
         src = ops.drop_to(pw, lvl)
         pscale = target_scale * primes[lvl] / src.scale
-        pt = _pt(ops, cache.plan, mask * c, lvl, pscale, lay.slots)
+        pt = _pt(ops, plan, mask * c, lvl, pscale, slots)
         return ops.rescale_one(ops.mult_pt(src, pt, pscale))
 
     def inner(cs, target_scale):
@@ -209,7 +202,7 @@ def attend(ops, q_ct, cache, coeffs, primes):
         for i, (pw, c) in enumerate(zip((x, x2, x3), cs[1:])):
             t_ = term(pw, c, target_scale)
             acc = t_ if acc is None else ops.add(acc, t_)
-        pt0 = _pt(ops, cache.plan, mask * cs[0], acc.top, acc.scale, lay.slots)
+        pt0 = _pt(ops, plan, mask * cs[0], acc.top, acc.scale, slots)
         return ops.add_pt(acc, pt0)
 
     # p = A + x^4 B: A at level lvl - 2 with scale S; B at lvl - 1 with scale S q_{lvl-1} / scale(x^4)
@@ -220,7 +213,21 @@ def attend(ops, q_ct, cache, coeffs, primes):
     A = inner(coeffs[:4], xb.scale)  # lvl - 1, the same scale as x^4 B ...
     A = ops.drop_to(A, xb.top)  # ... at the same level
     A.scale = xb.scale
-    P = ops.add(A, xb)
+    return ops.add(A, xb)
+
+
+def attend(ops, q_ct, cache, coeffs, primes):
+    """One decode step: the encrypted attention output (one head: slots 0..d-1; the lane layout of the block: slot m t
+    per block). `primes` = the chain's Q primes (bottom first); `ops` provides mult, rescale_one, rotate_and_sum,
+    drop_to, add, pt, mult_pt, add_pt. The layout gives the three ladders and the score mask."""
+    lay = cache.lay
+    top = q_ct.top
+    # 1. scores
+    k_ct = ops.drop_to(cache.k, top)
+    prod = ops.rescale_one(ops.mult(q_ct, k_ct))
+    x = ops.rotate_and_sum(prod, *lay.score_ladder(), lay.radix_bits)  # top L-1
+    # 2. masked polynomial
+    P = poly7(ops, cache.plan, x, coeffs, lay.mask(), primes, lay.slots)
     # 3. replicate each weight over its block
     R = ops.rotate_and_sum(P, *lay.replicate_ladder(), lay.radix_bits)
     # 4. weighted values, summed over tokens

@@ -70,6 +70,10 @@ class LaneLayout:
     def query_ladder(self):
         return -1, self.t
 
+    def norm_ladder(self):
+        """Every element block's lane 0 summed into every one (LayerNorm's mean and variance)."""
+        return self.t, self.t * self.geo.d
+
     def mask(self):
         """Every lane (token) of each head's first element block: where the scores land."""
         m = np.zeros(self.slots)
@@ -95,7 +99,8 @@ class LaneLayout:
 
     def rot_steps(self):
         steps = self.geo.rot_steps(self.radix_bits)
-        for lad in (self.score_ladder(), self.replicate_ladder(), self.sum_ladder(), self.query_ladder()):
+        for lad in (self.score_ladder(), self.replicate_ladder(), self.sum_ladder(), self.query_ladder(),
+                    self.norm_ladder()):
             steps += ladder_steps(*lad, self.radix_bits)
         seen = set()
         return [s % self.slots for s in steps if s % self.slots and not (s % self.slots in seen or seen.add(s % self.slots))]
@@ -164,10 +169,63 @@ class LaneCache:
         self.count += 1
 
 
-def _masked(ops, cache, x, values, target_scale, primes):
+@dataclass
+class NormCfg:
+    """LayerNorm without its affine part: (x - mean) / sqrt(var + eps) over the real width, the inverse square root
+    replaced by the degree-7 Chebyshev interpolant of 1 / sqrt(u) on [lo, hi] (the variances of the block's inputs lie
+    there), as the softmax is by its polynomial; gamma and beta go into the next linears (fold_norm)."""
+
+    lo: float = 0.5
+    hi: float = 2.0
+    eps: float = 1e-5
+
+    def coeffs(self):
+        """Power-basis coefficients in z = (2 u - lo - hi) / (hi - lo) in [-1, 1]."""
+        k = np.arange(8)
+        z = np.cos((2 * k + 1) * np.pi / 16)
+        u = 0.5 * (self.hi - self.lo) * z + 0.5 * (self.hi + self.lo)
+        return [float(c) for c in np.polynomial.polynomial.polyfit(z, 1.0 / np.sqrt(u), 7)]
+
+    def plain(self, x):
+        """fp64 reference: the same polynomial in place of 1 / sqrt."""
+        c = x - x.mean()
+        u = (c @ c) / x.size + self.eps
+        z = (2 * u - self.lo - self.hi) / (self.hi - self.lo)
+        return c * A.poly_eval(self.coeffs(), z)
+
+
+def fold_norm(w, gamma, beta):
+    """The LayerNorm's affine part folded into the Q, K and V linears: (n gamma + beta) W + b = n (diag(gamma) W) +
+    (beta W + b)."""
+    return Weights(gamma[:, None] * w.wq, beta @ w.wq + w.bq, gamma[:, None] * w.wk, beta @ w.wk + w.bk,
+                   gamma[:, None] * w.wv, beta @ w.wv + w.bv, w.wo, w.bo)
+
+
+def layer_norm(ops, x, lay, plan, cfg, primes):
+    """The normalized activation (projection layout, lane 0 of the real elements, zeros elsewhere), 8 levels below x
+    (the input: projection layout with zeros outside lane 0 of the real elements, as the client encrypts it):
+    1. every element block's lane 0 summed into every one: rotate_and_sum(x, t, t d) (the layout's other lanes hold
+       zeros), centred c = x - sum / d_real on the real elements;
+    2. the variance the same way from c^2;
+    3. z = (2 (var / d_real + eps) - lo - hi) / (hi - lo), then 1 / sqrt by the polynomial (attention.poly7 under the
+       real elements' lane-0 mask), times c."""
+    dr = lay.width
+    real = lay.lane0()
+    s = ops.rotate_and_sum(x, *lay.norm_ladder(), lay.radix_bits)
+    c = ops.add(ops.drop_to(x, x.top - 1), _masked(ops, plan, s, real * (-1.0 / dr), x.scale, primes))
+    sq = ops.rescale_one(ops.mult(c, c))
+    v = ops.rotate_and_sum(sq, *lay.norm_ladder(), lay.radix_bits)
+    z = _masked(ops, plan, v, real * (2.0 / (dr * (cfg.hi - cfg.lo))), primes[v.top - 1], primes)
+    z0 = A._pt(ops, plan, real * ((2 * cfg.eps - cfg.lo - cfg.hi) / (cfg.hi - cfg.lo)), z.top, z.scale, lay.slots)
+    z = ops.add_pt(z, z0)
+    inv = A.poly7(ops, plan, z, cfg.coeffs(), real, primes, lay.slots)
+    return ops.rescale_one(ops.mult(ops.drop_to(c, inv.top), inv))
+
+
+def _masked(ops, plan, x, values, target_scale, primes):
     """x * values (a plaintext of the plan), rescaled, landing at target_scale one level below x."""
     pscale = target_scale * primes[x.top] / x.scale
-    pt = A._pt(ops, cache.plan, values, x.top, pscale, cache.lay.slots)
+    pt = A._pt(ops, plan, values, x.top, pscale, x.slots)
     return ops.rescale_one(ops.mult_pt(x, pt, pscale))
 
 
@@ -179,35 +237,46 @@ def _linear(ops, cache, name, W, b, top, scale):
     return lin
 
 
-def decode(ops, x_ct, w, cache, coeffs, primes):
-    """One token: x_ct the activation (projection layout, at the cache's level + 2), w the block's Weights. Pushes the
-    token's K and V into the cache and returns the block's output (projection layout)."""
+def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
+    """One token: x_ct the activation (projection layout), w the block's Weights (with norm: gamma and beta folded in by
+    fold_norm). With norm the activation is layer-normalized first (8 levels); it must then sit at the cache's level
+    + 10, else + 2. Pushes the token's K and V into the cache and returns the block's output (projection layout), plus
+    the activation itself with residual."""
     lay = cache.lay
     rb = lay.radix_bits
+    x_in = x_ct
+    if norm is not None:
+        x_ct = layer_norm(ops, x_ct, lay, cache.plan, norm, primes)
     if x_ct.top != cache.top + 2:
-        raise ValueError(f"activation at top {x_ct.top}; the cache lives at {cache.top} (= the activation's - 2)")
+        raise ValueError(f"activation at top {x_ct.top} after the norm; the cache lives at {cache.top} (= that - 2)")
     lins = [_linear(ops, cache, n, W, b, x_ct.top, x_ct.scale)
             for n, W, b in (("q", w.wq, w.bq), ("k", w.wk, w.bk), ("v", w.wv, w.bv))]
     q, k, v = LIN.linear_multi(ops, x_ct, lins, rb)
     # the token's K and V rows: lane 0 kept, at the cache's scale
-    kv = _masked(ops, cache, ops.stack([k, v]), lay.lane0(), cache.scale, primes)
+    kv = _masked(ops, cache.plan, ops.stack([k, v]), lay.lane0(), cache.scale, primes)
     kr, vr = ops.split(kv, 2)
     cache.push(kr, vr)
     # the query: lane 0 with 1 / sqrt(d_h), at q_top 2^10 so the products land near the primes' size
-    qm = _masked(ops, cache, q, lay.lane0(1.0 / math.sqrt(lay.head_dim)), primes[q.top - 1] * 2.0**10, primes)
+    qm = _masked(ops, cache.plan, q, lay.lane0(1.0 / math.sqrt(lay.head_dim)), primes[q.top - 1] * 2.0**10, primes)
     qr = ops.rotate_and_sum(qm, *lay.query_ladder(), rb)
     qb = ops.stack([qr] * lay.blocks) if lay.blocks > 1 else qr
     yb = A.attend(ops, qb, cache, coeffs, primes)
     y = ops.sum(ops.split(yb, lay.blocks)) if lay.blocks > 1 else yb
     # the lane sums leave partial sums in lanes 1 .. t-1; the projection's replication ladder needs them zero
-    y = _masked(ops, cache, y, lay.lane0(), y.scale, primes)
+    y = _masked(ops, cache.plan, y, lay.lane0(), y.scale, primes)
     lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)
-    return LIN.linear(ops, y, lin_o, rb)
+    out = LIN.linear(ops, y, lin_o, rb)
+    if residual:  # x + block(x): the scales agree to the last bits (both ~2^40), the sum takes the output's
+        out = ops.add(out, ops.drop_to(x_in, out.top))
+    return out
 
 
-def plain_decode(x, w, K, V, coeffs, heads, head_dim):
-    """fp64 reference of the step: projections, the token appended to the cache, per-head attention with the same
-    polynomial softmax, output projection."""
+def plain_decode(x, w, K, V, coeffs, heads, head_dim, norm=None, residual=False):
+    """fp64 reference of the step: (the same polynomial LayerNorm,) projections, the token appended to the cache,
+    per-head attention with the same polynomial softmax, output projection (, plus x)."""
+    x_in = x
+    if norm is not None:
+        x = norm.plain(x)
     q, k, v = x @ w.wq + w.bq, x @ w.wk + w.bk, x @ w.wv + w.bv
     Ka, Va = np.vstack([K, k]), np.vstack([V, v])
     out = np.zeros(heads * head_dim)
@@ -215,4 +284,5 @@ def plain_decode(x, w, K, V, coeffs, heads, head_dim):
         sl = slice(h * head_dim, (h + 1) * head_dim)
         s = Ka[:, sl] @ q[sl] / math.sqrt(head_dim)
         out[sl] = A.poly_eval(coeffs, s) @ Va[:, sl]
-    return out @ w.wo + w.bo
+    y = out @ w.wo + w.bo
+    return y + x_in if residual else y

@@ -40,3 +40,43 @@ def test_block_decode_on_the_oracle(radix):
     got = B.LIN.output_values(ops.decrypt_slots(y).real, lay.geo, n)
     want = B.plain_decode(x, w, K, V, coeffs, 4, 8)
     assert np.abs(got - want).max() < 1e-3, np.abs(got - want).max()
+
+
+def test_block_with_norm_and_residual_on_the_oracle():
+    """LayerNorm (polynomial inverse square root, gamma and beta folded into Q/K/V), the block, the residual."""
+    lay = B.layout(1 << (LOGN - 1), 32, heads=4, head_dim=8, tokens=16, radix_bits=2)
+    q = O.ntt_primes(50, LOGN, 21)
+    p = O.ntt_primes(50, LOGN, 3, skip=21)
+    c = O.Ctx(LOGN, q, p, 7)
+    c.keygen(seed=0, h=64, sigma=3.2, galois=[1] + [O.lib().orc_rotation_galois(s, LOGN) for s in lay.rot_steps()])
+    ops = OracleOps(c)
+    rng = np.random.default_rng(10)
+    n, pre = 32, 3
+    w = _weights(rng, n)
+    gamma, beta = 1 + rng.normal(0, 0.1, n), rng.normal(0, 0.1, n)
+    wf = B.fold_norm(w, gamma, beta)
+    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+    x = rng.normal(0, 1, n)
+    norm = B.NormCfg(lo=0.25, hi=4.0)
+    u = ((x - x.mean()) ** 2).mean()
+    assert norm.lo < u < norm.hi
+    top = c.nq - 1
+    cache = B.LaneCache(ops, lay, top - 10)
+    cache.load(K, V)
+    coeffs = A.softmax_poly(lay.tokens)
+    xc = ops.encrypt(B.LIN.input_vector(x, lay.geo), top, 2.0**40, lay.slots)
+    y = B.decode(ops, xc, wf, cache, coeffs, c.q, norm=norm, residual=True)
+    assert y.top == top - 18
+    got = B.LIN.output_values(ops.decrypt_slots(y).real, lay.geo, n)
+    # the reference applies gamma and beta after the polynomial norm, the encrypted path inside the linears
+    want = B.plain_decode(x, B.Weights(w.wq, w.bq, w.wk, w.bk, w.wv, w.bv, w.wo, w.bo), K, V, coeffs, 4, 8,
+                          norm=_Affine(norm, gamma, beta), residual=True)
+    assert np.abs(got - want).max() < 1e-3, np.abs(got - want).max()
+
+
+class _Affine:
+    def __init__(self, norm, gamma, beta):
+        self.norm, self.gamma, self.beta = norm, gamma, beta
+
+    def plain(self, x):
+        return self.norm.plain(x) * self.gamma + self.beta

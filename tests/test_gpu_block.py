@@ -47,3 +47,36 @@ def test_block_decode_bit_exact(radix):
     got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
     want = B.plain_decode(x, w, K, V, coeffs, 4, 64)
     assert np.abs(got - want).max() < 1e-3
+
+
+def test_block_with_norm_bit_exact():
+    """LayerNorm (gamma, beta folded into Q/K/V), the block over one token block, the residual: GPU = oracle word for
+    word (21-limb FP64 chain at N = 2^14)."""
+    ch = fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 21)), tuple(fhe.ntt_primes(50, 14, 3, skip=21)), 7)
+    lay = B.layout(ch.n // 2, 256, heads=4, head_dim=64, tokens=32, radix_bits=2)
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=3, seed=0)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(0, 192, 3.2, s.galois)
+    oops = OracleOps(o)
+    rng = np.random.default_rng(13)
+    n, pre = 256, 9
+    w = B.Weights(*[rng.normal(0, 0.05, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+    gamma, beta = 1 + rng.normal(0, 0.1, n), rng.normal(0, 0.1, n)
+    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+    x = rng.normal(0, 1, n)
+    norm = B.NormCfg()
+    top = s.top()
+    coeffs = A.softmax_poly(lay.tokens)
+    outs = []
+    for ops in (s, oops):
+        cache = B.LaneCache(ops, lay, top - 10)
+        cache.load(K, V)
+        xc = ops.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots)
+        outs.append(B.decode(ops, xc, B.fold_norm(w, gamma, beta), cache, coeffs, ch.q, norm=norm, residual=True))
+    y, oy = outs
+    assert y.top == oy.top == top - 18
+    assert (host(y.data[0])[:, : y.top + 1] == oy.data[:, : y.top + 1]).all()
+    got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
+    xn = norm.plain(x) * gamma + beta
+    want = B.plain_decode(xn, w, K, V, coeffs, 4, 64) + x
+    assert np.abs(got - want).max() < 1e-3

@@ -1319,7 +1319,9 @@ int pcb_rotate_hoisted(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32
         rc = modup(*c, c1, top, K, s);
         if (rc) return rc;
     }
-    if (c->ext_groups > 1) {  // FP64 chains: the steps' inner products in groups sharing one read of the digits
+    // FP64 chains of up to 4 digits at this level: the steps' inner products in groups sharing one read of the digits
+    const bool grouped = c->ext_groups > 1 && c->lv[top].ndig <= 4;
+    if (grouped) {
         std::vector<int> todo;
         for (int i = 0; i < nsteps; ++i)
             if (keys[i]) todo.push_back(i);
@@ -1336,7 +1338,7 @@ int pcb_rotate_hoisted(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32
         }
     }
     for (int i = 0; i < nsteps; ++i) {
-        if (keys[i] && c->ext_groups > 1) continue;
+        if (keys[i] && grouped) continue;
         if (!keys[i]) {
             PcbEwArgs e;
             memset(&e, 0, sizeof e);
@@ -1403,7 +1405,7 @@ int pcb_rotate_sum(PcbCtx* c, const uint64_t* x, const int64_t* steps, int32_t n
     const uint64_t* c1 = x + (size_t)c->rows * c->n;
     rc = modup(*c, c1, top, K, s);
     if (rc) return rc;
-    if (c->f64) {  // every key's products summed in registers, SUM_KEYS_MAX keys per launch
+    if (c->f64 && c->lv[top].ndig <= 4) {  // every key's products summed in registers, SUM_KEYS_MAX keys per launch
         for (int i0 = 0; i0 < nsteps; i0 += ks::SUM_KEYS_MAX) {
             const int n = std::min(nsteps - i0, ks::SUM_KEYS_MAX);
             rc = dot_sum(*c, keys.data() + i0, n, c1, x, i0 == 0 ? 1 : 1 | PCB_KS_ACC, top, K, s);

@@ -353,9 +353,12 @@ def run_ours(a):
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
-                rate, cores, dt = cpu_rate(2)
+                rate, _, _ = cpu_rate(2)  # the estimate that sizes a ~10 s sample
+                ns = max(2, min(2000, int(10.0 * rate)))
+                rate, cores, dt = cpu_rate(ns)
                 line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                                        "sample": f"2 rotation key switches of one config-2 ciphertext ({dt:.1f} s)"}
+                                        "sample": f"{ns} rotation key switches of one config-2 ciphertext "
+                                                  f"({dt:.1f} s)"}
             except Exception as e:  # the baseline is reported, never required
                 line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": None, "kind": "port",
                                         "sample": f"failed: {e}"}

@@ -132,7 +132,15 @@ typedef struct PcbKsArgs {
     int32_t K, R, ndig, c0_mode, nq, nrows;
 } PcbKsArgs;
 
-/* args.cuh:258-271 (relin epilogue), :273-283 (KeyTab), :285-304 (KsRegenArgs); ks_dot_regen is not provided */
+/* args.cuh:258-271 (relin epilogue), :273-283 (KeyTab), :285-304 (KsRegenArgs), :764-768 (KsKeyArgs).
+ * ks_dot_regen: the relinearization inner product (K <= 4, no automorphism, no c0 term) with the key's `a`
+ * regenerated from `seed` by the frozen u64 expander lane (w13 = digit, the row's prime), `b` from ks.kb[0] (dense
+ * prime-id rows, key_digit_stride) or, with key.kb set, key 0 of the table (dense rows in the key's slot order);
+ * use_epi writes dst = f (alpha dst + (dot - conv) binv) [+ k on part 0] [+ add] on both parts instead of out0/out1.
+ * ks_dot_key: ks_dot (K <= 4 x R keys, automorphism, c0 modes, PCB_KS_ACC) with the keys read through the table:
+ * `a` regenerated for digits below key.nregen (key.seed[r]), else ks.ka[r]; `b` dense in the key's slot order
+ * (Q id t <= q_top at slot t, special id nq + j at q_top + 1 + j; q_top < 0: slot = prime id). Packed `b` rows
+ * (key.bits != 0, the reference's 32-bit words) are refused. */
 typedef struct PcbEpiArgs {
     void* dst;
     const void* conv;
@@ -158,6 +166,10 @@ typedef struct PcbKsRegenArgs {
     PcbKeyTab key;
     const void* add;
 } PcbKsRegenArgs;
+typedef struct PcbKsKeyArgs {
+    PcbKsArgs ks;
+    PcbKeyTab key;
+} PcbKsKeyArgs;
 
 /* args.cuh:306-323: out[d][m][N] = expander(seed, digit d, prime prime_ids[m]) (u64: the frozen KSKB lane) */
 typedef struct PcbKskExpandArgs {
@@ -328,8 +340,9 @@ typedef struct PcbKernelTable {
     PcbLaunch encode;
     int (*encrypt)(const PcbEncryptArgs*, cudaStream_t);
     int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
-    PcbLaunch ksk_unpack, mod_raise, small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen,
-        ks_dot_key, pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum;
+    PcbLaunch ksk_unpack, mod_raise, small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
+    int (*ks_dot_key)(const PcbKsKeyArgs*, cudaStream_t);
+    PcbLaunch pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum;
     int (*mul_add)(const PcbMulAddArgs*, cudaStream_t);
     PcbLaunch rescale_fwd;
     int (*mul_add_n)(const PcbMulAddNArgs*, cudaStream_t);
@@ -509,6 +522,7 @@ static_assert(sizeof(PcbKsArgs) == 176, "KsArgs layout");
 static_assert(sizeof(PcbEpiArgs) == 72, "EpiArgs layout");
 static_assert(sizeof(PcbKeyTab) == 40, "KeyTab layout");
 static_assert(sizeof(PcbKsRegenArgs) == 312, "KsRegenArgs layout");
+static_assert(sizeof(PcbKsKeyArgs) == 216, "KsKeyArgs layout");
 static_assert(sizeof(PcbKskExpandArgs) == 48, "KskExpandArgs layout");
 static_assert(sizeof(PcbTensorArgs) == 192, "TensorArgs layout");
 static_assert(sizeof(PcbMdEpiArgs) == 120, "MdEpiArgs layout");

@@ -73,6 +73,10 @@ class KsRegenArgs(C.Structure):
                 ("key", KeyTab), ("add", vp)]
 
 
+class KsKeyArgs(C.Structure):
+    _fields_ = [("ks", KsArgs), ("key", KeyTab)]
+
+
 class KskExpandArgs(C.Structure):
     _fields_ = [("out", vp), ("seed", vp), ("prime_ids", vp), ("pr", vp), ("nmod", C.c_int32), ("dnum", C.c_int32),
                 ("d0", C.c_int32), ("pad", C.c_int32)]
@@ -172,7 +176,7 @@ class Params(C.Structure):
 SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJob": 32, "BconvArgs": 56,
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
-         "EncryptArgs": 64, "KskGenArgs": 120, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
+         "EncryptArgs": 64, "KskGenArgs": 120, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
          "MulAddArgs": 104, "MulAddNArgs": 328, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
 
 _lib = None

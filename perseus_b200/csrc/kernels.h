@@ -69,6 +69,10 @@ template <int LOGN> int dot_sum_run(const PcbKsArgs*, const KeySum&, cudaStream_
 // f64: every prime below 2^50 (FP64 products)
 template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, cudaStream_t);
 }  // namespace ks
+namespace regen {
+template <int LOGN> int ks_dot_regen_launch(const PcbKsRegenArgs*, cudaStream_t);
+template <int LOGN> int ks_dot_key_launch(const PcbKsKeyArgs*, cudaStream_t);
+}  // namespace regen
 namespace keys {
 template <int LOGN> int ksk_expand_launch(const PcbKskExpandArgs*, cudaStream_t);
 template <int LOGN> int encrypt_launch(const PcbEncryptArgs*, cudaStream_t);

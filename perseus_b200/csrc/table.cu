@@ -5,7 +5,6 @@
 
 namespace {
 int absent(const void*, cudaStream_t) { return -1; }
-int no_regen(const PcbKsRegenArgs*, cudaStream_t) { return -1; }
 
 template <int LOGN>
 PcbKernelTable make_table() {
@@ -25,7 +24,8 @@ PcbKernelTable make_table() {
     t.ew_sub_mul = elem::ew_launch<LOGN, elem::SUB_MUL>;
     t.ew_copy = elem::ew_launch<LOGN, elem::COPY>;
     t.ks_dot = ks::ks_dot_launch<LOGN>;
-    t.ks_dot_regen = no_regen;
+    t.ks_dot_regen = regen::ks_dot_regen_launch<LOGN>;
+    t.ks_dot_key = regen::ks_dot_key_launch<LOGN>;
     t.ksk_expand = keys::ksk_expand_launch<LOGN>;
     t.pt_dot = pt::pt_dot_launch<LOGN>;
     t.add_const = pt::add_const_launch<LOGN>;

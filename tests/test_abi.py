@@ -122,3 +122,25 @@ def test_chain_primes():
     assert len(c2.q) == 24 and len(c2.p) == 8 and all(x.bit_length() == 50 for x in c2.q + c2.p)
     assert len(set(c2.q + c2.p)) == 32
     assert all((x - 1) % (2 << 16) == 0 for x in c2.q + c2.p)
+
+
+def test_regen_entries_refuse_out_of_range():
+    """ks_dot_regen / ks_dot_key: K in [0, 4], packed `b` rows (the reference's 32-bit words) refused on the host."""
+    t = L.kernel_table()
+    k = L.KsArgs()
+    k.c1, k.modup, k.rows, k.digit_of, k.pr, k.kb = 0x1000, 0x1000, 0x2000, 0x2000, 0x2000, 0x3000
+    k.out0 = k.out1 = 0x4000
+    k.ndig, k.nrows, k.nq = 2, 1, 1
+    r = L.KsRegenArgs()
+    r.ks, r.seed = k, 0x5000
+    r.ks.K = 5
+    assert t.ks_dot_regen(C.cast(C.pointer(r), C.c_void_p), None) == -1
+    r.ks.K, r.key.kb, r.key.srows, r.key.bits = 1, 0x6000, 2, 28
+    assert t.ks_dot_regen(C.cast(C.pointer(r), C.c_void_p), None) == -1
+    a = L.KsKeyArgs()
+    a.ks = k
+    a.ks.K, a.ks.R, a.ks.autok = 1, 1, 0x7000
+    a.key.kb, a.key.seed, a.key.srows, a.key.bits = 0x6000, 0x5000, 2, 28
+    assert t.ks_dot_key(C.cast(C.pointer(a), C.c_void_p), None) == -1
+    a.key.bits, a.ks.K = 0, 9
+    assert t.ks_dot_key(C.cast(C.pointer(a), C.c_void_p), None) == -1

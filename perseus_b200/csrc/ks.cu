@@ -711,6 +711,74 @@ __global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
     for (; cb < a.K; ++cb) dot_sum_chunk<LOGN, ND, 1>(a, ks, w, src, o, cb);
 }
 
+// One ciphertext (K = 1): the keys split over the CTA's 4 warps for the same 32 output slots (warp w takes keys w,
+// w + 4), each warp's partial sum canonical in shared memory, warp 0 adding them up: four warps' loads in flight per
+// slot where the one-thread-per-slot form walks the keys one after another.
+constexpr int SUM1_WARPS = 4;
+template <int LOGN, int ND>
+__global__ void __launch_bounds__(32 * SUM1_WARPS) dot_sum1_f(PcbKsArgs a, KeySum ks) {
+    __shared__ uint64_t part[2][SUM1_WARPS][32];
+    const uint32_t t = a.rows[blockIdx.y];
+    const uint64_t p = a.pr[t].p;
+    const double pf = to_f(p), pinv = 1.0 / pf;
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const uint32_t o = blockIdx.x * 32 + lane;
+    const int dt = (int)t < a.nq ? a.digit_of[t] : -1;
+    const size_t row = (size_t)t << LOGN;
+    const uint64_t* c1 = (const uint64_t*)a.c1;
+    const uint64_t* mu = (const uint64_t*)a.modup;
+    const uint64_t* c0 = (const uint64_t*)a.c0;
+    const bool addc0 = (a.c0_mode & 3) == 1 && (int)t < a.nq;
+    uint64_t pm = 0, pms = 0;
+    if (addc0) {
+        pm = ((const uint64_t*)a.pmod)[t];
+        pms = ((const uint64_t*)a.pmods)[t];
+    }
+    double s0 = 0.0, s1 = 0.0;
+    uint64_t cs = 0;  // this warp's keys' P sigma(c0) terms
+    for (int r = wp; r < ks.n; r += SUM1_WARPS) {
+        const size_t off = row + automorph_slot<LOGN>(ks.g[r], o);
+        uint64_t kbv[ND], kav[ND], xw[ND];
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            kbv[d] = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
+            kav[d] = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
+            xw[d] = __ldg(d == dt ? c1 + off : mu + (size_t)d * a.mu_digit_stride + off);
+        }
+        const uint64_t cw = addc0 ? __ldg(c0 + off) : 0;
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+            const double bw = kbv[d] > p / 2 ? -to_f(p - kbv[d]) : to_f(kbv[d]);
+            const double aw = kav[d] > p / 2 ? -to_f(p - kav[d]) : to_f(kav[d]);
+            const double x = to_f(xw[d]);
+            s0 = __dadd_rn(s0, mul_f(x, bw, __dmul_rn(bw, pinv), pf));
+            s1 = __dadd_rn(s1, mul_f(x, aw, __dmul_rn(aw, pinv), pf));
+        }
+        // at most ND <= 4 products since the last reduction: |s| < 9 p < 2^53
+        s0 = red_f(s0, pf, pinv);
+        s1 = red_f(s1, pf, pinv);
+        if (addc0) cs = add_mod(cs, shoup(cw, pm, pms, p), p);
+    }
+    part[0][wp][lane] = add_mod(canon_f(s0, pf, pinv), cs, p);
+    part[1][wp][lane] = canon_f(s1, pf, pinv);
+    __syncthreads();
+    if (wp == 0) {
+        uint64_t r0 = part[0][0][lane], r1 = part[1][0][lane];
+#pragma unroll
+        for (int w = 1; w < SUM1_WARPS; ++w) {
+            r0 = add_mod(r0, part[0][w][lane], p);
+            r1 = add_mod(r1, part[1][w][lane], p);
+        }
+        const size_t ob = row + o;
+        if (a.c0_mode & PCB_KS_ACC) {
+            r0 = add_mod(r0, ((const uint64_t*)a.out0)[ob], p);
+            r1 = add_mod(r1, ((const uint64_t*)a.out1)[ob], p);
+        }
+        ((uint64_t*)a.out0)[ob] = r0;
+        ((uint64_t*)a.out1)[ob] = r1;
+    }
+}
+
 template <int LOGN, int ND>
 void dot_keys_dispatch(const PcbKsArgs& a, const KeyGroup& kg, dim3 g, cudaStream_t s) {
     switch (kg.n) {
@@ -757,6 +825,16 @@ int dot_sum_run(const PcbKsArgs* ap, const KeySum& ks, cudaStream_t s) {
     if ((a.c0_mode & 3) == 1 && (!a.c0 || !a.pmod || !a.pmods)) return PCB_BAD_ARGS;
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
     if (a.K == 0 || a.nrows == 0) return 0;
+    if (a.K == 1) {
+        const dim3 g1((1 << LOGN) / 32, a.nrows);
+        switch (a.ndig) {
+            case 1: dot_sum1_f<LOGN, 1><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
+            case 2: dot_sum1_f<LOGN, 2><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
+            case 3: dot_sum1_f<LOGN, 3><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
+            default: dot_sum1_f<LOGN, 4><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks);
+        }
+        return PCB_LAUNCH_RESULT();
+    }
     const dim3 g((1 << LOGN) / BX, a.nrows);
     switch (a.ndig) {
         case 1: dot_sum_f<LOGN, 1, 4><<<g, BX, 0, s>>>(a, ks); break;

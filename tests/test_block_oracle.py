@@ -80,3 +80,24 @@ class _Affine:
 
     def plain(self, x):
         return self.norm.plain(x) * self.gamma + self.beta
+
+
+@pytest.mark.parametrize("radix", [1, 2, 3])
+def test_lane_layout_invariants(radix):
+    """GPT-2's lane layout: every lane reachable by rotations whose keys the layout generates; the score mask on lane
+    tau of each head's first element block; lane 0 of the real elements; the ladders' spans."""
+    lay = B.layout(1 << 15, 1024, heads=12, head_dim=64, tokens=128, radix_bits=radix)
+    assert (lay.t, lay.blocks, lay.width) == (32, 4, 768)
+    keys = {s % lay.slots for s in lay.rot_steps()}
+    for lane in range(lay.t):
+        steps = lay.push_steps(lane)
+        assert -sum(steps) == lane and all(s % lay.slots in keys for s in steps)
+        assert len(steps) <= (2 if radix == 3 else 5)
+    m = lay.mask()
+    assert m.sum() == 12 * 32 and all(m[h * 64 * 32 + tau] == 1 for h in range(12) for tau in range(32))
+    l0 = lay.lane0(0.5)
+    assert (np.flatnonzero(l0) == np.arange(768) * 32).all() and l0.max() == 0.5
+    assert lay.score_ladder() == (32, 2048) and lay.replicate_ladder() == (-32, 2048)
+    assert lay.sum_ladder() == (1, 32) and lay.norm_ladder() == (32, 32 * 1024)
+    with pytest.raises(ValueError):
+        B.layout(1 << 15, 1024, heads=12, head_dim=64, tokens=100)

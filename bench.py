@@ -324,6 +324,7 @@ def run_ours(a):
     attn, attn_err = attention_decode(a, world, rank, barrier, dist)
     proj = projection(a, world, barrier, dist)
     blk = block_decode(a, world, barrier, dist)
+    blk["batch_of_4"] = block_decode(a, world, barrier, dist, seqs=4)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -484,7 +485,7 @@ def projection(a, world, barrier, dist):
                         "ladders", "qkv_ms": t[0].item(), "out_ms": t[1].item(), "max_abs_err_vs_fp64": err}
 
 
-def block_decode(a, world, barrier, dist):
+def block_decode(a, world, barrier, dist, seqs=1):
     """Config 3's attention block, one token per step: the polynomial LayerNorm (gamma, beta folded into Q/K/V), Q/K/V
     projections, the token's K and V pushed into the lane cache (128 tokens in 4 blocks of 32, all 12 heads per
     block), attention over the cache, output projection, residual (perseus_b200.block; N = 2^16 with the 24-limb
@@ -500,20 +501,22 @@ def block_decode(a, world, barrier, dist):
 
     ch = fhe.config2_chain()
     lay = B.layout(ch.n // 2, 1024, heads=12, head_dim=64, tokens=128, radix_bits=3)
-    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=4, seed=0)
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=max(lay.blocks, 3) * seqs, seed=0)
     rng = np.random.default_rng(11)
     warm, steps = max(a.warmup, 3), min(a.steps, 64)  # the cache holds 128 tokens: the steps fill its last lanes
     n, pre, top = 768, lay.tokens - warm - steps, len(ch.q) - 1
     w = B.Weights(*[rng.normal(0, 0.02, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
     gamma, beta = 1 + rng.normal(0, 0.02, n), rng.normal(0, 0.02, n)
     wf, norm = B.fold_norm(w, gamma, beta), B.NormCfg()
-    K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
-    cache = B.LaneCache(s, lay, top - 10)
-    cache.load(K, V)
+    Ks = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
+    Vs = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
+    cache = B.LaneCache(s, lay, top - 10, seqs=seqs)
+    cache.load(Ks if seqs > 1 else Ks[0], Vs if seqs > 1 else Vs[0])
     coeffs = A.softmax_poly(lay.tokens)
-    xs = [rng.normal(0, 1, n) for _ in range(warm + steps)]
-    cts = [s.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots) for x in xs]
-    Kp, Vp = [K], [V]
+    xs = [[rng.normal(0, 1, n) for _ in range(seqs)] for _ in range(warm + steps)]
+    cts = [s.stack([s.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots) for x in xq])
+           for xq in xs]
+    Kp, Vp = [Ks[0]], [Vs[0]]
     y = None
     for i in range(warm):
         y = B.decode(s, cts[i], wf, cache, coeffs, ch.q, norm=norm, residual=True)
@@ -527,25 +530,30 @@ def block_decode(a, world, barrier, dist):
     e1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")  # per step of all sequences
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    # the fp64 step of the last token, with every earlier token's K and V rows appended as the cache saw them
-    for x in xs[:-1]:
-        xn = norm.plain(x) * gamma + beta
+    # sequence 0's fp64 step of the last token, with its earlier tokens' K and V rows appended as the cache saw them
+    for xq in xs[:-1]:
+        xn = norm.plain(xq[0]) * gamma + beta
         Kp.append((xn @ w.wk + w.bk)[None])
         Vp.append((xn @ w.wv + w.bv)[None])
-    want = B.plain_decode(norm.plain(xs[-1]) * gamma + beta, w, np.vstack(Kp), np.vstack(Vp), coeffs, 12, 64) + xs[-1]
-    got = B.LIN.output_values(s.decrypt_slots(y).real, lay.geo, n)
+    want = B.plain_decode(norm.plain(xs[-1][0]) * gamma + beta, w, np.vstack(Kp), np.vstack(Vp), coeffs, 12, 64) + \
+        xs[-1][0]
+    got = B.LIN.output_values(s.decrypt_slots(y, 0).real, lay.geo, n)
     err = float(np.abs(got - want).max())
     del s, cache, cts, y
     torch.cuda.empty_cache()
-    return {"workload": "config 3 attention block, one token: LayerNorm (degree-7 inverse square root), Q/K/V "
-                        "projections (768 of 1024), push into a 128-token lane cache (4 blocks x 32 tokens, 12 heads "
-                        "x 64 per block), attention with the degree-7 polynomial softmax, output projection, "
-                        "residual; N=2^16 24+8 limbs, radix-3 ladders, eager",
-            "ms_per_token": t.item(), "timed_tokens": steps, "max_abs_err_vs_fp64": err,
-            "tokens_in_cache_at_end": pre + len(xs)}
+    out = {"workload": "config 3 attention block, one token: LayerNorm (degree-7 inverse square root), Q/K/V "
+                       "projections (768 of 1024), push into a 128-token lane cache (4 blocks x 32 tokens, 12 heads "
+                       "x 64 per block), attention with the degree-7 polynomial softmax, output projection, "
+                       "residual; N=2^16 24+8 limbs, radix-3 ladders, eager",
+           "ms_per_token": t.item(), "timed_tokens": steps, "max_abs_err_vs_fp64": err,
+           "tokens_in_cache_at_end": pre + len(xs)}
+    if seqs > 1:
+        out = {"sequences": seqs, "ms_per_step": t.item(), "tokens_per_s": seqs / (t.item() * 1e-3),
+               "max_abs_err_vs_fp64_seq0": err}
+    return out
 
 
 def main():
@@ -554,7 +562,8 @@ def main():
         print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
         return
     if a.part == "block":
-        print(json.dumps({"part": "block", **block_decode(a, 1, lambda: None, None)}), flush=True)
+        print(json.dumps({"part": "block", **block_decode(a, 1, lambda: None, None),
+                          "batch_of_4": block_decode(a, 1, lambda: None, None, seqs=4)}), flush=True)
         return
     if a.part == "attention":
         ms, err = attention_decode(a, 1, 0, lambda: None, None)

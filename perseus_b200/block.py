@@ -129,10 +129,12 @@ class Weights:
 
 class LaneCache:
     """The encrypted K and V caches as batches of token blocks, at the level the pushed rows arrive at; the decode
-    step's plaintexts (masks, encoded weights) are kept in `plan`."""
+    step's plaintexts (masks, encoded weights) are kept in `plan`. `seqs` independent sequences decode together (one
+    token each per step, at the same position): their blocks are batch members s blocks + b, every op of the step
+    runs on all of them."""
 
-    def __init__(self, ops, lay, top, scale=2.0**40):
-        self.ops, self.lay, self.top, self.scale = ops, lay, top, scale
+    def __init__(self, ops, lay, top, scale=2.0**40, seqs=1):
+        self.ops, self.lay, self.top, self.scale, self.seqs = ops, lay, top, scale, seqs
         self.k = self.v = None
         self.count = 0
         self.plan = {}
@@ -143,20 +145,22 @@ class LaneCache:
         for tok, row in enumerate(rows):
             b, lane = divmod(tok, lay.t)
             vecs[b][np.arange(lay.width) * lay.t + lane] = row
-        cts = [self.ops.encrypt(v, top=self.top, scale=self.scale, slots=lay.slots) for v in vecs]
-        return self.ops.stack(cts)
+        return [self.ops.encrypt(v, top=self.top, scale=self.scale, slots=lay.slots) for v in vecs]
 
     def load(self, K, V):
-        """The client's cache of n tokens (n x d_real each), one encryption per block."""
-        if K.shape[0] > self.lay.tokens:
-            raise ValueError("more tokens than the cache holds")
-        self.k, self.v = self._blocks(K), self._blocks(V)
-        self.count = K.shape[0]
+        """The client's cache of n tokens (n x d_real each; with seqs > 1 a list of one such array per sequence, all of
+        n tokens), one encryption per block."""
+        Ks, Vs = (K, V) if self.seqs > 1 else ([K], [V])
+        if len(Ks) != self.seqs or len({k.shape[0] for k in Ks}) != 1 or Ks[0].shape[0] > self.lay.tokens:
+            raise ValueError(f"{self.seqs} caches of one token count up to {self.lay.tokens}")
+        self.k = self.ops.stack([c for k in Ks for c in self._blocks(k)])
+        self.v = self.ops.stack([c for v in Vs for c in self._blocks(v)])
+        self.count = Ks[0].shape[0]
 
     def push(self, k_row, v_row):
-        """The token's K and V rows (one batch of two at this cache's level and scale, each value at lane 0 of its
+        """The token's K and V rows (batches of `seqs`, at this cache's level and scale, each value at lane 0 of its
         element block, nothing in the other lanes) rotated to the token's lane and added into its block."""
-        ops, lay = self.ops, self.lay
+        ops, lay, S = self.ops, self.lay, self.seqs
         if self.count >= lay.tokens:
             raise ValueError(f"KV cache full ({lay.tokens} tokens)")
         b, lane = divmod(self.count, lay.t)
@@ -164,8 +168,11 @@ class LaneCache:
         for st in lay.push_steps(lane):
             kv = ops.rotate(kv, st)
         kr, vr = ops.split(kv, 2)
-        ops.inplace_add(ops.split(self.k, lay.blocks)[b], kr)
-        ops.inplace_add(ops.split(self.v, lay.blocks)[b], vr)
+        kblk, vblk = ops.split(self.k, S * lay.blocks), ops.split(self.v, S * lay.blocks)
+        krs, vrs = (ops.split(kr, S), ops.split(vr, S)) if S > 1 else ([kr], [vr])
+        for q in range(S):
+            ops.inplace_add(kblk[q * lay.blocks + b], krs[q])
+            ops.inplace_add(vblk[q * lay.blocks + b], vrs[q])
         self.count += 1
 
 
@@ -238,10 +245,10 @@ def _linear(ops, cache, name, W, b, top, scale):
 
 
 def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
-    """One token: x_ct the activation (projection layout), w the block's Weights (with norm: gamma and beta folded in by
-    fold_norm). With norm the activation is layer-normalized first (8 levels); it must then sit at the cache's level
-    + 10, else + 2. Pushes the token's K and V into the cache and returns the block's output (projection layout), plus
-    the activation itself with residual."""
+    """One token: x_ct the activation (projection layout; a batch of cache.seqs, one per sequence), w the block's
+    Weights (with norm: gamma and beta folded in by fold_norm). With norm the activation is layer-normalized first (8
+    levels); it must then sit at the cache's level + 10, else + 2. Pushes the token's K and V into the cache and
+    returns the block's output (projection layout), plus the activation itself with residual."""
     lay = cache.lay
     rb = lay.radix_bits
     x_in = x_ct
@@ -259,9 +266,15 @@ def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
     # the query: lane 0 with 1 / sqrt(d_h), at q_top 2^10 so the products land near the primes' size
     qm = _masked(ops, cache.plan, q, lay.lane0(1.0 / math.sqrt(lay.head_dim)), primes[q.top - 1] * 2.0**10, primes)
     qr = ops.rotate_and_sum(qm, *lay.query_ladder(), rb)
-    qb = ops.stack([qr] * lay.blocks) if lay.blocks > 1 else qr
+    S, nb = cache.seqs, lay.blocks
+    qs = ops.split(qr, S) if S > 1 else [qr]
+    qb = ops.stack([x for x in qs for _ in range(nb)]) if S * nb > 1 else qr  # one copy per block, [sequence][block]
     yb = A.attend(ops, qb, cache, coeffs, primes)
-    y = ops.sum(ops.split(yb, lay.blocks)) if lay.blocks > 1 else yb
+    if nb > 1:  # each sequence's blocks summed
+        ys = ops.split(yb, S * nb)
+        y = ops.stack([ops.sum(ys[q * nb:(q + 1) * nb]) for q in range(S)]) if S > 1 else ops.sum(ys)
+    else:
+        y = yb
     # the lane sums leave partial sums in lanes 1 .. t-1; the projection's replication ladder needs them zero
     y = _masked(ops, cache.plan, y, lay.lane0(), y.scale, primes)
     lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)

@@ -101,3 +101,29 @@ def test_lane_layout_invariants(radix):
     assert lay.sum_ladder() == (1, 32) and lay.norm_ladder() == (32, 32 * 1024)
     with pytest.raises(ValueError):
         B.layout(1 << 15, 1024, heads=12, head_dim=64, tokens=100)
+
+
+def test_block_two_sequences_on_the_oracle():
+    """Two independent sequences decoded in one batched step: each output equals its own fp64 step."""
+    lay = B.layout(1 << (LOGN - 1), 32, heads=4, head_dim=8, tokens=32, radix_bits=3)
+    q = O.ntt_primes(50, LOGN, 12)
+    p = O.ntt_primes(50, LOGN, 3, skip=12)
+    c = O.Ctx(LOGN, q, p, 4)
+    c.keygen(seed=0, h=64, sigma=3.2, galois=[1] + [O.lib().orc_rotation_galois(s, LOGN) for s in lay.rot_steps()])
+    ops = OracleOps(c)
+    rng = np.random.default_rng(31)
+    n, pre, S = 32, 19, 2
+    w = _weights(rng, n)
+    Ks = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(S)]
+    Vs = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(S)]
+    xs = [rng.normal(0, 1, n) / 2 for _ in range(S)]
+    top = c.nq - 1
+    cache = B.LaneCache(ops, lay, top - 2, seqs=S)
+    cache.load(Ks, Vs)
+    coeffs = A.softmax_poly(lay.tokens)
+    xc = ops.stack([ops.encrypt(B.LIN.input_vector(x, lay.geo), top, 2.0**40, lay.slots) for x in xs])
+    y = B.decode(ops, xc, w, cache, coeffs, c.q)
+    for s_ in range(S):
+        got = B.LIN.output_values(ops.decrypt_slots(y, s_).real, lay.geo, n)
+        want = B.plain_decode(xs[s_], w, Ks[s_], Vs[s_], coeffs, 4, 8)
+        assert np.abs(got - want).max() < 1e-3, (s_, np.abs(got - want).max())

@@ -81,3 +81,35 @@ def test_block_with_norm_bit_exact():
     xn = norm.plain(x) * gamma + beta
     want = B.plain_decode(xn, w, K, V, coeffs, 4, 64) + x
     assert np.abs(got - want).max() < 1e-3
+
+
+def test_block_two_sequences_bit_exact():
+    """Two sequences decoded in one batched step (their caches one batch of 2 x 2 blocks): GPU = oracle word for word,
+    each output against its own fp64 step."""
+    ch = fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 12)), tuple(fhe.ntt_primes(50, 14, 3, skip=12)), 4)
+    lay = B.layout(ch.n // 2, 256, heads=4, head_dim=64, tokens=64, radix_bits=3)
+    S = 2
+    s = fhe.Session(ch, rot_steps=lay.rot_steps(), k_max=3 * S, seed=0)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(0, 192, 3.2, s.galois)
+    oops = OracleOps(o)
+    rng = np.random.default_rng(14)
+    n, pre = 256, 40
+    w = B.Weights(*[rng.normal(0, 0.05, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+    Ks = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(S)]
+    Vs = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(S)]
+    xs = [rng.normal(0, 1, n) / 2 for _ in range(S)]
+    top = s.top()
+    coeffs = A.softmax_poly(lay.tokens)
+    outs = []
+    for ops in (s, oops):
+        cache = B.LaneCache(ops, lay, top - 2, seqs=S)
+        cache.load(Ks, Vs)
+        xc = ops.stack([ops.encrypt(B.LIN.input_vector(x, lay.geo), top=top, scale=2.0**40, slots=lay.slots)
+                        for x in xs])
+        outs.append(B.decode(ops, xc, w, cache, coeffs, ch.q))
+    y, oy = outs
+    for q in range(S):
+        assert (host(y.data[q])[:, : y.top + 1] == oy.cts[q].data[:, : y.top + 1]).all(), q
+        got = B.LIN.output_values(s.decrypt_slots(y, q).real, lay.geo, n)
+        assert np.abs(got - B.plain_decode(xs[q], w, Ks[q], Vs[q], coeffs, 4, 64)).max() < 1e-3

@@ -43,8 +43,9 @@ def test_table_headers():
 
 def test_absent_entries_refuse():
     t = L.kernel_table()
-    assert t.ks_dot_regen(None, None) == -1 and t.tfhe(None, None) == -1 and t.pcmm(None, None) == -1
-    assert t.pt_dot(None, None) == -1  # a null argument pointer is refused by every entry
+    assert t.tfhe(None, None) == -1 and t.pcmm(None, None) == -1 and t.cts_fused(None, None) == -1
+    for n in ("pt_dot", "ks_dot_regen", "ks_dot_key", "ntt_fwd"):  # a null argument pointer: refused by every entry
+        assert getattr(t, n)(None, None) == -1, n
 
 
 def test_plaintext_entries_refuse_out_of_range():

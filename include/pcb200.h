@@ -449,8 +449,10 @@ int pcb_rescale(PcbCtx* ctx, uint64_t* ct, int32_t top, int32_t K, cudaStream_t 
  * arena: its working rows live in a fixed 16 MiB device array the library owns (every GPU that loads the library
  * holds it until exit). For callers that must not allocate device memory where they call it. No counterpart in the
  * reference. Limit: 2 (nq + kp) N <= 2^21 words, else -1 with a message. The first call on each device looks the
- * array's address up (make it before any stream capture); calls share the array, so calls that overlap on the GPU
- * (other streams, other threads) race — issue them in one stream order. */
+ * array's address up (make it before any stream capture) and keeps it for the life of the process (a cudaDeviceReset
+ * invalidates it: reload the library after one); the device current at the call must be the context's, else -1
+ * with a message. Calls share the array, so calls that overlap on the GPU (other streams, other threads) race —
+ * issue them in one stream order. */
 int pcb_rescale_static(PcbCtx* ctx, uint64_t* ct, int32_t top, cudaStream_t stream);
 /* out = rot(x, step), left by step slots (crates/pc-gpu/src/rotate.rs:147-204); out must not alias x */
 int pcb_rotate(PcbCtx* ctx, const uint64_t* x, int64_t step, uint64_t* out, int32_t top, int32_t K,

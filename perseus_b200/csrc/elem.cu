@@ -201,9 +201,22 @@ int md_epilogue_launch(const PcbMdEpiArgs* ap, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ rescale
-// ndrop 1 (the u64 chains here have one prime per level): tmp_i = A_i lift(y_top) with lift(y) = y - q_top when
-// y > q_top / 2, reduced mod q_i (crates/pc-host/src/rescale.rs:54-70)
-// two consecutive words per thread, one row per grid row (the top word is re-read per row from L2)
+// Composite rescale by the top ndrop primes (crates/pc-kernels/kernels/args.cuh:530-552; crates/pc-host/src/
+// rescale.rs:54-70), with lift(y, q) = the centred representative of y mod q (y > q / 2: y - q) reduced mod q_i:
+//   ndrop 1: tmp_i = A_i lift(y_a)
+//   ndrop 2: y' = qinv_ab y_b + C_ab lift(y_a) mod q_b, tmp_i = A_i lift(y_a) + B_i lift(y')
+// y_a = x_top (times ca when ca != 1), y_b = x_(top-1) (times cb when cb != 1), coefficient form.
+// two consecutive words per thread, one row per grid row (the top words are re-read per row from L2)
+__device__ __forceinline__ uint64_t red_word(uint64_t y, const PcbPrimeConst& pq) {
+    const uint64_t q = pq.p;
+    return y < q ? y : (y < 2 * q ? y - q : reduce(Acc{y, 0}, pq));
+}
+// lift(y mod qo) mod the prime of pq; qom = qo mod that prime
+__device__ __forceinline__ uint64_t lift_word(uint64_t y, uint64_t qo, uint64_t qom, const PcbPrimeConst& pq) {
+    const uint64_t l = red_word(y, pq);
+    return y > (qo >> 1) ? sub_mod(l, qom, pq.p) : l;
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(BX) rescale_coef(PcbRescaleArgs a) {
     const int c = blockIdx.z >> 1, part = blockIdx.z & 1, row = blockIdx.y;
@@ -211,7 +224,23 @@ __global__ void __launch_bounds__(BX) rescale_coef(PcbRescaleArgs a) {
     const PcbPrimeConst& pa = a.pr[a.top];
     const uint64_t qa = pa.p;
     const ulonglong2 yv = *(const ulonglong2*)(at_row(a.x, c, part, a.top, LOGN) + i);
-    uint64_t ya[2] = {yv.x, yv.y};
+    uint64_t ya[2] = {yv.x, yv.y}, yp[2] = {0, 0}, qb = 0;
+    if (a.ca != 1) {
+        ya[0] = mul_mod(ya[0], a.ca, pa);
+        ya[1] = mul_mod(ya[1], a.ca, pa);
+    }
+    if (a.ndrop == 2) {
+        const PcbPrimeConst& pb = a.pr[a.top - 1];
+        qb = pb.p;
+        const uint64_t qab = red_word(qa, pb);
+        const ulonglong2 bv = *(const ulonglong2*)(at_row(a.x, c, part, a.top - 1, LOGN) + i);
+        const uint64_t yb[2] = {bv.x, bv.y};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint64_t b = a.cb != 1 ? mul_mod(yb[h], a.cb, pb) : yb[h];
+            yp[h] = add_mod(mul_mod(a.qinv_ab, b, pb), mul_mod(a.C_ab, lift_word(ya[h], qa, qab, pb), pb), qb);
+        }
+    }
     const PcbPrimeConst& pq = a.pr[row];
     const uint64_t q = pq.p;
     const uint64_t A = ((const uint64_t*)a.A)[row], As = ((const uint64_t*)a.As)[row];
@@ -219,11 +248,12 @@ __global__ void __launch_bounds__(BX) rescale_coef(PcbRescaleArgs a) {
     uint64_t r[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-        if (a.ca != 1) ya[h] = mul_mod(ya[h], a.ca, pa);
-        const bool neg = ya[h] > (qa >> 1);
-        uint64_t l = ya[h] < q ? ya[h] : (ya[h] < 2 * q ? ya[h] - q : reduce(Acc{ya[h], 0}, pq));
-        if (neg) l = sub_mod(l, qm, q);
-        r[h] = shoup(l, A, As, q);
+        r[h] = shoup(lift_word(ya[h], qa, qm, pq), A, As, q);
+        if (a.ndrop == 2) {
+            const uint64_t B = ((const uint64_t*)a.B)[row], Bs = ((const uint64_t*)a.Bs)[row];
+            const uint64_t qbm = ((const uint64_t*)a.qbm)[row];
+            r[h] = add_mod(r[h], shoup(lift_word(yp[h], qb, qbm, pq), B, Bs, q), q);
+        }
     }
     *(ulonglong2*)(at_row_w(a.tmp, c, part, row, LOGN) + i) = make_ulonglong2(r[0], r[1]);
 }
@@ -232,9 +262,10 @@ template <int LOGN>
 int rescale_coef_launch(const PcbRescaleArgs* ap, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbRescaleArgs& a = *ap;
-    if (a.ndrop != 1) return PCB_BAD_ARGS;  // two-prime (composite) levels are not part of the u64 chains here
-    if (a.top < 1 || a.nrows < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.A || !a.As || !a.qam)
+    if (a.ndrop != 1 && a.ndrop != 2) return PCB_BAD_ARGS;
+    if (a.top < a.ndrop || a.nrows < 0 || a.K < 0 || !a.pr || !a.x.base || !a.tmp.base || !a.A || !a.As || !a.qam)
         return PCB_BAD_ARGS;
+    if (a.ndrop == 2 && (!a.B || !a.Bs || !a.qbm)) return PCB_BAD_ARGS;
     if (!ok16(a.x) || !ok16(a.tmp)) return PCB_BAD_ARGS;
     if (a.nrows == 0 || a.K == 0) return 0;
     rescale_coef<LOGN><<<dim3((1 << LOGN) / (BX * 2), a.nrows, 2 * a.K), BX, 0, s>>>(a);

@@ -104,6 +104,7 @@ struct PcbCtx {
     int logn = 0;
     size_t n = 0;
     int nq = 0, kp = 0, rows = 0, dnum = 0, alpha = 0, k_max = 0, nkeys = 0;
+    int device = -1;  // the device current at pcb_ctx_create: the arena, the tables and the keys live there
     std::vector<uint64_t> primes;
     const PcbKernelTable* tab = nullptr;
     bool narrow = false;  // every prime below 2^52: the 26-bit-split conversion and inner-product kernels
@@ -909,6 +910,10 @@ int pcb_ctx_create(const PcbParams* prm, int32_t nkeys, void* arena, size_t aren
         delete c;
         return fail(PCB_BAD_ARGS, "arena of %zu bytes, %lld needed", arena_bytes, (long long)need);
     }
+    if (cudaGetDevice(&c->device) != cudaSuccess) {
+        delete c;
+        return fail(PCB_BAD_ARGS, "no current CUDA device");
+    }
     c->arena.base = (char*)(((uintptr_t)arena + 255) & ~(uintptr_t)255);
     c->arena.cap = arena_bytes - (size_t)(c->arena.base - (char*)arena);
     c->arena.measure = false;
@@ -1628,14 +1633,19 @@ constexpr size_t STATIC_SCRATCH_WORDS = (size_t)1 << 21;
 static __device__ __align__(256) uint64_t g_static_scratch[STATIC_SCRATCH_WORDS];
 
 // The array's device address per device, looked up once per device with that device current (host code cannot
-// use the symbol itself: on the host it names a stand-in, not device memory).
+// use the symbol itself: on the host it names a stand-in, not device memory). The cached address belongs to the
+// device's primary context as it was at the first call: after a cudaDeviceReset the library must be reloaded.
 constexpr int MAX_DEVICES = 64;
 std::mutex g_scratch_mu;
 uint64_t* g_scratch_ptr[MAX_DEVICES] = {};
 
-int static_scratch(uint64_t** out) {
+int static_scratch(const PcbCtx& c, uint64_t** out) {
     int dev = -1;
     CK(cudaGetDevice(&dev));
+    // the array used is the current device's; the ciphertext and the tables are on the context's device
+    if (dev != c.device)
+        return fail(PCB_BAD_ARGS, "pcb_rescale_static: device %d is current, the context was created on device %d",
+                    dev, c.device);
     if (dev < 0 || dev >= MAX_DEVICES) return fail(PCB_BAD_ARGS, "device %d beyond %d", dev, MAX_DEVICES);
     std::lock_guard<std::mutex> lock(g_scratch_mu);
     if (!g_scratch_ptr[dev]) {
@@ -1666,7 +1676,7 @@ int pcb_rescale_static(PcbCtx* c, uint64_t* ct, int32_t top, cudaStream_t s) {
                     "maximum of %zu (2 (nq + kp) N <= 2^21); use pcb_rescale",
                     c->rows, c->n, need, STATIC_SCRATCH_WORDS);
     uint64_t* scratch = nullptr;
-    rc = static_scratch(&scratch);
+    rc = static_scratch(*c, &scratch);
     if (rc) return rc;
     // the same three launches as pcb_rescale with K = 1; every scratch word read is written first in this call
     const LevelPlan& l = c->lv[top];

@@ -8,7 +8,7 @@ cannot run here. Their constants are parsed out of the test files instead and co
   (p, a[0], a[1], a[n-1], FNV-1a of the row) tuples of digits 0 / 3 / 6 at n = 2^16;
 - crates/pc-core/src/params/nbtheory.rs (tests): prime test / prime search / minimal 2N-th root answers.
 
-Usage: python tests/golden/make_pins.py [reference root]   (default /root/reference)
+Usage: python tests/golden/make_pins.py <reference root>
 """
 import json
 import os
@@ -60,4 +60,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_pins.py <reference root>")
+    main(sys.argv[1])

@@ -1,0 +1,869 @@
+"""The reference's OWN kernel table beside this build's: the same arguments must give the same words.
+
+`oracle/_ref/libpcref_u64.so` is the reference's `pc_table_u64_barrett64` and `oracle/_ref/libpcref_ring14.so` its
+`pc_ring_u64_14`, compiled from the reference's sources for sm_100a by `make -C oracle ref REF=<reference root>`
+(test infrastructure only: the product never loads them). Two kinds of checks:
+
+1. Launchers. Every entry that both tables implement runs on the same inputs and arguments (fresh copies for each
+   table) and must write the same words: the NTT (both directions, every epilogue, out-of-place and summed sources,
+   per-row inverse scales), base conversion, the key inner product (c0 modes, accumulation, automorphism), tensor,
+   ModDown epilogue, rescale (one and two dropped primes), automorphism, the element-wise and plaintext-operand
+   entries, key expansion, key generation and encryption; rows mix 50-bit and 60-bit primes.
+2. Compositions. The reference's launchers run in its device runtime's order — ModUp (INTT with the digit pre factor,
+   bconv of every live digit, NTT of the targets: crates/pc-gpu/src/ks.rs:954-1043), the key inner product
+   (crates/pc-gpu/src/ks.rs:1109), ModDown (INTT of the special rows, bconv P -> Q, NTT with epilogue 1:
+   crates/pc-gpu/src/ks.rs:1620-1656), relinearization (crates/pc-gpu/src/relin.rs:84-134) and rescale (INTT of the
+   top, rescale_coef, NTT, rescale_combine: crates/pc-gpu/src/rescale.rs:230) — on the keys of a config-2 session,
+   and must equal the oracle's rotation, relinearized product and rescale word for word. This pins the oracle's
+   compositions (and through it every evaluator parity test) to the reference's own code.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from perseus_b200 import _lib as L
+from perseus_b200 import fhe
+from tests import _oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_U64 = os.path.join(ROOT, "oracle", "_ref", "libpcref_u64.so")
+REF_R14 = os.path.join(ROOT, "oracle", "_ref", "libpcref_ring14.so")
+
+LOGN = 16
+N = 1 << LOGN
+KS_ACC = 4
+
+
+def host(t):
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.uint64)).view(np.int64)).cuda()
+
+
+def ptr(x):
+    return C.cast(C.pointer(x), C.c_void_p)
+
+
+def shoup(w, p):
+    return (int(w) << 64) // int(p)
+
+
+_REF = {}
+
+
+def ref_table(ring14=False):
+    path = REF_R14 if ring14 else REF_U64
+    if not os.path.exists(path):
+        pytest.skip(f"{os.path.relpath(path, ROOT)} not built (make -C oracle ref REF=<reference root>)")
+    if path not in _REF:
+        lib = C.CDLL(path)
+        if ring14:
+            f = lib.pc_ring_u64_14
+            f.restype = C.POINTER(L.RingTable)
+        else:
+            f = lib.pc_table_u64_barrett64
+            f.restype = C.POINTER(L.KernelTable)
+        _REF[path] = (lib, f().contents)
+    return _REF[path][1]
+
+
+def tables():
+    return [("ours", L.kernel_table()), ("ref", ref_table())]
+
+
+def stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def run_both(entry, make, tabs=None):
+    """make() builds fresh device inputs/outputs and returns (args, outputs, keep-alive); the entry of each table runs
+    on its own set. Returns {table name: [host copies of the outputs]}."""
+    got = {}
+    for name, t in tabs or tables():
+        args, outs, keep = make()
+        rc = getattr(t, entry)(ptr(args), stream())
+        assert rc == 0, f"{name} {entry} returned {rc}"
+        torch.cuda.synchronize()
+        got[name] = [host(o) for o in outs]
+    return got
+
+
+def same(got):
+    a, b = got["ours"], got["ref"]
+    assert len(a) == len(b)
+    for i, (x, y) in enumerate(zip(a, b)):
+        assert x.shape == y.shape and (x == y).all(), f"output {i} differs ({int((x != y).sum())} words)"
+
+
+# ------------------------------------------------------------------------------------------------ environment
+
+
+class Env:
+    """Prime ids 0..11: 8 primes below 2^50 then 4 below 2^60 (both arithmetic widths of the u64 word), with the
+    reference's constant and twiddle tables ([prime id][N], Shoup companions; N^-1 per prime id)."""
+
+    def __init__(self, logn=LOGN):
+        self.logn, self.n = logn, 1 << logn
+        self.primes = O.ntt_primes(50, logn, 8) + O.ntt_primes(60, logn, 4)
+        self.R = len(self.primes)
+        pc = np.zeros((self.R, 8), np.uint64)
+        fw = np.zeros((self.R, self.n), np.uint64)
+        fws, iw, iws = np.zeros_like(fw), np.zeros_like(fw), np.zeros_like(fw)
+        ninv, ninvs = np.zeros(self.R, np.uint64), np.zeros(self.R, np.uint64)
+        for i, p in enumerate(self.primes):
+            O.lib().orc_prime_const(p, pc[i])
+            psi = O.lib().orc_root_of_unity(2 * self.n, p)
+            O.lib().orc_twiddles(p, psi, logn, fw[i], fws[i], iw[i], iws[i])
+            ninv[i] = pow(self.n, -1, p)
+            ninvs[i] = shoup(ninv[i], p)
+        self.pc, self.fw, self.fws, self.iw, self.iws = dev(pc), dev(fw), dev(fws), dev(iw), dev(iws)
+        self.ninv, self.ninvs = dev(ninv), dev(ninvs)
+        self.P = np.array(self.primes, np.uint64)
+
+    def rows(self, rng, pids, lead=()):
+        """random canonical rows [*lead, len(pids), N], row j mod primes[pids[j]]"""
+        out = np.empty(tuple(lead) + (len(pids), self.n), np.uint64)
+        for j, pid in enumerate(pids):
+            out[..., j, :] = rng.integers(0, self.primes[pid], tuple(lead) + (self.n,), dtype=np.uint64)
+        return out
+
+    def cts(self, rng, K):
+        """K ciphertexts [K][2][R][N] (row r mod prime id r)"""
+        return self.rows(rng, range(self.R), lead=(K, 2))
+
+    def ntt_args(self, base, roff, rprime, keep, **kw):
+        a = L.NttArgs()
+        ro = torch.tensor(roff, dtype=torch.int32, device="cuda")
+        rp = torch.tensor(rprime, dtype=torch.int32, device="cuda")
+        keep += [ro, rp]
+        a.base, a.roff, a.rprime = base.data_ptr(), ro.data_ptr(), rp.data_ptr()
+        a.fw, a.fws, a.iw, a.iws = self.fw.data_ptr(), self.fws.data_ptr(), self.iw.data_ptr(), self.iws.data_ptr()
+        a.ninv, a.ninvs, a.pr = self.ninv.data_ptr(), self.ninvs.data_ptr(), self.pc.data_ptr()
+        a.nrows, a.snum, a.xnum = len(roff), 1, 1
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    def cref(self, t):
+        return L.PolyRef(t.data_ptr(), 2 * self.R * self.n, self.R * self.n)
+
+
+@pytest.fixture(scope="module")
+def env():
+    return Env()
+
+
+def test_headers_agree():
+    ours, ref = L.kernel_table(), ref_table()
+    assert (ours.abi, ours.word_bytes, ours.mm, ours.log_n) == (ref.abi, ref.word_bytes, ref.mm, ref.log_n)
+    r14o, r14r = L.ring_table(14), ref_table(ring14=True)
+    assert (r14o.abi, r14o.word_bytes, r14o.mm, r14o.log_n) == (r14r.abi, r14r.word_bytes, r14r.mm, r14r.log_n)
+
+
+# ------------------------------------------------------------------------------------------------ NTT
+
+
+@pytest.mark.parametrize("chunk", [0, 5])
+def test_ntt_plain_both_directions(env, chunk):
+    rng = np.random.default_rng(1)
+    pids = [0, 3, 7, 8, 11, 2, 9, 1, 10, 4, 5]
+    x = env.rows(rng, pids)
+    x[0, :8] = env.primes[0] - 1  # extreme words
+    x[4, 8:16] = 0
+
+    def make(inverse):
+        def mk():
+            keep = []
+            xd = dev(x)
+            a = env.ntt_args(xd, list(range(len(pids))), pids, keep, chunk=chunk)
+            return a, [xd], keep
+        return mk
+
+    fwd = run_both("ntt_fwd", make(False))
+    same(fwd)
+    want = x.copy()
+    O.lib().orc_ntt_fwd(want, len(pids), env.P[pids], LOGN)
+    assert (fwd["ours"][0] == want).all()
+    inv = run_both("ntt_inv", make(True))
+    same(inv)
+    want = x.copy()
+    O.lib().orc_ntt_inv(want, len(pids), env.P[pids], LOGN)
+    assert (inv["ref"][0] == want).all()
+
+
+@pytest.mark.parametrize("epi,with_ed", [(1, False), (2, False), (2, True), (3, False)])
+def test_ntt_epilogues_sources(env, epi, with_ed):
+    """Out-of-place first pass summing snum = 2 source rows, the epilogue's x summed over xnum = 2 rows."""
+    rng = np.random.default_rng(10 + epi)
+    pids = [1, 6, 9, 11]
+    nr = len(pids)
+    src = env.rows(rng, pids, lead=(2,))          # [2][nr][N]: source j of row i at soff[i] + j sstride
+    ex = env.rows(rng, pids, lead=(2,))           # x = ex[0] + ex[1]
+    eo0 = env.rows(rng, pids)
+    ed = env.rows(rng, pids)
+    es = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    ess = np.array([shoup(v, p) for v, p in zip(es, env.primes)], np.uint64)
+
+    def mk():
+        keep = []
+        base = torch.zeros((nr, N), dtype=torch.int64, device="cuda")
+        s, x, eo, e, sc, scs = dev(src), dev(ex), dev(eo0), dev(ed), dev(es), dev(ess)
+        soff = torch.arange(nr, dtype=torch.int32, device="cuda")
+        keep += [s, x, e, sc, scs, soff]
+        a = env.ntt_args(base, list(range(nr)), pids, keep, src=s.data_ptr(), soff=soff.data_ptr(), snum=2,
+                         sstride=nr * N, epi=epi, eout=eo.data_ptr(), ex=x.data_ptr(), xnum=2, xstride=nr * N,
+                         es=sc.data_ptr(), ess=scs.data_ptr(), ed=e.data_ptr() if with_ed else None)
+        # the result is eout; base only holds the first pass's intermediate (the ABI's out-of-place form with an
+        # epilogue writes no transform to base), which is not an output
+        return a, [eo], keep
+
+    same(run_both("ntt_fwd", mk))
+
+
+def test_ntt_inverse_row_scales(env):
+    rng = np.random.default_rng(3)
+    pids = [0, 8, 5, 10, 7]
+    x = env.rows(rng, pids)
+    es = np.array([rng.integers(1, env.primes[p]) for p in pids], np.uint64)  # per ROW (not per prime id)
+    ess = np.array([shoup(v, env.primes[p]) for v, p in zip(es, pids)], np.uint64)
+
+    def mk():
+        keep = []
+        xd, sc, scs = dev(x), dev(es), dev(ess)
+        keep += [sc, scs]
+        return env.ntt_args(xd, list(range(len(pids))), pids, keep, es=sc.data_ptr(), ess=scs.data_ptr()), [xd], keep
+
+    same(run_both("ntt_inv", mk))
+
+
+def test_ring14_tables():
+    """The 2^14 ring tables: NTT both directions, bconv and the element-wise entries."""
+    e14 = Env(14)
+    tabs = [("ours", L.ring_table(14)), ("ref", ref_table(ring14=True))]
+    rng = np.random.default_rng(4)
+    pids = list(range(e14.R))
+    x = e14.rows(rng, pids)
+
+    def mk():
+        keep = []
+        xd = dev(x)
+        return e14.ntt_args(xd, pids, pids, keep), [xd], keep
+
+    for entry in ("ntt_fwd", "ntt_inv"):
+        got = run_both(entry, mk, tabs)
+        same(got)
+        want = x.copy()
+        (O.lib().orc_ntt_fwd if entry == "ntt_fwd" else O.lib().orc_ntt_inv)(want, e14.R, e14.P, 14)
+        assert (got["ours"][0] == want).all()
+    _bconv_case(e14, tabs, seed=5)
+    _ew_cases(e14, tabs, seed=6)
+
+
+# ------------------------------------------------------------------------------------------------ bconv
+
+
+def _bconv_pool(primes, srcp, tgtp, src_rows, tgt_rows, rng):
+    B = 1
+    for i in srcp:
+        B *= primes[i]
+    pre = [pow(B // primes[i] % primes[i], -1, primes[i]) for i in srcp]
+    M = [[(B // primes[i]) % primes[t] for t in tgtp] for i in srcp]
+    return list(src_rows) + list(srcp) + pre + list(tgt_rows) + list(tgtp) + [v for row in M for v in row]
+
+
+def _bconv_case(e, tabs, seed):
+    """Four jobs over one source buffer: 1, 3, 8 and 12 sources, prescaled and not, row offsets on both sides."""
+    rng = np.random.default_rng(seed)
+    n = e.n
+    nsrc_rows = 2 * e.R
+    x = np.zeros((nsrc_rows, n), np.uint64)  # row r (and r + R) holds residues mod prime id r
+    for r in range(nsrc_rows):
+        x[r] = rng.integers(0, e.primes[r % e.R], n, dtype=np.uint64)
+    specs = [  # (src prime ids, tgt prime ids, src_off, dst_off, prescaled)
+        ([4], [0, 11, 7], 0, 0, 0),
+        ([0, 1, 2], [3, 8, 9, 10, 11, 5], e.R, e.R, 1),
+        ([0, 1, 2, 3, 4, 5, 6, 7], [8, 9, 10, 11], 0, 2 * e.R, 0),
+        (list(range(4, 12)) + [0, 1, 2], [3], 0, 3 * e.R, 1),  # 11 sources, 50- and 60-bit
+    ]
+    pool, jobs = [], []
+    for srcp, tgtp, soff, doff, pres in specs:
+        off = len(pool)
+        pool += _bconv_pool(e.primes, srcp, tgtp, srcp, tgtp, rng)
+        jobs.append(L.BconvJob(soff, doff, len(srcp), len(tgtp), off, 0, pres, 0))
+    jarr = (L.BconvJob * len(jobs))(*jobs)
+    jbytes = np.frombuffer(bytes(jarr), np.uint8).copy()
+    max_tgt = max(len(s[1]) for s in specs)
+
+    def mk():
+        keep = []
+        xd, pd = dev(x), dev(np.array(pool, np.uint64))
+        jd = torch.from_numpy(jbytes.copy()).cuda()
+        out = torch.zeros((4 * e.R, n), dtype=torch.int64, device="cuda")
+        keep += [xd, pd, jd]
+        a = L.BconvArgs()
+        a.src, a.dst, a.jobs, a.pool, a.pr = xd.data_ptr(), out.data_ptr(), jd.data_ptr(), pd.data_ptr(), e.pc.data_ptr()
+        a.njobs, a.max_tgt = len(jobs), max_tgt
+        return a, [out], keep
+
+    got = run_both("bconv", mk, tabs)
+    same(got)
+    # and the exact fast-conversion sum for job 2 (8 sources -> the 60-bit targets)
+    srcp, tgtp, soff, doff, pres = specs[2]
+    B = 1
+    for i in srcp:
+        B *= e.primes[i]
+    xs = x.astype(object)
+    for k, t in enumerate(tgtp):
+        y = [xs[soff + i] * pow(B // e.primes[i] % e.primes[i], -1, e.primes[i]) % e.primes[i] for i in srcp]
+        want = sum(yv * ((B // e.primes[i]) % e.primes[t]) for yv, i in zip(y, srcp)) % e.primes[t]
+        assert (got["ref"][0][doff + t].astype(object) == want).all()
+
+
+def test_bconv(env):
+    _bconv_case(env, tables(), seed=20)
+
+
+# ------------------------------------------------------------------------------------------------ key inner product
+
+
+@pytest.mark.parametrize("K,R,c0_mode,autok", [(1, 1, 0, 1), (3, 2, 1, 0), (2, 2, 2, 0), (4, 1, 1 | KS_ACC, 0),
+                                              (8, 1, 0, 0)])
+def test_ks_dot(env, K, R, c0_mode, autok):
+    rng = np.random.default_rng(30 + K + 7 * R + c0_mode)
+    nq, ndig = 8, 3
+    digit_of = np.array([t // 3 for t in range(nq)] + [-1] * (env.R - nq), np.int32)
+    rows = np.array(list(range(7)) + [8, 9, 10, 11], np.uint32)  # Q rows 0..6 (a partial top digit), 4 special rows
+    ks = [(int(2 * rng.integers(1, N) + 1) if autok == 0 else 1) for _ in range(R)]
+    c1 = env.cts(rng, K)[:, 1]                     # [K][R][N]
+    c0 = env.cts(rng, K)[:, 0]
+    mu = env.rows(rng, range(env.R), lead=(K, ndig))   # [K][ndig][R][N]
+    kb = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(R)]
+    ka = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(R)]
+    o0 = env.rows(rng, range(env.R), lead=(K, R))      # [K][R keys][rows][N] (accumulated onto in KS_ACC)
+    o1 = env.rows(rng, range(env.R), lead=(K, R))
+    pm = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    pms = np.array([shoup(v, p) for v, p in zip(pm, env.primes)], np.uint64)
+
+    def mk():
+        keep = [dev(c1), dev(c0), dev(mu), dev(pm), dev(pms)]
+        c1d, c0d, mud, pmd, pmsd = keep[:5]
+        kbd, kad = [dev(v) for v in kb], [dev(v) for v in ka]
+        keep += kbd + kad
+        kbt = dev(np.array([t.data_ptr() for t in kbd], np.uint64))
+        kat = dev(np.array([t.data_ptr() for t in kad], np.uint64))
+        autd = torch.tensor(ks, dtype=torch.int32, device="cuda")
+        rowd = torch.tensor(rows.astype(np.int32), dtype=torch.int32, device="cuda")
+        digd = torch.tensor(digit_of, dtype=torch.int32, device="cuda")
+        out0, out1 = dev(o0), dev(o1)
+        keep += [kbt, kat, autd, rowd, digd]
+        a = L.KsArgs()
+        a.c1, a.modup, a.c0, a.out0, a.out1 = c1d.data_ptr(), mud.data_ptr(), c0d.data_ptr(), out0.data_ptr(), \
+            out1.data_ptr()
+        a.kb, a.ka, a.autok, a.rows, a.digit_of = kbt.data_ptr(), kat.data_ptr(), autd.data_ptr(), rowd.data_ptr(), \
+            digd.data_ptr()
+        a.pmod, a.pmods, a.pr = pmd.data_ptr(), pmsd.data_ptr(), env.pc.data_ptr()
+        a.ct_stride, a.mu_ct_stride, a.mu_digit_stride = env.R * N, ndig * env.R * N, env.R * N
+        a.out_ct_stride, a.out_rot_stride, a.key_digit_stride = R * env.R * N, env.R * N, env.R * N
+        a.K, a.R, a.ndig, a.c0_mode, a.nq, a.nrows = K, R, ndig, c0_mode, nq, len(rows)
+        return a, [out0, out1], keep
+
+    same(run_both("ks_dot", mk))
+
+
+# ------------------------------------------------------------------------------------------------ element-wise
+
+
+def _ew_cases(e, tabs, seed):
+    rng = np.random.default_rng(seed)
+    K = 2
+    a, b = e.cts(rng, K), e.cts(rng, K)
+    sc = np.array([rng.integers(1, p) for p in e.primes], np.uint64)
+    scs = np.array([shoup(v, p) for v, p in zip(sc, e.primes)], np.uint64)
+    rs = L.RowSet(5, 3, e.R - 4, 0)  # Q rows 0..4, special rows R-4 .. R-2
+
+    for entry, sub, zero_p, nparts in [("ew_add", 0, 0, 2), ("ew_add", 1, 0, 1), ("ew_scale", 0, 1, 2),
+                                       ("ew_scale", 0, 0, 2), ("ew_sub_mul", 0, 0, 2), ("ew_copy", 0, 0, 2)]:
+        def mk():
+            keep = [dev(a), dev(b), dev(sc), dev(scs)]
+            ad, bd, scd, scsd = keep
+            out = dev(np.full_like(a, 7))
+            x = L.EwArgs(e.cref(out), e.cref(ad), e.cref(bd), rs, scd.data_ptr(), scsd.data_ptr(), e.pc.data_ptr(),
+                         K, nparts, sub, zero_p)
+            return x, [out], keep
+
+        got = run_both(entry, mk, tabs)
+        same(got)
+
+
+def test_elementwise(env):
+    _ew_cases(env, tables(), seed=40)
+
+
+@pytest.mark.parametrize("npairs,acc,dbl,acc_d2,coef", [(1, 0, 0, 0, 0), (2, 1, 1, 1, 1)])
+def test_tensor(env, npairs, acc, dbl, acc_d2, coef):
+    rng = np.random.default_rng(50 + npairs)
+    K, n = 3, 10
+    ins = [env.cts(rng, K) for _ in range(4)]
+    o, d2, cf = env.cts(rng, K), env.cts(rng, K), env.rows(rng, range(env.R), lead=(K,))
+
+    def mk():
+        keep = [dev(v) for v in ins]
+        out, d2d, cfd = dev(o), dev(d2), dev(cf)
+        x = L.TensorArgs(env.cref(out), env.cref(d2d), env.cref(keep[0]), env.cref(keep[1]), env.cref(keep[2]),
+                         env.cref(keep[3]), cfd.data_ptr() if coef else None, env.R * N, env.pc.data_ptr(), npairs, acc,
+                         n, K, dbl, acc_d2)
+        return x, [out, d2d, cfd], keep
+
+    same(run_both("tensor", mk))
+
+
+@pytest.mark.parametrize("dbl,with_k", [(0, False), (1, True)])
+def test_md_epilogue(env, dbl, with_k):
+    rng = np.random.default_rng(60 + dbl)
+    K, n = 2, 9
+    dst, x, t = env.cts(rng, K), env.cts(rng, K), env.cts(rng, K)
+    bi = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    bis = np.array([shoup(v, p) for v, p in zip(bi, env.primes)], np.uint64)
+    k = np.array([rng.integers(0, p + 1) for p in env.primes], np.uint64)  # k == p allowed
+
+    def mk():
+        keep = [dev(x), dev(t), dev(bi), dev(bis), dev(k)]
+        dd = dev(dst)
+        a = L.MdEpiArgs(env.cref(dd), env.cref(keep[0]), env.cref(keep[1]), keep[2].data_ptr(), keep[3].data_ptr(),
+                        keep[4].data_ptr() if with_k else None, env.pc.data_ptr(), dbl, n, K, 0)
+        return a, [dd], keep
+
+    same(run_both("md_epilogue", mk))
+
+
+@pytest.mark.parametrize("has_add", [0, 1])
+def test_automorph(env, has_add):
+    rng = np.random.default_rng(70 + has_add)
+    K = 2
+    x, ad = env.cts(rng, K), env.cts(rng, K)
+    k = int(fhe.rotation_galois(37, LOGN))
+
+    def mk():
+        keep = [dev(x), dev(ad)]
+        out = dev(np.zeros_like(x))
+        a = L.AutomorphArgs(env.cref(out), env.cref(keep[0]), env.cref(keep[1]), L.RowSet(6, 2, 9, 0), env.pc.data_ptr(),
+                            k, K, 2, has_add)
+        return a, [out], keep
+
+    same(run_both("automorph", mk))
+
+
+@pytest.mark.parametrize("ndrop", [1, 2])
+def test_rescale_launchers(env, ndrop):
+    """rescale_coef (one and two dropped primes, constant pre-factors ca/cb) and rescale_combine."""
+    rng = np.random.default_rng(80 + ndrop)
+    K, top = 2, 7
+    x = env.cts(rng, K)
+    q = env.primes
+    a_, b_ = top, top - 1
+    nrows = top + 1 - ndrop
+
+    def qlql(xp, i):
+        return (-pow(q[xp], -1, q[i])) % q[i]
+
+    A = [((pow(q[b_], -1, q[i]) * qlql(a_, i)) % q[i] if ndrop == 2 else qlql(a_, i)) for i in range(env.R)
+         if i < nrows] + [0] * (env.R - nrows)
+    B = [qlql(b_, i) if (ndrop == 2 and i < nrows) else 0 for i in range(env.R)]
+    al = [((pow(q[a_], -1, q[i]) * (pow(q[b_], -1, q[i]) if ndrop == 2 else 1)) % q[i]) if i < nrows else 1
+          for i in range(env.R)]
+    As, Bs, als = ([shoup(v, q[i]) for i, v in enumerate(arr)] for arr in (A, B, al))
+    qam = [q[a_] % q[i] for i in range(env.R)]
+    qbm = [q[b_] % q[i] for i in range(env.R)]
+    qinv_ab = pow(q[a_], -1, q[b_])
+    C_ab = qlql(a_, b_)
+    ca, cb = int(rng.integers(2, q[a_])), int(rng.integers(2, q[b_]))
+    tmp0 = env.cts(rng, K)
+
+    def mk_coef():
+        keep = [dev(x)] + [dev(v) for v in (A, B, As, Bs, qam, qbm)]
+        tmp = dev(tmp0)
+        r = L.RescaleArgs(env.cref(keep[0]), env.cref(tmp), *[v.data_ptr() for v in keep[1:]], env.pc.data_ptr(),
+                          qinv_ab, C_ab, ca, cb, top, nrows, K, ndrop)
+        return r, [tmp], keep
+
+    got = run_both("rescale_coef", mk_coef)
+    same(got)
+    tmp_h = got["ref"][0]
+
+    def mk_comb():
+        keep = [dev(tmp_h), dev(al), dev(als)]
+        xd = dev(x)
+        r = L.RescaleCombineArgs(env.cref(xd), env.cref(keep[0]), keep[1].data_ptr(), keep[2].data_ptr(),
+                                 env.pc.data_ptr(), nrows, K)
+        return r, [xd], keep
+
+    same(run_both("rescale_combine", mk_comb))
+
+
+# ------------------------------------------------------------------------------------------------ plaintext operands
+
+
+def test_plaintext_operand_entries(env):
+    rng = np.random.default_rng(90)
+    K, n = 3, 11
+    x, y = env.cts(rng, K), env.cts(rng, K)
+    xs = [env.cts(rng, K) for _ in range(8)]
+    ts = [env.rows(rng, range(env.R)) for _ in range(8)]
+    kc = np.array([rng.integers(0, p + 1) for p in env.primes], np.uint64)
+
+    def mk_const():
+        kd = dev(kc)
+        xd = dev(x)
+        return L.AddConstArgs(env.cref(xd), kd.data_ptr(), env.pc.data_ptr(), n, K), [xd], [kd]
+
+    same(run_both("add_const", mk_const))
+
+    def mk_table():
+        xd, td = dev(x), dev(ts[0])
+        out = dev(y)
+        return L.MulTableArgs(env.cref(out), env.cref(xd), td.data_ptr(), env.pc.data_ptr(), n, K), [out], [xd, td]
+
+    same(run_both("mul_table", mk_table))
+    for sub in (0, 1, 2):
+        def mk_add():
+            xd, td, yd = dev(x), dev(ts[1]), dev(y)
+            m = L.MulTableArgs(env.cref(yd), env.cref(xd), td.data_ptr(), env.pc.data_ptr(), n, K)
+            return L.MulAddArgs(m, env.cref(yd), sub, 0), [yd], [xd, td]
+
+        same(run_both("mul_add", mk_add))
+    for nterm, lazy, with_y in [(1, 0, True), (5, 1, False), (8, 0, True), (8, 1, True)]:
+        def mk_n():
+            keep = [dev(v) for v in xs[:nterm]] + [dev(v) for v in ts[:nterm]]
+            yd = dev(y)
+            out = dev(np.zeros_like(y))
+            a = L.MulAddNArgs()
+            a.out, a.y = env.cref(out), (env.cref(yd) if with_y else L.PolyRef())
+            for j in range(nterm):
+                a.x[j], a.t[j] = env.cref(keep[j]), keep[nterm + j].data_ptr()
+            a.pr, a.n, a.K, a.nterm, a.lazy = env.pc.data_ptr(), n, K, nterm, lazy
+            return a, [out], keep + [yd]
+
+        same(run_both("mul_add_n", mk_n))
+
+
+@pytest.mark.parametrize("K,enc,ptw", [(3, 0xFFFFFFFF, N), (5, 0x7F000001, N // 2), (1, N // 4 - 1, N // 4)])
+def test_pt_dot(env, K, enc, ptw):
+    rng = np.random.default_rng(100 + K)
+    bstep, gstep, npts = 3, 2, 5
+    nq, np_, qmax, pt_prow = 5, 2, 9, 5
+    rot = env.cts(rng, K * bstep)
+    pts = [rng.integers(0, 1 << 49, (pt_prow + np_, ptw), dtype=np.uint64) for _ in range(npts)]
+
+    def mk():
+        rd = dev(rot)
+        pd = [dev(v) for v in pts]
+        tab = dev(np.array([t.data_ptr() for t in pd], np.uint64))
+        res = torch.zeros((K * gstep, 2, env.R, N), dtype=torch.int64, device="cuda")
+        a = L.PtDotArgs()
+        a.rot = L.PolyRef(rd.data_ptr(), bstep * 2 * env.R * N, env.R * N)
+        a.res = L.PolyRef(res.data_ptr(), gstep * 2 * env.R * N, env.R * N)
+        a.rot_stride, a.res_stride = 2 * env.R * N, 2 * env.R * N
+        a.pts, a.pr, a.rs = tab.data_ptr(), env.pc.data_ptr(), L.RowSet(nq, np_, qmax, 0)
+        a.npts, a.bstep, a.gstep, a.K, a.ptw, a.pt_prow, a.enc = npts, bstep, gstep, K, ptw, pt_prow, enc
+        return a, [res], [rd, tab] + pd
+
+    same(run_both("pt_dot", mk))
+
+
+# ------------------------------------------------------------------------------------------------ keys, encryption
+
+
+def test_key_entries(env):
+    rng = np.random.default_rng(110)
+    seed = rng.integers(0, 1 << 32, 8, dtype=np.uint64).astype(np.uint32)
+    ids = np.array([0, 2, 5, 8, 11], np.int32)
+    dnum = 3
+
+    def mk_expand():
+        sd = torch.from_numpy(seed.view(np.int32).copy()).cuda()
+        idd = torch.tensor(ids, dtype=torch.int32, device="cuda")
+        out = torch.zeros((dnum - 1, len(ids), N), dtype=torch.int64, device="cuda")
+        return L.KskExpandArgs(out.data_ptr(), sd.data_ptr(), idd.data_ptr(), env.pc.data_ptr(), len(ids), dnum, 1,
+                               0), [out], [sd, idd]
+
+    same(run_both("ksk_expand", mk_expand))
+
+    nq, ndig = 8, 3
+    rows_ids = np.array(list(range(nq)) + [8, 9, 10, 11], np.int32)
+    digit_of = np.array([t // 3 for t in range(nq)] + [-1] * 4, np.int32)
+    e = env.rows(rng, rows_ids, lead=(ndig,))
+    s_new = env.rows(rng, range(env.R))
+    s_old = env.rows(rng, range(env.R))
+    pm = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    pms = np.array([shoup(v, p) for v, p in zip(pm, env.primes)], np.uint64)
+    for sq in (0, 1):
+        def mk_gen():
+            keep = [dev(e), dev(s_new), dev(s_old), dev(pm), dev(pms)]
+            sd = torch.from_numpy(seed.view(np.int32).copy()).cuda()
+            idd = torch.tensor(rows_ids, dtype=torch.int32, device="cuda")
+            dg = torch.tensor(digit_of, dtype=torch.int32, device="cuda")
+            b = torch.zeros((ndig, len(rows_ids), N), dtype=torch.int64, device="cuda")
+            a = torch.zeros_like(b)
+            g = L.KskGenArgs(b.data_ptr(), a.data_ptr(), *[k.data_ptr() for k in keep[:3]], sd.data_ptr(),
+                             idd.data_ptr(), dg.data_ptr(), keep[3].data_ptr(), keep[4].data_ptr(), env.pc.data_ptr(),
+                             N, len(rows_ids), ndig, nq, 0, sq, 0)
+            return g, [b, a], keep + [sd, idd, dg]
+
+        same(run_both("ksk_gen", mk_gen))
+
+    s = env.rows(rng, range(env.R))
+    err = env.rows(rng, range(env.R))
+    m = env.rows(rng, range(env.R))
+    for with_m, with_c1 in [(True, True), (False, False)]:
+        def mk_enc():
+            keep = [dev(s), dev(err), dev(m)]
+            sd = torch.from_numpy(seed.view(np.int32).copy()).cuda()
+            c0 = torch.zeros((env.R, N), dtype=torch.int64, device="cuda")
+            c1 = torch.zeros_like(c0)
+            a = L.EncryptArgs(c0.data_ptr(), c1.data_ptr() if with_c1 else None, keep[0].data_ptr(), keep[1].data_ptr(),
+                              keep[2].data_ptr() if with_m else None, sd.data_ptr(), env.pc.data_ptr(), 77, env.R)
+            return a, [c0, c1], keep + [sd]
+
+        same(run_both("encrypt", mk_enc))
+
+
+# ------------------------------------------------------------------------------------------------ compositions
+
+
+class RefRuntime:
+    """The reference's device runtime order (crates/pc-gpu) driven through the reference's own launchers, on the
+    tables and keys of a perseus-b200 session (the same prime-id layout)."""
+
+    def __init__(self, s, t):
+        self.s, self.t = s, t
+        self.n, self.rows, self.nq, self.kp = s.n, s.rows, s.nq, s.kp
+        self.primes = list(s.chain.q) + list(s.chain.p)
+        self.alpha = -(-self.nq // s.chain.dnum)
+        self.pr, self.fw, self.fws, self.iw, self.iws, self.ninv, self.ninvs = s.tables()
+        self.keep = []
+
+    def call(self, entry, args):
+        rc = getattr(self.t, entry)(ptr(args), stream())
+        assert rc == 0, f"reference {entry} returned {rc}"
+
+    def ntt(self, inverse, base, roff, rprime, **kw):
+        a = L.NttArgs()
+        ro = torch.tensor(roff, dtype=torch.int32, device="cuda")
+        rp = torch.tensor(rprime, dtype=torch.int32, device="cuda")
+        self.keep += [ro, rp]
+        a.base, a.roff, a.rprime = base.data_ptr(), ro.data_ptr(), rp.data_ptr()
+        a.fw, a.fws, a.iw, a.iws, a.ninv, a.ninvs, a.pr = self.fw, self.fws, self.iw, self.iws, self.ninv, \
+            self.ninvs, self.pr
+        a.nrows, a.snum, a.xnum = len(roff), 1, 1
+        for k, v in kw.items():
+            setattr(a, k, v)
+        self.call("ntt_inv" if inverse else "ntt_fwd", a)
+
+    def bconv(self, src, dst, jobs_spec):
+        """jobs_spec: [(src row list, src prime ids, tgt row list, tgt prime ids, src_off, dst_off, pre or None)]"""
+        pool, jobs = [], []
+        for srows, sp, trows, tp, soff, doff, prescaled in jobs_spec:
+            B = 1
+            for i in sp:
+                B *= self.primes[i]
+            pre = [pow(B // self.primes[i] % self.primes[i], -1, self.primes[i]) for i in sp]
+            M = [(B // self.primes[i]) % self.primes[t] for i in sp for t in tp]
+            off = len(pool)
+            pool += list(srows) + list(sp) + pre + list(trows) + list(tp) + M
+            jobs.append(L.BconvJob(soff, doff, len(sp), len(tp), off, 0, prescaled, 0))
+        jarr = (L.BconvJob * len(jobs))(*jobs)
+        jd = torch.from_numpy(np.frombuffer(bytes(jarr), np.uint8).copy()).cuda()
+        pd = dev(np.array(pool, np.uint64))
+        self.keep += [jd, pd]
+        a = L.BconvArgs()
+        a.src, a.dst, a.jobs, a.pool, a.pr = src.data_ptr(), dst.data_ptr(), jd.data_ptr(), pd.data_ptr(), self.pr
+        a.njobs, a.max_tgt = len(jobs), max(len(j[3]) for j in jobs_spec)
+        self.call("bconv", a)
+
+    def digit_range(self, d, top):
+        return d * self.alpha, min((d + 1) * self.alpha, self.nq, top + 1)
+
+    def keyswitch_ext(self, d, c0, c0_mode, kidx, autok, top):
+        """ModUp(d) then the inner product against key kidx: ext [2][rows][N] (Q rows 0..=top, special rows)."""
+        n, rows, nq, kp = self.n, self.rows, self.nq, self.kp
+        ndig = top // self.alpha + 1
+        # 1. INTT of rows 0..=top, the digit pre factor folded into the last pass (ks.rs:954-980)
+        coef = d[: top + 1].clone()
+        es, ess = [], []
+        for t in range(top + 1):
+            lo, hi = self.digit_range(t // self.alpha, top)
+            h = 1
+            for k in range(lo, hi):
+                if k != t:
+                    h = h * self.primes[k] % self.primes[t]
+            v = pow(self.n, -1, self.primes[t]) * pow(h, -1, self.primes[t]) % self.primes[t]
+            es.append(v)
+            ess.append(shoup(v, self.primes[t]))
+        esd, essd = dev(es), dev(ess)
+        self.keep += [esd, essd]
+        self.ntt(True, coef, list(range(top + 1)), list(range(top + 1)), es=esd.data_ptr(), ess=essd.data_ptr())
+        # 2. bconv of every live digit to its targets (prescaled sources), 3. NTT of the targets (ks.rs:1037-1043)
+        D = torch.zeros((ndig, rows, n), dtype=torch.int64, device="cuda")
+        spec, roff, rprime = [], [], []
+        for dg in range(ndig):
+            lo, hi = self.digit_range(dg, top)
+            tg = [t for t in range(top + 1) if t < lo or t >= hi] + [nq + j for j in range(kp)]
+            spec.append((list(range(lo, hi)), list(range(lo, hi)), tg, tg, 0, dg * rows, 1))
+            roff += [dg * rows + t for t in tg]
+            rprime += tg
+        self.bconv(coef, D, spec)
+        self.ntt(False, D, roff, rprime)
+        # 4. the inner product (ks.rs:1109)
+        b, a = self.s.key_tensors(kidx)
+        ext = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        kb = dev(np.array([b.data_ptr()], np.uint64))
+        ka = dev(np.array([a.data_ptr()], np.uint64))
+        krows = list(range(top + 1)) + [nq + j for j in range(kp)]
+        digit_of = [t // self.alpha for t in range(nq)] + [-1] * kp
+        pmod = [1] * rows
+        P = 1
+        for j in range(kp):
+            P *= self.primes[nq + j]
+        pmod = [P % self.primes[t] for t in range(rows)]
+        pms = [shoup(v, self.primes[t]) for t, v in enumerate(pmod)]
+        aut = torch.tensor([autok], dtype=torch.int64, device="cuda").to(torch.int32)
+        rd = torch.tensor(krows, dtype=torch.int32, device="cuda")
+        dd = torch.tensor(digit_of, dtype=torch.int32, device="cuda")
+        pmd, pmsd = dev(pmod), dev(pms)
+        self.keep += [b, a, kb, ka, aut, rd, dd, pmd, pmsd]
+        k = L.KsArgs()
+        k.c1, k.modup, k.c0 = d.data_ptr(), D.data_ptr(), (c0.data_ptr() if c0 is not None else None)
+        k.out0, k.out1 = ext[0].data_ptr(), ext[1].data_ptr()
+        k.kb, k.ka, k.autok, k.rows, k.digit_of = kb.data_ptr(), ka.data_ptr(), aut.data_ptr(), rd.data_ptr(), \
+            dd.data_ptr()
+        k.pmod, k.pmods, k.pr = pmd.data_ptr(), pmsd.data_ptr(), self.pr
+        k.ct_stride, k.mu_ct_stride, k.mu_digit_stride = rows * n, ndig * rows * n, rows * n
+        k.out_ct_stride, k.out_rot_stride, k.key_digit_stride = 2 * rows * n, 0, rows * n
+        k.K, k.R, k.ndig, k.c0_mode, k.nq, k.nrows = 1, 1, ndig, c0_mode, nq, len(krows)
+        self.call("ks_dot", k)
+        return ext
+
+    def moddown(self, ext, top):
+        """INTT of the special rows (N^-1 times the conversion's pre factor), bconv P -> Q rows 0..=top, NTT whose
+        epilogue writes (x - conv) P^-1 (ks.rs:1620-1656)."""
+        n, rows, nq, kp = self.n, self.rows, self.nq, self.kp
+        y = ext.clone()
+        sp = [nq + j for j in range(kp)]
+        P = 1
+        for t in sp:
+            P *= self.primes[t]
+        es = [pow(n, -1, self.primes[t]) * pow(P // self.primes[t] % self.primes[t], -1, self.primes[t])
+              % self.primes[t] for t in sp] * 2
+        ess = [shoup(v, self.primes[sp[i % kp]]) for i, v in enumerate(es)]
+        esd, essd = dev(es), dev(ess)
+        self.keep += [esd, essd]
+        self.ntt(True, y, [part * rows + t for part in (0, 1) for t in sp], sp * 2, es=esd.data_ptr(),
+                 ess=essd.data_ptr())
+        conv = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        tq = list(range(top + 1))
+        self.bconv(y, conv, [(sp, sp, tq, tq, part * rows, part * rows, 1) for part in (0, 1)])
+        pinv = [pow(P, -1, self.primes[t]) if t < nq else 0 for t in range(rows)]
+        pinvs = [shoup(v, self.primes[t]) for t, v in enumerate(pinv)]
+        pd, psd = dev(pinv), dev(pinvs)
+        out = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        self.keep += [pd, psd]
+        self.ntt(False, conv, [part * rows + t for part in (0, 1) for t in tq], tq * 2, epi=1, eout=out.data_ptr(),
+                 ex=ext.data_ptr(), es=pd.data_ptr(), ess=psd.data_ptr())
+        return out
+
+    def rotate(self, x, step, top):
+        g = fhe.rotation_galois(step, self.s.log_n)
+        ginv = pow(g, -1, 2 * self.n)
+        ext = self.keyswitch_ext(x[1], x[0], 1, self.s.galois.index(g), ginv, top)
+        return self.moddown(ext, top)
+
+    def mult(self, a, b, top):
+        rows, n = self.rows, self.n
+        c01 = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        d2 = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        pref = lambda t: L.PolyRef(t.data_ptr(), 2 * rows * n, rows * n)  # noqa: E731
+        ta = L.TensorArgs(pref(c01), pref(d2), pref(a), pref(b), pref(a), pref(b), None, 0, self.pr, 1, 0, top + 1,
+                          1, 0, 0)
+        self.call("tensor", ta)
+        md = self.moddown(self.keyswitch_ext(d2[1], None, 0, 0, 1, top), top)
+        out = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        ew = L.EwArgs(pref(out), pref(c01), pref(md), L.RowSet(top + 1, 0, self.nq, 0), None, None, self.pr, 1, 2, 0, 0)
+        self.call("ew_add", ew)
+        return out
+
+    def rescale(self, x, top):
+        rows, n, q = self.rows, self.n, self.primes
+        y = x.clone()
+        self.ntt(True, y, [top, rows + top], [top, top])  # the top row of both parts to coefficient form
+        tmp = torch.zeros((2, rows, n), dtype=torch.int64, device="cuda")
+        A = [(-pow(q[top], -1, q[i])) % q[i] if i < top else 0 for i in range(rows)]
+        As = [shoup(v, q[i]) for i, v in enumerate(A)]
+        qam = [q[top] % q[i] for i in range(rows)]
+        al = [pow(q[top], -1, q[i]) if i < top else 1 for i in range(rows)]
+        als = [shoup(v, q[i]) for i, v in enumerate(al)]
+        Ad, Asd, qd, ald, alsd, zd = dev(A), dev(As), dev(qam), dev(al), dev(als), dev([0] * rows)
+        self.keep += [Ad, Asd, qd, ald, alsd, zd]
+        pref = lambda t: L.PolyRef(t.data_ptr(), 2 * rows * n, rows * n)  # noqa: E731
+        r = L.RescaleArgs(pref(y), pref(tmp), Ad.data_ptr(), zd.data_ptr(), Asd.data_ptr(), zd.data_ptr(), qd.data_ptr(),
+                          qd.data_ptr(), self.pr, 0, 0, 1, 1, top, top, 1, 1)
+        self.call("rescale_coef", r)
+        self.ntt(False, tmp, [part * rows + t for part in (0, 1) for t in range(top)], list(range(top)) * 2)
+        out = x.clone()
+        c = L.RescaleCombineArgs(pref(out), pref(tmp), ald.data_ptr(), alsd.data_ptr(), self.pr, top, 1)
+        self.call("rescale_combine", c)
+        return out
+
+
+SEED, H, SIGMA = 0, 192, 3.2
+
+
+@pytest.fixture(scope="module")
+def cfg2():
+    ch = fhe.config2_chain()
+    s = fhe.Session(ch, rot_steps=(1, 5, -3), k_max=1, seed=SEED, h=H, sigma=SIGMA)
+    o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
+    o.keygen(SEED, H, SIGMA, s.galois)
+    return s, o
+
+
+@pytest.mark.parametrize("top,step", [(23, 1), (23, -3), (11, 5)])
+def test_reference_rotation_equals_oracle(cfg2, top, step):
+    s, o = cfg2
+    rt = RefRuntime(s, ref_table())
+    rng = np.random.default_rng(120 + top)
+    x = rng.normal(0, 1, 2048) / 8
+    ct = s.encrypt(x, top=top)
+    oc = o.encrypt(x, ct.slots, ct.scale, top)
+    assert (host(ct.data[0])[:, : top + 1] == oc[:, : top + 1]).all()
+    got = host(rt.rotate(ct.data[0], step, top))
+    want = o.rotate(oc, step, top)
+    assert (got[:, : top + 1] == want[:, : top + 1]).all(), "reference launchers' rotation != oracle"
+    ours = host(s.rotate(ct, step).data[0])
+    assert (ours[:, : top + 1] == got[:, : top + 1]).all()
+
+
+@pytest.mark.parametrize("top", [23, 12])
+def test_reference_relin_and_rescale_equal_oracle(cfg2, top):
+    s, o = cfg2
+    rt = RefRuntime(s, ref_table())
+    rng = np.random.default_rng(130 + top)
+    x, y = rng.normal(0, 1, 1024) / 8, rng.normal(0, 1, 1024) / 8
+    a, b = s.encrypt(x, top=top), s.encrypt(y, top=top)
+    oa, ob = o.encrypt(x, a.slots, a.scale, top), o.encrypt(y, b.slots, b.scale, top)
+    m = host(rt.mult(a.data[0], b.data[0], top))
+    om = o.mult(oa, ob, top)
+    assert (m[:, : top + 1] == om[:, : top + 1]).all(), "reference launchers' relinearized product != oracle"
+    ours = s.mult(a, b)
+    assert (host(ours.data[0])[:, : top + 1] == m[:, : top + 1]).all()
+    r = host(rt.rescale(ours.data[0], top))
+    orr = o.rescale(om, top)
+    assert (r[:, :top] == orr[:, :top]).all(), "reference launchers' rescale != oracle"
+    s.rescale_one(ours)
+    assert (host(ours.data[0])[:, :top] == r[:, :top]).all()

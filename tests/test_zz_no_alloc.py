@@ -19,9 +19,18 @@ from perseus_b200 import fhe
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def sess():
-    return fhe.Session(fhe.config1_chain(), rot_steps=(), k_max=1, seed=3, h=192, sigma=3.2)
+def _chain(which):
+    if which == "config1":  # integer kernels (a 60-bit special prime)
+        return fhe.config1_chain()
+    if which == "fp64":  # every prime below 2^50: the FP64 transforms
+        return fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 8)), tuple(fhe.ntt_primes(50, 14, 2, skip=8)), 4)
+    # 48 + 16 rows at N = 2^14: 2 (nq + kp) N = 2^21 words, the array exactly full
+    return fhe.Chain(14, tuple(fhe.ntt_primes(50, 14, 48)), tuple(fhe.ntt_primes(50, 14, 16, skip=48)), 3)
+
+
+@pytest.fixture(scope="module", params=["config1", "fp64", "full"])
+def sess(request):
+    return fhe.Session(_chain(request.param), rot_steps=(), k_max=1, seed=3, h=192, sigma=3.2)
 
 
 def _stream():

@@ -388,8 +388,16 @@ typedef struct PcbParams {
     const uint64_t* q;   /* nq primes, p = 1 mod 2N, < 2^61 */
     const uint64_t* p;   /* kp primes */
     int32_t k_max;       /* ciphertexts per batched key switch */
-    int32_t pad;
+    int32_t key_source;  /* PCB_KEYS_DENSE or PCB_KEYS_REGEN */
 } PcbParams;
+
+/* How the context stores its switching keys (the reference's KeySource, crates/pc-gpu/src/ks.rs:57):
+ *  PCB_KEYS_DENSE  b and a resident, 2 dnum (nq + kp) N words per key (the reference's Cached source);
+ *  PCB_KEYS_REGEN  b and the 8-word seed of a: a is regenerated from the seed inside every inner product (the frozen
+ *                  u64 expander lane), half the bytes per key (the reference's Regen source). The same keys and the
+ *                  same results word for word; pcb_key_ptrs gives a = NULL, pcb_key_copy expands a. */
+#define PCB_KEYS_DENSE 0
+#define PCB_KEYS_REGEN 1
 
 /* Message of the last failed call on this thread (empty when none). */
 const char* pcb_last_error(void);
@@ -413,10 +421,12 @@ int pcb_ctx_tables(const PcbCtx* ctx, const PcbPrimeConst** pr, const uint64_t**
  * encryptor seed. Keys are generated on the device (ksk_gen) into the arena. */
 int pcb_keygen(PcbCtx* ctx, uint64_t seed, uint32_t h, double sigma, int32_t ngal, const uint64_t* galois,
                cudaStream_t stream);
-/* key `idx` in keygen order: device pointers of b and a ([dnum][nq + kp][N]) and its galois element */
+/* key `idx` in keygen order: device pointers of b and a ([dnum][nq + kp][N]; a = NULL for PCB_KEYS_REGEN) and its
+ * galois element */
 int pcb_key_ptrs(const PcbCtx* ctx, int32_t idx, const uint64_t** b, const uint64_t** a, uint64_t* galois);
 
-/* Copy key `idx` (b then a, [dnum][nq + kp][N] words each) into caller device buffers on `stream`. */
+/* Copy key `idx` (b then a, [dnum][nq + kp][N] words each) into caller device buffers on `stream` (a regenerated
+ * key's a is expanded from its seed). */
 int pcb_key_copy(const PcbCtx* ctx, int32_t idx, uint64_t* b_out, uint64_t* a_out, cudaStream_t stream);
 
 /* Secret-key encryption of nvals (re, im) values into nslots slots at `scale`, rows 0..=top of ct (device). */

@@ -170,7 +170,7 @@ class RingTable(C.Structure):
 
 class Params(C.Structure):
     _fields_ = [("log_n", C.c_uint32), ("nq", C.c_int32), ("kp", C.c_int32), ("dnum", C.c_int32), ("q", u64p),
-                ("p", u64p), ("k_max", C.c_int32), ("pad", C.c_int32)]
+                ("p", u64p), ("k_max", C.c_int32), ("key_source", C.c_int32)]
 
 
 SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJob": 32, "BconvArgs": 56,

@@ -13,7 +13,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpcb200.so")
 SOURCES = ["ntt.cu", "elem.cu", "pt.cu", "ks.cu", "regen.cu", "keys.cu", "table.cu", "evaluator.cu"]
-HEADERS = ["arith.cuh", "chacha.cuh", "kernels.h", "host_math.h"]
+HEADERS = ["arith.cuh", "chacha.cuh", "keyregen.cuh", "kernels.h", "host_math.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

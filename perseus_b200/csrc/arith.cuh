@@ -141,6 +141,9 @@ __device__ __forceinline__ int rs_row(const PcbRowSet& rs, int y) { return y < r
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Start moving the 128-byte line holding p into L2 (no register result, no wait)
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // Launch with programmatic stream serialization: the kernel must call pdl_wait before its dependent reads
 template <typename... KArgs, typename... Args>
 __host__ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {

@@ -91,7 +91,7 @@ struct LevelPlan {
 
 struct KeySlot {
     uint64_t galois = 0, autok = 1;
-    uint64_t *b = nullptr, *a = nullptr;
+    uint64_t *b = nullptr, *a = nullptr;  // a null: regenerated from seed in the inner products (PCB_KEYS_REGEN)
     uint32_t* seed = nullptr;
     const void** kb = nullptr;  // device arrays of one pointer (KsArgs kb / ka)
     const void** ka = nullptr;
@@ -109,12 +109,14 @@ struct PcbCtx {
     const PcbKernelTable* tab = nullptr;
     bool narrow = false;  // every prime below 2^52: the 26-bit-split conversion and inner-product kernels
     bool f64 = false;     // every prime below 2^50: FP64 NTT butterflies
+    bool regen = false;   // PCB_KEYS_REGEN: keys stored as b + seed, `a` regenerated in the inner products
     Arena arena;
     // device tables
     PcbPrimeConst* pr = nullptr;
     uint64_t *fw = nullptr, *fws = nullptr, *iw = nullptr, *iws = nullptr, *ninv = nullptr, *ninvs = nullptr;
     double *fpk = nullptr, *ipk = nullptr;  // f64: forward / inverse twiddle packs, pack_words() doubles per prime
-    size_t pack_words() const { return 2 * ((n >> 8) + 256 + n); }
+    // (n / 256 + 256) {w, fl(w / p)} pairs, then n single twist factors (ntt.cu Pack)
+    size_t pack_words() const { return 2 * ((n >> 8) + 256) + n; }
     int32_t* digit_of = nullptr;
     uint64_t *pmod = nullptr, *pmods = nullptr, *pinv = nullptr, *pinvs = nullptr;
     uint32_t* id_roff = nullptr;   // i
@@ -238,8 +240,9 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
             CK(cudaMemcpyAsync(c.iw + (size_t)r * n, iw.data(), n * 8, cudaMemcpyHostToDevice, s));
             CK(cudaMemcpyAsync(c.iws + (size_t)r * n, iws.data(), n * 8, cudaMemcpyHostToDevice, s));
             if (c.f64) {
-                // pack: column twiddles w[0 .. R), the 256-point twiddles of psi^(N/256) in OpenFHE order, the twist
-                // gamma_b^k = psi^(k c_b) at b 256 + k with c_b = 1 - 2^(L-8) + 2 brev(b) (inverse: psi^-(k c_b)).
+                // pack: column twiddles w[0 .. R), the 256-point twiddles of psi^(N/256) in OpenFHE order (pairs), the
+                // twist gamma_b^k = psi^(k c_b) at b 256 + k with c_b = 1 - 2^(L-8) + 2 brev(b) (inverse: psi^-(k c_b)),
+                // single centred doubles after the pairs.
                 // Entry 0 is psi^0 = 1: {1, fl(1 / p)}, which the kernels read as 1 / p
                 const size_t R = n >> 8, m2 = 2 * n;
                 auto psi_pow = [&](size_t e) { e %= m2; return e < n ? pw[e] : (pw[e - n] ? p - pw[e - n] : 0); };
@@ -256,8 +259,9 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
                     const size_t cb = (1 + m2 - (n >> 8) + 2 * (size_t)hm::bitrev((uint32_t)b, L - 8)) % m2;
                     for (size_t k = 0; k < 256; ++k) {
                         const size_t e = k * cb % m2;
-                        centred(fpk, R + 256 + b * 256 + k, psi_pow(e), p);
-                        centred(ipk, R + 256 + b * 256 + k, psi_pow(m2 - e), p);
+                        const uint64_t fv = psi_pow(e), iv = psi_pow(m2 - e);
+                        fpk[2 * (R + 256) + b * 256 + k] = (double)(fv > p / 2 ? -(int64_t)(p - fv) : (int64_t)fv);
+                        ipk[2 * (R + 256) + b * 256 + k] = (double)(iv > p / 2 ? -(int64_t)(p - iv) : (int64_t)iv);
                     }
                 }
                 const size_t pwd = c.pack_words();
@@ -545,7 +549,7 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
     for (int k = 0; k < nkeys; ++k) {
         KeySlot& ks = c.keys[k];
         ks.b = A.take<uint64_t>((size_t)c.dnum * rows * n);
-        ks.a = A.take<uint64_t>((size_t)c.dnum * rows * n);
+        ks.a = c.regen ? nullptr : A.take<uint64_t>((size_t)c.dnum * rows * n);
         ks.seed = A.take<uint32_t>(8);
         ks.kb = A.take<const void*>(1);
         ks.ka = A.take<const void*>(1);
@@ -659,7 +663,7 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.out0 = c.ext + c0i * cw;
         a.out1 = c.ext + c0i * cw + rn;
         a.kb = ks.kb;
-        a.ka = ks.ka;
+        a.ka = ks.a ? ks.ka : nullptr;
         a.autok = ks.autok_dev;
         a.rows = l.ks_rows;
         a.digit_of = c.digit_of;
@@ -678,7 +682,9 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.c0_mode = c0_mode;
         a.nq = c.nq;
         a.nrows = top + 1 + c.kp;
-        CK(c.logn == 14 ? ks::dot_all_run<14>(&a, c.narrow, c.f64, s) : ks::dot_all_run<16>(&a, c.narrow, c.f64, s));
+        const uint32_t* seed = ks.a ? nullptr : ks.seed;
+        CK(c.logn == 14 ? ks::dot_all_run<14>(&a, c.narrow, c.f64, seed, s)
+                        : ks::dot_all_run<16>(&a, c.narrow, c.f64, seed, s));
     }
     return 0;
 }
@@ -719,6 +725,7 @@ int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, 
     for (int r = 0; r < n; ++r) {
         kg.kb[r] = keys[r]->b;
         kg.ka[r] = keys[r]->a;
+        kg.seed[r] = keys[r]->a ? nullptr : keys[r]->seed;
         kg.autok[r] = (uint32_t)keys[r]->autok;
     }
     CK(c.logn == 14 ? ks::dot_keys_run<14>(&a, kg, s) : ks::dot_keys_run<16>(&a, kg, s));
@@ -760,6 +767,7 @@ int dot_sum(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, co
     for (int r = 0; r < n; ++r) {
         kg.kb[r] = keys[r]->b;
         kg.ka[r] = keys[r]->a;
+        kg.seed[r] = keys[r]->a ? nullptr : keys[r]->seed;
         kg.g[r] = (uint32_t)keys[r]->galois;
     }
     CK(c.logn == 14 ? ks::dot_sum_run<14>(&a, kg, s) : ks::dot_sum_run<16>(&a, kg, s));
@@ -871,6 +879,9 @@ static int init_ctx(PcbCtx& c, const PcbParams* prm, int nkeys) {
     if (c.alpha > 16 || c.kp > 16) return fail(PCB_BAD_ARGS, "digits of %d limbs / %d special primes (max 16)", c.alpha, c.kp);
     c.k_max = prm->k_max;
     c.nkeys = nkeys;
+    if (prm->key_source != PCB_KEYS_DENSE && prm->key_source != PCB_KEYS_REGEN)
+        return fail(PCB_BAD_ARGS, "key_source %d (0 dense, 1 regenerated)", prm->key_source);
+    c.regen = prm->key_source == PCB_KEYS_REGEN;
     c.primes.assign(prm->q, prm->q + c.nq);
     c.primes.insert(c.primes.end(), prm->p, prm->p + c.kp);
     for (uint64_t p : c.primes)
@@ -1054,8 +1065,20 @@ int pcb_key_ptrs(const PcbCtx* c, int32_t idx, const uint64_t** b, const uint64_
 int pcb_key_copy(const PcbCtx* c, int32_t idx, uint64_t* b_out, uint64_t* a_out, cudaStream_t s) {
     if (!c || idx < 0 || idx >= c->nkeys_made) return fail(PCB_BAD_ARGS, "no key %d", idx);
     const size_t bytes = (size_t)c->dnum * c->rows * c->n * 8;
-    if (b_out) CK(cudaMemcpyAsync(b_out, c->keys[idx].b, bytes, cudaMemcpyDeviceToDevice, s));
-    if (a_out) CK(cudaMemcpyAsync(a_out, c->keys[idx].a, bytes, cudaMemcpyDeviceToDevice, s));
+    const KeySlot& k = c->keys[idx];
+    if (b_out) CK(cudaMemcpyAsync(b_out, k.b, bytes, cudaMemcpyDeviceToDevice, s));
+    if (a_out && k.a) CK(cudaMemcpyAsync(a_out, k.a, bytes, cudaMemcpyDeviceToDevice, s));
+    if (a_out && !k.a) {  // a regenerated key: expand its `a` from the seed, every digit and prime id
+        PcbKskExpandArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = a_out;
+        e.seed = k.seed;
+        e.prime_ids = c->key_rprime;
+        e.pr = c->pr;
+        e.nmod = c->rows;
+        e.dnum = c->dnum;
+        CK(c->tab->ksk_expand(&e, s));
+    }
     return 0;
 }
 

@@ -46,10 +46,13 @@ template <int LOGN> int bconv_run(const PcbBconvArgs*, bool narrow, bool f64, in
 template <int LOGN> int ks_dot_run(const PcbKsArgs*, bool narrow, cudaStream_t);
 // Up to KEYS_MAX keys against the same inputs in one launch (hoisted rotations): key pointers and automorphism
 // indices by value; key r's outputs go to out0 / out1 + r out_rot_stride. FP64 form (every prime below 2^50).
+// Key r's `a` is read from ka[r] (dense) or regenerated from the 8-word device seed seed[r] (keyregen.cuh); every key
+// of one launch has the same source.
 constexpr int KEYS_MAX = 4;
 struct KeyGroup {
     const uint64_t* kb[KEYS_MAX];
     const uint64_t* ka[KEYS_MAX];
+    const uint32_t* seed[KEYS_MAX];
     uint32_t autok[KEYS_MAX];
     int32_t n;
 };
@@ -61,13 +64,16 @@ constexpr int SUM_KEYS_MAX = 8;
 struct KeySum {
     const uint64_t* kb[SUM_KEYS_MAX];
     const uint64_t* ka[SUM_KEYS_MAX];
+    const uint32_t* seed[SUM_KEYS_MAX];  // as KeyGroup
+
     uint32_t g[SUM_KEYS_MAX];
     int32_t n;
 };
 template <int LOGN> int dot_sum_run(const PcbKsArgs*, const KeySum&, cudaStream_t);
 // one key, any batch K: key words read once per launch; inputs must not alias outputs
-// f64: every prime below 2^50 (FP64 products)
-template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, cudaStream_t);
+// f64: every prime below 2^50 (FP64 products); seed non-null: the key's `a` is regenerated from that 8-word device
+// seed (keyregen.cuh) and a.ka is not read
+template <int LOGN> int dot_all_run(const PcbKsArgs*, bool narrow, bool f64, const uint32_t* seed, cudaStream_t);
 }  // namespace ks
 namespace regen {
 template <int LOGN> int ks_dot_regen_launch(const PcbKsRegenArgs*, cudaStream_t);

@@ -11,6 +11,7 @@
 // The conversion matrix of a job and its target primes' Barrett constants sit in shared memory; source words stay in
 // registers across all targets.
 #include "arith.cuh"
+#include "keyregen.cuh"
 #include "kernels.h"
 
 namespace pcb {
@@ -413,9 +414,11 @@ int ks_dot_launch(const PcbKsArgs* ap, cudaStream_t s) {
 // The evaluator's inner product: one key (R = 1), any number K of ciphertexts. Each thread reads its slot's key
 // words of every digit once and then walks the K ciphertexts, so a batch streams the key once (ks_dot re-reads it
 // for every group of <= 8). The inputs (c1, the ModUp digits, c0) must not alias the outputs. ND > 0: exactly ND
-// live digits (unrolled); 0: a.ndig <= 16.
-template <int LOGN, int ND, bool NARROW>
-__global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
+// live digits (unrolled); 0: a.ndig <= 16. RG: the key's `a` is regenerated from `seed` into shared memory
+// (keyregen.cuh: the CTA's BX slots, every digit) instead of read from a.ka.
+template <int LOGN, int ND, bool NARROW, bool RG>
+__global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a, const uint32_t* seed) {
+    extern __shared__ __align__(16) uint64_t rg_sm[];
     constexpr int D = ND > 0 ? ND : 16;
     const int nd = ND > 0 ? ND : a.ndig;
     const uint32_t t = a.rows[blockIdx.y];
@@ -432,13 +435,20 @@ __global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
         pms = ((const uint64_t*)a.pmods)[t];
     }
     const uint64_t* kb = (const uint64_t*)a.kb[0] + roff;
-    const uint64_t* ka = (const uint64_t*)a.ka[0] + roff;
+    const uint64_t* ka = RG ? nullptr : (const uint64_t*)a.ka[0] + roff;
+    constexpr int NSEG = BX / keyregen::SEG;
+    if constexpr (RG) {
+        const uint32_t tile0 = blockIdx.x * BX;
+        keyregen::stage<LOGN>(&seed, 1, nd, NSEG, [tile0](int, int j) { return tile0 + (uint32_t)j * keyregen::SEG; },
+                              pc, rg_sm);
+    }
     uint64_t bv[D], av[D];
 #pragma unroll
     for (int d = 0; d < D; ++d) {
         if (ND > 0 || d < nd) {
             bv[d] = __ldcs(kb + (size_t)d * a.key_digit_stride);
-            av[d] = __ldcs(ka + (size_t)d * a.key_digit_stride);
+            av[d] = RG ? keyregen::at(rg_sm, nd, NSEG, 0, d, threadIdx.x / keyregen::SEG, idx)
+                       : __ldcs(ka + (size_t)d * a.key_digit_stride);
         }
     }
     const uint32_t k = a.autok[0];
@@ -489,8 +499,9 @@ __global__ void __launch_bounds__(BX) dot_all(PcbKsArgs a) {
 // b / p taken as fl(b fl(1 / p)) (relative error <= 2^-52: |x b / p| < 2^49, so q is within 0.63 of it and each
 // product lies in [-0.63p, 0.63p]); sums are reduced every 4 digits and made canonical once per output word. Each
 // thread takes two adjacent words (16-byte loads; the launcher checks the alignment) of every ciphertext.
-template <int LOGN, int ND>
-__global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
+template <int LOGN, int ND, bool RG>
+__global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a, const uint32_t* seed) {
+    extern __shared__ __align__(16) uint64_t rg_sm[];
     constexpr int D = ND > 0 ? ND : 16;
     const int nd = ND > 0 ? ND : a.ndig;
     const uint32_t t = a.rows[blockIdx.y];
@@ -507,13 +518,22 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
         pms = ((const uint64_t*)a.pmods)[t];
     }
     const uint64_t* kb = (const uint64_t*)a.kb[0] + roff;
-    const uint64_t* ka = (const uint64_t*)a.ka[0] + roff;
+    const uint64_t* ka = RG ? nullptr : (const uint64_t*)a.ka[0] + roff;
+    constexpr int NSEG = 2 * BX / keyregen::SEG;
+    if constexpr (RG) {  // the CTA's 2 BX slots of every digit
+        const uint32_t tile0 = 2 * blockIdx.x * BX;
+        keyregen::stage<LOGN>(&seed, 1, nd, NSEG, [tile0](int, int j) { return tile0 + (uint32_t)j * keyregen::SEG; },
+                              a.pr[t], rg_sm);
+    }
     double bw[D][2], bq[D][2], aw[D][2], aq[D][2];
 #pragma unroll
     for (int d = 0; d < D; ++d) {
         if (ND > 0 || d < nd) {
             const ulonglong2 b = __ldcs((const ulonglong2*)(kb + (size_t)d * a.key_digit_stride));
-            const ulonglong2 av = __ldcs((const ulonglong2*)(ka + (size_t)d * a.key_digit_stride));
+            const ulonglong2 av =
+                RG ? *(const ulonglong2*)&rg_sm[((size_t)d * NSEG + (2 * threadIdx.x) / keyregen::SEG) * keyregen::SEG +
+                                               ((2 * threadIdx.x) & (keyregen::SEG - 1))]
+                   : __ldcs((const ulonglong2*)(ka + (size_t)d * a.key_digit_stride));
             const uint64_t bb[2] = {b.x, b.y}, aa[2] = {av.x, av.y};
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -558,8 +578,10 @@ __global__ void __launch_bounds__(BX) dot_all_f(PcbKsArgs a) {
 // thread; the keys stay in registers as centred doubles (their quotients by p are formed per use, as in dot_all_f).
 // 6 CTAs per SM (at most 85 registers, 24 warps): the config-2 step took 100.0 ms, against 101.0 at 5 CTAs
 // (102 registers) and 101.5-102.5 with the compiler's choice of 116
-template <int LOGN, int ND, int RK>
+// RG: every key's `a` is regenerated from kg.seed[r] into shared memory (the CTA's BX slots, RK keys x ND digits).
+template <int LOGN, int ND, int RK, bool RG>
 __global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
+    extern __shared__ __align__(16) uint64_t rg_sm[];
     const uint32_t t = a.rows[blockIdx.y];
     const uint64_t p = a.pr[t].p;
     const double pf = to_f(p), pinv = 1.0 / pf;
@@ -573,6 +595,12 @@ __global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
         pm = ((const uint64_t*)a.pmod)[t];
         pms = ((const uint64_t*)a.pmods)[t];
     }
+    constexpr int NSEG = BX / keyregen::SEG;
+    if constexpr (RG) {
+        const uint32_t tile0 = blockIdx.x * BX;
+        keyregen::stage<LOGN>(kg.seed, RK, ND, NSEG, [tile0](int, int j) { return tile0 + (uint32_t)j * keyregen::SEG; },
+                              a.pr[t], rg_sm);
+    }
     double bw[RK][ND], aw[RK][ND];
     uint32_t o[RK];
 #pragma unroll
@@ -580,7 +608,8 @@ __global__ void __launch_bounds__(BX, 6) dot_keys_f(PcbKsArgs a, KeyGroup kg) {
 #pragma unroll
         for (int d = 0; d < ND; ++d) {
             const uint64_t b = __ldcs(kg.kb[r] + roff + (size_t)d * a.key_digit_stride);
-            const uint64_t av = __ldcs(kg.ka[r] + roff + (size_t)d * a.key_digit_stride);
+            const uint64_t av = RG ? keyregen::at(rg_sm, ND, NSEG, r, d, threadIdx.x / keyregen::SEG, idx)
+                                   : __ldcs(kg.ka[r] + roff + (size_t)d * a.key_digit_stride);
             bw[r][d] = b > p / 2 ? -to_f(p - b) : to_f(b);
             aw[r][d] = av > p / 2 ? -to_f(p - av) : to_f(av);
         }
@@ -627,9 +656,10 @@ struct SumRow {
 
 // CB ciphertexts from cb: per key, its 2 ND words and the CB x ND digit words are all loaded before any product (no
 // predicate between them), so each key costs one memory latency instead of one per ciphertext
+// rg: the keys' staged `a` segments (keyregen.cuh, nseg 4, this thread's segment j = its warp), or null (dense)
 template <int LOGN, int ND, int CB>
 __device__ __forceinline__ void dot_sum_chunk(const PcbKsArgs& a, const KeySum& ks, const SumRow& w,
-                                              const uint32_t* src, uint32_t o, int cb) {
+                                              const uint32_t* src, uint32_t o, int cb, const uint64_t* rg) {
     const uint64_t* c1 = (const uint64_t*)a.c1;
     const uint64_t* mu = (const uint64_t*)a.modup;
     double s0[CB], s1[CB];
@@ -641,7 +671,8 @@ __device__ __forceinline__ void dot_sum_chunk(const PcbKsArgs& a, const KeySum& 
 #pragma unroll
         for (int d = 0; d < ND; ++d) {
             kbv[d] = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
-            kav[d] = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
+            kav[d] = rg ? keyregen::at(rg, ND, BX / keyregen::SEG, r, d, threadIdx.x / keyregen::SEG, src[r])
+                        : __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
         }
 #pragma unroll
         for (int u = 0; u < CB; ++u)
@@ -687,8 +718,11 @@ __device__ __forceinline__ void dot_sum_chunk(const PcbKsArgs& a, const KeySum& 
 }
 
 // Ciphertexts in chunks of CB (then one at a time for the rest); with PCB_KS_ACC the previous batch is added
-template <int LOGN, int ND, int CB>
+// RG: the keys' `a` regenerated into shared memory: per key, the 4 aligned 32-slot source segments that the CTA's
+// 4 warps of output slots gather from
+template <int LOGN, int ND, int CB, bool RG>
 __global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
+    extern __shared__ __align__(16) uint64_t rg_sm[];
     SumRow w;
     w.t = a.rows[blockIdx.y];
     w.p = a.pr[w.t].p;
@@ -703,21 +737,35 @@ __global__ void __launch_bounds__(BX, 4) dot_sum_f(PcbKsArgs a, KeySum ks) {
         w.pms = ((const uint64_t*)a.pmods)[w.t];
     }
     const uint32_t o = blockIdx.x * BX + threadIdx.x;
+    if constexpr (RG) {
+        const uint32_t tile0 = blockIdx.x * BX;
+        const uint32_t* g = ks.g;
+        keyregen::stage<LOGN>(ks.seed, ks.n, ND, BX / keyregen::SEG,
+                              [tile0, g](int r, int j) {
+                                  return automorph_slot<LOGN>(g[r], tile0 + (uint32_t)j * keyregen::SEG) &
+                                         ~(uint32_t)(keyregen::SEG - 1);
+                              },
+                              a.pr[w.t], rg_sm);
+    }
+    const uint64_t* rg = RG ? rg_sm : nullptr;
     uint32_t src[SUM_KEYS_MAX];
 #pragma unroll
     for (int r = 0; r < SUM_KEYS_MAX; ++r) src[r] = r < ks.n ? automorph_slot<LOGN>(ks.g[r], o) : 0;
     int cb = 0;
-    for (; cb + CB <= a.K; cb += CB) dot_sum_chunk<LOGN, ND, CB>(a, ks, w, src, o, cb);
-    for (; cb < a.K; ++cb) dot_sum_chunk<LOGN, ND, 1>(a, ks, w, src, o, cb);
+    for (; cb + CB <= a.K; cb += CB) dot_sum_chunk<LOGN, ND, CB>(a, ks, w, src, o, cb, rg);
+    for (; cb < a.K; ++cb) dot_sum_chunk<LOGN, ND, 1>(a, ks, w, src, o, cb, rg);
 }
 
 // One ciphertext (K = 1): the keys split over the CTA's 4 warps for the same 32 output slots (warp w takes keys w,
 // w + 4), each warp's partial sum canonical in shared memory, warp 0 adding them up: four warps' loads in flight per
 // slot where the one-thread-per-slot form walks the keys one after another.
 constexpr int SUM1_WARPS = 4;
-template <int LOGN, int ND>
+// RG: every key's `a` regenerated into shared memory (per key the one aligned 32-slot segment the 32 outputs gather
+// from), staged by all four warps before the products
+template <int LOGN, int ND, bool RG>
 __global__ void __launch_bounds__(32 * SUM1_WARPS) dot_sum1_f(PcbKsArgs a, KeySum ks) {
     __shared__ uint64_t part[2][SUM1_WARPS][32];
+    extern __shared__ __align__(16) uint64_t rg_sm[];
     const uint32_t t = a.rows[blockIdx.y];
     const uint64_t p = a.pr[t].p;
     const double pf = to_f(p), pinv = 1.0 / pf;
@@ -734,15 +782,25 @@ __global__ void __launch_bounds__(32 * SUM1_WARPS) dot_sum1_f(PcbKsArgs a, KeySu
         pm = ((const uint64_t*)a.pmod)[t];
         pms = ((const uint64_t*)a.pmods)[t];
     }
+    if constexpr (RG) {
+        const uint32_t tile0 = blockIdx.x * 32;
+        const uint32_t* g = ks.g;
+        keyregen::stage<LOGN>(ks.seed, ks.n, ND, 1,
+                              [tile0, g](int r, int) {
+                                  return automorph_slot<LOGN>(g[r], tile0) & ~(uint32_t)(keyregen::SEG - 1);
+                              },
+                              a.pr[t], rg_sm);
+    }
     double s0 = 0.0, s1 = 0.0;
     uint64_t cs = 0;  // this warp's keys' P sigma(c0) terms
     for (int r = wp; r < ks.n; r += SUM1_WARPS) {
-        const size_t off = row + automorph_slot<LOGN>(ks.g[r], o);
+        const uint32_t src = automorph_slot<LOGN>(ks.g[r], o);
+        const size_t off = row + src;
         uint64_t kbv[ND], kav[ND], xw[ND];
 #pragma unroll
         for (int d = 0; d < ND; ++d) {
             kbv[d] = __ldg(ks.kb[r] + off + (size_t)d * a.key_digit_stride);
-            kav[d] = __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
+            kav[d] = RG ? keyregen::at(rg_sm, ND, 1, r, d, 0, src) : __ldg(ks.ka[r] + off + (size_t)d * a.key_digit_stride);
             xw[d] = __ldg(d == dt ? c1 + off : mu + (size_t)d * a.mu_digit_stride + off);
         }
         const uint64_t cw = addc0 ? __ldg(c0 + off) : 0;
@@ -779,14 +837,26 @@ __global__ void __launch_bounds__(32 * SUM1_WARPS) dot_sum1_f(PcbKsArgs a, KeySu
     }
 }
 
-template <int LOGN, int ND>
+template <int LOGN, int ND, bool RG>
 void dot_keys_dispatch(const PcbKsArgs& a, const KeyGroup& kg, dim3 g, cudaStream_t s) {
+    const size_t sm = RG ? (size_t)kg.n * ND * BX * sizeof(uint64_t) : 0;
     switch (kg.n) {
-        case 1: dot_keys_f<LOGN, ND, 1><<<g, BX, 0, s>>>(a, kg); break;
-        case 2: dot_keys_f<LOGN, ND, 2><<<g, BX, 0, s>>>(a, kg); break;
-        case 3: dot_keys_f<LOGN, ND, 3><<<g, BX, 0, s>>>(a, kg); break;
-        default: dot_keys_f<LOGN, ND, 4><<<g, BX, 0, s>>>(a, kg);
+        case 1: dot_keys_f<LOGN, ND, 1, RG><<<g, BX, sm, s>>>(a, kg); break;
+        case 2: dot_keys_f<LOGN, ND, 2, RG><<<g, BX, sm, s>>>(a, kg); break;
+        case 3: dot_keys_f<LOGN, ND, 3, RG><<<g, BX, sm, s>>>(a, kg); break;
+        default: dot_keys_f<LOGN, ND, 4, RG><<<g, BX, sm, s>>>(a, kg);
     }
+}
+
+// every key of a group or sum is either dense (ka set) or regenerated (seed set), the same for all
+template <class G>
+int key_source_of(const G& kg) {
+    bool dense = false, regen = false;
+    for (int r = 0; r < kg.n; ++r) {
+        if (!kg.kb[r] || (!kg.ka[r] == !kg.seed[r])) return -1;
+        (kg.seed[r] ? regen : dense) = true;
+    }
+    return dense && regen ? -1 : regen ? 1 : 0;
 }
 
 template <int LOGN>
@@ -796,20 +866,54 @@ int dot_keys_run(const PcbKsArgs* ap, const KeyGroup& kg, cudaStream_t s) {
     if (kg.n < 1 || kg.n > KEYS_MAX || a.K < 0 || a.ndig < 1 || a.ndig > 4 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
         (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.rows || !a.digit_of || !a.pr)
         return PCB_BAD_ARGS;
+    const int src = key_source_of(kg);
+    if (src < 0) return PCB_BAD_ARGS;
     for (int r = 0; r < kg.n; ++r)
-        if (!kg.kb[r] || !kg.ka[r] || !(kg.autok[r] & 1)) return PCB_BAD_ARGS;
+        if (!(kg.autok[r] & 1)) return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
     if (a.K == 0 || a.nrows == 0) return 0;
     const dim3 g((1 << LOGN) / BX, a.nrows);
-    switch (a.ndig) {
-        case 1: dot_keys_dispatch<LOGN, 1>(a, kg, g, s); break;
-        case 2: dot_keys_dispatch<LOGN, 2>(a, kg, g, s); break;
-        case 3: dot_keys_dispatch<LOGN, 3>(a, kg, g, s); break;
-        default: dot_keys_dispatch<LOGN, 4>(a, kg, g, s);
+    if (src) {
+        switch (a.ndig) {
+            case 1: dot_keys_dispatch<LOGN, 1, true>(a, kg, g, s); break;
+            case 2: dot_keys_dispatch<LOGN, 2, true>(a, kg, g, s); break;
+            case 3: dot_keys_dispatch<LOGN, 3, true>(a, kg, g, s); break;
+            default: dot_keys_dispatch<LOGN, 4, true>(a, kg, g, s);
+        }
+    } else {
+        switch (a.ndig) {
+            case 1: dot_keys_dispatch<LOGN, 1, false>(a, kg, g, s); break;
+            case 2: dot_keys_dispatch<LOGN, 2, false>(a, kg, g, s); break;
+            case 3: dot_keys_dispatch<LOGN, 3, false>(a, kg, g, s); break;
+            default: dot_keys_dispatch<LOGN, 4, false>(a, kg, g, s);
+        }
     }
     return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN, bool RG>
+void dot_sum_dispatch(const PcbKsArgs& a, const KeySum& ks, cudaStream_t s) {
+    if (a.K == 1) {
+        const dim3 g1((1 << LOGN) / 32, a.nrows);
+        const size_t sm = RG ? (size_t)ks.n * a.ndig * keyregen::SEG * sizeof(uint64_t) : 0;
+        switch (a.ndig) {
+            case 1: dot_sum1_f<LOGN, 1, RG><<<g1, 32 * SUM1_WARPS, sm, s>>>(a, ks); break;
+            case 2: dot_sum1_f<LOGN, 2, RG><<<g1, 32 * SUM1_WARPS, sm, s>>>(a, ks); break;
+            case 3: dot_sum1_f<LOGN, 3, RG><<<g1, 32 * SUM1_WARPS, sm, s>>>(a, ks); break;
+            default: dot_sum1_f<LOGN, 4, RG><<<g1, 32 * SUM1_WARPS, sm, s>>>(a, ks);
+        }
+        return;
+    }
+    const dim3 g((1 << LOGN) / BX, a.nrows);
+    const size_t sm = RG ? (size_t)ks.n * a.ndig * BX * sizeof(uint64_t) : 0;
+    switch (a.ndig) {
+        case 1: dot_sum_f<LOGN, 1, 4, RG><<<g, BX, sm, s>>>(a, ks); break;
+        case 2: dot_sum_f<LOGN, 2, 4, RG><<<g, BX, sm, s>>>(a, ks); break;
+        case 3: dot_sum_f<LOGN, 3, 4, RG><<<g, BX, sm, s>>>(a, ks); break;
+        default: dot_sum_f<LOGN, 4, 4, RG><<<g, BX, sm, s>>>(a, ks);
+    }
 }
 
 template <int LOGN>
@@ -820,63 +924,52 @@ int dot_sum_run(const PcbKsArgs* ap, const KeySum& ks, cudaStream_t s) {
         (a.c0_mode & 3) == 2 || (a.c0_mode & 3) == 3 || (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 ||
         !a.out1 || !a.rows || !a.digit_of || !a.pr)
         return PCB_BAD_ARGS;
+    const int src = key_source_of(ks);
+    if (src < 0) return PCB_BAD_ARGS;
     for (int r = 0; r < ks.n; ++r)
-        if (!ks.kb[r] || !ks.ka[r] || !(ks.g[r] & 1)) return PCB_BAD_ARGS;
+        if (!(ks.g[r] & 1)) return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) == 1 && (!a.c0 || !a.pmod || !a.pmods)) return PCB_BAD_ARGS;
     if (a.ndig > 1 && !a.modup) return PCB_BAD_ARGS;
     if (a.K == 0 || a.nrows == 0) return 0;
-    if (a.K == 1) {
-        const dim3 g1((1 << LOGN) / 32, a.nrows);
-        switch (a.ndig) {
-            case 1: dot_sum1_f<LOGN, 1><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
-            case 2: dot_sum1_f<LOGN, 2><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
-            case 3: dot_sum1_f<LOGN, 3><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks); break;
-            default: dot_sum1_f<LOGN, 4><<<g1, 32 * SUM1_WARPS, 0, s>>>(a, ks);
-        }
-        return PCB_LAUNCH_RESULT();
-    }
-    const dim3 g((1 << LOGN) / BX, a.nrows);
-    switch (a.ndig) {
-        case 1: dot_sum_f<LOGN, 1, 4><<<g, BX, 0, s>>>(a, ks); break;
-        case 2: dot_sum_f<LOGN, 2, 4><<<g, BX, 0, s>>>(a, ks); break;
-        case 3: dot_sum_f<LOGN, 3, 4><<<g, BX, 0, s>>>(a, ks); break;
-        default: dot_sum_f<LOGN, 4, 4><<<g, BX, 0, s>>>(a, ks);
-    }
+    if (src) dot_sum_dispatch<LOGN, true>(a, ks, s);
+    else dot_sum_dispatch<LOGN, false>(a, ks, s);
     return PCB_LAUNCH_RESULT();
 }
 
-template <int LOGN, bool NARROW>
-void dot_dispatch(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
+template <int LOGN, bool NARROW, bool RG>
+void dot_dispatch(const PcbKsArgs& a, const uint32_t* seed, dim3 g, cudaStream_t s) {
+    const size_t sm = RG ? (size_t)a.ndig * BX * sizeof(uint64_t) : 0;
     switch (a.ndig) {
-        case 1: dot_all<LOGN, 1, NARROW><<<g, BX, 0, s>>>(a); break;
-        case 2: dot_all<LOGN, 2, NARROW><<<g, BX, 0, s>>>(a); break;
-        case 3: dot_all<LOGN, 3, NARROW><<<g, BX, 0, s>>>(a); break;
-        case 4: dot_all<LOGN, 4, NARROW><<<g, BX, 0, s>>>(a); break;
-        case 8: dot_all<LOGN, 8, NARROW><<<g, BX, 0, s>>>(a); break;
-        default: dot_all<LOGN, 0, NARROW><<<g, BX, 0, s>>>(a);
+        case 1: dot_all<LOGN, 1, NARROW, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 2: dot_all<LOGN, 2, NARROW, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 3: dot_all<LOGN, 3, NARROW, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 4: dot_all<LOGN, 4, NARROW, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 8: dot_all<LOGN, 8, NARROW, RG><<<g, BX, sm, s>>>(a, seed); break;
+        default: dot_all<LOGN, 0, NARROW, RG><<<g, BX, sm, s>>>(a, seed);
     }
 }
 
 // Plain launches: programmatic dependent launch of bconv_f and dot_all_f (tables and keys staged before the wait)
-// measured 2.5 ms slower per config-2 step (111.3 against 108.8 ms), so only the NTT passes use it.
-template <int LOGN>
-void dot_dispatch_f(const PcbKsArgs& a, dim3 g, cudaStream_t s) {
+// measured slower here (108.8 -> 111.3 ms per config-2 step)
+template <int LOGN, bool RG>
+void dot_dispatch_f(const PcbKsArgs& a, const uint32_t* seed, dim3 g, cudaStream_t s) {
+    const size_t sm = RG ? (size_t)a.ndig * 2 * BX * sizeof(uint64_t) : 0;
     switch (a.ndig) {
-        case 1: dot_all_f<LOGN, 1><<<g, BX, 0, s>>>(a); break;
-        case 2: dot_all_f<LOGN, 2><<<g, BX, 0, s>>>(a); break;
-        case 3: dot_all_f<LOGN, 3><<<g, BX, 0, s>>>(a); break;
-        case 4: dot_all_f<LOGN, 4><<<g, BX, 0, s>>>(a); break;
-        default: dot_all_f<LOGN, 0><<<g, BX, 0, s>>>(a);
+        case 1: dot_all_f<LOGN, 1, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 2: dot_all_f<LOGN, 2, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 3: dot_all_f<LOGN, 3, RG><<<g, BX, sm, s>>>(a, seed); break;
+        case 4: dot_all_f<LOGN, 4, RG><<<g, BX, sm, s>>>(a, seed); break;
+        default: dot_all_f<LOGN, 0, RG><<<g, BX, sm, s>>>(a, seed);
     }
 }
 
 template <int LOGN>
-int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
+int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, const uint32_t* seed, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
     const PcbKsArgs& a = *ap;
     if (a.K < 0 || a.R != 1 || a.ndig < 1 || a.ndig > 16 || a.nrows < 0 || (a.c0_mode & 3) == 3 ||
-        (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.kb || !a.ka || !a.autok || !a.rows ||
-        !a.digit_of || !a.pr)
+        (a.c0_mode & ~(3 | PCB_KS_ACC)) || !a.c1 || !a.out0 || !a.out1 || !a.kb || (!a.ka && !seed) || !a.autok ||
+        !a.rows || !a.digit_of || !a.pr)
         return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) && !a.c0) return PCB_BAD_ARGS;
     if ((a.c0_mode & 3) == 1 && (!a.pmod || !a.pmods)) return PCB_BAD_ARGS;
@@ -889,11 +982,12 @@ int dot_all_run(const PcbKsArgs* ap, bool narrow, bool f64, cudaStream_t s) {
         const bool odd = (a.ct_stride | a.mu_ct_stride | a.mu_digit_stride | a.key_digit_stride) & 1;
         const uintptr_t bases = (uintptr_t)a.c1 | (uintptr_t)a.modup;
         if (odd || (bases & 15)) return PCB_BAD_ARGS;
-        dot_dispatch_f<LOGN>(a, dim3((1 << LOGN) / (2 * BX), a.nrows), s);
+        const dim3 gf((1 << LOGN) / (2 * BX), a.nrows);
+        seed ? dot_dispatch_f<LOGN, true>(a, seed, gf, s) : dot_dispatch_f<LOGN, false>(a, nullptr, gf, s);
     } else if (narrow) {
-        dot_dispatch<LOGN, true>(a, g, s);
+        seed ? dot_dispatch<LOGN, true, true>(a, seed, g, s) : dot_dispatch<LOGN, true, false>(a, nullptr, g, s);
     } else {
-        dot_dispatch<LOGN, false>(a, g, s);
+        seed ? dot_dispatch<LOGN, false, true>(a, seed, g, s) : dot_dispatch<LOGN, false, false>(a, nullptr, g, s);
     }
     return PCB_LAUNCH_RESULT();
 }
@@ -902,8 +996,8 @@ template int dot_sum_run<14>(const PcbKsArgs*, const KeySum&, cudaStream_t);
 template int dot_sum_run<16>(const PcbKsArgs*, const KeySum&, cudaStream_t);
 template int dot_keys_run<14>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
 template int dot_keys_run<16>(const PcbKsArgs*, const KeyGroup&, cudaStream_t);
-template int dot_all_run<14>(const PcbKsArgs*, bool, bool, cudaStream_t);
-template int dot_all_run<16>(const PcbKsArgs*, bool, bool, cudaStream_t);
+template int dot_all_run<14>(const PcbKsArgs*, bool, bool, const uint32_t*, cudaStream_t);
+template int dot_all_run<16>(const PcbKsArgs*, bool, bool, const uint32_t*, cudaStream_t);
 template int bconv_launch<14>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_launch<16>(const PcbBconvArgs*, cudaStream_t);
 template int bconv_run<14>(const PcbBconvArgs*, bool, bool, int, cudaStream_t);

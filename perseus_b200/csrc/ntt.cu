@@ -112,12 +112,25 @@ __device__ __forceinline__ ulonglong2 tw_int(const uint64_t* w, const uint64_t* 
     return make_ulonglong2(__ldg(w + idx), __ldg(ws + idx));
 }
 
-// FP64 twiddle pack of one prime (forward and inverse each): the column stages' twiddles (indices 0 .. R-1), the
-// fixed 256-point transform's twiddles, the N twist factors gamma_b^k (forward) or gamma_b^-k (inverse) at b 256 + k
+// FP64 twiddle pack of one prime (forward and inverse each), in doubles: R + 256 pairs {w, fl(w / p)} — the column
+// stages' twiddles (pair indices 0 .. R-1) and the fixed 256-point transform's (R .. R+255) — then the N twist factors
+// gamma_b^k (forward) or gamma_b^-k (inverse) at TWIST_D + b 256 + k as single centred doubles: their quotients by p
+// are formed as fl(w fl(1 / p)) at use (relative error <= 2^-52; the product y w with |y| < 4p then stays within
+// [-p, p], see mul_f), which halves the table each column pass re-reads per row.
 template <int LOGN>
 struct Pack {
-    static constexpr int R = 1 << (LOGN - 8), ROW = R, TWIST = R + 256, SIZE = R + 256 + (1 << LOGN);
+    static constexpr int R = 1 << (LOGN - 8), ROW = R;
+    static constexpr int TWIST_D = 2 * (R + 256), SIZE_D = TWIST_D + (1 << LOGN);
 };
+// the row's pack: pairs (double2 view) and the twist factors
+template <int LOGN>
+__device__ __forceinline__ const double2* pack_pairs(const void* tw, int pid) {
+    return (const double2*)((const double*)tw + (size_t)pid * Pack<LOGN>::SIZE_D);
+}
+template <int LOGN>
+__device__ __forceinline__ const double* pack_twist(const void* tw, int pid) {
+    return (const double*)tw + (size_t)pid * Pack<LOGN>::SIZE_D + Pack<LOGN>::TWIST_D;
+}
 // Shared-memory slot of fixed twiddle t. Stages whose twiddle varies with the thread (4 .. 7 forward, 0 .. 3
 // inverse) read region [2^e, 2^(e+1)) at offset u 2^(e-4) + j; stored as [j][u], 16 threads read consecutive slots.
 // The per-row constants: FP64 takes fl(1 / p) from entry 0 of the row's pack ({1, fl(1 / p)}: twiddle index 0 is
@@ -125,8 +138,7 @@ struct Pack {
 template <int LOGN, bool F>
 __device__ __forceinline__ Mod<F> mod_of(uint64_t p, const void* tw, int pid) {
     if constexpr (F) {
-        const double2* pk = (const double2*)tw + (size_t)pid * Pack<LOGN>::SIZE;
-        return FpMod{to_f(p), __ldg(&pk->y)};
+        return FpMod{to_f(p), __ldg(&pack_pairs<LOGN>(tw, pid)->y)};
     } else {
         return IntMod{p, 2 * p};
     }
@@ -186,10 +198,11 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     const Mod<F> md = mod_of<LOGN, F>(p, a.fw, ri.pid);
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
-    const double2* pk = nullptr;
+    const double* twist = nullptr;
     if constexpr (F) {
-        pk = (const double2*)a.fw + (size_t)ri.pid * Pack<LOGN>::SIZE;
+        const double2* pk = pack_pairs<LOGN>(a.fw, ri.pid);
         for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = pk[t];
+        twist = pack_twist<LOGN>(a.fw, ri.pid);
     } else {
         const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
         const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
@@ -233,8 +246,8 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     for (int k = 0; k < E; ++k) {
         const size_t w = (size_t)(E * g + k) * 256 + col;  // block E g + k, word col: twist gamma_b^col
         if constexpr (F) {
-            const double2 t = __ldg(pk + Pack<LOGN>::TWIST + w);
-            x[k] = mul_f(x[k], t.x, t.y, md.p);
+            const double t = __ldg(twist + w);
+            x[k] = mul_f(x[k], t, __dmul_rn(t, md.pinv), md.p);
         }
         store_mid<F>(ri.row + w, x[k]);
     }
@@ -263,15 +276,19 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
     const Mod<F> md = mod_of<LOGN, F>(p, a.fw, ri.pid);
     const uint64_t* fw = (const uint64_t*)a.fw + ((size_t)ri.pid << LOGN);
     const uint64_t* fws = (const uint64_t*)a.fws + ((size_t)ri.pid << LOGN);
-    if constexpr (F) {
-        const double2* pk = (const double2*)a.fw + (size_t)ri.pid * Pack<LOGN>::SIZE + Pack<LOGN>::ROW;
-        sw[tw_slot(threadIdx.x)] = pk[threadIdx.x];
-    }
+    if constexpr (F) sw[tw_slot(threadIdx.x)] = pack_pairs<LOGN>(a.fw, ri.pid)[Pack<LOGN>::ROW + threadIdx.x];
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;  // 256-word block of the row
     uint64_t* blk = ri.row + (size_t)b * 256;
     pdl_wait();
     pdl_release();
+    if constexpr (EPI != 0) {
+        // the epilogue's rows (this thread's 16 words = one 128-byte line of each) are read only after the
+        // butterflies: start moving them into L2 now
+        const size_t r = ((size_t)a.roff[i] << LOGN) + (size_t)b * 256 + 16 * u;
+        for (int j = 0; j < a.xnum; ++j) prefetch_l2((const uint64_t*)a.ex + r + (size_t)j * a.xstride);
+        if (EPI == 2) prefetch_l2(a.ed ? (const uint64_t*)a.ed + r : (const uint64_t*)a.eout + r);
+    }
     T x[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) x[k] = load_mid<F>(blk + u + 16 * k);
@@ -329,16 +346,30 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
     uint64_t* own = (uint64_t*)s;
 #pragma unroll
     for (int k = 0; k < 16; ++k) own[pad(16 * u + k)] = bits(x[k]);
+    // the loads of a group of 4 word pairs are all issued before any of them is used (one memory latency per group,
+    // not per pair; the rows were prefetched into L2 at the start); groups of 8 spill under the 80-register cap
+    constexpr int G = 4;
 #pragma unroll 1
-    for (int k = 0; k < 8; ++k) {
-        ulonglong2 xs = ex[k];
-        for (int j = 1; j < a.xnum; ++j) {
-            const ulonglong2 t = ex[k + (size_t)j * xs2];
-            xs = make_ulonglong2(add_mod(xs.x, t.x, p), add_mod(xs.y, t.y, p));
+    for (int k0 = 0; k0 < 8; k0 += G) {
+        ulonglong2 xs[G], d[G];
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            xs[k] = ex[k0 + k];
+            d[k] = EPI == 2 ? ed[k0 + k] : make_ulonglong2(0, 0);
         }
-        const ulonglong2 d = EPI == 2 ? ed[k] : make_ulonglong2(0, 0);
-        eo[k] = make_ulonglong2(epi_word(EPI, xs.x, own[pad(16 * u + 2 * k)], d.x, sc, scs, p),
-                                epi_word(EPI, xs.y, own[pad(16 * u + 2 * k + 1)], d.y, sc, scs, p));
+        for (int j = 1; j < a.xnum; ++j) {
+#pragma unroll
+            for (int k = 0; k < G; ++k) {
+                const ulonglong2 t = ex[k0 + k + (size_t)j * xs2];
+                xs[k] = make_ulonglong2(add_mod(xs[k].x, t.x, p), add_mod(xs[k].y, t.y, p));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            const int kk = k0 + k;
+            eo[kk] = make_ulonglong2(epi_word(EPI, xs[k].x, own[pad(16 * u + 2 * kk)], d[k].x, sc, scs, p),
+                                     epi_word(EPI, xs[k].y, own[pad(16 * u + 2 * kk + 1)], d[k].y, sc, scs, p));
+        }
     }
 }
 
@@ -356,10 +387,10 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
     const Mod<F> md = mod_of<LOGN, F>(p, a.iw, ri.pid);
     const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);
     const uint64_t* iws = (const uint64_t*)a.iws + ((size_t)ri.pid << LOGN);
-    const double2* pk = nullptr;
+    const double* twist = nullptr;
     if constexpr (F) {
-        pk = (const double2*)a.iw + (size_t)ri.pid * Pack<LOGN>::SIZE;
-        sw[tw_slot(threadIdx.x)] = pk[Pack<LOGN>::ROW + threadIdx.x];
+        sw[tw_slot(threadIdx.x)] = pack_pairs<LOGN>(a.iw, ri.pid)[Pack<LOGN>::ROW + threadIdx.x];
+        twist = pack_twist<LOGN>(a.iw, ri.pid);
     }
     const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
     const int b = blockIdx.x * 16 + lb;
@@ -411,8 +442,8 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_ROWS_BLOCKS_F : NTT_MIN_BLOCK
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
         if constexpr (F) {  // the inverse twist gamma_b^-k of word u + 16 k
-            const double2 t = __ldg(pk + Pack<LOGN>::TWIST + (size_t)b * 256 + u + 16 * k);
-            x[k] = mul_f(x[k], t.x, t.y, md.p);
+            const double t = __ldg(twist + (size_t)b * 256 + u + 16 * k);
+            x[k] = mul_f(x[k], t, __dmul_rn(t, md.pinv), md.p);
         }
         store_mid<F>(blk + u + 16 * k, x[k]);
     }
@@ -432,7 +463,7 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     const int cc = threadIdx.x % COLS, g = threadIdx.x / COLS;
     const int col = blockIdx.x * COLS + cc;
     if constexpr (F) {
-        const double2* pk = (const double2*)a.iw + (size_t)ri.pid * Pack<LOGN>::SIZE;
+        const double2* pk = pack_pairs<LOGN>(a.iw, ri.pid);
         for (int t = threadIdx.x; t < R; t += THREADS) stw[t] = pk[t];
     } else {
         const uint64_t* iw = (const uint64_t*)a.iw + ((size_t)ri.pid << LOGN);

@@ -1,132 +1,137 @@
-// Key inner products with the switching key's `a` regenerated in the kernel (the reference's Regen key source): the
-// key is stored as `b` and an 8-word seed, half the bytes of a dense key, and `a` comes back from the frozen u64
-// expander lane (chacha.cuh) for (seed, digit, the row's prime). Semantics of crates/pc-kernels/kernels/args.cuh
-// (KsRegenArgs :285-304, KeyTab :273-283, KsKeyArgs :764-768) and crates/pc-kernels/kernels/ks.cuh (ks_dot_regen
-// :130-215, ks_dot_key :218-300).
+// The launcher-table entries whose switching keys come with `a` regenerated in the kernel: ks_dot_regen (the
+// relinearization inner product, with its fused ModDown epilogue) and ks_dot_key (ks_dot over keys read through a
+// key table). Semantics: crates/pc-kernels/kernels/args.cuh (KsRegenArgs :285-304, EpiArgs :258-271, KeyTab
+// :273-283, KsKeyArgs :764-768); any prime below 2^62.
 //
-// Each thread owns 4 consecutive slots of one row: per digit it computes the ChaCha block of its 8-slot group and
-// keeps its half, loads `b` and the K ciphertexts' digit words 16 bytes at a time, and sums the products in 128 bits
-// with one reduction at the end, so the outputs are the canonical residues of the exact sums (any prime below 2^62).
-#include "chacha.cuh"
+// Design (shared with the evaluator's FP64 inner products, keyregen.cuh): a CTA owns a tile of 2 BX consecutive slots
+// of one row. For each key it first regenerates that key's `a` over the tile for every regenerated digit into shared
+// memory — whole ChaCha12 blocks of 8 slots spread over the CTA's threads — and then each thread takes two adjacent
+// slots (16-byte loads of the ciphertexts' digit words) and walks the ciphertexts one at a time: 128-bit sums of the
+// digit products for its two slots, one reduction each, the epilogue or the scattered store. The key's `b` words are
+// re-read per ciphertext from L1 (the tile's rows are a few KB), so only four accumulators are live per thread.
+#include "keyregen.cuh"
 #include "kernels.h"
 
 namespace pcb {
 namespace regen {
 
 constexpr int BX = 128;
+constexpr int TILE = 2 * BX;                     // slots per CTA
+constexpr int NSEG = TILE / keyregen::SEG;       // staged segments per digit
+constexpr int MAX_DIG = 16;
 
-struct W4 {
-    uint64_t v[4];
-};
-__device__ __forceinline__ W4 ld4(const uint64_t* p) {
-    const ulonglong2 a = __ldg((const ulonglong2*)p), b = __ldg((const ulonglong2*)p + 1);
-    return W4{{a.x, a.y, b.x, b.y}};
-}
-// key rows reached through device pointer tables, whose alignment the host cannot check: 16-byte loads when the row
-// start allows them, else 8-byte ones
-__device__ __forceinline__ W4 ld4k(const uint64_t* p) {
-    if (((uintptr_t)p & 15) == 0) return ld4(p);
-    return W4{{__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3)}};
-}
-__device__ __forceinline__ void st4(uint64_t* p, const uint64_t (&r)[4]) {
-    ((ulonglong2*)p)[0] = make_ulonglong2(r[0], r[1]);
-    ((ulonglong2*)p)[1] = make_ulonglong2(r[2], r[3]);
+// two adjacent words at p: one 16-byte load when p allows it (key rows reached through device pointer tables, whose
+// alignment the host cannot check), else two 8-byte loads
+__device__ __forceinline__ ulonglong2 ld2(const uint64_t* p) {
+    if (((uintptr_t)p & 15) == 0) return __ldg((const ulonglong2*)p);
+    return make_ulonglong2(__ldg(p), __ldg(p + 1));
 }
 
-// the key's slot of prime id t: Q ids at their index up to q_top, special ids after them; q_top < 0: the prime id
-__device__ __forceinline__ int slot_of(const PcbKeyTab& T, int t, int nq) {
+// the key-table slot of prime id t: Q ids at their index up to q_top, special ids right after; q_top < 0: prime id
+__device__ __forceinline__ int key_slot(const PcbKeyTab& T, int t, int nq) {
     return (t < nq || T.q_top < 0) ? t : T.q_top + 1 + (t - nq);
 }
 
+// Where a key's words of one row live: `b` at bsrc + d bstride, dense `a` (digits >= nreg) at asrc + d astride,
+// regenerated `a` (digits < nreg) from seed.
+struct KeyRow {
+    const uint64_t* bsrc;
+    size_t bstride;
+    const uint64_t* asrc;
+    size_t astride;
+    const uint32_t* seed;
+    int nreg;
+};
+
+// sums over the digits of ciphertext c at slots (i, i + 1) of row t: s0 = sum x_d b_d, s1 = sum x_d a_d
+__device__ __forceinline__ void digit_sums(const PcbKsArgs& A, const KeyRow& K, const uint64_t* sm, int c, int dt,
+                                           size_t roff, uint32_t tslot, Acc (&s0)[2], Acc (&s1)[2]) {
+    const uint64_t* c1 = (const uint64_t*)A.c1;
+    const uint64_t* mu = (const uint64_t*)A.modup;
+    s0[0] = s0[1] = s1[0] = s1[1] = Acc{0, 0};
+    for (int d = 0; d < A.ndig; ++d) {
+        const ulonglong2 x = __ldg((const ulonglong2*)(d == dt ? c1 + (size_t)c * A.ct_stride + roff
+                                                               : mu + (size_t)c * A.mu_ct_stride +
+                                                                     (size_t)d * A.mu_digit_stride + roff));
+        const ulonglong2 b = ld2(K.bsrc + (size_t)d * K.bstride);
+        const ulonglong2 a = d < K.nreg ? *(const ulonglong2*)&sm[(size_t)d * TILE + tslot]
+                                        : ld2(K.asrc + (size_t)d * K.astride);
+        mac(s0[0], x.x, b.x);
+        mac(s0[1], x.y, b.y);
+        mac(s1[0], x.x, a.x);
+        mac(s1[1], x.y, a.y);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ ks_dot_regen
-// TAB: the `b` rows come from key 0 of G.key (dense rows in the key's slot order) instead of ks.kb[0]
-template <int LOGN, int KMAX, bool EPI, bool TAB>
+// TAB: `b` from key 0 of G.key (dense rows in the key's slot order, row_words apart), else ks.kb[0] (prime-id rows)
+template <int LOGN, bool EPI, bool TAB>
 __global__ void __launch_bounds__(BX) ks_dot_regen(PcbKsRegenArgs G) {
+    extern __shared__ __align__(16) uint64_t sm[];
     const PcbKsArgs& A = G.ks;
     const uint32_t t = A.rows[blockIdx.y];
     const PcbPrimeConst& pc = A.pr[t];
     const uint64_t p = pc.p;
-    const uint32_t gtid = blockIdx.x * BX + threadIdx.x;
-    const uint32_t base = gtid * 4;
+    const uint32_t tile0 = blockIdx.x * TILE, tslot = 2 * threadIdx.x, i = tile0 + tslot;
+    const size_t roff = ((size_t)t << LOGN) + i;
     const int dt = (int)t < A.nq ? A.digit_of[t] : -1;
-    const size_t roff = ((size_t)t << LOGN) + base;
-    const uint64_t* c1 = (const uint64_t*)A.c1;
-    const uint64_t* mu = (const uint64_t*)A.modup;
-    const uint64_t* kb;
-    size_t brow0, bstride;  // word offset of digit 0's row (from the row base) and the digits' stride
+    KeyRow K;
     if constexpr (TAB) {
-        kb = (const uint64_t*)G.key.kb[0];
-        brow0 = (size_t)slot_of(G.key, (int)t, A.nq) * G.key.row_words;
-        bstride = (size_t)G.key.srows * G.key.row_words;
+        K.bsrc = (const uint64_t*)G.key.kb[0] + (size_t)key_slot(G.key, (int)t, A.nq) * G.key.row_words + i;
+        K.bstride = (size_t)G.key.srows * G.key.row_words;
     } else {
-        kb = (const uint64_t*)A.kb[0];
-        brow0 = (size_t)t << LOGN;
-        bstride = A.key_digit_stride;
+        K.bsrc = (const uint64_t*)A.kb[0] + roff;
+        K.bstride = A.key_digit_stride;
     }
-    Acc s0[KMAX][4], s1[KMAX][4];
-#pragma unroll
-    for (int c = 0; c < KMAX; ++c)
-#pragma unroll
-        for (int w = 0; w < 4; ++w) s0[c][w] = s1[c][w] = Acc{0, 0};
-    for (int d = 0; d < A.ndig; ++d) {
-        uint64_t a4[4];
-        keys::expand4<LOGN>(G.seed, gtid >> 1, gtid & 1, (uint32_t)d, keys::TAG_KSKA, pc, a4);
-        const W4 b4 = ld4k(kb + brow0 + (size_t)d * bstride + base);
-#pragma unroll
-        for (int c = 0; c < KMAX; ++c) {
-            if (c < A.K) {
-                const W4 x4 = d == dt ? ld4(c1 + (size_t)c * A.ct_stride + roff)
-                                      : ld4(mu + (size_t)c * A.mu_ct_stride + (size_t)d * A.mu_digit_stride + roff);
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    mac(s0[c][w], x4.v[w], b4.v[w]);
-                    mac(s1[c][w], x4.v[w], a4[w]);
-                }
-            }
+    K.asrc = nullptr;
+    K.astride = 0;
+    K.seed = G.seed;
+    K.nreg = A.ndig;
+    keyregen::stage<LOGN>(&K.seed, 1, A.ndig, NSEG,
+                          [tile0](int, int j) { return tile0 + (uint32_t)j * keyregen::SEG; }, pc, sm);
+    const PcbEpiArgs& E = G.epi;
+    uint64_t bi = 0, bis = 0, kk = 0, al = 0, als = 0;
+    if constexpr (EPI) {
+        bi = ((const uint64_t*)E.binv)[t];
+        bis = ((const uint64_t*)E.binvs)[t];
+        if (E.k) {
+            const uint64_t kv = ((const uint64_t*)E.k)[t];
+            kk = kv >= p ? kv - p : kv;
+        }
+        if (E.alpha) {
+            al = ((const uint64_t*)E.alpha)[t];
+            als = ((const uint64_t*)E.alphas)[t];
         }
     }
-    const PcbEpiArgs& E = G.epi;
+    for (int c = 0; c < A.K; ++c) {
+        Acc s0[2], s1[2];
+        digit_sums(A, K, sm, c, dt, roff, tslot, s0, s1);
+        const uint64_t r[2][2] = {{reduce(s0[0], pc), reduce(s0[1], pc)}, {reduce(s1[0], pc), reduce(s1[1], pc)}};
+        const size_t ob = (size_t)c * A.out_ct_stride + ((size_t)t << LOGN) + i;
+        if constexpr (EPI) {
+            // dst = f (alpha dst + (dot - conv) binv) [+ k on part 0] [+ add], f = 2 when dbl
+            for (int part = 0; part < 2; ++part) {
+                const size_t o = ob + (size_t)part * E.part_stride;
+                uint64_t* dp = (uint64_t*)E.dst + o;
+                const ulonglong2 cv = __ldg((const ulonglong2*)((const uint64_t*)E.conv + o));
+                const ulonglong2 dv = *(const ulonglong2*)dp;
+                ulonglong2 av = make_ulonglong2(0, 0);
+                if (G.add) av = __ldg((const ulonglong2*)((const uint64_t*)G.add + o));
+                const uint64_t cw[2] = {cv.x, cv.y}, dw[2] = {dv.x, dv.y}, aw[2] = {av.x, av.y};
+                uint64_t v[2];
 #pragma unroll
-    for (int c = 0; c < KMAX; ++c) {
-        if (c < A.K) {
-            uint64_t r0[4], r1[4];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                r0[w] = reduce(s0[c][w], pc);
-                r1[w] = reduce(s1[c][w], pc);
-            }
-            const size_t ob = (size_t)c * A.out_ct_stride + ((size_t)t << LOGN) + base;
-            if constexpr (EPI) {
-                // dst = f (alpha dst + (dot - conv) binv) [+ k on part 0] [+ add] (args.cuh:258-271, :285-304)
-                const uint64_t bi = ((const uint64_t*)E.binv)[t], bis = ((const uint64_t*)E.binvs)[t];
-                const uint64_t* kp = (const uint64_t*)E.k;
-                const uint64_t kk = kp ? (kp[t] >= p ? kp[t] - p : kp[t]) : 0;
-                const uint64_t* al = (const uint64_t*)E.alpha;
-                const uint64_t ai = al ? al[t] : 0, ais = al ? ((const uint64_t*)E.alphas)[t] : 0;
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    uint64_t* dp = (uint64_t*)E.dst + ob + part * E.part_stride;
-                    const W4 cv = ld4((const uint64_t*)E.conv + ob + part * E.part_stride);
-                    const W4 dv = ld4(dp);
-                    W4 av{};
-                    if (G.add) av = ld4((const uint64_t*)G.add + ob + part * E.part_stride);
-                    uint64_t r[4];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        const uint64_t x = part ? r1[w] : r0[w];
-                        const uint64_t dd = al ? shoup(dv.v[w], ai, ais, p) : dv.v[w];
-                        uint64_t v = add_mod(dd, shoup(sub_mod(x, cv.v[w], p), bi, bis, p), p);
-                        if (E.dbl) v = add_mod(v, v, p);
-                        if (part == 0) v = add_mod(v, kk, p);
-                        if (G.add) v = add_mod(v, av.v[w], p);
-                        r[w] = v;
-                    }
-                    st4(dp, r);
+                for (int h = 0; h < 2; ++h) {
+                    const uint64_t base = E.alpha ? shoup(dw[h], al, als, p) : dw[h];
+                    v[h] = add_mod(base, shoup(sub_mod(r[part][h], cw[h], p), bi, bis, p), p);
+                    if (E.dbl) v[h] = add_mod(v[h], v[h], p);
+                    if (part == 0) v[h] = add_mod(v[h], kk, p);
+                    if (G.add) v[h] = add_mod(v[h], aw[h], p);
                 }
-            } else {
-                st4((uint64_t*)A.out0 + ob, r0);
-                st4((uint64_t*)A.out1 + ob, r1);
+                *(ulonglong2*)dp = make_ulonglong2(v[0], v[1]);
             }
+        } else {
+            *(ulonglong2*)((uint64_t*)A.out0 + ob) = make_ulonglong2(r[0][0], r[0][1]);
+            *(ulonglong2*)((uint64_t*)A.out1 + ob) = make_ulonglong2(r[1][0], r[1][1]);
         }
     }
 }
@@ -135,12 +140,8 @@ __host__ inline bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 template <int LOGN, bool EPI, bool TAB>
 void regen_go(const PcbKsRegenArgs& a, cudaStream_t s) {
-    const dim3 g((1 << LOGN) / (4 * BX), a.ks.nrows);
-    switch (a.ks.K) {
-        case 1: ks_dot_regen<LOGN, 1, EPI, TAB><<<g, BX, 0, s>>>(a); break;
-        case 2: ks_dot_regen<LOGN, 2, EPI, TAB><<<g, BX, 0, s>>>(a); break;
-        default: ks_dot_regen<LOGN, 4, EPI, TAB><<<g, BX, 0, s>>>(a);
-    }
+    const dim3 g((1 << LOGN) / TILE, a.ks.nrows);
+    ks_dot_regen<LOGN, EPI, TAB><<<g, BX, (size_t)a.ks.ndig * TILE * sizeof(uint64_t), s>>>(a);
 }
 
 template <int LOGN>
@@ -149,11 +150,12 @@ int ks_dot_regen_launch(const PcbKsRegenArgs* ap, cudaStream_t s) {
     const PcbKsRegenArgs& a = *ap;
     const PcbKsArgs& k = a.ks;
     const bool tab = a.key.kb != nullptr;
-    if (k.K < 0 || k.K > 4 || k.ndig < 1 || k.ndig > 16 || k.nrows < 0 || !k.c1 || !k.rows || !k.digit_of || !k.pr ||
-        !a.seed || (k.ndig > 1 && !k.modup))
+    if (k.K < 0 || k.K > 4 || k.ndig < 1 || k.ndig > MAX_DIG || k.nrows < 0 || !k.c1 || !k.rows || !k.digit_of ||
+        !k.pr || !a.seed || (k.ndig > 1 && !k.modup))
         return PCB_BAD_ARGS;
     // key.kb / ks.kb are device arrays of device pointers: only the table pointers themselves are checked here
     if (tab ? (a.key.bits != 0 || a.key.srows < 1) : !k.kb) return PCB_BAD_ARGS;
+    if (a.add && !a.use_epi) return PCB_BAD_ARGS;
     if (a.use_epi ? (!a.epi.dst || !a.epi.conv || !a.epi.binv || !a.epi.binvs || (a.epi.alpha && !a.epi.alphas) ||
                      !al16(a.epi.dst) || !al16(a.epi.conv) || (a.epi.part_stride & 1) || (a.add && !al16(a.add)))
                   : (!k.out0 || !k.out1 || !al16(k.out0) || !al16(k.out1)))
@@ -168,80 +170,61 @@ int ks_dot_regen_launch(const PcbKsRegenArgs* ap, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ ks_dot_key
-template <int LOGN, int KMAX>
+// ks_dot over R keys read through the key table: key r's `a` regenerated from T.seed[r] for digits below T.nregen
+// (staged per key; the CTA re-stages between keys), dense ks.ka[r] rows for the others; outputs scattered to
+// automorph_slot(autok[r], i) with the c0 modes and accumulation of ks_dot.
+template <int LOGN>
 __global__ void __launch_bounds__(BX) ks_dot_key(PcbKsKeyArgs G) {
+    extern __shared__ __align__(16) uint64_t sm[];
     const PcbKsArgs& A = G.ks;
     const PcbKeyTab& T = G.key;
     const uint32_t t = A.rows[blockIdx.y];
     const PcbPrimeConst& pc = A.pr[t];
     const uint64_t p = pc.p;
-    const uint32_t gtid = blockIdx.x * BX + threadIdx.x;
-    const uint32_t base = gtid * 4;
+    const uint32_t tile0 = blockIdx.x * TILE, tslot = 2 * threadIdx.x, i = tile0 + tslot;
+    const size_t roff = ((size_t)t << LOGN) + i;
     const int dt = (int)t < A.nq ? A.digit_of[t] : -1;
-    const size_t roff = ((size_t)t << LOGN) + base;
-    const uint64_t* c1 = (const uint64_t*)A.c1;
-    const uint64_t* mu = (const uint64_t*)A.modup;
+    const int nreg = T.nregen < A.ndig ? T.nregen : A.ndig;
     const uint64_t* c0 = (const uint64_t*)A.c0;
-    const size_t brow0 = (size_t)slot_of(T, (int)t, A.nq) * T.row_words, bstride = (size_t)T.srows * T.row_words;
+    const int mode = A.c0_mode & 3;
     uint64_t pm = 0, pms = 0;
-    if ((A.c0_mode & 3) == 1 && (int)t < A.nq) {
+    if (mode == 1 && (int)t < A.nq) {
         pm = ((const uint64_t*)A.pmod)[t];
         pms = ((const uint64_t*)A.pmods)[t];
     }
+    const size_t brow = (size_t)key_slot(T, (int)t, A.nq) * T.row_words + i;
     for (int r = 0; r < A.R; ++r) {
-        Acc s0[KMAX][4], s1[KMAX][4];
-#pragma unroll
-        for (int c = 0; c < KMAX; ++c)
-#pragma unroll
-            for (int w = 0; w < 4; ++w) s0[c][w] = s1[c][w] = Acc{0, 0};
-        const uint64_t* kb = (const uint64_t*)T.kb[r];
-        for (int d = 0; d < A.ndig; ++d) {
-            uint64_t a4[4];
-            if (d < T.nregen) {
-                keys::expand4<LOGN>(T.seed[r], gtid >> 1, gtid & 1, (uint32_t)d, keys::TAG_KSKA, pc, a4);
-            } else {  // the resident dense `a` (prime-id rows)
-                const W4 av = ld4k((const uint64_t*)A.ka[r] + (size_t)d * A.key_digit_stride + roff);
-#pragma unroll
-                for (int w = 0; w < 4; ++w) a4[w] = av.v[w];
-            }
-            const W4 b4 = ld4k(kb + brow0 + (size_t)d * bstride + base);
-#pragma unroll
-            for (int c = 0; c < KMAX; ++c) {
-                if (c < A.K) {
-                    const W4 x4 = d == dt ? ld4(c1 + (size_t)c * A.ct_stride + roff)
-                                          : ld4(mu + (size_t)c * A.mu_ct_stride + (size_t)d * A.mu_digit_stride + roff);
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        mac(s0[c][w], x4.v[w], b4.v[w]);
-                        mac(s1[c][w], x4.v[w], a4[w]);
-                    }
-                }
-            }
-        }
+        KeyRow K;
+        K.bsrc = (const uint64_t*)T.kb[r] + brow;
+        K.bstride = (size_t)T.srows * T.row_words;
+        K.asrc = nreg < A.ndig ? (const uint64_t*)A.ka[r] + roff : nullptr;
+        K.astride = A.key_digit_stride;
+        K.seed = T.seed[r];
+        K.nreg = nreg;
+        if (r > 0) __syncthreads();  // every thread is done with the previous key's staged words
+        if (nreg > 0)
+            keyregen::stage<LOGN>(&K.seed, 1, nreg, NSEG,
+                                  [tile0](int, int j) { return tile0 + (uint32_t)j * keyregen::SEG; }, pc, sm);
         const uint32_t k = A.autok[r];
+        const uint32_t o[2] = {k == 1 ? i : automorph_slot<LOGN>(k, i), k == 1 ? i + 1 : automorph_slot<LOGN>(k, i + 1)};
+        for (int c = 0; c < A.K; ++c) {
+            Acc s0[2], s1[2];
+            digit_sums(A, K, sm, c, dt, roff, tslot, s0, s1);
+            ulonglong2 cv = make_ulonglong2(0, 0);
+            if (mode) cv = __ldg((const ulonglong2*)(c0 + (size_t)c * A.ct_stride + roff));
+            const uint64_t cw[2] = {cv.x, cv.y};
 #pragma unroll
-        for (int c = 0; c < KMAX; ++c) {
-            if (c < A.K) {
-                W4 c04{};
-                if (A.c0_mode & 3) c04 = ld4(c0 + (size_t)c * A.ct_stride + roff);
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    uint64_t r0 = reduce(s0[c][w], pc), r1 = reduce(s1[c][w], pc);
-                    if ((A.c0_mode & 3) == 1) {
-                        if ((int)t < A.nq) r0 = add_mod(r0, shoup(c04.v[w], pm, pms, p), p);
-                    } else if ((A.c0_mode & 3) == 2) {
-                        r0 = add_mod(r0, c04.v[w], p);
-                    }
-                    const uint32_t i = base + w;
-                    const uint32_t o = k == 1 ? i : automorph_slot<LOGN>(k, i);
-                    const size_t ob = (size_t)c * A.out_ct_stride + (size_t)r * A.out_rot_stride + ((size_t)t << LOGN) + o;
-                    if (A.c0_mode & PCB_KS_ACC) {
-                        r0 = add_mod(r0, ((const uint64_t*)A.out0)[ob], p);
-                        r1 = add_mod(r1, ((const uint64_t*)A.out1)[ob], p);
-                    }
-                    ((uint64_t*)A.out0)[ob] = r0;
-                    ((uint64_t*)A.out1)[ob] = r1;
+            for (int h = 0; h < 2; ++h) {
+                uint64_t r0 = reduce(s0[h], pc), r1 = reduce(s1[h], pc);
+                if (mode == 1 && (int)t < A.nq) r0 = add_mod(r0, shoup(cw[h], pm, pms, p), p);
+                else if (mode == 2) r0 = add_mod(r0, cw[h], p);
+                const size_t ob = (size_t)c * A.out_ct_stride + (size_t)r * A.out_rot_stride + ((size_t)t << LOGN) + o[h];
+                if (A.c0_mode & PCB_KS_ACC) {
+                    r0 = add_mod(r0, ((const uint64_t*)A.out0)[ob], p);
+                    r1 = add_mod(r1, ((const uint64_t*)A.out1)[ob], p);
                 }
+                ((uint64_t*)A.out0)[ob] = r0;
+                ((uint64_t*)A.out1)[ob] = r1;
             }
         }
     }
@@ -253,7 +236,7 @@ int ks_dot_key_launch(const PcbKsKeyArgs* ap, cudaStream_t s) {
     const PcbKsKeyArgs& a = *ap;
     const PcbKsArgs& k = a.ks;
     const PcbKeyTab& T = a.key;
-    if (k.K < 0 || k.K > 4 || k.R < 0 || k.ndig < 1 || k.ndig > 16 || k.nrows < 0 || (k.c0_mode & 3) == 3 ||
+    if (k.K < 0 || k.K > 4 || k.R < 0 || k.ndig < 1 || k.ndig > MAX_DIG || k.nrows < 0 || (k.c0_mode & 3) == 3 ||
         (k.c0_mode & ~(3 | PCB_KS_ACC)) || !k.c1 || !k.out0 || !k.out1 || !k.autok || !k.rows || !k.digit_of || !k.pr ||
         (k.ndig > 1 && !k.modup))
         return PCB_BAD_ARGS;
@@ -265,12 +248,9 @@ int ks_dot_key_launch(const PcbKsKeyArgs* ap, cudaStream_t s) {
         (k.mu_ct_stride & 1) || (k.mu_digit_stride & 1))
         return PCB_BAD_ARGS;
     if (k.K == 0 || k.R == 0 || k.nrows == 0) return 0;
-    const dim3 g((1 << LOGN) / (4 * BX), k.nrows);
-    switch (k.K) {
-        case 1: ks_dot_key<LOGN, 1><<<g, BX, 0, s>>>(a); break;
-        case 2: ks_dot_key<LOGN, 2><<<g, BX, 0, s>>>(a); break;
-        default: ks_dot_key<LOGN, 4><<<g, BX, 0, s>>>(a);
-    }
+    const int nreg = T.nregen < k.ndig ? T.nregen : k.ndig;
+    const dim3 g((1 << LOGN) / TILE, k.nrows);
+    ks_dot_key<LOGN><<<g, BX, (size_t)(nreg > 0 ? nreg : 1) * TILE * sizeof(uint64_t), s>>>(a);
     return PCB_LAUNCH_RESULT();
 }
 

@@ -140,10 +140,16 @@ class Diagonals:
             [j * self.bstep * self.stride for j in range(1, self.gstep)]
 
 
+# How a session stores its switching keys (the reference's KeySource, crates/pc-gpu/src/ks.rs:57): "dense" keeps b
+# and a resident (Cached); "regen" keeps b and the seed of a, which the inner-product kernels regenerate (Regen, half
+# the key bytes). Both give the same keys and the same results word for word.
+KEY_SOURCES = {"dense": 0, "regen": 1}
+
+
 class Session:
     """A context over one chain with device-resident keys (relinearization + the given rotation steps)."""
 
-    def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None):
+    def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None, key_source="dense"):
         self.chain = chain
         self.device = torch.device(device or "cuda")
         self.n, self.log_n = chain.n, chain.log_n
@@ -157,8 +163,11 @@ class Session:
         self.galois = gal
         self._q = (C.c_uint64 * self.nq)(*chain.q)
         self._p = (C.c_uint64 * self.kp)(*chain.p)
+        if key_source not in KEY_SOURCES:
+            raise ValueError(f"key_source {key_source!r}: one of {sorted(KEY_SOURCES)}")
+        self.key_source = key_source
         self.params = L.Params(chain.log_n, self.nq, self.kp, chain.dnum,
-                               C.cast(self._q, L.u64p), C.cast(self._p, L.u64p), k_max, 0)
+                               C.cast(self._q, L.u64p), C.cast(self._p, L.u64p), k_max, KEY_SOURCES[key_source])
         lib = L.lib()
         nbytes = lib.pcb_ctx_bytes(C.byref(self.params), len(gal))
         if nbytes < 0:

@@ -109,6 +109,21 @@ def test_ctx_bytes_config2():
     assert 5 < gib < 40, gib  # workspaces for 64 ciphertexts + 16 keys fit one B200 many times over
 
 
+def test_ctx_bytes_regenerated_keys():
+    """PCB_KEYS_REGEN keeps b and a seed per key: the arena shrinks by every key's `a` rows; other sources refused."""
+    ch = fhe.config2_chain()
+    q = (C.c_uint64 * 24)(*ch.q)
+    p = (C.c_uint64 * 8)(*ch.p)
+    dense = L.Params(16, 24, 8, 3, C.cast(q, L.u64p), C.cast(p, L.u64p), 4, fhe.KEY_SOURCES["dense"])
+    regen = L.Params(16, 24, 8, 3, C.cast(q, L.u64p), C.cast(p, L.u64p), 4, fhe.KEY_SOURCES["regen"])
+    nd, nr = L.lib().pcb_ctx_bytes(C.byref(dense), 16), L.lib().pcb_ctx_bytes(C.byref(regen), 16)
+    a_rows = 16 * 3 * 32 * (1 << 16) * 8
+    assert 0 < nr and nd - nr == a_rows, (nd, nr)
+    bad = L.Params(16, 24, 8, 3, C.cast(q, L.u64p), C.cast(p, L.u64p), 4, 7)
+    assert L.lib().pcb_ctx_bytes(C.byref(bad), 1) < 0
+    assert "key_source" in L.lib().pcb_last_error().decode()
+
+
 def test_ctx_bytes_rejects_bad_chains():
     q = (C.c_uint64 * 2)(97, 193)
     p = (C.c_uint64 * 1)(257)

@@ -6,7 +6,8 @@
 
 1. Launchers. Every entry that both tables implement runs on the same inputs and arguments (fresh copies for each
    table) and must write the same words: the NTT (both directions, every epilogue, out-of-place and summed sources,
-   per-row inverse scales), base conversion, the key inner product (c0 modes, accumulation, automorphism), tensor,
+   per-row inverse scales), base conversion, the key inner products (c0 modes, accumulation, automorphism; with
+   `a` regenerated from a seed, key tables, the fused relinearization epilogue), tensor,
    ModDown epilogue, rescale (one and two dropped primes), automorphism, the element-wise and plaintext-operand
    entries, key expansion, key generation and encryption; rows mix 50-bit and 60-bit primes.
 2. Compositions. The reference's launchers run in its device runtime's order — ModUp (INTT with the digit pre factor,
@@ -375,6 +376,108 @@ def test_ks_dot(env, K, R, c0_mode, autok):
         return a, [out0, out1], keep
 
     same(run_both("ks_dot", mk))
+
+
+@pytest.mark.parametrize("K,tab,epi", [(1, False, False), (3, True, False), (4, False, True), (2, True, True)])
+def test_ks_dot_regen(env, K, tab, epi):
+    """The relinearization inner product with `a` regenerated from the seed: dense or key-table `b`, plain outputs or
+    the fused epilogue (alpha, dbl, k, add)."""
+    rng = np.random.default_rng(140 + K)
+    nq, ndig = 8, 3
+    digit_of = np.array([t // 3 for t in range(nq)] + [-1] * (env.R - nq), np.int32)
+    rows = list(range(6)) + [8, 10, 11]
+    seed = rng.integers(0, 1 << 32, 8, dtype=np.uint64).astype(np.uint32)
+    c1 = env.cts(rng, K)[:, 1]
+    mu = env.rows(rng, range(env.R), lead=(K, ndig))
+    b = env.rows(rng, range(env.R), lead=(ndig,))
+    q_top, srows = 5, 6 + 4
+    bt = np.concatenate([b[:, :6], b[:, 8:12]], 1)  # key table: Q ids 0..5 at their slot, specials after
+    dst, conv, add = env.cts(rng, K), env.cts(rng, K), env.cts(rng, K)
+    vals = [np.array([rng.integers(1, p) for p in env.primes], np.uint64) for _ in range(3)]
+    binv, alpha, kc = vals
+    sh = [np.array([shoup(v, p) for v, p in zip(arr, env.primes)], np.uint64) for arr in (binv, alpha)]
+
+    def mk():
+        keep = [dev(c1), dev(mu), dev(b), dev(bt), torch.tensor(rows, dtype=torch.int32, device="cuda"),
+                torch.tensor(digit_of, dtype=torch.int32, device="cuda"),
+                torch.from_numpy(seed.view(np.int32).copy()).cuda()]
+        c1d, mud, bd, btd, rd, dd, sd = keep
+        kb = dev(np.array([bd.data_ptr()], np.uint64))
+        kt = dev(np.array([btd.data_ptr()], np.uint64))
+        extra = [dev(binv), dev(sh[0]), dev(alpha), dev(sh[1]), dev(kc), dev(conv), dev(add)]
+        keep += [kb, kt] + extra
+        out0 = torch.zeros((K, env.R, N), dtype=torch.int64, device="cuda")
+        out1 = torch.zeros_like(out0)
+        dd_ = dev(dst)
+        a = L.KsRegenArgs()
+        k = a.ks
+        k.c1, k.modup, k.pr, k.rows, k.digit_of = c1d.data_ptr(), mud.data_ptr(), env.pc.data_ptr(), rd.data_ptr(), \
+            dd.data_ptr()
+        k.ct_stride, k.mu_ct_stride, k.mu_digit_stride = env.R * N, ndig * env.R * N, env.R * N
+        k.key_digit_stride = env.R * N
+        k.K, k.R, k.ndig, k.nq, k.nrows = K, 1, ndig, nq, len(rows)
+        a.seed = sd.data_ptr()
+        if tab:
+            a.key.kb, a.key.row_words, a.key.q_top, a.key.srows = kt.data_ptr(), N, q_top, srows
+        else:
+            k.kb = kb.data_ptr()
+        if epi:
+            k.out_ct_stride = 2 * env.R * N
+            a.use_epi, a.add = 1, extra[6].data_ptr()
+            e = a.epi
+            e.dst, e.conv, e.part_stride, e.dbl = dd_.data_ptr(), extra[5].data_ptr(), env.R * N, 1
+            e.binv, e.binvs, e.alpha, e.alphas, e.k = [x.data_ptr() for x in extra[:5]]
+            return a, [dd_], keep
+        k.out_ct_stride = env.R * N
+        k.out0, k.out1 = out0.data_ptr(), out1.data_ptr()
+        return a, [out0, out1], keep
+
+    same(run_both("ks_dot_regen", mk))
+
+
+@pytest.mark.parametrize("K,R,nregen,c0_mode", [(1, 1, 3, 0), (2, 2, 1, 1 | KS_ACC), (4, 3, 2, 2), (3, 1, 0, 1)])
+def test_ks_dot_key(env, K, R, nregen, c0_mode):
+    """ks_dot through a key table: `a` regenerated below nregen, resident above; automorphism, c0 modes, accumulate."""
+    rng = np.random.default_rng(150 + 10 * K + R)
+    nq, ndig = 8, 3
+    digit_of = np.array([t // 3 for t in range(nq)] + [-1] * (env.R - nq), np.int32)
+    rows = list(range(8)) + [8, 9, 10, 11]
+    seeds = [rng.integers(0, 1 << 32, 8, dtype=np.uint64).astype(np.uint32) for _ in range(R)]
+    c1, c0 = env.cts(rng, K)[:, 1], env.cts(rng, K)[:, 0]
+    mu = env.rows(rng, range(env.R), lead=(K, ndig))
+    bs = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(R)]
+    kas = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(R)]
+    gal = [int(fhe.rotation_galois(int(s), LOGN)) for s in rng.integers(1, 1000, R)]
+    o0, o1 = env.rows(rng, range(env.R), lead=(K, R)), env.rows(rng, range(env.R), lead=(K, R))
+    pm = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    pms = np.array([shoup(v, p) for v, p in zip(pm, env.primes)], np.uint64)
+
+    def mk():
+        keep = [dev(c1), dev(c0), dev(mu), dev(pm), dev(pms), torch.tensor(rows, dtype=torch.int32, device="cuda"),
+                torch.tensor(digit_of, dtype=torch.int32, device="cuda"), torch.tensor(gal, dtype=torch.int32,
+                                                                                      device="cuda")]
+        c1d, c0d, mud, pmd, pmsd, rd, dd, gd = keep
+        bds, kads = [dev(x) for x in bs], [dev(x) for x in kas]
+        sds = [torch.from_numpy(x.view(np.int32).copy()).cuda() for x in seeds]
+        kbt = dev(np.array([x.data_ptr() for x in bds], np.uint64))
+        kat = dev(np.array([x.data_ptr() for x in kads], np.uint64))
+        st = dev(np.array([x.data_ptr() for x in sds], np.uint64))
+        keep += bds + kads + sds + [kbt, kat, st]
+        out0, out1 = dev(o0), dev(o1)
+        a = L.KsKeyArgs()
+        k = a.ks
+        k.c1, k.modup, k.c0, k.pr, k.rows, k.digit_of = c1d.data_ptr(), mud.data_ptr(), c0d.data_ptr(), \
+            env.pc.data_ptr(), rd.data_ptr(), dd.data_ptr()
+        k.ka, k.autok, k.pmod, k.pmods = kat.data_ptr(), gd.data_ptr(), pmd.data_ptr(), pmsd.data_ptr()
+        k.out0, k.out1 = out0.data_ptr(), out1.data_ptr()
+        k.ct_stride, k.mu_ct_stride, k.mu_digit_stride = env.R * N, ndig * env.R * N, env.R * N
+        k.out_ct_stride, k.out_rot_stride, k.key_digit_stride = R * env.R * N, env.R * N, env.R * N
+        k.K, k.R, k.ndig, k.c0_mode, k.nq, k.nrows = K, R, ndig, c0_mode, nq, len(rows)
+        a.key.kb, a.key.seed, a.key.row_words, a.key.q_top, a.key.srows, a.key.nregen = kbt.data_ptr(), \
+            st.data_ptr(), N, -1, env.R, nregen
+        return a, [out0, out1], keep
+
+    same(run_both("ks_dot_key", mk))
 
 
 # ------------------------------------------------------------------------------------------------ element-wise

@@ -107,9 +107,21 @@ class Clocks:
 _CPU = {}
 
 
-def cpu_rate(samples):
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo), for the baseline's record."""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_rate(samples, threads=None):
     """Key switches per second of the oracle port (crates/pc-host restated) on this host's cores: `samples` rotation
-    key switches of one config-2 ciphertext. Returns (rate, cores, seconds)."""
+    key switches of one config-2 ciphertext on `threads` threads (default: every host thread). Returns
+    (rate, threads, seconds)."""
     import numpy as np
 
     from perseus_b200 import fhe
@@ -128,6 +140,7 @@ def cpu_rate(samples):
         o.rotate(x, 1, o.nq - 1)  # warm
         _CPU.update(o=o, x=x)
     o, x = _CPU["o"], _CPU["x"]
+    O.lib().orc_set_threads(threads or len(os.sched_getaffinity(0)))
     cores = O.lib().orc_get_threads()
     t0 = time.perf_counter()
     for _ in range(samples):
@@ -309,6 +322,27 @@ def run_ours(a):
         traffic = json.load(open(os.path.join(ROOT, "profiles", "ntt_fwd_traffic.json")))["bytes_per_3072_row_pass"]
     except Exception:
         pass
+    # The key switches of the step against both rooflines, over the whole timed step (it also holds the NTT pass and
+    # the output sum: a lower bound on the key switches' own rates). Bytes: the algorithmic HBM traffic of one hybrid
+    # key switch of one polynomial (c1 and c0 read, both output parts written: 4 L rows) plus the key (2 dnum (L + K)
+    # rows, read once per batch); FP64 operations: every NTT row of the step (ModUp: L INTT + dnum (L + K) - L NTT
+    # rows per ModUp; ModDown: 2 K INTT + 2 L NTT rows), the conversions' exact products (6 operations each: ModUp
+    # dnum x alpha sources x (L + K - alpha) targets, ModDown 2 x K x L per coefficient) and the inner products'
+    # (2 dnum (L + K) per coefficient, 7 operations with the sum). The relinearization has its own ModUp; the 15
+    # rotations share one (hoisted) and each has its own ModDown and inner product.
+    L_, K_, D_ = nq, rows - nq, ch.dnum
+    alpha = -(-L_ // D_)
+    R_ = n * 8
+    real_rot = sum(1 for st in ROT_STEPS if st % (n // 2))
+    ks_step = BATCH * (1 + real_rot)
+    ks_bytes = BATCH * (1 + real_rot) * 4 * L_ * R_ + (1 + real_rot) * 2 * D_ * (L_ + K_) * R_
+    modup_rows, moddown_rows = L_ + (D_ * (L_ + K_) - L_), 2 * K_ + 2 * L_
+    ntt_rows_step = BATCH * (2 * modup_rows + (1 + real_rot) * moddown_rows)
+    conv_macs = BATCH * n * (2 * D_ * alpha * (L_ + K_ - alpha) + (1 + real_rot) * 2 * K_ * L_)
+    kip = BATCH * n * (1 + real_rot) * 2 * D_ * (L_ + K_)
+    ks_fp64 = ntt_rows_step * fp64_ops_row + 6 * conv_macs + 7 * kip
+    ks_gbs = ks_bytes / (ms * 1e-3) / 1e9
+    ks_tops = ks_fp64 / (ms * 1e-3) / 1e12
     # plain (unhoisted) rotations of the same batch, for comparison: one key switch per rotation, ModUp included
     r0, r1 = ev(), ev()
     s.rotate(ct, 1)
@@ -345,6 +379,14 @@ def run_ours(a):
                          "fp64_pipe": {"ops_per_row": fp64_ops_row, "achieved_tops": fp64_tops, "peak_tops": fp64_peak,
                                        "frac": fp64_tops / fp64_peak,
                                        "peak_source": "nominal: 64 FP64 FMA / clock / SM x 148 SMs x 1.965 GHz"}},
+            "keyswitch_roofline": {
+                "kernels": "the step's key switches (ModUp, inner products, ModDown) over the whole step time",
+                "key_switches_per_step": ks_step,
+                "hbm": {"algorithmic_bytes": ks_bytes, "achieved": ks_gbs, "peak": hbm, "unit": "GB/s",
+                        "frac": ks_gbs / hbm},
+                "fp64_pipe": {"ops": ks_fp64, "achieved_tops": ks_tops, "peak_tops": fp64_peak,
+                              "frac": ks_tops / fp64_peak, "floor_ms": ks_fp64 / (fp64_peak * 1e12) * 1e3},
+                "bound": "fp64"},
             "clocks": clk,
             "attn_decode_ms_per_token": attn,
             "attn_decode_max_abs_err_vs_fp64": attn_err,
@@ -359,7 +401,15 @@ def run_ours(a):
                 rate, cores, dt = cpu_rate(ns)
                 line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                                         "sample": f"{ns} rotation key switches of one config-2 ciphertext "
-                                                  f"({dt:.1f} s)"}
+                                                  f"({dt:.1f} s)", "cpu_model": cpu_model()}
+                # pc-host's default pool caps its threads at 36 (crates/pc-hostrt/src/lib.rs:219-226)
+                capped = min(cores, 36)
+                if capped != cores:
+                    r36, _, _ = cpu_rate(max(2, ns * capped // cores), capped)
+                    line["cpu_baseline"]["value_min_cores_36"] = r36
+                else:
+                    line["cpu_baseline"]["value_min_cores_36"] = rate
+                line["cpu_baseline"]["threads_note"] = f"all {cores} host threads; min(cores, 36) = {capped}"
             except Exception as e:  # the baseline is reported, never required
                 line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": None, "kind": "port",
                                         "sample": f"failed: {e}"}

@@ -375,6 +375,10 @@ const PcbRingTable* pc_ring_u64_16(void);
 
 /* Kernels this library has launched since it was loaded (all threads, all devices). */
 uint64_t pcb_launch_count(void);
+/* Bounded waits in this library's pipelined kernels (the NTT's bulk-copy stages) that ran out on the current device
+ * since the library was loaded: 0 in normal operation; a nonzero count means a copy never completed and the affected
+ * rows were left untransformed (synchronizes the device). No counterpart in the reference. */
+uint32_t pcb_device_timeouts(void);
 
 /* ================================================================ 2. evaluator */
 

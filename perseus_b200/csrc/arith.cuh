@@ -159,6 +159,62 @@ __host__ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, c
     cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// launch_pdl with dynamic shared memory
+template <typename... KArgs, typename... Args>
+__host__ inline void launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// ------------------------------------------------------------------------------------------------ bulk copies
+// Asynchronous global -> shared bulk copies (cp.async.bulk, the TMA engine's untiled form; no multicast) completing
+// on a shared-memory mbarrier by transaction bytes. Addresses 16-byte aligned, sizes multiples of 16 bytes.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+// order the barrier initialisation before its use by the async proxy
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// order this thread's earlier generic-proxy accesses to shared memory before a later bulk copy into it
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// one arrival that also expects `bytes` of transactions on the barrier's current phase
+__device__ __forceinline__ void mbar_expect(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of the barrier with an iteration limit (each try_wait blocks for a hardware-bounded time):
+// false when the limit ran out, which the caller reports (the wait never spins forever)
+constexpr uint32_t MBAR_WAIT_LIMIT = 1u << 20;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < MBAR_WAIT_LIMIT; ++it)
+        if (mbar_test(bar, parity)) return true;
+    return false;
+}
+
 // process-wide count of kernels this library launched (pcb_launch_count)
 void note_launches(unsigned n);
 

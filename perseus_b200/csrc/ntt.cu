@@ -522,6 +522,8 @@ __global__ void __launch_bounds__(THREADS, F ? NTT_COLS_BLOCKS_F : NTT_MIN_BLOCK
     }
 }
 
+#include "ntt_pipe.cuh"
+
 // ------------------------------------------------------------------------------------------------ launchers
 // Rows per chunk: both passes of a chunk run back to back so the intermediate state is read back from L2. The count
 // is a whole number of waves (the column pass's CTAs of the chunk fill every SM's NTT_MIN_BLOCKS slots exactly, so
@@ -566,6 +568,31 @@ __host__ void launch_rows(const PcbNttArgs& a, dim3 grid, cudaStream_t s, int r0
     }
 }
 
+// The pipelined FP64 inverse row pass (ntt_pipe.cuh): N = 2^16, the source read from at most one row, bulk copies
+// starting on 16-byte boundaries (the row bases, and the out-of-place source when there is one)
+template <int LOGN>
+__host__ bool pipelined(const PcbNttArgs& a, bool f64) {
+    return f64 && LOGN == 16 && !misaligned(a.base) && (a.soff == nullptr || (a.snum <= 1 && !misaligned(a.src)));
+}
+
+// Their dynamic shared memory exceeds the default 48 KiB: raised once per kernel and device (on the first launch,
+// which should come before any stream capture); a persistent grid of PIPE_CTAS_PER_SM CTAs per SM, at most one per tile
+template <auto KERN>
+__host__ int pipe_grid(int tiles) {
+    constexpr int MAXDEV = 64;
+    static int sms[MAXDEV] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAXDEV) dev = 0;
+    if (sms[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+        cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PIPE_SMEM);
+        sms[dev] = n;
+    }
+    const int g = sms[dev] * PIPE_CTAS_PER_SM;
+    return tiles < g ? tiles : g;
+}
+
 template <int LOGN>
 int fwd_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (!ap) return PCB_BAD_ARGS;
@@ -605,9 +632,17 @@ int inv_run(const PcbNttArgs* ap, bool f64, cudaStream_t s) {
     if (a.nrows == 0) return 0;
     constexpr int A = LOGN - 8, COLS = 256 / (1 << (A / 2));
     const int ch = chunk_rows<LOGN>(a);
+    const bool pipe = pipelined<LOGN>(a, f64);
     for (int r0 = 0; r0 < a.nrows; r0 += ch) {
         const int n = a.nrows - r0 < ch ? a.nrows - r0 : ch;
-        if (f64) {
+        if (pipe) {
+            if constexpr (LOGN == 16) {
+                const int tiles = n * (256 / 16);
+                launch_pdl_smem(inv_rows_p<LOGN>, dim3(pipe_grid<inv_rows_p<LOGN>>(tiles)), dim3(THREADS), PIPE_SMEM, s,
+                                a, r0, n);
+                launch_pdl(inv_cols<LOGN, true>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
+            }
+        } else if (f64) {
             launch_pdl(inv_rows<LOGN, true>, dim3((1 << A) / 16, n), dim3(THREADS), s, a, r0);
             launch_pdl(inv_cols<LOGN, true>, dim3(256 / COLS, n), dim3(THREADS), s, a, r0);
         } else {
@@ -628,6 +663,13 @@ int inv(const PcbNttArgs* ap, cudaStream_t s) {
     return inv_run<LOGN>(ap, false, s);
 }
 
+// waits of the pipelined passes that ran out on the current device (0 unless a bulk copy never completed)
+__host__ unsigned int device_timeouts() {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof v) != cudaSuccess) return ~0u;
+    return v;
+}
+
 template int fwd<14>(const PcbNttArgs*, cudaStream_t);
 template int fwd<16>(const PcbNttArgs*, cudaStream_t);
 template int inv<14>(const PcbNttArgs*, cudaStream_t);
@@ -639,3 +681,7 @@ template int inv_run<16>(const PcbNttArgs*, bool, cudaStream_t);
 
 }  // namespace ntt
 }  // namespace pcb
+
+// Waits of the pipelined transforms that ran out on the current device since the library was loaded (0 in normal
+// operation; each stopped one CTA, whose rows were then left untransformed).
+extern "C" uint32_t pcb_device_timeouts(void) { return pcb::ntt::device_timeouts(); }

@@ -130,6 +130,7 @@ def test_ntt_batch_fp64_path_matches_oracle(s2):
     xd = dev(x)
     s.ntt_batch(xd, nrows, inverse=True)
     assert (host(xd) == inv_want).all()
+    assert L.lib().pcb_device_timeouts() == 0  # the pipelined passes' bounded waits never ran out
 
 
 def test_ntt_epilogues_and_sources(s2):

@@ -540,8 +540,10 @@ def block_decode(a, world, barrier, dist, seqs=1):
     projections, the token's K and V pushed into the lane cache (128 tokens in 4 blocks of 32, all 12 heads per
     block), attention over the cache, output projection, residual (perseus_b200.block; N = 2^16 with the 24-limb
     chain, weights N(0, 0.02), biases, gamma 1 + N(0, 0.02), activation N(0, 1)).
-    The cache starts with client-encrypted tokens and grows by one per step up to its 128; ms per token with CUDA events (every
-    rank runs the same replica; max over ranks), and the last step's decrypted error against the fp64 step."""
+    The cache starts with client-encrypted tokens and grows by one per step up to its 128; ms per token with CUDA
+    events (max over ranks), and the last step's decrypted error against the fp64 step. On N GPUs the 4 cache blocks
+    are split over the ranks (LaneCache shard=: each rank attends over its share, one all_gather of the partial
+    outputs summed mod p on every rank); the LayerNorm and the projections run on every rank."""
     import numpy as np
     import torch
 
@@ -560,7 +562,8 @@ def block_decode(a, world, barrier, dist, seqs=1):
     wf, norm = B.fold_norm(w, gamma, beta), B.NormCfg()
     Ks = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
     Vs = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
-    cache = B.LaneCache(s, lay, top - 10, seqs=seqs)
+    shard_ = (world, int(os.environ.get("RANK", "0"))) if world > 1 else None
+    cache = B.LaneCache(s, lay, top - 10, seqs=seqs, shard=shard_)
     cache.load(Ks if seqs > 1 else Ks[0], Vs if seqs > 1 else Vs[0])
     coeffs = A.softmax_poly(lay.tokens)
     xs = [[rng.normal(0, 1, n) for _ in range(seqs)] for _ in range(warm + steps)]
@@ -599,7 +602,9 @@ def block_decode(a, world, barrier, dist, seqs=1):
                        "x 64 per block), attention with the degree-7 polynomial softmax, output projection, "
                        "residual; N=2^16 24+8 limbs, radix-3 ladders, eager",
            "ms_per_token": t.item(), "timed_tokens": steps, "max_abs_err_vs_fp64": err,
-           "tokens_in_cache_at_end": pre + len(xs)}
+           "tokens_in_cache_at_end": pre + len(xs),
+           "sharding": f"cache blocks over {world} GPU(s): {lay.blocks} blocks, one all_gather of the partial "
+                       "outputs per token" if world > 1 else "one GPU"}
     if seqs > 1:
         out = {"sequences": seqs, "ms_per_step": t.item(), "tokens_per_s": seqs / (t.item() * 1e-3),
                "max_abs_err_vs_fp64_seq0": err}
@@ -611,9 +616,31 @@ def main():
     if a.part == "projection":
         print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
         return
-    if a.part == "block":
-        print(json.dumps({"part": "block", **block_decode(a, 1, lambda: None, None),
-                          "batch_of_4": block_decode(a, 1, lambda: None, None, seqs=4)}), flush=True)
+    if a.part == "block":  # under torchrun the cache blocks are split over the ranks (rank 0 prints)
+        import torch
+
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+
+        def barrier():
+            if dist:
+                dist.barrier()
+
+        out = {"part": "block", "n_gpus": world, **block_decode(a, world, barrier, dist),
+               "batch_of_4": block_decode(a, world, barrier, dist, seqs=4)}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
         return
     if a.part == "attention":
         ms, err = attention_decode(a, 1, 0, lambda: None, None)

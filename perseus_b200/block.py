@@ -31,6 +31,7 @@ import numpy as np
 
 from . import attention as A
 from . import linear as LIN
+from . import shard as SH
 from .attention import ladder_steps
 
 
@@ -130,14 +131,28 @@ class Weights:
 class LaneCache:
     """The encrypted K and V caches as batches of token blocks, at the level the pushed rows arrive at; the decode
     step's plaintexts (masks, encoded weights) are kept in `plan`. `seqs` independent sequences decode together (one
-    token each per step, at the same position): their blocks are batch members s blocks + b, every op of the step
-    runs on all of them."""
+    token each per step, at the same position): their blocks are batch members s nblocks + b, every op of the step
+    runs on all of them.
 
-    def __init__(self, ops, lay, top, scale=2.0**40, seqs=1):
+    shard = (world, rank) or (world, rank, group) splits the blocks over the ranks of a process group: this rank holds
+    blocks SH.share(blocks, world, rank) (`mine`), attends over them, and decode adds the ranks' partial outputs with
+    one exchange (SH.gather_sum). A rank with no block (more ranks than blocks) holds one all-zero block, so it runs
+    the same ops and adds zeros. Every rank encrypts every block in the same order and keeps its own, so its blocks
+    are word for word those of an unsharded cache of the same session randomness."""
+
+    def __init__(self, ops, lay, top, scale=2.0**40, seqs=1, shard=None):
         self.ops, self.lay, self.top, self.scale, self.seqs = ops, lay, top, scale, seqs
         self.k = self.v = None
         self.count = 0
         self.plan = {}
+        self.shard = None if shard is None else (shard + (None,))[:3]
+        self.mine = list(range(lay.blocks)) if shard is None else list(SH.share(lay.blocks, shard[0], shard[1]))
+        self.idle = not self.mine
+
+    @property
+    def nblocks(self):
+        """Blocks per sequence held here (an idle rank's zero block counts as one)."""
+        return max(len(self.mine), 1)
 
     def _blocks(self, rows):
         lay = self.lay
@@ -145,7 +160,10 @@ class LaneCache:
         for tok, row in enumerate(rows):
             b, lane = divmod(tok, lay.t)
             vecs[b][np.arange(lay.width) * lay.t + lane] = row
-        return [self.ops.encrypt(v, top=self.top, scale=self.scale, slots=lay.slots) for v in vecs]
+        cts = [self.ops.encrypt(v, top=self.top, scale=self.scale, slots=lay.slots) for v in vecs]
+        if self.idle:
+            return [_zero_like(cts[0])]
+        return [cts[b] for b in self.mine]
 
     def load(self, K, V):
         """The client's cache of n tokens (n x d_real each; with seqs > 1 a list of one such array per sequence, all of
@@ -164,16 +182,19 @@ class LaneCache:
         if self.count >= lay.tokens:
             raise ValueError(f"KV cache full ({lay.tokens} tokens)")
         b, lane = divmod(self.count, lay.t)
+        self.count += 1
+        if b not in self.mine:  # another rank holds the token's block
+            return
+        lb, nb = self.mine.index(b), self.nblocks
         kv = ops.stack([k_row, v_row])
         for st in lay.push_steps(lane):
             kv = ops.rotate(kv, st)
         kr, vr = ops.split(kv, 2)
-        kblk, vblk = ops.split(self.k, S * lay.blocks), ops.split(self.v, S * lay.blocks)
+        kblk, vblk = ops.split(self.k, S * nb), ops.split(self.v, S * nb)
         krs, vrs = (ops.split(kr, S), ops.split(vr, S)) if S > 1 else ([kr], [vr])
         for q in range(S):
-            ops.inplace_add(kblk[q * lay.blocks + b], krs[q])
-            ops.inplace_add(vblk[q * lay.blocks + b], vrs[q])
-        self.count += 1
+            ops.inplace_add(kblk[q * nb + lb], krs[q])
+            ops.inplace_add(vblk[q * nb + lb], vrs[q])
 
 
 @dataclass
@@ -229,6 +250,15 @@ def layer_norm(ops, x, lay, plan, cfg, primes):
     return ops.rescale_one(ops.mult(ops.drop_to(c, inv.top), inv))
 
 
+def _zero_like(ct):
+    """An all-zero ciphertext with ct's level, scale and slots (a session Ct on the device or an oracle one)."""
+    import copy
+
+    z = copy.copy(ct)
+    z.data = ct.data.clone().zero_() if hasattr(ct.data, "zero_") else np.zeros_like(ct.data)
+    return z
+
+
 def _masked(ops, plan, x, values, target_scale, primes):
     """x * values (a plaintext of the plan), rescaled, landing at target_scale one level below x."""
     pscale = target_scale * primes[x.top] / x.scale
@@ -266,15 +296,17 @@ def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
     # the query: lane 0 with 1 / sqrt(d_h), at q_top 2^10 so the products land near the primes' size
     qm = _masked(ops, cache.plan, q, lay.lane0(1.0 / math.sqrt(lay.head_dim)), primes[q.top - 1] * 2.0**10, primes)
     qr = ops.rotate_and_sum(qm, *lay.query_ladder(), rb)
-    S, nb = cache.seqs, lay.blocks
+    S, nb = cache.seqs, cache.nblocks
     qs = ops.split(qr, S) if S > 1 else [qr]
     qb = ops.stack([x for x in qs for _ in range(nb)]) if S * nb > 1 else qr  # one copy per block, [sequence][block]
     yb = A.attend(ops, qb, cache, coeffs, primes)
-    if nb > 1:  # each sequence's blocks summed
+    if nb > 1:  # each sequence's blocks (held here) summed
         ys = ops.split(yb, S * nb)
         y = ops.stack([ops.sum(ys[q * nb:(q + 1) * nb]) for q in range(S)]) if S > 1 else ops.sum(ys)
     else:
         y = yb
+    if cache.shard is not None:  # the other ranks' blocks: their partial outputs added, the same words everywhere
+        y = SH.gather_sum(ops, y, cache.shard[2])
     # the lane sums leave partial sums in lanes 1 .. t-1; the projection's replication ladder needs them zero
     y = _masked(ops, cache.plan, y, lay.lane0(), y.scale, primes)
     lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)

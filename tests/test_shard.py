@@ -122,3 +122,79 @@ def _wrong_share(port, errq):
     except ValueError:
         errq.put("ValueError")
     dist.destroy_process_group()
+
+
+def _block_rank_main(rank, world, port, errq):
+    """The lane-layout attention block with its cache blocks split over the ranks (perseus_b200.block.LaneCache
+    shard=...), against the unsharded step on the same session randomness: every rank's output equals the
+    unsharded output word for word, and its blocks equal the matching unsharded blocks, over two tokens."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from perseus_b200 import block as B
+        from tests import _oracle as O
+        from tests._oracle_ops import OracleOps
+
+        O.lib().orc_set_threads(2)
+        logn = 10
+        lay = B.layout(1 << (logn - 1), 32, heads=4, head_dim=8, tokens=32, radix_bits=3)  # 2 blocks of 16
+        q = O.ntt_primes(50, logn, 12)
+        p = O.ntt_primes(50, logn, 3, skip=12)
+        gal = [1] + [O.lib().orc_rotation_galois(s, logn) for s in lay.rot_steps()]
+        rng = np.random.default_rng(9)
+        n, pre = 32, 15  # tokens 15 (block 0, lane 15) and 16 (block 1, lane 0) are pushed
+        w = B.Weights(*[rng.normal(0, 0.1, (n, n)) if i % 2 == 0 else rng.normal(0, 0.02, n) for i in range(8)])
+        K, V = rng.normal(0, 1, (pre, n)) / 8, rng.normal(0, 1, (pre, n)) / 8
+        xs = [rng.normal(0, 1, n) / 2 for _ in range(2)]
+        coeffs = A.softmax_poly(lay.tokens)
+        runs = []
+        for sh in (None, (world, rank)):
+            c = O.Ctx(logn, q, p, 4)
+            c.keygen(seed=0, h=64, sigma=3.2, galois=gal)
+            ops = OracleOps(c)
+            top = c.nq - 1
+            cache = B.LaneCache(ops, lay, top - 2, shard=sh)
+            cache.load(K, V)
+            ys = []
+            for x in xs:
+                xc = ops.encrypt(B.LIN.input_vector(x, lay.geo), top, 2.0**40, lay.slots)
+                ys.append(B.decode(ops, xc, w, cache, coeffs, c.q))
+            runs.append((ys, cache))
+        (ys, full), (zs, part) = runs
+        one = lambda c: c.cts[0] if hasattr(c, "cts") else c  # noqa: E731
+        for y, z in zip(ys, zs):
+            y, z = one(y), one(z)
+            assert z.top == y.top and (z.data[:, : y.top + 1] == y.data[:, : y.top + 1]).all()
+        assert part.mine == list(shard.share(lay.blocks, world, rank))
+        blocks = lambda b: b.cts if hasattr(b, "cts") else [b]  # noqa: E731
+        for li, b in enumerate(part.mine):
+            for mine_b, all_b in ((blocks(part.k)[li], blocks(full.k)[b]), (blocks(part.v)[li], blocks(full.v)[b])):
+                assert (mine_b.data[:, : part.top + 1] == all_b.data[:, : part.top + 1]).all(), b
+        if part.idle:
+            assert not blocks(part.k)[0].data.any()
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # the parent reports it
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_block_gloo(world):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_block_rank_main, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not alive, "a rank did not finish"
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs)

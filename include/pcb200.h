@@ -312,6 +312,19 @@ typedef struct PcbKskGenArgs {
     int32_t nrows, ndig, nq, bits, sq, pad;
 } PcbKskGenArgs;
 
+/* args.cuh:665-677: composite ModRaise, coefficient form: for rows t in [r0, r1) of K ciphertexts (nparts polynomials
+ * from part 0), x[t] = sum_{k < d} centred([x_k qhatinv_k]_{q_k}) qhat[k][t] mod q_t, the sources x_k = rows 0..d-1
+ * of the same polynomial (d <= 4, t < 64; the sources are not written). d = 1, qhatinv = qhat = 1: the level-0 raise
+ * of CKKS bootstrapping (every row t gets the centred lift of row 0). */
+typedef struct PcbModRaiseArgs {
+    void* x;
+    const PcbPrimeConst* pr;
+    uint64_t ct_stride, part_stride;
+    uint64_t qhatinv[4];
+    uint64_t qhat[4][64];
+    int32_t K, d, r0, r1, nparts, pad;
+} PcbModRaiseArgs;
+
 typedef int (*PcbLaunch)(const void* args, cudaStream_t stream);
 
 /* args.cuh:1034-1097: 16-byte header then 52 launchers, in the reference's order */
@@ -340,7 +353,9 @@ typedef struct PcbKernelTable {
     PcbLaunch encode;
     int (*encrypt)(const PcbEncryptArgs*, cudaStream_t);
     int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
-    PcbLaunch ksk_unpack, mod_raise, small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
+    PcbLaunch ksk_unpack;
+    int (*mod_raise)(const PcbModRaiseArgs*, cudaStream_t);
+    PcbLaunch small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
     int (*ks_dot_key)(const PcbKsKeyArgs*, cudaStream_t);
     PcbLaunch pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum;
     int (*mul_add)(const PcbMulAddArgs*, cudaStream_t);
@@ -513,6 +528,11 @@ int pcb_linear_transform_multi(PcbCtx* ctx, const uint64_t* x, const uint64_t* c
                                int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
                                cudaStream_t stream);
 
+/* ModRaise of K ciphertexts for bootstrapping (crates/pc-gpu/src/bts/raise.rs): rows 0 of both parts (evaluation
+ * form, level 0) become rows 0..top_out: every residue the centred lift of the level-0 residue (the mod_raise entry
+ * with d = 1), back in evaluation form. In place; the ciphertext then decrypts to m + q_0 I with small integer I. */
+int pcb_mod_raise(PcbCtx* ctx, uint64_t* ct, int32_t top_out, int32_t K, cudaStream_t stream);
+
 /* The hybrid key switch of one polynomial per ciphertext (the north star's fused KeySwitcher): ext = dot(ModUp(d))
  * against key `kidx` with c0 mode (0 none, 1 P c0 on Q rows) and output permutation autok, then ModDown into out.
  * d, c0: rows 0..=top of K polynomials `in_stride` words apart; out: K ciphertexts. */
@@ -547,6 +567,7 @@ static_assert(sizeof(PcbRescaleCombineArgs) == 80, "RescaleCombineArgs layout");
 static_assert(sizeof(PcbAutomorphArgs) == 112, "AutomorphArgs layout");
 static_assert(sizeof(PcbEncryptArgs) == 64, "EncryptArgs layout");
 static_assert(sizeof(PcbKskGenArgs) == 120, "KskGenArgs layout");
+static_assert(sizeof(PcbModRaiseArgs) == 2136, "ModRaiseArgs layout");
 static_assert(sizeof(PcbPtDotArgs) == 128, "PtDotArgs layout");
 static_assert(sizeof(PcbAddConstArgs) == 48, "AddConstArgs layout");
 static_assert(sizeof(PcbMulTableArgs) == 72, "MulTableArgs layout");

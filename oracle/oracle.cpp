@@ -1077,6 +1077,29 @@ int orc_tensor(void* cv, const uint64_t* a, const uint64_t* b, uint64_t* c01, ui
     return 0;
 }
 int orc_rescale(void* cv, uint64_t* ct, int top) { return rescale(*(Ctx*)cv, ct, top); }
+// ModRaise for bootstrapping (crates/pc-gpu/src/bts/raise.rs with crates/pc-kernels/kernels/bts.cuh:15 at d = 1): row 0
+// of both parts to coefficient form, every row t <= top_out the centred lift of it mod q_t, back to evaluation form
+int orc_mod_raise(void* cv, uint64_t* ct, int top_out) {
+    Ctx& c = *(Ctx*)cv;
+    if (top_out < 0 || top_out >= c.nq) return -1;
+    const size_t n = c.n;
+    const int rows = c.rows();
+    const uint64_t q0 = c.primes[0];
+    for (int part = 0; part < 2; ++part) {
+        uint64_t* x = ct + (size_t)part * rows * n;
+        ntt_inv_row(c, x, 0);
+        for (int t = 1; t <= top_out; ++t) {
+            const uint64_t qt = c.primes[t];
+            uint64_t* o = x + (size_t)t * n;
+            for (size_t k = 0; k < n; ++k) {
+                const uint64_t y = x[k];
+                o[k] = y > q0 / 2 ? submod(y % qt, q0 % qt, qt) : y % qt;
+            }
+        }
+        for (int t = 0; t <= top_out; ++t) fwd_exact(x + (size_t)t * n, c.tab[t], n);
+    }
+    return 0;
+}
 int orc_rotate(void* cv, const uint64_t* x, int64_t step, uint64_t* out, int top) {
     return rotate(*(Ctx*)cv, x, step, out, top);
 }

@@ -93,6 +93,8 @@ int orc_mult(void* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int t
 int orc_tensor(void* c, const uint64_t* a, const uint64_t* b, uint64_t* c01, uint64_t* d2, int top);
 /* rescale by q_top in place: rows 0..top-1 hold the result */
 int orc_rescale(void* c, uint64_t* ct, int top);
+/* ModRaise in place: row 0 (level 0) of both parts lifted (centred) to rows 0..top_out, evaluation form */
+int orc_mod_raise(void* c, uint64_t* ct, int top_out);
 /* rotation by `step` slots (left), key of galois element 5^step must exist */
 int orc_rotate(void* c, const uint64_t* x, int64_t step, uint64_t* out, int top);
 /* x + rot(x, s) ladder: gaps start, 2 start, ... < stop (rotate_and_sum, radix 1) */

@@ -138,6 +138,12 @@ class EncryptArgs(C.Structure):
                 ("nonce", C.c_uint32), ("nl", C.c_int32)]
 
 
+class ModRaiseArgs(C.Structure):
+    _fields_ = [("x", vp), ("pr", vp), ("ct_stride", C.c_uint64), ("part_stride", C.c_uint64),
+                ("qhatinv", C.c_uint64 * 4), ("qhat", (C.c_uint64 * 64) * 4), ("K", C.c_int32), ("d", C.c_int32),
+                ("r0", C.c_int32), ("r1", C.c_int32), ("nparts", C.c_int32), ("pad", C.c_int32)]
+
+
 class KskGenArgs(C.Structure):
     _fields_ = [("b", vp), ("a", vp), ("e", vp), ("s_new", vp), ("s_old", vp), ("seed", vp), ("ids", vp),
                 ("digit_of", vp), ("pmod", vp), ("pmods", vp), ("pr", vp), ("row_words", C.c_uint64),
@@ -177,7 +183,7 @@ SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJo
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
          "EncryptArgs": 64, "KskGenArgs": 120, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
-         "MulAddArgs": 104, "MulAddNArgs": 328, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
+         "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
 
 _lib = None
 
@@ -231,6 +237,7 @@ def lib():
         "pcb_linear_transform": (C.c_int, [vp, vp, vp, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_linear_transform_multi": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
+        "pcb_mod_raise": (C.c_int, [vp, vp, i32, i32, vp]),
         "pcb_ntt_batch": (C.c_int, [vp, vp, i32, i32, vp]),
     }
     for name, (res, args) in sig.items():

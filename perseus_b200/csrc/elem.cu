@@ -272,6 +272,39 @@ int rescale_coef_launch(const PcbRescaleArgs* ap, cudaStream_t s) {
     return PCB_LAUNCH_RESULT();
 }
 
+// ------------------------------------------------------------------------------------------------ ModRaise
+// args.cuh:665-677: rows t in [r0, r1) of K ciphertexts (nparts parts), one output word per thread:
+// x[t] = sum_{k < d} lift_k([x_k qhatinv_k]_{q_k}) qhat[k][t] mod q_t, lift_k = the centred representative mod q_k
+template <int LOGN>
+__global__ void __launch_bounds__(BX) mod_raise(PcbModRaiseArgs a) {
+    const int c = blockIdx.z / a.nparts, part = blockIdx.z % a.nparts;
+    const int t = a.r0 + blockIdx.y;
+    const size_t i = (size_t)blockIdx.x * BX + threadIdx.x;
+    uint64_t* x = (uint64_t*)a.x + (size_t)c * a.ct_stride + (size_t)part * a.part_stride;
+    const PcbPrimeConst& pt = a.pr[t];
+    const uint64_t qt = pt.p;
+    uint64_t acc = 0;
+    for (int k = 0; k < a.d; ++k) {
+        const PcbPrimeConst& pk = a.pr[k];
+        const uint64_t y = mul_mod(x[((size_t)k << LOGN) + i], a.qhatinv[k], pk);
+        const uint64_t r = lift_word(y, pk.p, red_word(pk.p, pt), pt);
+        acc = add_mod(acc, mul_mod(r, a.qhat[k][t], pt), qt);
+    }
+    x[((size_t)t << LOGN) + i] = acc;
+}
+
+template <int LOGN>
+int mod_raise_launch(const PcbModRaiseArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbModRaiseArgs& a = *ap;
+    if (!a.x || !a.pr || a.d < 1 || a.d > 4 || a.r0 < a.d || a.r1 > 64 || a.r1 < a.r0 || a.K < 0 || a.nparts < 1 ||
+        a.nparts > 2)
+        return PCB_BAD_ARGS;
+    if (a.K == 0 || a.r1 == a.r0) return 0;
+    mod_raise<LOGN><<<dim3((1 << LOGN) / BX, a.r1 - a.r0, a.K * a.nparts), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(BX) rescale_combine(PcbRescaleCombineArgs a) {
     const int row = blockIdx.y, c = blockIdx.z >> 1, part = blockIdx.z & 1;
@@ -366,6 +399,7 @@ int sum_launch(const SumArgs* ap, cudaStream_t s) {
     template int tensor_launch<L>(const PcbTensorArgs*, cudaStream_t);                               \
     template int md_epilogue_launch<L>(const PcbMdEpiArgs*, cudaStream_t);                           \
     template int rescale_coef_launch<L>(const PcbRescaleArgs*, cudaStream_t);                        \
+    template int mod_raise_launch<L>(const PcbModRaiseArgs*, cudaStream_t);                          \
     template int rescale_combine_launch<L>(const PcbRescaleCombineArgs*, cudaStream_t);              \
     template int automorph_launch<L>(const PcbAutomorphArgs*, cudaStream_t);
 PCB_INST(14)

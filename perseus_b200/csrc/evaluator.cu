@@ -124,6 +124,8 @@ struct PcbCtx {
     int32_t* id_rprime_q = nullptr;
     uint32_t* key_roff = nullptr;
     int32_t* key_rprime = nullptr;
+    uint32_t* mr_roff = nullptr;  // pcb_mod_raise: the rows it transforms (filled per call), [2 k_max nq]
+    int32_t* mr_rprime = nullptr;
     std::vector<LevelPlan> lv;
     // workspaces
     uint64_t *coef = nullptr, *digits = nullptr, *ext = nullptr, *conv = nullptr, *dbuf = nullptr, *row = nullptr;
@@ -562,6 +564,8 @@ int layout(PcbCtx& c, int nkeys, cudaStream_t s) {
     }
     c.s_eval = A.take<uint64_t>((size_t)rows * n);
     c.enc_seed = A.take<uint32_t>(8);
+    c.mr_roff = A.take<uint32_t>((size_t)2 * km * c.nq);
+    c.mr_rprime = A.take<int32_t>((size_t)2 * km * c.nq);
     if (fill) CK(cudaStreamSynchronize(s));
     return 0;
 }
@@ -1273,6 +1277,46 @@ int pcb_rescale(PcbCtx* c, uint64_t* ct, int32_t top, int32_t K, cudaStream_t s)
     f.ex = ct;
     f.es = l.rs_alpha;
     f.ess = l.rs_alphas;
+    CK(ntt_fwd(*c, &f, s));
+    return 0;
+}
+
+int pcb_mod_raise(PcbCtx* c, uint64_t* ct, int32_t top_out, int32_t K, cudaStream_t s) {
+    if (!c || !ct) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top_out, K);
+    if (rc) return rc;
+    if (top_out > 63) return fail(PCB_BAD_ARGS, "raise to %d limbs (the mod_raise entry takes 64)", top_out + 1);
+    const LevelPlan& l0 = c->lv[0];
+    // row 0 of both parts to coefficient form, in place
+    PcbNttArgs a = ntt_args(*c, ct, l0.rs_intt_roff, l0.rs_intt_rprime, 2 * K);
+    CK(ntt_inv(*c, &a, s));
+    // rows 1..top_out: the centred lift of row 0 (one source row, qhatinv = qhat = 1)
+    PcbModRaiseArgs m;
+    memset(&m, 0, sizeof m);
+    m.x = ct;
+    m.pr = c->pr;
+    m.ct_stride = c->ct_words();
+    m.part_stride = (uint64_t)c->rows * c->n;
+    m.qhatinv[0] = 1;
+    for (int t = 0; t < 64; ++t) m.qhat[0][t] = 1;
+    m.K = K;
+    m.d = 1;
+    m.r0 = 1;
+    m.r1 = top_out + 1;
+    m.nparts = 2;
+    CK(c->tab->mod_raise(&m, s));
+    // every row back to evaluation form
+    std::vector<uint32_t> ro;
+    std::vector<int32_t> rp;
+    for (int cc = 0; cc < K; ++cc)
+        for (int part = 0; part < 2; ++part)
+            for (int t = 0; t <= top_out; ++t) {
+                ro.push_back((uint32_t)((2 * cc + part) * c->rows + t));
+                rp.push_back(t);
+            }
+    CK(upload(c->mr_roff, ro, s));
+    CK(upload(c->mr_rprime, rp, s));
+    PcbNttArgs f = ntt_args(*c, ct, c->mr_roff, c->mr_rprime, (int)ro.size());
     CK(ntt_fwd(*c, &f, s));
     return 0;
 }

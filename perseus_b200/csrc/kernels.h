@@ -27,6 +27,7 @@ template <int LOGN> int tensor_launch(const PcbTensorArgs*, cudaStream_t);
 template <int LOGN> int md_epilogue_launch(const PcbMdEpiArgs*, cudaStream_t);
 template <int LOGN> int rescale_coef_launch(const PcbRescaleArgs*, cudaStream_t);
 template <int LOGN> int rescale_combine_launch(const PcbRescaleCombineArgs*, cudaStream_t);
+template <int LOGN> int mod_raise_launch(const PcbModRaiseArgs*, cudaStream_t);
 template <int LOGN> int automorph_launch(const PcbAutomorphArgs*, cudaStream_t);
 }  // namespace elem
 namespace pt {

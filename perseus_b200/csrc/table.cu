@@ -39,6 +39,7 @@ PcbKernelTable make_table() {
     t.automorph = elem::automorph_launch<LOGN>;
     t.encrypt = keys::encrypt_launch<LOGN>;
     t.ksk_gen = keys::ksk_gen_launch<LOGN>;
+    t.mod_raise = elem::mod_raise_launch<LOGN>;
     return t;
 }
 

@@ -149,7 +149,8 @@ KEY_SOURCES = {"dense": 0, "regen": 1}
 class Session:
     """A context over one chain with device-resident keys (relinearization + the given rotation steps)."""
 
-    def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None, key_source="dense"):
+    def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None, key_source="dense",
+                 galois_extra=()):
         self.chain = chain
         self.device = torch.device(device or "cuda")
         self.n, self.log_n = chain.n, chain.log_n
@@ -158,6 +159,10 @@ class Session:
         gal = [1]
         for s in rot_steps:
             g = rotation_galois(s, chain.log_n)
+            if g != 1 and g not in gal:
+                gal.append(g)
+        for g in galois_extra:  # keys for other automorphisms, e.g. conjugation (2N - 1)
+            g %= 2 * chain.n
             if g != 1 and g not in gal:
                 gal.append(g)
         self.galois = gal
@@ -437,6 +442,47 @@ class Session:
         L.check(L.lib().pcb_add_pt(self.ctx, a.ptr(), C.c_void_p(pt.data_ptr()), out.ptr(), a.top, a.k,
                                    self._stream()), "pcb_add_pt")
         return out
+
+    def mod_raise(self, a, top):
+        """In place: a at level 0 raised to limbs 0..top (bootstrapping's ModRaise); decrypts to m + q_0 I."""
+        if a.top != 0:
+            raise ValueError(f"mod_raise takes a level-0 ciphertext, not top {a.top}")
+        L.check(L.lib().pcb_mod_raise(self.ctx, a.ptr(), int(top), a.k, self._stream()), "pcb_mod_raise")
+        a.top = top
+        return a
+
+    def automorph(self, a, g):
+        """The automorphism X -> X^g of a (a key switch with the key of galois element g): g = 2N - 1 conjugates
+        every slot; 5^r mod 2N rotates by r."""
+        g %= 2 * self.n
+        if g not in self.galois:
+            raise ValueError(f"no key for galois element {g}")
+        out = self.ct_like(a)
+        autok = pow(g, (2 * self.n >> 2) - 1, 2 * self.n)  # g^-1 in the group of 5 and -1 (crates/pc-core/src/galois.rs)
+        c1 = C.c_void_p(a.data.data_ptr() + self.rows * self.n * 8)
+        L.check(L.lib().pcb_keyswitch(self.ctx, c1, a.ptr(), 1, self.galois.index(g), autok, out.ptr(), a.top, a.k, 0,
+                                      self._stream()), "pcb_keyswitch")
+        return out
+
+    def conjugate(self, a):
+        return self.automorph(a, 2 * self.n - 1)
+
+    def monomial(self, power, top):
+        """X^power as a plaintext of scale 1 ([nq][N] evaluation rows): its slots are all zeta^(power 5^k); power
+        N / 2 multiplies every slot by i. mult_pt(a, monomial, 1.0) uses no level."""
+        key = ("monomial", int(power) % (2 * self.n), top)
+        cache = self.__dict__.setdefault("_monomials", {})
+        if key not in cache:
+            pw = int(power) % (2 * self.n)
+            rows = np.zeros((top + 1, self.n), np.uint64)
+            for r in range(top + 1):
+                q = self.chain.q[r]
+                rows[r, pw % self.n] = 1 if pw < self.n else q - 1  # X^N = -1
+            dev = torch.zeros((self.nq, self.n), dtype=torch.int64, device=self.device)
+            L.check(L.lib().pcb_pt_load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(dev.data_ptr()),
+                                        self._stream()), "pcb_pt_load")
+            cache[key] = dev
+        return cache[key]
 
     def keyswitch(self, d, c0, c0_mode, kidx, autok, out, top, k):
         L.check(L.lib().pcb_keyswitch(self.ctx, C.c_void_p(d), C.c_void_p(c0 or 0), c0_mode, kidx, autok,

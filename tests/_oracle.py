@@ -78,6 +78,7 @@ def lib():
         "orc_mult": (C.c_int, [C.c_void_p, u64p, u64p, u64p, C.c_int]),
         "orc_tensor": (C.c_int, [C.c_void_p, u64p, u64p, u64p, u64p, C.c_int]),
         "orc_rescale": (C.c_int, [C.c_void_p, u64p, C.c_int]),
+        "orc_mod_raise": (C.c_int, [C.c_void_p, u64p, C.c_int]),
         "orc_rotate": (C.c_int, [C.c_void_p, u64p, C.c_int64, u64p, C.c_int]),
         "orc_rotate_and_sum": (C.c_int, [C.c_void_p, u64p, C.c_int64, C.c_int64, u64p, C.c_int]),
         "orc_rotate_sum": (C.c_int, [C.c_void_p, u64p, C.c_void_p, C.c_int, u64p, C.c_int]),
@@ -233,6 +234,21 @@ class Ctx:
         x = np.ascontiguousarray(ct).copy()
         assert lib().orc_rescale(self.h, x, top) == 0
         return x
+
+    def mod_raise(self, ct, top_out):
+        x = np.ascontiguousarray(ct).copy()
+        assert lib().orc_mod_raise(self.h, x, top_out) == 0
+        return x
+
+    def keyswitch(self, d, c0, c0_mode, kidx, autok, top):
+        """ModUp(d), the inner product against key kidx (c0 mode, output at automorph_slot(autok, i)), ModDown."""
+        ext = self.ct()
+        rc = lib().orc_keyswitch_ext(self.h, np.ascontiguousarray(d), np.ascontiguousarray(c0) if c0 is not None
+                                     else np.zeros((self.rows, self.n), np.uint64), c0_mode, kidx, autok, ext, top)
+        assert rc == 0, rc
+        out = self.ct()
+        assert lib().orc_moddown(self.h, ext, out, top) == 0
+        return out
 
     def rotate(self, ct, step, top):
         out = self.ct()

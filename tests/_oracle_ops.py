@@ -81,6 +81,39 @@ class OracleOps:
         return OCt(self.c.mult(a.data, b.data, a.top), a.top, a.scale * b.scale, a.slots)
 
     @_batched
+    def sub(self, a, b):
+        assert a.top == b.top
+        return OCt(self.c.sub(a.data, b.data, a.top), a.top, a.scale, a.slots)
+
+    @_batched
+    def mod_raise(self, a, top):
+        assert a.top == 0
+        a.data = self.c.mod_raise(a.data, top)
+        a.top = top
+        return a
+
+    @_batched
+    def automorph(self, a, g):
+        """X -> X^g by the key of galois element g (g = 2N - 1: conjugation), as the session's automorph."""
+        n2 = 2 * self.c.n
+        g %= n2
+        autok = pow(g, (n2 >> 2) - 1, n2)
+        out = self.c.keyswitch(a.data[1], a.data[0], 1, self.c.galois.index(g), autok, a.top)
+        return OCt(out, a.top, a.scale, a.slots)
+
+    def conjugate(self, a):
+        return self.automorph(a, 2 * self.c.n - 1)
+
+    def monomial(self, power, top):
+        """X^power in coefficient form (rows 0..top) for mult_pt with scale 1."""
+        n = self.c.n
+        pw = int(power) % (2 * n)
+        rows = np.zeros((top + 1, n), np.uint64)
+        for r in range(top + 1):
+            rows[r, pw % n] = 1 if pw < n else self.c.q[r] - 1
+        return rows
+
+    @_batched
     def rescale_one(self, a):
         a.data = self.c.rescale(a.data, a.top)
         a.scale /= self.c.q[a.top]

@@ -610,6 +610,37 @@ def test_rescale_launchers(env, ndrop):
     same(run_both("rescale_combine", mk_comb))
 
 
+@pytest.mark.parametrize("d,r0,r1,nparts", [(1, 1, 12, 2), (2, 2, 9, 1), (3, 5, 12, 2), (4, 4, 12, 2)])
+def test_mod_raise(env, d, r0, r1, nparts):
+    """mod_raise: composite raise from the d bottom rows (random Garner constants), onto rows [r0, r1) of both widths;
+    d = 1 with unit constants is bootstrapping's level-0 raise."""
+    rng = np.random.default_rng(95 + d)
+    K = 3
+    x0 = env.cts(rng, K)
+    q = env.primes
+    a = L.ModRaiseArgs()
+    for k in range(d):
+        a.qhatinv[k] = 1 if d == 1 else int(rng.integers(1, q[k]))
+        for t in range(env.R):
+            a.qhat[k][t] = 1 if d == 1 else int(rng.integers(0, q[t]))
+
+    def mk():
+        xd = dev(x0)
+        a.x, a.pr = xd.data_ptr(), env.pc.data_ptr()
+        a.ct_stride, a.part_stride = 2 * env.R * env.n, env.R * env.n
+        a.K, a.d, a.r0, a.r1, a.nparts = K, d, r0, r1, nparts
+        return a, [xd], []
+
+    got = run_both("mod_raise", mk)
+    same(got)
+    if d == 1:  # every raised row holds the centred lift of row 0
+        x, out = x0[:, :nparts, 0].astype(object), got["ours"][0].reshape(x0.shape)
+        c = np.where(x > q[0] // 2, x - q[0], x)
+        for t in range(r0, r1):
+            assert (out[:, :nparts, t] == (c % q[t]).astype(np.uint64)).all()
+        assert (out[:, nparts:] == x0[:, nparts:]).all()
+
+
 # ------------------------------------------------------------------------------------------------ plaintext operands
 
 

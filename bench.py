@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
     ap.add_argument("--profile", action="store_true",
                     help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
-    ap.add_argument("--part", choices=["all", "projection", "attention", "block"], default="all",
+    ap.add_argument("--part", choices=["all", "projection", "attention", "block", "bootstrap"], default="all",
                     help="projection / attention: only that timing (one GPU; the timed steps in the NVTX range "
                          "'projection_step' / 'attention_step', the ncu case)")
     return ap.parse_args()
@@ -359,6 +359,7 @@ def run_ours(a):
     proj = projection(a, world, barrier, dist)
     blk = block_decode(a, world, barrier, dist)
     blk["batch_of_4"] = block_decode(a, world, barrier, dist, seqs=4)
+    bts = bootstrap(a, world, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -393,6 +394,7 @@ def run_ours(a):
             "plain_rotation_ks_per_s": plain_ks,
             "projection": proj,
             "attention_block": blk,
+            "bootstrap": bts,
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
@@ -611,8 +613,62 @@ def block_decode(a, world, barrier, dist, seqs=1):
     return out
 
 
+def bootstrap(a, world, barrier, dist):
+    """Config 4: CKKS bootstrapping at N = 2^16 with full slots (2^15), a level-0 ciphertext of uniform [-1, 1] slot
+    values (seeded) refreshed to 12 usable levels (perseus_b200.bootstrap: ModRaise, CoeffToSlot in 3 BSGS groups,
+    conjugate split, EvalMod by the degree-63 Chebyshev interpolant with 3 double angles, SlotToCoeff in 3 groups) on
+    the 29 + 11 limb chain (dnum 3, secret of Hamming weight 192). ms per bootstrap with CUDA events (every rank runs a
+    replica; max over ranks) and the refreshed ciphertext's decrypted error against the input slots."""
+    import numpy as np
+    import torch
+
+    from perseus_b200 import bootstrap as BS
+    from perseus_b200 import fhe
+
+    ch = fhe.config4_chain()
+    prm = BS.Params(ch.n, K=24, r=3, per_group=5)
+    s = fhe.Session(ch, rot_steps=BS.rot_steps(prm), k_max=2, seed=0, h=192, sigma=3.2,
+                    galois_extra=(BS.conj_galois(ch.n),))
+    z = np.random.default_rng(12).uniform(-1, 1, prm.slots)
+    ct = s.encrypt(z, top=0, scale=2.0**40, slots=prm.slots)
+    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)
+    top = len(ch.q) - 1
+    out = None
+    for _ in range(max(a.warmup, 3)):
+        out = bt(ct, top)
+    steps = max(1, min(a.steps, 10))
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("bootstrap_step")
+    e0.record()
+    for _ in range(steps):
+        out = bt(ct, top)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    got = s.decrypt_slots(out)
+    err = got - z
+    res = {"workload": "config 4: CKKS bootstrap, N=2^16, full slots (2^15), level 0 -> 12 usable levels, 29+11 x "
+                       "50-bit limbs, dnum 3, h=192, EvalMod K'=24 degree 63 + 3 double angles, CoeffToSlot / "
+                       "SlotToCoeff 3 groups of 5 FFT stages each",
+           "ms_per_bootstrap": t.item(), "bootstraps_per_s_all_gpus": world * 1e3 / t.item(), "timed": steps,
+           "levels_out": out.top, "max_abs_err": float(np.abs(err.real).max()),
+           "rms_err": float(np.sqrt((err.real ** 2).mean())), "max_abs_imag": float(np.abs(got.imag).max()),
+           "rotation_keys": len(BS.rot_steps(prm)) + 1}
+    del s, ct, out, bt
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     a = parse()
+    if a.part == "bootstrap":
+        print(json.dumps({"part": "bootstrap", **bootstrap(a, 1, lambda: None, None)}), flush=True)
+        return
     if a.part == "projection":
         print(json.dumps({"part": "projection", **projection(a, 1, lambda: None, None)}), flush=True)
         return

@@ -22,6 +22,13 @@ Steps, restated from the encoder's algebra (perseus_b200/csrc/host_math.h Encode
 5. The parts recombined, w' = u' + X^(N/2) v', then SlotToCoeff: the forward stages F on bitrev(w') give the slots
    F(bitrev(w')), the message.
 
+Precision: EvalMod's error is amplified by q_0 / (2 pi Delta) on the way out, and the sine's own error is about
+(2 pi^2 / 3) (Delta / q_0)^2 |m / Delta|^3 per coefficient. A level-0 input at a small scale is therefore first
+multiplied by the integer 2^b (exact, no level) so that EvalMod runs at q_0 / Delta' = 2^ratio_bits (2^8: about 1e-4
+of sine error for a constant slot vector of 1, where |m / Delta| peaks; far less for spread-out slots). The key switches
+of SlotToCoeff act on messages of about 2^-8 relative size, so their noise must stay far below the ModDown rounding: the
+special modulus P is one prime larger than a digit (config4_chain).
+
 Scales: the ciphertext's `scale` is bookkeeping (slots = decoding / scale). After ModRaise it is set to K' q_0, so
 the slots of CoeffToSlot's output are x in [-1, 1]; the last CoeffToSlot group's plaintexts are encoded so that its
 output lands at a working scale near the primes (stable products); the factor q_0 / (2 pi Delta) of EvalMod's output
@@ -104,6 +111,8 @@ class Params:
     r: int = 3             # double angles after the interpolant
     degree: int = 63
     per_group: int = 5     # FFT stages merged per CoeffToSlot / SlotToCoeff group
+    ratio_bits: int = 8    # log2(q_0 / Delta') EvalMod works at: the input is first multiplied by the integer
+    #                        2^round(log2(q_0 / Delta) - ratio_bits) when that is above 1
 
     @property
     def slots(self):
@@ -120,23 +129,41 @@ def _bsgs(npts):
     return best
 
 
-def _group_plan(stride, diags):
+def _group_plan(stride, diags, S):
+    """(D, npts, bstep, gstep) of a group: its offsets -D .. D strides, rotated by -D stride onto 0 .. 2D. A group whose
+    2D + 1 offsets exceed the S / stride distinct rotations is folded mod S instead (D = 0, npts = S / stride: offsets
+    congruent mod S are one rotation, their diagonals summed)."""
     D = max(abs(o) for o in diags) // stride
-    npts = 2 * D + 1
+    span = S // stride
+    if 2 * D + 1 > span:
+        D, npts = 0, span
+    else:
+        npts = 2 * D + 1
     bstep, gstep = _bsgs(npts)
     return D, npts, bstep, gstep
+
+
+def _plan_diagonals(stride, diags, S, factor):
+    """The npts diagonals of the group's BSGS product, in offset order (d stride for d < npts after the -D stride
+    pre-rotation, or mod S when folded)."""
+    D, npts, _, _ = _group_plan(stride, diags, S)
+    out = [np.zeros(S, np.complex128) for _ in range(npts)]
+    for o, d in diags.items():
+        j = (o // stride + D) if D else (o % S) // stride
+        out[j] = out[j] + factor * d
+    return out
 
 
 def rot_steps(p):
     """Every rotation step the bootstrap uses (the conjugation key is galois 2N - 1, added separately)."""
     steps = set()
+    S = p.slots
     for inverse in (True, False):
         for stride, diags in groups(p.n, inverse, p.per_group):
-            D, npts, bstep, gstep = _group_plan(stride, diags)
+            D, npts, bstep, gstep = _group_plan(stride, diags, S)
             steps.add(-D * stride)
             steps.update(b * stride for b in range(1, bstep))
             steps.update(j * bstep * stride for j in range(1, gstep))
-    S = p.slots
     return sorted({s % S for s in steps if s % S})
 
 
@@ -242,19 +269,21 @@ class Bootstrapper:
         self.plan = {}
         self.cts = groups(p.n, True, p.per_group)
         self.stc = groups(p.n, False, p.per_group)
+        self.boost = max(0, round(math.log2(self.q0 / self.delta)) - p.ratio_bits)
         f = lambda x: np.cos((2 * np.pi * p.K * x - np.pi / 2) / 2**p.r)  # noqa: E731
         self.coeffs = [float(v) for v in np.polynomial.chebyshev.chebinterpolate(f, p.degree)]
 
     def _transform(self, x, stride, diags, factor, out_scale=None):
         """x -> sum_o (factor diag_o) rot(x, o) (offsets o = d stride, |d| <= D): x rotated by -D stride, one BSGS
-        product with the diagonals shifted to 0 .. 2D, one rescale (the output at out_scale when given)."""
+        product with the diagonals shifted to 0 .. 2D (or folded mod S), one rescale (the output at out_scale when
+        given)."""
         ops, S = self.ops, self.p.slots
-        D, npts, bstep, _ = _group_plan(stride, diags)
+        D, npts, bstep, _ = _group_plan(stride, diags, S)
         top = x.top
         key = ("lt", stride, id(diags), top, float(x.scale), out_scale)
         lt = self.plan.get(key)
         if lt is None:
-            dl = [factor * diags.get((d - D) * stride, np.zeros(S, np.complex128)) for d in range(npts)]
+            dl = _plan_diagonals(stride, diags, S, factor)
             scale = float(self.primes[top]) if out_scale is None else out_scale * self.primes[top] / x.scale
             lt = self.plan[key] = ops.diagonals(dl, bstep, top=top, scale=scale, slots=S, stride=stride)
         y = ops.rotate(x, -D * stride) if D else x
@@ -271,7 +300,7 @@ class Bootstrapper:
             x = self._transform(x, stride, diags, f, out_scale=float(self.primes[x.top - 1]) if last else None)
         return x
 
-    def eval_mod(self, uv):
+    def eval_mod(self, uv, delta):
         ops, p, primes = self.ops, self.p, self.primes
         ch = Cheb(ops, self.plan, uv, primes)
         lev = ch.maxlev(p.degree)
@@ -280,7 +309,7 @@ class Bootstrapper:
             sq = _mul(ops, c, c)
             c = _add_const(ops, self.plan, ops.add(sq, sq), -1.0)
         # (q0 / 2 pi Delta) sin(2 pi t / q0) ~ t_msg / Delta: the factor taken into the scale
-        c.scale /= self.q0 / (2 * np.pi * self.delta)
+        c.scale /= self.q0 / (2 * np.pi * delta)
         return c
 
     def slot_to_coeff(self, w):
@@ -294,13 +323,17 @@ class Bootstrapper:
         ops, p, n = self.ops, self.p, self.p.n
         if ct.slots != p.slots:
             raise ValueError(f"bootstrapping takes full slots ({p.slots}), not {ct.slots}")
+        delta = self.delta
+        if self.boost:  # m -> 2^boost m at level 0 (exact; the noise grows by the same factor)
+            ct = ops.mult_pt(ct, ops.monomial(0, 0, 1 << self.boost), 1.0)
+            delta *= 1 << self.boost
         x = ops.mod_raise(ct, top)
         x.scale = p.K * self.q0  # slots: t / (K' q0) (after CoeffToSlot)
         w = self.coeff_to_slot(x)
         cw = ops.conjugate(w)
         u = ops.add(w, cw)                                                          # 2 Re w
         v = ops.mult_pt(ops.sub(w, cw), ops.monomial(3 * n // 2, w.top), 1.0)       # (w - conj w)(-i) = 2 Im w
-        uv = self.eval_mod(ops.stack([u, v]))
+        uv = self.eval_mod(ops.stack([u, v]), delta)
         u2, v2 = ops.split(uv, 2)
         w2 = ops.add(u2, ops.mult_pt(v2, ops.monomial(n // 2, v2.top), 1.0))        # u' + i v'
         return self.slot_to_coeff(w2)

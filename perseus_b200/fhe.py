@@ -86,6 +86,13 @@ def config2_chain():
     return Chain(16, tuple(ntt_primes(50, 16, 24)), tuple(ntt_primes(50, 16, 8, skip=24)), 3)
 
 
+def config4_chain():
+    """BASELINE config 4 (bootstrapping): N = 2^16, 29 x 50-bit Q primes (the refresh spends 16 levels and leaves 12
+    usable ones) + 11 x 50-bit special primes, dnum 3 (digits of 10 limbs: P one prime larger than a digit, so the
+    key-switch noise stays below the rescale rounding)."""
+    return Chain(16, tuple(ntt_primes(50, 16, 29)), tuple(ntt_primes(50, 16, 11, skip=29)), 3)
+
+
 def rotation_galois(step, log_n):
     """5^(step mod N/2) mod 2N (crates/pc-core/src/galois.rs:38-44)."""
     h = 1 << (log_n - 1)
@@ -444,12 +451,14 @@ class Session:
         return out
 
     def mod_raise(self, a, top):
-        """In place: a at level 0 raised to limbs 0..top (bootstrapping's ModRaise); decrypts to m + q_0 I."""
+        """a at level 0 raised to limbs 0..top in a new ciphertext (bootstrapping's ModRaise); decrypts to
+        m + q_0 I. pcb_mod_raise works in place on the copy's buffer; `a` is left as it was."""
         if a.top != 0:
             raise ValueError(f"mod_raise takes a level-0 ciphertext, not top {a.top}")
-        L.check(L.lib().pcb_mod_raise(self.ctx, a.ptr(), int(top), a.k, self._stream()), "pcb_mod_raise")
-        a.top = top
-        return a
+        out = Ct(self.empty(a.k), int(top), a.scale, a.slots)
+        out.data[:, :, 0].copy_(a.data[:, :, 0])
+        L.check(L.lib().pcb_mod_raise(self.ctx, out.ptr(), int(top), a.k, self._stream()), "pcb_mod_raise")
+        return out
 
     def automorph(self, a, g):
         """The automorphism X -> X^g of a (a key switch with the key of galois element g): g = 2N - 1 conjugates
@@ -467,17 +476,18 @@ class Session:
     def conjugate(self, a):
         return self.automorph(a, 2 * self.n - 1)
 
-    def monomial(self, power, top):
-        """X^power as a plaintext of scale 1 ([nq][N] evaluation rows): its slots are all zeta^(power 5^k); power
-        N / 2 multiplies every slot by i. mult_pt(a, monomial, 1.0) uses no level."""
-        key = ("monomial", int(power) % (2 * self.n), top)
+    def monomial(self, power, top, coef=1):
+        """coef X^power (coef an integer) as a plaintext of scale 1 ([nq][N] evaluation rows): its slots are all
+        coef zeta^(power 5^k); power N / 2 multiplies every slot by i, power 0 by the integer coef.
+        mult_pt(a, monomial, 1.0) uses no level."""
+        key = ("monomial", int(power) % (2 * self.n), top, int(coef))
         cache = self.__dict__.setdefault("_monomials", {})
         if key not in cache:
             pw = int(power) % (2 * self.n)
             rows = np.zeros((top + 1, self.n), np.uint64)
             for r in range(top + 1):
                 q = self.chain.q[r]
-                rows[r, pw % self.n] = 1 if pw < self.n else q - 1  # X^N = -1
+                rows[r, pw % self.n] = (int(coef) if pw < self.n else -int(coef)) % q  # X^N = -1
             dev = torch.zeros((self.nq, self.n), dtype=torch.int64, device=self.device)
             L.check(L.lib().pcb_pt_load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(dev.data_ptr()),
                                         self._stream()), "pcb_pt_load")

@@ -88,9 +88,7 @@ class OracleOps:
     @_batched
     def mod_raise(self, a, top):
         assert a.top == 0
-        a.data = self.c.mod_raise(a.data, top)
-        a.top = top
-        return a
+        return OCt(self.c.mod_raise(a.data, top), top, a.scale, a.slots)
 
     @_batched
     def automorph(self, a, g):
@@ -104,13 +102,13 @@ class OracleOps:
     def conjugate(self, a):
         return self.automorph(a, 2 * self.c.n - 1)
 
-    def monomial(self, power, top):
-        """X^power in coefficient form (rows 0..top) for mult_pt with scale 1."""
+    def monomial(self, power, top, coef=1):
+        """coef X^power in coefficient form (rows 0..top) for mult_pt with scale 1."""
         n = self.c.n
         pw = int(power) % (2 * n)
         rows = np.zeros((top + 1, n), np.uint64)
         for r in range(top + 1):
-            rows[r, pw % n] = 1 if pw < n else self.c.q[r] - 1
+            rows[r, pw % n] = (int(coef) if pw < n else -int(coef)) % self.c.q[r]
         return rows
 
     @_batched

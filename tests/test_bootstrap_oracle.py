@@ -34,18 +34,18 @@ def _bitrev(v):
 @pytest.fixture(scope="module")
 def ctx():
     q = O.ntt_primes(50, LOGN, 20)
-    p = O.ntt_primes(50, LOGN, 5, skip=20)
-    prm = BS.Params(N, K=24, r=3, per_group=3)
-    gal = list(dict.fromkeys([1] + [fhe.rotation_galois(s, LOGN) for s in BS.rot_steps(prm)] + [BS.conj_galois(N)]))
+    p = O.ntt_primes(50, LOGN, 6, skip=20)  # P one prime larger than a digit of 5
+    steps = sorted(set(BS.rot_steps(BS.Params(N, per_group=3))) | set(BS.rot_steps(BS.Params(N, per_group=5))))
+    gal = list(dict.fromkeys([1] + [fhe.rotation_galois(s, LOGN) for s in steps] + [BS.conj_galois(N)]))
     c = O.Ctx(LOGN, q, p, 4)
     c.keygen(seed=0, h=64, sigma=3.2, galois=gal)
-    return c, prm
+    return c
 
 
 @pytest.mark.parametrize("per", [2, 3, 4])
 def test_stage_groups_are_the_encoders_fft(ctx, per):
     """Slots = F(bitrev(w)) for w_i = (c_i + i c_(i+S)) / scale of the oracle's own encoding; G = S F^-1."""
-    c, _ = ctx
+    c = ctx
     rng = np.random.default_rng(per)
     z = rng.uniform(-1, 1, S) + 1j * rng.uniform(-1, 1, S)
     scale = 2.0**40
@@ -59,15 +59,19 @@ def test_stage_groups_are_the_encoders_fft(ctx, per):
     assert len(F) == len(G) == -(-int(math.log2(S)) // per)
 
 
-def test_bootstrap_refreshes_a_level0_ciphertext(ctx):
-    c, prm = ctx
+@pytest.mark.parametrize("per", [3, 5])
+def test_bootstrap_refreshes_a_level0_ciphertext(ctx, per):
+    """per 5 at this ring: a group of 63 offsets over 32 distinct rotations, folded mod S."""
+    c = ctx
+    prm = BS.Params(N, K=24, r=3, per_group=per)
     ops = OracleOps(c)
     rng = np.random.default_rng(5)
     z = rng.uniform(-1, 1, S)
     ct = ops.encrypt(z, 0, 2.0**40, S)
     bt = BS.Bootstrapper(ops, prm, c.q, c.q[0], 2.0**40)
     out = bt(ct, len(c.q) - 1)
-    assert out.top == len(c.q) - 1 - (3 + 7 + prm.r + 3)  # CoeffToSlot 3, EvalMod 7 + r, SlotToCoeff 3 levels
+    ng = len(BS.groups(N, True, per))  # CoeffToSlot and SlotToCoeff: one level per group; EvalMod 7 + r
+    assert out.top == len(c.q) - 1 - (ng + 7 + prm.r + ng)
     got = ops.decrypt_slots(out)
     assert np.abs(got.real - z).max() < 1e-4 and np.abs(got.imag).max() < 1e-4
     # the refreshed ciphertext computes: one more product at its level

@@ -4,8 +4,11 @@ conjugation, EvalMod, SlotToCoeff):
 - at N = 2^14 (8192 slots, 20 + 5 limbs) the refreshed ciphertext equals the oracle's word for word, both run on the
   same level-0 ciphertext with the same keys, and decrypts to the input slots;
 - BASELINE config 4 at its size: N = 2^16 with full slots (2^15), uniform [-1, 1] slot values (seeded) at level 0,
-  refreshed to 12 usable levels (29 + 10 limbs of 50 bits, secret of Hamming weight 192), decrypting within 1e-3.
+  refreshed to 12 usable levels (29 + 11 limbs of 50 bits, secret of Hamming weight 192), decrypting within 1e-3
+  absolute of the input slots; one product of the refreshed ciphertext with itself within 1e-3 of z^2.
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -22,8 +25,7 @@ def host(t):
     return t.detach().cpu().numpy().view(np.uint64)
 
 
-def session(logn, nq, kp, dnum, prm, h):
-    ch = fhe.Chain(logn, tuple(fhe.ntt_primes(50, logn, nq)), tuple(fhe.ntt_primes(50, logn, kp, skip=nq)), dnum)
+def session(ch, prm, h):
     s = fhe.Session(ch, rot_steps=BS.rot_steps(prm), k_max=2, seed=0, h=h, sigma=3.2,
                     galois_extra=(BS.conj_galois(ch.n),))
     return ch, s
@@ -32,7 +34,9 @@ def session(logn, nq, kp, dnum, prm, h):
 def test_bootstrap_bit_exact_with_the_oracle():
     logn = 14
     prm = BS.Params(1 << logn, K=24, r=3, per_group=5)
-    ch, s = session(logn, 20, 5, 4, prm, h=64)
+    ch = fhe.Chain(logn, tuple(fhe.ntt_primes(50, logn, 20)), tuple(fhe.ntt_primes(50, logn, 6, skip=20)), 4)
+    ch, s = session(ch, prm, h=64)
+    O.lib().orc_set_threads(os.cpu_count() or 1)
     o = O.Ctx(ch.log_n, ch.q, ch.p, ch.dnum)
     o.keygen(0, 64, 3.2, s.galois)
     oo = OracleOps(o)
@@ -54,12 +58,15 @@ def test_bootstrap_bit_exact_with_the_oracle():
 def test_bootstrap_config4():
     logn = 16
     prm = BS.Params(1 << logn, K=24, r=3, per_group=5)
-    ch, s = session(logn, 29, 10, 3, prm, h=192)
+    ch, s = session(fhe.config4_chain(), prm, h=192)
     rng = np.random.default_rng(4)
     z = rng.uniform(-1, 1, prm.slots)
     ct = s.encrypt(z, top=0, scale=2.0**40, slots=prm.slots)
-    out = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)(ct, len(ch.q) - 1)
+    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)
+    out = bt(ct, len(ch.q) - 1)
     assert out.top == 12  # 12 usable levels above the bottom limb
+    again = bt(ct, len(ch.q) - 1)  # the input is left as it was; the refresh is deterministic
+    assert ct.top == 0 and torch.equal(again.data[:, :, : out.top + 1], out.data[:, :, : out.top + 1])
     got = s.decrypt_slots(out)
     assert np.abs(got.real - z).max() < 1e-3 and np.abs(got.imag).max() < 1e-3
     sq = s.rescale_one(s.mult(out, out))

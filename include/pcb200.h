@@ -394,6 +394,10 @@ uint64_t pcb_launch_count(void);
  * since the library was loaded: 0 in normal operation; a nonzero count means a copy never completed and the affected
  * rows were left untransformed (synchronizes the device). No counterpart in the reference. */
 uint32_t pcb_device_timeouts(void);
+/* Measurement: iters x 8 dependent-chain FP64 FMAs on every thread of 4 x 256-thread blocks per SM, on stream s; returns
+ * the FMA count (negative: a cudaError_t). Timed by the caller with CUDA events, it gives the FP64 pipe's throughput
+ * (the denominator of the benchmark's FP64 fractions). `sink`: one double per block. No counterpart in the reference. */
+int64_t pcb_fp64_fma_loop(double* sink, int32_t iters, cudaStream_t s);
 
 /* ================================================================ 2. evaluator */
 

@@ -208,6 +208,7 @@ def lib():
         "pcb_last_error": (C.c_char_p, []),
         "pcb_launch_count": (C.c_uint64, []),
         "pcb_device_timeouts": (C.c_uint32, []),
+        "pcb_fp64_fma_loop": (C.c_int64, [vp, i32, vp]),
         "pcb_ctx_bytes": (i64, [C.POINTER(Params), i32]),
         "pcb_ctx_create": (C.c_int, [C.POINTER(Params), i32, vp, C.c_size_t, vp, C.POINTER(vp)]),
         "pcb_ctx_destroy": (None, [vp]),

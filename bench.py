@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="ciphertexts per GPU (profiling cases only)")
     ap.add_argument("--profile", action="store_true",
                     help="the timed steps only (no e2e, plain-rotation, attention or CPU legs): the ncu case")
-    ap.add_argument("--part", choices=["all", "projection", "attention", "block", "bootstrap"], default="all",
+    ap.add_argument("--part", choices=["all", "projection", "attention", "block", "bootstrap", "model"],
+                    default="all",
                     help="projection / attention: only that timing (one GPU; the timed steps in the NVTX range "
                          "'projection_step' / 'attention_step', the ncu case)")
     return ap.parse_args()
@@ -382,6 +383,7 @@ def run_ours(a):
     blk = block_decode(a, world, barrier, dist)
     blk["batch_of_4"] = block_decode(a, world, barrier, dist, seqs=4)
     bts = bootstrap(a, world, barrier, dist)
+    mdl = model_decode(a, world, barrier, dist)
     if rank == 0:
         line = {
             "metric": METRIC, "value": ks / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
@@ -418,6 +420,7 @@ def run_ours(a):
             "projection": proj,
             "attention_block": blk,
             "bootstrap": bts,
+            "model_decode": mdl,
         }
         if world == 1 and not a.no_cpu_baseline:
             try:
@@ -654,7 +657,7 @@ def bootstrap(a, world, barrier, dist):
                     galois_extra=(BS.conj_galois(ch.n),))
     z = np.random.default_rng(12).uniform(-1, 1, prm.slots)
     ct = s.encrypt(z, top=0, scale=2.0**40, slots=prm.slots)
-    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)
+    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0])
     top = len(ch.q) - 1
     out = None
     for _ in range(max(a.warmup, 3)):
@@ -687,8 +690,100 @@ def bootstrap(a, world, barrier, dist):
     return res
 
 
+def model_decode(a, world, barrier, dist):
+    """Config 5: GPT-2 small's 12 layers decoded on encrypted activations (perseus_b200.model: LayerNorm, attention
+    over a 256-token encrypted cache per layer resident in HBM, MLP with the polynomial GELU, residuals, 4 refreshes
+    per layer), N = 2^16 on config 4's chain, random-init weights N(0, 0.02); the caches start with client-encrypted
+    tokens and grow by one per token. One warm-up token (it also encodes every plaintext once), then `steps` tokens
+    (at most 4) timed with CUDA events (max over ranks), the last decrypted against the fp64 decode. On N GPUs every
+    layer's 8 cache blocks are split over the ranks (one all_gather of the partial attention outputs per layer)."""
+    import numpy as np
+    import torch
+
+    from perseus_b200 import bootstrap as BS
+    from perseus_b200 import fhe
+    from perseus_b200 import linear as LIN
+    from perseus_b200 import model as M
+
+    cfg = M.ModelCfg()
+    ch = fhe.config4_chain()
+    prm = BS.Params(ch.n, K=24, r=3, per_group=5)
+    lay = M.B.layout(ch.n // 2, cfg.width, cfg.heads, cfg.head_dim, cfg.tokens, cfg.radix_bits)
+    steps_rot = sorted(set(BS.rot_steps(prm)) | set(lay.rot_steps()))
+    s = fhe.Session(ch, rot_steps=steps_rot, k_max=lay.blocks, seed=0, h=192, sigma=3.2,
+                    galois_extra=(BS.conj_galois(ch.n),))
+    rng = np.random.default_rng(13)
+    weights = [M.random_layer(rng) for _ in range(cfg.layers)]
+    warm, steps = 1, max(1, min(a.steps, 4))
+    pre = cfg.tokens - warm - steps
+    Ks = [rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(cfg.layers)]
+    Vs = [rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(cfg.layers)]
+    shard_ = (world, int(os.environ.get("RANK", "0"))) if world > 1 else None
+    dec = M.Decoder(s, cfg, weights, ch.q, BS.Bootstrapper(s, prm, ch.q, ch.q[0]), shard=shard_)
+    dec.load(Ks, Vs)
+    plain = [[K.copy(), V.copy()] for K, V in zip(Ks, Vs)]
+    xs = [rng.normal(0, 1, cfg.d) for _ in range(warm + steps)]
+    cts = [s.encrypt(LIN.input_vector(x, lay.geo), top=0, scale=2.0**40, slots=lay.slots) for x in xs]
+    y = None
+    for i in range(warm):
+        y = dec.decode(cts[i])
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("model_step")
+    e0.record()
+    for i in range(warm, warm + steps):
+        y = dec.decode(cts[i])
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    want = None
+    for x in xs:
+        want = M.plain_decode(x, weights, plain, cfg, dec.coeffs)
+    got = LIN.output_values(s.decrypt_slots(y).real, lay.geo, cfg.d)
+    err = float(np.abs(got - want).max())
+    res = {"workload": "config 5: GPT-2 small, 12 layers (768 wide, 12 heads x 64, MLP 3072), one token per step, "
+                       "a 256-token encrypted KV cache per layer in HBM (8 blocks x 32 tokens), N=2^16 on 29+11 x "
+                       "50-bit limbs, 4 refreshes (bootstraps) per layer, degree-7 polynomial LayerNorm / softmax / "
+                       "GELU, eager",
+           "ms_per_token": t.item(), "timed_tokens": steps, "refreshes_per_token": 4 * cfg.layers,
+           "max_abs_err_vs_fp64": err, "max_abs_value": float(np.abs(want).max()),
+           "sharding": f"every layer's cache blocks over {world} GPU(s)" if world > 1 else "one GPU"}
+    del s, dec, cts, y
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     a = parse()
+    if a.part == "model":  # under torchrun every layer's cache blocks are split over the ranks (rank 0 prints)
+        import torch
+
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+
+        def barrier():
+            if dist:
+                dist.barrier()
+
+        out = {"part": "model", "n_gpus": world, **model_decode(a, world, barrier, dist)}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if a.part == "bootstrap":
         print(json.dumps({"part": "bootstrap", **bootstrap(a, 1, lambda: None, None)}), flush=True)
         return

@@ -274,11 +274,13 @@ def _linear(ops, cache, name, W, b, top, scale):
     return lin
 
 
-def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
+def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False, out_scale=None, residual_to=None):
     """One token: x_ct the activation (projection layout; a batch of cache.seqs, one per sequence), w the block's
     Weights (with norm: gamma and beta folded in by fold_norm). With norm the activation is layer-normalized first (8
     levels); it must then sit at the cache's level + 10, else + 2. Pushes the token's K and V into the cache and
-    returns the block's output (projection layout), plus the activation itself with residual."""
+    returns the block's output (projection layout), plus the activation itself with residual, or plus `residual_to`
+    (another ciphertext, e.g. the stream before a refreshed norm) when given. out_scale: the output projection lands
+    there (the residual's scale, so the sum is exact), else at its input's scale."""
     lay = cache.lay
     rb = lay.radix_bits
     x_in = x_ct
@@ -309,9 +311,17 @@ def decode(ops, x_ct, w, cache, coeffs, primes, norm=None, residual=False):
         y = SH.gather_sum(ops, y, cache.shard[2])
     # the lane sums leave partial sums in lanes 1 .. t-1; the projection's replication ladder needs them zero
     y = _masked(ops, cache.plan, y, lay.lane0(), y.scale, primes)
-    lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)
+    if out_scale is None:
+        lin_o = _linear(ops, cache, "o", w.wo, w.bo, y.top, y.scale)
+    else:
+        key = ("linear", "o", y.top, float(y.scale), float(out_scale))
+        lin_o = cache.plan.get(key)
+        if lin_o is None:
+            lin_o = cache.plan[key] = LIN.encode(ops, w.wo, lay.geo, y.top, y.scale, bias=w.bo, out_scale=out_scale)
     out = LIN.linear(ops, y, lin_o, rb)
-    if residual:  # x + block(x): the scales agree to the last bits (both ~2^40), the sum takes the output's
+    if residual_to is not None:
+        out = ops.add(out, ops.drop_to(residual_to, out.top))
+    elif residual:  # x + block(x): the scales agree to the last bits (both ~2^40), the sum takes the output's
         out = ops.add(out, ops.drop_to(x_in, out.top))
     return out
 

@@ -264,26 +264,33 @@ class Cheb:
 class Bootstrapper:
     """The encoded CoeffToSlot / SlotToCoeff diagonals and EvalMod coefficients of one chain, and the refresh."""
 
-    def __init__(self, ops, p, primes, q0, delta):
-        self.ops, self.p, self.primes, self.q0, self.delta = ops, p, list(primes), float(q0), float(delta)
+    def __init__(self, ops, p, primes, q0):
+        self.ops, self.p, self.primes, self.q0 = ops, p, list(primes), float(q0)
         self.plan = {}
         self.cts = groups(p.n, True, p.per_group)
         self.stc = groups(p.n, False, p.per_group)
-        self.boost = max(0, round(math.log2(self.q0 / self.delta)) - p.ratio_bits)
         f = lambda x: np.cos((2 * np.pi * p.K * x - np.pi / 2) / 2**p.r)  # noqa: E731
         self.coeffs = [float(v) for v in np.polynomial.chebyshev.chebinterpolate(f, p.degree)]
 
-    def _transform(self, x, stride, diags, factor, out_scale=None):
+    @property
+    def levels(self):
+        """Levels one refresh spends: one per CoeffToSlot and SlotToCoeff group, 7 + r in EvalMod."""
+        return len(self.cts) + 7 + self.p.r + len(self.stc)
+
+    def _transform(self, x, stride, diags, factor, out_scale=None, out_mask=None):
         """x -> sum_o (factor diag_o) rot(x, o) (offsets o = d stride, |d| <= D): x rotated by -D stride, one BSGS
         product with the diagonals shifted to 0 .. 2D (or folded mod S), one rescale (the output at out_scale when
         given)."""
         ops, S = self.ops, self.p.slots
         D, npts, bstep, _ = _group_plan(stride, diags, S)
         top = x.top
-        key = ("lt", stride, id(diags), top, float(x.scale), out_scale)
+        key = ("lt", stride, id(diags), top, float(x.scale), out_scale, None if out_mask is None else id(out_mask))
         lt = self.plan.get(key)
         if lt is None:
             dl = _plan_diagonals(stride, diags, S, factor)
+            if out_mask is not None:  # output slot j of every diagonal times mask[j]: the masked transform
+                dl = [d * out_mask for d in dl]
+                self.plan[("mask", id(out_mask))] = out_mask  # kept alive with the entry keyed by its id
             scale = float(self.primes[top]) if out_scale is None else out_scale * self.primes[top] / x.scale
             lt = self.plan[key] = ops.diagonals(dl, bstep, top=top, scale=scale, slots=S, stride=stride)
         y = ops.rotate(x, -D * stride) if D else x
@@ -312,21 +319,27 @@ class Bootstrapper:
         c.scale /= self.q0 / (2 * np.pi * delta)
         return c
 
-    def slot_to_coeff(self, w):
+    def slot_to_coeff(self, w, out_mask=None):
+        """The forward stages; out_mask (a slot vector) multiplies the output slots, folded into the last group."""
         x = w
-        for stride, diags in self.stc:
-            x = self._transform(x, stride, diags, 1.0)
+        for gi, (stride, diags) in enumerate(self.stc):
+            last = gi == len(self.stc) - 1
+            x = self._transform(x, stride, diags, 1.0, out_mask=out_mask if last else None)
         return x
 
-    def __call__(self, ct, top):
-        """ct at level 0 (scale Delta, full slots) -> a ciphertext of the same slots at a higher level."""
+    def __call__(self, ct, top, out_mask=None):
+        """ct at level 0 (full slots; its scale is Delta) -> a ciphertext of the same slots at level `top` minus the
+        refresh's levels; out_mask (a slot vector) multiplies the output slots at no level."""
         ops, p, n = self.ops, self.p, self.p.n
         if ct.slots != p.slots:
             raise ValueError(f"bootstrapping takes full slots ({p.slots}), not {ct.slots}")
-        delta = self.delta
-        if self.boost:  # m -> 2^boost m at level 0 (exact; the noise grows by the same factor)
-            ct = ops.mult_pt(ct, ops.monomial(0, 0, 1 << self.boost), 1.0)
-            delta *= 1 << self.boost
+        delta = float(ct.scale)
+        if self.q0 / delta < 8.0:
+            raise ValueError(f"a level-0 scale of 2^{math.log2(delta):.1f} leaves the message no room below q0")
+        boost = max(0, round(math.log2(self.q0 / delta)) - p.ratio_bits)
+        if boost:  # m -> 2^boost m at level 0 (exact; the noise grows by the same factor)
+            ct = ops.mult_pt(ct, ops.monomial(0, 0, 1 << boost), 1.0)
+            delta *= 1 << boost
         x = ops.mod_raise(ct, top)
         x.scale = p.K * self.q0  # slots: t / (K' q0) (after CoeffToSlot)
         w = self.coeff_to_slot(x)
@@ -336,4 +349,4 @@ class Bootstrapper:
         uv = self.eval_mod(ops.stack([u, v]), delta)
         u2, v2 = ops.split(uv, 2)
         w2 = ops.add(u2, ops.mult_pt(v2, ops.monomial(n // 2, v2.top), 1.0))        # u' + i v'
-        return self.slot_to_coeff(w2)
+        return self.slot_to_coeff(w2, out_mask)

@@ -394,7 +394,7 @@ class Session:
         diags = [np.asarray(v) for v in diags]
         slots = slots or len(diags[0])
         scale = float(self.chain.q[top]) if scale is None else scale
-        pts = torch.zeros((len(diags), self.nq, self.n), dtype=torch.int64, device=self.device)
+        pts = torch.zeros((len(diags), top + 1, self.n), dtype=torch.int64, device=self.device)  # rows 0..top read
         for d, v in enumerate(diags):
             g = (d // bstep) * bstep * stride
             rows = self.encode(np.roll(v, g), slots=slots, scale=scale, top=top)

@@ -112,14 +112,16 @@ class Linear:
     bias_scale: float
 
 
-def encode(ops, W, geo, top, x_scale, bias=None):
-    """Encode W (and b) for inputs at level `top` and scale x_scale: R plaintexts at q_top, the bias at level top - 1
-    and the output scale x_scale."""
-    lt = ops.diagonals(weight_vectors(W, geo), geo.bstep, top=top, slots=geo.slots, stride=geo.stride)
+def encode(ops, W, geo, top, x_scale, bias=None, out_scale=None):
+    """Encode W (and b) for inputs at level `top` and scale x_scale: R plaintexts at q_top, the bias at level top - 1;
+    the output lands at x_scale, or at out_scale when given (the plaintexts encoded at out_scale q_top / x_scale)."""
+    pscale = None if out_scale is None else out_scale * ops.chain.q[top] / x_scale
+    lt = ops.diagonals(weight_vectors(W, geo), geo.bstep, top=top, scale=pscale, slots=geo.slots, stride=geo.stride)
+    y_scale = x_scale if out_scale is None else out_scale
     bpt = None
     if bias is not None:
-        bpt = ops.pt(bias_vector(bias, geo), top - 1, x_scale, geo.slots)
-    return Linear(geo, lt, bpt, x_scale)
+        bpt = ops.pt(bias_vector(bias, geo), top - 1, y_scale, geo.slots)
+    return Linear(geo, lt, bpt, y_scale)
 
 
 def prepare(ops, x, geo, radix_bits=1):

@@ -85,6 +85,11 @@ class OracleOps:
         assert a.top == b.top
         return OCt(self.c.sub(a.data, b.data, a.top), a.top, a.scale, a.slots)
 
+    @property
+    def chain(self):
+        """The prime chain (`q`, `p`) as the session's."""
+        return self.c
+
     @_batched
     def mod_raise(self, a, top):
         assert a.top == 0

@@ -68,7 +68,7 @@ def test_bootstrap_refreshes_a_level0_ciphertext(ctx, per):
     rng = np.random.default_rng(5)
     z = rng.uniform(-1, 1, S)
     ct = ops.encrypt(z, 0, 2.0**40, S)
-    bt = BS.Bootstrapper(ops, prm, c.q, c.q[0], 2.0**40)
+    bt = BS.Bootstrapper(ops, prm, c.q, c.q[0])
     out = bt(ct, len(c.q) - 1)
     ng = len(BS.groups(N, True, per))  # CoeffToSlot and SlotToCoeff: one level per group; EvalMod 7 + r
     assert out.top == len(c.q) - 1 - (ng + 7 + prm.r + ng)

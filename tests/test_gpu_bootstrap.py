@@ -45,8 +45,8 @@ def test_bootstrap_bit_exact_with_the_oracle():
     ct = s.encrypt(z, top=0, scale=2.0**40, slots=prm.slots)
     oc = OCt(host(ct.data[0]).copy(), 0, ct.scale, ct.slots)
     top = len(ch.q) - 1
-    out = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)(ct, top)
-    oout = BS.Bootstrapper(oo, prm, ch.q, ch.q[0], 2.0**40)(oc, top)
+    out = BS.Bootstrapper(s, prm, ch.q, ch.q[0])(ct, top)
+    oout = BS.Bootstrapper(oo, prm, ch.q, ch.q[0])(oc, top)
     torch.cuda.synchronize()
     oout = oout.cts[0] if hasattr(oout, "cts") else oout
     assert out.top == oout.top == top - 16
@@ -62,7 +62,7 @@ def test_bootstrap_config4():
     rng = np.random.default_rng(4)
     z = rng.uniform(-1, 1, prm.slots)
     ct = s.encrypt(z, top=0, scale=2.0**40, slots=prm.slots)
-    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0], 2.0**40)
+    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0])
     out = bt(ct, len(ch.q) - 1)
     assert out.top == 12  # 12 usable levels above the bottom limb
     again = bt(ct, len(ch.q) - 1)  # the input is left as it was; the refresh is deterministic

@@ -312,6 +312,16 @@ typedef struct PcbKskGenArgs {
     int32_t nrows, ndig, nq, bits, sq, pad;
 } PcbKskGenArgs;
 
+/* args.cuh:656-663: packed key rows -> dense rows, out[r][i] = value i of packed row r (in + r row_words), r < nrows.
+ * Values are `bits` bits LSB first (the wire format's pack_row order); the reference's u64 table takes bits 1..32, this
+ * one 1..64 (a 50-bit residue of these chains packs at 50). */
+typedef struct PcbKskUnpackArgs {
+    void* out;
+    const uint32_t* in;
+    uint64_t row_words;
+    int32_t nrows, bits;
+} PcbKskUnpackArgs;
+
 /* args.cuh:665-677: composite ModRaise, coefficient form: for rows t in [r0, r1) of K ciphertexts (nparts polynomials
  * from part 0), x[t] = sum_{k < d} centred([x_k qhatinv_k]_{q_k}) qhat[k][t] mod q_t, the sources x_k = rows 0..d-1
  * of the same polynomial (d <= 4, t < 64; the sources are not written). d = 1, qhatinv = qhat = 1: the level-0 raise
@@ -353,7 +363,7 @@ typedef struct PcbKernelTable {
     PcbLaunch encode;
     int (*encrypt)(const PcbEncryptArgs*, cudaStream_t);
     int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
-    PcbLaunch ksk_unpack;
+    int (*ksk_unpack)(const PcbKskUnpackArgs*, cudaStream_t);
     int (*mod_raise)(const PcbModRaiseArgs*, cudaStream_t);
     PcbLaunch small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
     int (*ks_dot_key)(const PcbKsKeyArgs*, cudaStream_t);
@@ -387,6 +397,9 @@ const PcbKernelTable* pc_table_u64_barrett64(void);
 /* replaces `pc_ring_u64_<log_n>` of crates/pc-kernels/kernels/args.cuh:1099-1104 at log_n 14 and 16 */
 const PcbRingTable* pc_ring_u64_14(void);
 const PcbRingTable* pc_ring_u64_16(void);
+/* The full 52-launcher table at log_n 14 or 16 (NULL otherwise): the reference builds one table per ring size
+ * (PC_LOGN at compile time); this library carries both. pcb_kernel_table(16) == pc_table_u64_barrett64(). */
+const PcbKernelTable* pcb_kernel_table(int32_t log_n);
 
 /* Kernels this library has launched since it was loaded (all threads, all devices). */
 uint64_t pcb_launch_count(void);
@@ -451,6 +464,14 @@ int pcb_key_ptrs(const PcbCtx* ctx, int32_t idx, const uint64_t** b, const uint6
 /* Copy key `idx` (b then a, [dnum][nq + kp][N] words each) into caller device buffers on `stream` (a regenerated
  * key's a is expanded from its seed). */
 int pcb_key_copy(const PcbCtx* ctx, int32_t idx, uint64_t* b_out, uint64_t* a_out, cudaStream_t stream);
+/* The 8-word KSKB seed key `idx`'s `a` is drawn from (host copy; synchronizes). */
+int pcb_key_seed(const PcbCtx* ctx, int32_t idx, uint32_t* seed8);
+/* Load key `idx` from a client's material (a key bundle's Ksk entry, crates/pc-client/src/wire.rs:78-85): its galois
+ * element (1: relinearization), b ([dnum][nq + kp][N] words, device or host) and the seed of its a (KSKA: the frozen
+ * ChaCha12 lane; a dense context expands a once here, a regenerating one keeps the seed). Keys load in order: idx is
+ * at most the number already loaded or generated; no secret is needed (a server context). Synchronizes `stream`. */
+int pcb_key_load(PcbCtx* ctx, int32_t idx, uint64_t galois, const uint64_t* b, const uint32_t* seed8,
+                 cudaStream_t stream);
 
 /* Secret-key encryption of nvals (re, im) values into nslots slots at `scale`, rows 0..=top of ct (device). */
 int pcb_encrypt(PcbCtx* ctx, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
@@ -537,6 +558,38 @@ int pcb_linear_transform_multi(PcbCtx* ctx, const uint64_t* x, const uint64_t* c
  * with d = 1), back in evaluation form. In place; the ciphertext then decrypts to m + q_0 I with small integer I. */
 int pcb_mod_raise(PcbCtx* ctx, uint64_t* ct, int32_t top_out, int32_t K, cudaStream_t stream);
 
+/* ================================================================ 3. wire format (crates/pc-client/src/wire.rs) */
+
+/* The compressed ciphertext frame's payload (wire.rs CtHeader::bits, pack_coeffs + pack_bits per part, as
+ * crates/pc-py/src/client.rs:596-612 export_ct(bits=) writes it): rows 0..=top (1 or 2 limbs) of both parts of ct
+ * (device, evaluation form) to coefficient form, each coefficient's CRT x in [0, Q) as round(x 2^bits / Q) mod
+ * 2^bits, packed LSB first: out (device) = part 0's N bits / 32 words, then part 1's. bits 1..64 with the primes'
+ * bits + bits <= 127. The rounding is exact (the reference's exact path; its f64 shortcut serves only two primes with
+ * Q < 2^63, which these chains never have). */
+int pcb_ct_compress(PcbCtx* ctx, const uint64_t* ct, int32_t top, int32_t bits, uint32_t* out, cudaStream_t stream);
+
+/* wire.rs:12-25 sum64: FNV-1a over little-endian u64 words (a trailing odd u32 word widened). */
+uint64_t pcb_wire_sum64(const uint32_t* words, size_t n);
+/* wire.rs packed_words: ceil(n bits / 32). */
+size_t pcb_wire_packed_words(size_t n, int32_t bits);
+/* wire.rs:124-128 packed_row_words: n bits / 32 + 1 (a zero guard word), padded to a multiple of 4. */
+size_t pcb_wire_packed_row_words(size_t n, int32_t bits);
+/* wire.rs pack_bits / unpack_bits: n values of `bits` (1..64) bits LSB first (values masked to `bits`); unpack reads
+ * at most in_words words. 0, or -1 on a bad argument. */
+int pcb_wire_pack_bits(const uint64_t* v, size_t n, int32_t bits, uint32_t* out);
+int pcb_wire_unpack_bits(const uint32_t* in, size_t in_words, size_t n, int32_t bits, uint64_t* out);
+/* wire.rs:137-150 pack_row, widened to values of up to 64 bits: the values packed, the rest of out (out_words >=
+ * pcb_wire_packed_row_words) zero. pcb_wire_unpack_bits reads a row back (wire.rs unpack_row). */
+int pcb_wire_pack_row(const uint64_t* v, size_t n, int32_t bits, uint32_t* out, size_t out_words);
+/* wire.rs:42-74 frame header: magic (4 bytes), version 1 (u32 LE), JSON length (u64 LE), the JSON. write returns the
+ * bytes written (16 + len) or -1; read returns the JSON's offset (16) and its length, or -1 (short), -2 (magic),
+ * -3 (version), -4 (length above 1 GiB or past the buffer). */
+int64_t pcb_wire_write_header(const char* magic, const uint8_t* json, uint64_t len, uint8_t* out, uint64_t cap);
+int64_t pcb_wire_read_header(const uint8_t* buf, uint64_t n, const char* magic, uint64_t* json_len);
+/* wire.rs:405-410 unpack_coeffs (the client's side of a compressed frame): rows[r][i] = round(y_i Q / 2^bits) mod
+ * q[r] for nq = 1..2 primes below 2^63. 0, or -1 on a bad argument. */
+int pcb_wire_unpack_coeffs(const uint64_t* q, int32_t nq, const uint64_t* y, size_t n, int32_t bits, uint64_t* rows);
+
 /* The hybrid key switch of one polynomial per ciphertext (the north star's fused KeySwitcher): ext = dot(ModUp(d))
  * against key `kidx` with c0 mode (0 none, 1 P c0 on Q rows) and output permutation autok, then ModDown into out.
  * d, c0: rows 0..=top of K polynomials `in_stride` words apart; out: K ciphertexts. */
@@ -571,6 +624,7 @@ static_assert(sizeof(PcbRescaleCombineArgs) == 80, "RescaleCombineArgs layout");
 static_assert(sizeof(PcbAutomorphArgs) == 112, "AutomorphArgs layout");
 static_assert(sizeof(PcbEncryptArgs) == 64, "EncryptArgs layout");
 static_assert(sizeof(PcbKskGenArgs) == 120, "KskGenArgs layout");
+static_assert(sizeof(PcbKskUnpackArgs) == 32, "KskUnpackArgs layout");
 static_assert(sizeof(PcbModRaiseArgs) == 2136, "ModRaiseArgs layout");
 static_assert(sizeof(PcbPtDotArgs) == 128, "PtDotArgs layout");
 static_assert(sizeof(PcbAddConstArgs) == 48, "AddConstArgs layout");

@@ -144,6 +144,10 @@ class ModRaiseArgs(C.Structure):
                 ("r0", C.c_int32), ("r1", C.c_int32), ("nparts", C.c_int32), ("pad", C.c_int32)]
 
 
+class KskUnpackArgs(C.Structure):
+    _fields_ = [("out", vp), ("in_", vp), ("row_words", C.c_uint64), ("nrows", C.c_int32), ("bits", C.c_int32)]
+
+
 class KskGenArgs(C.Structure):
     _fields_ = [("b", vp), ("a", vp), ("e", vp), ("s_new", vp), ("s_old", vp), ("seed", vp), ("ids", vp),
                 ("digit_of", vp), ("pmod", vp), ("pmods", vp), ("pr", vp), ("row_words", C.c_uint64),
@@ -182,7 +186,7 @@ class Params(C.Structure):
 SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJob": 32, "BconvArgs": 56,
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
-         "EncryptArgs": 64, "KskGenArgs": 120, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
+         "EncryptArgs": 64, "KskGenArgs": 120, "KskUnpackArgs": 32, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
          "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
 
 _lib = None
@@ -204,11 +208,24 @@ def lib():
     sig = {
         "pc_table_u64_barrett64": (C.POINTER(KernelTable), []),
         "pc_ring_u64_14": (C.POINTER(RingTable), []),
+        "pcb_kernel_table": (C.POINTER(KernelTable), [C.c_int32]),
         "pc_ring_u64_16": (C.POINTER(RingTable), []),
         "pcb_last_error": (C.c_char_p, []),
         "pcb_launch_count": (C.c_uint64, []),
         "pcb_device_timeouts": (C.c_uint32, []),
         "pcb_fp64_fma_loop": (C.c_int64, [vp, i32, vp]),
+        "pcb_key_seed": (C.c_int, [vp, i32, vp]),
+        "pcb_key_load": (C.c_int, [vp, i32, u64, vp, vp, vp]),
+        "pcb_ct_compress": (C.c_int, [vp, vp, i32, i32, vp, vp]),
+        "pcb_wire_sum64": (u64, [vp, C.c_size_t]),
+        "pcb_wire_packed_words": (C.c_size_t, [C.c_size_t, i32]),
+        "pcb_wire_packed_row_words": (C.c_size_t, [C.c_size_t, i32]),
+        "pcb_wire_pack_bits": (C.c_int, [vp, C.c_size_t, i32, vp]),
+        "pcb_wire_unpack_bits": (C.c_int, [vp, C.c_size_t, C.c_size_t, i32, vp]),
+        "pcb_wire_pack_row": (C.c_int, [vp, C.c_size_t, i32, vp, C.c_size_t]),
+        "pcb_wire_write_header": (i64, [C.c_char_p, vp, u64, vp, u64]),
+        "pcb_wire_read_header": (i64, [vp, u64, C.c_char_p, C.POINTER(C.c_uint64)]),
+        "pcb_wire_unpack_coeffs": (C.c_int, [vp, i32, vp, C.c_size_t, i32, vp]),
         "pcb_ctx_bytes": (i64, [C.POINTER(Params), i32]),
         "pcb_ctx_create": (C.c_int, [C.POINTER(Params), i32, vp, C.c_size_t, vp, C.POINTER(vp)]),
         "pcb_ctx_destroy": (None, [vp]),
@@ -256,8 +273,13 @@ def check(rc, what=""):
     return rc
 
 
-def kernel_table():
-    return lib().pc_table_u64_barrett64().contents
+def kernel_table(log_n=16):
+    if log_n == 16:
+        return lib().pc_table_u64_barrett64().contents
+    t = lib().pcb_kernel_table(log_n)
+    if not t:
+        raise ValueError(f"no kernel table at log n {log_n}")
+    return t.contents
 
 
 def ring_table(log_n):

@@ -1086,6 +1086,77 @@ int pcb_key_copy(const PcbCtx* c, int32_t idx, uint64_t* b_out, uint64_t* a_out,
     return 0;
 }
 
+int pcb_key_seed(const PcbCtx* c, int32_t idx, uint32_t* seed8) {
+    if (!c || !seed8 || idx < 0 || idx >= c->nkeys_made) return fail(PCB_BAD_ARGS, "no key %d", idx);
+    CK(cudaMemcpy(seed8, c->keys[idx].seed, 32, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int pcb_key_load(PcbCtx* c, int32_t idx, uint64_t galois, const uint64_t* b, const uint32_t* seed8, cudaStream_t s) {
+    if (!c || !b || !seed8) return fail(PCB_BAD_ARGS, "null argument");
+    if (idx < 0 || idx >= c->nkeys || idx > c->nkeys_made)
+        return fail(PCB_BAD_ARGS, "key %d: the context holds %d, %d loaded", idx, c->nkeys, c->nkeys_made);
+    const uint64_t two_n = 2 * (uint64_t)c->n;
+    if (!(galois % two_n & 1)) return fail(PCB_BAD_ARGS, "galois element %llu is even", (unsigned long long)galois);
+    for (int j = 0; j < c->nkeys_made; ++j)
+        if (j != idx && c->keys[j].galois == galois % two_n)
+            return fail(PCB_BAD_ARGS, "galois element %llu is key %d's", (unsigned long long)galois, j);
+    KeySlot& k = c->keys[idx];
+    k.galois = galois % two_n;
+    k.autok = hm::powmod(k.galois, (two_n >> 2) - 1, two_n);
+    const size_t bytes = (size_t)c->dnum * c->rows * c->n * 8;
+    CK(cudaMemcpyAsync(k.b, b, bytes, cudaMemcpyDefault, s));
+    std::vector<uint32_t> sd(seed8, seed8 + 8), ak{(uint32_t)k.autok};
+    CK(upload(k.seed, sd, s));
+    CK(upload(k.autok_dev, ak, s));
+    if (k.a) {  // dense key source: `a` expanded from the seed once, here
+        PcbKskExpandArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = k.a;
+        e.seed = k.seed;
+        e.prime_ids = c->key_rprime;
+        e.pr = c->pr;
+        e.nmod = c->rows;
+        e.dnum = c->dnum;
+        CK(c->tab->ksk_expand(&e, s));
+    }
+    CK(cudaStreamSynchronize(s));  // the seed and autok staging vectors end here
+    if (idx == c->nkeys_made) ++c->nkeys_made;
+    return 0;
+}
+
+int pcb_ct_compress(PcbCtx* c, const uint64_t* ct, int32_t top, int32_t bits, uint32_t* out, cudaStream_t s) {
+    if (!c || !ct || !out) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    const int k = top + 1;
+    int qbits = 0;
+    for (int r = 0; r < k; ++r) qbits += 64 - __builtin_clzll(c->primes[r]);
+    if (k > 2 || bits < 1 || bits > 64 || qbits + bits > 127)
+        return fail(PCB_BAD_ARGS, "%d bits over %d limbs (%d bits of modulus; at most 127 together, 2 limbs)", bits, k,
+                    qbits);
+    const size_t n = c->n;
+    // rows 0..top of both parts, coefficient form, in the workspace: part p row t at coef + (p k + t) N
+    for (int part = 0; part < 2; ++part)
+        CK(cudaMemcpyAsync(c->coef + (size_t)part * k * n, ct + (size_t)part * c->rows * n, (size_t)k * n * 8,
+                           cudaMemcpyDeviceToDevice, s));
+    std::vector<uint32_t> ro;
+    std::vector<int32_t> rp;
+    for (int part = 0; part < 2; ++part)
+        for (int t = 0; t < k; ++t) {
+            ro.push_back((uint32_t)(part * k + t));
+            rp.push_back(t);
+        }
+    CK(upload(c->mr_roff, ro, s));
+    CK(upload(c->mr_rprime, rp, s));
+    PcbNttArgs a = ntt_args(*c, c->coef, c->mr_roff, c->mr_rprime, 2 * k);
+    CK(ntt_inv(*c, &a, s));
+    const uint64_t q0 = c->primes[0], q1 = k == 2 ? c->primes[1] : q0;
+    const uint64_t inv01 = k == 2 ? hm::invmod(q0 % q1, q1) : 0;
+    CK(pcb::wire_compress_launch(c->coef, k, n, hm::prime_const(q0), hm::prime_const(q1), inv01, bits, out, s));
+    return 0;
+}
+
 int pcb_encode(PcbCtx* c, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
                uint64_t* rows) {
     if (!c || !rows || (nvals && !vals)) return fail(PCB_BAD_ARGS, "null argument");

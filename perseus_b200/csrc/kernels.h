@@ -84,5 +84,9 @@ namespace keys {
 template <int LOGN> int ksk_expand_launch(const PcbKskExpandArgs*, cudaStream_t);
 template <int LOGN> int encrypt_launch(const PcbEncryptArgs*, cudaStream_t);
 template <int LOGN> int ksk_gen_launch(const PcbKskGenArgs*, cudaStream_t);
+template <int LOGN> int ksk_unpack_launch(const PcbKskUnpackArgs*, cudaStream_t);
 }  // namespace keys
+// wire.cu: the compressed ciphertext frame of k <= 2 coefficient rows per part (both parts), `bits` per coefficient
+int wire_compress_launch(const uint64_t* coef, int k, size_t n, const PcbPrimeConst& c0, const PcbPrimeConst& c1,
+                         uint64_t inv01, int bits, uint32_t* out, cudaStream_t s);
 }  // namespace pcb

@@ -39,6 +39,7 @@ PcbKernelTable make_table() {
     t.automorph = elem::automorph_launch<LOGN>;
     t.encrypt = keys::encrypt_launch<LOGN>;
     t.ksk_gen = keys::ksk_gen_launch<LOGN>;
+    t.ksk_unpack = keys::ksk_unpack_launch<LOGN>;
     t.mod_raise = elem::mod_raise_launch<LOGN>;
     return t;
 }
@@ -87,4 +88,5 @@ uint64_t pcb_launch_count(void) { return g_launches.load(std::memory_order_relax
 const PcbKernelTable* pc_table_u64_barrett64(void) { return &g_table16; }
 const PcbRingTable* pc_ring_u64_14(void) { return &g_ring14; }
 const PcbRingTable* pc_ring_u64_16(void) { return &g_ring16; }
+const PcbKernelTable* pcb_kernel_table(int32_t log_n) { return pcb::table_for(log_n); }
 }

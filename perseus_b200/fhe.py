@@ -157,7 +157,9 @@ class Session:
     """A context over one chain with device-resident keys (relinearization + the given rotation steps)."""
 
     def __init__(self, chain, rot_steps=(), k_max=1, seed=0, h=192, sigma=3.2, device=None, key_source="dense",
-                 galois_extra=()):
+                 galois_extra=(), keygen=True):
+        """keygen=False: a server's session, no secret; its key slots (relinearization first, then the galois
+        elements of rot_steps and galois_extra) are filled from a client's key bundle (wire.import_keys)."""
         self.chain = chain
         self.device = torch.device(device or "cuda")
         self.n, self.log_n = chain.n, chain.log_n
@@ -190,8 +192,10 @@ class Session:
             L.check(lib.pcb_ctx_create(C.byref(self.params), len(gal), C.c_void_p(self.arena.data_ptr()),
                                        int(nbytes), self._stream(), C.byref(h_ctx)), "pcb_ctx_create")
             self.ctx = h_ctx
-            g = (C.c_uint64 * len(gal))(*gal)
-            L.check(lib.pcb_keygen(self.ctx, seed, h, sigma, len(gal), C.cast(g, L.u64p), self._stream()), "pcb_keygen")
+            if keygen:
+                g = (C.c_uint64 * len(gal))(*gal)
+                L.check(lib.pcb_keygen(self.ctx, seed, h, sigma, len(gal), C.cast(g, L.u64p), self._stream()),
+                        "pcb_keygen")
 
     def __del__(self):
         ctx = getattr(self, "ctx", None)

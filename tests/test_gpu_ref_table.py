@@ -641,6 +641,24 @@ def test_mod_raise(env, d, r0, r1, nparts):
         assert (out[:, nparts:] == x0[:, nparts:]).all()
 
 
+@pytest.mark.parametrize("bits", [1, 20, 28, 32])
+def test_ksk_unpack(env, bits):
+    """ksk_unpack: packed rows (random words, the guard word included) to dense u64 rows, at the widths the
+    reference's u64 table takes."""
+    rng = np.random.default_rng(97 + bits)
+    nrows = 3
+    rw = ((env.n * bits // 32 + 1) + 3) // 4 * 4
+    packed = rng.integers(0, 2**32, (nrows, rw), dtype=np.uint64).astype(np.uint32)
+
+    def mk():
+        inp = torch.from_numpy(packed.view(np.int32).copy()).cuda()
+        out = torch.zeros((nrows, env.n), dtype=torch.int64, device="cuda")
+        a = L.KskUnpackArgs(out.data_ptr(), inp.data_ptr(), rw, nrows, bits)
+        return a, [out], [inp]
+
+    same(run_both("ksk_unpack", mk))
+
+
 # ------------------------------------------------------------------------------------------------ plaintext operands
 
 

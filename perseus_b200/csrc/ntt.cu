@@ -558,8 +558,28 @@ __host__ inline bool misaligned(const void* p) { return ((uintptr_t)p & 15) != 0
 template <int LOGN, bool F>
 __host__ void launch_rows(const PcbNttArgs& a, dim3 grid, cudaStream_t s, int r0);
 
+// fwd_rows_md's dynamic shared memory exceeds the default 48 KiB: raised once per device on its first launch
+template <int LOGN>
+__host__ void md_smem_once() {
+    constexpr int MAXDEV = 64;
+    static bool done[MAXDEV] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAXDEV) dev = 0;
+    if (!done[dev]) {
+        cudaFuncSetAttribute(fwd_rows_md<LOGN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MD_SMEM);
+        done[dev] = true;
+    }
+}
+
 template <int LOGN, bool F>
 __host__ void launch_rows(const PcbNttArgs& a, dim3 grid, cudaStream_t s, int r0) {
+    if constexpr (F && LOGN == 16) {
+        if (a.epi == 1 && a.xnum == 1) {  // ModDown: the epilogue's tile staged by a bulk copy (ntt_pipe.cuh)
+            md_smem_once<LOGN>();
+            launch_pdl_smem(fwd_rows_md<LOGN>, grid, dim3(THREADS), MD_SMEM, s, a, r0);
+            return;
+        }
+    }
     switch (a.epi) {
         case 0: launch_pdl(fwd_rows<LOGN, F, 0>, grid, dim3(THREADS), s, a, r0); break;
         case 1: launch_pdl(fwd_rows<LOGN, F, 1>, grid, dim3(THREADS), s, a, r0); break;

@@ -182,3 +182,106 @@ __global__ void __launch_bounds__(THREADS, PIPE_CTAS_PER_SM) inv_rows_p(PcbNttAr
         pipe_release();
     }
 }
+
+// ------------------------------------------------------------------------------------------------ forward rows, ModDown
+// fwd_rows<LOGN, FP64, epilogue 1> (out = (ex - o) s, one source batch) with the epilogue's source tile staged while
+// the butterflies run: the CTA's 16 blocks of the row are 4096 consecutive words of `ex` (32 KiB), which thread 0
+// requests with one bulk copy right after the launch dependency is met. The plain kernel reads them only after its
+// butterflies, so the row pass's FP64 work and the epilogue's HBM traffic ran one after the other (58 against 35 us
+// per 111-row chunk). The output words go back to natural order through the thread's padded exchange slots, so the
+// staged words (u + 16 k), the output words and the coalesced stores share one conflict-free layout.
+// The wait is bounded like the pipelined pass's: a wait that ran out is counted (pcb_device_timeouts), waited once
+// more, and the epilogue then reads `ex` from global memory (the same words).
+constexpr size_t MD_STAGE_BYTES = 16 * 256 * 8;
+constexpr size_t MD_SMEM = MD_STAGE_BYTES + 64;  // stage, mbarrier, the waiting thread's outcome
+
+template <int LOGN>
+__global__ void __launch_bounds__(THREADS, NTT_ROWS_BLOCKS_F) fwd_rows_md(PcbNttArgs a, int row0) {
+    __shared__ double sm[16 * BLKPAD];
+    __shared__ double2 sw[256];
+    extern __shared__ __align__(128) unsigned char raw[];
+    uint64_t* stage = (uint64_t*)raw;
+    uint64_t* bar = (uint64_t*)(raw + MD_STAGE_BYTES);
+    int* flag = (int*)(bar + 1);
+    const int i = row0 + blockIdx.y;
+    const RowInfo ri = row_of<LOGN>(a, i);
+    const uint64_t p = a.pr[ri.pid].p;
+    const FpMod md = mod_of<LOGN, true>(p, a.fw, ri.pid);
+    sw[tw_slot(threadIdx.x)] = pack_pairs<LOGN>(a.fw, ri.pid)[Pack<LOGN>::ROW + threadIdx.x];
+    const int lb = threadIdx.x / 16, u = threadIdx.x % 16;
+    const int b = blockIdx.x * 16 + lb;  // 256-word block of the row
+    uint64_t* blk = ri.row + (size_t)b * 256;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_release();
+    const size_t erow = (size_t)a.roff[i] << LOGN;  // the row's offset in ex and eout
+    if (threadIdx.x == 0) {
+        fence_async_smem();
+        mbar_expect(bar, MD_STAGE_BYTES);
+        bulk_load(stage, (const uint64_t*)a.ex + erow + (size_t)blockIdx.x * 4096, MD_STAGE_BYTES, bar);
+    }
+    double x[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = load_mid<true>(blk + u + 16 * k);
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const int half = 16 >> (l + 1);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & half) continue;
+            ct(x[k], x[k + half], sw[(1 << l) + (k >> (4 - l))], md);
+        }
+    }
+    double* s = sm + lb * BLKPAD;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        round_end(x[k], md);
+        s[pad(u + 16 * k)] = x[k];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) x[k] = s[pad(16 * u + k)];
+#pragma unroll
+    for (int l = 4; l < 8; ++l) {
+        const int half = 16 >> (l - 3);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k & half) continue;
+            ct(x[k], x[k + half], sw[(1 << l) + ((k >> (8 - l)) << 4) + u], md);
+        }
+    }
+    // canonical words 16 u + k back through this thread's slots; words u + 16 k read out (the block's 16 threads are
+    // one half-warp)
+    uint64_t* own = (uint64_t*)s;
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        canon(x[k], md);
+        own[pad(16 * u + k)] = bits(x[k]);
+    }
+    __syncwarp();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait(bar, 0);
+        if (!ok) {
+            atomicAdd(&g_wait_timeouts, 1u);
+            mbar_wait(bar, 0);
+        }
+        *flag = ok;
+    }
+    __syncthreads();
+    const bool staged = *flag != 0;
+    const uint64_t sc = ((const uint64_t*)a.es)[ri.pid], scs = ((const uint64_t*)a.ess)[ri.pid];
+    const uint64_t* exg = (const uint64_t*)a.ex + erow + (size_t)b * 256;
+    const uint64_t* exs = stage + lb * 256;
+    uint64_t* eo = (uint64_t*)a.eout + erow + (size_t)b * 256;
+#pragma unroll 4
+    for (int k = 0; k < 16; ++k) {
+        const int w = u + 16 * k;
+        const uint64_t xs = staged ? exs[w] : exg[w];
+        eo[w] = epi_word(1, xs, own[pad(w)], 0, sc, scs, p);
+    }
+}

@@ -695,8 +695,10 @@ def model_decode(a, world, barrier, dist):
     over a 256-token encrypted cache per layer resident in HBM, MLP with the polynomial GELU, residuals, 4 refreshes
     per layer), N = 2^16 on config 4's chain, random-init weights N(0, 0.02); the caches start with client-encrypted
     tokens and grow by one per token. One warm-up token (it also encodes every plaintext once), then `steps` tokens
-    (at most 4) timed with CUDA events (max over ranks), the last decrypted against the fp64 decode. On N GPUs every
-    layer's 8 cache blocks are split over the ranks (one all_gather of the partial attention outputs per layer)."""
+    (at most 4) timed with CUDA events (max over ranks), the last decrypted against the fp64 decode. Then 4 sequences
+    decoding together (one token each per step, every op on their batch): one warm-up step and `steps` (at most 2)
+    timed. On N GPUs every layer's 8 cache blocks are split over the ranks (one all_gather of the partial attention
+    outputs per layer)."""
     import numpy as np
     import torch
 
@@ -710,49 +712,58 @@ def model_decode(a, world, barrier, dist):
     prm = BS.Params(ch.n, K=24, r=3, per_group=5)
     lay = M.B.layout(ch.n // 2, cfg.width, cfg.heads, cfg.head_dim, cfg.tokens, cfg.radix_bits)
     steps_rot = sorted(set(BS.rot_steps(prm)) | set(lay.rot_steps()))
-    s = fhe.Session(ch, rot_steps=steps_rot, k_max=lay.blocks, seed=0, h=192, sigma=3.2,
+    S4 = 4
+    s = fhe.Session(ch, rot_steps=steps_rot, k_max=lay.blocks * S4, seed=0, h=192, sigma=3.2,
                     galois_extra=(BS.conj_galois(ch.n),))
     rng = np.random.default_rng(13)
     weights = [M.random_layer(rng) for _ in range(cfg.layers)]
-    warm, steps = 1, max(1, min(a.steps, 4))
-    pre = cfg.tokens - warm - steps
-    Ks = [rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(cfg.layers)]
-    Vs = [rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(cfg.layers)]
+    bt = BS.Bootstrapper(s, prm, ch.q, ch.q[0])
     shard_ = (world, int(os.environ.get("RANK", "0"))) if world > 1 else None
-    dec = M.Decoder(s, cfg, weights, ch.q, BS.Bootstrapper(s, prm, ch.q, ch.q[0]), shard=shard_)
-    dec.load(Ks, Vs)
-    plain = [[K.copy(), V.copy()] for K, V in zip(Ks, Vs)]
-    xs = [rng.normal(0, 1, cfg.d) for _ in range(warm + steps)]
-    cts = [s.encrypt(LIN.input_vector(x, lay.geo), top=0, scale=2.0**40, slots=lay.slots) for x in xs]
-    y = None
-    for i in range(warm):
-        y = dec.decode(cts[i])
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.nvtx.range_push("model_step")
-    e0.record()
-    for i in range(warm, warm + steps):
-        y = dec.decode(cts[i])
-    e1.record()
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    want = None
-    for x in xs:
-        want = M.plain_decode(x, weights, plain, cfg, dec.coeffs)
-    got = LIN.output_values(s.decrypt_slots(y).real, lay.geo, cfg.d)
-    err = float(np.abs(got - want).max())
+
+    def run(seqs, warm, steps, plan):
+        pre = cfg.tokens - warm - steps
+        Ks = [[rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(seqs)] for _ in range(cfg.layers)]
+        Vs = [[rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(seqs)] for _ in range(cfg.layers)]
+        dec = M.Decoder(s, cfg, weights, ch.q, bt, shard=shard_, seqs=seqs, plan=plan)
+        dec.load(Ks if seqs > 1 else [k[0] for k in Ks], Vs if seqs > 1 else [v[0] for v in Vs])
+        plain = [[Ks[l][0].copy(), Vs[l][0].copy()] for l in range(cfg.layers)]  # sequence 0's fp64 caches
+        xs = [[rng.normal(0, 1, cfg.d) for _ in range(seqs)] for _ in range(warm + steps)]
+        cts = [s.stack([s.encrypt(LIN.input_vector(x, lay.geo), top=0, scale=2.0**40, slots=lay.slots) for x in xq])
+               for xq in xs]
+        y = None
+        for i in range(warm):
+            y = dec.decode(cts[i])
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("model_step")
+        e0.record()
+        for i in range(warm, warm + steps):
+            y = dec.decode(cts[i])
+        e1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device="cuda")
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        want = None
+        for xq in xs:
+            want = M.plain_decode(xq[0], weights, plain, cfg, dec.coeffs)
+        got = LIN.output_values(s.decrypt_slots(y, 0).real, lay.geo, cfg.d)
+        return t.item(), float(np.abs(got - want).max()), float(np.abs(want).max()), dec.plan
+
+    ms1, err1, mx1, plan = run(1, 1, max(1, min(a.steps, 4)), None)
+    ms4, err4, _, _ = run(S4, 1, max(1, min(a.steps, 2)), plan)
     res = {"workload": "config 5: GPT-2 small, 12 layers (768 wide, 12 heads x 64, MLP 3072), one token per step, "
                        "a 256-token encrypted KV cache per layer in HBM (8 blocks x 32 tokens), N=2^16 on 29+11 x "
                        "50-bit limbs, 4 refreshes (bootstraps) per layer, degree-7 polynomial LayerNorm / softmax / "
                        "GELU, eager",
-           "ms_per_token": t.item(), "timed_tokens": steps, "refreshes_per_token": 4 * cfg.layers,
-           "max_abs_err_vs_fp64": err, "max_abs_value": float(np.abs(want).max()),
+           "ms_per_token": ms1, "timed_tokens": max(1, min(a.steps, 4)), "refreshes_per_token": 4 * cfg.layers,
+           "max_abs_err_vs_fp64": err1, "max_abs_value": mx1,
+           "batch_of_4": {"sequences": S4, "ms_per_step": ms4, "tokens_per_s": S4 / (ms4 * 1e-3),
+                          "max_abs_err_vs_fp64_seq0": err4},
            "sharding": f"every layer's cache blocks over {world} GPU(s)" if world > 1 else "one GPU"}
-    del s, dec, cts, y
+    del s, bt, plan
     torch.cuda.empty_cache()
     return res
 

@@ -119,10 +119,14 @@ class Decoder:
     """The encrypted decode on `ops` (a session, or the oracle's ops: the same op sequence) over the chain's Q
     `primes`. `bt` refreshes (a bootstrap.Bootstrapper on the same ops): a refresh raises to the chain's top and leaves
     `out_top`; every layer's cache lives at cache_top = out_top - 2, where the pushed rows arrive. shard =
-    (world, rank[, group]) splits every layer's cache blocks over the ranks (block.LaneCache)."""
+    (world, rank[, group]) splits every layer's cache blocks over the ranks (block.LaneCache). seqs = S independent
+    sequences decode together, one token each per step: every op of the step (refreshes included) runs on their batch
+    (the session needs k_max >= S x the cache's blocks)."""
 
-    def __init__(self, ops, cfg, weights, primes, bt, shard=None):
+    def __init__(self, ops, cfg, weights, primes, bt, shard=None, seqs=1, plan=None):
+        """plan: another decoder's plaintext plan (the same weights and session) to share its encodings."""
         self.ops, self.cfg, self.w, self.primes, self.bt = ops, cfg, weights, list(primes), bt
+        self.seqs = seqs
         self.raise_top = len(self.primes) - 1
         self.out_top = self.raise_top - bt.levels
         self.cache_top = self.out_top - 2
@@ -132,7 +136,7 @@ class Decoder:
         self.coeffs = A.softmax_poly(self.lay.tokens)
         self.gcoef = gelu_poly(cfg.gelu_bound)
         self.caches = []
-        self.plan = {}
+        self.plan = {} if plan is None else plan
         self.shard = shard
         self.mask = self.lay.lane0()  # lane 0 of the real elements: the residual stream
         self.hidden_mask = np.zeros(self.lay.slots)  # lane 0 of every element: an MLP block's 1024 hidden units
@@ -141,10 +145,11 @@ class Decoder:
 
     # -------------------------------------------------------------- setup
     def load(self, Ks, Vs):
-        """The client's caches: per layer K, V (n x d rows), one LaneCache per layer at cache_top."""
+        """The client's caches: per layer K, V (n x d rows; with seqs > 1 a list of one such array per sequence), one
+        LaneCache per layer at cache_top."""
         self.caches = []
         for K, V in zip(Ks, Vs):
-            c = B.LaneCache(self.ops, self.lay, self.cache_top, shard=self.shard)
+            c = B.LaneCache(self.ops, self.lay, self.cache_top, seqs=self.seqs, shard=self.shard)
             c.load(K, V)
             self.caches.append(c)
 
@@ -208,8 +213,9 @@ class Decoder:
         return self.mlp(l, n2, r1)
 
     def decode(self, x):
-        """One token (the activation in the projection layout) through every layer; pushes the token's K and V rows
-        into every layer's cache. Returns the last layer's output (lane 0 of each element block carries the value)."""
+        """One token (the activation in the projection layout; a batch of seqs, one per sequence) through every layer;
+        pushes the token's K and V rows into every layer's cache. Returns the last layer's output (lane 0 of each
+        element block carries the value)."""
         for l in range(len(self.w)):
             x = self.layer(l, x)
         return x

@@ -63,3 +63,26 @@ def test_gelu_poly_and_levels():
     # config 4's chain: a refresh spends 16 levels and leaves 12, the attention stage's 10 fit
     ch = fhe.config4_chain()
     assert len(ch.q) - 1 - (3 + 7 + 3 + 3) == 12
+
+
+def test_two_sequences_decode_together(setup):
+    """seqs = 2: one step decodes both sequences' tokens (every op on their batch, refreshes included); each output
+    matches its own fp64 decode, and each sequence's caches grow by its own token."""
+    cfg, prm, c = setup
+    cfg = M.ModelCfg(layers=1, d=cfg.d, width=cfg.width, heads=cfg.heads, head_dim=cfg.head_dim, mlp=cfg.mlp,
+                     tokens=cfg.tokens, radix_bits=cfg.radix_bits)
+    ops = OracleOps(c)
+    rng = np.random.default_rng(51)
+    weights = [M.random_layer(rng, d=cfg.d, mlp=cfg.mlp, std=0.1)]
+    pre, S = 10, 2
+    Ks = [[rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(S)]]
+    Vs = [[rng.normal(0, 1, (pre, cfg.d)) / 8 for _ in range(S)]]
+    dec = M.Decoder(ops, cfg, weights, c.q, BS.Bootstrapper(ops, prm, c.q, c.q[0]), seqs=S)
+    dec.load(Ks, Vs)
+    xs = [rng.normal(0, 1, cfg.d) for _ in range(S)]
+    xc = ops.stack([ops.encrypt(LIN.input_vector(x, dec.lay.geo), 0, 2.0**40, dec.lay.slots) for x in xs])
+    y = dec.decode(xc)
+    for q in range(S):
+        want = M.plain_decode(xs[q], weights, [[Ks[0][q].copy(), Vs[0][q].copy()]], cfg, dec.coeffs)
+        got = LIN.output_values(ops.decrypt_slots(y, q).real, dec.lay.geo, cfg.d)
+        assert np.abs(got - want).max() < 1e-3, q

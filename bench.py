@@ -288,9 +288,13 @@ def run_ours(a):
     in_ready = [torch.cuda.Event() for _ in range(2)]
     in_free = [torch.cuda.Event() for _ in range(2)]
 
+    # per (ciphertext, part) slice: rows 0..nq of a part are contiguous on both sides, so each is one direct
+    # host<->device copy (a copy through the strided view of all parts would stage 1.6 GB in a device temporary)
     def fetch(b):
         with torch.cuda.stream(cin):
-            bufs[b].data[:, :, :nq].copy_(host_in, non_blocking=True)
+            for c in range(BATCH):
+                for part in range(2):
+                    bufs[b].data[c, part, :nq].copy_(host_in[c, part], non_blocking=True)
             in_ready[b].record(cin)
 
     barrier()
@@ -312,7 +316,9 @@ def run_ours(a):
         done.record(stream)
         cout.wait_event(done)
         with torch.cuda.stream(cout):
-            host_out[b].copy_(res.data[:, :, :nq], non_blocking=True)
+            for c in range(BATCH):
+                for part in range(2):
+                    host_out[b][c, part].copy_(res.data[c, part, :nq], non_blocking=True)
         res.data.record_stream(cout)
     stream.wait_stream(cout)
     e1.record(stream)

@@ -273,6 +273,20 @@ typedef struct PcbRescaleCombineArgs {
     int32_t n, K;
 } PcbRescaleCombineArgs;
 
+/* args.cuh:553-562: rescale_fwd, rescale_coef's corrections and their forward NTT `ntt` (rows of tmp, epilogue 3 = MUL_ADD:
+ * x = alpha x + NTT(tmp)) in one entry (the corrections are written to tmp here; the reference forms them inside the
+ * transform: the same words in x) */
+typedef struct PcbRescaleNttArgs {
+    PcbRescaleArgs rs;
+    PcbNttArgs ntt;
+} PcbRescaleNttArgs;
+
+/* args.cuh:573-578: rescale_combine_to, out = alpha x + tmp (x read only) */
+typedef struct PcbRescaleCombineToArgs {
+    PcbRescaleCombineArgs a;
+    PcbPolyRef out;
+} PcbRescaleCombineToArgs;
+
 /* args.cuh:580-592: out[o] = in[automorph_slot(k, o)] (+ add[o]) over row set rs, K cts x nparts parts */
 typedef struct PcbAutomorphArgs {
     PcbPolyRef out, in, add;
@@ -311,6 +325,84 @@ typedef struct PcbKskGenArgs {
     uint64_t row_words;
     int32_t nrows, ndig, nq, bits, sq, pad;
 } PcbKskGenArgs;
+
+/* args.cuh:159-170: ew_many, out[j] = a[j] (+ b[j]) (+ c[j]) for n <= 48 polynomials by pointer, Q rows [0, nrows) (row r
+ * at + r N words; a null b / c skipped; out may alias its sources) */
+#define PCB_EWM_MAX 48
+typedef struct PcbEwManyArgs {
+    void* out[PCB_EWM_MAX];
+    const void* a[PCB_EWM_MAX];
+    const void* b[PCB_EWM_MAX];
+    const void* c[PCB_EWM_MAX];
+    const PcbPrimeConst* pr;
+    int32_t n, nrows;
+} PcbEwManyArgs;
+
+/* args.cuh:172-182: submul_many, out[j] = (a[j] - b[j]) t[row] for n <= 48 polynomials (t one table of nrows rows) */
+typedef struct PcbSubMulManyArgs {
+    void* out[PCB_EWM_MAX];
+    const void* a[PCB_EWM_MAX];
+    const void* b[PCB_EWM_MAX];
+    const void* t;
+    const PcbPrimeConst* pr;
+    int32_t n, nrows;
+} PcbSubMulManyArgs;
+
+/* args.cuh:380-389: tensor_sum, c0 = sum_j a0 b0, c1 = sum_j a0 b1 + a1 b0 into out, d2 = sum_j a1 b1 into part 1 of d2, over
+ * npairs <= 16 pairs (acc as tensor's) */
+#define PCB_TSUM_MAX 16
+typedef struct PcbTensorSumArgs {
+    PcbPolyRef out, d2;
+    PcbPolyRef a[PCB_TSUM_MAX], b[PCB_TSUM_MAX];
+    const PcbPrimeConst* pr;
+    int32_t npairs, acc, n, K;
+} PcbTensorSumArgs;
+
+/* args.cuh:391-404: tensor_multi, nout <= 4 tensor sums of npairs <= 32 pairs in one launch */
+#define PCB_TMULTI_OUT 4
+#define PCB_TMULTI_PAIRS 32
+typedef struct PcbTensorMultiArgs {
+    PcbPolyRef out[PCB_TMULTI_OUT], d2[PCB_TMULTI_OUT];
+    PcbPolyRef a[PCB_TMULTI_OUT][PCB_TMULTI_PAIRS], b[PCB_TMULTI_OUT][PCB_TMULTI_PAIRS];
+    const PcbPrimeConst* pr;
+    int32_t nout, npairs, acc, n, K, pad;
+} PcbTensorMultiArgs;
+
+/* args.cuh:449-457: md_epilogue_to, dst = a +- (x - t) binv over Q rows [0, n), both parts (sub: minus) */
+typedef struct PcbMdEpiToArgs {
+    PcbMdEpiArgs m;
+    PcbPolyRef a;
+    int32_t sub, pad;
+} PcbMdEpiToArgs;
+
+/* args.cuh:459-468: wsum, out = sum_{j < nsrc <= 8} w[j rowstride + row] src_j (both parts, Shoup companions ws), rows
+ * [0, n) */
+typedef struct PcbWsumArgs {
+    PcbPolyRef out;
+    PcbPolyRef src[8];
+    const void* w;
+    const void* ws;
+    const PcbPrimeConst* pr;
+    int32_t nsrc, rowstride, n, K;
+} PcbWsumArgs;
+
+/* args.cuh:470-474: wsum_k, wsum then part 0 += k[row] (raw, reduced once when >= p) */
+typedef struct PcbWsumKArgs {
+    PcbWsumArgs w;
+    const void* k;
+} PcbWsumKArgs;
+
+/* args.cuh:476-489: wsum_multi, nout <= 3 weighted sums of one source list, out[m] on rows [0, n[m]) (k[m]: wsum_k's) */
+typedef struct PcbWsumMultiArgs {
+    PcbPolyRef out[3];
+    PcbPolyRef src[8];
+    const void* w[3];
+    const void* ws[3];
+    const void* k[3];
+    const PcbPrimeConst* pr;
+    int32_t nout, nsrc, rowstride, K;
+    int32_t n[3], nmax;
+} PcbWsumMultiArgs;
 
 /* args.cuh:656-663: packed key rows -> dense rows, out[r][i] = value i of packed row r (in + r row_words), r < nrows.
  * Values are `bits` bits LSB first (the wire format's pack_row order); the reference's u64 table takes bits 1..32, this
@@ -354,7 +446,7 @@ typedef struct PcbKernelTable {
     PcbLaunch cts_fused;
     int (*tensor)(const PcbTensorArgs*, cudaStream_t);
     int (*md_epilogue)(const PcbMdEpiArgs*, cudaStream_t);
-    PcbLaunch wsum;
+    int (*wsum)(const PcbWsumArgs*, cudaStream_t);
     int (*add_const)(const PcbAddConstArgs*, cudaStream_t);
     int (*mul_table)(const PcbMulTableArgs*, cudaStream_t);
     int (*rescale_coef)(const PcbRescaleArgs*, cudaStream_t);
@@ -367,12 +459,23 @@ typedef struct PcbKernelTable {
     int (*mod_raise)(const PcbModRaiseArgs*, cudaStream_t);
     PcbLaunch small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
     int (*ks_dot_key)(const PcbKsKeyArgs*, cudaStream_t);
-    PcbLaunch pcmm, ccmm, wsum_k, rescale_combine_to, md_epilogue_to, small_int1, coeff_sum;
+    PcbLaunch pcmm, ccmm;
+    int (*wsum_k)(const PcbWsumKArgs*, cudaStream_t);
+    int (*rescale_combine_to)(const PcbRescaleCombineToArgs*, cudaStream_t);
+    int (*md_epilogue_to)(const PcbMdEpiToArgs*, cudaStream_t);
+    PcbLaunch small_int1, coeff_sum;
     int (*mul_add)(const PcbMulAddArgs*, cudaStream_t);
-    PcbLaunch rescale_fwd;
+    int (*rescale_fwd)(const PcbRescaleNttArgs*, cudaStream_t);
     int (*mul_add_n)(const PcbMulAddNArgs*, cudaStream_t);
-    PcbLaunch tensor_y, wsum_multi, bconv_wide, tfhe, tensor_sum, tensor_multi, tensor_seeded, ew_many, submul_many,
-        pack_split, pack_dot;
+    PcbLaunch tensor_y;
+    int (*wsum_multi)(const PcbWsumMultiArgs*, cudaStream_t);
+    PcbLaunch bconv_wide, tfhe;
+    int (*tensor_sum)(const PcbTensorSumArgs*, cudaStream_t);
+    int (*tensor_multi)(const PcbTensorMultiArgs*, cudaStream_t);
+    PcbLaunch tensor_seeded;
+    int (*ew_many)(const PcbEwManyArgs*, cudaStream_t);
+    int (*submul_many)(const PcbSubMulManyArgs*, cudaStream_t);
+    PcbLaunch pack_split, pack_dot;
 } PcbKernelTable;
 
 /* args.cuh:1099-1119: ring-size tables (rows of 2^log_n words) */
@@ -625,6 +728,17 @@ static_assert(sizeof(PcbAutomorphArgs) == 112, "AutomorphArgs layout");
 static_assert(sizeof(PcbEncryptArgs) == 64, "EncryptArgs layout");
 static_assert(sizeof(PcbKskGenArgs) == 120, "KskGenArgs layout");
 static_assert(sizeof(PcbKskUnpackArgs) == 32, "KskUnpackArgs layout");
+static_assert(sizeof(PcbEwManyArgs) == 4 * PCB_EWM_MAX * 8 + 16, "EwManyArgs layout");
+static_assert(sizeof(PcbSubMulManyArgs) == 3 * PCB_EWM_MAX * 8 + 24, "SubMulManyArgs layout");
+static_assert(sizeof(PcbTensorSumArgs) == 2 * 24 + 2 * PCB_TSUM_MAX * 24 + 8 + 16, "TensorSumArgs layout");
+static_assert(sizeof(PcbTensorMultiArgs) == (2 * PCB_TMULTI_OUT + 2 * PCB_TMULTI_OUT * PCB_TMULTI_PAIRS) * 24 + 8 + 24,
+              "TensorMultiArgs layout");
+static_assert(sizeof(PcbMdEpiToArgs) == 152, "MdEpiToArgs layout");
+static_assert(sizeof(PcbWsumArgs) == 256, "WsumArgs layout");
+static_assert(sizeof(PcbWsumKArgs) == 264, "WsumKArgs layout");
+static_assert(sizeof(PcbWsumMultiArgs) == 376, "WsumMultiArgs layout");
+static_assert(sizeof(PcbRescaleNttArgs) == 328, "RescaleNttArgs layout");
+static_assert(sizeof(PcbRescaleCombineToArgs) == 104, "RescaleCombineToArgs layout");
 static_assert(sizeof(PcbModRaiseArgs) == 2136, "ModRaiseArgs layout");
 static_assert(sizeof(PcbPtDotArgs) == 128, "PtDotArgs layout");
 static_assert(sizeof(PcbAddConstArgs) == 48, "AddConstArgs layout");

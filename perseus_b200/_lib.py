@@ -104,6 +104,57 @@ class RescaleCombineArgs(C.Structure):
                 ("K", C.c_int32)]
 
 
+class RescaleNttArgs(C.Structure):
+    _fields_ = [("rs", RescaleArgs), ("ntt", NttArgs)]
+
+
+class RescaleCombineToArgs(C.Structure):
+    _fields_ = [("a", RescaleCombineArgs), ("out", PolyRef)]
+
+
+class MdEpiToArgs(C.Structure):
+    _fields_ = [("m", MdEpiArgs), ("a", PolyRef), ("sub", C.c_int32), ("pad", C.c_int32)]
+
+
+class WsumArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("src", PolyRef * 8), ("w", vp), ("ws", vp), ("pr", vp), ("nsrc", C.c_int32),
+                ("rowstride", C.c_int32), ("n", C.c_int32), ("K", C.c_int32)]
+
+
+class WsumKArgs(C.Structure):
+    _fields_ = [("w", WsumArgs), ("k", vp)]
+
+
+class WsumMultiArgs(C.Structure):
+    _fields_ = [("out", PolyRef * 3), ("src", PolyRef * 8), ("w", vp * 3), ("ws", vp * 3), ("k", vp * 3), ("pr", vp),
+                ("nout", C.c_int32), ("nsrc", C.c_int32), ("rowstride", C.c_int32), ("K", C.c_int32),
+                ("n", C.c_int32 * 3), ("nmax", C.c_int32)]
+
+
+EWM_MAX, TSUM_MAX, TMULTI_OUT, TMULTI_PAIRS = 48, 16, 4, 32
+
+
+class EwManyArgs(C.Structure):
+    _fields_ = [("out", vp * EWM_MAX), ("a", vp * EWM_MAX), ("b", vp * EWM_MAX), ("c", vp * EWM_MAX), ("pr", vp),
+                ("n", C.c_int32), ("nrows", C.c_int32)]
+
+
+class SubMulManyArgs(C.Structure):
+    _fields_ = [("out", vp * EWM_MAX), ("a", vp * EWM_MAX), ("b", vp * EWM_MAX), ("t", vp), ("pr", vp),
+                ("n", C.c_int32), ("nrows", C.c_int32)]
+
+
+class TensorSumArgs(C.Structure):
+    _fields_ = [("out", PolyRef), ("d2", PolyRef), ("a", PolyRef * TSUM_MAX), ("b", PolyRef * TSUM_MAX), ("pr", vp),
+                ("npairs", C.c_int32), ("acc", C.c_int32), ("n", C.c_int32), ("K", C.c_int32)]
+
+
+class TensorMultiArgs(C.Structure):
+    _fields_ = [("out", PolyRef * TMULTI_OUT), ("d2", PolyRef * TMULTI_OUT), ("a", (PolyRef * TMULTI_PAIRS) * TMULTI_OUT),
+                ("b", (PolyRef * TMULTI_PAIRS) * TMULTI_OUT), ("pr", vp), ("nout", C.c_int32), ("npairs", C.c_int32),
+                ("acc", C.c_int32), ("n", C.c_int32), ("K", C.c_int32), ("pad", C.c_int32)]
+
+
 class PtDotArgs(C.Structure):
     _fields_ = [("rot", PolyRef), ("res", PolyRef), ("rot_stride", C.c_uint64), ("res_stride", C.c_uint64),
                 ("pts", vp), ("pr", vp), ("rs", RowSet), ("npts", C.c_int32), ("bstep", C.c_int32),
@@ -187,7 +238,10 @@ SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJo
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
          "EncryptArgs": 64, "KskGenArgs": 120, "KskUnpackArgs": 32, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
-         "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
+         "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "RescaleNttArgs": 328,
+         "RescaleCombineToArgs": 104, "MdEpiToArgs": 152, "WsumArgs": 256, "WsumKArgs": 264, "WsumMultiArgs": 376,
+         "EwManyArgs": 4 * 48 * 8 + 16, "SubMulManyArgs": 3 * 48 * 8 + 24, "TensorSumArgs": 2 * 24 + 2 * 16 * 24 + 24,
+         "TensorMultiArgs": (2 * 4 + 2 * 4 * 32) * 24 + 32, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}
 
 _lib = None
 

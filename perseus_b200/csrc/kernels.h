@@ -80,6 +80,18 @@ namespace regen {
 template <int LOGN> int ks_dot_regen_launch(const PcbKsRegenArgs*, cudaStream_t);
 template <int LOGN> int ks_dot_key_launch(const PcbKsKeyArgs*, cudaStream_t);
 }  // namespace regen
+namespace elem {  // elem_multi.cu
+template <int LOGN> int ew_many_launch(const PcbEwManyArgs*, cudaStream_t);
+template <int LOGN> int submul_many_launch(const PcbSubMulManyArgs*, cudaStream_t);
+template <int LOGN> int wsum_launch(const PcbWsumArgs*, cudaStream_t);
+template <int LOGN> int wsum_k_launch(const PcbWsumKArgs*, cudaStream_t);
+template <int LOGN> int wsum_multi_launch(const PcbWsumMultiArgs*, cudaStream_t);
+template <int LOGN> int tensor_sum_launch(const PcbTensorSumArgs*, cudaStream_t);
+template <int LOGN> int tensor_multi_launch(const PcbTensorMultiArgs*, cudaStream_t);
+template <int LOGN> int md_epilogue_to_launch(const PcbMdEpiToArgs*, cudaStream_t);
+template <int LOGN> int rescale_combine_to_launch(const PcbRescaleCombineToArgs*, cudaStream_t);
+template <int LOGN> int rescale_fwd_launch(const PcbRescaleNttArgs*, cudaStream_t);
+}  // namespace elem
 namespace keys {
 template <int LOGN> int ksk_expand_launch(const PcbKskExpandArgs*, cudaStream_t);
 template <int LOGN> int encrypt_launch(const PcbEncryptArgs*, cudaStream_t);

@@ -41,6 +41,16 @@ PcbKernelTable make_table() {
     t.ksk_gen = keys::ksk_gen_launch<LOGN>;
     t.ksk_unpack = keys::ksk_unpack_launch<LOGN>;
     t.mod_raise = elem::mod_raise_launch<LOGN>;
+    t.wsum = elem::wsum_launch<LOGN>;
+    t.wsum_k = elem::wsum_k_launch<LOGN>;
+    t.wsum_multi = elem::wsum_multi_launch<LOGN>;
+    t.rescale_combine_to = elem::rescale_combine_to_launch<LOGN>;
+    t.rescale_fwd = elem::rescale_fwd_launch<LOGN>;
+    t.md_epilogue_to = elem::md_epilogue_to_launch<LOGN>;
+    t.tensor_sum = elem::tensor_sum_launch<LOGN>;
+    t.tensor_multi = elem::tensor_multi_launch<LOGN>;
+    t.ew_many = elem::ew_many_launch<LOGN>;
+    t.submul_many = elem::submul_many_launch<LOGN>;
     return t;
 }
 

@@ -1019,3 +1019,214 @@ def test_reference_relin_and_rescale_equal_oracle(cfg2, top):
     assert (r[:, :top] == orr[:, :top]).all(), "reference launchers' rescale != oracle"
     s.rescale_one(ours)
     assert (host(ours.data[0])[:, :top] == r[:, :top]).all()
+
+
+# ------------------------------------------------------------------------------------------------ the evaluator's other entries
+# (crates/pc-gpu/src: ops.rs wsum / wsum_k / tensor_sum / tensor_multi, relin.rs wsum, ks.rs ew_many / submul_many,
+# rescale.rs rescale_fwd / rescale_combine_to, bts/evalmod.rs wsum_multi / md_epilogue_to)
+
+
+def _poly_ptr(t, env, c, part):
+    """pointer to polynomial (c, part) of a [K][2][R][N] device tensor (rows at + r N words)"""
+    return t.data_ptr() + ((c * 2 + part) * env.R * env.n) * 8
+
+
+def test_ew_many_and_submul_many(env):
+    rng = np.random.default_rng(120)
+    K, nrows = 3, 9
+    srcs = [env.cts(rng, K) for _ in range(3)]
+    t = env.rows(rng, range(nrows))
+
+    def mk_many():
+        a, b, c = (dev(x) for x in srcs)
+        out = torch.zeros_like(a)
+        args = L.EwManyArgs()
+        polys = [(cc, part) for cc in range(K) for part in range(2)]
+        for j, (cc, part) in enumerate(polys):
+            args.out[j] = _poly_ptr(out, env, cc, part)
+            args.a[j] = _poly_ptr(a, env, cc, part)
+            args.b[j] = _poly_ptr(b, env, cc, part) if j % 3 != 1 else None  # null b / c skipped
+            args.c[j] = _poly_ptr(c, env, cc, part) if j % 2 == 0 else None
+        args.pr, args.n, args.nrows = env.pc.data_ptr(), len(polys), nrows
+        return args, [out], [a, b, c]
+
+    same(run_both("ew_many", mk_many))
+
+    def mk_submul():
+        a, b = dev(srcs[0]), dev(srcs[1])
+        td = dev(t)
+        out = torch.zeros_like(a)
+        args = L.SubMulManyArgs()
+        polys = [(cc, part) for cc in range(K) for part in range(2)]
+        for j, (cc, part) in enumerate(polys):
+            args.out[j] = _poly_ptr(out, env, cc, part)
+            args.a[j] = _poly_ptr(a, env, cc, part)
+            args.b[j] = _poly_ptr(b, env, cc, part)
+        args.t, args.pr, args.n, args.nrows = td.data_ptr(), env.pc.data_ptr(), len(polys), nrows
+        return args, [out], [a, b, td]
+
+    same(run_both("submul_many", mk_submul))
+
+
+@pytest.mark.parametrize("nsrc", [1, 3, 8])
+def test_weighted_sums(env, nsrc):
+    rng = np.random.default_rng(130 + nsrc)
+    K, n = 2, env.R
+    srcs = [env.cts(rng, K) for _ in range(nsrc)]
+    rowstride = env.R
+    w = [[int(rng.integers(0, env.primes[r])) for r in range(rowstride)] for _ in range(nsrc)]
+    ws = [[shoup(v, env.primes[r]) for r, v in enumerate(row)] for row in w]
+    kraw = [int(rng.integers(0, 2 * env.primes[r])) for r in range(env.R)]  # raw: reduced once when >= p
+
+    def base_args(keep):
+        sd = [dev(x) for x in srcs]
+        wd, wsd = dev(np.array(w, np.uint64).ravel()), dev(np.array(ws, np.uint64).ravel())
+        out = torch.zeros_like(sd[0])
+        keep += sd + [wd, wsd]
+        a = L.WsumArgs()
+        a.out = env.cref(out)
+        for j in range(nsrc):
+            a.src[j] = env.cref(sd[j])
+        a.w, a.ws, a.pr, a.nsrc, a.rowstride, a.n, a.K = wd.data_ptr(), wsd.data_ptr(), env.pc.data_ptr(), nsrc, \
+            rowstride, n, K
+        return a, out
+
+    def mk_wsum():
+        keep = []
+        a, out = base_args(keep)
+        return a, [out], keep
+
+    same(run_both("wsum", mk_wsum))
+
+    def mk_wsum_k():
+        keep = []
+        a, out = base_args(keep)
+        kd = dev(kraw)
+        keep.append(kd)
+        return L.WsumKArgs(a, kd.data_ptr()), [out], keep
+
+    same(run_both("wsum_k", mk_wsum_k))
+
+    def mk_multi():
+        keep = []
+        sd = [dev(x) for x in srcs]
+        keep += sd
+        a = L.WsumMultiArgs()
+        outs = []
+        for m in range(3):
+            wm = [[int(rng.integers(0, env.primes[r])) for r in range(rowstride)] for _ in range(nsrc)]
+            wd = dev(np.array(wm, np.uint64).ravel())
+            wsd = dev(np.array([[shoup(v, env.primes[r]) for r, v in enumerate(row)] for row in wm], np.uint64).ravel())
+            out = torch.zeros_like(sd[0])
+            keep += [wd, wsd]
+            outs.append(out)
+            a.out[m], a.w[m], a.ws[m] = env.cref(out), wd.data_ptr(), wsd.data_ptr()
+            a.n[m] = [env.R, 7, 10][m]
+            if m == 1:
+                kd = dev(kraw)
+                keep.append(kd)
+                a.k[m] = kd.data_ptr()
+        for j in range(nsrc):
+            a.src[j] = env.cref(sd[j])
+        a.pr, a.nout, a.nsrc, a.rowstride, a.K, a.nmax = env.pc.data_ptr(), 3, nsrc, rowstride, K, env.R
+        return a, outs, keep
+
+    same(run_both("wsum_multi", mk_multi))
+
+
+@pytest.mark.parametrize("acc", [0, 1, 3])
+def test_tensor_sum_and_multi(env, acc):
+    rng = np.random.default_rng(140 + acc)
+    K, n, npairs = 2, env.R, 5
+    A = [env.cts(rng, K) for _ in range(npairs)]
+    Bv = [env.cts(rng, K) for _ in range(npairs)]
+    out0, d20 = env.cts(rng, K), env.cts(rng, K)
+
+    def mk_sum():
+        ad, bd = [dev(x) for x in A], [dev(x) for x in Bv]
+        out, d2 = dev(out0), dev(d20)
+        a = L.TensorSumArgs()
+        a.out, a.d2 = env.cref(out), env.cref(d2)
+        for j in range(npairs):
+            a.a[j], a.b[j] = env.cref(ad[j]), env.cref(bd[j])
+        a.pr, a.npairs, a.acc, a.n, a.K = env.pc.data_ptr(), npairs, acc, n, K
+        return a, [out, d2], ad + bd
+
+    same(run_both("tensor_sum", mk_sum))
+
+    def mk_multi():
+        ad, bd = [dev(x) for x in A], [dev(x) for x in Bv]
+        outs = [(dev(out0), dev(d20)) for _ in range(3)]
+        a = L.TensorMultiArgs()
+        for o in range(3):
+            a.out[o], a.d2[o] = env.cref(outs[o][0]), env.cref(outs[o][1])
+            for j in range(npairs):  # output o pairs (a[j], b[(j + o) % npairs])
+                a.a[o][j], a.b[o][j] = env.cref(ad[j]), env.cref(bd[(j + o) % npairs])
+        a.pr, a.nout, a.npairs, a.acc, a.n, a.K = env.pc.data_ptr(), 3, npairs, acc, n, K
+        return a, [t for pair in outs for t in pair], ad + bd
+
+    same(run_both("tensor_multi", mk_multi))
+
+
+@pytest.mark.parametrize("sub", [0, 1])
+def test_md_epilogue_to_and_combine_to(env, sub):
+    rng = np.random.default_rng(150 + sub)
+    K, n = 2, 9
+    x, t, a0, d0 = env.cts(rng, K), env.cts(rng, K), env.cts(rng, K), env.cts(rng, K)
+    binv = [int(rng.integers(1, p)) for p in env.primes]
+    binvs = [shoup(v, p) for v, p in zip(binv, env.primes)]
+
+    def mk_md():
+        xd, td, ad, dd = dev(x), dev(t), dev(a0), dev(d0)
+        bi, bis = dev(binv), dev(binvs)
+        m = L.MdEpiArgs(env.cref(dd), env.cref(xd), env.cref(td), bi.data_ptr(), bis.data_ptr(), None,
+                        env.pc.data_ptr(), 0, n, K, 0)
+        return L.MdEpiToArgs(m, env.cref(ad), sub, 0), [dd], [xd, td, ad, bi, bis]
+
+    same(run_both("md_epilogue_to", mk_md))
+
+    def mk_comb():
+        xd, td, od = dev(x), dev(t), dev(d0)
+        al, als = dev(binv), dev(binvs)
+        r = L.RescaleCombineArgs(env.cref(xd), env.cref(td), al.data_ptr(), als.data_ptr(), env.pc.data_ptr(), n, K)
+        return L.RescaleCombineToArgs(r, env.cref(od)), [od, xd], [td, al, als]
+
+    same(run_both("rescale_combine_to", mk_comb))
+
+
+def test_rescale_fwd(env):
+    """rescale_fwd (two dropped primes, pre-factors): the corrections and their forward NTT with the combine epilogue;
+    rows 0..top-2 of x must agree (tmp is scratch)."""
+    rng = np.random.default_rng(160)
+    K, top = 2, 7
+    q = env.primes
+    a_, b_ = top, top - 1
+    nrows = top - 1
+
+    def qlql(xp, i):
+        return (-pow(q[xp], -1, q[i])) % q[i]
+
+    A = [((pow(q[b_], -1, q[i]) * qlql(a_, i)) % q[i]) if i < nrows else 0 for i in range(env.R)]
+    B = [qlql(b_, i) if i < nrows else 0 for i in range(env.R)]
+    al = [((pow(q[a_], -1, q[i]) * pow(q[b_], -1, q[i])) % q[i]) if i < nrows else 1 for i in range(env.R)]
+    As, Bs, als = ([shoup(v, q[i]) for i, v in enumerate(arr)] for arr in (A, B, al))
+    qam = [q[a_] % q[i] for i in range(env.R)]
+    qbm = [q[b_] % q[i] for i in range(env.R)]
+    x0 = env.cts(rng, K)
+    ca, cb = int(rng.integers(2, q[a_])), int(rng.integers(2, q[b_]))
+    roff = [(c * 2 + part) * env.R + i for c in range(K) for part in range(2) for i in range(nrows)]
+    rprime = [i for c in range(K) for part in range(2) for i in range(nrows)]
+
+    def mk():
+        keep = [dev(v) for v in (A, B, As, Bs, qam, qbm, al, als)]
+        xd, tmp = dev(x0), torch.zeros((K, 2, env.R, env.n), dtype=torch.int64, device="cuda")
+        keep.append(tmp)
+        rs = L.RescaleArgs(env.cref(xd), env.cref(tmp), *[v.data_ptr() for v in keep[:6]], env.pc.data_ptr(),
+                           pow(q[a_], -1, q[b_]), qlql(a_, b_), ca, cb, top, nrows, K, 2)
+        ntt = env.ntt_args(tmp, roff, rprime, keep, eout=xd.data_ptr(), ex=xd.data_ptr(), es=keep[6].data_ptr(),
+                           ess=keep[7].data_ptr(), epi=3, xnum=1)
+        return L.RescaleNttArgs(rs, ntt), [xd], keep
+
+    got = run_both("rescale_fwd", mk)
+    a, b = got["ours"][0].reshape(K, 2, env.R, env.n), got["ref"][0].reshape(K, 2, env.R, env.n)
+    assert (a[:, :, :nrows] == b[:, :, :nrows]).all()

@@ -1107,6 +1107,8 @@ def test_weighted_sums(env, nsrc):
 
     same(run_both("wsum_k", mk_wsum_k))
 
+    wmulti = [[[int(rng.integers(0, env.primes[r])) for r in range(rowstride)] for _ in range(nsrc)] for _ in range(3)]
+
     def mk_multi():
         keep = []
         sd = [dev(x) for x in srcs]
@@ -1114,7 +1116,7 @@ def test_weighted_sums(env, nsrc):
         a = L.WsumMultiArgs()
         outs = []
         for m in range(3):
-            wm = [[int(rng.integers(0, env.primes[r])) for r in range(rowstride)] for _ in range(nsrc)]
+            wm = wmulti[m]
             wd = dev(np.array(wm, np.uint64).ravel())
             wsd = dev(np.array([[shoup(v, env.primes[r]) for r, v in enumerate(row)] for row in wm], np.uint64).ravel())
             out = torch.zeros_like(sd[0])

@@ -578,8 +578,9 @@ void ntt_inv_row(const Ctx& c, uint64_t* x, int pid) {
 // ModUp + key inner product (crates/pc-gpu/src/ks.rs:954-1043 modup_from / modup_tail, crates/pc-gpu/src/ks.rs:
 // 602-677 level_specs_with, the dot of crates/pc-kernels/src/bin/selftest.rs:1118-1152 and crates/pc-host/src/ks.rs:
 // 60-140): ext[part][row] over Q rows 0..=top and the special rows, output scattered at automorph_slot(autok, i).
-void keyswitch_ext(const Ctx& c, const uint64_t* d, const uint64_t* c0, int c0_mode, const Key& key, uint32_t autok,
-                   uint64_t* ext, int top) {
+// ModUp of d (steps 1-3): every live digit extended to the rows outside it, D[digit][row][N] (a digit's own rows
+// are read from d by the inner product)
+std::vector<uint64_t> modup(const Ctx& c, const uint64_t* d, int top) {
     const size_t n = c.n;
     const int rows = c.rows(), nq = c.nq, kp = c.kp;
     const int ndig = c.live_digits(top);
@@ -637,6 +638,16 @@ void keyswitch_ext(const Ctx& c, const uint64_t* d, const uint64_t* c0, int c0_m
         }
         fwd_exact(o, c.tab[t], n);
     }
+    return D;
+}
+
+// The inner product (step 4) over a ModUp's digits: ext[part][row] over Q rows 0..=top and the special rows, output
+// scattered at automorph_slot(autok, i)
+void dot_ext(const Ctx& c, const uint64_t* d, const std::vector<uint64_t>& D, const uint64_t* c0, int c0_mode,
+             const Key& key, uint32_t autok, uint64_t* ext, int top) {
+    const size_t n = c.n;
+    const int rows = c.rows(), nq = c.nq, kp = c.kp;
+    const int ndig = c.live_digits(top);
     // 4. the inner product: s0 = C0 + sum_d D_d b_d, s1 = sum_d D_d a_d, D_d[t] = c1[t] on digit d's own rows
     std::vector<int> krow;
     for (int t = 0; t <= top; ++t) krow.push_back(t);
@@ -667,6 +678,12 @@ void keyswitch_ext(const Ctx& c, const uint64_t* d, const uint64_t* c0, int c0_m
             o1[o] = r1[k];
         }
     }
+}
+
+void keyswitch_ext(const Ctx& c, const uint64_t* d, const uint64_t* c0, int c0_mode, const Key& key, uint32_t autok,
+                   uint64_t* ext, int top) {
+    const std::vector<uint64_t> D = modup(c, d, top);
+    dot_ext(c, d, D, c0, c0_mode, key, autok, ext, top);
 }
 
 // ModDown (crates/pc-gpu/src/ks.rs:1604-1656 moddown_to_j and 1428-1438 md_intt): INTT of the special rows with
@@ -1247,6 +1264,40 @@ int orc_ntt_batch(void* cv, uint64_t* x, int nrows, int inverse) {
     }
     return 0;
 }
+// Hoisted rotations (crates/pc-gpu/src/rotate.rs:456 Rotator::Hoisted): one ModUp of c1 shared by every step, then
+// per step the inner product with its key (c0 added, output at automorph_slot(g^-1)) and its own ModDown; a step
+// with g = 1 is a copy. outs: nsteps ciphertexts [2][rows][N].
+int orc_rotate_hoisted(void* cv, const uint64_t* x, const int64_t* steps, int nsteps, uint64_t* const* outs, int top) {
+    Ctx& c = *(Ctx*)cv;
+    const size_t n = c.n;
+    const int rows = c.rows();
+    const int64_t h = (int64_t)n / 2;
+    std::vector<const Key*> keys(nsteps, nullptr);
+    std::vector<uint64_t> gs(nsteps);
+    bool any = false;
+    for (int i = 0; i < nsteps; ++i) {
+        gs[i] = powmod(5, (uint64_t)(((steps[i] % h) + h) % h), 2 * n);
+        if (gs[i] == 1) continue;
+        keys[i] = c.key_of(gs[i]);
+        if (!keys[i]) return -3;
+        any = true;
+    }
+    const uint64_t* c1 = x + (size_t)rows * n;
+    const std::vector<uint64_t> D = any ? modup(c, c1, top) : std::vector<uint64_t>();
+    std::vector<uint64_t> ext(c.ct_words());
+    for (int i = 0; i < nsteps; ++i) {
+        if (!keys[i]) {
+            for (int part = 0; part < 2; ++part)
+                memcpy(outs[i] + (size_t)part * rows * n, x + (size_t)part * rows * n, (size_t)(top + 1) * n * 8);
+            continue;
+        }
+        const uint64_t ginv = powmod(gs[i], (2 * n >> 2) - 1, 2 * n);
+        dot_ext(c, c1, D, x, 1, *keys[i], (uint32_t)ginv, ext.data(), top);
+        moddown(c, ext.data(), outs[i], top);
+    }
+    return 0;
+}
+
 int orc_rotate_batch(void* cv, const uint64_t* x, int k, int64_t step, uint64_t* out, int top) {
     Ctx& c = *(Ctx*)cv;
     const size_t cw = c.ct_words();

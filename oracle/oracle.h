@@ -117,6 +117,9 @@ int orc_moddown(void* c, const uint64_t* ext, uint64_t* out, int top);
  * Q ids; one rotation key switch of k ciphertexts. */
 int orc_ntt_batch(void* c, uint64_t* x, int nrows, int inverse);
 int orc_rotate_batch(void* c, const uint64_t* x, int k, int64_t step, uint64_t* out, int top);
+/* Hoisted rotations of one ciphertext: one ModUp shared by the nsteps steps, each with its own inner product and
+ * ModDown (a step of galois 1 is a copy); outs[i] [2][rows][N]. */
+int orc_rotate_hoisted(void* c, const uint64_t* x, const int64_t* steps, int nsteps, uint64_t* const* outs, int top);
 
 /* ---------------------------------------------------------------- plaintext-operand kernels (linear layers)
  * out[m][y] = x[m][y] t[y] for nx polynomials of nrows rows ([nx][nrows][N]; t [nrows][N]; row y mod primes[y]) */

@@ -89,6 +89,7 @@ def lib():
         "orc_moddown": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int]),
         "orc_ntt_batch": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int]),
         "orc_rotate_batch": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int64, u64p, C.c_int]),
+        "orc_rotate_hoisted": (C.c_int, [C.c_void_p, u64p, C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
         "orc_linear_transform": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_int64, u64p, C.c_int]),
         "orc_mul_rows": (C.c_int, [u64p, u64p, u64p, u64p, C.c_int, C.c_int, C.c_int]),
         "orc_pt_dot": (C.c_int, [u64p, u64p, u64p, u64p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -255,6 +256,15 @@ class Ctx:
         rc = lib().orc_rotate(self.h, np.ascontiguousarray(ct), step, out, top)
         assert rc == 0, rc
         return out
+
+    def rotate_hoisted(self, ct, steps, top):
+        """One ModUp shared by every step (orc_rotate_hoisted): one output per step."""
+        outs = [self.ct() for _ in steps]
+        st = np.asarray(steps, np.int64)
+        ptrs = (C.c_void_p * len(outs))(*[o.ctypes.data for o in outs])
+        rc = lib().orc_rotate_hoisted(self.h, np.ascontiguousarray(ct), st.ctypes.data, len(st), ptrs, top)
+        assert rc == 0, rc
+        return outs
 
     def rotate_and_sum(self, ct, start, stop, top, radix_bits=1):
         out = self.ct()

@@ -180,3 +180,23 @@ def test_linear_transform(ctx_r, npts, bstep):
     got = ctx_r.decrypt(out, top - 1, SLOTS, SCALE).real
     want = sum(dg * np.roll(x, -d) for d, dg in enumerate(diags))
     assert np.abs(got - want).max() < 1e-4
+
+
+def test_hoisted_rotations_equal_plain_ones():
+    """orc_rotate_hoisted (one ModUp for every step) = orc_rotate step by step, word for word; a step of galois 1
+    copies."""
+    logn = 10
+    q = O.ntt_primes(50, logn, 6)
+    p = O.ntt_primes(50, logn, 2, skip=6)
+    steps = [1, 3, 5, 1 << (logn - 1)]
+    c = O.Ctx(logn, q, p, 3)
+    c.keygen(0, 32, 3.2, [1] + [pow(5, s % (1 << (logn - 1)), 2 << logn) for s in steps[:3]])
+    rng = np.random.default_rng(7)
+    x = c.ct()
+    for r in range(len(q)):
+        x[:, r] = rng.integers(0, q[r], (2, 1 << logn), dtype=np.uint64)
+    for top in (len(q) - 1, 2):
+        outs = c.rotate_hoisted(x, steps, top)
+        for s, o in zip(steps[:3], outs):
+            assert (o[:, : top + 1] == c.rotate(x, s, top)[:, : top + 1]).all(), (top, s)
+        assert (outs[3][:, : top + 1] == x[:, : top + 1]).all()

@@ -596,9 +596,10 @@ def block_decode(a, world, barrier, dist, seqs=1):
     block), attention over the cache, output projection, residual (perseus_b200.block; N = 2^16 with the 24-limb
     chain, weights N(0, 0.02), biases, gamma 1 + N(0, 0.02), activation N(0, 1)).
     The cache starts with client-encrypted tokens and grows by one per step up to its 128; ms per token with CUDA
-    events (max over ranks), and the last step's decrypted error against the fp64 step. On N GPUs the 4 cache blocks
-    are split over the ranks (LaneCache shard=: each rank attends over its share, one all_gather of the partial
-    outputs summed mod p on every rank); the LayerNorm and the projections run on every rank."""
+    events (max over ranks), and the last step's decrypted error against the fp64 step. On N GPUs a single sequence's
+    4 cache blocks are split over the ranks (LaneCache shard=: each rank attends over its share, one all_gather of the
+    partial outputs summed mod p on every rank; the LayerNorm and the projections run on every rank); with seqs > 1
+    every rank decodes its own sequences (replicas, tokens/s over all GPUs)."""
     import numpy as np
     import torch
 
@@ -617,7 +618,8 @@ def block_decode(a, world, barrier, dist, seqs=1):
     wf, norm = B.fold_norm(w, gamma, beta), B.NormCfg()
     Ks = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
     Vs = [rng.normal(0, 1, (pre, n)) / 8 for _ in range(seqs)]
-    shard_ = (world, int(os.environ.get("RANK", "0"))) if world > 1 else None
+    # one sequence: its cache blocks split over the ranks (latency); several: every rank decodes its own (throughput)
+    shard_ = (world, int(os.environ.get("RANK", "0"))) if world > 1 and seqs == 1 else None
     cache = B.LaneCache(s, lay, top - 10, seqs=seqs, shard=shard_)
     cache.load(Ks if seqs > 1 else Ks[0], Vs if seqs > 1 else Vs[0])
     coeffs = A.softmax_poly(lay.tokens)
@@ -661,7 +663,8 @@ def block_decode(a, world, barrier, dist, seqs=1):
            "sharding": f"cache blocks over {world} GPU(s): {lay.blocks} blocks, one all_gather of the partial "
                        "outputs per token" if world > 1 else "one GPU"}
     if seqs > 1:
-        out = {"sequences": seqs, "ms_per_step": t.item(), "tokens_per_s": seqs / (t.item() * 1e-3),
+        out = {"sequences_per_gpu": seqs, "ms_per_step": t.item(), "tokens_per_s_all_gpus": world * seqs / (t.item() * 1e-3),
+               "parallelism": f"replicas x{world} (independent sequences)",
                "max_abs_err_vs_fp64_seq0": err}
     return out
 

@@ -198,3 +198,77 @@ def test_sharded_block_gloo(world):
     assert not alive, "a rank did not finish"
     assert not errs, errs
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _model_rank_main(rank, world, port, errq):
+    """The multi-layer decode (perseus_b200.model.Decoder) with every layer's cache blocks split over the ranks,
+    refreshes and MLP on every rank, against the unsharded decode on the same session randomness: every rank's
+    output equals the unsharded output word for word, and its blocks equal the matching unsharded blocks."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from perseus_b200 import bootstrap as BS
+        from perseus_b200 import fhe
+        from perseus_b200 import linear as LIN
+        from perseus_b200 import model as M
+        from tests import _oracle as O
+        from tests._oracle_ops import OracleOps
+
+        O.lib().orc_set_threads(2)
+        logn = 10
+        n_ring = 1 << logn
+        cfg = M.ModelCfg(layers=1, d=24, width=32, heads=3, head_dim=8, mlp=64, tokens=32, radix_bits=2)
+        prm = BS.Params(n_ring, K=24, r=3, per_group=5)
+        q = O.ntt_primes(50, logn, 25)
+        p = O.ntt_primes(50, logn, 6, skip=25)
+        lay = M.B.layout(n_ring // 2, cfg.width, cfg.heads, cfg.head_dim, cfg.tokens, cfg.radix_bits)
+        steps = sorted(set(BS.rot_steps(prm)) | set(lay.rot_steps()))
+        gal = list(dict.fromkeys([1] + [fhe.rotation_galois(s, logn) for s in steps] + [BS.conj_galois(n_ring)]))
+        rng = np.random.default_rng(52)
+        weights = [M.random_layer(rng, d=cfg.d, mlp=cfg.mlp, std=0.1)]
+        pre = 15  # token 15 lands in block 0, lane 15
+        Ks, Vs = [rng.normal(0, 1, (pre, cfg.d)) / 8], [rng.normal(0, 1, (pre, cfg.d)) / 8]
+        x = rng.normal(0, 1, cfg.d)
+        runs = []
+        for sh in (None, (world, rank)):
+            c = O.Ctx(logn, q, p, 5)
+            c.keygen(seed=0, h=64, sigma=3.2, galois=gal)
+            ops = OracleOps(c)
+            dec = M.Decoder(ops, cfg, weights, c.q, BS.Bootstrapper(ops, prm, c.q, c.q[0]), shard=sh)
+            dec.load(Ks, Vs)
+            y = dec.decode(ops.encrypt(LIN.input_vector(x, dec.lay.geo), 0, 2.0**40, dec.lay.slots))
+            runs.append((y, dec.caches[0]))
+        (y, full), (z, part) = runs
+        one = lambda c: c.cts[0] if hasattr(c, "cts") else c  # noqa: E731
+        y, z = one(y), one(z)
+        assert z.top == y.top and (z.data[:, : y.top + 1] == y.data[:, : y.top + 1]).all()
+        blocks = lambda b: b.cts if hasattr(b, "cts") else [b]  # noqa: E731
+        for li, b in enumerate(part.mine):
+            for mine_b, all_b in ((blocks(part.k)[li], blocks(full.k)[b]), (blocks(part.v)[li], blocks(full.v)[b])):
+                assert (mine_b.data[:, : part.top + 1] == all_b.data[:, : part.top + 1]).all(), b
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # the parent reports it
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_sharded_model_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_model_rank_main, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not alive, "a rank did not finish"
+    assert not errs, errs
+    assert all(p.exitcode == 0 for p in procs)

@@ -171,6 +171,94 @@ typedef struct PcbKsKeyArgs {
     PcbKeyTab key;
 } PcbKsKeyArgs;
 
+/* args.cuh:909-927 (coeff_sum): out (+)= sum_{r < n} ct[r] pt_r over Q limbs 0..L-1 (prime id = limb), pt_r[k] =
+ * round(rows[r][k] scale) (half to even; past the int64 range clamped to +-2^62 and counted per limb in *overflow when
+ * non-null) mod p_l, in the NTT domain (fw / fws: the forward twiddle tables of ntt_fwd). ct[r] and out: part 0 row 0,
+ * part 1 at + part_stride words, row l at + l N. rows[r]: N float32 coefficients in device memory. scratch: n L N
+ * words. accumulate != 0 adds onto out. n in [1, 32], L in [1, 64]. */
+#define PCB_COEFF_MAXT 32
+#define PCB_COEFF_MAXL 64
+typedef struct PcbCoeffArgs {
+    void* scratch;
+    void* out;
+    const void* fw;
+    const void* fws;
+    const PcbPrimeConst* pr;
+    unsigned long long* overflow;
+    uint64_t part_stride;
+    double scale;
+    int32_t n, L, accumulate, pad;
+    const float* rows[PCB_COEFF_MAXT];
+    const void* ct[PCB_COEFF_MAXT];
+} PcbCoeffArgs;
+
+/* args.cuh:230-242 (pack_split, the subring switch): rows y < nq of polynomial c at q + c q_stride + y N, the others
+ * at p + c p_stride + (y - nq) N (coefficient form); digit j (the exponents = j mod sub, zeros elsewhere) written
+ * at out + c out_stride + (j nrows + y) N. sub in {2, 4, 8, 16}, 0 <= nq <= nrows, K >= 1. */
+typedef struct PcbPackSplitArgs {
+    const void* q;
+    const void* p;
+    void* out;
+    uint64_t q_stride, p_stride, out_stride;
+    int32_t K, sub, nq, nrows;
+} PcbPackSplitArgs;
+
+/* args.cuh:244-261 (pack_dot, evaluation form): s1 = sum_j D_j a_j, s0 = sum_j D_j b_j (+ P c0 on rows y < nq) at prime
+ * id rows[y]; D as pack_split's out (dig, dig_stride), kb / ka [digit][row y][N]; c0 and the outputs by prime id
+ * rows, polynomial c at + c ct_stride / + c out_ct_stride. */
+typedef struct PcbPackDotArgs {
+    const void* dig;
+    const void* kb;
+    const void* ka;
+    const void* c0;
+    void* out0;
+    void* out1;
+    const uint32_t* rows;
+    const void* pmod;
+    const void* pmods;
+    const PcbPrimeConst* pr;
+    uint64_t dig_stride, ct_stride, out_ct_stride;
+    int32_t K, sub, nq, nrows;
+} PcbPackDotArgs;
+
+/* args.cuh:325-352 (cts_fused): one BSGS stage of CoeffToSlot with its baby rotations hoisted and never written, in
+ * the extended basis (Q rows and the special rows), K ciphertexts. For output slot o of row rows[y] (prime id t):
+ *   rot_0[o] = (P c0[o], P c1[o]) on Q rows, 0 on special rows (x0 non-null: the stored extended x0 row instead);
+ *   rot_i[o] = (P c0[s] + sum_d D_d[s] kb[i-1]_d[s], sum_d D_d[s] ka[i-1]_d[s]), s = automorph_slot(kinv[i-1], o),
+ *              D_d = c1 on digit d's own Q rows, else the ModUp output of digit d;
+ *   res_j[o] = sum_{i < B, B j + i < npts} rot_i[o] pts[B j + i][o]  for j < G <= 2.
+ * x: ct c at x + c ct_stride (c1 at + part_stride); modup: + c mu_ct_stride + d mu_digit_stride; keys [digit][prime id][N]
+ * (key_digit_stride); pts rows: Q prime id t at row t, special ids at pt_prow + (t - nq), ptw words, compact index enc;
+ * res (c, j) at res + (c G + j) ct_stride. ngrp is the launcher's; kmax a grouping hint; pair_cts must be 0 here. */
+typedef struct PcbCtsArgs {
+    const void* x;
+    const void* modup;
+    void* res;
+    const void* const* kb;
+    const void* const* ka;
+    const uint32_t* kinv;
+    const void* const* pts;
+    const uint32_t* rows;
+    const int32_t* digit_of;
+    const void* pmod;
+    const void* pmods;
+    const PcbPrimeConst* pr;
+    uint64_t ct_stride, part_stride, mu_ct_stride, mu_digit_stride, key_digit_stride;
+    int32_t K, B, G, npts, ndig, nq, nlive, ptw, pt_prow;
+    uint32_t enc;
+    int32_t ngrp;
+    int32_t nrows, kmax;
+    int32_t pair_cts;
+    const void* x0;
+} PcbCtsArgs;
+
+/* args.cuh:754-758 (cts_fused_regen): cts_fused with the baby keys read through the key table: `b` dense rows of
+ * key.kb[i-1] in the key's slot order, `a` regenerated from key.seed[i-1] below key.nregen (cts.ka[i-1] above). */
+typedef struct PcbCtsRegenArgs {
+    PcbCtsArgs cts;
+    PcbKeyTab key;
+} PcbCtsRegenArgs;
+
 /* args.cuh:306-323: out[d][m][N] = expander(seed, digit d, prime prime_ids[m]) (u64: the frozen KSKB lane) */
 typedef struct PcbKskExpandArgs {
     void* out;
@@ -190,6 +278,16 @@ typedef struct PcbTensorArgs {
     int32_t npairs, acc, n, K;
     int32_t dbl, acc_d2;
 } PcbTensorArgs;
+
+/* args.cuh:369-378 (tensor_y): the tensor above, then (c0, c1) += c[row] y (sub: -=) with Shoup companion cs[row],
+ * both parts of y, after the doubling; d2 unchanged. EvalMod's x y +- c t before its relinearization in one pass. */
+typedef struct PcbTensorYArgs {
+    PcbTensorArgs t;
+    PcbPolyRef y;
+    const void* c;
+    const void* cs;
+    int32_t sub, pad;
+} PcbTensorYArgs;
 
 /* args.cuh:184-200: BSGS plaintext dot of K ciphertexts' baby rotations (rows of rs, both parts):
  *   res[c][j] = sum_{b < bstep, d = bstep j + b < npts} rot[c][b] * pts[d]   for j < gstep
@@ -427,6 +525,17 @@ typedef struct PcbModRaiseArgs {
     int32_t K, d, r0, r1, nparts, pad;
 } PcbModRaiseArgs;
 
+/* args.cuh:892-907 (small_int1): the exact post-raise scaling from one source prime, in place over rows [0, nrows)
+ * of K cts (nparts polynomials from part 0, coefficient form): x = row 0 centred against q0, q = round(|x| mc / 2^sh)
+ * (half up; 1 <= sh <= 127, q < 2^64 by the caller), row t := sign(x) q mod q_t. Row 0 is read before any write. */
+typedef struct PcbSmallInt1Args {
+    void* x;
+    const PcbPrimeConst* pr;
+    uint64_t ct_stride, part_stride;
+    uint64_t mc;
+    int32_t sh, nrows, K, nparts;
+} PcbSmallInt1Args;
+
 typedef int (*PcbLaunch)(const void* args, cudaStream_t stream);
 
 /* args.cuh:1034-1097: 16-byte header then 52 launchers, in the reference's order */
@@ -443,7 +552,7 @@ typedef struct PcbKernelTable {
     int (*ks_dot)(const PcbKsArgs*, cudaStream_t);
     int (*ks_dot_regen)(const PcbKsRegenArgs*, cudaStream_t);
     int (*ksk_expand)(const PcbKskExpandArgs*, cudaStream_t);
-    PcbLaunch cts_fused;
+    int (*cts_fused)(const PcbCtsArgs*, cudaStream_t);
     int (*tensor)(const PcbTensorArgs*, cudaStream_t);
     int (*md_epilogue)(const PcbMdEpiArgs*, cudaStream_t);
     int (*wsum)(const PcbWsumArgs*, cudaStream_t);
@@ -457,25 +566,29 @@ typedef struct PcbKernelTable {
     int (*ksk_gen)(const PcbKskGenArgs*, cudaStream_t);
     int (*ksk_unpack)(const PcbKskUnpackArgs*, cudaStream_t);
     int (*mod_raise)(const PcbModRaiseArgs*, cudaStream_t);
-    PcbLaunch small_int, spru_extract, spru_fft_pass, spru_scatter, cts_fused_regen;
+    PcbLaunch small_int, spru_extract, spru_fft_pass, spru_scatter;
+    int (*cts_fused_regen)(const PcbCtsRegenArgs*, cudaStream_t);
     int (*ks_dot_key)(const PcbKsKeyArgs*, cudaStream_t);
     PcbLaunch pcmm, ccmm;
     int (*wsum_k)(const PcbWsumKArgs*, cudaStream_t);
     int (*rescale_combine_to)(const PcbRescaleCombineToArgs*, cudaStream_t);
     int (*md_epilogue_to)(const PcbMdEpiToArgs*, cudaStream_t);
-    PcbLaunch small_int1, coeff_sum;
+    int (*small_int1)(const PcbSmallInt1Args*, cudaStream_t);
+    int (*coeff_sum)(const PcbCoeffArgs*, cudaStream_t);
     int (*mul_add)(const PcbMulAddArgs*, cudaStream_t);
     int (*rescale_fwd)(const PcbRescaleNttArgs*, cudaStream_t);
     int (*mul_add_n)(const PcbMulAddNArgs*, cudaStream_t);
-    PcbLaunch tensor_y;
+    int (*tensor_y)(const PcbTensorYArgs*, cudaStream_t);
     int (*wsum_multi)(const PcbWsumMultiArgs*, cudaStream_t);
-    PcbLaunch bconv_wide, tfhe;
+    int (*bconv_wide)(const PcbBconvArgs*, cudaStream_t);
+    PcbLaunch tfhe;
     int (*tensor_sum)(const PcbTensorSumArgs*, cudaStream_t);
     int (*tensor_multi)(const PcbTensorMultiArgs*, cudaStream_t);
     PcbLaunch tensor_seeded;
     int (*ew_many)(const PcbEwManyArgs*, cudaStream_t);
     int (*submul_many)(const PcbSubMulManyArgs*, cudaStream_t);
-    PcbLaunch pack_split, pack_dot;
+    int (*pack_split)(const PcbPackSplitArgs*, cudaStream_t);
+    int (*pack_dot)(const PcbPackDotArgs*, cudaStream_t);
 } PcbKernelTable;
 
 /* args.cuh:1099-1119: ring-size tables (rows of 2^log_n words) */
@@ -721,6 +834,13 @@ static_assert(sizeof(PcbKsRegenArgs) == 312, "KsRegenArgs layout");
 static_assert(sizeof(PcbKsKeyArgs) == 216, "KsKeyArgs layout");
 static_assert(sizeof(PcbKskExpandArgs) == 48, "KskExpandArgs layout");
 static_assert(sizeof(PcbTensorArgs) == 192, "TensorArgs layout");
+static_assert(sizeof(PcbTensorYArgs) == 240, "TensorYArgs layout");
+static_assert(sizeof(PcbCtsArgs) == 200, "CtsArgs layout");
+static_assert(sizeof(PcbPackSplitArgs) == 64, "PackSplitArgs layout");
+static_assert(sizeof(PcbCoeffArgs) == 80 + 16 * PCB_COEFF_MAXT, "CoeffArgs layout");
+static_assert(sizeof(PcbPackDotArgs) == 120, "PackDotArgs layout");
+static_assert(sizeof(PcbCtsRegenArgs) == 240, "CtsRegenArgs layout");
+static_assert(sizeof(PcbSmallInt1Args) == 56, "SmallInt1Args layout");
 static_assert(sizeof(PcbMdEpiArgs) == 120, "MdEpiArgs layout");
 static_assert(sizeof(PcbRescaleArgs) == 152, "RescaleArgs layout");
 static_assert(sizeof(PcbRescaleCombineArgs) == 80, "RescaleCombineArgs layout");

@@ -77,6 +77,39 @@ class KsKeyArgs(C.Structure):
     _fields_ = [("ks", KsArgs), ("key", KeyTab)]
 
 
+class CoeffArgs(C.Structure):
+    _fields_ = [("scratch", vp), ("out", vp), ("fw", vp), ("fws", vp), ("pr", vp), ("overflow", vp),
+                ("part_stride", C.c_uint64), ("scale", C.c_double), ("n", C.c_int32), ("L", C.c_int32),
+                ("accumulate", C.c_int32), ("pad", C.c_int32), ("rows", vp * 32), ("ct", vp * 32)]
+
+
+class PackSplitArgs(C.Structure):
+    _fields_ = [("q", vp), ("p", vp), ("out", vp), ("q_stride", C.c_uint64), ("p_stride", C.c_uint64),
+                ("out_stride", C.c_uint64), ("K", C.c_int32), ("sub", C.c_int32), ("nq", C.c_int32),
+                ("nrows", C.c_int32)]
+
+
+class PackDotArgs(C.Structure):
+    _fields_ = [("dig", vp), ("kb", vp), ("ka", vp), ("c0", vp), ("out0", vp), ("out1", vp), ("rows", vp),
+                ("pmod", vp), ("pmods", vp), ("pr", vp), ("dig_stride", C.c_uint64), ("ct_stride", C.c_uint64),
+                ("out_ct_stride", C.c_uint64), ("K", C.c_int32), ("sub", C.c_int32), ("nq", C.c_int32),
+                ("nrows", C.c_int32)]
+
+
+class CtsArgs(C.Structure):
+    _fields_ = [("x", vp), ("modup", vp), ("res", vp), ("kb", vp), ("ka", vp), ("kinv", vp), ("pts", vp), ("rows", vp),
+                ("digit_of", vp), ("pmod", vp), ("pmods", vp), ("pr", vp), ("ct_stride", C.c_uint64),
+                ("part_stride", C.c_uint64), ("mu_ct_stride", C.c_uint64), ("mu_digit_stride", C.c_uint64),
+                ("key_digit_stride", C.c_uint64)] + [(n, C.c_int32) for n in (
+                    "K", "B", "G", "npts", "ndig", "nq", "nlive", "ptw", "pt_prow")] + [
+                ("enc", C.c_uint32), ("ngrp", C.c_int32), ("nrows", C.c_int32), ("kmax", C.c_int32),
+                ("pair_cts", C.c_int32), ("x0", vp)]
+
+
+class CtsRegenArgs(C.Structure):
+    _fields_ = [("cts", CtsArgs), ("key", KeyTab)]
+
+
 class KskExpandArgs(C.Structure):
     _fields_ = [("out", vp), ("seed", vp), ("prime_ids", vp), ("pr", vp), ("nmod", C.c_int32), ("dnum", C.c_int32),
                 ("d0", C.c_int32), ("pad", C.c_int32)]
@@ -86,6 +119,10 @@ class TensorArgs(C.Structure):
     _fields_ = [("out", PolyRef), ("d2", PolyRef), ("a0", PolyRef), ("b0", PolyRef), ("a1", PolyRef),
                 ("b1", PolyRef), ("coef", vp), ("coef_ct_stride", C.c_uint64), ("pr", vp), ("npairs", C.c_int32),
                 ("acc", C.c_int32), ("n", C.c_int32), ("K", C.c_int32), ("dbl", C.c_int32), ("acc_d2", C.c_int32)]
+
+
+class TensorYArgs(C.Structure):
+    _fields_ = [("t", TensorArgs), ("y", PolyRef), ("c", vp), ("cs", vp), ("sub", C.c_int32), ("pad", C.c_int32)]
 
 
 class MdEpiArgs(C.Structure):
@@ -195,6 +232,11 @@ class ModRaiseArgs(C.Structure):
                 ("r0", C.c_int32), ("r1", C.c_int32), ("nparts", C.c_int32), ("pad", C.c_int32)]
 
 
+class SmallInt1Args(C.Structure):
+    _fields_ = [("x", vp), ("pr", vp), ("ct_stride", C.c_uint64), ("part_stride", C.c_uint64), ("mc", C.c_uint64),
+                ("sh", C.c_int32), ("nrows", C.c_int32), ("K", C.c_int32), ("nparts", C.c_int32)]
+
+
 class KskUnpackArgs(C.Structure):
     _fields_ = [("out", vp), ("in_", vp), ("row_words", C.c_uint64), ("nrows", C.c_int32), ("bits", C.c_int32)]
 
@@ -238,7 +280,7 @@ SIZES = {"PrimeConst": 64, "RowSet": 16, "PolyRef": 24, "NttArgs": 176, "BconvJo
          "EwArgs": 128, "KsArgs": 176, "EpiArgs": 72, "KeyTab": 40, "KsRegenArgs": 312, "KskExpandArgs": 48,
          "TensorArgs": 192, "MdEpiArgs": 120, "RescaleArgs": 152, "RescaleCombineArgs": 80, "AutomorphArgs": 112,
          "EncryptArgs": 64, "KskGenArgs": 120, "KskUnpackArgs": 32, "KsKeyArgs": 216, "PtDotArgs": 128, "AddConstArgs": 48, "MulTableArgs": 72,
-         "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "RescaleNttArgs": 328,
+         "MulAddArgs": 104, "MulAddNArgs": 328, "ModRaiseArgs": 2136, "TensorYArgs": 240, "CtsArgs": 200, "PackSplitArgs": 64, "CoeffArgs": 80 + 16 * 32, "PackDotArgs": 120, "CtsRegenArgs": 240, "SmallInt1Args": 56, "RescaleNttArgs": 328,
          "RescaleCombineToArgs": 104, "MdEpiToArgs": 152, "WsumArgs": 256, "WsumKArgs": 264, "WsumMultiArgs": 376,
          "EwManyArgs": 4 * 48 * 8 + 16, "SubMulManyArgs": 3 * 48 * 8 + 24, "TensorSumArgs": 2 * 24 + 2 * 16 * 24 + 24,
          "TensorMultiArgs": (2 * 4 + 2 * 4 * 32) * 24 + 32, "KernelTable": 16 + 52 * 8, "RingTable": 16 + 9 * 8}

@@ -12,7 +12,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpcb200.so")
-SOURCES = ["ntt.cu", "elem.cu", "pt.cu", "ks.cu", "regen.cu", "keys.cu", "table.cu", "evaluator.cu", "probe.cu", "wire.cu", "elem_multi.cu"]
+SOURCES = ["ntt.cu", "elem.cu", "pt.cu", "ks.cu", "regen.cu", "keys.cu", "table.cu", "evaluator.cu", "probe.cu", "wire.cu", "elem_multi.cu", "cts.cu"]
 HEADERS = ["arith.cuh", "chacha.cuh", "keyregen.cuh", "kernels.h", "host_math.h", "ntt_pipe.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [

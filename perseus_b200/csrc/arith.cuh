@@ -119,6 +119,11 @@ __device__ __forceinline__ uint32_t automorph_slot(uint32_t k, uint32_t o) {
     const uint32_t r = (((j << 1) + 1) * k & ((2u << LOGN) - 1)) >> 1;
     return __brev(r) >> (32 - LOGN);
 }
+// compact plaintext index (args.cuh:184-188): enc = 0xFFFFFFFF full rows; (enc >> 24) == 0x7F: i >> (enc & 0xFF)
+// (each plaintext word serves 2^s consecutive slots); otherwise i & enc (a period)
+__device__ __forceinline__ uint32_t pt_index(uint32_t i, uint32_t enc) {
+    return (enc >> 24) == 0x7Fu ? i >> (enc & 0xFFu) : i & enc;
+}
 __device__ __forceinline__ uint32_t automorph_slot_n(uint32_t k, uint32_t o, int logn) {
     const uint32_t j = __brev(o) >> (32 - logn);
     const uint32_t r = (((j << 1) + 1) * k & ((2u << logn) - 1)) >> 1;

@@ -89,9 +89,11 @@ int ew_launch(const PcbEwArgs* ap, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ tensor
-// (c0, c1, d2) = sum over up to two pairs (a, b) of (a0 b0, a0 b1 + a1 b0, a1 b1): lazy 128-bit sums, one reduction
-template <int LOGN>
-__global__ void __launch_bounds__(BX) tensor(PcbTensorArgs a) {
+// (c0, c1, d2) = sum over up to two pairs (a, b) of (a0 b0, a0 b1 + a1 b0, a1 b1): lazy 128-bit sums, one reduction.
+// Y (tensor_y, args.cuh:369-378): then (c0, c1) +/-= c[row] y, after the doubling (EvalMod's x y +/- c t in one pass).
+template <int LOGN, bool Y>
+__global__ void __launch_bounds__(BX) tensor(PcbTensorYArgs g) {
+    const PcbTensorArgs& a = g.t;
     const int row = blockIdx.y, c = blockIdx.z;
     const PcbPrimeConst& pc = a.pr[row];
     const uint64_t p = pc.p;
@@ -143,23 +145,50 @@ __global__ void __launch_bounds__(BX) tensor(PcbTensorArgs a) {
             r2[w] = add_mod(r2[w], r2[w], p);
         }
     }
+    if (Y) {
+        const uint64_t m = ((const uint64_t*)g.c)[row], ms = ((const uint64_t*)g.cs)[row];
+        const V4 y0 = ld4(at_row(g.y, c, 0, row, LOGN) + i), y1 = ld4(at_row(g.y, c, 1, row, LOGN) + i);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint64_t u0 = shoup(y0.v[w], m, ms, p), u1 = shoup(y1.v[w], m, ms, p);
+            r0[w] = g.sub ? sub_mod(r0[w], u0, p) : add_mod(r0[w], u0, p);
+            r1[w] = g.sub ? sub_mod(r1[w], u1, p) : add_mod(r1[w], u1, p);
+        }
+    }
     st4(o0, r0);
     st4(o1, r1);
     st4(o2, r2);
     if (a.coef) st4((uint64_t*)a.coef + (size_t)c * a.coef_ct_stride + ((size_t)row << LOGN) + i, r2);
 }
 
-template <int LOGN>
-int tensor_launch(const PcbTensorArgs* ap, cudaStream_t s) {
-    if (!ap) return PCB_BAD_ARGS;
-    const PcbTensorArgs& a = *ap;
+__host__ inline int tensor_check(const PcbTensorArgs& a) {
     if (a.npairs < 1 || a.npairs > 2 || a.n < 0 || a.K < 0 || !a.pr || !a.out.base || !a.d2.base || !a.a0.base ||
         !a.b0.base || (a.npairs == 2 && (!a.a1.base || !a.b1.base)))
         return PCB_BAD_ARGS;
     if (!ok16(a.out) || !ok16(a.d2) || !ok16(a.a0) || !ok16(a.b0) || (a.npairs == 2 && (!ok16(a.a1) || !ok16(a.b1))))
         return PCB_BAD_ARGS;
-    if (a.n == 0 || a.K == 0) return 0;
-    tensor<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.n, a.K), BX, 0, s>>>(a);
+    return 0;
+}
+
+template <int LOGN>
+int tensor_launch(const PcbTensorArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    if (const int rc = tensor_check(*ap)) return rc;
+    if (ap->n == 0 || ap->K == 0) return 0;
+    PcbTensorYArgs g;
+    memset(&g, 0, sizeof g);
+    g.t = *ap;
+    tensor<LOGN, false><<<dim3((1 << LOGN) / (BX * WPT), ap->n, ap->K), BX, 0, s>>>(g);
+    return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int tensor_y_launch(const PcbTensorYArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    if (const int rc = tensor_check(ap->t)) return rc;
+    if (!ap->c || !ap->cs || !ap->y.base || !ok16(ap->y)) return PCB_BAD_ARGS;
+    if (ap->t.n == 0 || ap->t.K == 0) return 0;
+    tensor<LOGN, true><<<dim3((1 << LOGN) / (BX * WPT), ap->t.n, ap->t.K), BX, 0, s>>>(*ap);
     return PCB_LAUNCH_RESULT();
 }
 
@@ -305,6 +334,45 @@ int mod_raise_launch(const PcbModRaiseArgs* ap, cudaStream_t s) {
     return PCB_LAUNCH_RESULT();
 }
 
+// args.cuh:892-907 (small_int1): the raise of a one-prime source with an exact scaling folded in. The centred
+// value x of row 0 times the scale mc 2^-sh is rounded half up in 128-bit integers (|x| < 2^63, mc < 2^64: the
+// product and the half fit), and its sign put back on the residue of every row.
+template <int LOGN>
+__global__ void __launch_bounds__(BX) small_int1(PcbSmallInt1Args a) {
+    const size_t i = (size_t)blockIdx.x * BX + threadIdx.x;
+    uint64_t* x = (uint64_t*)a.x + (size_t)blockIdx.z * a.ct_stride + (size_t)blockIdx.y * a.part_stride;
+    const uint64_t q0 = a.pr[0].p;
+    const uint64_t v = x[i];
+    const bool neg = v > q0 / 2;
+    const uint64_t mag = neg ? q0 - v : v;
+    uint64_t lo = mag * a.mc, hi = __umul64hi(mag, a.mc);
+    if (a.sh <= 64) {
+        const uint64_t h = 1ull << (a.sh - 1);
+        lo += h;
+        hi += lo < h;
+    } else {
+        hi += 1ull << (a.sh - 65);
+    }
+    const uint64_t q = a.sh < 64 ? (lo >> a.sh) | (hi << (64 - a.sh)) : hi >> (a.sh - 64);
+    for (int t = 0; t < a.nrows; ++t) {
+        const PcbPrimeConst& pt = a.pr[t];
+        const uint64_t r = reduce(Acc{q, 0}, pt);
+        x[((size_t)t << LOGN) + i] = neg && r ? pt.p - r : r;
+    }
+}
+
+template <int LOGN>
+int small_int1_launch(const PcbSmallInt1Args* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbSmallInt1Args& a = *ap;
+    if (!a.x || !a.pr || a.sh < 1 || a.sh > 127 || a.nrows < 1 || a.nrows > 64 || a.K < 0 || a.nparts < 1 ||
+        a.nparts > 2)
+        return PCB_BAD_ARGS;
+    if (a.K == 0) return 0;
+    small_int1<LOGN><<<dim3((1 << LOGN) / BX, a.nparts, a.K), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
 template <int LOGN>
 __global__ void __launch_bounds__(BX) rescale_combine(PcbRescaleCombineArgs a) {
     const int row = blockIdx.y, c = blockIdx.z >> 1, part = blockIdx.z & 1;
@@ -397,9 +465,11 @@ int sum_launch(const SumArgs* ap, cudaStream_t s) {
     template int ew_launch<L, EW_SUB_MUL>(const PcbEwArgs*, cudaStream_t);                           \
     template int ew_launch<L, EW_COPY>(const PcbEwArgs*, cudaStream_t);                              \
     template int tensor_launch<L>(const PcbTensorArgs*, cudaStream_t);                               \
+    template int tensor_y_launch<L>(const PcbTensorYArgs*, cudaStream_t);                            \
     template int md_epilogue_launch<L>(const PcbMdEpiArgs*, cudaStream_t);                           \
     template int rescale_coef_launch<L>(const PcbRescaleArgs*, cudaStream_t);                        \
     template int mod_raise_launch<L>(const PcbModRaiseArgs*, cudaStream_t);                          \
+    template int small_int1_launch<L>(const PcbSmallInt1Args*, cudaStream_t);                       \
     template int rescale_combine_launch<L>(const PcbRescaleCombineArgs*, cudaStream_t);              \
     template int automorph_launch<L>(const PcbAutomorphArgs*, cudaStream_t);
 PCB_INST(14)

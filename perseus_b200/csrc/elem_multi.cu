@@ -6,7 +6,8 @@
 // RescaleNttArgs :553-562, RescaleCombineToArgs :573-578). Every output is the canonical residue of an exact sum, so
 // the words equal the reference's whatever the order of the reduction.
 //
-// All are HBM-bound streams laid out as elem.cu's: 4 consecutive words per thread with 16-byte accesses, grids
+// The subring switch's pack_split / pack_dot (crates/pc-gpu/src/ks/pack.rs; PackSplitArgs :230-242, PackDotArgs
+// :244-261) sit here too. All are HBM-bound streams laid out as elem.cu's: 4 consecutive words per thread with 16-byte accesses, grids
 // (N / 1024, rows, ciphertexts [x parts]).
 #include "arith.cuh"
 #include "kernels.h"
@@ -365,7 +366,104 @@ int rescale_fwd_launch(const PcbRescaleNttArgs* ap, cudaStream_t s) {
     return ntt::fwd<LOGN>(&ap->ntt, s);
 }
 
+// ------------------------------------------------------------------------------------------------ subring switch
+// pack_split (coefficient form): digit j of row y keeps the coefficients whose exponent is j mod sub, zeros elsewhere;
+// rows y < nq come from q, the others from p (row y - nq). Four words per thread: their classes are consecutive.
+template <int LOGN>
+__global__ void __launch_bounds__(BXM) pack_split(PcbPackSplitArgs a) {
+    const int y = blockIdx.y, c = blockIdx.z;
+    const size_t i = word0();
+    const uint64_t* src = y < a.nq ? (const uint64_t*)a.q + (size_t)c * a.q_stride + ((size_t)y << LOGN)
+                                   : (const uint64_t*)a.p + (size_t)c * a.p_stride + ((size_t)(y - a.nq) << LOGN);
+    const W4 v = ld(src + i);
+    uint64_t* o = (uint64_t*)a.out + (size_t)c * a.out_stride + ((size_t)y << LOGN) + i;
+    const size_t dstride = (size_t)a.nrows << LOGN;
+    const uint32_t m = (uint32_t)a.sub - 1;
+    for (int j = 0; j < a.sub; ++j) {
+        uint64_t r[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r[w] = ((uint32_t)(i + w) & m) == (uint32_t)j ? v.v[w] : 0;
+        st(o + (size_t)j * dstride, r);
+    }
+}
+
+// pack_dot (evaluation form): s1 = sum_j D_j a_j, s0 = sum_j D_j b_j (+ P c0 on rows y < nq) at prime id rows[y]; the
+// digits and the key rows by row index y, c0 and the outputs by prime id. sub <= 16 products of words below 2^62
+// stay below 2^128: one reduction.
+template <int LOGN>
+__global__ void __launch_bounds__(BXM) pack_dot(PcbPackDotArgs a) {
+    const int y = blockIdx.y, c = blockIdx.z;
+    const uint32_t t = a.rows[y];
+    const PcbPrimeConst& pc = a.pr[t];
+    const uint64_t p = pc.p;
+    const size_t i = word0();
+    const size_t koff = ((size_t)y << LOGN) + i, dstride = (size_t)a.nrows << LOGN;
+    const uint64_t* dg = (const uint64_t*)a.dig + (size_t)c * a.dig_stride + koff;
+    Acc s0[4], s1[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) s0[w] = s1[w] = Acc{0, 0};
+    for (int j = 0; j < a.sub; ++j) {
+        const W4 x = ld(dg + (size_t)j * dstride);
+        const W4 b = ld((const uint64_t*)a.kb + koff + (size_t)j * dstride);
+        const W4 k = ld((const uint64_t*)a.ka + koff + (size_t)j * dstride);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            mac(s0[w], x.v[w], b.v[w]);
+            mac(s1[w], x.v[w], k.v[w]);
+        }
+    }
+    const size_t roff = ((size_t)t << LOGN) + i;
+    uint64_t r0[4], r1[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        r0[w] = reduce(s0[w], pc);
+        r1[w] = reduce(s1[w], pc);
+    }
+    if (y < a.nq) {
+        const uint64_t pm = ((const uint64_t*)a.pmod)[t], pms = ((const uint64_t*)a.pmods)[t];
+        const W4 x = ld((const uint64_t*)a.c0 + (size_t)c * a.ct_stride + roff);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) r0[w] = add_mod(r0[w], shoup(x.v[w], pm, pms, p), p);
+    }
+    st((uint64_t*)a.out0 + (size_t)c * a.out_ct_stride + roff, r0);
+    st((uint64_t*)a.out1 + (size_t)c * a.out_ct_stride + roff, r1);
+}
+
+__host__ inline bool pack_ok(int sub, int nq, int nrows, int K) {
+    return sub >= 2 && sub <= 16 && (sub & (sub - 1)) == 0 && nq >= 0 && nq <= nrows && K >= 1;
+}
+
+template <int LOGN>
+int pack_split_launch(const PcbPackSplitArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbPackSplitArgs& a = *ap;
+    if (!pack_ok(a.sub, a.nq, a.nrows, a.K) || !a.out || (a.nq > 0 && !a.q) || (a.nrows > a.nq && !a.p))
+        return PCB_BAD_ARGS;
+    if (!al16(a.out) || (a.q && !al16(a.q)) || (a.p && !al16(a.p)) || ((a.q_stride | a.p_stride | a.out_stride) & 1))
+        return PCB_BAD_ARGS;
+    if (a.nrows == 0) return 0;
+    pack_split<LOGN><<<dim3((1 << LOGN) / (BXM * 4), a.nrows, a.K), BXM, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
+template <int LOGN>
+int pack_dot_launch(const PcbPackDotArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbPackDotArgs& a = *ap;
+    if (!pack_ok(a.sub, a.nq, a.nrows, a.K) || !a.dig || !a.kb || !a.ka || !a.out0 || !a.out1 || !a.rows || !a.pr ||
+        (a.nq > 0 && (!a.c0 || !a.pmod || !a.pmods)))
+        return PCB_BAD_ARGS;
+    if (!al16(a.dig) || !al16(a.kb) || !al16(a.ka) || !al16(a.out0) || !al16(a.out1) || (a.c0 && !al16(a.c0)) ||
+        ((a.dig_stride | a.ct_stride | a.out_ct_stride) & 1))
+        return PCB_BAD_ARGS;
+    if (a.nrows == 0) return 0;
+    pack_dot<LOGN><<<dim3((1 << LOGN) / (BXM * 4), a.nrows, a.K), BXM, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
 #define PCB_MULTI_INST(L)                                                                    \
+    template int pack_split_launch<L>(const PcbPackSplitArgs*, cudaStream_t);                \
+    template int pack_dot_launch<L>(const PcbPackDotArgs*, cudaStream_t);                    \
     template int ew_many_launch<L>(const PcbEwManyArgs*, cudaStream_t);                      \
     template int submul_many_launch<L>(const PcbSubMulManyArgs*, cudaStream_t);              \
     template int wsum_launch<L>(const PcbWsumArgs*, cudaStream_t);                           \

@@ -24,10 +24,12 @@ struct SumArgs {
 template <int LOGN> int sum_launch(const SumArgs*, cudaStream_t);
 template <int LOGN, int OP> int ew_launch(const PcbEwArgs*, cudaStream_t);
 template <int LOGN> int tensor_launch(const PcbTensorArgs*, cudaStream_t);
+template <int LOGN> int tensor_y_launch(const PcbTensorYArgs*, cudaStream_t);
 template <int LOGN> int md_epilogue_launch(const PcbMdEpiArgs*, cudaStream_t);
 template <int LOGN> int rescale_coef_launch(const PcbRescaleArgs*, cudaStream_t);
 template <int LOGN> int rescale_combine_launch(const PcbRescaleCombineArgs*, cudaStream_t);
 template <int LOGN> int mod_raise_launch(const PcbModRaiseArgs*, cudaStream_t);
+template <int LOGN> int small_int1_launch(const PcbSmallInt1Args*, cudaStream_t);
 template <int LOGN> int automorph_launch(const PcbAutomorphArgs*, cudaStream_t);
 }  // namespace elem
 namespace pt {
@@ -36,6 +38,7 @@ template <int LOGN> int mul_table_launch(const PcbMulTableArgs*, cudaStream_t);
 template <int LOGN> int mul_add_launch(const PcbMulAddArgs*, cudaStream_t);
 template <int LOGN> int mul_add_n_launch(const PcbMulAddNArgs*, cudaStream_t);
 template <int LOGN> int pt_dot_launch(const PcbPtDotArgs*, cudaStream_t);
+template <int LOGN> int coeff_sum_launch(const PcbCoeffArgs*, cudaStream_t);
 }  // namespace pt
 namespace ks {
 template <int LOGN> int bconv_launch(const PcbBconvArgs*, cudaStream_t);
@@ -80,9 +83,15 @@ namespace regen {
 template <int LOGN> int ks_dot_regen_launch(const PcbKsRegenArgs*, cudaStream_t);
 template <int LOGN> int ks_dot_key_launch(const PcbKsKeyArgs*, cudaStream_t);
 }  // namespace regen
+namespace cts {
+template <int LOGN> int cts_fused_launch(const PcbCtsArgs*, cudaStream_t);
+template <int LOGN> int cts_fused_regen_launch(const PcbCtsRegenArgs*, cudaStream_t);
+}  // namespace cts
 namespace elem {  // elem_multi.cu
 template <int LOGN> int ew_many_launch(const PcbEwManyArgs*, cudaStream_t);
 template <int LOGN> int submul_many_launch(const PcbSubMulManyArgs*, cudaStream_t);
+template <int LOGN> int pack_split_launch(const PcbPackSplitArgs*, cudaStream_t);
+template <int LOGN> int pack_dot_launch(const PcbPackDotArgs*, cudaStream_t);
 template <int LOGN> int wsum_launch(const PcbWsumArgs*, cudaStream_t);
 template <int LOGN> int wsum_k_launch(const PcbWsumKArgs*, cudaStream_t);
 template <int LOGN> int wsum_multi_launch(const PcbWsumMultiArgs*, cudaStream_t);

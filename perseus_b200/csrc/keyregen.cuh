@@ -38,6 +38,11 @@ __device__ __forceinline__ void stage(const uint32_t* const* seeds, int nkeys, i
     __syncthreads();
 }
 
+// the key-table slot of prime id t: Q ids at their index up to q_top, special ids right after; q_top < 0: prime id
+__device__ __forceinline__ int key_slot(const PcbKeyTab& T, int t, int nq) {
+    return (t < nq || T.q_top < 0) ? t : T.q_top + 1 + (t - nq);
+}
+
 // The staged word of key r, digit d at slot `slot` of segment j (the slot's own segment, 0 <= slot % SEG < SEG)
 __device__ __forceinline__ uint64_t at(const uint64_t* sm, int ndig, int nseg, int r, int d, int j, uint32_t slot) {
     return sm[((size_t)(r * ndig + d) * nseg + j) * SEG + (slot & (SEG - 1))];

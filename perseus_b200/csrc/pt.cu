@@ -1,7 +1,8 @@
 // Plaintext-operand kernels of the linear layers: pt_dot (the BSGS baby-step dot), mul_table (ct x pt), mul_add
 // (y +- ct x pt in one pass), mul_add_n (a chain of ct x pt products summed in one pass) and add_const. Semantics
 // of crates/pc-kernels/kernels/args.cuh (PtDotArgs :184-200, AddConstArgs / MulTableArgs / MulAddArgs /
-// MulAddNArgs :491-528); host twin crates/pc-host/src/elem.rs:145-180.
+// MulAddNArgs :491-528); host twin crates/pc-host/src/elem.rs:145-180. coeff_sum (the streamed-weight inner sum,
+// CoeffArgs :909-927; caller crates/pc-gpu/src/encode_dev.rs) closes the file.
 //
 // All five are HBM streams over residue rows: no reuse inside a thread beyond the pt_dot sums, so the design is about
 // bytes. Sums of products are kept in 128-bit accumulators and reduced once (the Barrett reduction of arith.cuh is
@@ -154,12 +155,6 @@ int mul_add_n_launch(const PcbMulAddNArgs* ap, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ pt_dot
-// compact plaintext index (args.cuh:184-188): enc = 0xFFFFFFFF full rows; (enc >> 24) == 0x7F: i >> (enc & 0xFF)
-// (each plaintext word serves 2^s consecutive slots); otherwise i & enc (a period)
-__device__ __forceinline__ uint32_t pt_index(uint32_t i, uint32_t enc) {
-    return (enc >> 24) == 0x7Fu ? i >> (enc & 0xFFu) : i & enc;
-}
-
 template <int W>
 struct Words {
     uint64_t v[W];
@@ -276,7 +271,114 @@ int pt_dot_launch(const PcbPtDotArgs* ap, cudaStream_t s) {
                     : pt_dot_go<LOGN, 8>(a, s);
 }
 
+// ------------------------------------------------------------------------------------------------ coeff_sum
+// args.cuh:909-927: out (+)= sum_{r < n} ct_r pt_r over Q limbs 0..L-1, with pt_r[k] = round(rows_r[k] scale) mod p_l
+// (round half to even; a value past the int64 range clamped to +-2^62 and counted once per limb in *overflow) taken
+// to the NTT domain by the forward transform of the launcher table's twiddles. The plaintext is never stored as an
+// object: its float32 row (the weight as streamed from the host) is expanded into the caller's scratch
+// [term][limb][N], transformed in place, and consumed by one multiply-accumulate pass over all terms (128-bit sums,
+// folded every 8 terms: 8 products below 2^124 and a residue stay below 2^128).
+__device__ const uint32_t g_limb_ident[PCB_COEFF_MAXL] = {
+    0,  1,  2,  3,  4,  5,  6,  7,  8,  9,  10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 20, 21,
+    22, 23, 24, 25, 26, 27, 28, 29, 30, 31, 32, 33, 34, 35, 36, 37, 38, 39, 40, 41, 42, 43,
+    44, 45, 46, 47, 48, 49, 50, 51, 52, 53, 54, 55, 56, 57, 58, 59, 60, 61, 62, 63};
+
+__device__ __forceinline__ uint64_t coeff_residue(float f, double scale, const PcbPrimeConst& pc,
+                                                  unsigned long long* ovf) {
+    const double x = (double)f * scale;
+    long long m;
+    if (fabs(x) < 9.2e18) {
+        m = __double2ll_rn(x);
+    } else {  // past the int64 range, or not a number
+        m = x < 0 ? -(1ll << 62) : (1ll << 62);
+        if (ovf) atomicAdd(ovf, 1ull);
+    }
+    const uint64_t mag = m < 0 ? (uint64_t)(-m) : (uint64_t)m;
+    const uint64_t v = reduce(Acc{mag, 0}, pc);
+    return m < 0 && v ? pc.p - v : v;
+}
+
+// grid (N / (BX WPT), L, n): scratch[r][l][k] = the residue of coefficient k of row r mod p_l
+template <int LOGN>
+__global__ void __launch_bounds__(BX) coeff_expand(PcbCoeffArgs a) {
+    const int l = blockIdx.y, r = blockIdx.z;
+    const PcbPrimeConst& pc = a.pr[l];
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    const float4 f = *(const float4*)(a.rows[r] + i);
+    const uint64_t w[4] = {coeff_residue(f.x, a.scale, pc, a.overflow), coeff_residue(f.y, a.scale, pc, a.overflow),
+                           coeff_residue(f.z, a.scale, pc, a.overflow), coeff_residue(f.w, a.scale, pc, a.overflow)};
+    st4((uint64_t*)a.scratch + (((size_t)r * a.L + l) << LOGN) + i, w);
+}
+
+// grid (N / (BX WPT), L, 2 parts): out[part][l] (+)= sum_r ct_r[part][l] pt_r[l]
+template <int LOGN>
+__global__ void __launch_bounds__(BX) coeff_mac(PcbCoeffArgs a) {
+    const int l = blockIdx.y, part = blockIdx.z;
+    const PcbPrimeConst& pc = a.pr[l];
+    const uint64_t p = pc.p;
+    const size_t i = ((size_t)blockIdx.x * BX + threadIdx.x) * WPT;
+    const size_t row = (size_t)part * a.part_stride + ((size_t)l << LOGN) + i;
+    Acc acc[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc[w] = Acc{0, 0};
+    for (int r = 0; r < a.n; ++r) {
+        const V4 x = ld4((const uint64_t*)a.ct[r] + row);
+        const V4 y = ld4((const uint64_t*)a.scratch + (((size_t)r * a.L + l) << LOGN) + i);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) mac(acc[w], x.v[w], y.v[w]);
+        if ((r & 7) == 7) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) acc[w] = Acc{reduce(acc[w], pc), 0};
+        }
+    }
+    uint64_t* o = (uint64_t*)a.out + row;
+    uint64_t res[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) res[w] = reduce(acc[w], pc);
+    if (a.accumulate) {
+        const V4 d = ld4(o);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) res[w] = add_mod(res[w], d.v[w], p);
+    }
+    st4(o, res);
+}
+
+template <int LOGN>
+int coeff_sum_launch(const PcbCoeffArgs* ap, cudaStream_t s) {
+    if (!ap) return PCB_BAD_ARGS;
+    const PcbCoeffArgs& a = *ap;
+    if (a.n < 1 || a.n > PCB_COEFF_MAXT || a.L < 1 || a.L > PCB_COEFF_MAXL || !a.scratch || !a.out || !a.fw || !a.fws ||
+        !a.pr)
+        return PCB_BAD_ARGS;
+    const auto a16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
+    if (!a16(a.scratch) || !a16(a.out) || (a.part_stride & 1)) return PCB_BAD_ARGS;
+    for (int r = 0; r < a.n; ++r)
+        if (!a.rows[r] || !a.ct[r] || !a16(a.rows[r]) || !a16(a.ct[r])) return PCB_BAD_ARGS;
+    const uint32_t* ident = nullptr;
+    if (cudaGetSymbolAddress((void**)&ident, g_limb_ident) != cudaSuccess) return PCB_LAUNCH_RESULT();
+    coeff_expand<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.L, a.n), BX, 0, s>>>(a);
+    int rc = PCB_LAUNCH_RESULT();
+    for (int r = 0; r < a.n && rc == 0; ++r) {
+        PcbNttArgs na;
+        memset(&na, 0, sizeof na);
+        na.base = (uint64_t*)a.scratch + (((size_t)r * a.L) << LOGN);
+        na.roff = ident;
+        na.rprime = (const int32_t*)ident;
+        na.fw = a.fw;
+        na.fws = a.fws;
+        na.pr = a.pr;
+        na.nrows = a.L;
+        na.snum = 1;
+        na.xnum = 1;
+        rc = ntt::fwd<LOGN>(&na, s);
+    }
+    if (rc) return rc;
+    coeff_mac<LOGN><<<dim3((1 << LOGN) / (BX * WPT), a.L, 2), BX, 0, s>>>(a);
+    return PCB_LAUNCH_RESULT();
+}
+
 #define PCB_PT_INST(L)                                                      \
+    template int coeff_sum_launch<L>(const PcbCoeffArgs*, cudaStream_t);   \
     template int add_const_launch<L>(const PcbAddConstArgs*, cudaStream_t); \
     template int mul_table_launch<L>(const PcbMulTableArgs*, cudaStream_t); \
     template int mul_add_launch<L>(const PcbMulAddArgs*, cudaStream_t);     \

@@ -27,11 +27,6 @@ __device__ __forceinline__ ulonglong2 ld2(const uint64_t* p) {
     return make_ulonglong2(__ldg(p), __ldg(p + 1));
 }
 
-// the key-table slot of prime id t: Q ids at their index up to q_top, special ids right after; q_top < 0: prime id
-__device__ __forceinline__ int key_slot(const PcbKeyTab& T, int t, int nq) {
-    return (t < nq || T.q_top < 0) ? t : T.q_top + 1 + (t - nq);
-}
-
 // Where a key's words of one row live: `b` at bsrc + d bstride, dense `a` (digits >= nreg) at asrc + d astride,
 // regenerated `a` (digits < nreg) from seed.
 struct KeyRow {
@@ -77,7 +72,7 @@ __global__ void __launch_bounds__(BX) ks_dot_regen(PcbKsRegenArgs G) {
     const int dt = (int)t < A.nq ? A.digit_of[t] : -1;
     KeyRow K;
     if constexpr (TAB) {
-        K.bsrc = (const uint64_t*)G.key.kb[0] + (size_t)key_slot(G.key, (int)t, A.nq) * G.key.row_words + i;
+        K.bsrc = (const uint64_t*)G.key.kb[0] + (size_t)keyregen::key_slot(G.key, (int)t, A.nq) * G.key.row_words + i;
         K.bstride = (size_t)G.key.srows * G.key.row_words;
     } else {
         K.bsrc = (const uint64_t*)A.kb[0] + roff;
@@ -192,7 +187,7 @@ __global__ void __launch_bounds__(BX) ks_dot_key(PcbKsKeyArgs G) {
         pm = ((const uint64_t*)A.pmod)[t];
         pms = ((const uint64_t*)A.pmods)[t];
     }
-    const size_t brow = (size_t)key_slot(T, (int)t, A.nq) * T.row_words + i;
+    const size_t brow = (size_t)keyregen::key_slot(T, (int)t, A.nq) * T.row_words + i;
     for (int r = 0; r < A.R; ++r) {
         KeyRow K;
         K.bsrc = (const uint64_t*)T.kb[r] + brow;

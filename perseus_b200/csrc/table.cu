@@ -5,6 +5,8 @@
 
 namespace {
 int absent(const void*, cudaStream_t) { return -1; }
+// the reference's small_int is defined for 32-bit words only; its 64-bit tables answer -2 (crates/pc-kernels/kernels/bts.cuh)
+int words32_only(const void*, cudaStream_t) { return -2; }
 
 template <int LOGN>
 PcbKernelTable make_table() {
@@ -19,6 +21,8 @@ PcbKernelTable make_table() {
     t.ntt_fwd = ntt::fwd<LOGN>;
     t.ntt_inv = ntt::inv<LOGN>;
     t.bconv = ks::bconv_launch<LOGN>;
+    // on 64-bit words the reference's wide conversion takes the same jobs (up to 16 sources) with the same sums
+    t.bconv_wide = ks::bconv_launch<LOGN>;
     t.ew_add = elem::ew_launch<LOGN, elem::ADD>;
     t.ew_scale = elem::ew_launch<LOGN, elem::SCALE>;
     t.ew_sub_mul = elem::ew_launch<LOGN, elem::SUB_MUL>;
@@ -26,13 +30,17 @@ PcbKernelTable make_table() {
     t.ks_dot = ks::ks_dot_launch<LOGN>;
     t.ks_dot_regen = regen::ks_dot_regen_launch<LOGN>;
     t.ks_dot_key = regen::ks_dot_key_launch<LOGN>;
+    t.cts_fused = cts::cts_fused_launch<LOGN>;
+    t.cts_fused_regen = cts::cts_fused_regen_launch<LOGN>;
     t.ksk_expand = keys::ksk_expand_launch<LOGN>;
     t.pt_dot = pt::pt_dot_launch<LOGN>;
+    t.coeff_sum = pt::coeff_sum_launch<LOGN>;
     t.add_const = pt::add_const_launch<LOGN>;
     t.mul_table = pt::mul_table_launch<LOGN>;
     t.mul_add = pt::mul_add_launch<LOGN>;
     t.mul_add_n = pt::mul_add_n_launch<LOGN>;
     t.tensor = elem::tensor_launch<LOGN>;
+    t.tensor_y = elem::tensor_y_launch<LOGN>;
     t.md_epilogue = elem::md_epilogue_launch<LOGN>;
     t.rescale_coef = elem::rescale_coef_launch<LOGN>;
     t.rescale_combine = elem::rescale_combine_launch<LOGN>;
@@ -41,6 +49,8 @@ PcbKernelTable make_table() {
     t.ksk_gen = keys::ksk_gen_launch<LOGN>;
     t.ksk_unpack = keys::ksk_unpack_launch<LOGN>;
     t.mod_raise = elem::mod_raise_launch<LOGN>;
+    t.small_int1 = elem::small_int1_launch<LOGN>;
+    t.small_int = words32_only;
     t.wsum = elem::wsum_launch<LOGN>;
     t.wsum_k = elem::wsum_k_launch<LOGN>;
     t.wsum_multi = elem::wsum_multi_launch<LOGN>;
@@ -51,6 +61,8 @@ PcbKernelTable make_table() {
     t.tensor_multi = elem::tensor_multi_launch<LOGN>;
     t.ew_many = elem::ew_many_launch<LOGN>;
     t.submul_many = elem::submul_many_launch<LOGN>;
+    t.pack_split = elem::pack_split_launch<LOGN>;
+    t.pack_dot = elem::pack_dot_launch<LOGN>;
     return t;
 }
 

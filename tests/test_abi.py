@@ -44,6 +44,7 @@ def test_table_headers():
 def test_absent_entries_refuse():
     t = L.kernel_table()
     assert t.tfhe(None, None) == -1 and t.pcmm(None, None) == -1 and t.cts_fused(None, None) == -1
+    assert t.small_int(None, None) == -2  # 32-bit words only, as the reference's 64-bit table answers
     for n in ("pt_dot", "ks_dot_regen", "ks_dot_key", "ntt_fwd"):  # a null argument pointer: refused by every entry
         assert getattr(t, n)(None, None) == -1, n
 

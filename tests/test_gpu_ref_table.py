@@ -279,7 +279,7 @@ def _bconv_pool(primes, srcp, tgtp, src_rows, tgt_rows, rng):
     return list(src_rows) + list(srcp) + pre + list(tgt_rows) + list(tgtp) + [v for row in M for v in row]
 
 
-def _bconv_case(e, tabs, seed):
+def _bconv_case(e, tabs, seed, entry="bconv"):
     """Four jobs over one source buffer: 1, 3, 8 and 12 sources, prescaled and not, row offsets on both sides."""
     rng = np.random.default_rng(seed)
     n = e.n
@@ -313,7 +313,7 @@ def _bconv_case(e, tabs, seed):
         a.njobs, a.max_tgt = len(jobs), max_tgt
         return a, [out], keep
 
-    got = run_both("bconv", mk, tabs)
+    got = run_both(entry, mk, tabs)
     same(got)
     # and the exact fast-conversion sum for job 2 (8 sources -> the 60-bit targets)
     srcp, tgtp, soff, doff, pres = specs[2]
@@ -329,6 +329,11 @@ def _bconv_case(e, tabs, seed):
 
 def test_bconv(env):
     _bconv_case(env, tables(), seed=20)
+
+
+def test_bconv_wide(env):
+    """bconv_wide: on 64-bit words the reference's wide kernel takes jobs of up to 16 sources, as bconv does"""
+    _bconv_case(env, tables(), seed=21, entry="bconv_wide")
 
 
 # ------------------------------------------------------------------------------------------------ key inner product
@@ -480,6 +485,293 @@ def test_ks_dot_key(env, K, R, nregen, c0_mode):
     same(run_both("ks_dot_key", mk))
 
 
+# ------------------------------------------------------------------------------------------------ fused CtS stage
+
+
+def _brev(x, bits):
+    return int(format(x, f"0{bits}b")[::-1], 2)
+
+
+def _auto_slot(k, o, logn):
+    j = _brev(o, logn)
+    return _brev((((2 * j + 1) * k) % (2 << logn)) >> 1, logn)
+
+
+def _cts_case(env, rng, K, B, G, npts, ptw, enc, x0, ndig=3, nq=8):
+    digit_of = np.array([t // 3 for t in range(nq)] + [-1] * (env.R - nq), np.int32)
+    rows = [5, 0, 1, 2, 3, 4, 6, 7, 11, 8, 9, 10]  # every prime id, out of order
+    nb = max(B - 1, 0)
+    case = dict(K=K, B=B, G=G, npts=npts, ptw=ptw, enc=enc, ndig=ndig, nq=nq, digit_of=digit_of, rows=rows)
+    case["x"] = env.cts(rng, K)
+    case["x0"] = env.cts(rng, K) if x0 else None
+    case["mu"] = env.rows(rng, range(env.R), lead=(K, ndig))
+    case["kb"] = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(nb)]
+    case["ka"] = [env.rows(rng, range(env.R), lead=(ndig,)) for _ in range(nb)]
+    case["kinv"] = [int(fhe.rotation_galois(int(v), LOGN)) for v in rng.integers(1, 5000, nb)]
+    pts = []
+    for _ in range(npts):  # Q rows at their prime id, special rows at pt_prow = nq: R rows of ptw words
+        pt = np.empty((env.R, ptw), np.uint64)
+        for t in range(env.R):
+            pt[t] = rng.integers(0, env.primes[t], ptw, dtype=np.uint64)
+        pts.append(pt)
+    case["pts"] = pts
+    case["pm"] = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    case["pms"] = np.array([shoup(v, p) for v, p in zip(case["pm"], env.primes)], np.uint64)
+    case["seeds"] = [rng.integers(0, 1 << 32, 8, dtype=np.uint64).astype(np.uint32) for _ in range(nb)]
+    return case
+
+
+def _cts_args(env, cs, keep, regen=False, nregen=0, ka_rows=None):
+    K, B, G = cs["K"], cs["B"], cs["G"]
+    xd, mud = dev(cs["x"]), dev(cs["mu"])
+    res = torch.zeros((K * G, 2, env.R, N), dtype=torch.int64, device="cuda")
+    kbs, kas = [dev(v) for v in cs["kb"]], [dev(v) for v in (ka_rows or cs["ka"])]
+    pts = [dev(v) for v in cs["pts"]]
+    sds = [torch.from_numpy(v.view(np.int32).copy()).cuda() for v in cs["seeds"]]
+    tabs = [dev(np.array([v.data_ptr() for v in lst] or [0], np.uint64)) for lst in (kbs, kas, pts, sds)]
+    small = [torch.tensor(v, dtype=torch.int32, device="cuda") for v in (cs["rows"], cs["digit_of"], cs["kinv"] or [1])]
+    pmd, pmsd = dev(cs["pm"]), dev(cs["pms"])
+    x0d = dev(cs["x0"]) if cs["x0"] is not None else None
+    keep += [xd, mud, res, pmd, pmsd] + kbs + kas + pts + sds + tabs + small + ([x0d] if x0d is not None else [])
+    a = L.CtsRegenArgs() if regen else L.CtsArgs()
+    c = a.cts if regen else a
+    c.x, c.modup, c.res = xd.data_ptr(), mud.data_ptr(), res.data_ptr()
+    c.kb, c.ka, c.pts = tabs[0].data_ptr(), tabs[1].data_ptr(), tabs[2].data_ptr()
+    c.kinv, c.rows, c.digit_of = small[2].data_ptr(), small[0].data_ptr(), small[1].data_ptr()
+    c.pmod, c.pmods, c.pr = pmd.data_ptr(), pmsd.data_ptr(), env.pc.data_ptr()
+    c.ct_stride, c.part_stride = 2 * env.R * N, env.R * N
+    c.mu_ct_stride, c.mu_digit_stride, c.key_digit_stride = cs["ndig"] * env.R * N, env.R * N, env.R * N
+    c.K, c.B, c.G, c.npts, c.ndig, c.nq, c.nlive = K, B, G, cs["npts"], cs["ndig"], cs["nq"], cs["ndig"]
+    # the reference runs the x0 form one ciphertext per group at 64-bit words (kmax 1); the grouping is its own choice
+    c.ptw, c.pt_prow, c.enc, c.nrows = cs["ptw"], cs["nq"], cs["enc"], len(cs["rows"])
+    c.kmax = 1 if cs["x0"] is not None else 4
+    c.x0 = x0d.data_ptr() if x0d is not None else None
+    if regen:
+        a.key.kb, a.key.seed, a.key.row_words = tabs[0].data_ptr(), tabs[3].data_ptr(), N
+        a.key.q_top, a.key.srows, a.key.nregen = -1, env.R, nregen
+    return a, res
+
+
+def _pt_word(cs, o):
+    enc = cs["enc"]
+    return o if enc == 0xFFFFFFFF else (o >> (enc & 0xFF) if (enc >> 24) == 0x7F else o & enc)
+
+
+def _cts_formula(env, cs, res, slots):
+    """res_j[o] = sum_i rot_i[o] pts[B j + i][o] from the definition, on a few slots of every row"""
+    P = env.primes
+    for t in range(env.R):
+        p, isq, dt = P[t], t < cs["nq"], int(cs["digit_of"][t])
+        prow = t  # pt_prow = nq: special ids follow the Q ids
+        for c in range(cs["K"]):
+            x = cs["x"][c]
+            for o in slots:
+                rot = []
+                for i in range(cs["B"]):
+                    if i == 0:
+                        if cs["x0"] is not None:
+                            rot.append((int(cs["x0"][c, 0, t, o]), int(cs["x0"][c, 1, t, o])))
+                        else:
+                            pm = int(cs["pm"][t])
+                            rot.append((int(x[0, t, o]) * pm % p, int(x[1, t, o]) * pm % p) if isq else (0, 0))
+                        continue
+                    s = _auto_slot(cs["kinv"][i - 1], o, LOGN)
+                    D = [int(x[1, t, s]) if d == dt else int(cs["mu"][c, d, t, s]) for d in range(cs["ndig"])]
+                    r0 = sum(D[d] * int(cs["kb"][i - 1][d, t, s]) for d in range(cs["ndig"]))
+                    r1 = sum(D[d] * int(cs["ka"][i - 1][d, t, s]) for d in range(cs["ndig"]))
+                    if isq:
+                        r0 += int(x[0, t, s]) * int(cs["pm"][t])
+                    rot.append((r0 % p, r1 % p))
+                for j in range(cs["G"]):
+                    w = [int(cs["pts"][cs["B"] * j + i][prow, _pt_word(cs, o)]) if cs["B"] * j + i < cs["npts"] else 0
+                         for i in range(cs["B"])]
+                    want = (sum(r[0] * wi for r, wi in zip(rot, w)) % p, sum(r[1] * wi for r, wi in zip(rot, w)) % p)
+                    got = (int(res[c * cs["G"] + j, 0, t, o]), int(res[c * cs["G"] + j, 1, t, o]))
+                    assert got == want, (t, c, o, j)
+
+
+@pytest.mark.parametrize("K,B,G,npts,compact,x0", [(1, 4, 1, 4, False, False), (5, 5, 2, 9, False, False),
+                                                     (3, 9, 2, 18, True, False), (2, 3, 2, 6, False, True),
+                                                     (4, 1, 2, 2, False, False)])
+def test_cts_fused(env, K, B, G, npts, compact, x0):
+    """cts_fused: one BSGS stage of CoeffToSlot with the baby rotations formed in the extended basis at the slot they
+    are used, over every row of both widths; diagonals past npts skipped; compact plaintexts; the x0 form; more than
+    8 baby steps (the sums' periodic reduction). Word for word with the reference's launcher, and the definition on
+    sampled slots."""
+    rng = np.random.default_rng(300 + 7 * K + B)
+    ptw, enc = (N // 4, 0x7F000002) if compact else (N, 0xFFFFFFFF)
+    cs = _cts_case(env, rng, K, B, G, npts, ptw, enc, x0)
+
+    def mk():
+        keep = []
+        a, res = _cts_args(env, cs, keep)
+        return a, [res], keep
+
+    got = run_both("cts_fused", mk)
+    same(got)
+    res = got["ours"][0].reshape(K * G, 2, env.R, N)
+    _cts_formula(env, cs, res, [0, 1, 37, N // 2 + 5, N - 1])
+
+
+@pytest.mark.parametrize("K,B,G,nregen", [(1, 4, 1, 3), (5, 6, 2, 2), (2, 3, 2, 0)])
+def test_cts_fused_regen(env, K, B, G, nregen):
+    """cts_fused_regen: the baby keys through a key table, `a` regenerated below nregen. Word for word with the
+    reference's launcher, and equal to cts_fused given the expanded `a` rows (ksk_expand of the same seeds)."""
+    rng = np.random.default_rng(330 + K + B)
+    cs = _cts_case(env, rng, K, B, G, 2 * B - 1, N, 0xFFFFFFFF, False)
+
+    def mk():
+        keep = []
+        a, res = _cts_args(env, cs, keep, regen=True, nregen=nregen)
+        return a, [res], keep
+
+    got = run_both("cts_fused_regen", mk)
+    same(got)
+    # the dense form with `a` expanded: digits below nregen from the seeds, the others as stored
+    t = L.kernel_table()
+    ka_rows = []
+    for i, sd in enumerate(cs["seeds"]):
+        out = torch.zeros((cs["ndig"], env.R, N), dtype=torch.int64, device="cuda")
+        sdd = torch.from_numpy(sd.view(np.int32).copy()).cuda()
+        ids = torch.arange(env.R, dtype=torch.int32, device="cuda")
+        e = L.KskExpandArgs(out.data_ptr(), sdd.data_ptr(), ids.data_ptr(), env.pc.data_ptr(), env.R, cs["ndig"], 0, 0)
+        assert t.ksk_expand(ptr(e), stream()) == 0
+        torch.cuda.synchronize()
+        a = host(out).reshape(cs["ndig"], env.R, N).copy()
+        a[nregen:] = cs["ka"][i][nregen:]
+        ka_rows.append(a)
+    keep = []
+    cs_dense = dict(cs, ka=ka_rows)
+    a, res = _cts_args(env, cs_dense, keep)
+    assert t.cts_fused(ptr(a), stream()) == 0
+    torch.cuda.synchronize()
+    assert (host(res) == got["ours"][0]).all()
+
+
+# ------------------------------------------------------------------------------------------------ streamed weights
+
+
+@pytest.mark.parametrize("n,nl,acc", [(1, 3, 0), (11, 12, 1), (32, 5, 0)])
+def test_coeff_sum(env, n, nl, acc):
+    """coeff_sum: float32 coefficient rows expanded (scale, round half to even, clamped and counted past the int64
+    range, NaN included), transformed, and summed against n ciphertexts over nl limbs of both widths; word for word
+    with the reference's launcher (output and overflow count), and this build's scratch equal to ntt_fwd of the
+    expected residues."""
+    rng = np.random.default_rng(500 + n)
+    scale = 2.0 ** 40
+    rows = rng.standard_normal((n, N)).astype(np.float32)
+    rows[0, :6] = [0.5 / scale, 1.5 / scale, -2.5 / scale, 1e30, -np.inf, np.nan]  # ties to even; clamps
+    cts = env.cts(rng, n)
+    o = env.cts(rng, 1)[0]
+
+    def mk():
+        rd = torch.from_numpy(rows.copy()).cuda()
+        cd = dev(cts)
+        out = dev(o)
+        scratch = torch.zeros((n, nl, N), dtype=torch.int64, device="cuda")
+        ovf = torch.zeros(1, dtype=torch.int64, device="cuda")
+        a = L.CoeffArgs()
+        a.scratch, a.out, a.fw, a.fws, a.pr = scratch.data_ptr(), out.data_ptr(), env.fw.data_ptr(), \
+            env.fws.data_ptr(), env.pc.data_ptr()
+        a.overflow, a.part_stride, a.scale, a.n, a.L, a.accumulate = ovf.data_ptr(), env.R * N, scale, n, nl, acc
+        for r in range(n):
+            a.rows[r] = rd.data_ptr() + r * N * 4
+            a.ct[r] = cd.data_ptr() + r * 2 * env.R * N * 8
+        return a, [out, ovf, scratch], [rd, cd]
+
+    got = run_both("coeff_sum", mk)
+    same({k: v[:2] for k, v in got.items()})
+    assert int(got["ours"][1][0]) == 3 * nl  # 1e30, -inf and NaN, once per limb
+    # the expansion, transformed by ntt_fwd, equals this build's scratch
+    x = rows.astype(np.float64) * scale
+    big = ~(np.abs(x) < 9.2e18)
+    m = np.where(big, np.where(x < 0, -(2.0 ** 62), 2.0 ** 62), np.rint(np.where(big, 0, x))).astype(np.int64)
+    want = np.empty((n, nl, N), np.uint64)
+    for l in range(nl):
+        want[:, l] = np.mod(m, np.int64(env.primes[l])).astype(np.uint64)
+    wd = dev(want.reshape(n * nl, N))
+    keep = []
+    na = env.ntt_args(wd, list(range(n * nl)), [i % nl for i in range(n * nl)], keep)
+    assert L_tab().ntt_fwd(ptr(na), stream()) == 0
+    torch.cuda.synchronize()
+    assert (host(wd).reshape(n, nl, N) == got["ours"][2].reshape(n, nl, N)).all()
+    # and the sum on a few words of every limb
+    pt = host(wd).reshape(n, nl, N)
+    out = got["ours"][0].reshape(2, env.R, N)
+    for part in range(2):
+        for l in range(nl):
+            sl = slice(0, 32)
+            v = sum(cts[r, part, l, sl].astype(object) * pt[r, l, sl].astype(object) for r in range(n))
+            if acc:
+                v = v + o[part, l, sl].astype(object)
+            assert (out[part, l, sl].astype(object) == v % env.primes[l]).all()
+    assert (out[:, nl:] == o[:, nl:]).all()
+
+
+def L_tab():
+    return L.kernel_table()
+
+
+# ------------------------------------------------------------------------------------------------ subring switch
+
+
+@pytest.mark.parametrize("sub,nq,K", [(2, 8, 1), (4, 5, 3), (16, 12, 2)])
+def test_pack_split_dot(env, sub, nq, K):
+    """pack_split (digit j = the coefficients at exponents j mod sub) and pack_dot (the digits against a key, + P c0 on
+    the Q rows) over Q rows then special rows; the key rows by row index, c0 and the outputs by prime id."""
+    rng = np.random.default_rng(400 + sub)
+    nrows = env.R
+    rows = list(range(nq)) + list(range(nq, env.R))[::-1]  # the special rows in reverse prime-id order
+    q = env.rows(rng, rows[:nq], lead=(K,)) if nq else np.zeros((K, 0, N), np.uint64)
+    pv = env.rows(rng, rows[nq:], lead=(K,))
+    sp = np.zeros((K, sub, nrows, N), np.uint64)
+
+    def mk_split():
+        qd, pd = dev(q if nq else np.zeros((K, 1, N), np.uint64)), dev(pv)
+        out = dev(sp)
+        a = L.PackSplitArgs(qd.data_ptr(), pd.data_ptr(), out.data_ptr(), nq * N if nq else N, (nrows - nq) * N,
+                            sub * nrows * N, K, sub, nq, nrows)
+        return a, [out], [qd, pd]
+
+    got = run_both("pack_split", mk_split)
+    same(got)
+    dig = got["ours"][0].reshape(K, sub, nrows, N)
+    src = np.concatenate([q, pv], axis=1)
+    cls = np.arange(N) % sub
+    for j in range(sub):
+        assert (dig[:, j] == np.where(cls == j, src, 0)).all()
+    kb = np.stack([env.rows(rng, rows) for _ in range(sub)])  # [digit][row y][N], row y mod prime rows[y]
+    ka = np.stack([env.rows(rng, rows) for _ in range(sub)])
+    # the digits reduced per target row: D_j on row y mod prime rows[y] (pack_split leaves the residues as read)
+    c0 = env.cts(rng, K)[:, 0]
+    pm = np.array([rng.integers(1, p) for p in env.primes], np.uint64)
+    pms = np.array([shoup(v, p) for v, p in zip(pm, env.primes)], np.uint64)
+    o0, o1 = env.cts(rng, K)[:, 0], env.cts(rng, K)[:, 1]
+
+    def mk_dot():
+        keep = [dev(dig), dev(kb), dev(ka), dev(c0), dev(pm), dev(pms),
+                torch.tensor(rows, dtype=torch.int32, device="cuda")]
+        out0, out1 = dev(o0), dev(o1)
+        a = L.PackDotArgs(keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), keep[3].data_ptr(),
+                          out0.data_ptr(), out1.data_ptr(), keep[6].data_ptr(), keep[4].data_ptr(), keep[5].data_ptr(),
+                          env.pc.data_ptr(), sub * nrows * N, env.R * N, env.R * N, K, sub, nq, nrows)
+        return a, [out0, out1], keep
+
+    got = run_both("pack_dot", mk_dot)
+    same(got)
+    out0 = got["ours"][0].reshape(K, env.R, N)
+    for y in (0, nq - 1, nq, nrows - 1):
+        if y < 0 or y >= nrows:
+            continue
+        t, p = rows[y], env.primes[rows[y]]
+        for c in range(K):
+            sl = slice(0, 64)
+            want = sum(dig[c, j, y, sl].astype(object) * kb[j, y, sl].astype(object) for j in range(sub))
+            if y < nq:
+                want = want + c0[c, t, sl].astype(object) * int(pm[t])
+            assert (out0[c, t, sl].astype(object) == want % p).all(), (y, c)
+
+
 # ------------------------------------------------------------------------------------------------ element-wise
 
 
@@ -525,6 +817,73 @@ def test_tensor(env, npairs, acc, dbl, acc_d2, coef):
         return x, [out, d2d, cfd], keep
 
     same(run_both("tensor", mk))
+
+
+@pytest.mark.parametrize("sub,dbl", [(0, 0), (1, 1)])
+def test_tensor_y(env, sub, dbl):
+    """tensor_y: the tensor, then (c0, c1) +/-= c[row] y after the doubling (EvalMod's x y +/- c t)"""
+    rng = np.random.default_rng(56 + sub)
+    K, n = 2, 10
+    ins = [env.cts(rng, K) for _ in range(5)]
+    o, d2 = env.cts(rng, K), env.cts(rng, K)
+    c = np.array([int(rng.integers(0, p)) for p in env.primes], np.uint64)
+    cs = np.array([shoup(int(v), p) for v, p in zip(c, env.primes)], np.uint64)
+
+    def mk():
+        keep = [dev(v) for v in ins] + [dev(c), dev(cs)]
+        out, d2d = dev(o), dev(d2)
+        t = L.TensorArgs(env.cref(out), env.cref(d2d), env.cref(keep[0]), env.cref(keep[1]), env.cref(keep[2]),
+                         env.cref(keep[3]), None, 0, env.pc.data_ptr(), 2, 1, n, K, dbl, 0)
+        x = L.TensorYArgs(t, env.cref(keep[4]), keep[5].data_ptr(), keep[6].data_ptr(), sub, 0)
+        return x, [out, d2d], keep
+
+    got = run_both("tensor_y", mk)
+    same(got)
+    # the formula on the rows of both widths
+    P = np.array(env.primes, dtype=object)[None, :, None]
+    a0, a1, b0, b1, y = (v.astype(object) for v in ins)
+    r0 = (a0[:, 0] * b0[:, 0] + a1[:, 0] * b1[:, 0] + o[:, 0].astype(object)) % P
+    r0 = r0 * (1 + dbl) % P
+    cy = c.astype(object)[None, :, None] * y[:, 0] % P
+    r0 = (r0 - cy if sub else r0 + cy) % P
+    out = got["ours"][0].reshape(o.shape)
+    assert (out[:, 0, :n] == r0[:, :n].astype(np.uint64)).all()
+    assert (out[:, :, n:] == o[:, :, n:]).all()
+
+
+@pytest.mark.parametrize("mc,sh,nrows,nparts", [(None, 60, 12, 2), (None, 64, 9, 1), (1 << 52, 100, 12, 2),
+                                                  (3, 1, 12, 2), (None, 127, 5, 2), (None, 65, 12, 2)])
+def test_small_int1(env, mc, sh, nrows, nparts):
+    """small_int1: row 0 centred, times mc 2^-sh rounded half up, onto rows [0, nrows) of both widths (in place);
+    a 53-bit mc is a double's mantissa, the raise's exact scale"""
+    rng = np.random.default_rng(97 + sh)
+    K = 3
+    x0 = env.cts(rng, K)
+    q = env.primes
+    x0[:, :, 0, :4] = np.array([0, q[0] // 2, q[0] // 2 + 1, q[0] - 1], np.uint64)  # the centring edges
+    mcv = int(rng.integers(1 << 52, 1 << 53)) if mc is None else mc
+    a = L.SmallInt1Args()
+
+    def mk():
+        xd = dev(x0)
+        a.x, a.pr = xd.data_ptr(), env.pc.data_ptr()
+        a.ct_stride, a.part_stride = 2 * env.R * env.n, env.R * env.n
+        a.mc, a.sh, a.nrows, a.K, a.nparts = mcv, sh, nrows, K, nparts
+        return a, [xd], []
+
+    got = run_both("small_int1", mk)
+    same(got)
+    out = got["ours"][0].reshape(x0.shape)
+    for c in range(K):
+        for part in range(nparts):
+            v = x0[c, part, 0, :256].astype(object)
+            xc = [int(w) - q[0] if int(w) > q[0] // 2 else int(w) for w in v]
+            m = [(abs(w) * mcv + (1 << (sh - 1))) >> sh for w in xc]
+            for t in range(nrows):
+                want = [(-mm if w < 0 else mm) % q[t] for w, mm in zip(xc, m)]
+                assert [int(u) for u in out[c, part, t, :256]] == want, (c, part, t)
+    assert (out[:, :, nrows:] == x0[:, :, nrows:]).all()
+    assert (out[:, nparts:] == x0[:, nparts:]).all()
 
 
 @pytest.mark.parametrize("dbl,with_k", [(0, False), (1, True)])

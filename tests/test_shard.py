@@ -179,7 +179,7 @@ def _block_rank_main(rank, world, port, errq):
         raise
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_sharded_block_gloo(world):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
@@ -253,8 +253,9 @@ def _model_rank_main(rank, world, port, errq):
         raise
 
 
-def test_sharded_model_gloo():
-    world = 2
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_model_gloo(world):
+    """world 3: the two cache blocks over three ranks leave one rank idle in every layer's attention"""
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()

@@ -190,18 +190,18 @@ def poly7(ops, plan, x, coeffs, mask, primes, slots):
     x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
     lvl = L1 - 2  # the level of x^3 / x^4
 
-    def term(pw, c, target_scale):
-        # c * mask * x^pw, landing at level lvl - 1 with scale target_scale (the plaintext scale solves for it)
-        src = ops.drop_to(pw, lvl)
-        pscale = target_scale * primes[lvl] / src.scale
-        pt = _pt(ops, plan, mask * c, lvl, pscale, slots)
-        return ops.rescale_one(ops.mult_pt(src, pt, pscale))
-
     def inner(cs, target_scale):
+        # sum_i c_i mask x^i at level lvl - 1 with scale target_scale: each x^i at level lvl times its coefficient at
+        # the plaintext scale that puts the product at target_scale q_lvl, summed in the same pass, one rescale
+        pre = target_scale * primes[lvl]
         acc = None
-        for i, (pw, c) in enumerate(zip((x, x2, x3), cs[1:])):
-            t_ = term(pw, c, target_scale)
-            acc = t_ if acc is None else ops.add(acc, t_)
+        for pw, c in zip((x, x2, x3), cs[1:]):
+            src = ops.drop_to(pw, lvl)
+            pscale = pre / src.scale
+            pt = _pt(ops, plan, mask * c, lvl, pscale, slots)
+            acc = ops.mult_pt(src, pt, pscale) if acc is None else ops.mult_pt_add(src, pt, pscale, acc)
+        acc.scale = pre
+        acc = ops.rescale_one(acc)
         pt0 = _pt(ops, plan, mask * cs[0], acc.top, acc.scale, slots)
         return ops.add_pt(acc, pt0)
 

@@ -180,12 +180,6 @@ def _const_pt(ops, plan, value, top, scale, slots):
     return pt
 
 
-def _land(ops, plan, x, value, target_scale, primes):
-    """value * x (value a real constant), landing at exactly target_scale one level below x."""
-    pscale = target_scale * primes[x.top] / x.scale
-    return ops.rescale_one(ops.mult_pt(x, _const_pt(ops, plan, value, x.top, pscale, x.slots), pscale))
-
-
 def _add_const(ops, plan, x, value):
     return ops.add_pt(x, _const_pt(ops, plan, value, x.top, x.scale, x.slots))
 
@@ -202,13 +196,18 @@ class Cheb:
         self.ops, self.plan, self.primes = ops, plan, primes
         T = {1: x}
 
-        def lin(j, k):  # 2 T_j T_k - T_(j-k) (or - 1 when j == k)
-            p = _mul(ops, T[j], T[k])
-            p2 = ops.add(p, p)
+        def lin(j, k):  # 2 T_j T_k - T_(j-k) (or - 1 when j == k), one rescale
+            top = min(T[j].top, T[k].top)
+            m = ops.mult(ops.drop_to(T[j], top), ops.drop_to(T[k], top))
+            m2 = ops.add(m, m)
             if j == k:
-                return _add_const(ops, plan, p2, -1.0)
-            sub = _land(ops, plan, ops.drop_to(T[j - k], min(T[j - k].top, p.top + 1)), 1.0, p.scale, primes)
-            return ops.sub(p2, ops.drop_to(sub, p2.top))
+                return _add_const(ops, plan, ops.rescale_one(m2), -1.0)
+            # T_(j-k) times 1 at the product's scale, subtracted before the rescale
+            x = ops.drop_to(T[j - k], top)
+            pscale = m2.scale / x.scale
+            d = ops.mult_pt_add(x, _const_pt(ops, plan, 1.0, top, pscale, x.slots), pscale, m2, sub=1)
+            d.scale = m2.scale
+            return ops.rescale_one(d)
 
         T[2] = lin(1, 1)
         T[3] = lin(2, 1)
@@ -236,16 +235,20 @@ class Cheb:
             c.pop()
         d = len(c) - 1
         if d < 8:
-            lb = self.maxlev(d)  # the terms' level (one below the lowest T used)
+            # the terms c_k T_k meet at one scale before a single rescale: every T_k at level lb + 1 times c_k at the
+            # plaintext scale that makes the product's scale scale q_(lb+1), summed in the same pass, then rescaled
+            lb = self.maxlev(d)  # the result's level (one below the lowest T used)
+            pre = scale * primes[lb + 1]
             acc = None
             for k in range(1, d + 1):
-                if c[k] == 0.0:
-                    continue
-                t = _land(ops, plan, ops.drop_to(self.T[k], lb + 1), c[k], scale, primes)
-                acc = t if acc is None else ops.add(acc, t)
-            if acc is None:  # a constant: c_0 x 0 + c_0 needs a ciphertext at the level and scale
-                acc = _land(ops, plan, ops.drop_to(self.T[1], lb + 1), 0.0, scale, primes)
-            acc = _add_const(ops, plan, acc, c[0])
+                if c[k] == 0.0 and not (k == 1 and all(v == 0.0 for v in c[1:])):
+                    continue  # (a constant keeps the c_1 = 0 term: c_0 needs a ciphertext at the level and scale)
+                x = ops.drop_to(self.T[k], lb + 1)
+                pscale = pre / x.scale
+                pt = _const_pt(ops, plan, c[k], lb + 1, pscale, x.slots)
+                acc = ops.mult_pt(x, pt, pscale) if acc is None else ops.mult_pt_add(x, pt, pscale, acc)
+            acc.scale = pre
+            acc = _add_const(ops, plan, ops.rescale_one(acc), c[0])
             return ops.drop_to(acc, level)
         m = 1 << (d.bit_length() - 1)
         q = [c[m]] + [2.0 * c[m + j] for j in range(1, d - m + 1)]

@@ -54,11 +54,11 @@ class OracleDiagonals:
 def _batched(f):
     """Apply f member by member when an argument is a batch (other arguments shared)."""
 
-    def g(self, *args):
+    def g(self, *args, **kw):
         n = next((a.k for a in args if isinstance(a, OBatch)), None)
         if n is None:
-            return f(self, *args)
-        return OBatch([f(self, *[a.cts[i] if isinstance(a, OBatch) else a for a in args]) for i in range(n)])
+            return f(self, *args, **kw)
+        return OBatch([f(self, *[a.cts[i] if isinstance(a, OBatch) else a for a in args], **kw) for i in range(n)])
 
     return g
 
@@ -145,6 +145,15 @@ class OracleOps:
     @_batched
     def mult_pt(self, a, pt, pt_scale):
         return OCt(self.c.mult_pt(a.data, pt, a.top), a.top, a.scale * pt_scale, a.slots)
+
+    @_batched
+    def mult_pt_add(self, a, pt, pt_scale, y, sub=0, out=None):
+        """y + a pt (sub 1: y - a pt, 2: a pt - y), the session's fused op as two oracle ops (the same residues)"""
+        assert a.top == y.top
+        m = self.c.mult_pt(a.data, pt, a.top)
+        d = self.c.add(y.data, m, a.top) if sub == 0 else (
+            self.c.sub(y.data, m, a.top) if sub == 1 else self.c.sub(m, y.data, a.top))
+        return OCt(d, y.top, y.scale, y.slots)
 
     @_batched
     def add_pt(self, a, pt):

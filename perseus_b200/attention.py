@@ -190,30 +190,33 @@ def poly7(ops, plan, x, coeffs, mask, primes, slots):
     x4 = ops.rescale_one(ops.mult(x2, x2))  # L-3
     lvl = L1 - 2  # the level of x^3 / x^4
 
-    def inner(cs, target_scale):
-        # sum_i c_i mask x^i at level lvl - 1 with scale target_scale: each x^i at level lvl times its coefficient at
-        # the plaintext scale that puts the product at target_scale q_lvl, summed in the same pass, one rescale
-        pre = target_scale * primes[lvl]
+    def inner_pre(cs, pre, level):
+        # sum_{i >= 1} c_i mask x^i at `level`, one rescale short: each x^i taken to `level` times its coefficient at
+        # the plaintext scale that puts the product at `pre`, summed in the same pass (the constant returned apart)
         acc = None
         for pw, c in zip((x, x2, x3), cs[1:]):
-            src = ops.drop_to(pw, lvl)
+            src = ops.drop_to(pw, level)
             pscale = pre / src.scale
-            pt = _pt(ops, plan, mask * c, lvl, pscale, slots)
+            pt = _pt(ops, plan, mask * c, level, pscale, slots)
             acc = ops.mult_pt(src, pt, pscale) if acc is None else ops.mult_pt_add(src, pt, pscale, acc)
         acc.scale = pre
-        acc = ops.rescale_one(acc)
-        pt0 = _pt(ops, plan, mask * cs[0], acc.top, acc.scale, slots)
-        return ops.add_pt(acc, pt0)
+        return acc, cs[0]
 
-    # p = A + x^4 B: A at level lvl - 2 with scale S; B at lvl - 1 with scale S q_{lvl-1} / scale(x^4)
-    S = primes[lvl - 1]  # A's scale (~2^50)
+    def with_const(acc, c0):
+        return ops.add_pt(acc, _pt(ops, plan, mask * c0, acc.top, acc.scale, slots))
+
+    # p = A + x^4 B: B at lvl - 1 with scale S q_(lvl-1) / scale(x^4); the product x^4 B and A's terms meet at
+    # level lvl - 1 before one rescale to lvl - 2 (scale ~ S)
+    S = primes[lvl - 1]  # the result's scale (~2^50)
     x4d = ops.drop_to(x4, lvl - 1)
-    B = inner(coeffs[4:8] if len(coeffs) > 4 else [0.0], S * primes[lvl - 1] / x4d.scale)
-    xb = ops.rescale_one(ops.mult(x4d, B))  # lvl - 2, scale ~ S
-    A = inner(coeffs[:4], xb.scale)  # lvl - 1, the same scale as x^4 B ...
-    A = ops.drop_to(A, xb.top)  # ... at the same level
-    A.scale = xb.scale
-    return ops.add(A, xb)
+    b_pre, b0 = inner_pre(coeffs[4:8] if len(coeffs) > 4 else [0.0], S * primes[lvl - 1] / x4d.scale * primes[lvl],
+                          lvl)
+    B = with_const(ops.rescale_one(b_pre), b0)
+    P = ops.mult(x4d, B)
+    a_pre, a0 = inner_pre(coeffs[:4], P.scale, lvl - 1)
+    X = ops.add(P, a_pre)
+    X.scale = P.scale
+    return with_const(ops.rescale_one(X), a0)
 
 
 def attend(ops, q_ct, cache, coeffs, primes):

@@ -229,27 +229,31 @@ class Cheb:
 
     def eval(self, c, scale, level):
         """sum_k c[k] T_k at exactly `scale`, level `level` (<= maxlev(deg))."""
+        x, k0 = self.eval_pre(c, scale, level)
+        return _add_const(self.ops, self.plan, self.ops.rescale_one(x), k0)
+
+    def eval_pre(self, c, scale, level):
+        """(X, k0): the polynomial without its constant term, one rescale short (level + 1, scale scale q_(level+1)),
+        and that constant, so that rescale(X) + k0 = sum_k c[k] T_k at `scale`, `level`. Every partial sum meets at
+        that one scale before the rescale: a leaf's terms c_k T_k (each T_k taken to level + 1 and times c_k at the
+        plaintext scale that lands it there), a node's product Q T_m with its remainder's unrescaled sum."""
         ops, plan, primes = self.ops, self.plan, self.primes
         c = list(c)
         while len(c) > 1 and c[-1] == 0.0:
             c.pop()
         d = len(c) - 1
+        pre = scale * primes[level + 1]
         if d < 8:
-            # the terms c_k T_k meet at one scale before a single rescale: every T_k at level lb + 1 times c_k at the
-            # plaintext scale that makes the product's scale scale q_(lb+1), summed in the same pass, then rescaled
-            lb = self.maxlev(d)  # the result's level (one below the lowest T used)
-            pre = scale * primes[lb + 1]
             acc = None
-            for k in range(1, d + 1):
-                if c[k] == 0.0 and not (k == 1 and all(v == 0.0 for v in c[1:])):
-                    continue  # (a constant keeps the c_1 = 0 term: c_0 needs a ciphertext at the level and scale)
-                x = ops.drop_to(self.T[k], lb + 1)
+            for k in range(1, max(d, 1) + 1):
+                if d > 0 and c[k] == 0.0:
+                    continue  # (a constant keeps a zero c_1 term: c_0 needs a ciphertext at the level and scale)
+                x = ops.drop_to(self.T[k], level + 1)
                 pscale = pre / x.scale
-                pt = _const_pt(ops, plan, c[k], lb + 1, pscale, x.slots)
+                pt = _const_pt(ops, plan, c[k] if d > 0 else 0.0, level + 1, pscale, x.slots)
                 acc = ops.mult_pt(x, pt, pscale) if acc is None else ops.mult_pt_add(x, pt, pscale, acc)
             acc.scale = pre
-            acc = _add_const(ops, plan, ops.rescale_one(acc), c[0])
-            return ops.drop_to(acc, level)
+            return acc, c[0]
         m = 1 << (d.bit_length() - 1)
         q = [c[m]] + [2.0 * c[m + j] for j in range(1, d - m + 1)]
         r = c[:m]
@@ -257,10 +261,12 @@ class Cheb:
             r[m - j] -= c[m + j]
         Tm = self.T[m]
         lq = level + 1
-        Q = self.eval(q, scale * primes[lq] / Tm.scale, lq)
-        P = ops.rescale_one(ops.mult(Q, ops.drop_to(Tm, lq)))
-        R = self.eval(r, P.scale, level)
-        return ops.add(P, R)
+        Q = self.eval(q, pre / Tm.scale, lq)
+        P = ops.mult(Q, ops.drop_to(Tm, lq))
+        R, k0 = self.eval_pre(r, scale, level)
+        X = ops.add(P, R)
+        X.scale = pre
+        return X, k0
 
 
 # ------------------------------------------------------------------------------------------------ bootstrap

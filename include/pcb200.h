@@ -700,6 +700,12 @@ int pcb_encode(PcbCtx* ctx, const double* vals, int32_t nvals, int32_t nslots, d
                uint64_t* rows);
 /* Upload host coefficient rows 0..=top and take them to evaluation form into pt (device, [nq][N]). */
 int pcb_pt_load(PcbCtx* ctx, const uint64_t* rows_host, int32_t top, uint64_t* pt, cudaStream_t stream);
+/* The same over the extended rows: rows 0..=top of the Q primes, then one row per special prime (top + 1 + kp rows),
+ * for pcb_linear_transform_ext's plaintexts. No counterpart in the reference's Fhe API (its fused CoeffToSlot stage
+ * encodes its diagonals over the special primes too, crates/pc-gpu/src/bts/cts.rs). */
+int pcb_encode_ext(PcbCtx* ctx, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
+                   uint64_t* rows);
+int pcb_pt_load_ext(PcbCtx* ctx, const uint64_t* rows_host, int32_t top, uint64_t* pt, cudaStream_t stream);
 
 /* Ciphertext ops over K ciphertexts `ct_stride` words apart (0 = one ciphertext layout apart), rows 0..=top. */
 int pcb_add(PcbCtx* ctx, const uint64_t* a, const uint64_t* b, uint64_t* out, int32_t top, int32_t K,
@@ -768,6 +774,16 @@ int pcb_linear_transform(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* 
 int pcb_linear_transform_multi(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
                                int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
                                cudaStream_t stream);
+/* pcb_linear_transform_multi with the babies kept in the extended basis (double hoisting: the sums of the reference's
+ * fused CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs and the cts_fused launcher): babies as key inner products
+ * with P c0 added and no ModDown, baby 0 = P x; the baby sums over the Q rows and the special rows (plaintexts of
+ * top + 1 + kp rows, pcb_pt_load_ext); each giant step's sum brought down, rotated, and the extended outputs summed
+ * with giant step 0's for one ModDown. Fewer ModDowns than pcb_linear_transform_multi (gstep against bstep - 1), so
+ * it pays with many baby steps. Same arguments and workspace; the words differ from pcb_linear_transform_multi's
+ * (the ModDowns round at other points), the decrypted values agree within the key-switch noise. */
+int pcb_linear_transform_ext(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
+                             int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
+                             cudaStream_t stream);
 
 /* ModRaise of K ciphertexts for bootstrapping (crates/pc-gpu/src/bts/raise.rs): rows 0 of both parts (evaluation
  * form, level 0) become rows 0..top_out: every residue the centred lift of the level-0 residue (the mod_raise entry

@@ -1010,6 +1010,18 @@ int orc_encode(void* cv, const double* vals, int nvals, int nslots, double scale
         for (size_t k = 0; k < c.n; ++k) rows[(size_t)r * c.n + k] = i128_mod(co[k], c.primes[r]);
     return 0;
 }
+// orc_encode over the extended rows: Q primes 0..=top, then every special prime (top + 1 + kp rows)
+int orc_encode_ext(void* cv, const double* vals, int nvals, int nslots, double scale, int top, uint64_t* rows) {
+    Ctx& c = *(Ctx*)cv;
+    if (nslots < 1 || (nslots & (nslots - 1)) || (size_t)nslots > c.n / 2 || top < 0 || top >= c.nq) return -1;
+    std::vector<i128> co;
+    if (!c.enc.coeffs(vals, nvals, nslots, scale, co)) return -2;
+    for (int r = 0; r <= top + c.kp; ++r) {
+        const uint64_t p = c.primes[r <= top ? r : c.nq + (r - top - 1)];
+        for (size_t k = 0; k < c.n; ++k) rows[(size_t)r * c.n + k] = i128_mod(co[k], p);
+    }
+    return 0;
+}
 int orc_decode(void* cv, const uint64_t* row0, int nslots, double scale, double* vals) {
     Ctx& c = *(Ctx*)cv;
     // crt_bottom at composite degree 1 (encode.rs:236-268): the centred residue of q0
@@ -1416,6 +1428,84 @@ int orc_linear_transform(void* cv, const uint64_t* x, const uint64_t* pts, int n
             const size_t o = ((size_t)part * rows + t) * n;
             for (size_t i = 0; i < n; ++i) out[o + i] = addmod(res[o + i], md[o + i], p);
         }
+    return 0;
+}
+
+// The BSGS product with the babies in the extended basis (double hoisting; the sums of the reference's fused
+// CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs and crates/pc-kernels/kernels/args.cuh:325-352): baby 0 = P x on the
+// Q rows and 0 on the special rows; baby b >= 1 = the key inner product of one shared ModUp of x with P c0 added and
+// the output at the automorphism slot, not brought down; res_j = sum_b baby_b pts[bstep j + b] over the Q rows and the
+// special rows; res_j (j >= 1) brought down and rotated (its extended output), summed with res_0; one ModDown.
+// pts: npts evaluation-form plaintexts of top + 1 + kp rows (Q primes 0..=top, then the special primes).
+int orc_linear_transform_ext(void* cv, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
+                             uint64_t* out, int top) {
+    Ctx& c = *(Ctx*)cv;
+    if (npts < 1 || bstep < 1 || stride == 0) return -1;
+    const size_t n = c.n, cw = c.ct_words();
+    const int rows = c.rows(), nq = c.nq, kp = c.kp, nprow = top + 1 + kp;
+    const int gstep = (npts + bstep - 1) / bstep;
+    const int64_t h = (int64_t)n / 2;
+    auto galois = [&](int64_t st) { return powmod(5, (uint64_t)(((st % h) + h) % h), 2 * n); };
+    std::vector<int> erow;  // the extended rows (prime ids) and their plaintext rows
+    for (int t = 0; t <= top; ++t) erow.push_back(t);
+    for (int j = 0; j < kp; ++j) erow.push_back(nq + j);
+    std::vector<uint64_t> baby((size_t)bstep * cw, 0), res((size_t)gstep * cw, 0);
+    std::vector<uint64_t> D;
+    bool have_d = false;
+    for (int b = 0; b < bstep; ++b) {
+        uint64_t* o = baby.data() + (size_t)b * cw;
+        const uint64_t g = galois((int64_t)b * stride);
+        if (g == 1) {  // P x on the Q rows
+            for (int part = 0; part < 2; ++part)
+                for (int t = 0; t <= top; ++t)
+                    for (size_t i = 0; i < n; ++i) {
+                        const size_t k = ((size_t)part * rows + t) * n + i;
+                        o[k] = mul_shoup(x[k], c.pmod[t], c.pmods[t], c.primes[t]);
+                    }
+            continue;
+        }
+        const Key* key = c.key_of(g);
+        if (!key) return -3;
+        if (!have_d) {
+            D = modup(c, x + (size_t)rows * n, top);
+            have_d = true;
+        }
+        const uint64_t ginv = powmod(g, (2 * n >> 2) - 1, 2 * n);
+        dot_ext(c, x + (size_t)rows * n, D, x, 1, *key, (uint32_t)ginv, o, top);
+    }
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int j = 0; j < gstep; ++j)
+        for (int ri = 0; ri < (int)erow.size(); ++ri) {
+            const int t = erow[ri];
+            const uint64_t p = c.primes[t];
+            for (int part = 0; part < 2; ++part) {
+                uint64_t* o = res.data() + (size_t)j * cw + ((size_t)part * rows + t) * n;
+                for (size_t i = 0; i < n; ++i) {
+                    u128 acc = 0;
+                    for (int b = 0; b < bstep && bstep * j + b < npts; ++b)
+                        acc += (u128)baby[(size_t)b * cw + ((size_t)part * rows + t) * n + i] *
+                               pts[((size_t)(bstep * j + b) * nprow + ri) * n + i];
+                    o[i] = (uint64_t)(acc % p);
+                }
+            }
+        }
+    std::vector<uint64_t> sum(res.begin(), res.begin() + cw), ext(cw), md(cw, 0);
+    for (int j = 1; j < gstep; ++j) {
+        const uint64_t g = galois((int64_t)j * bstep * stride);
+        if (g == 1) return -1;
+        const Key* key = c.key_of(g);
+        if (!key) return -3;
+        const uint64_t ginv = powmod(g, (2 * n >> 2) - 1, 2 * n);
+        moddown(c, res.data() + (size_t)j * cw, md.data(), top);
+        keyswitch_ext(c, md.data() + (size_t)rows * n, md.data(), 1, *key, (uint32_t)ginv, ext.data(), top);
+        for (int part = 0; part < 2; ++part)
+            for (int t : erow) {
+                const uint64_t p = c.primes[t];
+                const size_t o = ((size_t)part * rows + t) * n;
+                for (size_t i = 0; i < n; ++i) sum[o + i] = addmod(sum[o + i], ext[o + i], p);
+            }
+    }
+    moddown(c, sum.data(), out, top);
     return 0;
 }
 

@@ -334,6 +334,8 @@ def lib():
         "pcb_decrypt": (C.c_int, [vp, vp, i32, i32, dbl, C.POINTER(dbl), vp]),
         "pcb_encode": (C.c_int, [vp, C.POINTER(dbl), i32, i32, dbl, i32, u64p]),
         "pcb_pt_load": (C.c_int, [vp, u64p, i32, vp, vp]),
+        "pcb_encode_ext": (C.c_int, [vp, C.POINTER(dbl), i32, i32, dbl, i32, u64p]),
+        "pcb_pt_load_ext": (C.c_int, [vp, u64p, i32, vp, vp]),
         "pcb_add": (C.c_int, [vp, vp, vp, vp, i32, i32, vp]),
         "pcb_sum": (C.c_int, [vp, vp, i32, vp, i32, i32, vp]),
         "pcb_rotate_sum": (C.c_int, [vp, vp, vp, i32, vp, i32, i32, vp]),
@@ -350,6 +352,7 @@ def lib():
         "pcb_mult_pt_add": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
         "pcb_linear_transform": (C.c_int, [vp, vp, vp, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_linear_transform_multi": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
+        "pcb_linear_transform_ext": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
         "pcb_mod_raise": (C.c_int, [vp, vp, i32, i32, vp]),
         "pcb_ntt_batch": (C.c_int, [vp, vp, i32, i32, vp]),

@@ -113,6 +113,7 @@ class Params:
     per_group: int = 5     # FFT stages merged per CoeffToSlot / SlotToCoeff group
     ratio_bits: int = 8    # log2(q_0 / Delta') EvalMod works at: the input is first multiplied by the integer
     #                        2^round(log2(q_0 / Delta) - ratio_bits) when that is above 1
+    ext: bool = True       # the groups' BSGS products double-hoisted (babies in the extended basis)
 
     @property
     def slots(self):
@@ -129,17 +130,30 @@ def _bsgs(npts):
     return best
 
 
-def _group_plan(stride, diags, S):
+def _bsgs_ext(npts):
+    """(bstep, gstep) of the double-hoisted product: a baby costs one key inner product, a giant step a ModDown, a
+    ModUp and an inner product; with weights 0.7 and 3.1 (in ModDowns, from the config-4 stage timings) the cheapest
+    split covering npts (ties to the smaller bstep: fewer keys)."""
+    best = None
+    for b in range(1, npts + 1):
+        g = -(-npts // b)
+        cost = 0.7 * (b - 1) + 3.1 * (g - 1)
+        if best is None or cost < best[0] - 1e-9:
+            best = (cost, b, g)
+    return best[1], best[2]
+
+
+def _group_plan(stride, diags, S, ext=False):
     """(D, npts, bstep, gstep) of a group: its offsets -D .. D strides, rotated by -D stride onto 0 .. 2D. A group whose
     2D + 1 offsets exceed the S / stride distinct rotations is folded mod S instead (D = 0, npts = S / stride: offsets
-    congruent mod S are one rotation, their diagonals summed)."""
+    congruent mod S are one rotation, their diagonals summed). ext: the split of the double-hoisted product."""
     D = max(abs(o) for o in diags) // stride
     span = S // stride
     if 2 * D + 1 > span:
         D, npts = 0, span
     else:
         npts = 2 * D + 1
-    bstep, gstep = _bsgs(npts)
+    bstep, gstep = _bsgs_ext(npts) if ext else _bsgs(npts)
     return D, npts, bstep, gstep
 
 
@@ -160,7 +174,7 @@ def rot_steps(p):
     S = p.slots
     for inverse in (True, False):
         for stride, diags in groups(p.n, inverse, p.per_group):
-            D, npts, bstep, gstep = _group_plan(stride, diags, S)
+            D, npts, bstep, gstep = _group_plan(stride, diags, S, p.ext)
             steps.add(-D * stride)
             steps.update(b * stride for b in range(1, bstep))
             steps.update(j * bstep * stride for j in range(1, gstep))
@@ -291,7 +305,7 @@ class Bootstrapper:
         product with the diagonals shifted to 0 .. 2D (or folded mod S), one rescale (the output at out_scale when
         given)."""
         ops, S = self.ops, self.p.slots
-        D, npts, bstep, _ = _group_plan(stride, diags, S)
+        D, npts, bstep, _ = _group_plan(stride, diags, S, self.p.ext)
         top = x.top
         key = ("lt", stride, id(diags), top, float(x.scale), out_scale, None if out_mask is None else id(out_mask))
         lt = self.plan.get(key)
@@ -301,7 +315,8 @@ class Bootstrapper:
                 dl = [d * out_mask for d in dl]
                 self.plan[("mask", id(out_mask))] = out_mask  # kept alive with the entry keyed by its id
             scale = float(self.primes[top]) if out_scale is None else out_scale * self.primes[top] / x.scale
-            lt = self.plan[key] = ops.diagonals(dl, bstep, top=top, scale=scale, slots=S, stride=stride)
+            lt = self.plan[key] = ops.diagonals(dl, bstep, top=top, scale=scale, slots=S, stride=stride,
+                                                ext=self.p.ext)
         y = ops.rotate(x, -D * stride) if D else x
         return ops.rescale_one(ops.linear_transform(y, lt))
 

@@ -653,9 +653,10 @@ int modup(PcbCtx& c, const uint64_t* c1, int top, int K, cudaStream_t s) {
 
 // key inner product of K cts against key `ks` into c.ext: c1 / c0 in ct layout (c0 mode 1 adds P c0 on Q rows)
 int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, int c0_mode, int top, int K,
-        cudaStream_t s) {
+        cudaStream_t s, uint64_t* dst = nullptr) {
     const LevelPlan& l = c.lv[top];
     const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
+    if (!dst) dst = c.ext;
     // one launch for the batch: every key word is read once (the inputs never alias c.ext)
     {
         const int c0i = 0, kk = K;
@@ -664,8 +665,8 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
         a.c1 = c1 + c0i * cw;
         a.modup = c.digits + (size_t)c0i * c.dnum * rn;
         a.c0 = c0 ? c0 + c0i * cw : nullptr;
-        a.out0 = c.ext + c0i * cw;
-        a.out1 = c.ext + c0i * cw + rn;
+        a.out0 = dst + c0i * cw;
+        a.out1 = dst + c0i * cw + rn;
         a.kb = ks.kb;
         a.ka = ks.a ? ks.ka : nullptr;
         a.autok = ks.autok_dev;
@@ -696,16 +697,20 @@ int dot(PcbCtx& c, const KeySlot& ks, const uint64_t* c1, const uint64_t* c0, in
 // Key inner products of K cts against up to KEYS_MAX keys at once (FP64 chains): key r's extended outputs go to
 // the r-th batch of c.ext; the ModUp digits are read once for the whole group
 int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, const uint64_t* c0, int c0_mode,
-              int top, int K, cudaStream_t s) {
+              int top, int K, cudaStream_t s, uint64_t* dst = nullptr, uint64_t dst_stride = 0) {
     const LevelPlan& l = c.lv[top];
     const size_t cw = c.ct_words(), rn = (size_t)c.rows * c.n;
+    if (!dst) {
+        dst = c.ext;
+        dst_stride = (uint64_t)c.k_max * cw;
+    }
     PcbKsArgs a;
     memset(&a, 0, sizeof a);
     a.c1 = c1;
     a.modup = c.digits;
     a.c0 = c0;
-    a.out0 = c.ext;
-    a.out1 = c.ext + rn;
+    a.out0 = dst;
+    a.out1 = dst + rn;
     a.rows = l.ks_rows;
     a.digit_of = c.digit_of;
     a.pmod = c.pmod;
@@ -715,7 +720,7 @@ int dot_group(PcbCtx& c, const KeySlot* const* keys, int n, const uint64_t* c1, 
     a.mu_ct_stride = (uint64_t)c.dnum * rn;
     a.mu_digit_stride = rn;
     a.out_ct_stride = cw;
-    a.out_rot_stride = (uint64_t)c.k_max * cw;
+    a.out_rot_stride = dst_stride;
     a.key_digit_stride = rn;
     a.K = K;
     a.R = n;
@@ -1243,6 +1248,33 @@ int pcb_pt_load(PcbCtx* c, const uint64_t* rows_host, int32_t top, uint64_t* pt,
     return 0;
 }
 
+int pcb_encode_ext(PcbCtx* c, const double* vals, int32_t nvals, int32_t nslots, double scale, int32_t top,
+                   uint64_t* rows) {
+    if (!c || !rows || (nvals && !vals)) return fail(PCB_BAD_ARGS, "null argument");
+    if (nslots < 1 || (nslots & (nslots - 1)) || (size_t)nslots > c->n / 2 || nvals < 0 || nvals > nslots)
+        return fail(PCB_BAD_ARGS, "%d values into %d slots", nvals, nslots);
+    if (top < 0 || top >= c->nq) return fail(PCB_BAD_ARGS, "top %d", top);
+    std::vector<hm::i128> co;
+    if (!c->enc->encode(vals, nvals, nslots, scale, co)) return fail(-2, "scaled value exceeds 2^126");
+    for (int r = 0; r <= top + c->kp; ++r) {
+        const uint64_t p = c->primes[r <= top ? r : c->nq + (r - top - 1)];
+        for (size_t k = 0; k < c->n; ++k) rows[(size_t)r * c->n + k] = hm::mod_i128(co[k], p);
+    }
+    return 0;
+}
+
+int pcb_pt_load_ext(PcbCtx* c, const uint64_t* rows_host, int32_t top, uint64_t* pt, cudaStream_t s) {
+    if (!c || !rows_host || !pt) return fail(PCB_BAD_ARGS, "null argument");
+    int rc = check_top(*c, top, 1);
+    if (rc) return rc;
+    const int nr = top + 1 + c->kp;
+    CK(cudaMemcpyAsync(pt, rows_host, (size_t)nr * c->n * 8, cudaMemcpyHostToDevice, s));
+    PcbNttArgs a = ntt_args(*c, pt, c->id_roff, (const int32_t*)c->lv[top].ks_rows, nr);
+    CK(ntt_fwd(*c, &a, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
 static int ew_ct(PcbCtx* c, const uint64_t* a, const uint64_t* b, uint64_t* out, int top, int K, int sub,
                  cudaStream_t s) {
     if (!c || !a || !b || !out) return fail(PCB_BAD_ARGS, "null argument");
@@ -1742,6 +1774,138 @@ int pcb_linear_transform_multi(PcbCtx* c, const uint64_t* x, const uint64_t* con
 int pcb_linear_transform(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t npts, int32_t bstep,
                          int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K, cudaStream_t s) {
     return pcb_linear_transform_multi(c, x, pts, 1, npts, bstep, stride, work, out, top, K, s);
+}
+
+// The BSGS product with the babies kept in the extended basis (double hoisting; the sums of the reference's fused
+// CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs with the cts_fused launcher, argument rules of args.cuh:325-352):
+// 1. baby 0 = P x on the Q rows and 0 on the special rows; babies b >= 1 = one ModUp of x, then each key's inner
+//    product with P c0 added, scattered by the automorphism, written straight into its slot: no ModDown;
+// 2. the baby sums res_j over the Q rows and the special rows (plaintexts with special rows: pcb_pt_load_ext);
+// 3. res_j (j >= 1) brought down (ModDown) and rotated by its giant step, the extended outputs summed with res_0;
+//    one ModDown. bstep - 1 ModDowns fewer than pcb_linear_transform_multi for gstep - 1 more.
+int pcb_linear_transform_ext(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
+                             int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
+                             cudaStream_t s) {
+    if (!c || !x || !pts || !work || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (nw < 1 || npts < 1 || bstep < 1 || bstep > 256 || stride == 0)
+        return fail(PCB_BAD_ARGS, "nw %d, npts %d, bstep %d (1..256), stride %lld", nw, npts, bstep, (long long)stride);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    const int KW = nw * K;
+    if (KW > c->k_max) return fail(PCB_BAD_ARGS, "%d weights x %d ciphertexts exceed k_max %d", nw, K, c->k_max);
+    const int gstep = (npts + bstep - 1) / bstep;
+    const size_t cw = c->ct_words(), kw = (size_t)K * cw, gw = (size_t)KW * cw, rn = (size_t)c->rows * c->n;
+    uint64_t* baby = work;
+    uint64_t* res = work + (size_t)bstep * kw;  // [gstep][nw][K], extended
+    const uint64_t* wend = res + (size_t)gstep * gw;
+    if (x >= work && x < wend) return fail(PCB_BAD_ARGS, "x inside the workspace");
+    if (out + gw > work && out < wend) return fail(PCB_BAD_ARGS, "out overlaps the workspace");
+    std::vector<const KeySlot*> giant(gstep, nullptr), bk(bstep, nullptr);
+    for (int j = 1; j < gstep; ++j) {
+        const int64_t st = (int64_t)j * bstep * stride;
+        const uint64_t g = rot_galois(*c, st);
+        if (g == 1) return fail(PCB_BAD_ARGS, "giant step %lld is the identity", (long long)st);
+        giant[j] = key_of(*c, g);
+        if (!giant[j]) return fail(-3, "no rotation key for giant step %lld (galois %llu)", (long long)st, (unsigned long long)g);
+    }
+    bool any = false;
+    for (int b = 1; b < bstep; ++b) {
+        const uint64_t g = rot_galois(*c, (int64_t)b * stride);
+        if (g == 1) continue;
+        bk[b] = key_of(*c, g);
+        if (!bk[b]) return fail(-3, "no rotation key for baby step %lld (galois %llu)", (long long)(b * stride), (unsigned long long)g);
+        any = true;
+    }
+    PcbRowSet ext_rows;
+    memset(&ext_rows, 0, sizeof ext_rows);
+    ext_rows.nq = top + 1;
+    ext_rows.np = c->kp;
+    ext_rows.qmax = c->nq;
+    // 1. babies: P x (baby 0 and any identity step), the others by the hoisted inner products
+    for (int b = 0; b < bstep; ++b) {
+        if (b > 0 && bk[b]) continue;
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, baby + (size_t)b * kw);
+        e.a = ct_ref(*c, x);
+        e.rs = ext_rows;
+        e.sc = c->pmod;
+        e.scs = c->pmods;
+        e.zero_p = 1;
+        e.pr = c->pr;
+        e.K = K;
+        e.nparts = 2;
+        CK(c->tab->ew_scale(&e, s));
+    }
+    if (any) {
+        const uint64_t* c1 = x + rn;
+        rc = modup(*c, c1, top, K, s);
+        if (rc) return rc;
+        const bool grouped = c->ext_groups > 1 && c->lv[top].ndig <= 4;
+        std::vector<int> todo;
+        for (int b = 1; b < bstep; ++b)
+            if (bk[b]) todo.push_back(b);
+        size_t g0 = 0;
+        while (g0 < todo.size()) {
+            // a group: consecutive baby slots (their outputs kw apart), up to ext_groups keys
+            size_t n = 1;
+            while (grouped && g0 + n < todo.size() && (int)n < c->ext_groups && todo[g0 + n] == todo[g0] + (int)n) ++n;
+            uint64_t* dst = baby + (size_t)todo[g0] * kw;
+            if (n > 1) {
+                const KeySlot* grp[ks::KEYS_MAX];
+                for (size_t r = 0; r < n; ++r) grp[r] = bk[todo[g0 + r]];
+                rc = dot_group(*c, grp, (int)n, c1, x, 1, top, K, s, dst, kw);
+            } else {
+                rc = dot(*c, *bk[todo[g0]], c1, x, 1, top, K, s, dst);
+            }
+            if (rc) return rc;
+            g0 += n;
+        }
+    }
+    // 2. baby sums over the extended rows
+    for (int w = 0; w < nw; ++w)
+        for (int c0 = 0; c0 < K; c0 += 8) {
+            PcbPtDotArgs a;
+            memset(&a, 0, sizeof a);
+            a.rot = ct_ref(*c, baby + (size_t)c0 * cw);
+            a.res = ct_ref(*c, res + (size_t)w * kw + (size_t)c0 * cw);
+            a.rot_stride = kw;
+            a.res_stride = gw;
+            a.pts = (const void* const*)(pts + (size_t)w * npts);
+            a.pr = c->pr;
+            a.rs = ext_rows;
+            a.npts = npts;
+            a.bstep = bstep;
+            a.gstep = gstep;
+            a.K = std::min(8, K - c0);
+            a.ptw = (int32_t)c->n;
+            a.pt_prow = top + 1;
+            a.enc = 0xFFFFFFFFu;
+            CK(c->logn == 14 ? pt::pt_dot_launch<14>(&a, s) : pt::pt_dot_launch<16>(&a, s));
+        }
+    if (gstep == 1) return moddown(*c, out, false, top, KW, s, res);
+    // 3. giant steps over the nw K batch: res_j down, rotated, summed in c.ext with res_0, one ModDown
+    for (int j = 1; j < gstep; ++j) {
+        rc = moddown(*c, c->dbuf, false, top, KW, s, res + (size_t)j * gw);
+        if (rc) return rc;
+        rc = modup(*c, c->dbuf + rn, top, KW, s);
+        if (rc) return rc;
+        rc = dot(*c, *giant[j], c->dbuf + rn, c->dbuf, j == 1 ? 1 : 1 | PCB_KS_ACC, top, KW, s);
+        if (rc) return rc;
+    }
+    {
+        PcbEwArgs e;
+        memset(&e, 0, sizeof e);
+        e.out = ct_ref(*c, c->ext);
+        e.a = ct_ref(*c, c->ext);
+        e.b = ct_ref(*c, res);
+        e.rs = ext_rows;
+        e.pr = c->pr;
+        e.K = KW;
+        e.nparts = 2;
+        CK(c->tab->ew_add(&e, s));
+    }
+    return moddown(*c, out, false, top, KW, s);
 }
 
 int pcb_ntt_batch(PcbCtx* c, uint64_t* x, int32_t nrows, int32_t inverse, cudaStream_t s) {

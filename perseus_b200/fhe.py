@@ -132,6 +132,7 @@ class Diagonals:
     top: int
     scale: float
     slots: int
+    ext: bool = False  # rows over the special primes too (top + 1 + kp rows): the double-hoisted product
 
     @property
     def npts(self):
@@ -390,22 +391,28 @@ class Session:
                                         a.top, a.k, self._stream()), "pcb_mult_pt_add")
         return out
 
-    def diagonals(self, diags, bstep, top=None, scale=None, slots=None, stride=1):
+    def diagonals(self, diags, bstep, top=None, scale=None, slots=None, stride=1, ext=False):
         """Encode the generalized diagonals diag_d (d < npts; slot vectors) of a slots x slots matrix M (diag_d[i] =
         M[i, i + d stride]) for linear_transform: y = sum_d diag_d * rot(x, d stride). scale defaults to q_top, so
-        one rescale returns the product to x's scale."""
+        one rescale returns the product to x's scale. ext: the rows of the special primes too, for the
+        double-hoisted product (pcb_linear_transform_ext)."""
         top = self.top() if top is None else top
         diags = [np.asarray(v) for v in diags]
         slots = slots or len(diags[0])
         scale = float(self.chain.q[top]) if scale is None else scale
-        pts = torch.zeros((len(diags), top + 1, self.n), dtype=torch.int64, device=self.device)  # rows 0..top read
+        nr = top + 1 + (len(self.chain.p) if ext else 0)
+        pts = torch.zeros((len(diags), nr, self.n), dtype=torch.int64, device=self.device)  # the rows read
+        enc, load = (L.lib().pcb_encode_ext, L.lib().pcb_pt_load_ext) if ext else (L.lib().pcb_encode, L.lib().pcb_pt_load)
         for d, v in enumerate(diags):
             g = (d // bstep) * bstep * stride
-            rows = self.encode(np.roll(v, g), slots=slots, scale=scale, top=top)
-            L.check(L.lib().pcb_pt_load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(pts[d].data_ptr()),
-                                        self._stream()), "pcb_pt_load")
+            flat, nv = self._vals(np.roll(v, g))
+            rows = np.zeros((nr, self.n), np.uint64)
+            L.check(enc(self.ctx, flat.ctypes.data_as(C.POINTER(C.c_double)), nv, slots, scale, top,
+                        rows.ctypes.data_as(L.u64p)), "pcb_encode")
+            L.check(load(self.ctx, rows.ctypes.data_as(L.u64p), top, C.c_void_p(pts[d].data_ptr()), self._stream()),
+                    "pcb_pt_load")
         table = torch.tensor([pts[d].data_ptr() for d in range(len(diags))], dtype=torch.int64, device=self.device)
-        return Diagonals(pts, table, int(bstep), int(stride), top, scale, slots)
+        return Diagonals(pts, table, int(bstep), int(stride), top, scale, slots, bool(ext))
 
     def linear_work(self, lt, k=1, nw=1):
         """Scratch for linear_transform(_multi): (bstep + gstep nw) k ciphertexts."""
@@ -419,9 +426,14 @@ class Session:
             raise ValueError(f"ciphertext at top {a.top}, diagonals encoded at top {lt.top}")
         out = out if out is not None else Ct(self.empty(a.k), a.top, a.scale * lt.scale, a.slots)
         work = work if work is not None else self.linear_work(lt, a.k)
-        L.check(L.lib().pcb_linear_transform(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), lt.npts, lt.bstep,
-                                             lt.stride, C.c_void_p(work.data_ptr()), out.ptr(), a.top, a.k,
-                                             self._stream()), "pcb_linear_transform")
+        if lt.ext:  # the double-hoisted form (babies in the extended basis)
+            L.check(L.lib().pcb_linear_transform_ext(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), 1, lt.npts,
+                                                     lt.bstep, lt.stride, C.c_void_p(work.data_ptr()), out.ptr(),
+                                                     a.top, a.k, self._stream()), "pcb_linear_transform_ext")
+        else:
+            L.check(L.lib().pcb_linear_transform(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), lt.npts,
+                                                 lt.bstep, lt.stride, C.c_void_p(work.data_ptr()), out.ptr(), a.top,
+                                                 a.k, self._stream()), "pcb_linear_transform")
         out.scale = a.scale * lt.scale
         return out
 
@@ -438,9 +450,11 @@ class Session:
         out = Ct(self.empty(len(lts) * a.k), a.top, a.scale * lt0.scale, a.slots)
         work = work if work is not None else self.linear_work(lt0, a.k, len(lts))
         table = torch.cat([lt.table for lt in lts])
-        L.check(L.lib().pcb_linear_transform_multi(self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts),
-                                                   lt0.npts, lt0.bstep, lt0.stride, C.c_void_p(work.data_ptr()),
-                                                   out.ptr(), a.top, a.k, self._stream()), "pcb_linear_transform_multi")
+        if any(lt.ext != lt0.ext for lt in lts):
+            raise ValueError("linear_transform_multi: extended and plain diagonal sets mixed")
+        f = L.lib().pcb_linear_transform_ext if lt0.ext else L.lib().pcb_linear_transform_multi
+        L.check(f(self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts), lt0.npts, lt0.bstep, lt0.stride,
+                  C.c_void_p(work.data_ptr()), out.ptr(), a.top, a.k, self._stream()), "pcb_linear_transform_multi")
         return out
 
     def split(self, a, n):

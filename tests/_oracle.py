@@ -70,6 +70,8 @@ def lib():
         "orc_secret": (None, [C.c_void_p, i8p]),
         "orc_key": (C.c_int, [C.c_void_p, C.c_int, u64p, u64p, u32p]),
         "orc_encode": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
+        "orc_encode_ext": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
+        "orc_linear_transform_ext": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_int64, u64p, C.c_int]),
         "orc_decode": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_double, f64p]),
         "orc_encrypt": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
         "orc_decrypt": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int, C.c_double, f64p]),
@@ -199,6 +201,13 @@ class Ctx:
         assert lib().orc_encode(self.h, vals, nv, nslots, scale, top, rows) == 0
         return rows
 
+    def encode_ext(self, values, nslots, scale, top):
+        """the encoding's rows over the Q primes 0..=top, then every special prime"""
+        vals, nv = self._vals(values)
+        rows = np.zeros((top + 1 + self.kp, self.n), np.uint64)
+        assert lib().orc_encode_ext(self.h, vals, nv, nslots, scale, top, rows) == 0
+        return rows
+
     def encrypt(self, values, nslots, scale, top):
         vals, nv = self._vals(values)
         ct = self.ct()
@@ -280,6 +289,15 @@ class Ctx:
         out = self.ct()
         pts = np.ascontiguousarray(pts, np.uint64)
         rc = lib().orc_linear_transform(self.h, np.ascontiguousarray(ct), pts, pts.shape[0], bstep, stride, out, top)
+        assert rc == 0, rc
+        return out
+
+    def linear_transform_ext(self, ct, pts, bstep, stride, top):
+        """The double-hoisted product; pts [npts][top + 1 + kp][N] evaluation-form plaintexts over the extended rows."""
+        out = self.ct()
+        pts = np.ascontiguousarray(pts, np.uint64)
+        rc = lib().orc_linear_transform_ext(self.h, np.ascontiguousarray(ct), pts, pts.shape[0], bstep, stride, out,
+                                            top)
         assert rc == 0, rc
         return out
 

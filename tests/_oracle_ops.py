@@ -49,6 +49,7 @@ class OracleDiagonals:
     stride: int
     top: int
     scale: float
+    ext: bool = False
 
 
 def _batched(f):
@@ -187,22 +188,26 @@ class OracleOps:
             acc = self.add(acc, c)
         return acc
 
-    def diagonals(self, diags, bstep, top, scale=None, slots=None, stride=1):
-        """Evaluation-form plaintexts of a BSGS product (diagonal d pre-rotated by -bstep (d // bstep) stride)."""
+    def diagonals(self, diags, bstep, top, scale=None, slots=None, stride=1, ext=False):
+        """Evaluation-form plaintexts of a BSGS product (diagonal d pre-rotated by -bstep (d // bstep) stride); ext:
+        over the Q primes 0..=top and every special prime, for the double-hoisted product."""
         from tests import _oracle as O
         slots = slots or len(diags[0])
         scale = float(self.c.q[top]) if scale is None else scale
-        pts = np.zeros((len(diags), self.c.nq, self.c.n), np.uint64)
+        primes = list(self.c.q[: top + 1]) + (list(self.c.p) if ext else [])
+        pts = np.zeros((len(diags), len(primes) if ext else self.c.nq, self.c.n), np.uint64)
         for d, v in enumerate(diags):
-            rows = self.c.encode(np.roll(np.asarray(v), (d // bstep) * bstep * stride), slots, scale, top)
-            O.lib().orc_ntt_fwd(rows, top + 1, np.asarray(self.c.q[: top + 1], np.uint64), self.c.logn)
-            pts[d, : top + 1] = rows
-        return OracleDiagonals(pts, bstep, stride, top, scale)
+            vr = np.roll(np.asarray(v), (d // bstep) * bstep * stride)
+            rows = self.c.encode_ext(vr, slots, scale, top) if ext else self.c.encode(vr, slots, scale, top)
+            O.lib().orc_ntt_fwd(rows, len(primes), np.asarray(primes, np.uint64), self.c.logn)
+            pts[d, : len(primes)] = rows
+        return OracleDiagonals(pts, bstep, stride, top, scale, ext)
 
     @_batched
     def linear_transform(self, a, lt):
         assert a.top == lt.top
-        out = self.c.linear_transform(a.data, lt.pts, lt.bstep, lt.stride, a.top)
+        f = self.c.linear_transform_ext if lt.ext else self.c.linear_transform
+        out = f(a.data, lt.pts, lt.bstep, lt.stride, a.top)
         return OCt(out, a.top, a.scale * lt.scale, a.slots)
 
     def linear_transform_multi(self, a, lts):

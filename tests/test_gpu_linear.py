@@ -81,6 +81,38 @@ def test_linear_transform_bit_exact(case):
         assert np.abs(got - ref).max() < 1e-4, name
 
 
+def test_linear_transform_ext_bit_exact(case):
+    """The double-hoisted product (pcb_linear_transform_ext: babies in the extended basis, plaintexts over the
+    special primes too) equals the oracle's restatement word for word, below the top level too, and decrypts to the
+    generalized diagonal method."""
+    name, s, o, bstep, npts, stride, k = case
+    rng = np.random.default_rng(41)
+    slots = s.n // 2
+    for top in (s.top(), s.top() - 2):
+        xs = [rng.normal(0, 1, slots) / 4 for _ in range(k)]
+        cts = [s.encrypt(x, top=top, slots=slots) for x in xs]
+        a = s.stack(cts) if k > 1 else cts[0]
+        diags = [rng.normal(0, 1, slots) / 4 for _ in range(npts)]
+        lt = s.diagonals(diags, bstep, top=top, stride=stride, ext=True)
+        primes = list(o.q[: top + 1]) + list(o.p)
+        opts = np.zeros((npts, len(primes), s.n), np.uint64)
+        for d, v in enumerate(diags):
+            rows = o.encode_ext(np.roll(v, (d // bstep) * bstep * stride), slots, lt.scale, top)
+            O.lib().orc_ntt_fwd(rows, len(primes), np.asarray(primes, np.uint64), s.log_n)
+            opts[d] = rows
+        assert (host(lt.pts) == opts).all()
+        out = s.linear_transform(a, lt)
+        for c in range(k):
+            oc = o.encrypt(xs[c], slots, cts[c].scale, top)
+            want = o.linear_transform_ext(oc, opts, bstep, stride, top)
+            assert (host(out.data[c])[:, : top + 1] == want[:, : top + 1]).all(), (name, top, c)
+        s.rescale_one(out)
+        for c in range(k):
+            got = s.decrypt_slots(out, c).real
+            ref = sum(dg * np.roll(xs[c], -d * stride) for d, dg in enumerate(diags))
+            assert np.abs(got - ref).max() < 1e-4, (name, top)
+
+
 def test_mult_pt_add_bit_exact(case):
     name, s, o, *_ = case
     rng = np.random.default_rng(41)

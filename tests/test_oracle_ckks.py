@@ -182,6 +182,39 @@ def test_linear_transform(ctx_r, npts, bstep):
     assert np.abs(got - want).max() < 1e-4
 
 
+def eval_pts_ext(ctx, vecs, scale, top):
+    primes = list(ctx.q[: top + 1]) + list(ctx.p)
+    pts = np.zeros((len(vecs), len(primes), N), np.uint64)
+    for d, v in enumerate(vecs):
+        rows = ctx.encode_ext(v, SLOTS, scale, top)
+        O.lib().orc_ntt_fwd(rows, len(primes), np.asarray(primes, np.uint64), LOGN)
+        pts[d] = rows
+    return pts
+
+
+@pytest.mark.parametrize("npts,bstep,top", [(8, 4, 5), (7, 4, 5), (3, 4, 5), (12, 4, 3), (16, 16, 5)])
+def test_linear_transform_ext(ctx_r, npts, bstep, top):
+    """The double-hoisted BSGS product (babies in the extended basis, no baby ModDown; plaintexts over the special
+    primes too) decrypts to sum_d diag_d * rot(x, d) as the plain product does (within the key-switch noise), at the
+    top level and below it; a single giant step and 16 babies included. The two forms round at other points."""
+    x = vals(18)
+    rng = np.random.default_rng(19)
+    diags = [rng.normal(0, 1, SLOTS) for _ in range(npts)]
+    ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    pscale = float(ctx_r.q[top])
+    vecs = bsgs_diagonals(diags, bstep, 1)
+    want = sum(dg * np.roll(x, -d) for d, dg in enumerate(diags))
+    if bstep <= 4:  # the plain form with the same keys
+        ref = ctx_r.rescale(ctx_r.linear_transform(ct, eval_pts(ctx_r, vecs, pscale, top), bstep, 1, top), top)
+        assert np.abs(ctx_r.decrypt(ref, top - 1, SLOTS, SCALE).real - want).max() < 1e-4
+    else:  # keys for every baby step
+        ctx_r = make_ctx(nq=6, kp=3, dnum=2, pbits=50, steps=tuple(range(1, bstep)))
+        ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    ext = ctx_r.linear_transform_ext(ct, eval_pts_ext(ctx_r, vecs, pscale, top), bstep, 1, top)
+    got = ctx_r.decrypt(ctx_r.rescale(ext, top), top - 1, SLOTS, SCALE).real
+    assert np.abs(got - want).max() < 1e-4
+
+
 def test_hoisted_rotations_equal_plain_ones():
     """orc_rotate_hoisted (one ModUp for every step) = orc_rotate step by step, word for word; a step of galois 1
     copies."""

@@ -585,9 +585,11 @@ def projection(a, world, barrier, dist):
               for y, W, b in zip(ys, Ws, bs))
     del s, qkv, out, xc, ys
     torch.cuda.empty_cache()
+    form = "double-hoisted: babies in the extended basis" if geo.ext else "hoisted babies"
     return {"workload": "GPT-2 attention projections, one token: Q/K/V linears (768 of 1024, shared input) and the "
-                        "output linear, N=2^16 24+8 limbs, 32 weight plaintexts each (8 baby x 4 giant), radix-3 "
-                        "ladders", "qkv_ms": t[0].item(), "out_ms": t[1].item(), "max_abs_err_vs_fp64": err}
+                        f"output linear, N=2^16 24+8 limbs, {geo.npts} weight plaintexts each ({geo.bstep} baby x "
+                        f"{geo.gstep} giant, {form}), radix-3 ladders",
+            "qkv_ms": t[0].item(), "out_ms": t[1].item(), "max_abs_err_vs_fp64": err}
 
 
 def block_decode(a, world, barrier, dist, seqs=1):

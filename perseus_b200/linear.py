@@ -16,7 +16,9 @@ The layout, restated (S slots, t = S / d, R = d^2 / S weight plaintexts):
   W[(m + u + j t) mod d, m] x[(m + u + j t) mod d] = (x W)[m], since u + j t runs over 0 .. d - 1;
 - bias: b[m] on every slot of block m (added after the fold).
 bstep g = R with bstep + gstep minimal, ties to the larger bstep (the reference's choice, so the rotation keys and
-the plaintext order are the same).
+the plaintext order are the same) for the plain product; the double-hoisted product (babies in the extended basis,
+pcb_linear_transform_ext, the default) takes the divisor split of least cost with a baby at 0.7 and a giant step at
+3.1 ModDowns (R = 32: 16 x 2 instead of 8 x 4).
 
 One rescale after the product: the output sits one level below the input at the input's scale (the weight
 plaintexts are encoded at q_top). The same functions run on the CUDA session and, in the tests, on an oracle-backed
@@ -37,6 +39,7 @@ class Geometry:
     npts: int  # weight plaintexts R = d^2 / S
     bstep: int
     gstep: int
+    ext: bool = False  # the double-hoisted product (plaintexts over the special primes too)
 
     @property
     def stride(self):
@@ -58,16 +61,21 @@ class Geometry:
         return [s % self.slots for s in steps if s % self.slots and not (s % self.slots in seen or seen.add(s % self.slots))]
 
 
-def geometry(slots, d):
-    """The square-layer geometry of cm_params (layout.py:77-98) for d_in = d_out = d."""
+def geometry(slots, d, ext=True):
+    """The square-layer geometry of cm_params (layout.py:77-98) for d_in = d_out = d; ext: the double-hoisted
+    product's split (else the reference's)."""
     if d & (d - 1) or slots & (slots - 1) or d > slots or d * d < slots:
         raise ValueError(f"width {d} must be a power of two with d^2 >= slots ({slots}) and d <= slots")
     t, r = slots // d, d * d // slots
-    best = (r, 1)
-    for b in range(1, r + 1):
-        if r % b == 0 and (b + r // b < sum(best) or (b + r // b == sum(best) and b > best[0])):
-            best = (b, r // b)
-    return Geometry(slots, d, t, r, best[0], best[1])
+    splits = [(b, r // b) for b in range(1, r + 1) if r % b == 0]
+    if ext:
+        best = min(splits, key=lambda s: (0.7 * (s[0] - 1) + 3.1 * (s[1] - 1), s[0]))
+    else:
+        best = (r, 1)
+        for b, g in splits:
+            if b + g < sum(best) or (b + g == sum(best) and b > best[0]):
+                best = (b, g)
+    return Geometry(slots, d, t, r, best[0], best[1], bool(ext))
 
 
 def input_vector(x, geo):
@@ -116,7 +124,8 @@ def encode(ops, W, geo, top, x_scale, bias=None, out_scale=None):
     """Encode W (and b) for inputs at level `top` and scale x_scale: R plaintexts at q_top, the bias at level top - 1;
     the output lands at x_scale, or at out_scale when given (the plaintexts encoded at out_scale q_top / x_scale)."""
     pscale = None if out_scale is None else out_scale * ops.chain.q[top] / x_scale
-    lt = ops.diagonals(weight_vectors(W, geo), geo.bstep, top=top, scale=pscale, slots=geo.slots, stride=geo.stride)
+    lt = ops.diagonals(weight_vectors(W, geo), geo.bstep, top=top, scale=pscale, slots=geo.slots, stride=geo.stride,
+                       ext=geo.ext)
     y_scale = x_scale if out_scale is None else out_scale
     bpt = None
     if bias is not None:

@@ -22,10 +22,14 @@ def ladder(v, start, stop):
 
 
 def test_gpt2_geometry():
-    g = LIN.geometry(1 << 15, 1024)
+    g = LIN.geometry(1 << 15, 1024, ext=False)  # the reference's split
     assert (g.t, g.npts, g.bstep, g.gstep, g.stride) == (32, 32, 8, 4, 1024)
     assert sorted(g.rot_steps()) == sorted([31, 62, 124, 248, 496] + [1024 * b for b in range(1, 8)] +
                                            [8192, 16384, 24576] + [1, 2, 4, 8, 16])
+    g = LIN.geometry(1 << 15, 1024)  # the double-hoisted product's
+    assert (g.t, g.npts, g.bstep, g.gstep, g.stride, g.ext) == (32, 32, 16, 2, 1024, True)
+    assert sorted(g.rot_steps()) == sorted([31, 62, 124, 248, 496] + [1024 * b for b in range(1, 16)] +
+                                           [16384] + [1, 2, 4, 8, 16])
     with pytest.raises(ValueError):
         LIN.geometry(1 << 15, 96)
 

@@ -758,6 +758,12 @@ int pcb_add_pt(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, uint64_t* out
  * (crates/pc-gpu/src/ops.rs:968-1005, one mul_add launch). out may alias x or y. */
 int pcb_mult_pt_add(PcbCtx* ctx, const uint64_t* x, const uint64_t* pt, const uint64_t* y, uint64_t* out, int32_t sub,
                     int32_t top, int32_t K, cudaStream_t stream);
+/* out = sum_{j < n} xs[j] * pts[j] (n in [1, 8]; xs: host array of device ciphertext batches, pts: host array of
+ * device plaintexts as pcb_mult_pt's) in one pass, the table's mul_add_n: e.g. every term of a polynomial multiplied
+ * by its coefficient and summed, one read of each operand and one write. out may alias one of xs. No counterpart in
+ * the reference's Fhe API (its evaluator chains mult_pt_add). */
+int pcb_mult_pt_sum(PcbCtx* ctx, const uint64_t* const* xs, const uint64_t* const* pts, int32_t n, uint64_t* out,
+                    int32_t top, int32_t K, cudaStream_t stream);
 /* The BSGS plaintext-matrix product of K ciphertexts (the LT stage of crates/pc-gpu/src/bts/cts.rs; apply_linear of
  * python/perseus/impl/linear.py):
  *   out = sum_{j < gstep} rot(sum_{b < bstep} rot(x, b stride) * pts[bstep j + b], bstep j stride),

@@ -193,12 +193,12 @@ def poly7(ops, plan, x, coeffs, mask, primes, slots):
     def inner_pre(cs, pre, level):
         # sum_{i >= 1} c_i mask x^i at `level`, one rescale short: each x^i taken to `level` times its coefficient at
         # the plaintext scale that puts the product at `pre`, summed in the same pass (the constant returned apart)
-        acc = None
+        terms = []
         for pw, c in zip((x, x2, x3), cs[1:]):
             src = ops.drop_to(pw, level)
             pscale = pre / src.scale
-            pt = _pt(ops, plan, mask * c, level, pscale, slots)
-            acc = ops.mult_pt(src, pt, pscale) if acc is None else ops.mult_pt_add(src, pt, pscale, acc)
+            terms.append((src, _pt(ops, plan, mask * c, level, pscale, slots), pscale))
+        acc = ops.mult_pt_sum(terms)  # the terms multiplied and summed in one pass
         acc.scale = pre
         return acc, cs[0]
 

@@ -258,14 +258,14 @@ class Cheb:
         d = len(c) - 1
         pre = scale * primes[level + 1]
         if d < 8:
-            acc = None
+            terms = []
             for k in range(1, max(d, 1) + 1):
                 if d > 0 and c[k] == 0.0:
                     continue  # (a constant keeps a zero c_1 term: c_0 needs a ciphertext at the level and scale)
                 x = ops.drop_to(self.T[k], level + 1)
                 pscale = pre / x.scale
-                pt = _const_pt(ops, plan, c[k] if d > 0 else 0.0, level + 1, pscale, x.slots)
-                acc = ops.mult_pt(x, pt, pscale) if acc is None else ops.mult_pt_add(x, pt, pscale, acc)
+                terms.append((x, _const_pt(ops, plan, c[k] if d > 0 else 0.0, level + 1, pscale, x.slots), pscale))
+            acc = ops.mult_pt_sum(terms)  # every term multiplied and summed in one pass
             acc.scale = pre
             return acc, c[0]
         m = 1 << (d.bit_length() - 1)

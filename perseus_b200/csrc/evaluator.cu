@@ -1663,6 +1663,30 @@ int pcb_mult_pt_add(PcbCtx* c, const uint64_t* x, const uint64_t* pt, const uint
     return 0;
 }
 
+// out = sum_j xs[j] pts[j] in one pass of the table's mul_add_n (every ciphertext and plaintext read once, one write)
+int pcb_mult_pt_sum(PcbCtx* c, const uint64_t* const* xs, const uint64_t* const* pts, int32_t n, uint64_t* out,
+                    int32_t top, int32_t K, cudaStream_t s) {
+    if (!c || !xs || !pts || !out) return fail(PCB_BAD_ARGS, "null argument");
+    if (n < 1 || n > 8) return fail(PCB_BAD_ARGS, "%d terms (1..8)", n);
+    int rc = check_top(*c, top, K);
+    if (rc) return rc;
+    PcbMulAddNArgs a;
+    memset(&a, 0, sizeof a);
+    a.out = ct_ref(*c, out);
+    for (int j = 0; j < n; ++j) {
+        if (!xs[j] || !pts[j]) return fail(PCB_BAD_ARGS, "term %d is null", j);
+        a.x[j] = ct_ref(*c, xs[j]);
+        a.t[j] = pts[j];
+    }
+    a.pr = c->pr;
+    a.n = top + 1;
+    a.K = K;
+    a.nterm = n;
+    a.lazy = 1;
+    CK(c->logn == 14 ? pt::mul_add_n_launch<14>(&a, s) : pt::mul_add_n_launch<16>(&a, s));
+    return 0;
+}
+
 int pcb_add_pt(PcbCtx* c, const uint64_t* x, const uint64_t* pt, uint64_t* out, int32_t top, int32_t K,
                cudaStream_t s) {
     if (!c || !x || !pt || !out) return fail(PCB_BAD_ARGS, "null argument");

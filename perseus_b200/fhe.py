@@ -391,6 +391,19 @@ class Session:
                                         a.top, a.k, self._stream()), "pcb_mult_pt_add")
         return out
 
+    def mult_pt_sum(self, terms):
+        """sum_j x_j * pt_j for terms (x_j, pt_j, pt_scale_j) at one level and batch, every product at the first
+        term's scale, in one pass (pcb_mult_pt_sum; up to 8 terms)."""
+        x0, _, s0 = terms[0]
+        for x, _, _ in terms[1:]:
+            self._same(x0, x)
+        out = Ct(self.empty(x0.k), x0.top, x0.scale * s0, x0.slots)
+        xs = (C.c_void_p * len(terms))(*[x.data.data_ptr() for x, _, _ in terms])
+        ps = (C.c_void_p * len(terms))(*[p.data_ptr() for _, p, _ in terms])
+        L.check(L.lib().pcb_mult_pt_sum(self.ctx, xs, ps, len(terms), out.ptr(), x0.top, x0.k, self._stream()),
+                "pcb_mult_pt_sum")
+        return out
+
     def diagonals(self, diags, bstep, top=None, scale=None, slots=None, stride=1, ext=False):
         """Encode the generalized diagonals diag_d (d < npts; slot vectors) of a slots x slots matrix M (diag_d[i] =
         M[i, i + d stride]) for linear_transform: y = sum_d diag_d * rot(x, d stride). scale defaults to q_top, so

@@ -156,6 +156,14 @@ class OracleOps:
             self.c.sub(y.data, m, a.top) if sub == 1 else self.c.sub(m, y.data, a.top))
         return OCt(d, y.top, y.scale, y.slots)
 
+    def mult_pt_sum(self, terms):
+        """sum_j x_j * pt_j (the session's one-pass op) as oracle products and sums: the same residues"""
+        acc = None
+        for x, pt, ps in terms:
+            m = self.mult_pt(x, pt, ps)
+            acc = m if acc is None else self.add(acc, m)
+        return acc
+
     @_batched
     def add_pt(self, a, pt):
         return OCt(self.c.add_pt(a.data, pt, a.top), a.top, a.scale, a.slots)

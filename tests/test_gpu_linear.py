@@ -132,6 +132,24 @@ def test_mult_pt_add_bit_exact(case):
         assert (host(out.data[0])[:, : top + 1] == want[:, : top + 1]).all(), (name, sub)
 
 
+def test_mult_pt_sum_bit_exact(case):
+    """pcb_mult_pt_sum (a polynomial's terms in one pass, the mul_add_n launcher): 1, 3 and 8 terms of ciphertexts at
+    one level, below the top too, equal the oracle's products summed, word for word."""
+    name, s, o, *_ = case
+    rng = np.random.default_rng(43)
+    for top, n in ((s.top(), 1), (s.top(), 3), (s.top() - 1, 8)):
+        xs = [rng.normal(0, 1, 256) / 4 for _ in range(n)]
+        ws = [rng.normal(0, 1, 256) / 4 for _ in range(n)]
+        cts = [s.encrypt(x, top=top) for x in xs]
+        pts = [s.pt(w, top, 2.0**30, cts[0].slots) for w in ws]
+        out = s.mult_pt_sum([(c, p, 2.0**30) for c, p in zip(cts, pts)])
+        want = None
+        for x, c, w in zip(xs, cts, ws):
+            m = o.mult_pt(o.encrypt(x, c.slots, c.scale, top), s.encode(w, slots=c.slots, scale=2.0**30, top=top), top)
+            want = m if want is None else o.add(want, m, top)
+        assert (host(out.data[0])[:, : top + 1] == want[:, : top + 1]).all(), (name, top, n)
+
+
 # ------------------------------------------------------------------------------------------------ projections
 
 from perseus_b200 import linear as LIN  # noqa: E402

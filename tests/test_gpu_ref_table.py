@@ -841,7 +841,7 @@ def test_tensor_y(env, sub, dbl):
     same(got)
     # the formula on the rows of both widths
     P = np.array(env.primes, dtype=object)[None, :, None]
-    a0, a1, b0, b1, y = (v.astype(object) for v in ins)
+    a0, b0, a1, b1, y = (v.astype(object) for v in ins)  # pair 0 (a0, b0), pair 1 (a1, b1), as the args
     r0 = (a0[:, 0] * b0[:, 0] + a1[:, 0] * b1[:, 0] + o[:, 0].astype(object)) % P
     r0 = r0 * (1 + dbl) % P
     cy = c.astype(object)[None, :, None] * y[:, 0] % P

@@ -786,10 +786,12 @@ int pcb_linear_transform_multi(PcbCtx* ctx, const uint64_t* x, const uint64_t* c
  * top + 1 + kp rows, pcb_pt_load_ext); each giant step's sum brought down, rotated, and the extended outputs summed
  * with giant step 0's for one ModDown. Fewer ModDowns than pcb_linear_transform_multi (gstep against bstep - 1), so
  * it pays with many baby steps. Same arguments and workspace; the words differ from pcb_linear_transform_multi's
- * (the ModDowns round at other points), the decrypted values agree within the key-switch noise. */
+ * (the ModDowns round at other points), the decrypted values agree within the key-switch noise. baby_offset: baby b
+ * is x rotated by (b + baby_offset) stride, i.e. the product of rot(x, baby_offset stride) with that rotation folded
+ * into the hoisted babies (keys for those steps); 0 is the plain product. */
 int pcb_linear_transform_ext(PcbCtx* ctx, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
-                             int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
-                             cudaStream_t stream);
+                             int32_t bstep, int64_t stride, int64_t baby_offset, uint64_t* work, uint64_t* out,
+                             int32_t top, int32_t K, cudaStream_t stream);
 
 /* ModRaise of K ciphertexts for bootstrapping (crates/pc-gpu/src/bts/raise.rs): rows 0 of both parts (evaluation
  * form, level 0) become rows 0..top_out: every residue the centred lift of the level-0 residue (the mod_raise entry

@@ -1432,13 +1432,13 @@ int orc_linear_transform(void* cv, const uint64_t* x, const uint64_t* pts, int n
 }
 
 // The BSGS product with the babies in the extended basis (double hoisting; the sums of the reference's fused
-// CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs and crates/pc-kernels/kernels/args.cuh:325-352): baby 0 = P x on the
-// Q rows and 0 on the special rows; baby b >= 1 = the key inner product of one shared ModUp of x with P c0 added and
-// the output at the automorphism slot, not brought down; res_j = sum_b baby_b pts[bstep j + b] over the Q rows and the
+// CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs and crates/pc-kernels/kernels/args.cuh:325-352): baby b is x rotated
+// by (b + baby_offset) stride, P x on the Q rows and 0 on the special rows for the identity, else the key inner product
+// of one shared ModUp of x with P c0 added and the output at the automorphism slot, not brought down; res_j = sum_b baby_b pts[bstep j + b] over the Q rows and the
 // special rows; res_j (j >= 1) brought down and rotated (its extended output), summed with res_0; one ModDown.
 // pts: npts evaluation-form plaintexts of top + 1 + kp rows (Q primes 0..=top, then the special primes).
 int orc_linear_transform_ext(void* cv, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
-                             uint64_t* out, int top) {
+                             int64_t baby_offset, uint64_t* out, int top) {
     Ctx& c = *(Ctx*)cv;
     if (npts < 1 || bstep < 1 || stride == 0) return -1;
     const size_t n = c.n, cw = c.ct_words();
@@ -1454,7 +1454,7 @@ int orc_linear_transform_ext(void* cv, const uint64_t* x, const uint64_t* pts, i
     bool have_d = false;
     for (int b = 0; b < bstep; ++b) {
         uint64_t* o = baby.data() + (size_t)b * cw;
-        const uint64_t g = galois((int64_t)b * stride);
+        const uint64_t g = galois(((int64_t)b + baby_offset) * stride);
         if (g == 1) {  // P x on the Q rows
             for (int part = 0; part < 2; ++part)
                 for (int t = 0; t <= top; ++t)

@@ -134,10 +134,11 @@ int orc_pt_dot(const uint64_t* rot, uint64_t* res, const uint64_t* pts, const ui
 int orc_linear_transform(void* c, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
                          uint64_t* out, int top);
 /* the encoding's rows over the Q primes 0..=top and then every special prime; the same product with the babies in
- * the extended basis (pts [npts][top + 1 + kp][N]): res_j over the extended rows, each brought down and rotated */
+ * the extended basis (pts [npts][top + 1 + kp][N]): res_j over the extended rows, each brought down and rotated;
+ * baby b is x rotated by (b + baby_offset) stride */
 int orc_encode_ext(void* c, const double* vals, int nvals, int nslots, double scale, int top, uint64_t* rows);
 int orc_linear_transform_ext(void* c, const uint64_t* x, const uint64_t* pts, int npts, int bstep, int64_t stride,
-                             uint64_t* out, int top);
+                             int64_t baby_offset, uint64_t* out, int top);
 
 #ifdef __cplusplus
 }

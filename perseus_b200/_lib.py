@@ -352,7 +352,7 @@ def lib():
         "pcb_mult_pt_add": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
         "pcb_linear_transform": (C.c_int, [vp, vp, vp, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_linear_transform_multi": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
-        "pcb_linear_transform_ext": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, vp, vp, i32, i32, vp]),
+        "pcb_linear_transform_ext": (C.c_int, [vp, vp, vp, i32, i32, i32, C.c_int64, C.c_int64, vp, vp, i32, i32, vp]),
         "pcb_mult_pt_sum": (C.c_int, [vp, vp, vp, i32, vp, i32, i32, vp]),
         "pcb_keyswitch": (C.c_int, [vp, vp, vp, i32, i32, u32, vp, i32, i32, u64, vp]),
         "pcb_mod_raise": (C.c_int, [vp, vp, i32, i32, vp]),

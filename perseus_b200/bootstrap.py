@@ -175,8 +175,11 @@ def rot_steps(p):
     for inverse in (True, False):
         for stride, diags in groups(p.n, inverse, p.per_group):
             D, npts, bstep, gstep = _group_plan(stride, diags, S, p.ext)
-            steps.add(-D * stride)
-            steps.update(b * stride for b in range(1, bstep))
+            if p.ext:  # the pre-rotation by -D stride folded into the babies: steps (b - D) stride
+                steps.update((b - D) * stride for b in range(bstep))
+            else:
+                steps.add(-D * stride)
+                steps.update(b * stride for b in range(1, bstep))
             steps.update(j * bstep * stride for j in range(1, gstep))
     return sorted({s % S for s in steps if s % S})
 
@@ -301,7 +304,7 @@ class Bootstrapper:
         return len(self.cts) + 7 + self.p.r + len(self.stc)
 
     def _transform(self, x, stride, diags, factor, out_scale=None, out_mask=None):
-        """x -> sum_o (factor diag_o) rot(x, o) (offsets o = d stride, |d| <= D): x rotated by -D stride, one BSGS
+        """x -> sum_o (factor diag_o) rot(x, o) (offsets o = d stride, |d| <= D): x rotated by -D stride (folded into the babies of the double-hoisted product), one BSGS
         product with the diagonals shifted to 0 .. 2D (or folded mod S), one rescale (the output at out_scale when
         given)."""
         ops, S = self.ops, self.p.slots
@@ -317,6 +320,8 @@ class Bootstrapper:
             scale = float(self.primes[top]) if out_scale is None else out_scale * self.primes[top] / x.scale
             lt = self.plan[key] = ops.diagonals(dl, bstep, top=top, scale=scale, slots=S, stride=stride,
                                                 ext=self.p.ext)
+        if self.p.ext:  # rot(x, -D stride) folded into the double-hoisted product's babies
+            return ops.rescale_one(ops.linear_transform(x, lt, baby_offset=-D))
         y = ops.rotate(x, -D * stride) if D else x
         return ops.rescale_one(ops.linear_transform(y, lt))
 

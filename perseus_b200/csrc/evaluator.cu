@@ -1802,14 +1802,15 @@ int pcb_linear_transform(PcbCtx* c, const uint64_t* x, const uint64_t* const* pt
 
 // The BSGS product with the babies kept in the extended basis (double hoisting; the sums of the reference's fused
 // CoeffToSlot stage, crates/pc-gpu/src/bts/cts.rs with the cts_fused launcher, argument rules of args.cuh:325-352):
-// 1. baby 0 = P x on the Q rows and 0 on the special rows; babies b >= 1 = one ModUp of x, then each key's inner
-//    product with P c0 added, scattered by the automorphism, written straight into its slot: no ModDown;
+// 1. baby b = x rotated by (b + baby_offset) stride: P x on the Q rows and 0 on the special rows for the identity,
+//    the others one ModUp of x, then each key's inner product with P c0 added, scattered by the automorphism, written
+//    straight into its slot: no ModDown (a nonzero baby_offset folds a rotation of x before the product into them);
 // 2. the baby sums res_j over the Q rows and the special rows (plaintexts with special rows: pcb_pt_load_ext);
 // 3. res_j (j >= 1) brought down (ModDown) and rotated by its giant step, the extended outputs summed with res_0;
 //    one ModDown. bstep - 1 ModDowns fewer than pcb_linear_transform_multi for gstep - 1 more.
 int pcb_linear_transform_ext(PcbCtx* c, const uint64_t* x, const uint64_t* const* pts, int32_t nw, int32_t npts,
-                             int32_t bstep, int64_t stride, uint64_t* work, uint64_t* out, int32_t top, int32_t K,
-                             cudaStream_t s) {
+                             int32_t bstep, int64_t stride, int64_t baby_offset, uint64_t* work, uint64_t* out,
+                             int32_t top, int32_t K, cudaStream_t s) {
     if (!c || !x || !pts || !work || !out) return fail(PCB_BAD_ARGS, "null argument");
     if (nw < 1 || npts < 1 || bstep < 1 || bstep > 256 || stride == 0)
         return fail(PCB_BAD_ARGS, "nw %d, npts %d, bstep %d (1..256), stride %lld", nw, npts, bstep, (long long)stride);
@@ -1832,12 +1833,14 @@ int pcb_linear_transform_ext(PcbCtx* c, const uint64_t* x, const uint64_t* const
         giant[j] = key_of(*c, g);
         if (!giant[j]) return fail(-3, "no rotation key for giant step %lld (galois %llu)", (long long)st, (unsigned long long)g);
     }
+    // baby b is x rotated by (b + baby_offset) stride: the product of rot(x, baby_offset stride) without that rotation
     bool any = false;
-    for (int b = 1; b < bstep; ++b) {
-        const uint64_t g = rot_galois(*c, (int64_t)b * stride);
+    for (int b = 0; b < bstep; ++b) {
+        const int64_t st = ((int64_t)b + baby_offset) * stride;
+        const uint64_t g = rot_galois(*c, st);
         if (g == 1) continue;
         bk[b] = key_of(*c, g);
-        if (!bk[b]) return fail(-3, "no rotation key for baby step %lld (galois %llu)", (long long)(b * stride), (unsigned long long)g);
+        if (!bk[b]) return fail(-3, "no rotation key for baby step %lld (galois %llu)", (long long)st, (unsigned long long)g);
         any = true;
     }
     PcbRowSet ext_rows;
@@ -1845,9 +1848,9 @@ int pcb_linear_transform_ext(PcbCtx* c, const uint64_t* x, const uint64_t* const
     ext_rows.nq = top + 1;
     ext_rows.np = c->kp;
     ext_rows.qmax = c->nq;
-    // 1. babies: P x (baby 0 and any identity step), the others by the hoisted inner products
+    // 1. babies: P x (the identity step), the others by the hoisted inner products
     for (int b = 0; b < bstep; ++b) {
-        if (b > 0 && bk[b]) continue;
+        if (bk[b]) continue;
         PcbEwArgs e;
         memset(&e, 0, sizeof e);
         e.out = ct_ref(*c, baby + (size_t)b * kw);
@@ -1867,7 +1870,7 @@ int pcb_linear_transform_ext(PcbCtx* c, const uint64_t* x, const uint64_t* const
         if (rc) return rc;
         const bool grouped = c->ext_groups > 1 && c->lv[top].ndig <= 4;
         std::vector<int> todo;
-        for (int b = 1; b < bstep; ++b)
+        for (int b = 0; b < bstep; ++b)
             if (bk[b]) todo.push_back(b);
         size_t g0 = 0;
         while (g0 < todo.size()) {

@@ -432,17 +432,21 @@ class Session:
         return torch.empty(((lt.bstep + lt.gstep * nw) * k, 2, self.rows, self.n), dtype=torch.int64,
                            device=self.device)
 
-    def linear_transform(self, a, lt, out=None, work=None):
+    def linear_transform(self, a, lt, out=None, work=None, baby_offset=0):
         """The BSGS plaintext-matrix product sum_d diag_d * rot(a, d stride) of a K-batch (hoisted babies, one
-        pt_dot launch, the giant rotations summed in the extended basis with one ModDown). Scale a.scale lt.scale."""
+        pt_dot launch, the giant rotations summed in the extended basis with one ModDown). Scale a.scale lt.scale.
+        baby_offset (double-hoisted diagonals only): the product of rot(a, baby_offset stride), that rotation folded
+        into the babies."""
         if a.top != lt.top:
             raise ValueError(f"ciphertext at top {a.top}, diagonals encoded at top {lt.top}")
+        if baby_offset and not lt.ext:
+            raise ValueError("a baby offset needs the double-hoisted diagonals (ext=True)")
         out = out if out is not None else Ct(self.empty(a.k), a.top, a.scale * lt.scale, a.slots)
         work = work if work is not None else self.linear_work(lt, a.k)
         if lt.ext:  # the double-hoisted form (babies in the extended basis)
             L.check(L.lib().pcb_linear_transform_ext(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), 1, lt.npts,
-                                                     lt.bstep, lt.stride, C.c_void_p(work.data_ptr()), out.ptr(),
-                                                     a.top, a.k, self._stream()), "pcb_linear_transform_ext")
+                                                     lt.bstep, lt.stride, int(baby_offset), C.c_void_p(work.data_ptr()),
+                                                     out.ptr(), a.top, a.k, self._stream()), "pcb_linear_transform_ext")
         else:
             L.check(L.lib().pcb_linear_transform(self.ctx, a.ptr(), C.c_void_p(lt.table.data_ptr()), lt.npts,
                                                  lt.bstep, lt.stride, C.c_void_p(work.data_ptr()), out.ptr(), a.top,
@@ -465,9 +469,12 @@ class Session:
         table = torch.cat([lt.table for lt in lts])
         if any(lt.ext != lt0.ext for lt in lts):
             raise ValueError("linear_transform_multi: extended and plain diagonal sets mixed")
-        f = L.lib().pcb_linear_transform_ext if lt0.ext else L.lib().pcb_linear_transform_multi
-        L.check(f(self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts), lt0.npts, lt0.bstep, lt0.stride,
-                  C.c_void_p(work.data_ptr()), out.ptr(), a.top, a.k, self._stream()), "pcb_linear_transform_multi")
+        args = (self.ctx, a.ptr(), C.c_void_p(table.data_ptr()), len(lts), lt0.npts, lt0.bstep, lt0.stride)
+        rest = (C.c_void_p(work.data_ptr()), out.ptr(), a.top, a.k, self._stream())
+        if lt0.ext:
+            L.check(L.lib().pcb_linear_transform_ext(*args, 0, *rest), "pcb_linear_transform_ext")
+        else:
+            L.check(L.lib().pcb_linear_transform_multi(*args, *rest), "pcb_linear_transform_multi")
         return out
 
     def split(self, a, n):

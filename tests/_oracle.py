@@ -71,7 +71,8 @@ def lib():
         "orc_key": (C.c_int, [C.c_void_p, C.c_int, u64p, u64p, u32p]),
         "orc_encode": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
         "orc_encode_ext": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
-        "orc_linear_transform_ext": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_int64, u64p, C.c_int]),
+        "orc_linear_transform_ext": (C.c_int, [C.c_void_p, u64p, u64p, C.c_int, C.c_int, C.c_int64, C.c_int64, u64p,
+                                               C.c_int]),
         "orc_decode": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_double, f64p]),
         "orc_encrypt": (C.c_int, [C.c_void_p, f64p, C.c_int, C.c_int, C.c_double, C.c_int, u64p]),
         "orc_decrypt": (C.c_int, [C.c_void_p, u64p, C.c_int, C.c_int, C.c_double, f64p]),
@@ -292,12 +293,13 @@ class Ctx:
         assert rc == 0, rc
         return out
 
-    def linear_transform_ext(self, ct, pts, bstep, stride, top):
-        """The double-hoisted product; pts [npts][top + 1 + kp][N] evaluation-form plaintexts over the extended rows."""
+    def linear_transform_ext(self, ct, pts, bstep, stride, top, baby_offset=0):
+        """The double-hoisted product; pts [npts][top + 1 + kp][N] evaluation-form plaintexts over the extended rows;
+        baby b is ct rotated by (b + baby_offset) stride."""
         out = self.ct()
         pts = np.ascontiguousarray(pts, np.uint64)
-        rc = lib().orc_linear_transform_ext(self.h, np.ascontiguousarray(ct), pts, pts.shape[0], bstep, stride, out,
-                                            top)
+        rc = lib().orc_linear_transform_ext(self.h, np.ascontiguousarray(ct), pts, pts.shape[0], bstep, stride,
+                                            baby_offset, out, top)
         assert rc == 0, rc
         return out
 

@@ -212,10 +212,12 @@ class OracleOps:
         return OracleDiagonals(pts, bstep, stride, top, scale, ext)
 
     @_batched
-    def linear_transform(self, a, lt):
-        assert a.top == lt.top
-        f = self.c.linear_transform_ext if lt.ext else self.c.linear_transform
-        out = f(a.data, lt.pts, lt.bstep, lt.stride, a.top)
+    def linear_transform(self, a, lt, baby_offset=0):
+        assert a.top == lt.top and (lt.ext or not baby_offset)
+        if lt.ext:
+            out = self.c.linear_transform_ext(a.data, lt.pts, lt.bstep, lt.stride, a.top, baby_offset)
+        else:
+            out = self.c.linear_transform(a.data, lt.pts, lt.bstep, lt.stride, a.top)
         return OCt(out, a.top, a.scale * lt.scale, a.slots)
 
     def linear_transform_multi(self, a, lts):

@@ -25,7 +25,9 @@ def _session(ch, steps, k_max):
 
 
 def _lt_steps(bstep, npts, stride=1):
-    return [b * stride for b in range(1, bstep)] + [j * bstep * stride for j in range(1, -(-npts // bstep))]
+    # -stride: the babies of the double-hoisted product with a baby offset of -1
+    return ([b * stride for b in range(1, bstep)] + [j * bstep * stride for j in range(1, -(-npts // bstep))] +
+            [-stride])
 
 
 CASES = {
@@ -88,7 +90,7 @@ def test_linear_transform_ext_bit_exact(case):
     name, s, o, bstep, npts, stride, k = case
     rng = np.random.default_rng(41)
     slots = s.n // 2
-    for top in (s.top(), s.top() - 2):
+    for top, off in ((s.top(), 0), (s.top() - 2, 0), (s.top(), -1)):  # off: the product of rot(x, off stride)
         xs = [rng.normal(0, 1, slots) / 4 for _ in range(k)]
         cts = [s.encrypt(x, top=top, slots=slots) for x in xs]
         a = s.stack(cts) if k > 1 else cts[0]
@@ -101,16 +103,16 @@ def test_linear_transform_ext_bit_exact(case):
             O.lib().orc_ntt_fwd(rows, len(primes), np.asarray(primes, np.uint64), s.log_n)
             opts[d] = rows
         assert (host(lt.pts) == opts).all()
-        out = s.linear_transform(a, lt)
+        out = s.linear_transform(a, lt, baby_offset=off)
         for c in range(k):
             oc = o.encrypt(xs[c], slots, cts[c].scale, top)
-            want = o.linear_transform_ext(oc, opts, bstep, stride, top)
-            assert (host(out.data[c])[:, : top + 1] == want[:, : top + 1]).all(), (name, top, c)
+            want = o.linear_transform_ext(oc, opts, bstep, stride, top, off)
+            assert (host(out.data[c])[:, : top + 1] == want[:, : top + 1]).all(), (name, top, off, c)
         s.rescale_one(out)
         for c in range(k):
             got = s.decrypt_slots(out, c).real
-            ref = sum(dg * np.roll(xs[c], -d * stride) for d, dg in enumerate(diags))
-            assert np.abs(got - ref).max() < 1e-4, (name, top)
+            ref = sum(dg * np.roll(xs[c], -(d + off) * stride) for d, dg in enumerate(diags))
+            assert np.abs(got - ref).max() < 1e-4, (name, top, off)
 
 
 def test_mult_pt_add_bit_exact(case):

@@ -215,6 +215,22 @@ def test_linear_transform_ext(ctx_r, npts, bstep, top):
     assert np.abs(got - want).max() < 1e-4
 
 
+@pytest.mark.parametrize("off", [-1, -2])
+def test_linear_transform_ext_baby_offset(ctx_r, off):
+    """A baby offset folds a rotation of the input into the babies: the product of rot(x, off) without that rotation
+    (babies x rotated by b + off, the identity among them as P x)."""
+    top, bstep, npts = 5, 4, 8
+    x = vals(20)
+    rng = np.random.default_rng(21)
+    diags = [rng.normal(0, 1, SLOTS) for _ in range(npts)]
+    ct = ctx_r.encrypt(x, SLOTS, SCALE, top)
+    pts = eval_pts_ext(ctx_r, bsgs_diagonals(diags, bstep, 1), float(ctx_r.q[top]), top)
+    out = ctx_r.linear_transform_ext(ct, pts, bstep, 1, top, baby_offset=off)
+    got = ctx_r.decrypt(ctx_r.rescale(out, top), top - 1, SLOTS, SCALE).real
+    want = sum(dg * np.roll(x, -(d + off)) for d, dg in enumerate(diags))
+    assert np.abs(got - want).max() < 1e-4
+
+
 def test_hoisted_rotations_equal_plain_ones():
     """orc_rotate_hoisted (one ModUp for every step) = orc_rotate step by step, word for word; a step of galois 1
     copies."""
